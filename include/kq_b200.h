@@ -1,0 +1,224 @@
+/*
+ * kq_b200 — B200-specific additions to the Kestrel-Q operator ABI.
+ *
+ * Three groups of entry points:
+ *
+ *  1. Reference internals that the reference's layer code calls and that a
+ *     drop-in therefore has to export (declared in Kestrel-Q's
+ *     src/kq_gdn_internal.h and src/kq_qsa_internal.h):
+ *       kq_gdn_test_config_create   src/kq_gdn_internal.h:61-64
+ *       kq_gdn_execute_quantized    src/kq_gdn_internal.h:81-96
+ *       kq_qsa_test_config_create   src/kq_qsa_internal.h:65-68
+ *       kq_qsa_execute_quantized    src/kq_qsa_internal.h:94-102
+ *     The dimension records keep the reference's field order and types
+ *     (src/kq_gdn_internal.h:11-20, src/kq_qsa_internal.h:11-25).
+ *
+ *  2. The device weight provider that stands in for the GGUF-backed one
+ *     (src/kq_weight_provider.c:378-509): quantized GGUF blocks are uploaded
+ *     once to HBM and are only ever dequantised in registers.
+ *
+ *  3. Asynchronous batched decode over device buffers, the serving path that
+ *     the reference (batch 1, synchronous) has no counterpart for.
+ *
+ * Threading: every entry point takes a per-device lock; calls are ordered on
+ * one CUDA stream per device (kq_b200_set_stream replaces it).
+ */
+#ifndef KQ_B200_H
+#define KQ_B200_H
+
+#include <stdint.h>
+
+#include "kq_gdn.h"
+#include "kq_model.h"
+#include "kq_qsa.h"
+#include "kq_status.h"
+#include "kq_weight_provider.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- group 1 */
+
+typedef struct kq_gdn_dimensions {
+    uint32_t hidden_size;
+    uint32_t key_head_count;
+    uint32_t value_head_count;
+    uint32_t key_head_dimension;
+    uint32_t value_head_dimension;
+    uint32_t conv_kernel_size;
+    float rms_norm_epsilon;
+    kq_gdn_activation_dtype activation_dtype;
+} kq_gdn_dimensions;
+
+typedef struct kq_qsa_dimensions {
+    uint32_t hidden_size;
+    uint32_t query_head_count;
+    uint32_t key_value_head_count;
+    uint32_t head_dimension;
+    uint32_t index_query_head_count;
+    uint32_t index_head_dimension;
+    uint32_t block_size;
+    uint32_t token_budget;
+    uint32_t max_context;
+    uint32_t rotary_dimension;
+    float rms_norm_epsilon;
+    float rope_theta;
+    kq_qsa_activation_dtype activation_dtype;
+} kq_qsa_dimensions;
+
+kq_status kq_gdn_test_config_create(const kq_gdn_dimensions *dimensions,
+                                    kq_gdn_config **out_config,
+                                    kq_diagnostic *diagnostic);
+kq_status kq_qsa_test_config_create(const kq_qsa_dimensions *dimensions,
+                                    kq_qsa_config **out_config,
+                                    kq_diagnostic *diagnostic);
+
+/* Provider mode: weights are the tensors bound to the config with
+ * kq_b200_gdn_config_bind / kq_b200_qsa_config_bind.  weight_scratch keeps
+ * the reference's minimum-size contract and is otherwise unused. */
+kq_status kq_gdn_execute_quantized(const kq_gdn_config *config,
+                                   kq_weight_provider *provider,
+                                   const float *hidden_states,
+                                   uint64_t sequence_length,
+                                   const uint8_t *padding_mask,
+                                   float *output,
+                                   uint64_t output_capacity,
+                                   kq_gdn_state *state,
+                                   void *scratch,
+                                   uint64_t scratch_bytes,
+                                   void *weight_scratch,
+                                   uint64_t weight_scratch_bytes,
+                                   kq_gdn_checkpoint_observer observer,
+                                   void *observer_user_data,
+                                   kq_diagnostic *diagnostic);
+kq_status kq_qsa_execute_quantized(const kq_qsa_config *config,
+                                   kq_weight_provider *provider,
+                                   const float *hidden_states,
+                                   uint64_t sequence_length,
+                                   float *output,
+                                   uint64_t output_capacity,
+                                   kq_qsa_state *state,
+                                   void *scratch,
+                                   uint64_t scratch_bytes,
+                                   void *weight_scratch,
+                                   uint64_t weight_scratch_bytes,
+                                   kq_qsa_selection_observer selection_observer,
+                                   kq_qsa_checkpoint_observer checkpoint_observer,
+                                   void *observer_user_data,
+                                   kq_diagnostic *diagnostic);
+
+/* ---------------------------------------------------------------- group 2 */
+
+/* Creates an empty device-resident provider on `device`. */
+kq_status kq_b200_provider_create(int device,
+                                  kq_weight_provider **out_provider,
+                                  kq_diagnostic *diagnostic);
+
+/* Uploads a rows x columns matrix stored as consecutive GGUF rows of
+ * `type_id` blocks (F32, BF16, Q8_0, Q4_K or Q6_K; blocks run along the
+ * columns).  `packed` is host memory of exactly rows * row_bytes bytes.
+ * The returned descriptor is owned by the provider. */
+kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider,
+                                      const char *semantic_id,
+                                      kq_semantic_role role,
+                                      uint32_t type_id,
+                                      uint64_t rows,
+                                      uint64_t columns,
+                                      const void *packed,
+                                      uint64_t packed_bytes,
+                                      const kq_semantic_tensor **out_tensor,
+                                      kq_diagnostic *diagnostic);
+
+/* Uploads a small F32 vector (norm weights, conv taps, A_log, dt_bias). */
+kq_status kq_b200_provider_add_vector_f32(kq_weight_provider *provider,
+                                          const char *semantic_id,
+                                          kq_semantic_role role,
+                                          const float *values,
+                                          uint64_t count,
+                                          const kq_semantic_tensor **out_tensor,
+                                          kq_diagnostic *diagnostic);
+
+typedef struct kq_b200_gdn_tensors {
+    const kq_semantic_tensor *a_log;    /* F32 [Hv] */
+    const kq_semantic_tensor *conv;     /* F32 [C*K] */
+    const kq_semantic_tensor *dt_bias;  /* F32 [Hv] */
+    const kq_semantic_tensor *alpha;    /* matrix [Hv x H] */
+    const kq_semantic_tensor *beta;     /* matrix [Hv x H] */
+    const kq_semantic_tensor *qkv;      /* matrix [C x H] */
+    const kq_semantic_tensor *gate;     /* matrix [Hv*dv x H] */
+    const kq_semantic_tensor *norm;     /* F32 [dv] */
+    const kq_semantic_tensor *output;   /* matrix [H x Hv*dv] */
+} kq_b200_gdn_tensors;
+
+typedef struct kq_b200_qsa_tensors {
+    const kq_semantic_tensor *query;            /* [2*Hq*d x H], q/gate interleaved per head */
+    const kq_semantic_tensor *key;              /* [Hkv*d x H] */
+    const kq_semantic_tensor *value;            /* [Hkv*d x H] */
+    const kq_semantic_tensor *output;           /* [H x Hq*d] */
+    const kq_semantic_tensor *query_norm;       /* F32 [d], (1+w) form */
+    const kq_semantic_tensor *key_norm;         /* F32 [d] */
+    const kq_semantic_tensor *index_query;      /* [Hi*di x H] */
+    const kq_semantic_tensor *index_key;        /* [di x H] */
+    const kq_semantic_tensor *index_query_norm; /* F32 [di] */
+    const kq_semantic_tensor *index_key_norm;   /* F32 [di] */
+} kq_b200_qsa_tensors;
+
+/* Binds provider tensors to a config (what kq_*_config_create does from a
+ * GGUF model in the reference).  Shapes are validated against the config. */
+kq_status kq_b200_gdn_config_bind(kq_gdn_config *config,
+                                  kq_weight_provider *provider,
+                                  const kq_b200_gdn_tensors *tensors,
+                                  kq_diagnostic *diagnostic);
+kq_status kq_b200_qsa_config_bind(kq_qsa_config *config,
+                                  kq_weight_provider *provider,
+                                  const kq_b200_qsa_tensors *tensors,
+                                  kq_diagnostic *diagnostic);
+
+/* ---------------------------------------------------------------- group 3 */
+
+/* Selects the device used by subsequently created objects (default 0). */
+kq_status kq_b200_set_device(int device, kq_diagnostic *diagnostic);
+/* Replaces the library's stream on the current device (cudaStream_t, or
+ * NULL to restore the library's own non-blocking stream). */
+kq_status kq_b200_set_stream(void *cuda_stream, kq_diagnostic *diagnostic);
+void *kq_b200_get_stream(void);
+
+/* One decode token for each of `batch` independent sequences.
+ * `hidden` and `output` are device arrays [batch][hidden_size]; states are
+ * distinct states of `config`.  Asynchronous on the library stream: errors
+ * (non-finite values, capacity) surface at kq_b200_synchronize, which then
+ * rolls every state back to its value after the last successful call. */
+kq_status kq_b200_gdn_decode_batch(const kq_gdn_config *config,
+                                   kq_gdn_state *const *states,
+                                   uint32_t batch,
+                                   const float *hidden,
+                                   float *output,
+                                   kq_diagnostic *diagnostic);
+kq_status kq_b200_qsa_decode_batch(const kq_qsa_config *config,
+                                   kq_qsa_state *const *states,
+                                   uint32_t batch,
+                                   const float *hidden,
+                                   float *output,
+                                   kq_diagnostic *diagnostic);
+
+/* Waits for the library stream and reports the first device-side error
+ * raised since the previous synchronize. */
+kq_status kq_b200_synchronize(kq_diagnostic *diagnostic);
+
+/* Number of kernels this library has launched on the current device. */
+uint64_t kq_b200_kernel_launch_count(void);
+
+/* Device timing of one kernel family with CUDA events recorded around each
+ * of its launches on the launching stream ("gdn_recurrence", "proj",
+ * "qsa_attend", "qsa_score", "qsa_select", "gdn_conv", "qsa_prepare",
+ * "qsa_combine"; NULL or "" turns timing off).  Selecting a family resets
+ * the totals; kq_b200_profile_read waits for the recorded events. */
+void kq_b200_profile_kernel(const char *kernel_family);
+void kq_b200_profile_read(uint64_t *launches, double *total_ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,241 @@
+// Device-resident weight provider: the GEMV seam of the operator ABI
+// (kq_weight_provider_linear_f32, src/kq_weight_provider.c:378-509 of
+// Kestrel-Q) over GGUF blocks uploaded once to HBM.
+#include <cfenv>
+#include <cmath>
+#include <cstring>
+
+#include "kq_b200.h"
+#include "kq_tensor_view.h"
+#include "provider.hpp"
+#include "quant.cuh"
+
+using namespace kqb;
+
+ProviderTensor *provider_lookup(const kq_weight_provider *provider,
+                                const kq_semantic_tensor *semantic) {
+    if (provider == nullptr || semantic == nullptr || provider->magic != kProviderMagic) return nullptr;
+    for (const auto &t : provider->tensors)
+        if (&t->desc == semantic) return t.get();
+    return nullptr;
+}
+
+static ProviderTensor *new_tensor(kq_weight_provider *p, const char *id, kq_semantic_role role) {
+    auto t = std::make_unique<ProviderTensor>();
+    std::memset(&t->desc, 0, sizeof(t->desc));
+    if (id) std::strncpy(t->desc.semantic_id, id, KQ_SEMANTIC_ID_CAPACITY - 1);
+    t->desc.role = role;
+    t->desc.relation = KQ_BINDING_DIRECT_ONE_TO_ONE;
+    t->desc.runtime_scope = KQ_SCOPE_REQUIRED_INITIAL_TEXT;
+    t->desc.canonical_dtype = KQ_CANONICAL_DTYPE_BF16;
+    t->desc.layer_id = KQ_MODEL_NO_LAYER;
+    t->desc.canonical_expert_axis = KQ_MODEL_NO_AXIS;
+    t->desc.binding_count = 1;
+    t->desc.bindings[0].part_role = KQ_BINDING_PART_WHOLE;
+    t->desc.bindings[0].part_count = 1;
+    ProviderTensor *raw = t.get();
+    p->tensors.push_back(std::move(t));
+    return raw;
+}
+
+extern "C" {
+
+kq_status kq_weight_provider_open(const kq_gguf *, const kq_model *, uint64_t,
+                                  kq_weight_provider **out_provider, kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_provider) *out_provider = nullptr;
+    return fail(diagnostic, KQ_STATUS_UNSUPPORTED_MODEL,
+                "GGUF-backed providers are not supported by the B200 library; "
+                "use kq_b200_provider_create");
+}
+
+kq_status kq_b200_provider_create(int device, kq_weight_provider **out, kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out == nullptr) return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "provider output is required");
+    *out = nullptr;
+    kq_status st = kq_b200_set_device(device, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    DeviceContext *c;
+    st = context(&c, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    auto *p = new kq_weight_provider();
+    p->device = device;
+    *out = p;
+    return KQ_STATUS_OK;
+}
+
+void kq_weight_provider_close(kq_weight_provider *provider) {
+    if (provider == nullptr || provider->magic != kProviderMagic) return;
+    cudaSetDevice(provider->device);
+    cudaDeviceSynchronize();
+    for (auto &t : provider->tensors)
+        if (t->owned) cudaFree(t->owned);
+    provider->magic = 0;
+    delete provider;
+}
+
+kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *semantic_id,
+                                      kq_semantic_role role, uint32_t type_id, uint64_t rows,
+                                      uint64_t columns, const void *packed, uint64_t packed_bytes,
+                                      const kq_semantic_tensor **out_tensor,
+                                      kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_tensor) *out_tensor = nullptr;
+    if (provider == nullptr || provider->magic != kProviderMagic || packed == nullptr ||
+        out_tensor == nullptr || rows == 0 || columns == 0)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, data and output are required");
+    uint32_t be, bb;
+    if (!block_geometry(type_id, be, bb))
+        return fail(diagnostic, KQ_STATUS_UNSUPPORTED_TENSOR_TYPE,
+                    "matrix type must be F32, BF16, Q8_0, Q4_K or Q6_K");
+    if (columns % be != 0)
+        return fail(diagnostic, KQ_STATUS_INVALID_QUANTIZED_GEOMETRY, "columns are not whole blocks");
+    uint64_t row_bytes = columns / be * bb, total;
+    if (!mul_ok(rows, row_bytes, &total) || rows > UINT32_MAX || columns > UINT32_MAX ||
+        row_bytes > UINT32_MAX)
+        return fail(diagnostic, KQ_STATUS_ARITHMETIC_OVERFLOW, "matrix size overflows");
+    if (packed_bytes != total)
+        return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "packed byte count does not match the shape");
+    kq_status st = kq_b200_set_device(provider->device, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    void *dev = nullptr;
+    KQB_CUDA(cudaMalloc(&dev, total), diagnostic, "weight allocation");
+    cudaError_t e = cudaMemcpy(dev, packed, total, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        return cuda_fail(diagnostic, e, "weight upload");
+    }
+    ProviderTensor *t = new_tensor(provider, semantic_id, role);
+    t->owned = dev;
+    t->bytes = total;
+    t->m.data = static_cast<const uint8_t *>(dev);
+    t->m.type = type_id;
+    t->m.rows = (uint32_t)rows;
+    t->m.cols = (uint32_t)columns;
+    t->m.row_bytes = (uint32_t)row_bytes;
+    t->desc.canonical_rank = 2;
+    t->desc.canonical_dimensions[0] = rows;
+    t->desc.canonical_dimensions[1] = columns;
+    provider->metrics.provider_owned_bytes += total;
+    *out_tensor = &t->desc;
+    return KQ_STATUS_OK;
+}
+
+kq_status kq_b200_provider_add_vector_f32(kq_weight_provider *provider, const char *semantic_id,
+                                          kq_semantic_role role, const float *values,
+                                          uint64_t count, const kq_semantic_tensor **out_tensor,
+                                          kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_tensor) *out_tensor = nullptr;
+    if (provider == nullptr || provider->magic != kProviderMagic || values == nullptr ||
+        out_tensor == nullptr || count == 0 || count > (1ull << 28))
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, values and output are required");
+    for (uint64_t i = 0; i < count; ++i)
+        if (!std::isfinite(values[i]))
+            return fail(diagnostic, KQ_STATUS_NUMERIC_DOMAIN, "vector values must be finite");
+    kq_status st = kq_b200_set_device(provider->device, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    void *dev = nullptr;
+    KQB_CUDA(cudaMalloc(&dev, count * sizeof(float)), diagnostic, "vector allocation");
+    cudaError_t e = cudaMemcpy(dev, values, count * sizeof(float), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        return cuda_fail(diagnostic, e, "vector upload");
+    }
+    ProviderTensor *t = new_tensor(provider, semantic_id, role);
+    t->is_vector = true;
+    t->owned = dev;
+    t->vec_dev = static_cast<float *>(dev);
+    t->vec_host.assign(values, values + count);
+    t->bytes = count * sizeof(float);
+    t->desc.canonical_rank = 1;
+    t->desc.canonical_dimensions[0] = count;
+    provider->metrics.provider_owned_bytes += t->bytes;
+    *out_tensor = &t->desc;
+    return KQ_STATUS_OK;
+}
+
+kq_status kq_weight_provider_linear_f32(kq_weight_provider *provider,
+                                        const kq_semantic_tensor *semantic,
+                                        kq_binding_part_role part_role, uint32_t expert_id,
+                                        uint64_t rows, uint64_t columns, const float *input,
+                                        float *output, uint64_t output_capacity, void *scratch,
+                                        uint64_t scratch_bytes, kq_diagnostic *diagnostic) {
+    (void)scratch;
+    (void)scratch_bytes;
+    kq_diagnostic_clear(diagnostic);
+    ProviderTensor *t = provider_lookup(provider, semantic);
+    if (t == nullptr || input == nullptr || output == nullptr)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, semantic and buffers are required");
+    if (t->is_vector || part_role != KQ_BINDING_PART_WHOLE || expert_id != KQ_WEIGHT_PROVIDER_NO_EXPERT)
+        return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "semantic is not a whole dense matrix");
+    if (rows != t->m.rows || columns != t->m.cols)
+        return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "linear shape does not match the semantic");
+    if (output_capacity < rows) return fail(diagnostic, KQ_STATUS_BUFFER_TOO_SMALL, "linear output is too small");
+    if (ranges_overlap(input, columns * 4, output, rows * 4))
+        return fail(diagnostic, KQ_STATUS_ALIASING_VIOLATION, "linear input and output overlap");
+    if (std::fegetround() != FE_TONEAREST)
+        return fail(diagnostic, KQ_STATUS_NUMERIC_DOMAIN, "round-to-nearest floating mode is required");
+    kq_status st = kq_b200_set_device(provider->device, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    DeviceContext *c;
+    st = context(&c, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    st = c->synchronize(diagnostic);   // settle earlier asynchronous work first
+    if (st != KQ_STATUS_OK) return st;
+    const bool dev_in = is_device_pointer(input), dev_out = is_device_pointer(output);
+    void *ws;
+    st = c->workspace(Carve::round(columns * 4) + Carve::round(rows * 4) + 512, &ws, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    Carve cv(ws);
+    const float *x = input;
+    if (!dev_in) {
+        float *p = cv.take<float>(columns);
+        KQB_CUDA(cudaMemcpyAsync(p, input, columns * 4, cudaMemcpyHostToDevice, c->stream), diagnostic, "H2D");
+        x = p;
+    }
+    float *y = cv.take<float>(rows);
+    ErrorWord err = c->begin_call();
+    launch_check_finite(x, columns, err, c->stream);
+    ProjSegments segs{};
+    segs.count = 1;
+    segs.m[0] = t->m;
+    segs.out_offset[0] = 0;
+    launch_projection(segs, x, (uint32_t)columns, y, (uint32_t)rows, 1, err, c->stream);
+    launch_check_finite(y, rows, err, c->stream);
+    KQB_CUDA(cudaGetLastError(), diagnostic, "linear launch");
+    st = c->synchronize(diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    KQB_CUDA(cudaMemcpy(output, y, rows * 4, dev_out ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost),
+             diagnostic, "linear output");
+    provider->metrics.linear_requests += 1;
+    provider->metrics.row_requests += rows;
+    provider->metrics.logical_payload_bytes_touched += t->bytes;
+    return KQ_STATUS_OK;
+}
+
+kq_status kq_weight_provider_vector_f32(kq_weight_provider *provider,
+                                        const kq_semantic_tensor *semantic,
+                                        uint64_t element_count, float *output,
+                                        uint64_t output_capacity, void *, uint64_t,
+                                        kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    ProviderTensor *t = provider_lookup(provider, semantic);
+    if (t == nullptr || output == nullptr)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, semantic and output are required");
+    if (!t->is_vector) return fail(diagnostic, KQ_STATUS_LIMIT_EXCEEDED, "complete matrices are not materialised");
+    if (element_count != t->vec_host.size())
+        return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "vector element count mismatch");
+    if (output_capacity < element_count) return fail(diagnostic, KQ_STATUS_BUFFER_TOO_SMALL, "vector output is too small");
+    std::memcpy(output, t->vec_host.data(), element_count * sizeof(float));
+    provider->metrics.vector_requests += 1;
+    return KQ_STATUS_OK;
+}
+
+const kq_weight_provider_metrics *kq_weight_provider_get_metrics(const kq_weight_provider *provider) {
+    if (provider == nullptr || provider->magic != kProviderMagic) return nullptr;
+    return &provider->metrics;
+}
+
+}  // extern "C"

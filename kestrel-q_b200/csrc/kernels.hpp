@@ -1,0 +1,171 @@
+// Internal launch interface between the host ABI layer and the CUDA kernels.
+#pragma once
+
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace kqb {
+
+// Error word shared by every kernel of one device.  0 = no error; otherwise
+// the id of the first failing call (see Runtime::next_call_id) in the low
+// 32 bits and a kernel error code in the high 32 bits.
+enum DeviceError : uint32_t {
+    kErrNone = 0,
+    kErrNonFinite = 1,   // non-finite input, state or result
+    kErrDecay = 2,       // GDN log-decay not finite or positive
+    kErrSelection = 3,   // QSA selected-token count invalid
+};
+
+// One quantized (or F32/BF16) matrix in HBM: `rows` consecutive GGUF rows.
+struct QMatrix {
+    const uint8_t *data;
+    uint32_t type;
+    uint32_t rows;
+    uint32_t cols;
+    uint32_t row_bytes;
+};
+
+constexpr int kMaxSegments = 6;
+
+// Several matrices applied to the same input, outputs concatenated:
+// y[b][offset_s + r] = sum_k W_s[r][k] * x[b][k].
+struct ProjSegments {
+    QMatrix m[kMaxSegments];
+    uint32_t out_offset[kMaxSegments];
+    uint32_t tile_start[kMaxSegments + 1];  // filled by the launcher
+    int count;
+};
+
+struct ErrorWord {
+    unsigned long long *word;   // device
+    uint32_t call_id;
+};
+
+// ---- projections (kernels_proj.cu)
+void launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
+                       float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
+                       cudaStream_t stream);
+// Sequential-order product: each output is accumulated k = 0..K-1 from 0.0f
+// with separately rounded products and sums, i.e. bit-identical to the
+// reference's kq_f32_dot / kq_quantized_row_dot_f32.
+void launch_projection_exact(const ProjSegments &segs, const float *x,
+                             uint32_t ldx, float *y, uint32_t ldy,
+                             uint32_t batch, ErrorWord err,
+                             cudaStream_t stream);
+void launch_dequantize(uint32_t type, const uint8_t *packed, uint64_t elements,
+                       float *out, cudaStream_t stream);
+void launch_row_dot(uint32_t type, const uint8_t *packed, uint64_t elements,
+                    const float *x, float *out, int *status,
+                    cudaStream_t stream);
+void launch_check_finite(const float *x, uint64_t count, ErrorWord err,
+                         cudaStream_t stream);
+// y[t][i] = x[t][i] * (float)mask[t] (padding mask of src/kq_gdn_qwen38.c:548-553)
+void launch_mask_rows(const float *x, const uint8_t *mask, uint32_t rows,
+                      uint32_t cols, float *y, cudaStream_t stream);
+
+// ---- GDN (kernels_gdn.cu)
+constexpr int kMaxBatch = 64;
+
+struct GdnDims {
+    uint32_t hidden, key_heads, value_heads, key_dim, value_dim, kernel;
+    uint32_t conv_channels, key_width, value_width, repeat;
+    float eps;
+};
+
+struct GdnBatchPtrs {
+    const float *conv_in[kMaxBatch];
+    float *conv_out[kMaxBatch];
+    const float *rec_in[kMaxBatch];
+    float *rec_out[kMaxBatch];
+};
+
+struct GdnWeightsDev {
+    const float *a_log, *conv, *dt_bias, *norm;
+};
+
+// proj: [B*T][ldp] (qkv | gate | beta | alpha), item = b*T + t.
+void launch_gdn_conv_gates(const GdnDims &d, const GdnWeightsDev &w,
+                           const GdnBatchPtrs &p, uint32_t batch,
+                           uint32_t tokens, const float *proj, uint32_t ldp,
+                           float *qk, float *v, float *beta, float *decay,
+                           ErrorWord err, cudaStream_t stream);
+void launch_gdn_recurrence(const GdnDims &d, const GdnWeightsDev &w,
+                           const GdnBatchPtrs &p, uint32_t batch,
+                           uint32_t tokens, const float *qk, const float *v,
+                           const float *beta, const float *decay,
+                           const float *proj, uint32_t ldp, float *gated,
+                           ErrorWord err, cudaStream_t stream);
+
+// ---- QSA (kernels_qsa.cu)
+struct QsaDims {
+    uint32_t hidden, q_heads, kv_heads, head_dim, index_heads, index_dim;
+    uint32_t block, budget, topk, rotary, repeat, sel_capacity;
+    float eps;
+    float inv_sqrt_head;       // not used for exact paths
+    float sqrt_index_dim;      // sqrtf((float)index_dim), host-computed
+    float sqrt_head_dim;       // sqrtf((float)head_dim)
+};
+
+struct QsaSeq {
+    float *key;          // [capacity][Hkv*d]
+    float *value;        // [capacity][Hkv*d]
+    float *raw;          // [capacity][di]
+    float *block_keys;   // [di][capacity/block] feature-major
+    uint32_t length;     // committed length before this token
+    uint32_t capacity;
+};
+
+struct QsaBatch {
+    QsaSeq s[kMaxBatch];
+};
+
+struct QsaWeightsDev {
+    const float *q_norm, *k_norm, *iq_norm, *ik_norm;
+    const float *rope_cos, *rope_sin;   // [positions][rotary/2]
+    uint32_t rope_positions;
+};
+
+// proj: [B][2*Hq*d + 2*Hkv*d] (q/gate interleaved | k | v);
+// iproj: [B][Hi*di + di] (index query | raw index key), exact order.
+void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
+                        const QsaBatch &b, uint32_t batch, const float *proj,
+                        uint32_t ldp, const float *iproj, uint32_t ldi,
+                        float *q_out, float *iq_out, ErrorWord err,
+                        cudaStream_t stream);
+void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
+                      const float *iq, float *scores, uint32_t ld_scores,
+                      uint32_t max_blocks, ErrorWord err, cudaStream_t stream);
+void launch_qsa_select(const QsaDims &d, const QsaBatch &b, uint32_t batch,
+                       const float *scores, uint32_t ld_scores,
+                       uint32_t *selected, uint32_t *selected_count,
+                       ErrorWord err, cudaStream_t stream);
+void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
+                       const float *q, const uint32_t *selected,
+                       const uint32_t *selected_count, float *partial_o,
+                       float *partial_ml, uint32_t splits,
+                       ErrorWord err, cudaStream_t stream);
+void launch_qsa_combine(const QsaDims &d, uint32_t batch,
+                        const float *partial_o, const float *partial_ml,
+                        uint32_t splits, const float *proj, uint32_t ldp,
+                        float *gated, ErrorWord err, cudaStream_t stream);
+// Recomputes the block-key cache entries [first_block, end_block) of one
+// sequence from its raw index keys (after an import).
+void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
+                           const QsaSeq &s, uint32_t first_block,
+                           uint32_t end_block, ErrorWord err,
+                           cudaStream_t stream);
+
+uint64_t launches_total();
+void count_launch();
+
+// Optional CUDA-event timing of one named kernel family (kq_b200_profile_*):
+// construct before the launch, destroy after it.
+struct KernelTimer {
+    KernelTimer(const char *name, cudaStream_t stream);
+    ~KernelTimer();
+    int slot;
+    cudaStream_t stream;
+};
+
+}  // namespace kqb

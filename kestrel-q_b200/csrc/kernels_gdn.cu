@@ -1,0 +1,355 @@
+// Gated delta-net (GDN) kernels.
+//
+// Math follows the per-token loop of kq_gdn_execute_common
+// (src/kq_gdn_qwen38.c:545-842 of Kestrel-Q):
+//   conv + SiLU (:602-621), head split with consecutive key-head repeat
+//   (:631-648), beta = sigmoid(b) and g = -exp(A_log) * softplus(a + dt_bias)
+//   (:662-678), L2 norms with q scaled by 1/sqrt(dk) (:679-686), delta-rule
+//   recurrence (:705-761) and gated RMSNorm with the norm weight applied
+//   directly (:787-815).
+//
+// Work layout: items are (sequence b, token t) pairs, B sequences x T tokens
+// per launch (decode: T = 1; prefill: B = 1).  The projections of all items
+// are produced beforehand by the projection GEMM into `proj`
+// ([B*T][ldp]: qkv | gate | beta | alpha).
+#include "kernels.hpp"
+
+#include <cmath>
+
+namespace kqb {
+
+__device__ __forceinline__ bool gdn_error_raised(const ErrorWord &e) {
+    return *reinterpret_cast<volatile unsigned long long *>(e.word) != 0ull;
+}
+__device__ __forceinline__ void gdn_raise(const ErrorWord &e, uint32_t code) {
+    atomicCAS(e.word, 0ull, ((unsigned long long)code << 32) | e.call_id);
+}
+
+// Branch-stable sigmoid of kq_sigmoid_scalar (src/kq_numeric.c:628-638).
+__device__ __forceinline__ float stable_sigmoid(float x) {
+    if (x >= 0.0f) {
+        float e = expf(-x);
+        return 1.0f / (1.0f + e);
+    }
+    float e = expf(x);
+    return e / (1.0f + e);
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) s += red[w];
+    return s;
+}
+
+// ------------------------------------------------------------ conv + gates
+//
+// grid (Hk, B*T); 128 threads.  For key head kh it handles the q and k
+// channels of kh and the v channels / gates of value heads
+// kh*repeat .. kh*repeat+repeat-1.  Writes:
+//   qk    [item][2][Hk][dk]  normalised (q additionally * 1/sqrt(dk))
+//   v     [item][Vd]         SiLU(conv)
+//   beta  [item][Hv]
+//   decay [item][Hv]         exp(g)
+// and, for the last token of each sequence, the new conv state.
+
+constexpr int kConvThreads = 128;
+
+__device__ __forceinline__ float conv_history(const GdnDims &d, const float *conv_in,
+                                              const float *proj, uint32_t ldp,
+                                              uint32_t seq_item0, int t, int j,
+                                              uint32_t c) {
+    // history slot j (0..K-1) after the shift for token t: x_{t-K+1+j}
+    int src = t - (int)d.kernel + 1 + j;
+    if (src >= 0) return proj[(size_t)(seq_item0 + src) * ldp + c];
+    return conv_in[(size_t)c * d.kernel + (uint32_t)(t + 1 + j)];
+}
+
+__global__ void __launch_bounds__(kConvThreads)
+gdn_conv_gates_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t tokens,
+                      const float *__restrict__ proj, uint32_t ldp,
+                      float *__restrict__ qk, float *__restrict__ vout,
+                      float *__restrict__ beta, float *__restrict__ decay,
+                      ErrorWord err) {
+    __shared__ float red[kConvThreads / 32];
+    if (gdn_error_raised(err)) return;
+    const uint32_t kh = blockIdx.x;
+    const uint32_t item = blockIdx.y;
+    const uint32_t b = item / tokens;
+    const int t = (int)(item % tokens);
+    const uint32_t item0 = b * tokens;
+    const float *conv_in = p.conv_in[b];
+    float *conv_out = p.conv_out[b];
+    const bool last = (uint32_t)t == tokens - 1;
+    const float *prow = proj + (size_t)item * ldp;
+    bool bad = false;
+
+    // q and k channels of key head kh: conv + SiLU, then L2 norm
+    for (int which = 0; which < 2; ++which) {
+        float val = 0.0f;
+        const uint32_t i = threadIdx.x;
+        if (i < d.key_dim) {
+            uint32_t c = which * d.key_width + kh * d.key_dim + i;
+            float s = 0.0f;
+            for (uint32_t j = 0; j < d.kernel; ++j) {
+                float h = conv_history(d, conv_in, proj, ldp, item0, t, (int)j, c);
+                s = __fadd_rn(s, __fmul_rn(w.conv[(size_t)c * d.kernel + j], h));
+                if (last) conv_out[(size_t)c * d.kernel + j] = h;
+            }
+            val = s * stable_sigmoid(s);
+            bad |= !isfinite(val);
+        }
+        float sumsq = block_sum<kConvThreads>(i < d.key_dim ? val * val : 0.0f, red);
+        float inv = 1.0f / sqrtf(sumsq + 1.0e-6f);
+        if (i < d.key_dim) {
+            float out = val * inv;
+            if (which == 0) out = out * (1.0f / sqrtf((float)d.key_dim));
+            qk[((size_t)item * 2 + which) * d.key_width + kh * d.key_dim + i] = out;
+        }
+    }
+    // v channels of the value heads that share key head kh
+    for (uint32_t r = 0; r < d.repeat; ++r) {
+        uint32_t h = kh * d.repeat + r;
+        for (uint32_t i = threadIdx.x; i < d.value_dim; i += blockDim.x) {
+            uint32_t c = 2 * d.key_width + h * d.value_dim + i;
+            float s = 0.0f;
+            for (uint32_t j = 0; j < d.kernel; ++j) {
+                float hv = conv_history(d, conv_in, proj, ldp, item0, t, (int)j, c);
+                s = __fadd_rn(s, __fmul_rn(w.conv[(size_t)c * d.kernel + j], hv));
+                if (last) conv_out[(size_t)c * d.kernel + j] = hv;
+            }
+            float val = s * stable_sigmoid(s);
+            bad |= !isfinite(val);
+            vout[(size_t)item * d.value_width + h * d.value_dim + i] = val;
+        }
+        if (threadIdx.x == 0) {
+            const float pb = prow[d.conv_channels + d.value_width + h];
+            const float pa = prow[d.conv_channels + d.value_width + d.value_heads + h];
+            float bt = stable_sigmoid(pb);
+            float a = pa + w.dt_bias[h];
+            float sp = a > 20.0f ? a : log1pf(expf(a));
+            float g = -expf(w.a_log[h]) * sp;
+            if (!isfinite(g) || g > 0.0f || !isfinite(bt)) {
+                gdn_raise(err, kErrDecay);
+            }
+            beta[(size_t)item * d.value_heads + h] = bt;
+            decay[(size_t)item * d.value_heads + h] = expf(g);
+        }
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
+}
+
+// ------------------------------------------------------------ recurrence
+//
+// Fast path for dk = dv = 128: grid (Hv, B), 256 threads.  The head's
+// 128 x 128 state (64 KB) is held in registers for all tokens of the launch:
+// thread (warp w, lane l) owns columns 4l..4l+3 of rows w, w+8, ..., w+120.
+// Per token: decay, read = S^T k, delta = (v - read) * beta, S += k delta^T,
+// o = S^T q, then the gated RMSNorm of o.  The state is read from HBM once
+// and written once per launch with 128-bit coalesced accesses.
+
+constexpr int kRecThreads = 256;
+constexpr int kDim = 128;
+constexpr int kRows = kDim / (kRecThreads / 32);   // 16 rows per thread
+
+__global__ void __launch_bounds__(kRecThreads, 2)
+gdn_recurrence128_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t tokens,
+                         const float *__restrict__ qk, const float *__restrict__ vin,
+                         const float *__restrict__ beta, const float *__restrict__ decay,
+                         const float *__restrict__ proj, uint32_t ldp,
+                         float *__restrict__ gated, ErrorWord err) {
+    __shared__ __align__(16) float ks[kDim];
+    __shared__ __align__(16) float qs[kDim];
+    __shared__ __align__(16) float part[kRecThreads / 32][kDim];
+    __shared__ __align__(16) float delta[kDim];
+    __shared__ float red[kRecThreads / 32];
+    if (gdn_error_raised(err)) return;
+
+    const uint32_t h = blockIdx.x;
+    const uint32_t b = blockIdx.y;
+    const uint32_t kh = h / d.repeat;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *sin_ = p.rec_in[b] + (size_t)h * kDim * kDim;
+    float *sout = p.rec_out[b] + (size_t)h * kDim * kDim;
+
+    float4 s[kRows];
+#pragma unroll
+    for (int j = 0; j < kRows; ++j)
+        s[j] = *reinterpret_cast<const float4 *>(sin_ + (size_t)(warp + 8 * j) * kDim + 4 * lane);
+
+    bool bad = false;
+    for (uint32_t t = 0; t < tokens; ++t) {
+        const size_t item = (size_t)b * tokens + t;
+        if (threadIdx.x < kDim) {
+            qs[threadIdx.x] = qk[(item * 2 + 0) * d.key_width + kh * kDim + threadIdx.x];
+            ks[threadIdx.x] = qk[(item * 2 + 1) * d.key_width + kh * kDim + threadIdx.x];
+        }
+        const float dec = decay[item * d.value_heads + h];
+        const float bt = beta[item * d.value_heads + h];
+        __syncthreads();
+        // decay and read partials
+        float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) {
+            s[j].x *= dec; s[j].y *= dec; s[j].z *= dec; s[j].w *= dec;
+            float kv = ks[warp + 8 * j];
+            r0 = fmaf(s[j].x, kv, r0);
+            r1 = fmaf(s[j].y, kv, r1);
+            r2 = fmaf(s[j].z, kv, r2);
+            r3 = fmaf(s[j].w, kv, r3);
+        }
+        *reinterpret_cast<float4 *>(&part[warp][4 * lane]) = make_float4(r0, r1, r2, r3);
+        __syncthreads();
+        if (threadIdx.x < kDim) {
+            float rd = 0.f;
+#pragma unroll
+            for (int wv = 0; wv < kRecThreads / 32; ++wv) rd += part[wv][threadIdx.x];
+            float vv = vin[item * d.value_width + h * kDim + threadIdx.x];
+            delta[threadIdx.x] = (vv - rd) * bt;
+        }
+        __syncthreads();
+        // rank-1 update and output partials
+        const float4 dl = *reinterpret_cast<const float4 *>(&delta[4 * lane]);
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) {
+            float kv = ks[warp + 8 * j];
+            float qv = qs[warp + 8 * j];
+            s[j].x = fmaf(kv, dl.x, s[j].x);
+            s[j].y = fmaf(kv, dl.y, s[j].y);
+            s[j].z = fmaf(kv, dl.z, s[j].z);
+            s[j].w = fmaf(kv, dl.w, s[j].w);
+            o0 = fmaf(s[j].x, qv, o0);
+            o1 = fmaf(s[j].y, qv, o1);
+            o2 = fmaf(s[j].z, qv, o2);
+            o3 = fmaf(s[j].w, qv, o3);
+        }
+        *reinterpret_cast<float4 *>(&part[warp][4 * lane]) = make_float4(o0, o1, o2, o3);
+        __syncthreads();
+        // gated RMSNorm of o (threads 0..127 own one feature each)
+        float o = 0.f;
+        if (threadIdx.x < kDim) {
+#pragma unroll
+            for (int wv = 0; wv < kRecThreads / 32; ++wv) o += part[wv][threadIdx.x];
+            bad |= !isfinite(o);
+        }
+        float sumsq = block_sum<kRecThreads>(threadIdx.x < kDim ? o * o : 0.f, red);
+        if (threadIdx.x < kDim) {
+            float mean = sumsq / (float)kDim;
+            float inv = 1.0f / sqrtf(mean + d.eps);
+            float z = proj[item * ldp + d.conv_channels + h * kDim + threadIdx.x];
+            float g = (w.norm[threadIdx.x] * (o * inv)) * stable_sigmoid(z);
+            bad |= !isfinite(g);
+            gated[item * d.value_width + h * kDim + threadIdx.x] = g;
+        }
+        // part/ks/qs are rewritten next token only after the barrier inside
+        // block_sum's successor __syncthreads at the loop head
+        __syncthreads();
+    }
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+        bad |= !isfinite(s[j].x) || !isfinite(s[j].y) || !isfinite(s[j].z) || !isfinite(s[j].w);
+        *reinterpret_cast<float4 *>(sout + (size_t)(warp + 8 * j) * kDim + 4 * lane) = s[j];
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
+}
+
+// Generic dims (any dk, dv <= 1024): one thread per value feature f, state
+// streamed through global memory (rec_out doubles as the working copy).
+__global__ void __launch_bounds__(128)
+gdn_recurrence_generic_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t tokens,
+                              const float *__restrict__ qk, const float *__restrict__ vin,
+                              const float *__restrict__ beta, const float *__restrict__ decay,
+                              const float *__restrict__ proj, uint32_t ldp,
+                              float *__restrict__ gated, ErrorWord err) {
+    __shared__ float red[4];
+    if (gdn_error_raised(err)) return;
+    const uint32_t h = blockIdx.x, b = blockIdx.y;
+    const uint32_t kh = h / d.repeat;
+    const uint32_t dk = d.key_dim, dv = d.value_dim;
+    const float *sin_ = p.rec_in[b] + (size_t)h * dk * dv;
+    float *S = p.rec_out[b] + (size_t)h * dk * dv;
+    bool bad = false;
+    for (uint32_t i = threadIdx.x; i < dk * dv; i += blockDim.x) S[i] = sin_[i];
+    __syncthreads();
+    for (uint32_t t = 0; t < tokens; ++t) {
+        const size_t item = (size_t)b * tokens + t;
+        const float *q = qk + (item * 2 + 0) * d.key_width + kh * dk;
+        const float *k = qk + (item * 2 + 1) * d.key_width + kh * dk;
+        const float dec = decay[item * d.value_heads + h];
+        const float bt = beta[item * d.value_heads + h];
+        float ssq_local = 0.f;
+        float outs[8];
+        int n = 0;
+        for (uint32_t f = threadIdx.x; f < dv; f += blockDim.x, ++n) {
+            float rd = 0.f;
+            for (uint32_t kf = 0; kf < dk; ++kf) {
+                float sv = S[kf * dv + f] * dec;
+                S[kf * dv + f] = sv;
+                rd = rd + sv * k[kf];
+            }
+            float dl = (vin[item * d.value_width + h * dv + f] - rd) * bt;
+            float o = 0.f;
+            for (uint32_t kf = 0; kf < dk; ++kf) {
+                float sv = S[kf * dv + f] + k[kf] * dl;
+                S[kf * dv + f] = sv;
+                o = o + sv * q[kf];
+                bad |= !isfinite(sv);
+            }
+            bad |= !isfinite(o);
+            if (n < 8) outs[n] = o;
+            ssq_local += o * o;
+        }
+        float sumsq = block_sum<128>(ssq_local, red);
+        float mean = sumsq / (float)dv;
+        float inv = 1.0f / sqrtf(mean + d.eps);
+        n = 0;
+        for (uint32_t f = threadIdx.x; f < dv && n < 8; f += blockDim.x, ++n) {
+            float z = proj[item * ldp + d.conv_channels + h * dv + f];
+            float g = (w.norm[f] * (outs[n] * inv)) * stable_sigmoid(z);
+            bad |= !isfinite(g);
+            gated[item * d.value_width + h * dv + f] = g;
+        }
+        __syncthreads();
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
+}
+
+void launch_gdn_conv_gates(const GdnDims &d, const GdnWeightsDev &w,
+                           const GdnBatchPtrs &p, uint32_t batch,
+                           uint32_t tokens, const float *proj, uint32_t ldp,
+                           float *qk, float *v, float *beta, float *decay,
+                           ErrorWord err, cudaStream_t stream) {
+    dim3 grid(d.key_heads, batch * tokens);
+    KernelTimer timer("gdn_conv", stream);
+    gdn_conv_gates_kernel<<<grid, kConvThreads, 0, stream>>>(d, w, p, tokens, proj, ldp, qk, v,
+                                                            beta, decay, err);
+    count_launch();
+}
+
+void launch_gdn_recurrence(const GdnDims &d, const GdnWeightsDev &w,
+                           const GdnBatchPtrs &p, uint32_t batch,
+                           uint32_t tokens, const float *qk, const float *v,
+                           const float *beta, const float *decay,
+                           const float *proj, uint32_t ldp, float *gated,
+                           ErrorWord err, cudaStream_t stream) {
+    dim3 grid(d.value_heads, batch);
+    KernelTimer timer("gdn_recurrence", stream);
+    if (d.key_dim == kDim && d.value_dim == kDim) {
+        gdn_recurrence128_kernel<<<grid, kRecThreads, 0, stream>>>(d, w, p, tokens, qk, v, beta,
+                                                                  decay, proj, ldp, gated, err);
+    } else {
+        gdn_recurrence_generic_kernel<<<grid, 128, 0, stream>>>(d, w, p, tokens, qk, v, beta,
+                                                               decay, proj, ldp, gated, err);
+    }
+    count_launch();
+}
+
+}  // namespace kqb

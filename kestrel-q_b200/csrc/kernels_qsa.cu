@@ -1,0 +1,591 @@
+// QSA (gated block-sparse grouped-query attention) decode kernels.
+//
+// Math follows the per-token loop of kq_qsa_execute_common
+// (src/kq_qsa_qwen38.c:524-828 of Kestrel-Q):
+//   (1+w) RMSNorm (:231-256) and NeoX partial RoPE (:258-281) of q, k and the
+//   index query; KV / raw-index-key append (:603-606); block indexer over all
+//   complete blocks (:608-648); stable top-k by (score desc, id asc)
+//   (:328-359); token list = selected blocks in rank order then the partial
+//   tail (:654-665); softmax attention over the selected tokens (:716-773);
+//   sigmoid output gate (:774-782).
+//
+// Exactness: every step of the indexer (norms, RoPE, block-key mean, scores)
+// is evaluated with explicitly rounded F32 operations in the reference's
+// order, and the RoPE cos/sin values come from a host table computed with
+// the reference's powf/cosf/sinf expression, so candidate scores - and hence
+// the selected blocks - are bit-identical to the reference given identical
+// inputs.  The block key of a block is computed once, when the block
+// completes, and cached feature-major; the reference recomputes the same
+// value from the raw keys on every token.
+#include "kernels.hpp"
+
+#include <algorithm>
+#include <cmath>
+
+namespace kqb {
+
+__device__ __forceinline__ bool qsa_error_raised(const ErrorWord &e) {
+    return *reinterpret_cast<volatile unsigned long long *>(e.word) != 0ull;
+}
+__device__ __forceinline__ void qsa_raise(const ErrorWord &e, uint32_t code) {
+    atomicCAS(e.word, 0ull, ((unsigned long long)code << 32) | e.call_id);
+}
+
+// Sequential (1+w) RMS statistic: returns 1/sqrt(mean(x^2) + eps) computed as
+// the reference does (:234-242), or a non-finite value.
+__device__ __forceinline__ float exact_rms_inverse(const float *x, uint32_t n, float eps) {
+    float sum = 0.0f;
+    for (uint32_t i = 0; i < n; ++i) sum = __fadd_rn(sum, __fmul_rn(x[i], x[i]));
+    sum = __fdiv_rn(sum, (float)n);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sum, eps)));
+}
+
+// Applies (x * inv) * (1 + w) to x[i] (:247-249).
+__device__ __forceinline__ float exact_norm_apply(float x, float inv, float w) {
+    return __fmul_rn(__fmul_rn(x, inv), __fadd_rn(1.0f, w));
+}
+
+// Rotates the pair (i, i + half) of `x` at a table row (:265-274).
+__device__ __forceinline__ void exact_rope_pair(float *x, uint32_t i, uint32_t half,
+                                                float cs, float sn) {
+    float a = x[i], b = x[i + half];
+    x[i] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(b, sn));
+    x[i + half] = __fadd_rn(__fmul_rn(b, cs), __fmul_rn(a, sn));
+}
+
+// Normalise + rotate a head vector held in shared memory; `scratch_inv` is
+// one float of shared memory per head.  Thread `owner` computes the
+// statistic sequentially, then the CTA applies it.
+__device__ void exact_norm_rope_shared(float *x, uint32_t n, const float *w, float eps,
+                                       const QsaWeightsDev &wd, uint32_t rot,
+                                       uint32_t pos, float *inv_slot, bool &bad) {
+    if (threadIdx.x == 0) *inv_slot = exact_rms_inverse(x, n, eps);
+    __syncthreads();
+    float inv = *inv_slot;
+    if (!isfinite(inv)) bad = true;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        x[i] = exact_norm_apply(x[i], inv, w[i]);
+        if (!isfinite(x[i])) bad = true;
+    }
+    __syncthreads();
+    const uint32_t half = rot / 2;
+    const float *cs = wd.rope_cos + (size_t)pos * half;
+    const float *sn = wd.rope_sin + (size_t)pos * half;
+    for (uint32_t i = threadIdx.x; i < half; i += blockDim.x) {
+        exact_rope_pair(x, i, half, cs[i], sn[i]);
+        if (!isfinite(x[i]) || !isfinite(x[i + half])) bad = true;
+    }
+    __syncthreads();
+}
+
+// Block key of block `bi` from raw index keys, exactly as :614-631; one
+// thread, result written feature-major into s.block_keys.  `tmp` holds di
+// floats of thread-private or shared storage.
+__device__ bool exact_block_key(const QsaDims &d, const QsaWeightsDev &w, const QsaSeq &s,
+                                uint32_t bi, float *tmp) {
+    const uint32_t di = d.index_dim;
+    for (uint32_t f = 0; f < di; ++f) {
+        float sum = 0.0f;
+        for (uint32_t o = 0; o < d.block; ++o)
+            sum = __fadd_rn(sum, s.raw[(size_t)(bi * d.block + o) * di + f]);
+        tmp[f] = __fdiv_rn(sum, (float)d.block);
+    }
+    float inv = exact_rms_inverse(tmp, di, d.eps);
+    bool ok = isfinite(inv);
+    for (uint32_t f = 0; f < di; ++f) tmp[f] = exact_norm_apply(tmp[f], inv, w.ik_norm[f]);
+    const uint32_t half = d.rotary / 2;
+    const uint32_t pos = bi * d.block;
+    for (uint32_t i = 0; i < half; ++i)
+        exact_rope_pair(tmp, i, half, w.rope_cos[(size_t)pos * half + i],
+                        w.rope_sin[(size_t)pos * half + i]);
+    const uint32_t ld = s.capacity / d.block;
+    for (uint32_t f = 0; f < di; ++f) {
+        ok &= isfinite(tmp[f]);
+        s.block_keys[(size_t)f * ld + bi] = tmp[f];
+    }
+    return ok;
+}
+
+// ------------------------------------------------------------ prepare
+//
+// grid (B); 256 threads.  Shared memory holds one head vector at a time.
+
+constexpr int kPrepThreads = 256;
+
+__global__ void __launch_bounds__(kPrepThreads)
+qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
+                   const float *__restrict__ proj, uint32_t ldp,
+                   const float *__restrict__ iproj, uint32_t ldi,
+                   float *__restrict__ q_out, float *__restrict__ iq_out,
+                   ErrorWord err) {
+    extern __shared__ float sh[];   // max(d, di) floats + 1
+    if (qsa_error_raised(err)) return;
+    const uint32_t b = blockIdx.x;
+    const QsaSeq s = bt.s[b];
+    const uint32_t pos = s.length;
+    const float *prow = proj + (size_t)b * ldp;
+    const float *irow = iproj + (size_t)b * ldi;
+    const uint32_t hd = d.head_dim, di = d.index_dim;
+    const uint32_t kvw = d.kv_heads * hd;
+    float *vec = sh;
+    float *inv_slot = sh + max(hd, di);
+    bool bad = false;
+
+    // query heads: q part of the interleaved [q | gate] rows of head h
+    for (uint32_t h = 0; h < d.q_heads; ++h) {
+        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) vec[i] = prow[(size_t)h * 2 * hd + i];
+        __syncthreads();
+        exact_norm_rope_shared(vec, hd, w.q_norm, d.eps, w, d.rotary, pos, inv_slot, bad);
+        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) q_out[((size_t)b * d.q_heads + h) * hd + i] = vec[i];
+        __syncthreads();
+    }
+    // key heads -> key cache row `pos`; values copied as projected
+    const float *kproj = prow + (size_t)2 * d.q_heads * hd;
+    const float *vproj = kproj + kvw;
+    for (uint32_t h = 0; h < d.kv_heads; ++h) {
+        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) vec[i] = kproj[h * hd + i];
+        __syncthreads();
+        exact_norm_rope_shared(vec, hd, w.k_norm, d.eps, w, d.rotary, pos, inv_slot, bad);
+        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) s.key[(size_t)pos * kvw + h * hd + i] = vec[i];
+        __syncthreads();
+    }
+    for (uint32_t i = threadIdx.x; i < kvw; i += blockDim.x) {
+        float v = vproj[i];
+        if (!isfinite(v)) bad = true;
+        s.value[(size_t)pos * kvw + i] = v;
+    }
+    // index query heads
+    for (uint32_t h = 0; h < d.index_heads; ++h) {
+        for (uint32_t i = threadIdx.x; i < di; i += blockDim.x) vec[i] = irow[h * di + i];
+        __syncthreads();
+        exact_norm_rope_shared(vec, di, w.iq_norm, d.eps, w, d.rotary, pos, inv_slot, bad);
+        for (uint32_t i = threadIdx.x; i < di; i += blockDim.x) iq_out[((size_t)b * d.index_heads + h) * di + i] = vec[i];
+        __syncthreads();
+    }
+    // raw index key -> raw cache row `pos`
+    const float *rk = irow + (size_t)d.index_heads * di;
+    for (uint32_t i = threadIdx.x; i < di; i += blockDim.x) {
+        float v = rk[i];
+        if (!isfinite(v)) bad = true;
+        s.raw[(size_t)pos * di + i] = v;
+    }
+    __syncthreads();
+    // the token completes a block: cache that block's key
+    if ((pos + 1) % d.block == 0 && threadIdx.x == 0) {
+        if (!exact_block_key(d, w, s, pos / d.block, vec)) bad = true;
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) qsa_raise(err, kErrNonFinite);
+}
+
+void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
+                        const QsaBatch &b, uint32_t batch, const float *proj,
+                        uint32_t ldp, const float *iproj, uint32_t ldi,
+                        float *q_out, float *iq_out, ErrorWord err,
+                        cudaStream_t stream) {
+    size_t smem = (std::max(d.head_dim, d.index_dim) + 1) * sizeof(float);
+    KernelTimer timer("qsa_prepare", stream);
+    qsa_prepare_kernel<<<batch, kPrepThreads, smem, stream>>>(d, w, b, proj, ldp, iproj, ldi,
+                                                             q_out, iq_out, err);
+    count_launch();
+}
+
+// ------------------------------------------------------------ block keys
+__global__ void qsa_block_keys_kernel(QsaDims d, QsaWeightsDev w, QsaSeq s,
+                                      uint32_t first, uint32_t end, ErrorWord err) {
+    extern __shared__ float tmp_all[];
+    uint32_t bi = first + blockIdx.x * blockDim.x + threadIdx.x;
+    bool bad = false;
+    if (bi < end) {
+        float *tmp = tmp_all + (size_t)threadIdx.x * d.index_dim;
+        bad = !exact_block_key(d, w, s, bi, tmp);
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) qsa_raise(err, kErrNonFinite);
+}
+
+void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
+                           const QsaSeq &s, uint32_t first_block,
+                           uint32_t end_block, ErrorWord err,
+                           cudaStream_t stream) {
+    if (end_block <= first_block) return;
+    const uint32_t threads = 64;
+    uint32_t n = end_block - first_block;
+    size_t smem = (size_t)threads * d.index_dim * sizeof(float);
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(qsa_block_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+    qsa_block_keys_kernel<<<(n + threads - 1) / threads, threads, smem, stream>>>(
+        d, w, s, first_block, end_block, err);
+    count_launch();
+}
+
+// ------------------------------------------------------------ score
+//
+// grid (ceil(max_blocks / 128), B); one thread per candidate block; the
+// index query of the sequence sits in shared memory.  Score of block bi:
+// sum over index heads of max(0, q_h . key_bi) (sequential dot), / sqrt(di).
+
+__global__ void __launch_bounds__(128)
+qsa_score_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ iq,
+                 float *__restrict__ scores, uint32_t ld_scores, ErrorWord err) {
+    extern __shared__ float qsh[];   // [Hi * di]
+    if (qsa_error_raised(err)) return;
+    const uint32_t b = blockIdx.y;
+    const QsaSeq s = bt.s[b];
+    const uint32_t nblocks = (s.length + 1) / d.block;
+    const uint32_t base = blockIdx.x * blockDim.x;
+    if (base >= nblocks) return;
+    const uint32_t n = d.index_heads * d.index_dim;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) qsh[i] = iq[(size_t)b * n + i];
+    __syncthreads();
+    const uint32_t bi = base + threadIdx.x;
+    if (bi >= nblocks) return;
+    const uint32_t ld = s.capacity / d.block;
+    const float *key = s.block_keys + bi;
+    float score = 0.0f;
+    for (uint32_t h = 0; h < d.index_heads; ++h) {
+        const float *q = qsh + h * d.index_dim;
+        float dot = 0.0f;
+        for (uint32_t f = 0; f < d.index_dim; ++f)
+            dot = __fadd_rn(dot, __fmul_rn(q[f], key[(size_t)f * ld]));
+        if (dot > 0.0f) score = __fadd_rn(score, dot);
+    }
+    score = __fdiv_rn(score, d.sqrt_index_dim);
+    if (!isfinite(score)) qsa_raise(err, kErrNonFinite);
+    scores[(size_t)b * ld_scores + bi] = score;
+}
+
+void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
+                      const float *iq, float *scores, uint32_t ld_scores,
+                      uint32_t max_blocks, ErrorWord err, cudaStream_t stream) {
+    if (max_blocks == 0) return;
+    dim3 grid((max_blocks + 127) / 128, batch);
+    size_t smem = (size_t)d.index_heads * d.index_dim * sizeof(float);
+    KernelTimer timer("qsa_score", stream);
+    qsa_score_kernel<<<grid, 128, smem, stream>>>(d, b, iq, scores, ld_scores, err);
+    count_launch();
+}
+
+// ------------------------------------------------------------ select
+//
+// grid (B); 1024 threads.  Exact stable top-k: radix select (4 passes of 8
+// bits over order-preserving score keys) finds the k-th largest key T; all
+// keys > T are taken plus the lowest-id keys == T; the k winners are then
+// bitonic-sorted by (key desc, id asc), which is the reference's insertion
+// order (:328-359).
+
+constexpr int kSelThreads = 1024;
+constexpr int kSelMax = 1024;   // power of two >= the selection limit
+
+__device__ __forceinline__ uint32_t order_key(float v) {
+    if (v == 0.0f) v = 0.0f;   // -0 and +0 compare equal in the reference
+    uint32_t bits = __float_as_uint(v);
+    return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kSelThreads)
+qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
+                  uint32_t ld_scores, uint32_t *__restrict__ selected,
+                  uint32_t *__restrict__ selected_count, ErrorWord err) {
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_prefix, s_need, s_taken, s_tie_base;
+    __shared__ unsigned long long cand[kSelMax];
+    __shared__ uint32_t warp_tot[kSelThreads / 32];
+    if (qsa_error_raised(err)) return;
+    const uint32_t b = blockIdx.x;
+    const QsaSeq s = bt.s[b];
+    const uint32_t n = (s.length + 1) / d.block;
+    const uint32_t k = min(n, d.topk);
+    const float *sc = scores + (size_t)b * ld_scores;
+    const uint32_t tid = threadIdx.x;
+    if (k > kSelMax) {   // configuration guard: host rejects such configs
+        if (tid == 0) qsa_raise(err, kErrSelection);
+        return;
+    }
+    if (tid == 0) { s_prefix = 0; s_need = k; s_taken = 0; s_tie_base = 0; }
+    uint32_t mask = 0;
+    __syncthreads();
+    if (k > 0 && k < n) {
+        for (int pass = 3; pass >= 0; --pass) {
+            for (uint32_t i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+            __syncthreads();
+            const uint32_t prefix = s_prefix;
+            const int shift = pass * 8;
+            for (uint32_t i = tid; i < n; i += blockDim.x) {
+                uint32_t key = order_key(sc[i]);
+                if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (tid == 0) {
+                uint32_t need = s_need, acc = 0, bin = 255;
+                for (int bb = 255; bb >= 0; --bb) {
+                    if (acc + hist[bb] >= need) { bin = (uint32_t)bb; break; }
+                    acc += hist[bb];
+                }
+                s_need = need - acc;
+                s_prefix = prefix | (bin << shift);
+            }
+            mask |= 255u << shift;
+            __syncthreads();
+        }
+    }
+    // gather: keys above the threshold, then the s_need lowest-id ties
+    const bool take_all = (k == n);
+    const uint32_t thr = s_prefix;
+    const uint32_t ties_needed = take_all ? 0 : s_need;
+    for (uint32_t i = tid; i < kSelMax; i += blockDim.x) cand[i] = 0ull;
+    __syncthreads();
+    for (uint32_t start = 0; start < n; start += blockDim.x) {
+        uint32_t i = start + tid;
+        uint32_t key = 0;
+        bool valid = i < n;
+        if (valid) key = order_key(sc[i]);
+        bool above = valid && (take_all || key > thr);
+        bool tie = valid && !take_all && key == thr;
+        // ordered rank of ties within this chunk (ascending id)
+        unsigned ballot = __ballot_sync(0xffffffffu, tie);
+        uint32_t lane = tid & 31, warp = tid >> 5;
+        uint32_t before_in_warp = __popc(ballot & ((1u << lane) - 1u));
+        if (lane == 0) warp_tot[warp] = __popc(ballot);
+        __syncthreads();
+        uint32_t before = 0;
+        for (uint32_t w = 0; w < warp; ++w) before += warp_tot[w];
+        uint32_t tie_rank = s_tie_base + before + before_in_warp;
+        if (above) {
+            uint32_t slot = atomicAdd(&s_taken, 1u);
+            cand[slot] = ((unsigned long long)key << 32) | (uint32_t)(~i);
+        } else if (tie && tie_rank < ties_needed) {
+            uint32_t slot = atomicAdd(&s_taken, 1u);
+            cand[slot] = ((unsigned long long)key << 32) | (uint32_t)(~i);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t tot = 0;
+            for (uint32_t w = 0; w < blockDim.x / 32; ++w) tot += warp_tot[w];
+            s_tie_base += tot;
+        }
+        __syncthreads();
+    }
+    // bitonic sort, descending
+    for (uint32_t size = 2; size <= kSelMax; size <<= 1) {
+        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+            for (uint32_t i = tid; i < kSelMax; i += blockDim.x) {
+                uint32_t j = i ^ stride;
+                if (j > i) {
+                    bool desc = (i & size) == 0;
+                    unsigned long long a = cand[i], c = cand[j];
+                    if ((a < c) == desc) { cand[i] = c; cand[j] = a; }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (uint32_t i = tid; i < k; i += blockDim.x)
+        selected[(size_t)b * d.topk + i] = ~(uint32_t)(cand[i] & 0xffffffffull);
+    if (tid == 0) {
+        selected_count[b] = k;
+        if (s_taken != k) qsa_raise(err, kErrSelection);
+    }
+}
+
+void launch_qsa_select(const QsaDims &d, const QsaBatch &b, uint32_t batch,
+                       const float *scores, uint32_t ld_scores,
+                       uint32_t *selected, uint32_t *selected_count,
+                       ErrorWord err, cudaStream_t stream) {
+    KernelTimer timer("qsa_select", stream);
+    qsa_select_kernel<<<batch, kSelThreads, 0, stream>>>(d, b, scores, ld_scores, selected,
+                                                        selected_count, err);
+    count_launch();
+}
+
+// ------------------------------------------------------------ attend
+//
+// grid (splits, Hkv, B); 256 threads = 8 warps.  A split owns a contiguous
+// range of the selected-token list.  Each warp takes every 8th token of the
+// range, one token at a time: its lanes hold FPL features of the K and V
+// rows, compute the logits of all query heads sharing the KV head (warp
+// shuffle reductions) and keep an online softmax per head.  The warps'
+// partial states are merged in shared memory and written per split.
+
+template <int FPL, int HPW>
+__global__ void __launch_bounds__(256)
+qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
+                  const uint32_t *__restrict__ selected,
+                  const uint32_t *__restrict__ selected_count,
+                  float *__restrict__ part_o, float *__restrict__ part_ml,
+                  uint32_t splits, ErrorWord err) {
+    extern __shared__ float smem[];   // [8 warps][HPW][hd + 2]
+    if (qsa_error_raised(err)) return;
+    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const QsaSeq s = bt.s[b];
+    const uint32_t pos = s.length;
+    const uint32_t nblocks = (pos + 1) / d.block;
+    const uint32_t tail = (pos + 1) % d.block;
+    const uint32_t ksel = selected_count[b];
+    const uint32_t ntok = ksel * d.block + tail;
+    const uint32_t per = (ntok + splits - 1) / splits;
+    const uint32_t t0 = split * per, t1 = min(ntok, t0 + per);
+    const uint32_t hd = d.head_dim;
+    const uint32_t kvw = d.kv_heads * hd;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t heads = d.repeat;   // query heads of this KV head (<= HPW)
+
+    float qr[HPW][FPL];
+    float acc[HPW][FPL];
+    float m[HPW], l[HPW];
+#pragma unroll
+    for (int h = 0; h < HPW; ++h) {
+        m[h] = -INFINITY;
+        l[h] = 0.0f;
+#pragma unroll
+        for (int f = 0; f < FPL; ++f) {
+            uint32_t feat = lane * FPL + f;
+            acc[h][f] = 0.0f;
+            qr[h][f] = ((uint32_t)h < heads && feat < hd)
+                           ? q[((size_t)b * d.q_heads + kvh * heads + h) * hd + feat] : 0.0f;
+        }
+    }
+    const float scale = d.sqrt_head_dim;
+    for (uint32_t i = t0 + warp; i < t1; i += 8) {
+        uint32_t tok = (i < ksel * d.block)
+                           ? selected[(size_t)b * d.topk + i / d.block] * d.block + i % d.block
+                           : nblocks * d.block + (i - ksel * d.block);
+        const float *krow = s.key + (size_t)tok * kvw + kvh * hd;
+        const float *vrow = s.value + (size_t)tok * kvw + kvh * hd;
+        float kv[FPL], vv[FPL];
+        if (FPL % 4 == 0) {
+#pragma unroll
+            for (int f = 0; f < FPL; f += 4) {
+                float4 k4 = *reinterpret_cast<const float4 *>(krow + lane * FPL + f);
+                float4 v4 = *reinterpret_cast<const float4 *>(vrow + lane * FPL + f);
+                kv[f] = k4.x; kv[f + 1] = k4.y; kv[f + 2] = k4.z; kv[f + 3] = k4.w;
+                vv[f] = v4.x; vv[f + 1] = v4.y; vv[f + 2] = v4.z; vv[f + 3] = v4.w;
+            }
+        } else {
+#pragma unroll
+            for (int f = 0; f < FPL; ++f) {
+                uint32_t feat = lane * FPL + f;
+                kv[f] = feat < hd ? krow[feat] : 0.0f;
+                vv[f] = feat < hd ? vrow[feat] : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < HPW; ++h) {
+            float dot = 0.0f;
+#pragma unroll
+            for (int f = 0; f < FPL; ++f) dot = fmaf(qr[h][f], kv[f], dot);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            float logit = dot / scale;
+            float mn = fmaxf(m[h], logit);
+            float corr = expf(m[h] - mn);
+            float p = expf(logit - mn);
+            l[h] = l[h] * corr + p;
+#pragma unroll
+            for (int f = 0; f < FPL; ++f) acc[h][f] = fmaf(p, vv[f], acc[h][f] * corr);
+            m[h] = mn;
+        }
+    }
+    // merge the 8 warps
+    const uint32_t stride = hd + 2;
+    float *mine = smem + (size_t)warp * HPW * stride;
+#pragma unroll
+    for (int h = 0; h < HPW; ++h) {
+#pragma unroll
+        for (int f = 0; f < FPL; ++f) {
+            uint32_t feat = lane * FPL + f;
+            if (feat < hd) mine[h * stride + feat] = acc[h][f];
+        }
+        if (lane == 0) { mine[h * stride + hd] = m[h]; mine[h * stride + hd + 1] = l[h]; }
+    }
+    __syncthreads();
+    for (uint32_t idx = threadIdx.x; idx < heads * hd; idx += blockDim.x) {
+        uint32_t h = idx / hd, feat = idx % hd;
+        float mx = -INFINITY;
+        for (int wv = 0; wv < 8; ++wv) mx = fmaxf(mx, smem[(size_t)wv * HPW * stride + h * stride + hd]);
+        float o = 0.0f, ll = 0.0f;
+        for (int wv = 0; wv < 8; ++wv) {
+            const float *src = smem + (size_t)wv * HPW * stride + h * stride;
+            float mw = src[hd];
+            float c = (mw == -INFINITY) ? 0.0f : expf(mw - mx);
+            o += src[feat] * c;
+            ll += src[hd + 1] * c;
+        }
+        uint32_t qh = kvh * heads + h;
+        size_t slot = ((size_t)b * d.q_heads + qh) * splits + split;
+        part_o[slot * hd + feat] = o;
+        if (feat == 0) { part_ml[slot * 2] = mx; part_ml[slot * 2 + 1] = ll; }
+    }
+}
+
+void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
+                       const float *q, const uint32_t *selected,
+                       const uint32_t *selected_count, float *partial_o,
+                       float *partial_ml, uint32_t splits,
+                       ErrorWord err, cudaStream_t stream) {
+    dim3 grid(splits, d.kv_heads, batch);
+    KernelTimer timer("qsa_attend", stream);
+    // HPW covers all query heads of one KV head (host validates repeat <= 8)
+    if (d.head_dim == 256) {
+        size_t smem = (size_t)8 * 8 * (d.head_dim + 2) * sizeof(float);
+        cudaFuncSetAttribute(qsa_attend_kernel<8, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
+        qsa_attend_kernel<8, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+                                                           partial_o, partial_ml, splits, err);
+    } else if (d.head_dim == 128) {
+        size_t smem = (size_t)8 * 8 * (d.head_dim + 2) * sizeof(float);
+        qsa_attend_kernel<4, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+                                                           partial_o, partial_ml, splits, err);
+    } else {
+        size_t smem = (size_t)8 * 8 * (d.head_dim + 2) * sizeof(float);
+        qsa_attend_kernel<1, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+                                                           partial_o, partial_ml, splits, err);
+    }
+    count_launch();
+}
+
+// ------------------------------------------------------------ combine + gate
+//
+// grid (Hq, B); one thread per feature: merge the split partials, then apply
+// the simple-form sigmoid gate 1 / (1 + exp(-g)) of :778.
+
+__global__ void qsa_combine_kernel(QsaDims d, const float *__restrict__ part_o,
+                                   const float *__restrict__ part_ml, uint32_t splits,
+                                   const float *__restrict__ proj, uint32_t ldp,
+                                   float *__restrict__ gated, ErrorWord err) {
+    if (qsa_error_raised(err)) return;
+    const uint32_t h = blockIdx.x, b = blockIdx.y;
+    const uint32_t hd = d.head_dim;
+    const size_t base = ((size_t)b * d.q_heads + h) * splits;
+    float mx = -INFINITY;
+    for (uint32_t s = 0; s < splits; ++s) mx = fmaxf(mx, part_ml[(base + s) * 2]);
+    bool bad = false;
+    for (uint32_t f = threadIdx.x; f < hd; f += blockDim.x) {
+        float o = 0.0f, ll = 0.0f;
+        for (uint32_t s = 0; s < splits; ++s) {
+            float ms = part_ml[(base + s) * 2];
+            float c = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
+            o += part_o[(base + s) * hd + f] * c;
+            ll += part_ml[(base + s) * 2 + 1] * c;
+        }
+        float ctx = o / ll;
+        float g = proj[(size_t)b * ldp + (size_t)h * 2 * hd + hd + f];
+        float sg = 1.0f / (1.0f + expf(-g));
+        float out = ctx * sg;
+        if (!isfinite(out) || !(ll > 0.0f)) bad = true;
+        gated[((size_t)b * d.q_heads + h) * hd + f] = out;
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) qsa_raise(err, kErrNonFinite);
+}
+
+void launch_qsa_combine(const QsaDims &d, uint32_t batch,
+                        const float *partial_o, const float *partial_ml,
+                        uint32_t splits, const float *proj, uint32_t ldp,
+                        float *gated, ErrorWord err, cudaStream_t stream) {
+    dim3 grid(d.q_heads, batch);
+    KernelTimer timer("qsa_combine", stream);
+    qsa_combine_kernel<<<grid, 256, 0, stream>>>(d, partial_o, partial_ml, splits, proj, ldp,
+                                                 gated, err);
+    count_launch();
+}
+
+}  // namespace kqb

@@ -1,0 +1,34 @@
+// Device weight provider internals (shared by the GDN / QSA ABI units).
+#pragma once
+
+#include <memory>
+#include <vector>
+
+#include "kernels.hpp"
+#include "kq_model.h"
+#include "kq_weight_provider.h"
+#include "runtime.hpp"
+
+constexpr uint32_t kProviderMagic = 0x4b514250u;   // "KQBP"
+
+struct ProviderTensor {
+    kq_semantic_tensor desc;   // first member: handed out as the descriptor
+    bool is_vector = false;
+    kqb::QMatrix m{};          // matrices (device)
+    float *vec_dev = nullptr;  // vectors (device copy)
+    std::vector<float> vec_host;
+    uint64_t bytes = 0;
+    void *owned = nullptr;
+};
+
+struct kq_weight_provider {
+    uint32_t magic = kProviderMagic;
+    int device = 0;
+    std::vector<std::unique_ptr<ProviderTensor>> tensors;
+    kq_weight_provider_metrics metrics{};
+};
+
+// Returns the provider record behind a descriptor, or nullptr when the
+// descriptor was not created by `provider`.
+ProviderTensor *provider_lookup(const kq_weight_provider *provider,
+                                const kq_semantic_tensor *semantic);

@@ -1,0 +1,206 @@
+"""ctypes declarations of the B200 operator ABI (include/*.h).
+
+Loads ``kestrel-q_b200/lib/libkqb200.so``; there is no fallback: a missing
+library raises, and every compute entry point reports an error status when no
+GPU is present.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libkqb200.so"
+
+u32, u64, f32, vp = C.c_uint32, C.c_uint64, C.c_float, C.c_void_p
+
+# kq_status values used by the host code (include/kq_status.h)
+OK = 0
+INVALID_ARGUMENT = 1
+OUT_OF_MEMORY = 2
+UNSUPPORTED_TENSOR_TYPE = 12
+ARITHMETIC_OVERFLOW = 13
+LIMIT_EXCEEDED = 14
+SPAN_OUT_OF_RANGE = 16
+UNSUPPORTED_MODEL = 20
+SEMANTIC_MAPPING_FAILED = 22
+INVALID_QUANTIZED_GEOMETRY = 25
+TENSOR_LAYOUT_MISMATCH = 27
+BUFFER_TOO_SMALL = 32
+MALFORMED_QUANTIZED_DATA = 38
+NUMERIC_DOMAIN = 39
+DIMENSION_MISMATCH = 40
+ALIASING_VIOLATION = 41
+INCOMPATIBLE_GDN = 42
+INVALID_GDN_STATE = 43
+INCOMPATIBLE_QSA = 44
+INVALID_QSA_STATE = 45
+
+TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_BF16 = 0, 8, 12, 14, 30
+
+
+class Diagnostic(C.Structure):
+    _fields_ = [("status", C.c_int), ("message", C.c_char * 256)]
+
+    def text(self) -> str:
+        return self.message.decode(errors="replace")
+
+
+class GdnDimensions(C.Structure):
+    _fields_ = [("hidden_size", u32), ("key_head_count", u32), ("value_head_count", u32),
+                ("key_head_dimension", u32), ("value_head_dimension", u32),
+                ("conv_kernel_size", u32), ("rms_norm_epsilon", f32), ("activation_dtype", C.c_int)]
+
+
+class QsaDimensions(C.Structure):
+    _fields_ = [("hidden_size", u32), ("query_head_count", u32), ("key_value_head_count", u32),
+                ("head_dimension", u32), ("index_query_head_count", u32),
+                ("index_head_dimension", u32), ("block_size", u32), ("token_budget", u32),
+                ("max_context", u32), ("rotary_dimension", u32), ("rms_norm_epsilon", f32),
+                ("rope_theta", f32), ("activation_dtype", C.c_int)]
+
+
+GDN_WEIGHT_FIELDS = ["a_log", "conv", "dt_bias", "alpha", "beta", "qkv", "gate", "norm", "output"]
+QSA_WEIGHT_FIELDS = ["query", "key", "value", "output", "query_norm", "key_norm", "index_query",
+                     "index_key", "index_query_norm", "index_key_norm"]
+
+
+def _pair_fields(names):
+    out = []
+    for n in names:
+        out += [(n, vp), (n + "_count", u64)]
+    return out
+
+
+class GdnWeightsF32(C.Structure):
+    _fields_ = _pair_fields(GDN_WEIGHT_FIELDS)
+
+
+class QsaWeightsF32(C.Structure):
+    _fields_ = _pair_fields(QSA_WEIGHT_FIELDS)
+
+
+class GdnTensors(C.Structure):
+    _fields_ = [(n, vp) for n in GDN_WEIGHT_FIELDS]
+
+
+class QsaTensors(C.Structure):
+    _fields_ = [(n, vp) for n in QSA_WEIGHT_FIELDS]
+
+
+class QuantGeometry(C.Structure):
+    _fields_ = [("type_id", u32), ("block_elements", u64), ("bytes_per_block", u64)]
+
+
+class QuantBlockSpan(C.Structure):
+    _fields_ = [("requested_element_offset", u64), ("requested_element_count", u64),
+                ("first_block", u64), ("block_count", u64), ("physical_byte_offset", u64),
+                ("physical_byte_length", u64), ("leading_elements", u64), ("trailing_elements", u64)]
+
+
+class QsaSelection(C.Structure):
+    _fields_ = [("token_index", u64), ("absolute_position", u64),
+                ("candidate_block_ids", C.POINTER(u32)), ("candidate_scores", C.POINTER(f32)),
+                ("candidate_count", u64), ("selected_block_ids", C.POINTER(u32)),
+                ("selected_block_count", u64), ("selected_token_positions", C.POINTER(u32)),
+                ("selected_token_count", u64), ("tail_count", u64)]
+
+
+SELECTION_OBSERVER = C.CFUNCTYPE(None, C.POINTER(QsaSelection), vp)
+
+_SIGNATURES = {
+    "kq_status_string": (C.c_char_p, [C.c_int]),
+    "kq_diagnostic_clear": (None, [vp]),
+    "kq_quant_geometry_for_type": (C.c_int, [u32, C.POINTER(QuantGeometry), vp]),
+    "kq_quant_packed_size": (C.c_int, [u32, u64, C.POINTER(u64), vp]),
+    "kq_quant_element_to_block": (C.c_int, [u32, u64, u64, C.POINTER(u64), C.POINTER(u64), vp]),
+    "kq_quant_range_to_blocks": (C.c_int, [u32, u64, u64, u64, C.POINTER(QuantBlockSpan), vp]),
+    "kq_dequantize_blocks_f32": (C.c_int, [u32, vp, u64, vp, u64, C.POINTER(u64), vp]),
+    "kq_quantized_row_dot_f32": (C.c_int, [u32, vp, u64, vp, u64, vp, vp]),
+    "kq_b200_set_device": (C.c_int, [C.c_int, vp]),
+    "kq_b200_set_stream": (C.c_int, [vp, vp]),
+    "kq_b200_get_stream": (vp, []),
+    "kq_b200_synchronize": (C.c_int, [vp]),
+    "kq_b200_kernel_launch_count": (u64, []),
+    "kq_b200_provider_create": (C.c_int, [C.c_int, C.POINTER(vp), vp]),
+    "kq_weight_provider_close": (None, [vp]),
+    "kq_weight_provider_open": (C.c_int, [vp, vp, u64, C.POINTER(vp), vp]),
+    "kq_b200_provider_add_matrix": (C.c_int, [vp, C.c_char_p, C.c_int, u32, u64, u64, vp, u64,
+                                              C.POINTER(vp), vp]),
+    "kq_b200_provider_add_vector_f32": (C.c_int, [vp, C.c_char_p, C.c_int, vp, u64, C.POINTER(vp), vp]),
+    "kq_weight_provider_linear_f32": (C.c_int, [vp, vp, C.c_int, u32, u64, u64, vp, vp, u64, vp, u64, vp]),
+    "kq_weight_provider_vector_f32": (C.c_int, [vp, vp, u64, vp, u64, vp, u64, vp]),
+    "kq_gdn_test_config_create": (C.c_int, [C.POINTER(GdnDimensions), C.POINTER(vp), vp]),
+    "kq_gdn_config_create": (C.c_int, [vp, u32, C.POINTER(vp), vp]),
+    "kq_gdn_config_close": (None, [vp]),
+    "kq_b200_gdn_config_bind": (C.c_int, [vp, vp, C.POINTER(GdnTensors), vp]),
+    "kq_gdn_config_scratch_bytes": (u64, [vp]),
+    "kq_gdn_config_token_scratch_bytes": (u64, [vp]),
+    "kq_gdn_config_dequant_scratch_bytes": (u64, [vp]),
+    "kq_gdn_config_recurrent_element_count": (u64, [vp]),
+    "kq_gdn_config_conv_state_element_count": (u64, [vp]),
+    "kq_gdn_config_conv_channel_count": (u32, [vp]),
+    "kq_gdn_config_hidden_size": (u32, [vp]),
+    "kq_gdn_state_create": (C.c_int, [vp, C.POINTER(vp), vp]),
+    "kq_gdn_state_close": (None, [vp]),
+    "kq_gdn_state_reset": (C.c_int, [vp, vp]),
+    "kq_gdn_state_export_f32": (C.c_int, [vp, vp, u64, vp, u64, C.POINTER(C.c_int), vp]),
+    "kq_gdn_state_import_f32": (C.c_int, [vp, vp, u64, vp, u64, C.c_int, vp]),
+    "kq_gdn_prefill_f32": (C.c_int, [vp, C.POINTER(GdnWeightsF32), vp, u64, vp, vp, u64, vp, vp, u64,
+                                     vp, vp, vp]),
+    "kq_gdn_decode_f32": (C.c_int, [vp, C.POINTER(GdnWeightsF32), vp, vp, u64, vp, vp, u64, vp, vp, vp]),
+    "kq_gdn_execute_quantized": (C.c_int, [vp, vp, vp, u64, vp, vp, u64, vp, vp, u64, vp, u64, vp, vp, vp]),
+    "kq_b200_gdn_decode_batch": (C.c_int, [vp, C.POINTER(vp), u32, vp, vp, vp]),
+    "kq_qsa_test_config_create": (C.c_int, [C.POINTER(QsaDimensions), C.POINTER(vp), vp]),
+    "kq_qsa_config_close": (None, [vp]),
+    "kq_b200_qsa_config_bind": (C.c_int, [vp, vp, C.POINTER(QsaTensors), vp]),
+    "kq_qsa_config_block_selection_limit": (u32, [vp]),
+    "kq_qsa_config_semantic_state_bytes_per_token": (u64, [vp]),
+    "kq_qsa_state_create": (C.c_int, [vp, u64, C.POINTER(vp), vp]),
+    "kq_qsa_state_close": (None, [vp]),
+    "kq_qsa_state_reset": (C.c_int, [vp, vp]),
+    "kq_qsa_state_length": (u64, [vp]),
+    "kq_qsa_state_capacity": (u64, [vp]),
+    "kq_qsa_state_export_f32": (C.c_int, [vp, vp, u64, vp, u64, vp, u64, C.POINTER(u64), vp]),
+    "kq_qsa_state_import_f32": (C.c_int, [vp, vp, u64, vp, u64, vp, u64, u64, vp]),
+    "kq_qsa_required_scratch_bytes": (C.c_int, [vp, vp, u64, C.POINTER(u64), vp]),
+    "kq_qsa_select_blocks_f32": (C.c_int, [vp, u64, u64, vp, u64, C.POINTER(u64), vp]),
+    "kq_qsa_prefill_f32": (C.c_int, [vp, C.POINTER(QsaWeightsF32), vp, u64, vp, u64, vp, vp, u64,
+                                     SELECTION_OBSERVER, vp, vp, vp]),
+    "kq_qsa_decode_f32": (C.c_int, [vp, C.POINTER(QsaWeightsF32), vp, vp, u64, vp, vp, u64,
+                                    SELECTION_OBSERVER, vp, vp, vp]),
+    "kq_qsa_execute_quantized": (C.c_int, [vp, vp, vp, u64, vp, u64, vp, vp, u64, vp, u64,
+                                           SELECTION_OBSERVER, vp, vp, vp]),
+    "kq_b200_qsa_decode_batch": (C.c_int, [vp, C.POINTER(vp), u32, vp, vp, vp]),
+    "kq_gdn_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
+    "kq_qsa_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Loads the library (raises if it was not built: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: run kestrel-q_b200/build.py "
+                               "(the B200 operators have no CPU fallback)")
+        handle = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+class KQError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"kq status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+def check(status: int, diag: Diagnostic) -> None:
+    if status != OK:
+        raise KQError(status, diag.text())

@@ -1,0 +1,608 @@
+/*
+ * kq_oracle.c — CPU restatement of Kestrel-Q's token-mixing hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY (see kq_oracle.h).  Build: make -C oracle port.
+ * Must be compiled with -fno-fast-math -ffp-contract=off: every product and
+ * every sum below is a separately rounded F32 operation, in the reference's
+ * order, so the results are bit-identical to the reference's scalar C.
+ * File:line citations point into the Kestrel-Q source tree.
+ */
+#include "kq_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ---------------------------------------------------------------- dequant */
+
+/* f16 -> f32 with exact subnormal handling: src/kq_numeric.c:58-82. */
+static float kqo_half(uint16_t h) {
+    uint32_t sign = ((uint32_t)h & 0x8000U) << 16;
+    uint32_t exponent = ((uint32_t)h >> 10) & 0x1fU;
+    uint32_t mantissa = (uint32_t)h & 0x3ffU;
+    uint32_t bits;
+    float value;
+    if (exponent == 0U) {
+        if (mantissa == 0U) {
+            bits = sign;
+        } else {
+            /* normalise the subnormal: shift until the implicit bit appears */
+            uint32_t e = 113U;
+            while ((mantissa & 0x400U) == 0U) {
+                mantissa <<= 1;
+                e -= 1U;
+            }
+            bits = sign | (e << 23) | ((mantissa & 0x3ffU) << 13);
+        }
+    } else if (exponent == 31U) {
+        bits = sign | 0x7f800000U | (mantissa << 13);
+    } else {
+        bits = sign | ((exponent + 112U) << 23) | (mantissa << 13);
+    }
+    memcpy(&value, &bits, sizeof(value));
+    return value;
+}
+
+static uint16_t kqo_u16(const unsigned char *p) {
+    return (uint16_t)(p[0] | (p[1] << 8));
+}
+
+int kqo_block_geometry(uint32_t type_id, uint64_t *block_elements,
+                       uint64_t *bytes_per_block) {
+    uint64_t e = 0, b = 0;
+    switch (type_id) {
+    case KQO_TYPE_F32: e = 1; b = 4; break;
+    case KQO_TYPE_BF16: e = 1; b = 2; break;
+    case KQO_TYPE_Q8_0: e = 32; b = 34; break;
+    case KQO_TYPE_Q4_K: e = 256; b = 144; break;
+    case KQO_TYPE_Q6_K: e = 256; b = 210; break;
+    default: return KQO_UNSUPPORTED_TYPE;
+    }
+    if (block_elements) *block_elements = e;
+    if (bytes_per_block) *bytes_per_block = b;
+    return KQO_OK;
+}
+
+/* K-quant 6-bit scale/min unpack: src/kq_numeric.c:161-174. */
+static void kqo_k_scale(uint32_t j, const unsigned char *s, uint8_t *sc,
+                        uint8_t *mn) {
+    if (j < 4U) {
+        *sc = (uint8_t)(s[j] & 63U);
+        *mn = (uint8_t)(s[j + 4U] & 63U);
+    } else {
+        *sc = (uint8_t)((s[j + 4U] & 15U) | ((s[j - 4U] >> 6) << 4));
+        *mn = (uint8_t)((s[j + 4U] >> 4) | ((s[j] >> 6) << 4));
+    }
+}
+
+static int kqo_decode_block(uint32_t type_id, const unsigned char *p,
+                            float *out) {
+    uint32_t i;
+    if (type_id == KQO_TYPE_F32) {
+        uint32_t bits = (uint32_t)p[0] | ((uint32_t)p[1] << 8) |
+                        ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+        memcpy(out, &bits, 4);
+        return KQO_OK;
+    }
+    if (type_id == KQO_TYPE_BF16) {
+        uint32_t bits = (uint32_t)kqo_u16(p) << 16;
+        memcpy(out, &bits, 4);
+        return KQO_OK;
+    }
+    if (type_id == KQO_TYPE_Q8_0) {
+        /* src/kq_numeric.c:210-222: out = (float)code * d */
+        float d = kqo_half(kqo_u16(p));
+        if (!isfinite(d)) return KQO_NUMERIC_DOMAIN;
+        for (i = 0; i < 32U; ++i) {
+            out[i] = (float)(int8_t)p[2U + i] * d;
+        }
+        return KQO_OK;
+    }
+    if (type_id == KQO_TYPE_Q4_K) {
+        /* src/kq_numeric.c:223-277: two separately rounded products per
+         * group, then (d*sc)*q - (dmin*m). */
+        float d = kqo_half(kqo_u16(p));
+        float dmin = kqo_half(kqo_u16(p + 2));
+        const unsigned char *scales = p + 4;
+        const unsigned char *q = p + 16;
+        uint32_t g;
+        if (!isfinite(d) || !isfinite(dmin)) return KQO_NUMERIC_DOMAIN;
+        for (g = 0; g < 4U; ++g) {
+            uint8_t s0, m0, s1, m1;
+            float dl, ml, dh, mh;
+            kqo_k_scale(2U * g, scales, &s0, &m0);
+            kqo_k_scale(2U * g + 1U, scales, &s1, &m1);
+            dl = d * (float)s0;
+            ml = dmin * (float)m0;
+            dh = d * (float)s1;
+            mh = dmin * (float)m1;
+            for (i = 0; i < 32U; ++i) {
+                uint8_t byte = q[g * 32U + i];
+                out[g * 64U + i] = dl * (float)(byte & 15U) - ml;
+                out[g * 64U + 32U + i] = dh * (float)(byte >> 4) - mh;
+            }
+        }
+        return KQO_OK;
+    }
+    if (type_id == KQO_TYPE_Q6_K) {
+        /* Public GGUF Q6_K super-block (210 bytes, 256 values):
+         *   ql[128]  low 4 bits of each 6-bit code
+         *   qh[64]   high 2 bits, four codes per byte
+         *   sc[16]   signed 8-bit sub-block scales (16 values each)
+         *   d        fp16 super-block scale
+         * Two halves of 128 values; within a half, value l (0..31) and its
+         * neighbours at +32, +64, +96 take their low nibbles from
+         * ql[l], ql[l+32], ql[l] >> 4, ql[l+32] >> 4 and their high bits
+         * from qh[l] bit pairs 0-1, 2-3, 4-5, 6-7.  value = (d * sc) * (q - 32)
+         * with each product rounded separately.  Not in the reference:
+         * parity for this type is pinned only by this restatement. */
+        const unsigned char *ql = p;
+        const unsigned char *qh = p + 128;
+        const signed char *sc = (const signed char *)(p + 192);
+        float d = kqo_half(kqo_u16(p + 208));
+        uint32_t half;
+        if (!isfinite(d)) return KQO_NUMERIC_DOMAIN;
+        for (half = 0; half < 2U; ++half) {
+            const unsigned char *L = ql + half * 64U;
+            const unsigned char *Hb = qh + half * 32U;
+            const signed char *S = sc + half * 8U;
+            float *o = out + half * 128U;
+            for (i = 0; i < 32U; ++i) {
+                uint32_t sub = i / 16U;
+                int c0 = (int)((L[i] & 15U) | (((Hb[i] >> 0) & 3U) << 4)) - 32;
+                int c1 = (int)((L[i + 32U] & 15U) | (((Hb[i] >> 2) & 3U) << 4)) - 32;
+                int c2 = (int)((L[i] >> 4) | (((Hb[i] >> 4) & 3U) << 4)) - 32;
+                int c3 = (int)((L[i + 32U] >> 4) | (((Hb[i] >> 6) & 3U) << 4)) - 32;
+                float s0 = d * (float)S[sub + 0U];
+                float s1 = d * (float)S[sub + 2U];
+                float s2 = d * (float)S[sub + 4U];
+                float s3 = d * (float)S[sub + 6U];
+                o[i] = s0 * (float)c0;
+                o[i + 32U] = s1 * (float)c1;
+                o[i + 64U] = s2 * (float)c2;
+                o[i + 96U] = s3 * (float)c3;
+            }
+        }
+        return KQO_OK;
+    }
+    return KQO_UNSUPPORTED_TYPE;
+}
+
+int kqo_dequantize(uint32_t type_id, const void *packed, uint64_t packed_bytes,
+                   float *output, uint64_t output_capacity) {
+    uint64_t be, bb, blocks, i;
+    int st = kqo_block_geometry(type_id, &be, &bb);
+    if (st != KQO_OK) return st;
+    if (packed == NULL || output == NULL || packed_bytes % bb != 0U)
+        return KQO_INVALID_ARGUMENT;
+    blocks = packed_bytes / bb;
+    if (output_capacity < blocks * be) return KQO_INVALID_ARGUMENT;
+    for (i = 0; i < blocks; ++i) {
+        st = kqo_decode_block(type_id, (const unsigned char *)packed + i * bb,
+                              output + i * be);
+        if (st != KQO_OK) return st;
+    }
+    return KQO_OK;
+}
+
+/* Quantized row dot: src/kq_numeric.c:420-503.  Block by block, sequential
+ * F32 accumulation from 0.0f in element order. */
+int kqo_row_dot(uint32_t type_id, const void *packed, uint64_t packed_bytes,
+                const float *x, uint64_t count, float *output) {
+    float scratch[256];
+    float acc = 0.0f;
+    uint64_t be, bb, blocks, b, i;
+    int st = kqo_block_geometry(type_id, &be, &bb);
+    if (st != KQO_OK) return st;
+    if (packed_bytes % bb != 0U || (packed_bytes / bb) * be != count)
+        return KQO_INVALID_ARGUMENT;
+    blocks = packed_bytes / bb;
+    for (b = 0; b < blocks; ++b) {
+        st = kqo_decode_block(type_id, (const unsigned char *)packed + b * bb,
+                              scratch);
+        if (st != KQO_OK) return st;
+        for (i = 0; i < be; ++i) {
+            float product = scratch[i] * x[b * be + i];
+            acc = acc + product;
+        }
+    }
+    if (!isfinite(acc)) return KQO_NUMERIC_DOMAIN;
+    *output = acc;
+    return KQO_OK;
+}
+
+int kqo_matvec(uint32_t type_id, const void *packed, uint64_t rows,
+               uint64_t cols, const float *x, uint64_t batch, float *y) {
+    uint64_t be, bb, row_bytes, r, b;
+    int st = kqo_block_geometry(type_id, &be, &bb);
+    if (st != KQO_OK) return st;
+    if (cols % be != 0U) return KQO_INVALID_ARGUMENT;
+    row_bytes = (cols / be) * bb;
+    for (b = 0; b < batch; ++b) {
+        for (r = 0; r < rows; ++r) {
+            st = kqo_row_dot(type_id,
+                             (const unsigned char *)packed + r * row_bytes,
+                             row_bytes, x + b * cols, cols, &y[b * rows + r]);
+            if (st != KQO_OK) return st;
+        }
+    }
+    return KQO_OK;
+}
+
+/* ------------------------------------------------------------- primitives */
+
+/* kq_f32_dot: src/kq_numeric.c:591-626 (sequential, from 0.0f). */
+static float kqo_dot(const float *a, const float *b, uint64_t n) {
+    float acc = 0.0f;
+    uint64_t i;
+    for (i = 0; i < n; ++i) {
+        float product = a[i] * b[i];
+        acc = acc + product;
+    }
+    return acc;
+}
+
+/* Branch-stable sigmoid: src/kq_numeric.c:628-638. */
+static float kqo_sigmoid(float x) {
+    if (x >= 0.0f) {
+        float e = expf(-x);
+        return 1.0f / (1.0f + e);
+    } else {
+        float e = expf(x);
+        return e / (1.0f + e);
+    }
+}
+
+/* ------------------------------------------------------------------- GDN */
+
+/* Per-token loop of src/kq_gdn_qwen38.c:545-842 over F32 weights. */
+int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
+                const float *hidden, uint64_t tokens, const uint8_t *mask,
+                float *output, float *conv_state, float *recurrent_state) {
+    const uint64_t H = dm->hidden_size, Hv = dm->value_heads,
+                   dk = dm->key_dim, dv = dm->value_dim, K = dm->conv_kernel;
+    const uint64_t key_width = (uint64_t)dm->key_heads * dk;
+    const uint64_t Vd = Hv * dv;
+    const uint64_t C = 2U * key_width + Vd;
+    const uint64_t repeat = Hv / dm->key_heads;
+    const uint64_t conv_n = C * K, rec_n = Hv * dk * dv;
+    const float query_scale = 1.0f / sqrtf((float)dk);
+    float *ws, *conv, *rec, *xin, *proj, *gate, *pb, *pa, *co, *q, *k, *v,
+          *beta, *g, *core, *sg, *y;
+    uint64_t t, i, h, f, kf, c, j;
+    int status = KQO_OK;
+
+    if (dm->conv_kernel == 0U || dm->key_heads == 0U || Hv % dm->key_heads)
+        return KQO_INVALID_ARGUMENT;
+    ws = (float *)malloc(sizeof(float) *
+                         (conv_n + rec_n + H + C + Vd + 2 * Hv + C +
+                          2 * Hv * dk + Vd + 2 * Hv + Vd + Vd + H));
+    if (ws == NULL) return KQO_INVALID_ARGUMENT;
+    conv = ws;            rec = conv + conv_n;  xin = rec + rec_n;
+    proj = xin + H;       gate = proj + C;      pb = gate + Vd;
+    pa = pb + Hv;         co = pa + Hv;         q = co + C;
+    k = q + Hv * dk;      v = k + Hv * dk;      beta = v + Vd;
+    g = beta + Hv;        core = g + Hv;        sg = core + Vd;
+    y = sg + Vd;
+    /* transactional: work on a copy (src/kq_gdn_qwen38.c:532-536) */
+    memcpy(conv, conv_state, sizeof(float) * conv_n);
+    memcpy(rec, recurrent_state, sizeof(float) * rec_n);
+
+    for (t = 0; t < tokens && status == KQO_OK; ++t) {
+        const float *x = hidden + t * H;
+        float m = mask == NULL ? 1.0f : (float)mask[t];
+        for (i = 0; i < H; ++i) xin[i] = x[i] * m;
+        /* projections (:558-579) */
+        for (i = 0; i < C; ++i) proj[i] = kqo_dot(w->qkv + i * H, xin, H);
+        for (i = 0; i < Vd; ++i) gate[i] = kqo_dot(w->gate + i * H, xin, H);
+        for (i = 0; i < Hv; ++i) pb[i] = kqo_dot(w->beta + i * H, xin, H);
+        for (i = 0; i < Hv; ++i) pa[i] = kqo_dot(w->alpha + i * H, xin, H);
+        /* causal conv over pre-activation history, then SiLU (:602-621) */
+        for (c = 0; c < C; ++c) {
+            float *hist = conv + c * K;
+            float s;
+            for (j = 1; j < K; ++j) hist[j - 1] = hist[j];
+            hist[K - 1] = proj[c];
+            s = kqo_dot(w->conv + c * K, hist, K);
+            co[c] = s * kqo_sigmoid(s);
+        }
+        /* head split with consecutive key-head repeat (:631-648) */
+        for (h = 0; h < Hv; ++h) {
+            uint64_t kh = h / repeat;
+            memcpy(q + h * dk, co + kh * dk, sizeof(float) * dk);
+            memcpy(k + h * dk, co + key_width + kh * dk, sizeof(float) * dk);
+            memcpy(v + h * dv, co + 2 * key_width + h * dv, sizeof(float) * dv);
+        }
+        /* beta, log-decay, L2 norms (:662-687) */
+        for (h = 0; h < Hv; ++h) {
+            float sp, a = pa[h] + w->dt_bias[h];
+            float base = -expf(w->a_log[h]);
+            float sum, inv;
+            beta[h] = kqo_sigmoid(pb[h]);
+            sp = a > 20.0f ? a : log1pf(expf(a));
+            g[h] = base * sp;
+            if (!isfinite(g[h]) || g[h] > 0.0f) { status = KQO_NUMERIC_DOMAIN; break; }
+            sum = kqo_dot(q + h * dk, q + h * dk, dk);
+            sum = sum + 1.0e-6f;
+            inv = 1.0f / sqrtf(sum);
+            for (i = 0; i < dk; ++i) {
+                float nrm = q[h * dk + i] * inv;
+                q[h * dk + i] = nrm * query_scale;
+            }
+            sum = kqo_dot(k + h * dk, k + h * dk, dk);
+            sum = sum + 1.0e-6f;
+            inv = 1.0f / sqrtf(sum);
+            for (i = 0; i < dk; ++i) {
+                float nrm = k[h * dk + i] * inv;
+                k[h * dk + i] = nrm * 1.0f;
+            }
+        }
+        if (status != KQO_OK) break;
+        /* delta-rule recurrence (:705-761) */
+        for (h = 0; h < Hv; ++h) {
+            float decay = expf(g[h]);
+            float *S = rec + h * dk * dv;
+            const float *kh = k + h * dk, *qh = q + h * dk, *vh = v + h * dv;
+            float delta[1024];
+            for (i = 0; i < dk * dv; ++i) S[i] = S[i] * decay;
+            for (f = 0; f < dv; ++f) {
+                float sum = 0.0f;
+                for (kf = 0; kf < dk; ++kf) {
+                    float product = S[kf * dv + f] * kh[kf];
+                    sum = sum + product;
+                }
+                delta[f] = (vh[f] - sum) * beta[h];
+            }
+            for (kf = 0; kf < dk; ++kf) {
+                for (f = 0; f < dv; ++f) {
+                    float update = kh[kf] * delta[f];
+                    S[kf * dv + f] = S[kf * dv + f] + update;
+                }
+            }
+            for (f = 0; f < dv; ++f) {
+                float sum = 0.0f;
+                for (kf = 0; kf < dk; ++kf) {
+                    float product = S[kf * dv + f] * qh[kf];
+                    sum = sum + product;
+                }
+                core[h * dv + f] = sum;
+            }
+        }
+        for (i = 0; i < rec_n; ++i)
+            if (!isfinite(rec[i])) { status = KQO_NUMERIC_DOMAIN; break; }
+        if (status != KQO_OK) break;
+        /* gated RMSNorm (:787-815): norm weight applied directly */
+        for (i = 0; i < Vd; ++i) sg[i] = kqo_sigmoid(gate[i]);
+        for (h = 0; h < Hv; ++h) {
+            float sum = 0.0f, inv;
+            float *cr = core + h * dv;
+            for (f = 0; f < dv; ++f) {
+                float sq = cr[f] * cr[f];
+                sum = sum + sq;
+            }
+            sum = sum / (float)dv;
+            inv = 1.0f / sqrtf(sum + dm->rms_norm_epsilon);
+            for (f = 0; f < dv; ++f) {
+                float nrm = cr[f] * inv;
+                float wt = w->norm[f] * nrm;
+                cr[f] = wt * sg[h * dv + f];
+            }
+        }
+        /* output projection (:826-831) */
+        for (i = 0; i < H; ++i) {
+            y[i] = kqo_dot(w->output + i * Vd, core, Vd);
+            if (!isfinite(y[i])) { status = KQO_NUMERIC_DOMAIN; break; }
+        }
+        if (status != KQO_OK) break;
+        memcpy(output + t * H, y, sizeof(float) * H);
+    }
+    if (status == KQO_OK) {
+        memcpy(conv_state, conv, sizeof(float) * conv_n);
+        memcpy(recurrent_state, rec, sizeof(float) * rec_n);
+    }
+    free(ws);
+    return status;
+}
+
+/* ------------------------------------------------------------------- QSA */
+
+/* (1 + w) RMSNorm: src/kq_qsa_qwen38.c:231-256. */
+static int kqo_qsa_norm(float *x, uint64_t n, const float *dw, float eps) {
+    float sum = 0.0f, inv;
+    uint64_t i;
+    for (i = 0; i < n; ++i) {
+        float sq = x[i] * x[i];
+        sum = sum + sq;
+    }
+    sum = sum / (float)n;
+    inv = 1.0f / sqrtf(sum + eps);
+    if (!isfinite(inv)) return KQO_NUMERIC_DOMAIN;
+    for (i = 0; i < n; ++i) {
+        x[i] = (x[i] * inv) * (1.0f + dw[i]);
+        if (!isfinite(x[i])) return KQO_NUMERIC_DOMAIN;
+    }
+    return KQO_OK;
+}
+
+/* NeoX half rotation on the first `rot` dims: src/kq_qsa_qwen38.c:258-281. */
+static int kqo_rope(float *x, uint32_t rot, float theta, uint64_t pos) {
+    uint32_t half = rot / 2U, i;
+    for (i = 0; i < half; ++i) {
+        float e = (2.0f * (float)i) / (float)rot;
+        float freq = 1.0f / powf(theta, e);
+        float ang = (float)pos * freq;
+        float cs = cosf(ang), sn = sinf(ang);
+        float a = x[i], b = x[i + half];
+        x[i] = a * cs - b * sn;
+        x[i + half] = b * cs + a * sn;
+        if (!isfinite(x[i]) || !isfinite(x[i + half])) return KQO_NUMERIC_DOMAIN;
+    }
+    return KQO_OK;
+}
+
+uint64_t kqo_select_blocks(const float *scores, uint64_t count, uint64_t limit,
+                           uint32_t *sel) {
+    uint64_t n = 0, cand;
+    for (cand = 0; cand < count; ++cand) {
+        uint64_t pos = 0;
+        while (pos < n) {
+            float cs = scores[cand], ps = scores[sel[pos]];
+            int better = cs > ps || (cs == ps && (uint32_t)cand < sel[pos]);
+            if (better) break;
+            pos += 1;
+        }
+        if (pos < limit) {
+            uint64_t end = n < limit ? n : limit - 1U;
+            while (end > pos) { sel[end] = sel[end - 1]; end -= 1; }
+            sel[pos] = (uint32_t)cand;
+            if (n < limit) n += 1;
+        }
+    }
+    return n;
+}
+
+/* Per-token loop of src/kq_qsa_qwen38.c:524-828 over F32 weights. */
+int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
+                const float *hidden, uint64_t tokens, float *output,
+                float *kc, float *vc, float *rc, uint64_t capacity,
+                uint64_t *length, uint32_t *sel_out, uint32_t *sel_counts,
+                float *scores_out) {
+    const uint64_t H = dm->hidden_size, Hq = dm->query_heads,
+                   Hkv = dm->kv_heads, d = dm->head_dim, Hi = dm->index_heads,
+                   di = dm->index_dim, blk = dm->block_size;
+    const uint64_t qw = Hq * d, kvw = Hkv * d, iqw = Hi * di;
+    const uint64_t topk = dm->token_budget / blk;
+    const uint64_t sel_cap = dm->token_budget + blk - 1U;
+    const uint64_t rep = Hq / Hkv;
+    const uint64_t max_blocks = capacity / blk;
+    uint64_t L0, t;
+    float *qg, *q, *kk, *vv, *iq, *rk, *bk, *sc, *logit, *ctx, *y, *staged;
+    uint32_t *sel, *tok;
+    int st = KQO_OK;
+
+    if (length == NULL || *length + tokens > capacity || Hkv == 0U ||
+        blk == 0U || Hq % Hkv)
+        return KQO_LIMIT_EXCEEDED;
+    L0 = *length;
+    qg = (float *)malloc(sizeof(float) * (2 * qw + qw + kvw + kvw + iqw + di +
+                                          max_blocks * di + max_blocks +
+                                          sel_cap + qw + H + tokens * H));
+    sel = (uint32_t *)malloc(sizeof(uint32_t) * (topk + sel_cap + 1));
+    if (qg == NULL || sel == NULL) { free(qg); free(sel); return KQO_INVALID_ARGUMENT; }
+    tok = sel + topk;
+    q = qg + 2 * qw;  kk = q + qw;   vv = kk + kvw;  iq = vv + kvw;
+    rk = iq + iqw;    bk = rk + di;  sc = bk + max_blocks * di;
+    logit = sc + max_blocks; ctx = logit + sel_cap; y = ctx + qw;
+    staged = y + H;
+
+    for (t = 0; t < tokens && st == KQO_OK; ++t) {
+        const float *x = hidden + t * H;
+        uint64_t pos = L0 + t, h, f, b, i, nblocks, tail, nsel, ntok = 0;
+        /* projections (:539-565); pending rows are written straight into the
+         * caches beyond the committed length, which is only advanced on
+         * success (equivalent to the reference's pending buffers) */
+        for (i = 0; i < 2 * qw; ++i) qg[i] = kqo_dot(w->query + i * H, x, H);
+        for (i = 0; i < kvw; ++i) kk[i] = kqo_dot(w->key + i * H, x, H);
+        for (i = 0; i < kvw; ++i) vv[i] = kqo_dot(w->value + i * H, x, H);
+        for (i = 0; i < iqw; ++i) iq[i] = kqo_dot(w->index_query + i * H, x, H);
+        for (i = 0; i < di; ++i) rk[i] = kqo_dot(w->index_key + i * H, x, H);
+        /* norms + RoPE (:567-602) */
+        for (h = 0; h < Hq && st == KQO_OK; ++h) {
+            memcpy(q + h * d, qg + h * 2 * d, sizeof(float) * d);
+            st = kqo_qsa_norm(q + h * d, d, w->query_norm, dm->rms_norm_epsilon);
+            if (st == KQO_OK) st = kqo_rope(q + h * d, dm->rotary_dim, dm->rope_theta, pos);
+        }
+        for (h = 0; h < Hkv && st == KQO_OK; ++h) {
+            st = kqo_qsa_norm(kk + h * d, d, w->key_norm, dm->rms_norm_epsilon);
+            if (st == KQO_OK) st = kqo_rope(kk + h * d, dm->rotary_dim, dm->rope_theta, pos);
+        }
+        for (h = 0; h < Hi && st == KQO_OK; ++h) {
+            st = kqo_qsa_norm(iq + h * di, di, w->index_query_norm, dm->rms_norm_epsilon);
+            if (st == KQO_OK) st = kqo_rope(iq + h * di, dm->rotary_dim, dm->rope_theta, pos);
+        }
+        if (st != KQO_OK) break;
+        memcpy(kc + pos * kvw, kk, sizeof(float) * kvw);
+        memcpy(vc + pos * kvw, vv, sizeof(float) * kvw);
+        memcpy(rc + pos * di, rk, sizeof(float) * di);
+        /* block indexer over all complete blocks (:608-648) */
+        nblocks = (pos + 1) / blk;
+        tail = (pos + 1) % blk;
+        for (b = 0; b < nblocks && st == KQO_OK; ++b) {
+            float *key = bk + b * di, score = 0.0f;
+            for (f = 0; f < di; ++f) {
+                float sum = 0.0f;
+                for (i = 0; i < blk; ++i) sum = sum + rc[(b * blk + i) * di + f];
+                key[f] = sum / (float)blk;
+            }
+            st = kqo_qsa_norm(key, di, w->index_key_norm, dm->rms_norm_epsilon);
+            if (st == KQO_OK) st = kqo_rope(key, dm->rotary_dim, dm->rope_theta, b * blk);
+            if (st != KQO_OK) break;
+            for (h = 0; h < Hi; ++h) {
+                float dot = kqo_dot(iq + h * di, key, di);
+                if (dot > 0.0f) score = score + dot;
+            }
+            score = score / sqrtf((float)di);
+            if (!isfinite(score)) { st = KQO_NUMERIC_DOMAIN; break; }
+            sc[b] = score;
+        }
+        if (st != KQO_OK) break;
+        nsel = kqo_select_blocks(sc, nblocks, nblocks < topk ? nblocks : topk, sel);
+        for (b = 0; b < nsel; ++b)
+            for (i = 0; i < blk; ++i) tok[ntok++] = (uint32_t)(sel[b] * blk + i);
+        for (i = 0; i < tail; ++i) tok[ntok++] = (uint32_t)(nblocks * blk + i);
+        if (sel_out != NULL) {
+            memset(sel_out + t * topk, 0, sizeof(uint32_t) * topk);
+            memcpy(sel_out + t * topk, sel, sizeof(uint32_t) * nsel);
+        }
+        if (sel_counts != NULL) sel_counts[t] = (uint32_t)nsel;
+        if (scores_out != NULL && nblocks > 0)
+            memcpy(scores_out + t * max_blocks, sc, sizeof(float) * nblocks);
+        /* sparse softmax attention (:716-773) */
+        for (h = 0; h < Hq; ++h) {
+            uint64_t kvh = h / rep, s;
+            float mx = -INFINITY, sum = 0.0f;
+            for (s = 0; s < ntok; ++s) {
+                const float *krow = kc + (uint64_t)tok[s] * kvw + kvh * d;
+                float dot = 0.0f;
+                for (f = 0; f < d; ++f) dot = dot + q[h * d + f] * krow[f];
+                dot = dot / sqrtf((float)d);
+                logit[s] = dot;
+                if (dot > mx) mx = dot;
+            }
+            for (s = 0; s < ntok; ++s) {
+                float p = expf(logit[s] - mx);
+                logit[s] = p;
+                sum = sum + p;
+            }
+            if (!(sum > 0.0f) || !isfinite(sum)) { st = KQO_NUMERIC_DOMAIN; break; }
+            for (s = 0; s < ntok; ++s) logit[s] /= sum;
+            for (f = 0; f < d; ++f) {
+                float acc = 0.0f;
+                for (s = 0; s < ntok; ++s)
+                    acc = acc + logit[s] * vc[(uint64_t)tok[s] * kvw + kvh * d + f];
+                ctx[h * d + f] = acc;
+            }
+        }
+        if (st != KQO_OK) break;
+        /* sigmoid output gate (:774-782), simple form */
+        for (h = 0; h < Hq; ++h)
+            for (f = 0; f < d; ++f) {
+                float gt = qg[h * 2 * d + d + f];
+                float sg = 1.0f / (1.0f + expf(-gt));
+                ctx[h * d + f] = ctx[h * d + f] * sg;
+            }
+        for (i = 0; i < H; ++i) {
+            y[i] = kqo_dot(w->output + i * qw, ctx, qw);
+            if (!isfinite(y[i])) { st = KQO_NUMERIC_DOMAIN; break; }
+        }
+        if (st != KQO_OK) break;
+        memcpy(staged + t * H, y, sizeof(float) * H);
+    }
+    if (st == KQO_OK) {
+        memcpy(output, staged, sizeof(float) * tokens * H);
+        *length = L0 + tokens;
+    }
+    free(qg);
+    free(sel);
+    return st;
+}

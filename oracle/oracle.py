@@ -1,0 +1,342 @@
+"""ctypes wrapper of the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+Two implementations of the reference algorithm, selected by ``impl``:
+
+  "port"       oracle/_build/libkqoracle.so — this repository's C restatement
+               (kq_oracle.c), including Q6_K which the reference lacks;
+  "reference"  oracle/_ref/libkqref.so — Kestrel-Q's own hot-path C sources
+               compiled from the reference tree by ``make -C oracle ref``.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module; the product library never does.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+PORT_LIB = HERE / "_build" / "libkqoracle.so"
+REF_LIB = HERE / "_ref" / "libkqref.so"
+
+u32, u64, f32, vp = C.c_uint32, C.c_uint64, C.c_float, C.c_void_p
+
+GEOMETRY = {0: (1, 4), 30: (1, 2), 8: (32, 34), 12: (256, 144), 14: (256, 210)}
+
+
+class _GdnDims(C.Structure):   # kqo_gdn_dims
+    _fields_ = [("hidden_size", u32), ("key_heads", u32), ("value_heads", u32), ("key_dim", u32),
+                ("value_dim", u32), ("conv_kernel", u32), ("rms_norm_epsilon", f32)]
+
+
+class _GdnWeights(C.Structure):   # kqo_gdn_weights
+    _fields_ = [(n, vp) for n in ["a_log", "conv", "dt_bias", "alpha", "beta", "qkv", "gate", "norm", "output"]]
+
+
+class _QsaDims(C.Structure):   # kqo_qsa_dims
+    _fields_ = [("hidden_size", u32), ("query_heads", u32), ("kv_heads", u32), ("head_dim", u32),
+                ("index_heads", u32), ("index_dim", u32), ("block_size", u32), ("token_budget", u32),
+                ("rotary_dim", u32), ("rms_norm_epsilon", f32), ("rope_theta", f32)]
+
+
+QSA_FIELDS = ["query", "key", "value", "output", "query_norm", "key_norm", "index_query", "index_key",
+              "index_query_norm", "index_key_norm"]
+GDN_FIELDS = ["a_log", "conv", "dt_bias", "alpha", "beta", "qkv", "gate", "norm", "output"]
+
+
+class _QsaWeights(C.Structure):   # kqo_qsa_weights
+    _fields_ = [(n, vp) for n in QSA_FIELDS]
+
+
+# reference ABI structures (Kestrel-Q src/kq_gdn_internal.h:11-20,
+# src/kq_qsa_internal.h:11-25, include/kq_gdn.h:64-83, include/kq_qsa.h:82-103)
+class _RefGdnDims(C.Structure):
+    _fields_ = [("hidden_size", u32), ("key_head_count", u32), ("value_head_count", u32),
+                ("key_head_dimension", u32), ("value_head_dimension", u32), ("conv_kernel_size", u32),
+                ("rms_norm_epsilon", f32), ("activation_dtype", C.c_int)]
+
+
+class _RefQsaDims(C.Structure):
+    _fields_ = [("hidden_size", u32), ("query_head_count", u32), ("key_value_head_count", u32),
+                ("head_dimension", u32), ("index_query_head_count", u32), ("index_head_dimension", u32),
+                ("block_size", u32), ("token_budget", u32), ("max_context", u32), ("rotary_dimension", u32),
+                ("rms_norm_epsilon", f32), ("rope_theta", f32), ("activation_dtype", C.c_int)]
+
+
+def _pairs(names):
+    out = []
+    for n in names:
+        out += [(n, vp), (n + "_count", u64)]
+    return out
+
+
+class _RefGdnWeights(C.Structure):
+    _fields_ = _pairs(GDN_FIELDS)
+
+
+class _RefQsaWeights(C.Structure):
+    _fields_ = _pairs(QSA_FIELDS)
+
+
+class _Diag(C.Structure):
+    _fields_ = [("status", C.c_int), ("message", C.c_char * 256)]
+
+
+class _RefSelection(C.Structure):
+    _fields_ = [("token_index", u64), ("absolute_position", u64), ("candidate_block_ids", C.POINTER(u32)),
+                ("candidate_scores", C.POINTER(f32)), ("candidate_count", u64),
+                ("selected_block_ids", C.POINTER(u32)), ("selected_block_count", u64),
+                ("selected_token_positions", C.POINTER(u32)), ("selected_token_count", u64),
+                ("tail_count", u64)]
+
+
+_SEL_CB = C.CFUNCTYPE(None, C.POINTER(_RefSelection), vp)
+_port = None
+_ref = None
+
+
+def build() -> None:
+    """Builds the restatement, and the reference when its sources are present."""
+    subprocess.run(["make", "-s", "-C", str(HERE), "port"], check=True)
+    if Path("/root/reference/src/kq_gdn.c").exists():
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+
+
+def port():
+    global _port
+    if _port is None:
+        if not PORT_LIB.exists():
+            build()
+        _port = C.CDLL(str(PORT_LIB))
+    return _port
+
+
+def ref_available() -> bool:
+    return REF_LIB.exists()
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        if not REF_LIB.exists():
+            raise RuntimeError("reference oracle not built (make -C oracle ref)")
+        _ref = C.CDLL(str(REF_LIB))
+    return _ref
+
+
+def _a(x) -> np.ndarray:
+    return np.ascontiguousarray(x, dtype=np.float32)
+
+
+# ------------------------------------------------------------------ numerics
+
+def dequantize(type_id: int, packed: np.ndarray, impl: str = "port") -> np.ndarray:
+    be, bb = GEOMETRY[type_id]
+    data = np.ascontiguousarray(packed, np.uint8)
+    n = data.size // bb * be
+    out = np.empty(n, np.float32)
+    if impl == "port":
+        st = port().kqo_dequantize(u32(type_id), data.ctypes.data_as(vp), u64(data.size),
+                                   out.ctypes.data_as(vp), u64(n))
+    else:
+        cnt = u64()
+        d = _Diag()
+        st = ref().kq_dequantize_blocks_f32(u32(type_id), data.ctypes.data_as(vp), u64(data.size),
+                                            out.ctypes.data_as(vp), u64(n), C.byref(cnt), C.byref(d))
+    if st != 0:
+        raise RuntimeError(f"oracle dequantize failed: {st}")
+    return out
+
+
+def matvec(type_id: int, packed: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    """y[b, r] in the reference's sequential row-dot order."""
+    xv = _a(x).reshape(-1, cols)
+    y = np.empty((xv.shape[0], rows), np.float32)
+    data = np.ascontiguousarray(packed, np.uint8)
+    st = port().kqo_matvec(u32(type_id), data.ctypes.data_as(vp), u64(rows), u64(cols),
+                           xv.ctypes.data_as(vp), u64(xv.shape[0]), y.ctypes.data_as(vp))
+    if st != 0:
+        raise RuntimeError(f"oracle matvec failed: {st}")
+    return y
+
+
+def row_dot_ref(type_id: int, packed: np.ndarray, x: np.ndarray) -> float:
+    data = np.ascontiguousarray(packed, np.uint8)
+    xv = _a(x)
+    out = f32()
+    d = _Diag()
+    st = ref().kq_quantized_row_dot_f32(u32(type_id), data.ctypes.data_as(vp), u64(data.size),
+                                        xv.ctypes.data_as(vp), u64(xv.size), C.byref(out), C.byref(d))
+    if st != 0:
+        raise RuntimeError(f"reference row dot failed: {st} {d.message}")
+    return out.value
+
+
+# ------------------------------------------------------------------ GDN
+
+def gdn_run(dims, w: dict, x: np.ndarray, conv: np.ndarray, rec: np.ndarray, mask=None, impl: str = "port"):
+    """Runs T tokens; returns (status, y[T,H], conv', rec')."""
+    xv = _a(x).reshape(-1, dims.hidden)
+    T = xv.shape[0]
+    y = np.zeros((T, dims.hidden), np.float32)
+    conv2, rec2 = _a(conv).copy(), _a(rec).copy()
+    ws = {k: _a(w[k]) for k in GDN_FIELDS}
+    m = None if mask is None else np.ascontiguousarray(mask, np.uint8)
+    if impl == "port":
+        gd = _GdnDims(dims.hidden, dims.key_heads, dims.value_heads, dims.key_dim, dims.value_dim,
+                      dims.conv_kernel, dims.eps)
+        gw = _GdnWeights(*[ws[k].ctypes.data for k in GDN_FIELDS])
+        st = port().kqo_gdn_run(C.byref(gd), C.byref(gw), xv.ctypes.data_as(vp), u64(T),
+                                None if m is None else m.ctypes.data_as(vp), y.ctypes.data_as(vp),
+                                conv2.ctypes.data_as(vp), rec2.ctypes.data_as(vp))
+        return st, y, conv2, rec2
+    L = ref()
+    gd = _RefGdnDims(dims.hidden, dims.key_heads, dims.value_heads, dims.key_dim, dims.value_dim,
+                     dims.conv_kernel, dims.eps, 0)
+    cfg, state = vp(), vp()
+    d = _Diag()
+    if L.kq_gdn_test_config_create(C.byref(gd), C.byref(cfg), C.byref(d)) != 0:
+        raise RuntimeError(d.message)
+    try:
+        if L.kq_gdn_state_create(cfg, C.byref(state), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        init = 0 if (not conv2.any() and not rec2.any()) else 1
+        st = L.kq_gdn_state_import_f32(state, conv2.ctypes.data_as(vp), u64(conv2.size), rec2.ctypes.data_as(vp),
+                                       u64(rec2.size), C.c_int(init), C.byref(d))
+        if st != 0:
+            raise RuntimeError(d.message)
+        L.kq_gdn_config_scratch_bytes.restype = u64
+        sb = L.kq_gdn_config_scratch_bytes(cfg)
+        scratch = np.empty(sb // 4 + 1, np.float32)
+        gw = _RefGdnWeights()
+        for k in GDN_FIELDS:
+            setattr(gw, k, ws[k].ctypes.data)
+            setattr(gw, k + "_count", ws[k].size)
+        st = L.kq_gdn_prefill_f32(cfg, C.byref(gw), xv.ctypes.data_as(vp), u64(T),
+                                  None if m is None else m.ctypes.data_as(vp), y.ctypes.data_as(vp), u64(y.size),
+                                  state, scratch.ctypes.data_as(vp), u64(sb), None, None, C.byref(d))
+        init_out = C.c_int()
+        L.kq_gdn_state_export_f32(state, conv2.ctypes.data_as(vp), u64(conv2.size), rec2.ctypes.data_as(vp),
+                                  u64(rec2.size), C.byref(init_out), C.byref(d))
+        return st, y, conv2, rec2
+    finally:
+        if state:
+            L.kq_gdn_state_close(state)
+        L.kq_gdn_config_close(cfg)
+
+
+# ------------------------------------------------------------------ QSA
+
+def qsa_run(dims, w: dict, x: np.ndarray, key: np.ndarray, value: np.ndarray, raw: np.ndarray, length: int,
+            capacity: int, impl: str = "port"):
+    """Runs T tokens on caches holding `length` prior rows.
+
+    Returns (status, y[T,H], key', value', raw', new_length, selections) with
+    one selection dict per token (scores, selected block ids)."""
+    xv = _a(x).reshape(-1, dims.hidden)
+    T = xv.shape[0]
+    y = np.zeros((T, dims.hidden), np.float32)
+    kc = np.zeros((capacity, dims.kv_width), np.float32)
+    vc = np.zeros((capacity, dims.kv_width), np.float32)
+    rc = np.zeros((capacity, dims.index_dim), np.float32)
+    kc[:length], vc[:length], rc[:length] = key[:length], value[:length], raw[:length]
+    ws = {k: _a(w[k]) for k in QSA_FIELDS}
+    topk = dims.budget // dims.block
+    max_blocks = capacity // dims.block
+    sels = []
+    if impl == "port":
+        qd = _QsaDims(dims.hidden, dims.query_heads, dims.kv_heads, dims.head_dim, dims.index_heads, dims.index_dim,
+                      dims.block, dims.budget, dims.rotary, dims.eps, dims.theta)
+        qw = _QsaWeights(*[ws[k].ctypes.data for k in QSA_FIELDS])
+        ln = u64(length)
+        sel = np.zeros((T, topk), np.uint32)
+        cnt = np.zeros(T, np.uint32)
+        scores = np.zeros((T, max(1, max_blocks)), np.float32)
+        st = port().kqo_qsa_run(C.byref(qd), C.byref(qw), xv.ctypes.data_as(vp), u64(T), y.ctypes.data_as(vp),
+                                kc.ctypes.data_as(vp), vc.ctypes.data_as(vp), rc.ctypes.data_as(vp), u64(capacity),
+                                C.byref(ln), sel.ctypes.data_as(vp), cnt.ctypes.data_as(vp),
+                                scores.ctypes.data_as(vp))
+        for t in range(T):
+            nb = (length + t + 1) // dims.block
+            sels.append({"scores": scores[t, :nb].copy(), "selected": sel[t, :cnt[t]].copy()})
+        n = ln.value
+        return st, y, kc[:n], vc[:n], rc[:n], n, sels
+    L = ref()
+    qd = _RefQsaDims(dims.hidden, dims.query_heads, dims.kv_heads, dims.head_dim, dims.index_heads, dims.index_dim,
+                     dims.block, dims.budget, max(capacity, dims.max_context if dims.max_context else capacity),
+                     dims.rotary, dims.eps, dims.theta, 0)
+    cfg, state = vp(), vp()
+    d = _Diag()
+    if L.kq_qsa_test_config_create(C.byref(qd), C.byref(cfg), C.byref(d)) != 0:
+        raise RuntimeError(d.message)
+    try:
+        if L.kq_qsa_state_create(cfg, u64(capacity), C.byref(state), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        st = L.kq_qsa_state_import_f32(state, kc.ctypes.data_as(vp), u64(length * dims.kv_width),
+                                       vc.ctypes.data_as(vp), u64(length * dims.kv_width), rc.ctypes.data_as(vp),
+                                       u64(length * dims.index_dim), u64(length), C.byref(d))
+        if st != 0:
+            raise RuntimeError(d.message)
+        need = u64()
+        L.kq_qsa_required_scratch_bytes(cfg, state, u64(T), C.byref(need), C.byref(d))
+        scratch = np.empty(need.value // 4 + 1, np.float32)
+        qw = _RefQsaWeights()
+        for k in QSA_FIELDS:
+            setattr(qw, k, ws[k].ctypes.data)
+            setattr(qw, k + "_count", ws[k].size)
+
+        def on_sel(p, _u):
+            s = p.contents
+            nb = s.candidate_count
+            sels.append({"scores": np.ctypeslib.as_array(s.candidate_scores, (nb,)).copy() if nb else
+                         np.zeros(0, np.float32),
+                         "selected": np.ctypeslib.as_array(s.selected_block_ids, (s.selected_block_count,)).copy()
+                         if s.selected_block_count else np.zeros(0, np.uint32)})
+
+        cb = _SEL_CB(on_sel)
+        st = L.kq_qsa_prefill_f32(cfg, C.byref(qw), xv.ctypes.data_as(vp), u64(T), y.ctypes.data_as(vp),
+                                  u64(y.size), state, scratch.ctypes.data_as(vp), need, cb, None, None, C.byref(d))
+        ln = u64()
+        L.kq_qsa_state_length.restype = u64
+        n = L.kq_qsa_state_length(state)
+        k2 = np.zeros((max(n, 1), dims.kv_width), np.float32)
+        v2 = np.zeros_like(k2)
+        r2 = np.zeros((max(n, 1), dims.index_dim), np.float32)
+        L.kq_qsa_state_export_f32(state, k2.ctypes.data_as(vp), u64(k2.size), v2.ctypes.data_as(vp), u64(v2.size),
+                                  r2.ctypes.data_as(vp), u64(r2.size), C.byref(ln), C.byref(d))
+        return st, y, k2[:n], v2[:n], r2[:n], n, sels
+    finally:
+        if state:
+            L.kq_qsa_state_close(state)
+        L.kq_qsa_config_close(cfg)
+
+
+def select_blocks(scores: np.ndarray, limit: int) -> np.ndarray:
+    s = _a(scores)
+    out = np.zeros(max(1, limit), np.uint32)
+    port().kqo_select_blocks.restype = u64
+    n = port().kqo_select_blocks(s.ctypes.data_as(vp), u64(s.size), u64(limit), out.ctypes.data_as(vp))
+    return out[:n]
+
+
+# ------------------------------------------------------------------ helpers
+
+def gdn_weights_f32(layer) -> dict:
+    """Canonical F32 weights of a synth.GdnLayerWeights (dequantised here)."""
+    def dq(t):
+        return dequantize(t.type_id, t.data).reshape(t.rows, t.cols)
+    return {"a_log": layer.a_log, "conv": layer.conv, "dt_bias": layer.dt_bias, "alpha": dq(layer.alpha),
+            "beta": dq(layer.beta), "qkv": dq(layer.qkv), "gate": dq(layer.gate), "norm": layer.norm,
+            "output": dq(layer.output)}
+
+
+def qsa_weights_f32(layer) -> dict:
+    def dq(t):
+        return dequantize(t.type_id, t.data).reshape(t.rows, t.cols)
+    return {"query": dq(layer.query), "key": dq(layer.key), "value": dq(layer.value), "output": dq(layer.output),
+            "query_norm": layer.query_norm, "key_norm": layer.key_norm, "index_query": dq(layer.index_query),
+            "index_key": dq(layer.index_key), "index_query_norm": layer.index_query_norm,
+            "index_key_norm": layer.index_key_norm}

@@ -1,0 +1,155 @@
+"""C-ABI library checks that need no GPU: it loads, exports every entry point
+the headers in include/ declare, and its host-only entry points (status text,
+block geometry, argument validation) behave like the reference's
+(tests/numeric_test.c, tests/tensor_view_test.c of Kestrel-Q)."""
+import ctypes as C
+import re
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def declared_functions():
+    names = set()
+    for h in sorted((REPO / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        text = re.sub(r"typedef[^;]*;", "", text)
+        for m in re.finditer(r"\b(kq_\w+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_exports_every_declared_function(kq):
+    lib = kq.lib()
+    names = declared_functions()
+    assert len(names) > 80
+    missing = [n for n in sorted(names) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_only_abi_symbols_are_exported(kq):
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", str(kq.abi.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    exported = [l.split()[-1] for l in out.splitlines() if " T " in l]
+    assert exported and all(e.startswith("kq_") for e in exported)
+
+
+def test_status_strings(kq):
+    lib = kq.lib()
+    assert lib.kq_status_string(0) == b"ok"
+    assert lib.kq_status_string(39) == b"invalid numeric domain"
+    assert lib.kq_status_string(32) == b"output buffer too small"
+    assert lib.kq_status_string(9999) == b"unknown status"
+
+
+@pytest.mark.parametrize("type_id,elems,nbytes", [(0, 1, 4), (30, 1, 2), (8, 32, 34), (12, 256, 144),
+                                                   (14, 256, 210), (13, 256, 176), (7, 32, 24), (20, 32, 18)])
+def test_quant_geometry(kq, type_id, elems, nbytes):
+    g = kq.abi.QuantGeometry()
+    d = kq.abi.Diagnostic()
+    assert kq.lib().kq_quant_geometry_for_type(type_id, C.byref(g), C.byref(d)) == 0
+    assert (g.type_id, g.block_elements, g.bytes_per_block) == (type_id, elems, nbytes)
+
+
+def test_quant_geometry_rejects_unknown(kq):
+    g = kq.abi.QuantGeometry()
+    d = kq.abi.Diagnostic()
+    assert kq.lib().kq_quant_geometry_for_type(3, C.byref(g), C.byref(d)) == kq.abi.UNSUPPORTED_TENSOR_TYPE
+    assert kq.lib().kq_quant_geometry_for_type(0, None, C.byref(d)) == kq.abi.INVALID_ARGUMENT
+
+
+def test_packed_size_and_spans(kq):
+    lib, abi = kq.lib(), kq.abi
+    d = abi.Diagnostic()
+    out = C.c_uint64()
+    assert lib.kq_quant_packed_size(14, 2048, C.byref(out), C.byref(d)) == 0 and out.value == 8 * 210
+    assert lib.kq_quant_packed_size(12, 100, C.byref(out), C.byref(d)) == abi.INVALID_QUANTIZED_GEOMETRY
+    b, e = C.c_uint64(), C.c_uint64()
+    assert lib.kq_quant_element_to_block(8, 128, 70, C.byref(b), C.byref(e), C.byref(d)) == 0
+    assert (b.value, e.value) == (2, 6)
+    assert lib.kq_quant_element_to_block(8, 128, 128, C.byref(b), C.byref(e), C.byref(d)) == abi.SPAN_OUT_OF_RANGE
+    span = abi.QuantBlockSpan()
+    assert lib.kq_quant_range_to_blocks(12, 1024, 300, 300, C.byref(span), C.byref(d)) == 0
+    assert (span.first_block, span.block_count, span.physical_byte_offset, span.physical_byte_length,
+            span.leading_elements, span.trailing_elements) == (1, 2, 144, 288, 44, 168)
+    assert lib.kq_quant_range_to_blocks(12, 1024, 1000, 100, C.byref(span), C.byref(d)) == abi.SPAN_OUT_OF_RANGE
+
+
+def test_model_entry_points_report_unsupported(kq):
+    lib, abi = kq.lib(), kq.abi
+    d = abi.Diagnostic()
+    out = C.c_void_p(1)
+    assert lib.kq_gdn_config_create(None, 0, C.byref(out), C.byref(d)) == abi.UNSUPPORTED_MODEL
+    assert out.value is None
+    assert lib.kq_weight_provider_open(None, None, 0, C.byref(out), C.byref(d)) == abi.UNSUPPORTED_MODEL
+
+
+def test_gdn_config_geometry_matches_reference_accounting(kq):
+    """Config sizes of tests/gdn_test.c:336-338 (target geometry) and the
+    scratch formula of src/kq_gdn.c:184-219."""
+    lib, abi = kq.lib(), kq.abi
+    dims = abi.GdnDimensions(2560, 16, 48, 128, 128, 4, 1e-6, 0)
+    cfg = C.c_void_p()
+    d = abi.Diagnostic()
+    assert lib.kq_gdn_test_config_create(C.byref(dims), C.byref(cfg), C.byref(d)) == 0
+    try:
+        assert lib.kq_gdn_config_recurrent_element_count(cfg) == 786432
+        assert lib.kq_gdn_config_conv_state_element_count(cfg) == 40960
+        C_, V, Hv, H, rk = 10240, 6144, 48, 2560, 48 * 128
+        tok = H + C_ + V + Hv + Hv + C_ + rk + rk + V + Hv + Hv + V + V + V + V + H
+        assert lib.kq_gdn_config_token_scratch_bytes(cfg) == tok * 4
+        assert lib.kq_gdn_config_scratch_bytes(cfg) == (tok + 786432 + 40960) * 4
+        assert lib.kq_gdn_config_dequant_scratch_bytes(cfg) == 1024
+    finally:
+        lib.kq_gdn_config_close(cfg)
+    bad = abi.GdnDimensions(8, 2, 3, 4, 4, 4, 1e-6, 0)   # value heads not a multiple of key heads
+    assert lib.kq_gdn_test_config_create(C.byref(bad), C.byref(cfg), C.byref(d)) == abi.INCOMPATIBLE_GDN
+    bad = abi.GdnDimensions(8, 2, 4, 4, 4, 3, 1e-6, 0)   # kernel must be 4
+    assert lib.kq_gdn_test_config_create(C.byref(bad), C.byref(cfg), C.byref(d)) == abi.INCOMPATIBLE_GDN
+
+
+def test_qsa_config_geometry(kq):
+    lib, abi = kq.lib(), kq.abi
+    dims = abi.QsaDimensions(2048, 16, 2, 256, 4, 128, 4, 2048, 262144, 64, 1e-6, 1e7, 0)
+    cfg = C.c_void_p()
+    d = abi.Diagnostic()
+    assert lib.kq_qsa_test_config_create(C.byref(dims), C.byref(cfg), C.byref(d)) == 0
+    try:
+        assert lib.kq_qsa_config_block_selection_limit(cfg) == 512
+        # (2 * 2 * 256 + 128) * 4 bytes per token (F32 descriptor)
+        assert lib.kq_qsa_config_semantic_state_bytes_per_token(cfg) == (1024 + 128) * 4
+    finally:
+        lib.kq_qsa_config_close(cfg)
+    bad = abi.QsaDimensions(8, 2, 1, 4, 2, 4, 4, 6, 16, 2, 1e-6, 1e7, 0)   # budget % block != 0
+    assert lib.kq_qsa_test_config_create(C.byref(bad), C.byref(cfg), C.byref(d)) == abi.INCOMPATIBLE_QSA
+
+
+def test_selection_helper_tie_order(kq):
+    """kq_qsa_select_blocks_f32: (score desc, id asc), tests/qsa_test.c:203-209."""
+    import numpy as np
+    lib, abi = kq.lib(), kq.abi
+    s = np.array([0.5, 1.0, 1.0, -0.0, 0.0, 2.0], np.float32)
+    out = np.zeros(4, np.uint32)
+    n = C.c_uint64()
+    d = abi.Diagnostic()
+    assert lib.kq_qsa_select_blocks_f32(s.ctypes.data, s.size, 4, out.ctypes.data, 4, C.byref(n), C.byref(d)) == 0
+    assert n.value == 4 and list(out) == [5, 1, 2, 0]
+    assert lib.kq_qsa_select_blocks_f32(s.ctypes.data, s.size, 4, out.ctypes.data, 3, C.byref(n),
+                                        C.byref(d)) == abi.BUFFER_TOO_SMALL
+    s[2] = np.nan
+    assert lib.kq_qsa_select_blocks_f32(s.ctypes.data, s.size, 4, out.ctypes.data, 4, C.byref(n),
+                                        C.byref(d)) == abi.NUMERIC_DOMAIN
+
+
+def test_compute_entry_points_fail_loudly_without_gpu(kq):
+    from conftest import HAS_GPU
+    if HAS_GPU:
+        pytest.skip("GPU present")
+    lib, abi = kq.lib(), kq.abi
+    p = C.c_void_p()
+    d = abi.Diagnostic()
+    st = lib.kq_b200_provider_create(0, C.byref(p), C.byref(d))
+    assert st != 0 and p.value is None
