@@ -350,12 +350,9 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
         uint32_t before = 0;
         for (uint32_t w = 0; w < warp; ++w) before += warp_tot[w];
         uint32_t tie_rank = s_tie_base + before + before_in_warp;
-        if (above) {
+        if (above || (tie && tie_rank < ties_needed)) {
             uint32_t slot = atomicAdd(&s_taken, 1u);
-            cand[slot] = ((unsigned long long)key << 32) | (uint32_t)(~i);
-        } else if (tie && tie_rank < ties_needed) {
-            uint32_t slot = atomicAdd(&s_taken, 1u);
-            cand[slot] = ((unsigned long long)key << 32) | (uint32_t)(~i);
+            if (slot < kSelMax) cand[slot] = ((unsigned long long)key << 32) | (uint32_t)(~i);
         }
         __syncthreads();
         if (tid == 0) {
@@ -420,7 +417,7 @@ qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     const uint32_t pos = s.length;
     const uint32_t nblocks = (pos + 1) / d.block;
     const uint32_t tail = (pos + 1) % d.block;
-    const uint32_t ksel = selected_count[b];
+    const uint32_t ksel = min(selected_count[b], min(nblocks, d.topk));
     const uint32_t ntok = ksel * d.block + tail;
     const uint32_t per = (ntok + splits - 1) / splits;
     const uint32_t t0 = split * per, t1 = min(ntok, t0 + per);
@@ -446,9 +443,14 @@ qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     }
     const float scale = d.sqrt_head_dim;
     for (uint32_t i = t0 + warp; i < t1; i += 8) {
-        uint32_t tok = (i < ksel * d.block)
-                           ? selected[(size_t)b * d.topk + i / d.block] * d.block + i % d.block
-                           : nblocks * d.block + (i - ksel * d.block);
+        uint32_t tok;
+        if (i < ksel * d.block) {
+            const uint32_t blk = selected[(size_t)b * d.topk + i / d.block];
+            if (blk >= nblocks) continue;   // never taken: select raises an error first
+            tok = blk * d.block + i % d.block;
+        } else {
+            tok = nblocks * d.block + (i - ksel * d.block);
+        }
         const float *krow = s.key + (size_t)tok * kvw + kvh * hd;
         const float *vrow = s.value + (size_t)tok * kvw + kvh * hd;
         float kv[FPL], vv[FPL];
