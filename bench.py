@@ -262,7 +262,7 @@ def run_b200(args, rank, world, local_rank):
     gdn_w, qsa_w = layer_weights(rank)
     ctx = contexts(rank)
     B = BATCH
-    steps_total = args.warmup + 2 * args.steps + 4
+    steps_total = args.warmup + 2 * args.steps + 40
     prov = kqb200.Provider(local_rank)
     gdn_layers = [kqb200.GdnLayer(gd, w, prov, layer=l) for l, w in enumerate(gdn_w)]
     qsa_layer = kqb200.QsaLayer(qd, qsa_w, prov, layer=3)
@@ -339,6 +339,19 @@ def run_b200(args, rank, world, local_rank):
     lib.kq_b200_profile_read(C.byref(rec_n), C.byref(rec_ms))
     lib.kq_b200_profile_kernel(None)
 
+    breakdown = {}
+    if args.breakdown:
+        for fam in ("proj", "proj_exact", "gdn_conv", "gdn_recurrence", "qsa_prepare", "qsa_score",
+                    "qsa_select", "qsa_attend", "qsa_combine"):
+            lib.kq_b200_profile_kernel(fam.encode())
+            for _ in range(3):
+                step(x0, y0)
+            kqb200.synchronize()
+            n_, t_ = C.c_uint64(), C.c_double()
+            lib.kq_b200_profile_read(C.byref(n_), C.byref(t_))
+            breakdown[fam] = {"ms_per_step": t_.value / 3, "launches_per_step": n_.value / 3}
+        lib.kq_b200_profile_kernel(None)
+
     # ---- end-to-end: pinned host input -> block -> host result, every step
     xh = torch.randn(B, gd.hidden, generator=torch.Generator().manual_seed(5)).pin_memory()
     yh = torch.empty(B, gd.hidden).pin_memory()
@@ -411,6 +424,7 @@ def run_b200(args, rank, world, local_rank):
         "e2e": {"value": world * B * 1000.0 / e2e_ms, "unit": "tok/s",
                 "h2d_bytes_per_step": B * gd.hidden * 4, "d2h_bytes_per_step": B * gd.hidden * 4},
         "gpu_launches": int(launches),
+        **({"kernel_breakdown": breakdown} if breakdown else {}),
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -445,6 +459,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--breakdown", action="store_true", help="time every kernel family (extra steps)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

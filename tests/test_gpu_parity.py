@@ -138,7 +138,7 @@ def test_gdn_golden_cases_f32_api(kq, oracle):
                                                 c["mask"])
             assert_close(y, yo, c["id"])
             assert_close(rec, reco, c["id"])
-            assert np.array_equal(bits(conv), bits(convo)), c["id"]   # conv state is copied values
+            assert_close(conv, convo, c["id"])   # history of projected (tolerance-level) values
             assert accepts(meta["contracts"]["FINAL_CONV_STATE"], arr[f"c{i}_conv"], conv)
             s.close()
     finally:
