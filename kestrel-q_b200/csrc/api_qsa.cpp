@@ -195,11 +195,12 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     uint32_t max_blocks = 1;
     for (uint32_t b = 0; b < batch; ++b)
         max_blocks = std::max<uint32_t>(max_blocks, (uint32_t)((states[b]->length + tokens) / d.block));
-    uint32_t splits = (d.sel_capacity + 127) / 128;
-    uint32_t want_ctas = 2 * 148;
-    uint32_t per_seq = batch * d.kv_heads;
-    splits = std::max<uint32_t>(1, std::min<uint32_t>(std::max(splits, (want_ctas + per_seq - 1) / per_seq),
-                                                      (d.sel_capacity + 15) / 16));
+    // about 8 tiles of 32 selected tokens per split, and at least two waves
+    // of CTAs over the 148 SMs for small batches
+    const uint32_t tiles = (d.sel_capacity + 31) / 32;
+    const uint32_t per_seq = std::min<uint32_t>(batch, kMaxBatch) * d.kv_heads;
+    uint32_t splits = std::max<uint32_t>((tiles + 7) / 8, (2 * 148 + per_seq - 1) / per_seq);
+    splits = std::max<uint32_t>(1, std::min<uint32_t>(splits, tiles));
     const size_t need = Carve::round(items * ldp * 4) + Carve::round(items * ldi * 4) +
                         Carve::round(items * qw * 4) + Carve::round((size_t)batch * qw * 4) +
                         Carve::round((size_t)batch * d.index_heads * d.index_dim * 4) +

@@ -175,34 +175,73 @@ proj_warp_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
 
 // ------------------------------------------------------------ exact GEMV
 //
-// One thread per (row, batch row), k ascending, acc = acc + w*x with both
-// operations rounded separately: the reference's kq_f32_dot order
+// Every output is accumulated k = 0..K-1 from 0.0f as acc = acc + w*x with
+// both operations rounded separately: the reference's kq_f32_dot order
 // (src/kq_numeric.c:616-619).  Used for the QSA indexer projections so that
 // block selection is bit-identical to the reference.
+//
+// Layout: a CTA owns 16 rows x 32 batch rows; lane = batch row, so the
+// sequential chain of each output lives in one lane and a warp keeps four
+// independent chains (four rows) in flight.  Per 128-column chunk the
+// weights are decoded once into shared memory (read back as broadcasts) and
+// the activations are staged transposed (one conflict-free load per lane).
+
+constexpr int kExRows = 16;          // rows per CTA (4 per warp)
+constexpr int kExBatch = 32;         // batch rows per CTA (one per lane)
+constexpr int kExK = 128;            // columns per chunk
 
 __global__ void __launch_bounds__(128)
 proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                   float *__restrict__ y, uint32_t ldy, uint32_t batch,
                   ErrorWord err) {
-    extern __shared__ float xsh[];   // [cols] of this block's batch row
+    __shared__ __align__(16) float ws[kExRows][kExK];
+    __shared__ float xs[kExK][kExBatch + 1];
     if (error_raised(err)) return;
     int seg = 0;
     while (seg + 1 < segs.count && blockIdx.x >= segs.tile_start[seg + 1]) ++seg;
     const QMatrix m = segs.m[seg];
-    const uint32_t b = blockIdx.y;
-    for (uint32_t k = threadIdx.x; k < m.cols; k += blockDim.x) xsh[k] = x[(size_t)b * ldx + k];
-    __syncthreads();
-    const uint32_t row = (blockIdx.x - segs.tile_start[seg]) * blockDim.x + threadIdx.x;
-    if (row >= m.rows) return;
-    const uint8_t *wptr = m.data + (size_t)row * m.row_bytes;
-    float acc = 0.0f;
-    for (uint32_t base = 0; base < m.cols; base += 32u) {
-        float w[32];
-        uint32_t count = min(32u, m.cols - base);
-        decode_run(m.type, wptr, base, count, w);
-        for (uint32_t i = 0; i < count; ++i) acc = __fadd_rn(acc, __fmul_rn(w[i], xsh[base + i]));
+    const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * kExRows;
+    const uint32_t b0 = blockIdx.y * kExBatch;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (uint32_t k0 = 0; k0 < m.cols; k0 += kExK) {
+        const uint32_t kc = min((uint32_t)kExK, m.cols - k0);
+        // decode: thread t owns row t/8, 16-element run (t%8)*16 of the chunk
+        {
+            const int r = threadIdx.x >> 3, run = (threadIdx.x & 7) * 16;
+            const uint32_t grow = row0 + r;
+            float w[16];
+            uint32_t cnt = 0;
+            if ((uint32_t)run < kc) cnt = min(16u, kc - run);
+            if (grow < m.rows && cnt > 0)
+                decode_run(m.type, m.data + (size_t)grow * m.row_bytes, k0 + run, cnt, w);
+            for (int i = 0; i < 16; ++i) ws[r][run + i] = (grow < m.rows && (uint32_t)i < cnt) ? w[i] : 0.0f;
+        }
+        // activations, transposed: xs[k][b]
+        for (int idx = threadIdx.x; idx < kExBatch * kExK; idx += blockDim.x) {
+            const int bb = idx / kExK, kk = idx % kExK;
+            const uint32_t gb = b0 + bb;
+            xs[kk][bb] = (gb < batch && (uint32_t)kk < kc) ? x[(size_t)gb * ldx + k0 + kk] : 0.0f;
+        }
+        __syncthreads();
+        const float *w0 = ws[warp * 4 + 0], *w1 = ws[warp * 4 + 1];
+        const float *w2 = ws[warp * 4 + 2], *w3 = ws[warp * 4 + 3];
+        for (uint32_t k = 0; k < kc; ++k) {
+            const float xv = xs[k][lane];
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(w0[k], xv));
+            acc[1] = __fadd_rn(acc[1], __fmul_rn(w1[k], xv));
+            acc[2] = __fadd_rn(acc[2], __fmul_rn(w2[k], xv));
+            acc[3] = __fadd_rn(acc[3], __fmul_rn(w3[k], xv));
+        }
+        __syncthreads();
     }
-    y[(size_t)b * ldy + segs.out_offset[seg] + row] = acc;
+    const uint32_t b = b0 + lane;
+    if (b >= batch) return;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t row = row0 + warp * 4 + i;
+        if (row < m.rows) y[(size_t)b * ldy + segs.out_offset[seg] + row] = acc[i];
+    }
 }
 
 static void fill_tile_starts(ProjSegments &s, uint32_t unit) {
@@ -243,16 +282,9 @@ void launch_projection_exact(const ProjSegments &in, const float *x,
                              cudaStream_t stream) {
     ProjSegments segs = in;
     KernelTimer timer("proj_exact", stream);
-    fill_tile_starts(segs, 128);
-    uint32_t cols = 0;
-    for (int i = 0; i < segs.count; ++i) cols = std::max(cols, segs.m[i].cols);
-    dim3 grid(segs.tile_start[segs.count], batch);
-    size_t smem = (size_t)cols * sizeof(float);
-    if (smem > 48 * 1024) {
-        cudaFuncSetAttribute(proj_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-    }
-    proj_exact_kernel<<<grid, 128, smem, stream>>>(segs, x, ldx, y, ldy, batch, err);
+    fill_tile_starts(segs, kExRows);
+    dim3 grid(segs.tile_start[segs.count], (batch + kExBatch - 1) / kExBatch);
+    proj_exact_kernel<<<grid, 128, 0, stream>>>(segs, x, ldx, y, ldy, batch, err);
     count_launch();
 }
 

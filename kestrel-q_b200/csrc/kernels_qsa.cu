@@ -242,12 +242,20 @@ qsa_score_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ iq,
     const uint32_t ld = s.capacity / d.block;
     const float *key = s.block_keys + bi;
     float score = 0.0f;
-    for (uint32_t h = 0; h < d.index_heads; ++h) {
-        const float *q = qsh + h * d.index_dim;
-        float dot = 0.0f;
-        for (uint32_t f = 0; f < d.index_dim; ++f)
-            dot = __fadd_rn(dot, __fmul_rn(q[f], key[(size_t)f * ld]));
-        if (dot > 0.0f) score = __fadd_rn(score, dot);
+    // the index heads' dot products are independent chains: walk them
+    // together (each key feature read once), each in the reference's
+    // sequential feature order; then add the positive ones in head order
+    for (uint32_t h0 = 0; h0 < d.index_heads; h0 += 4) {
+        const uint32_t nh = min(4u, d.index_heads - h0);
+        float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (uint32_t f = 0; f < d.index_dim; ++f) {
+            const float kv = key[(size_t)f * ld];
+#pragma unroll
+            for (uint32_t h = 0; h < 4; ++h)
+                if (h < nh) dot[h] = __fadd_rn(dot[h], __fmul_rn(qsh[(h0 + h) * d.index_dim + f], kv));
+        }
+        for (uint32_t h = 0; h < nh; ++h)
+            if (dot[h] > 0.0f) score = __fadd_rn(score, dot[h]);
     }
     score = __fdiv_rn(score, d.sqrt_index_dim);
     if (!isfinite(score)) qsa_raise(err, kErrNonFinite);
@@ -519,6 +527,162 @@ qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     }
 }
 
+// Tiled variant for head dimensions 128 / 256 (the BASELINE shapes).
+// grid (splits, Hkv, B); 256 threads = 8 warps; warp h owns query head
+// kvh*repeat + h.  The split's token range is walked in tiles of 32 selected
+// tokens whose K and V rows are staged with cp.async into double-buffered
+// shared memory (the next tile loads while the current one is consumed).
+// Logits: lane = token (float4 dot over the padded K rows, conflict-free);
+// online softmax per warp; P.V: lane = 8 consecutive features.
+
+constexpr int kAtTile = 32;
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;\n" ::); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n" ::); }
+
+template <int HD>
+__global__ void __launch_bounds__(256, 1)
+qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
+                        const uint32_t *__restrict__ selected,
+                        const uint32_t *__restrict__ selected_count,
+                        float *__restrict__ part_o, float *__restrict__ part_ml,
+                        uint32_t splits, ErrorWord err) {
+    constexpr int KLD = HD + 4;          // padded K row (conflict-free float4 reads)
+    constexpr int FPL = HD / 32;         // features per lane in P.V
+    constexpr int CH = HD / 4;           // 16-byte chunks per row
+    extern __shared__ __align__(16) float sm[];
+    float *qs = sm;                                  // [8][HD]
+    float *ks = qs + 8 * HD;                         // [2][32][KLD]
+    float *vs = ks + 2 * kAtTile * KLD;              // [2][32][HD]
+    if (qsa_error_raised(err)) return;
+    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const QsaSeq s = bt.s[b];
+    const uint32_t pos = s.length;
+    const uint32_t nblocks = (pos + 1) / d.block;
+    const uint32_t tail = (pos + 1) % d.block;
+    const uint32_t ksel = min(selected_count[b], min(nblocks, d.topk));
+    const uint32_t ntok = ksel * d.block + tail;
+    const uint32_t ntiles = (ntok + kAtTile - 1) / kAtTile;
+    const uint32_t per = (ntiles + splits - 1) / splits;
+    const uint32_t tile0 = split * per, tile1 = min(ntiles, tile0 + per);
+    const uint32_t heads = d.repeat;
+    const uint32_t kvw = d.kv_heads * HD;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t *selb = selected + (size_t)b * d.topk;
+
+    for (uint32_t i = threadIdx.x; i < heads * HD; i += blockDim.x)
+        qs[i] = q[((size_t)b * d.q_heads + kvh * heads) * HD + i];
+
+    auto token_of = [&](uint32_t i, bool &ok) -> uint32_t {
+        ok = i < ntok;
+        if (!ok) return 0;
+        if (i < ksel * d.block) {
+            const uint32_t blk = selb[i / d.block];
+            ok = blk < nblocks;
+            return ok ? blk * d.block + i % d.block : 0;
+        }
+        return nblocks * d.block + (i - ksel * d.block);
+    };
+    auto load_tile = [&](uint32_t tile, int buf) {
+        float *kd = ks + buf * kAtTile * KLD;
+        float *vd = vs + buf * kAtTile * HD;
+        for (int c = threadIdx.x; c < kAtTile * CH; c += blockDim.x) {
+            const int t = c / CH, col = (c % CH) * 4;
+            bool ok;
+            const uint32_t tok = token_of(tile * kAtTile + t, ok);
+            if (ok) {
+                const size_t off = (size_t)tok * kvw + kvh * HD + col;
+                cp_async16(kd + t * KLD + col, s.key + off);
+                cp_async16(vd + t * HD + col, s.value + off);
+            } else {
+                *reinterpret_cast<float4 *>(kd + t * KLD + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4 *>(vd + t * HD + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        cp_async_commit();
+    };
+
+    float m_run = -INFINITY, l_run = 0.0f;
+    float acc[FPL];
+#pragma unroll
+    for (int f = 0; f < FPL; ++f) acc[f] = 0.0f;
+    const float scale = d.sqrt_head_dim;
+    const bool active = (uint32_t)warp < heads;
+    const float *qh = qs + warp * HD;
+
+    if (tile0 < tile1) load_tile(tile0, 0);
+    for (uint32_t tile = tile0; tile < tile1; ++tile) {
+        const int buf = (tile - tile0) & 1;
+        if (tile + 1 < tile1) {
+            load_tile(tile + 1, buf ^ 1);
+            cp_async_wait1();
+        } else {
+            cp_async_wait0();
+        }
+        __syncthreads();
+        if (active) {
+            const float *kr = ks + buf * kAtTile * KLD + lane * KLD;
+            float dot = 0.0f;
+#pragma unroll 8
+            for (int f = 0; f < HD; f += 4) {
+                const float4 qv = *reinterpret_cast<const float4 *>(qh + f);
+                const float4 kv = *reinterpret_cast<const float4 *>(kr + f);
+                dot = fmaf(qv.x, kv.x, dot);
+                dot = fmaf(qv.y, kv.y, dot);
+                dot = fmaf(qv.z, kv.z, dot);
+                dot = fmaf(qv.w, kv.w, dot);
+            }
+            bool ok;
+            token_of(tile * kAtTile + lane, ok);
+            const float logit = ok ? dot / scale : -INFINITY;
+            float mt = logit;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            const float m_new = fmaxf(m_run, mt);
+            const float corr = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
+            const float p = ok ? expf(logit - m_new) : 0.0f;
+            float ps = p;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            l_run = l_run * corr + ps;
+            m_run = m_new;
+#pragma unroll
+            for (int f = 0; f < FPL; ++f) acc[f] *= corr;
+            const float *vb = vs + buf * kAtTile * HD + lane * FPL;
+#pragma unroll 4
+            for (int t = 0; t < kAtTile; ++t) {
+                const float pt = __shfl_sync(0xffffffffu, p, t);
+                const float *vr = vb + t * HD;
+#pragma unroll
+                for (int f = 0; f < FPL; f += 4) {
+                    const float4 vv = *reinterpret_cast<const float4 *>(vr + f);
+                    acc[f] = fmaf(pt, vv.x, acc[f]);
+                    acc[f + 1] = fmaf(pt, vv.y, acc[f + 1]);
+                    acc[f + 2] = fmaf(pt, vv.z, acc[f + 2]);
+                    acc[f + 3] = fmaf(pt, vv.w, acc[f + 3]);
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (!active) return;
+    const uint32_t qhead = kvh * heads + warp;
+    const size_t slot = ((size_t)b * d.q_heads + qhead) * splits + split;
+#pragma unroll
+    for (int f = 0; f < FPL; f += 4)
+        *reinterpret_cast<float4 *>(part_o + slot * HD + lane * FPL + f) =
+            make_float4(acc[f], acc[f + 1], acc[f + 2], acc[f + 3]);
+    if (lane == 0) {
+        part_ml[slot * 2] = m_run;
+        part_ml[slot * 2 + 1] = l_run;
+    }
+}
+
 void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const float *q, const uint32_t *selected,
                        const uint32_t *selected_count, float *partial_o,
@@ -526,21 +690,30 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        ErrorWord err, cudaStream_t stream) {
     dim3 grid(splits, d.kv_heads, batch);
     KernelTimer timer("qsa_attend", stream);
-    // HPW covers all query heads of one KV head (host validates repeat <= 8)
-    if (d.head_dim == 256) {
-        size_t smem = (size_t)8 * 8 * (d.head_dim + 2) * sizeof(float);
-        cudaFuncSetAttribute(qsa_attend_kernel<8, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-        qsa_attend_kernel<8, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
-                                                           partial_o, partial_ml, splits, err);
-    } else if (d.head_dim == 128) {
-        size_t smem = (size_t)8 * 8 * (d.head_dim + 2) * sizeof(float);
-        qsa_attend_kernel<4, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
-                                                           partial_o, partial_ml, splits, err);
+    if (d.head_dim == 256 || d.head_dim == 128) {
+        const int hd = (int)d.head_dim;
+        const size_t smem = (size_t)(8 * hd + 2 * kAtTile * (hd + 4) + 2 * kAtTile * hd) * sizeof(float);
+        if (hd == 256) {
+            cudaFuncSetAttribute(qsa_attend_tiled_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+            qsa_attend_tiled_kernel<256><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+                                                                    partial_o, partial_ml, splits, err);
+        } else {
+            cudaFuncSetAttribute(qsa_attend_tiled_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+            qsa_attend_tiled_kernel<128><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+                                                                    partial_o, partial_ml, splits, err);
+        }
     } else {
+        // small heads (reduced test shapes): warp-per-token kernel
         size_t smem = (size_t)8 * 8 * (d.head_dim + 2) * sizeof(float);
-        qsa_attend_kernel<1, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
-                                                           partial_o, partial_ml, splits, err);
+        if (d.head_dim <= 32) {
+            qsa_attend_kernel<1, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+                                                               partial_o, partial_ml, splits, err);
+        } else {
+            qsa_attend_kernel<2, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+                                                               partial_o, partial_ml, splits, err);
+        }
     }
     count_launch();
 }
