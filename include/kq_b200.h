@@ -139,6 +139,20 @@ kq_status kq_b200_provider_add_vector_f32(kq_weight_provider *provider,
                                           const kq_semantic_tensor **out_tensor,
                                           kq_diagnostic *diagnostic);
 
+/* Batched form of kq_weight_provider_linear_f32:
+ * y[b][r] = sum_c W[r][c] * x[b][c] for b < batch, with x [batch][columns]
+ * and y [batch][rows] device arrays.  Batches above 8 run on the tensor
+ * cores (three-term BF16 split, F32 accumulate); smaller ones on a warp
+ * GEMV.  Asynchronous on the library stream (see kq_b200_synchronize). */
+kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
+                                            const kq_semantic_tensor *semantic,
+                                            uint64_t rows,
+                                            uint64_t columns,
+                                            const float *x,
+                                            uint32_t batch,
+                                            float *y,
+                                            kq_diagnostic *diagnostic);
+
 typedef struct kq_b200_gdn_tensors {
     const kq_semantic_tensor *a_log;    /* F32 [Hv] */
     const kq_semantic_tensor *conv;     /* F32 [C*K] */

@@ -29,6 +29,7 @@ SOURCES = [
     "kernels_proj.cu",
     "kernels_gdn.cu",
     "kernels_qsa.cu",
+    "kernels_umma.cu",
     "runtime.cpp",
     "api_basic.cpp",
     "api_provider.cpp",

@@ -7,6 +7,7 @@
 // that is only committed when the device reported no error.
 #include <cfenv>
 #include <cmath>
+#include <algorithm>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -145,6 +146,9 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
     size_t need = Carve::round(items * ldp * 4) + Carve::round(items * 2 * gd.key_width * 4) +
                   Carve::round(items * Vd * 4) * 2 + Carve::round(items * Hv * 4) * 2 +
                   (mask ? Carve::round(items * H * 4) : 0) + 4096;
+    // split-K work space of the tensor-core projections (small batches only)
+    const size_t partial_floats = items <= 512 ? (size_t)kProjPartialSplits * items * std::max(ldp, H) : 0;
+    need += Carve::round(partial_floats * 4);
     void *ws;
     kq_status st = c->workspace(need, &ws, diag);
     if (st != KQ_STATUS_OK) return st;
@@ -156,6 +160,7 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
     float *beta = cv.take<float>(items * Hv);
     float *decay = cv.take<float>(items * Hv);
     float *xm = mask ? cv.take<float>(items * H) : nullptr;
+    float *partial = partial_floats ? cv.take<float>(partial_floats) : nullptr;
 
     ProjSegments in{};
     in.count = 4;
@@ -187,11 +192,11 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
                 p.rec_out[b] = s->rec[1 - s->cur];
             }
             const uint32_t n_items = gb * tc;
-            launch_projection(in, xin, H, proj, ldp, n_items, err, c->stream);
+            launch_projection(in, xin, H, proj, ldp, n_items, err, c->stream, partial, partial_floats);
             launch_gdn_conv_gates(gd, w.vec, p, gb, tc, proj, ldp, qk, v, beta, decay, err, c->stream);
             launch_gdn_recurrence(gd, w.vec, p, gb, tc, qk, v, beta, decay, proj, ldp, gated, err,
                                   c->stream);
-            launch_projection(out, gated, Vd, y + row0 * H, H, n_items, err, c->stream);
+            launch_projection(out, gated, Vd, y + row0 * H, H, n_items, err, c->stream, partial, partial_floats);
             launch_check_finite(y + row0 * H, (uint64_t)n_items * H, err, c->stream);
             for (uint32_t b = 0; b < gb; ++b) {
                 kq_gdn_state *s = states[g0 + b];

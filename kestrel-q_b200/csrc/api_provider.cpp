@@ -215,6 +215,43 @@ kq_status kq_weight_provider_linear_f32(kq_weight_provider *provider,
     return KQ_STATUS_OK;
 }
 
+kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
+                                            const kq_semantic_tensor *semantic, uint64_t rows,
+                                            uint64_t columns, const float *x, uint32_t batch, float *y,
+                                            kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    ProviderTensor *t = provider_lookup(provider, semantic);
+    if (t == nullptr || x == nullptr || y == nullptr || batch == 0)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, semantic and buffers are required");
+    if (t->is_vector) return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "semantic is not a matrix");
+    if (rows != t->m.rows || columns != t->m.cols)
+        return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "linear shape does not match the semantic");
+    if (!is_device_pointer(x) || !is_device_pointer(y))
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "batched linear takes device buffers");
+    if (ranges_overlap(x, (uint64_t)batch * columns * 4, y, (uint64_t)batch * rows * 4))
+        return fail(diagnostic, KQ_STATUS_ALIASING_VIOLATION, "linear input and output overlap");
+    kq_status st = kq_b200_set_device(provider->device, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    DeviceContext *c;
+    st = context(&c, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    const size_t partial_floats = (size_t)kProjPartialSplits * batch * rows;
+    void *ws;
+    st = c->workspace(Carve::round(partial_floats * 4) + 256, &ws, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    ErrorWord err = c->begin_call();
+    launch_check_finite(x, (uint64_t)batch * columns, err, c->stream);
+    ProjSegments segs{};
+    segs.count = 1;
+    segs.m[0] = t->m;
+    launch_projection(segs, x, (uint32_t)columns, y, (uint32_t)rows, batch, err, c->stream,
+                      static_cast<float *>(ws), partial_floats);
+    KQB_CUDA(cudaGetLastError(), diagnostic, "linear launch");
+    provider->metrics.linear_requests += 1;
+    return KQ_STATUS_OK;
+}
+
 kq_status kq_weight_provider_vector_f32(kq_weight_provider *provider,
                                         const kq_semantic_tensor *semantic,
                                         uint64_t element_count, float *output,

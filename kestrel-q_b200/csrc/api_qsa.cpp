@@ -208,8 +208,9 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                         Carve::round((size_t)batch * d.topk * 4) + Carve::round((size_t)batch * 4) +
                         Carve::round((size_t)batch * d.q_heads * splits * hd * 4) +
                         Carve::round((size_t)batch * d.q_heads * splits * 2 * 4) + 8192;
+    const size_t partial_floats = items <= 512 ? (size_t)kProjPartialSplits * items * std::max(ldp, H) : 0;
     void *ws;
-    kq_status st = c->workspace(need, &ws, diag);
+    kq_status st = c->workspace(need + Carve::round(partial_floats * 4), &ws, diag);
     if (st != KQ_STATUS_OK) return st;
     Carve cv(ws);
     float *proj = cv.take<float>(items * ldp);
@@ -222,6 +223,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     uint32_t *sel_count = cv.take<uint32_t>(batch);
     float *part_o = cv.take<float>((size_t)batch * d.q_heads * splits * hd);
     float *part_ml = cv.take<float>((size_t)batch * d.q_heads * splits * 2);
+    float *partial = partial_floats ? cv.take<float>(partial_floats) : nullptr;
 
     ProjSegments main{};
     main.count = 3;
@@ -250,7 +252,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
         const uint32_t gb = std::min<uint32_t>(kMaxBatch, batch - g0);
         const size_t row0 = (size_t)g0 * tokens;
         const size_t n_items = (size_t)gb * tokens;
-        launch_projection(main, x + row0 * H, H, proj, ldp, (uint32_t)n_items, err, c->stream);
+        launch_projection(main, x + row0 * H, H, proj, ldp, (uint32_t)n_items, err, c->stream, partial,
+                          partial_floats);
         launch_projection_exact(index, x + row0 * H, H, iproj, ldi, (uint32_t)n_items, err, c->stream);
         for (uint32_t b = 0; b < gb; ++b) {
             kq_qsa_state *s = states[g0 + b];
@@ -294,7 +297,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 selection->push_back(std::move(sc));
             }
         }
-        launch_projection(out, gated, qw, y + row0 * H, H, (uint32_t)n_items, err, c->stream);
+        launch_projection(out, gated, qw, y + row0 * H, H, (uint32_t)n_items, err, c->stream, partial,
+                          partial_floats);
         launch_check_finite(y + row0 * H, n_items * H, err, c->stream);
         for (uint32_t b = 0; b < gb; ++b) {
             kq_qsa_state *s = states[g0 + b];

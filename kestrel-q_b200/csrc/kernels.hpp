@@ -43,9 +43,17 @@ struct ErrorWord {
 };
 
 // ---- projections (kernels_proj.cu)
+// `partial` (may be null) is split-K work space of partial_floats floats;
+// kProjPartialSplits * batch * ldy floats let every shape use split K.
+constexpr int kProjPartialSplits = 4;
 void launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
                        float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
-                       cudaStream_t stream);
+                       cudaStream_t stream, float *partial = nullptr,
+                       size_t partial_floats = 0);
+// Tensor-core path (kernels_umma.cu), used for batches above 8.
+bool launch_projection_umma(const ProjSegments &segs, const float *x, uint32_t ldx,
+                            float *y, uint32_t ldy, uint32_t batch, float *partial,
+                            size_t partial_floats, ErrorWord err, cudaStream_t stream);
 // Sequential-order product: each output is accumulated k = 0..K-1 from 0.0f
 // with separately rounded products and sums, i.e. bit-identical to the
 // reference's kq_f32_dot / kq_quantized_row_dot_f32.
@@ -157,6 +165,7 @@ void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
                            cudaStream_t stream);
 
 uint64_t launches_total();
+bool force_simt_projection();
 void count_launch();
 
 // Optional CUDA-event timing of one named kernel family (kq_b200_profile_*):

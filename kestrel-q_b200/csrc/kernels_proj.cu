@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 
 namespace kqb {
 
@@ -17,6 +18,17 @@ std::atomic<uint64_t> g_launches{0};
 }
 
 uint64_t launches_total() { return g_launches.load(); }
+
+// KQ_B200_SIMT_PROJECTION=1 selects the CUDA-core tiled GEMM for batches
+// above 8 (used by the tests to cross-check the tensor-core path).
+bool force_simt_projection() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("KQ_B200_SIMT_PROJECTION");
+        v = (e != nullptr && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
 void count_launch() { g_launches.fetch_add(1); }
 
 __device__ __forceinline__ bool error_raised(const ErrorWord &e) {
@@ -255,9 +267,13 @@ static void fill_tile_starts(ProjSegments &s, uint32_t unit) {
 
 void launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
                        float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, float *partial, size_t partial_floats) {
     ProjSegments segs = in;
     KernelTimer timer("proj", stream);
+    if (batch > 8 && !force_simt_projection()) {
+        launch_projection_umma(segs, x, ldx, y, ldy, batch, partial, partial_floats, err, stream);
+        return;
+    }
     if (batch <= 8) {
         fill_tile_starts(segs, 1);
         uint32_t rows = segs.tile_start[segs.count];

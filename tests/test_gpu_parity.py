@@ -99,6 +99,35 @@ def test_provider_linear(kq, oracle, type_id):
         p.close()
 
 
+@pytest.mark.parametrize("type_id,rows,cols,batch", [
+    (12, 520, 2048, 64), (14, 2048, 4096, 64), (8, 300, 2048, 9), (30, 640, 2048, 100),
+    (0, 200, 512, 33), (12, 12352, 2048, 64), (14, 130, 256, 129)])
+def test_tensor_core_projection(kq, oracle, type_id, rows, cols, batch):
+    """Dequant-fused tcgen05 GEMM (three-term BF16 split) against the
+    reference's sequential F32 row dots: ragged rows, batches and K."""
+    import torch
+    from kqb200 import synth
+    rng = np.random.default_rng(rows + cols + batch)
+    q = synth.pack(type_id, rng, rows, cols)
+    p = kq.Provider(0)
+    try:
+        h = p.add_matrix("m", 11, q)
+        x = rng.normal(size=(batch, cols)).astype(np.float32)
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.full((batch, rows), float("nan"), device="cuda")
+        torch.cuda.synchronize()
+        d = kq.abi.Diagnostic()
+        st = kq.lib().kq_b200_provider_linear_batch_f32(p.handle, h, rows, cols, xd.data_ptr(), batch,
+                                                        yd.data_ptr(), C.byref(d))
+        assert st == 0, d.text()
+        kq.synchronize()
+        y = yd.cpu().numpy()
+        want = oracle.matvec(type_id, q.data, rows, cols, x)
+        assert_close(y, want, f"type {type_id}")
+    finally:
+        p.close()
+
+
 # ------------------------------------------------------------------ GDN
 
 def _gdn_f32_call(kq, layer_handle, dims, w, x, state, mask=None):
