@@ -272,6 +272,7 @@ static kq_status gdn_execute_sync(const kq_gdn_config *cfg, const GdnResolved *w
             m.rows = rows;
             m.cols = cols;
             m.row_bytes = cols * 4;
+            m.layout = 0;
             return m;
         };
         w.vec.a_log = views[0].ptr;

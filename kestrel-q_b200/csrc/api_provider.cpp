@@ -4,6 +4,7 @@
 #include <cfenv>
 #include <cmath>
 #include <cstring>
+#include <vector>
 
 #include "kq_b200.h"
 #include "kq_tensor_view.h"
@@ -98,9 +99,36 @@ kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *
         return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "packed byte count does not match the shape");
     kq_status st = kq_b200_set_device(provider->device, diagnostic);
     if (st != KQ_STATUS_OK) return st;
+    // Q6_K and Q8_0 rows are stored as aligned planes (same bytes, see
+    // kernels.hpp QMatrix) so the kernels can use 16-byte loads
+    const uint8_t *src = static_cast<const uint8_t *>(packed);
+    std::vector<uint8_t> planar;
+    uint32_t layout = 0;
+    if (type_id == KQ_GGUF_TYPE_Q6_K || type_id == KQ_GGUF_TYPE_Q8_0) {
+        planar.resize(total);
+        const uint64_t nblk = columns / be;
+        for (uint64_t r = 0; r < rows; ++r) {
+            const uint8_t *in = src + r * row_bytes;
+            uint8_t *out = planar.data() + r * row_bytes;
+            for (uint64_t b = 0; b < nblk; ++b) {
+                const uint8_t *blk = in + b * bb;
+                if (type_id == KQ_GGUF_TYPE_Q6_K) {
+                    std::memcpy(out + b * 128, blk, 128);                     // ql
+                    std::memcpy(out + nblk * 128 + b * 64, blk + 128, 64);    // qh
+                    std::memcpy(out + nblk * 192 + b * 16, blk + 192, 16);    // scales
+                    std::memcpy(out + nblk * 208 + b * 2, blk + 208, 2);      // d
+                } else {
+                    std::memcpy(out + b * 32, blk + 2, 32);                   // codes
+                    std::memcpy(out + nblk * 32 + b * 2, blk, 2);             // d
+                }
+            }
+        }
+        src = planar.data();
+        layout = 1;
+    }
     void *dev = nullptr;
     KQB_CUDA(cudaMalloc(&dev, total), diagnostic, "weight allocation");
-    cudaError_t e = cudaMemcpy(dev, packed, total, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpy(dev, src, total, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         cudaFree(dev);
         return cuda_fail(diagnostic, e, "weight upload");
@@ -113,6 +141,7 @@ kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *
     t->m.rows = (uint32_t)rows;
     t->m.cols = (uint32_t)columns;
     t->m.row_bytes = (uint32_t)row_bytes;
+    t->m.layout = layout;
     t->desc.canonical_rank = 2;
     t->desc.canonical_dimensions[0] = rows;
     t->desc.canonical_dimensions[1] = columns;

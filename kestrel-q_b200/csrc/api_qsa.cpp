@@ -468,6 +468,7 @@ static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w
             m.rows = rows;
             m.cols = cols;
             m.row_bytes = cols * 4;
+            m.layout = 0;
             return m;
         };
         w.q = dense(views[0].ptr, 2 * qw, H);

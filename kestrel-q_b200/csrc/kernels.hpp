@@ -18,12 +18,20 @@ enum DeviceError : uint32_t {
 };
 
 // One quantized (or F32/BF16) matrix in HBM: `rows` consecutive GGUF rows.
+//
+// layout 0: the GGUF byte stream as given.  layout 1 ("planar"): each row's
+// blocks are split into aligned planes with the same byte count, so that a
+// 32-element run loads with 16-byte vector loads:
+//   Q6_K: [ql nsb*128][qh nsb*64][scales nsb*16][d nsb*2]
+//   Q8_0: [codes nb*32][d nb*2]
+// (Q4_K's 144-byte super-blocks are already 16-byte aligned and stay GGUF.)
 struct QMatrix {
     const uint8_t *data;
     uint32_t type;
     uint32_t rows;
     uint32_t cols;
     uint32_t row_bytes;
+    uint32_t layout;
 };
 
 constexpr int kMaxSegments = 6;
@@ -45,7 +53,7 @@ struct ErrorWord {
 // ---- projections (kernels_proj.cu)
 // `partial` (may be null) is split-K work space of partial_floats floats;
 // kProjPartialSplits * batch * ldy floats let every shape use split K.
-constexpr int kProjPartialSplits = 4;
+constexpr int kProjPartialSplits = 8;
 void launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
                        float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
                        cudaStream_t stream, float *partial = nullptr,

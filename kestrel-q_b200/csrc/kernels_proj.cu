@@ -83,7 +83,7 @@ proj_tiled_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
             uint32_t count = 0;
             if (first < m.cols) count = min(16u, m.cols - first);
             if (wrow < m.rows && count > 0) {
-                decode_run(m.type, wptr, first, count, vals);
+                decode_any(m, wptr, first, count, vals);
             }
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -149,7 +149,7 @@ proj_warp_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
     for (uint32_t base = (uint32_t)lane * 32u; base < m.cols; base += 1024u) {
         float w[32];
         uint32_t count = min(32u, m.cols - base);
-        decode_run(m.type, wptr, base, count, w);
+        decode_any(m, wptr, base, count, w);
         const bool vec_ok = count == 32u && (ldx & 3u) == 0u &&
                             (reinterpret_cast<uintptr_t>(x) & 15u) == 0u;
         if (vec_ok) {
@@ -226,7 +226,7 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
             uint32_t cnt = 0;
             if ((uint32_t)run < kc) cnt = min(16u, kc - run);
             if (grow < m.rows && cnt > 0)
-                decode_run(m.type, m.data + (size_t)grow * m.row_bytes, k0 + run, cnt, w);
+                decode_any(m, m.data + (size_t)grow * m.row_bytes, k0 + run, cnt, w);
             for (int i = 0; i < 16; ++i) ws[r][run + i] = (grow < m.rows && (uint32_t)i < cnt) ? w[i] : 0.0f;
         }
         // activations, transposed: xs[k][b]

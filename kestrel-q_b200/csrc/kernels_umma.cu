@@ -197,11 +197,12 @@ proj_umma_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
         {
             float w[32];
             const uint32_t first = k0 + a_half * 32;
-            uint32_t cnt = first < m.cols ? min(32u, m.cols - first) : 0u;
-            if (wrow < m.rows && cnt > 0) decode_run(m.type, wptr, first, cnt, w);
+            if (wrow < m.rows && first < m.cols) {
+                decode32_any(m, wptr, first, w);
+            } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (!(wrow < m.rows && (uint32_t)i < cnt)) w[i] = 0.0f;
+                for (int i = 0; i < 32; ++i) w[i] = 0.0f;
+            }
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 uint4 hi, lo;
@@ -346,7 +347,8 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
     // split K until there are about two CTAs per SM (148 SMs), keeping at
     // least 8 chunks per split
     uint32_t splits = 1;
-    while (splits < 4 && acc * btiles * splits < 2 * 148 && nchunks / (splits * 2) >= 8) splits *= 2;
+    while (splits < kProjPartialSplits && acc * btiles * splits < 2 * 148 && nchunks / (splits * 2) >= 4)
+        splits *= 2;
     if (splits > 1 && (partial == nullptr || partial_floats < (size_t)splits * batch * ldy)) splits = 1;
     // the split-K reduce covers one contiguous column range
     uint32_t covered = 0;

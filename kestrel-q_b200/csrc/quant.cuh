@@ -139,4 +139,183 @@ __device__ __forceinline__ void decode_run(uint32_t type, const uint8_t *row,
     }
 }
 
+// ------------------------------------------------------------------ fast path
+//
+// decode32: 32 consecutive elements starting at `first` (a multiple of 32,
+// first + 32 <= cols) of one row, with 16-byte vector loads.  Same
+// arithmetic as decode_run (bit-identical results).  `row` must be 16-byte
+// aligned and the row length a multiple of 16 bytes for the planar and Q4_K
+// layouts; callers fall back to decode_run otherwise.
+
+__device__ __forceinline__ void bytes16(uint4 v, uint8_t *b) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        b[4 * i + 0] = (uint8_t)(w[i]);
+        b[4 * i + 1] = (uint8_t)(w[i] >> 8);
+        b[4 * i + 2] = (uint8_t)(w[i] >> 16);
+        b[4 * i + 3] = (uint8_t)(w[i] >> 24);
+    }
+}
+
+template <uint32_t TYPE, uint32_t LAYOUT>
+__device__ __forceinline__ void decode32_t(const uint8_t *row, uint32_t cols, uint32_t first, float *out) {
+    if constexpr (TYPE == kTypeQ4_K) {
+        const uint8_t *b = row + (first >> 8) * 144u;
+        const uint32_t w = first & 255u, group = w >> 6, high = (w >> 5) & 1u;
+        uint8_t hdr[16], q[32];
+        bytes16(*reinterpret_cast<const uint4 *>(b), hdr);
+        bytes16(*reinterpret_cast<const uint4 *>(b + 16 + group * 32), q);
+        bytes16(*reinterpret_cast<const uint4 *>(b + 32 + group * 32), q + 16);
+        const float d = half_bits_to_float((uint32_t)hdr[0] | ((uint32_t)hdr[1] << 8));
+        const float dmin = half_bits_to_float((uint32_t)hdr[2] | ((uint32_t)hdr[3] << 8));
+        uint32_t sc, mn;
+        q4k_scale_min(hdr + 4, (int)(2u * group + high), sc, mn);
+        const float dl = __fmul_rn(d, (float)sc), ml = __fmul_rn(dmin, (float)mn);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const uint32_t code = high ? (q[i] >> 4) : (q[i] & 15u);
+            out[i] = __fsub_rn(__fmul_rn(dl, (float)code), ml);
+        }
+    } else if constexpr (TYPE == kTypeQ6_K && LAYOUT == 1) {
+        const uint32_t nsb = cols >> 8, sb = first >> 8, w = first & 255u;
+        const uint32_t half = w >> 7, s = (w & 127u) >> 5;
+        const uint8_t *ql = row + sb * 128u + half * 64u + 32u * (s & 1u);
+        const uint8_t *qh = row + nsb * 128u + sb * 64u + half * 32u;
+        const int8_t *sc = reinterpret_cast<const int8_t *>(row + nsb * 192u + sb * 16u + half * 8u + 2u * s);
+        const uint8_t *dp = row + nsb * 208u + sb * 2u;
+        uint8_t lo[32], hi[32];
+        bytes16(*reinterpret_cast<const uint4 *>(ql), lo);
+        bytes16(*reinterpret_cast<const uint4 *>(ql + 16), lo + 16);
+        bytes16(*reinterpret_cast<const uint4 *>(qh), hi);
+        bytes16(*reinterpret_cast<const uint4 *>(qh + 16), hi + 16);
+        const float d = half_bits_to_float((uint32_t)dp[0] | ((uint32_t)dp[1] << 8));
+        const float s0 = __fmul_rn(d, (float)sc[0]), s1 = __fmul_rn(d, (float)sc[1]);
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+            const uint32_t nib = (s & 2u) ? (lo[l] >> 4) : (lo[l] & 15u);
+            const int code = (int)(nib | (((hi[l] >> (2u * s)) & 3u) << 4)) - 32;
+            out[l] = __fmul_rn(l < 16 ? s0 : s1, (float)code);
+        }
+    } else if constexpr (TYPE == kTypeQ8_0 && LAYOUT == 1) {
+        const uint32_t nb = cols >> 5, blk = first >> 5;
+        const uint8_t *codes = row + blk * 32u;
+        const uint8_t *dp = row + nb * 32u + blk * 2u;
+        uint8_t c[32];
+        bytes16(*reinterpret_cast<const uint4 *>(codes), c);
+        bytes16(*reinterpret_cast<const uint4 *>(codes + 16), c + 16);
+        const float d = half_bits_to_float((uint32_t)dp[0] | ((uint32_t)dp[1] << 8));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) out[i] = __fmul_rn((float)(int8_t)c[i], d);
+    } else if constexpr (TYPE == kTypeBF16) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + (size_t)first * 2u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint4 v = p[j];
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                out[8 * j + 2 * i] = __uint_as_float(w4[i] << 16);
+                out[8 * j + 2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+            }
+        }
+    } else {   // F32
+        const float4 *p = reinterpret_cast<const float4 *>(row + (size_t)first * 4u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float4 v = p[j];
+            out[4 * j] = v.x; out[4 * j + 1] = v.y; out[4 * j + 2] = v.z; out[4 * j + 3] = v.w;
+        }
+    }
+}
+
+// Scalar decode of `count` elements of a planar-layout row (tails).
+__device__ __forceinline__ void decode_run_planar(uint32_t type, const uint8_t *row, uint32_t cols,
+                                                  uint32_t first, uint32_t count, float *out) {
+    if (type == kTypeQ8_0) {
+        const uint32_t nb = cols >> 5;
+        for (uint32_t i = 0; i < count; ++i) {
+            const uint32_t e = first + i, blk = e >> 5;
+            const uint8_t *dp = row + nb * 32u + blk * 2u;
+            const float d = half_bits_to_float((uint32_t)dp[0] | ((uint32_t)dp[1] << 8));
+            out[i] = __fmul_rn((float)(int8_t)row[blk * 32u + (e & 31u)], d);
+        }
+    } else {   // Q6_K
+        const uint32_t nsb = cols >> 8;
+        for (uint32_t i = 0; i < count; ++i) {
+            const uint32_t e = first + i, sb = e >> 8, w = e & 255u;
+            const uint32_t half = w >> 7, s = (w & 127u) >> 5, l = w & 31u;
+            const uint8_t lob = row[sb * 128u + half * 64u + 32u * (s & 1u) + l];
+            const uint8_t hib = row[nsb * 128u + sb * 64u + half * 32u + l];
+            const int8_t scv = (int8_t)row[nsb * 192u + sb * 16u + half * 8u + 2u * s + (l >> 4)];
+            const uint8_t *dp = row + nsb * 208u + sb * 2u;
+            const float d = half_bits_to_float((uint32_t)dp[0] | ((uint32_t)dp[1] << 8));
+            const uint32_t nib = (s & 2u) ? (lob >> 4) : (lob & 15u);
+            const int code = (int)(nib | (((hib >> (2u * s)) & 3u) << 4)) - 32;
+            out[i] = __fmul_rn(__fmul_rn(d, (float)scv), (float)code);
+        }
+    }
+}
+
+// Any run of a provider matrix (layout-aware).  A 32-element aligned run
+// of an aligned row takes the vectorised path.
+template <typename M>
+__device__ __forceinline__ void decode_any(const M &m, const uint8_t *row, uint32_t first, uint32_t count,
+                                           float *out) {
+    const bool fast = count == 32u && (first & 31u) == 0u && (m.row_bytes & 15u) == 0u &&
+                      (reinterpret_cast<uintptr_t>(row) & 15u) == 0u;
+    if (fast) {
+        switch (m.type) {
+        case kTypeQ4_K: decode32_t<kTypeQ4_K, 0>(row, m.cols, first, out); return;
+        case kTypeQ6_K:
+            if (m.layout == 1) { decode32_t<kTypeQ6_K, 1>(row, m.cols, first, out); return; }
+            break;
+        case kTypeQ8_0:
+            if (m.layout == 1) { decode32_t<kTypeQ8_0, 1>(row, m.cols, first, out); return; }
+            break;
+        case kTypeBF16: decode32_t<kTypeBF16, 0>(row, m.cols, first, out); return;
+        case kTypeF32: decode32_t<kTypeF32, 0>(row, m.cols, first, out); return;
+        default: break;
+        }
+    }
+    if (m.layout == 1 && (m.type == kTypeQ6_K || m.type == kTypeQ8_0))
+        decode_run_planar(m.type, row, m.cols, first, count, out);
+    else
+        decode_run(m.type, row, first, count, out);
+}
+
+// Exactly 32 values (zero past the row end) with static indexing only, so
+// `out` stays in registers.  Fast vector path when aligned, element-wise
+// otherwise.
+template <typename M>
+__device__ __forceinline__ void decode32_any(const M &m, const uint8_t *row, uint32_t first, float (&out)[32]) {
+    const bool fast = (first & 31u) == 0u && first + 32u <= m.cols && (m.row_bytes & 15u) == 0u &&
+                      (reinterpret_cast<uintptr_t>(row) & 15u) == 0u;
+    if (fast) {
+        switch (m.type) {
+        case kTypeQ4_K: decode32_t<kTypeQ4_K, 0>(row, m.cols, first, out); return;
+        case kTypeQ6_K:
+            if (m.layout == 1) { decode32_t<kTypeQ6_K, 1>(row, m.cols, first, out); return; }
+            break;
+        case kTypeQ8_0:
+            if (m.layout == 1) { decode32_t<kTypeQ8_0, 1>(row, m.cols, first, out); return; }
+            break;
+        case kTypeBF16: decode32_t<kTypeBF16, 0>(row, m.cols, first, out); return;
+        case kTypeF32: decode32_t<kTypeF32, 0>(row, m.cols, first, out); return;
+        default: break;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        float v[1] = {0.0f};
+        if (first + i < m.cols) {
+            if (m.layout == 1 && (m.type == kTypeQ6_K || m.type == kTypeQ8_0))
+                decode_run_planar(m.type, row, m.cols, first + i, 1, v);
+            else
+                decode_run(m.type, row, first + i, 1, v);
+        }
+        out[i] = v[0];
+    }
+}
+
 }  // namespace kqb
