@@ -59,9 +59,9 @@ def dims():
     return synth.GdnDims(), synth.QsaDims()
 
 
-def contexts(rank: int, n: int = BATCH):
+def contexts(rank: int, n: int = BATCH, ctx_max: int = CTX_RANGE[1]):
     rng = np.random.default_rng(0 + rank)
-    return rng.integers(CTX_RANGE[0], CTX_RANGE[1] + 1, size=n)
+    return rng.integers(CTX_RANGE[0], ctx_max + 1, size=n)
 
 
 def layer_weights(rank: int):
@@ -260,7 +260,7 @@ def run_b200(args, rank, world, local_rank):
                                 device_id=torch.device("cuda", local_rank))
     gd, qd = dims()
     gdn_w, qsa_w = layer_weights(rank)
-    ctx = contexts(rank)
+    ctx = contexts(rank, ctx_max=args.ctx_max)
     B = BATCH
     steps_total = args.warmup + 2 * args.steps + 40
     prov = kqb200.Provider(local_rank)
@@ -399,8 +399,9 @@ def run_b200(args, rank, world, local_rank):
         "dtype": "f32",
         "data": "synthetic",
         "config": {
-            "workload": "config3: 4-layer block (3 GDN + 1 QSA) decode, 64 sequences/GPU, ctx U[1k,32k] "
-                        "(seed 0+rank), in-proj Q4_K, out-proj Q6_K, index BF16, F32 state/KV",
+            "workload": f"config3: 4-layer block (3 GDN + 1 QSA) decode, 64 sequences/GPU, "
+                        f"ctx U[1k,{args.ctx_max // 1024}k] (seed 0+rank), in-proj Q4_K, out-proj Q6_K, "
+                        f"index BF16, F32 state/KV",
             "batch_per_gpu": B,
             "parallelism": f"sequence-sharded x{world} (no collective)",
             "l2": "working set per step >> 126 MB L2 (no flush needed)",
@@ -460,6 +461,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--breakdown", action="store_true", help="time every kernel family (extra steps)")
+    ap.add_argument("--ctx-max", type=int, default=CTX_RANGE[1],
+                    help="upper end of the context distribution (profiling runs use a small one)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

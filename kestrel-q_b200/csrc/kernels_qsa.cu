@@ -108,9 +108,13 @@ __device__ bool exact_block_key(const QsaDims &d, const QsaWeightsDev &w, const 
 
 // ------------------------------------------------------------ prepare
 //
-// grid (B); 256 threads.  Shared memory holds one head vector at a time.
+// grid (B, Hq + Hkv + Hi + 1); 128 threads.  blockIdx.y selects one head:
+// a query head (-> q_out), a key head (-> key cache row `pos`, with the
+// head's values), an index-query head (-> iq_out), or the raw index key
+// (-> raw cache row `pos`, then the key of the block this token completes).
+// Each head's RMS statistic is a sequential sum in the reference's order.
 
-constexpr int kPrepThreads = 256;
+constexpr int kPrepThreads = 128;
 
 __global__ void __launch_bounds__(kPrepThreads)
 qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
@@ -121,6 +125,7 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
     extern __shared__ float sh[];   // max(d, di) floats + 1
     if (qsa_error_raised(err)) return;
     const uint32_t b = blockIdx.x;
+    uint32_t role = blockIdx.y;
     const QsaSeq s = bt.s[b];
     const uint32_t pos = s.length;
     const float *prow = proj + (size_t)b * ldp;
@@ -131,48 +136,46 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
     float *inv_slot = sh + max(hd, di);
     bool bad = false;
 
-    // query heads: q part of the interleaved [q | gate] rows of head h
-    for (uint32_t h = 0; h < d.q_heads; ++h) {
+    if (role < d.q_heads) {
+        // query head: q part of the interleaved [q | gate] rows of the head
+        const uint32_t h = role;
         for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) vec[i] = prow[(size_t)h * 2 * hd + i];
         __syncthreads();
         exact_norm_rope_shared(vec, hd, w.q_norm, d.eps, w, d.rotary, pos, inv_slot, bad);
         for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) q_out[((size_t)b * d.q_heads + h) * hd + i] = vec[i];
-        __syncthreads();
-    }
-    // key heads -> key cache row `pos`; values copied as projected
-    const float *kproj = prow + (size_t)2 * d.q_heads * hd;
-    const float *vproj = kproj + kvw;
-    for (uint32_t h = 0; h < d.kv_heads; ++h) {
+    } else if ((role -= d.q_heads) < d.kv_heads) {
+        // key head -> key cache; the head's values are copied as projected
+        const uint32_t h = role;
+        const float *kproj = prow + (size_t)2 * d.q_heads * hd;
+        const float *vproj = kproj + kvw;
         for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) vec[i] = kproj[h * hd + i];
         __syncthreads();
         exact_norm_rope_shared(vec, hd, w.k_norm, d.eps, w, d.rotary, pos, inv_slot, bad);
-        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) s.key[(size_t)pos * kvw + h * hd + i] = vec[i];
-        __syncthreads();
-    }
-    for (uint32_t i = threadIdx.x; i < kvw; i += blockDim.x) {
-        float v = vproj[i];
-        if (!isfinite(v)) bad = true;
-        s.value[(size_t)pos * kvw + i] = v;
-    }
-    // index query heads
-    for (uint32_t h = 0; h < d.index_heads; ++h) {
+        for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
+            s.key[(size_t)pos * kvw + h * hd + i] = vec[i];
+            const float v = vproj[h * hd + i];
+            if (!isfinite(v)) bad = true;
+            s.value[(size_t)pos * kvw + h * hd + i] = v;
+        }
+    } else if ((role -= d.kv_heads) < d.index_heads) {
+        const uint32_t h = role;
         for (uint32_t i = threadIdx.x; i < di; i += blockDim.x) vec[i] = irow[h * di + i];
         __syncthreads();
         exact_norm_rope_shared(vec, di, w.iq_norm, d.eps, w, d.rotary, pos, inv_slot, bad);
         for (uint32_t i = threadIdx.x; i < di; i += blockDim.x) iq_out[((size_t)b * d.index_heads + h) * di + i] = vec[i];
+    } else {
+        // raw index key -> raw cache row `pos`
+        const float *rk = irow + (size_t)d.index_heads * di;
+        for (uint32_t i = threadIdx.x; i < di; i += blockDim.x) {
+            const float v = rk[i];
+            if (!isfinite(v)) bad = true;
+            s.raw[(size_t)pos * di + i] = v;
+        }
         __syncthreads();
-    }
-    // raw index key -> raw cache row `pos`
-    const float *rk = irow + (size_t)d.index_heads * di;
-    for (uint32_t i = threadIdx.x; i < di; i += blockDim.x) {
-        float v = rk[i];
-        if (!isfinite(v)) bad = true;
-        s.raw[(size_t)pos * di + i] = v;
-    }
-    __syncthreads();
-    // the token completes a block: cache that block's key
-    if ((pos + 1) % d.block == 0 && threadIdx.x == 0) {
-        if (!exact_block_key(d, w, s, pos / d.block, vec)) bad = true;
+        // the token completes a block: cache that block's key
+        if ((pos + 1) % d.block == 0 && threadIdx.x == 0) {
+            if (!exact_block_key(d, w, s, pos / d.block, vec)) bad = true;
+        }
     }
     if (__syncthreads_or(bad) && threadIdx.x == 0) qsa_raise(err, kErrNonFinite);
 }
@@ -183,9 +186,10 @@ void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
                         float *q_out, float *iq_out, ErrorWord err,
                         cudaStream_t stream) {
     size_t smem = (std::max(d.head_dim, d.index_dim) + 1) * sizeof(float);
+    dim3 grid(batch, d.q_heads + d.kv_heads + d.index_heads + 1);
     KernelTimer timer("qsa_prepare", stream);
-    qsa_prepare_kernel<<<batch, kPrepThreads, smem, stream>>>(d, w, b, proj, ldp, iproj, ldi,
-                                                             q_out, iq_out, err);
+    qsa_prepare_kernel<<<grid, kPrepThreads, smem, stream>>>(d, w, b, proj, ldp, iproj, ldi,
+                                                            q_out, iq_out, err);
     count_launch();
 }
 

@@ -179,6 +179,36 @@ proj_umma_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
 
     bool ok = true;
     uint32_t issued = 0;
+    // software pipeline: the raw bytes of chunk c+1 are loaded into
+    // registers while chunk c is decoded and stored
+    const bool a_live = wrow < m.rows;
+    const bool x_vec = (ldx & 3u) == 0u && (reinterpret_cast<uintptr_t>(x) & 15u) == 0u;
+    Raw32 raw_cur, raw_nxt;
+    float4 x_cur[4], x_nxt[4];
+    auto load_chunk = [&](uint32_t c, Raw32 &raw, float4 (&xv)[4]) {
+        const uint32_t k0 = c * kUK;
+        const uint32_t fa = k0 + a_half * 32;
+        raw.fast = 0u;
+        if (a_live && fa < m.cols) load_raw32(m, wptr, fa, raw);
+        const uint32_t fb = k0 + b_quarter * 16;
+        if (xb < batch && fb + 16 <= m.cols && x_vec) {
+            const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)xb * ldx + fb);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = src[i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float t[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t k = fb + 4 * i + j;
+                    t[j] = (xb < batch && k < m.cols) ? x[(size_t)xb * ldx + k] : 0.0f;
+                }
+                xv[i] = make_float4(t[0], t[1], t[2], t[3]);
+            }
+        }
+    };
+    if (c_begin < c_end) load_chunk(c_begin, raw_cur, x_cur);
     for (uint32_t c = c_begin; c < c_end; ++c) {
         const uint32_t it = c - c_begin;
         const int stage = it % kStages;
@@ -192,13 +222,14 @@ proj_umma_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
             const bool got = mbar_wait(&bars[stage], ((it - kStages) / kStages) & 1u);
             if (!__syncthreads_and(got)) { ok = false; break; }
         }
+        if (c + 1 < c_end) load_chunk(c + 1, raw_nxt, x_nxt);
         const uint32_t k0 = c * kUK;
         // A: weights, 32 elements per thread
         {
             float w[32];
             const uint32_t first = k0 + a_half * 32;
-            if (wrow < m.rows && first < m.cols) {
-                decode32_any(m, wptr, first, w);
+            if (a_live && first < m.cols) {
+                decode_raw32(m, raw_cur, wptr, first, w);
             } else {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) w[i] = 0.0f;
@@ -215,19 +246,10 @@ proj_umma_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
         // B: activations, 16 elements per thread
         {
             float v[16];
-            const uint32_t first = k0 + b_quarter * 16;
-            if (xb < batch && first + 16 <= m.cols && (ldx & 3u) == 0u &&
-                (reinterpret_cast<uintptr_t>(x) & 15u) == 0u) {
-                const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)xb * ldx + first);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    float4 q = src[i];
-                    v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    v[i] = (xb < batch && first + i < m.cols) ? x[(size_t)xb * ldx + first + i] : 0.0f;
+            for (int i = 0; i < 4; ++i) {
+                v[4 * i] = x_cur[i].x; v[4 * i + 1] = x_cur[i].y;
+                v[4 * i + 2] = x_cur[i].z; v[4 * i + 3] = x_cur[i].w;
             }
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -238,6 +260,9 @@ proj_umma_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                 *reinterpret_cast<uint4 *>(B_lo + off) = lo;
             }
         }
+        raw_cur = raw_nxt;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x_cur[i] = x_nxt[i];
         // make the generic-proxy stores visible to the tensor core (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();

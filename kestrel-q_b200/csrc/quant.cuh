@@ -318,4 +318,111 @@ __device__ __forceinline__ void decode32_any(const M &m, const uint8_t *row, uin
     }
 }
 
+// Two-phase form of decode32_any for software pipelining: load_raw32 issues
+// the 16-byte loads of a run (no use of the data), decode_raw32 decodes it
+// later.  Runs that are not vector-aligned, and F32 rows, are decoded
+// directly from memory by decode_raw32.
+struct Raw32 {
+    uint4 v[4];
+    uint32_t e;
+    uint32_t fast;
+};
+
+__device__ __forceinline__ uint4 ld16(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+
+template <typename M>
+__device__ __forceinline__ void load_raw32(const M &m, const uint8_t *row, uint32_t first, Raw32 &r) {
+    r.fast = ((first & 31u) == 0u && first + 32u <= m.cols && (m.row_bytes & 15u) == 0u &&
+              (reinterpret_cast<uintptr_t>(row) & 15u) == 0u) ? 1u : 0u;
+    if (!r.fast) return;
+    if (m.type == kTypeQ4_K) {
+        const uint8_t *b = row + (first >> 8) * 144u;
+        const uint32_t g = (first & 255u) >> 6;
+        r.v[0] = ld16(b);
+        r.v[1] = ld16(b + 16 + g * 32);
+        r.v[2] = ld16(b + 32 + g * 32);
+    } else if (m.type == kTypeQ6_K && m.layout == 1) {
+        const uint32_t nsb = m.cols >> 8, sb = first >> 8, w = first & 255u;
+        const uint32_t half = w >> 7, s = (w & 127u) >> 5;
+        const uint8_t *ql = row + sb * 128u + half * 64u + 32u * (s & 1u);
+        const uint8_t *qh = row + nsb * 128u + sb * 64u + half * 32u;
+        r.v[0] = ld16(ql);
+        r.v[1] = ld16(ql + 16);
+        r.v[2] = ld16(qh);
+        r.v[3] = ld16(qh + 16);
+        const uint32_t scp = *reinterpret_cast<const uint16_t *>(row + nsb * 192u + sb * 16u + half * 8u + 2u * s);
+        const uint32_t dp = *reinterpret_cast<const uint16_t *>(row + nsb * 208u + sb * 2u);
+        r.e = scp | (dp << 16);
+    } else if (m.type == kTypeQ8_0 && m.layout == 1) {
+        const uint32_t nb = m.cols >> 5, blk = first >> 5;
+        r.v[0] = ld16(row + blk * 32u);
+        r.v[1] = ld16(row + blk * 32u + 16);
+        r.e = *reinterpret_cast<const uint16_t *>(row + nb * 32u + blk * 2u);
+    } else if (m.type == kTypeBF16) {
+        const uint8_t *p = row + (size_t)first * 2u;
+        r.v[0] = ld16(p); r.v[1] = ld16(p + 16); r.v[2] = ld16(p + 32); r.v[3] = ld16(p + 48);
+    } else {
+        r.fast = 0u;
+    }
+}
+
+template <typename M>
+__device__ __forceinline__ void decode_raw32(const M &m, const Raw32 &r, const uint8_t *row, uint32_t first,
+                                             float (&out)[32]) {
+    if (!r.fast) {
+        decode32_any(m, row, first, out);
+        return;
+    }
+    if (m.type == kTypeQ4_K) {
+        uint8_t hdr[16], q[32];
+        bytes16(r.v[0], hdr);
+        bytes16(r.v[1], q);
+        bytes16(r.v[2], q + 16);
+        const uint32_t w = first & 255u, group = w >> 6, high = (w >> 5) & 1u;
+        const float d = half_bits_to_float((uint32_t)hdr[0] | ((uint32_t)hdr[1] << 8));
+        const float dmin = half_bits_to_float((uint32_t)hdr[2] | ((uint32_t)hdr[3] << 8));
+        uint32_t sc, mn;
+        q4k_scale_min(hdr + 4, (int)(2u * group + high), sc, mn);
+        const float dl = __fmul_rn(d, (float)sc), ml = __fmul_rn(dmin, (float)mn);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const uint32_t code = high ? (q[i] >> 4) : (q[i] & 15u);
+            out[i] = __fsub_rn(__fmul_rn(dl, (float)code), ml);
+        }
+    } else if (m.type == kTypeQ6_K) {
+        uint8_t lo[32], hi[32];
+        bytes16(r.v[0], lo);
+        bytes16(r.v[1], lo + 16);
+        bytes16(r.v[2], hi);
+        bytes16(r.v[3], hi + 16);
+        const uint32_t s = ((first & 255u) & 127u) >> 5;
+        const float d = half_bits_to_float(r.e >> 16);
+        const float s0 = __fmul_rn(d, (float)(int8_t)(r.e & 0xFFu));
+        const float s1 = __fmul_rn(d, (float)(int8_t)((r.e >> 8) & 0xFFu));
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+            const uint32_t nib = (s & 2u) ? (lo[l] >> 4) : (lo[l] & 15u);
+            const int code = (int)(nib | (((hi[l] >> (2u * s)) & 3u) << 4)) - 32;
+            out[l] = __fmul_rn(l < 16 ? s0 : s1, (float)code);
+        }
+    } else if (m.type == kTypeQ8_0) {
+        uint8_t c[32];
+        bytes16(r.v[0], c);
+        bytes16(r.v[1], c + 16);
+        const float d = half_bits_to_float(r.e & 0xFFFFu);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) out[i] = __fmul_rn((float)(int8_t)c[i], d);
+    } else {   // BF16
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t w4[4] = {r.v[j].x, r.v[j].y, r.v[j].z, r.v[j].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                out[8 * j + 2 * i] = __uint_as_float(w4[i] << 16);
+                out[8 * j + 2 * i + 1] = __uint_as_float(w4[i] & 0xFFFF0000u);
+            }
+        }
+    }
+}
+
 }  // namespace kqb
