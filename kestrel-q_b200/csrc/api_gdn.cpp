@@ -146,8 +146,9 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
     size_t need = Carve::round(items * ldp * 4) + Carve::round(items * 2 * gd.key_width * 4) +
                   Carve::round(items * Vd * 4) * 2 + Carve::round(items * Hv * 4) * 2 +
                   (mask ? Carve::round(items * H * 4) : 0) + 4096;
-    // split-K work space of the tensor-core projections (small batches only)
-    const size_t partial_floats = items <= 512 ? (size_t)kProjPartialSplits * items * std::max(ldp, H) : 0;
+    // work space of the tensor-core projections (in-proj and out-proj)
+    const size_t partial_floats = std::max(projection_workspace_floats((uint32_t)items, ldp, H),
+                                           projection_workspace_floats((uint32_t)items, H, Vd));
     need += Carve::round(partial_floats * 4);
     void *ws;
     kq_status st = c->workspace(need, &ws, diag);

@@ -265,7 +265,7 @@ kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
     st = context(&c, diagnostic);
     if (st != KQ_STATUS_OK) return st;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
-    const size_t partial_floats = (size_t)kProjPartialSplits * batch * rows;
+    const size_t partial_floats = projection_workspace_floats(batch, (uint32_t)rows, (uint32_t)columns);
     void *ws;
     st = c->workspace(Carve::round(partial_floats * 4) + 256, &ws, diagnostic);
     if (st != KQ_STATUS_OK) return st;
@@ -275,7 +275,7 @@ kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
     segs.count = 1;
     segs.m[0] = t->m;
     launch_projection(segs, x, (uint32_t)columns, y, (uint32_t)rows, batch, err, c->stream,
-                      static_cast<float *>(ws), partial_floats);
+                      partial_floats ? static_cast<float *>(ws) : nullptr, partial_floats);
     KQB_CUDA(cudaGetLastError(), diagnostic, "linear launch");
     provider->metrics.linear_requests += 1;
     return KQ_STATUS_OK;

@@ -195,11 +195,11 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     uint32_t max_blocks = 1;
     for (uint32_t b = 0; b < batch; ++b)
         max_blocks = std::max<uint32_t>(max_blocks, (uint32_t)((states[b]->length + tokens) / d.block));
-    // about 8 tiles of 32 selected tokens per split, and at least two waves
+    // about 8 tiles of 16 selected tokens per split, and at least two waves
     // of CTAs over the 148 SMs for small batches
-    const uint32_t tiles = (d.sel_capacity + 31) / 32;
+    const uint32_t tiles = (d.sel_capacity + 15) / 16;
     const uint32_t per_seq = std::min<uint32_t>(batch, kMaxBatch) * d.kv_heads;
-    uint32_t splits = std::max<uint32_t>((tiles + 7) / 8, (2 * 148 + per_seq - 1) / per_seq);
+    uint32_t splits = std::max<uint32_t>((tiles + 7) / 8, (3 * 148 + per_seq - 1) / per_seq);
     splits = std::max<uint32_t>(1, std::min<uint32_t>(splits, tiles));
     const size_t need = Carve::round(items * ldp * 4) + Carve::round(items * ldi * 4) +
                         Carve::round(items * qw * 4) + Carve::round((size_t)batch * qw * 4) +
@@ -208,7 +208,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                         Carve::round((size_t)batch * d.topk * 4) + Carve::round((size_t)batch * 4) +
                         Carve::round((size_t)batch * d.q_heads * splits * hd * 4) +
                         Carve::round((size_t)batch * d.q_heads * splits * 2 * 4) + 8192;
-    const size_t partial_floats = items <= 512 ? (size_t)kProjPartialSplits * items * std::max(ldp, H) : 0;
+    const size_t partial_floats = std::max(projection_workspace_floats((uint32_t)items, ldp, H),
+                                           projection_workspace_floats((uint32_t)items, H, qw));
     void *ws;
     kq_status st = c->workspace(need + Carve::round(partial_floats * 4), &ws, diag);
     if (st != KQ_STATUS_OK) return st;

@@ -58,10 +58,18 @@ void launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
                        float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
                        cudaStream_t stream, float *partial = nullptr,
                        size_t partial_floats = 0);
-// Tensor-core path (kernels_umma.cu), used for batches above 8.
+// Tensor-core path (kernels_umma.cu), used for batches above 8.  Returns
+// false (nothing launched) for shapes / types it does not cover.  `xtiles`
+// is work space of umma_xtile_bytes(batch, cols) bytes.
 bool launch_projection_umma(const ProjSegments &segs, const float *x, uint32_t ldx,
                             float *y, uint32_t ldy, uint32_t batch, float *partial,
-                            size_t partial_floats, ErrorWord err, cudaStream_t stream);
+                            size_t partial_floats, uint8_t *xtiles, size_t xtile_bytes,
+                            ErrorWord err, cudaStream_t stream);
+size_t umma_xtile_bytes(uint32_t batch, uint32_t cols);
+// Work space (in floats) that launch_projection uses for `batch` rows of
+// input with `cols` columns and output stride `ldy`: the activation tiles of
+// the tensor-core path plus split-K partials for batches up to 512.
+size_t projection_workspace_floats(uint32_t batch, uint32_t ldy, uint32_t cols);
 // Sequential-order product: each output is accumulated k = 0..K-1 from 0.0f
 // with separately rounded products and sums, i.e. bit-identical to the
 // reference's kq_f32_dot / kq_quantized_row_dot_f32.

@@ -533,13 +533,16 @@ qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
 
 // Tiled variant for head dimensions 128 / 256 (the BASELINE shapes).
 // grid (splits, Hkv, B); 256 threads = 8 warps; warp h owns query head
-// kvh*repeat + h.  The split's token range is walked in tiles of 32 selected
-// tokens whose K and V rows are staged with cp.async into double-buffered
-// shared memory (the next tile loads while the current one is consumed).
-// Logits: lane = token (float4 dot over the padded K rows, conflict-free);
-// online softmax per warp; P.V: lane = 8 consecutive features.
+// kvh*repeat + h.  The split's token range is walked in tiles of 16
+// selected tokens whose K and V rows are staged with cp.async into
+// double-buffered shared memory (the next tile loads while the current one
+// is consumed); 73 KB of shared memory lets three CTAs share an SM.
+// Logits: lanes l and l+16 each take half of token l's dot product
+// (float4 reads of padded K rows, conflict-free) and combine with a shuffle;
+// online softmax per warp; P.V: lane l owns features [4l, 4l+4) and
+// [HD/2 + 4l, HD/2 + 4l + 4) (consecutive lanes, conflict-free).
 
-constexpr int kAtTile = 32;
+constexpr int kAtTile = 16;
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -550,19 +553,19 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;\n" ::); }
 
 template <int HD>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(256, 3)
 qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
                         const uint32_t *__restrict__ selected,
                         const uint32_t *__restrict__ selected_count,
                         float *__restrict__ part_o, float *__restrict__ part_ml,
                         uint32_t splits, ErrorWord err) {
     constexpr int KLD = HD + 4;          // padded K row (conflict-free float4 reads)
-    constexpr int FPL = HD / 32;         // features per lane in P.V
+    constexpr int HALF = HD / 2;
     constexpr int CH = HD / 4;           // 16-byte chunks per row
     extern __shared__ __align__(16) float sm[];
     float *qs = sm;                                  // [8][HD]
-    float *ks = qs + 8 * HD;                         // [2][32][KLD]
-    float *vs = ks + 2 * kAtTile * KLD;              // [2][32][HD]
+    float *ks = qs + 8 * HD;                         // [2][16][KLD]
+    float *vs = ks + 2 * kAtTile * KLD;              // [2][16][HD]
     if (qsa_error_raised(err)) return;
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
     const QsaSeq s = bt.s[b];
@@ -612,12 +615,13 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     };
 
     float m_run = -INFINITY, l_run = 0.0f;
-    float acc[FPL];
+    float acc[8];
 #pragma unroll
-    for (int f = 0; f < FPL; ++f) acc[f] = 0.0f;
+    for (int f = 0; f < 8; ++f) acc[f] = 0.0f;
     const float scale = d.sqrt_head_dim;
     const bool active = (uint32_t)warp < heads;
-    const float *qh = qs + warp * HD;
+    const int tok_lane = lane & 15, part = lane >> 4;
+    const float *qh = qs + warp * HD + part * HALF;
 
     if (tile0 < tile1) load_tile(tile0, 0);
     for (uint32_t tile = tile0; tile < tile1; ++tile) {
@@ -630,10 +634,10 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
         }
         __syncthreads();
         if (active) {
-            const float *kr = ks + buf * kAtTile * KLD + lane * KLD;
+            const float *kr = ks + buf * kAtTile * KLD + tok_lane * KLD + part * HALF;
             float dot = 0.0f;
 #pragma unroll 8
-            for (int f = 0; f < HD; f += 4) {
+            for (int f = 0; f < HALF; f += 4) {
                 const float4 qv = *reinterpret_cast<const float4 *>(qh + f);
                 const float4 kv = *reinterpret_cast<const float4 *>(kr + f);
                 dot = fmaf(qv.x, kv.x, dot);
@@ -641,35 +645,40 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
                 dot = fmaf(qv.z, kv.z, dot);
                 dot = fmaf(qv.w, kv.w, dot);
             }
+            dot += __shfl_xor_sync(0xffffffffu, dot, 16);
             bool ok;
-            token_of(tile * kAtTile + lane, ok);
+            token_of(tile * kAtTile + tok_lane, ok);
             const float logit = ok ? dot / scale : -INFINITY;
             float mt = logit;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            for (int o = 8; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
             const float m_new = fmaxf(m_run, mt);
             const float corr = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
             const float p = ok ? expf(logit - m_new) : 0.0f;
             float ps = p;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
             l_run = l_run * corr + ps;
             m_run = m_new;
 #pragma unroll
-            for (int f = 0; f < FPL; ++f) acc[f] *= corr;
-            const float *vb = vs + buf * kAtTile * HD + lane * FPL;
+            for (int f = 0; f < 8; ++f) acc[f] *= corr;
+            // HD = 128: lanes 16..31 own no features; they read an in-bounds
+            // column and their sums are never stored
+            const bool pv_lane = lane * 4 < HALF;
+            const float *vb = vs + buf * kAtTile * HD + (pv_lane ? lane * 4 : 0);
 #pragma unroll 4
             for (int t = 0; t < kAtTile; ++t) {
-                const float pt = __shfl_sync(0xffffffffu, p, t);
-                const float *vr = vb + t * HD;
-#pragma unroll
-                for (int f = 0; f < FPL; f += 4) {
-                    const float4 vv = *reinterpret_cast<const float4 *>(vr + f);
-                    acc[f] = fmaf(pt, vv.x, acc[f]);
-                    acc[f + 1] = fmaf(pt, vv.y, acc[f + 1]);
-                    acc[f + 2] = fmaf(pt, vv.z, acc[f + 2]);
-                    acc[f + 3] = fmaf(pt, vv.w, acc[f + 3]);
-                }
+                const float pt = __shfl_sync(0xffffffffu, p, t);   // lanes without features read row 0..3
+                const float4 v0 = *reinterpret_cast<const float4 *>(vb + t * HD);
+                const float4 v1 = *reinterpret_cast<const float4 *>(vb + t * HD + HALF);
+                acc[0] = fmaf(pt, v0.x, acc[0]);
+                acc[1] = fmaf(pt, v0.y, acc[1]);
+                acc[2] = fmaf(pt, v0.z, acc[2]);
+                acc[3] = fmaf(pt, v0.w, acc[3]);
+                acc[4] = fmaf(pt, v1.x, acc[4]);
+                acc[5] = fmaf(pt, v1.y, acc[5]);
+                acc[6] = fmaf(pt, v1.z, acc[6]);
+                acc[7] = fmaf(pt, v1.w, acc[7]);
             }
         }
         __syncthreads();
@@ -677,10 +686,11 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     if (!active) return;
     const uint32_t qhead = kvh * heads + warp;
     const size_t slot = ((size_t)b * d.q_heads + qhead) * splits + split;
-#pragma unroll
-    for (int f = 0; f < FPL; f += 4)
-        *reinterpret_cast<float4 *>(part_o + slot * HD + lane * FPL + f) =
-            make_float4(acc[f], acc[f + 1], acc[f + 2], acc[f + 3]);
+    if (lane * 4 < HALF) {
+        *reinterpret_cast<float4 *>(part_o + slot * HD + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4 *>(part_o + slot * HD + HALF + lane * 4) =
+            make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
     if (lane == 0) {
         part_ml[slot * 2] = m_run;
         part_ml[slot * 2 + 1] = l_run;
