@@ -51,9 +51,8 @@ struct ErrorWord {
 };
 
 // ---- projections (kernels_proj.cu)
-// `partial` (may be null) is split-K work space of partial_floats floats;
-// kProjPartialSplits * batch * ldy floats let every shape use split K.
-constexpr int kProjPartialSplits = 8;
+// `partial` (may be null) is work space of partial_floats floats; the
+// tensor-core path runs when it holds projection_workspace_floats().
 void launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
                        float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
                        cudaStream_t stream, float *partial = nullptr,
@@ -62,13 +61,11 @@ void launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
 // false (nothing launched) for shapes / types it does not cover.  `xtiles`
 // is work space of umma_xtile_bytes(batch, cols) bytes.
 bool launch_projection_umma(const ProjSegments &segs, const float *x, uint32_t ldx,
-                            float *y, uint32_t ldy, uint32_t batch, float *partial,
-                            size_t partial_floats, uint8_t *xtiles, size_t xtile_bytes,
-                            ErrorWord err, cudaStream_t stream);
+                            float *y, uint32_t ldy, uint32_t batch, uint8_t *xtiles,
+                            size_t xtile_bytes, ErrorWord err, cudaStream_t stream);
 size_t umma_xtile_bytes(uint32_t batch, uint32_t cols);
 // Work space (in floats) that launch_projection uses for `batch` rows of
-// input with `cols` columns and output stride `ldy`: the activation tiles of
-// the tensor-core path plus split-K partials for batches up to 512.
+// input with `cols` columns: the activation tiles of the tensor-core path.
 size_t projection_workspace_floats(uint32_t batch, uint32_t ldy, uint32_t cols);
 // Sequential-order product: each output is accumulated k = 0..K-1 from 0.0f
 // with separately rounded products and sums, i.e. bit-identical to the

@@ -265,10 +265,9 @@ static void fill_tile_starts(ProjSegments &s, uint32_t unit) {
     s.tile_start[s.count] = acc;
 }
 
-size_t projection_workspace_floats(uint32_t batch, uint32_t ldy, uint32_t cols) {
+size_t projection_workspace_floats(uint32_t batch, uint32_t /*ldy*/, uint32_t cols) {
     if (batch <= 8) return 0;
-    const size_t xt = ((umma_xtile_bytes(batch, cols) + 255) & ~size_t(255)) / 4;
-    return xt + (batch <= 512 ? (size_t)kProjPartialSplits * batch * ldy : 0);
+    return ((umma_xtile_bytes(batch, cols) + 255) & ~size_t(255)) / 4;
 }
 
 void launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
@@ -276,19 +275,10 @@ void launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
                        cudaStream_t stream, float *partial, size_t partial_floats) {
     ProjSegments segs = in;
     KernelTimer timer("proj", stream);
-    if (batch > 8 && !force_simt_projection() && partial != nullptr) {
-        // work space: [activation tiles | split-K partials]
-        uint32_t cols = 0;
-        for (int i = 0; i < segs.count; ++i) cols = std::max(cols, segs.m[i].cols);
-        const size_t xt = (umma_xtile_bytes(batch, cols) + 255) & ~size_t(255);
-        if (partial_floats * 4 > xt) {
-            uint8_t *xtiles = reinterpret_cast<uint8_t *>(partial);
-            float *part = reinterpret_cast<float *>(xtiles + xt);
-            if (launch_projection_umma(segs, x, ldx, y, ldy, batch, part, partial_floats - xt / 4, xtiles, xt,
-                                       err, stream))
-                return;
-        }
-    }
+    if (batch > 8 && !force_simt_projection() && partial != nullptr &&
+        launch_projection_umma(segs, x, ldx, y, ldy, batch, reinterpret_cast<uint8_t *>(partial),
+                               partial_floats * 4, err, stream))
+        return;
     if (batch <= 8) {
         fill_tile_starts(segs, 1);
         uint32_t rows = segs.tile_start[segs.count];

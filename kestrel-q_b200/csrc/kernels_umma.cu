@@ -5,53 +5,82 @@
 // One CTA computes a 128 (weight rows, MMA M) x 64 (batch rows, MMA N) tile
 // of y^T with tcgen05.mma (kind::f16, BF16 operands, F32 accumulator in
 // TMEM).  F32 accuracy is kept with a three-term split: w = wh + wl and
-// x = xh + xl (bf16 each, the low part rounded from the residual), and
-// y ~= wh*xh + wh*xl + wl*xh, the dropped wl*xl term being ~2^-16 relative.
+// x = xh + xl (bf16 each), y ~= wh*xh + wh*xl + wl*xh; the dropped wl*xl
+// term and the rounding of the low parts are ~2^-16 relative.  BF16
+// weights are exact in bf16 and take two terms (w*xh + w*xl).
 //
-// Pipeline per K chunk of 64 (all 256 threads take part in every phase):
-//   1. cp.async stages, two chunks ahead, the chunk's raw GGUF bytes of the
-//      128 weight rows (16-byte pieces of each row: Q4_K header + quants,
-//      Q6_K/Q8_0 planes, BF16 values) and the chunk's activation tile, which
-//      a small kernel converted once per launch into bf16 hi/lo already in
-//      the shared-memory image the MMA reads (4-slot ring).
-//   2. The raw bytes are decoded from shared memory (quant.cuh, bit-exact
-//      with the reference decoder), split into bf16 hi/lo and stored in the
-//      canonical K-major 128-byte-swizzle layout (row r at r*128 B, 16-byte
-//      chunk c stored at chunk c ^ (r & 7)).  Dequantised weights never
-//      reach HBM.
-//   3. Thread 0 issues the 4 x 3 tcgen05.mma of the chunk and commits them
-//      to the ring slot's mbarrier.
-// Epilogue: tcgen05.ld 32x32b from TMEM.  One kernel instance per weight
-// type keeps the code small.
-// Split-K over gridDim.z writes partial tiles that a second kernel sums in
-// a fixed order (deterministic results).
+// Warp roles (576 threads, one CTA per SM):
+//   TMA warp     per K chunk of 64: 2-D TMA loads of the chunk's raw GGUF
+//                bytes (16-byte columns x 128 rows: Q4_K header + quants,
+//                Q6_K/Q8_0 planes, BF16 values) and a 1-D bulk copy of the
+//                chunk's activation tile, which a small kernel converted
+//                once per launch into bf16 hi/lo in the 128-byte-swizzled
+//                K-major image the MMA reads.  Ring of 6 (Q6_K, BF16) to
+//                9 (Q4_K) slots in 200 KB of shared memory.
+//   16 decode    each thread owns one weight row (its TMEM lane) and 16 K
+//   warps        values of the chunk: decodes them from shared memory with
+//                exact arithmetic (an FMA on a byte-to-float bit pattern,
+//                same values as the reference decoder, src/kq_numeric.c),
+//                splits them into bf16 hi/lo and stores both
+//                straight into TMEM with tcgen05.st: the A operand never
+//                touches shared memory.  Four A buffers in TMEM.
+//   MMA warp     one thread issues, per K-step of 16, one N=128 MMA
+//                wh * [xh | xl] (the activation tile's hi and lo halves are
+//                adjacent, so one instruction covers both terms) and one
+//                N=64 MMA wl * xh into a second accumulator, A from TMEM and
+//                B from shared memory, and commits to the chunk's mbarrier,
+//                which frees both the ring slot and the TMEM A buffer.
+//                (An M=128 tcgen05.mma costs about the same issue time for
+//                N=64 and N=128, so merging terms halves the MMA time.)
+// Epilogue: the decode warps read the three partial products with
+// tcgen05.ld and add them.
+// Split-K runs as a thread-block cluster along gridDim.z: every CTA leaves
+// its accumulator tile in shared memory and each CTA sums one slice of the
+// rows over all CTAs of the cluster in rank order (distributed shared
+// memory, deterministic, no second kernel and no partials in HBM).
 //
-// Every mbarrier wait is bounded; on time-out the kernel records an error
-// in the call's error word, waits (bounded) for its own MMAs, frees TMEM and
-// returns.
+// Every mbarrier wait is bounded.  A wait that gives up records an error in
+// the call's error word and raises a CTA-wide abort flag; every role then
+// leaves its loop, waits (bounded) for MMAs in flight, frees TMEM and the
+// CTA still reaches the cluster barriers, so no CTA is left waiting.
 #include "kernels.hpp"
 #include "quant.cuh"
 
 #include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <mutex>
+#include <unordered_map>
 
+#include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 namespace kqb {
 
 namespace {
 
-constexpr int kUM = 128;         // weight rows per CTA (MMA M)
-constexpr int kUN = 64;          // batch rows per CTA (MMA N)
-constexpr int kUK = 64;          // K per stage (one 128-byte swizzle row of bf16)
-constexpr int kRing = 4;                  // raw + activation slots (2 chunks ahead)
-constexpr int kDec = 2;                   // decoded weight tiles
-constexpr int kATile = kUM * kUK * 2;     // bytes of one bf16 A tile (16 KB)
+constexpr int kUM = 128;                  // weight rows per CTA (MMA M)
+constexpr int kUN = 64;                   // batch rows per CTA (MMA N)
+constexpr int kUK = 64;                   // K per chunk (one 128-byte swizzle row of bf16)
 constexpr int kBTile = kUN * kUK * 2;     // bytes of one bf16 B tile (8 KB)
-constexpr int kRawBytes = 16 * 1024;      // raw weight bytes of one chunk (max over types)
-constexpr int kSlotBytes = kRawBytes + 2 * kBTile;
-constexpr int kSmemBytes = kRing * kSlotBytes + kDec * 2 * kATile + 1024 /*align*/;
-constexpr uint32_t kTmemCols = 64;
-constexpr uint32_t kWaitLimit = 1u << 26;  // mbarrier polls before giving up
+constexpr int kXSlot = 2 * kBTile;        // activation tile of one chunk: [xh | xl]
+constexpr int kMaxXRing = 10;
+constexpr int kRawRing = 3;               // raw super-block slots
+constexpr int kSmemBudget = 200 * 1024;
+constexpr int kABufs = 4;                 // decoded A buffers in TMEM
+constexpr int kDecodeWarps = 16;
+constexpr int kTmaWarp = kDecodeWarps;
+constexpr int kMmaWarp = kDecodeWarps + 1;
+constexpr int kThreads = (kDecodeWarps + 2) * 32;
+constexpr int kAccStride = kUN + 1;       // floats per row of the split-K exchange tile
+// TMEM columns: [0, 128) wh * [xh | xl] (N = 128), [128, 192) wl * xh,
+// A buffer b at 192 + 64 b: hi 32 | lo 32.
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccLo = 128;
+constexpr uint32_t kABase = 192;
+static_assert(kABase + 64 * kABufs <= kTmemCols, "TMEM budget");
+constexpr uint32_t kWaitLimit = 1u << 22;  // mbarrier polls before giving up
 constexpr uint32_t kErrTimeout = 4;
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -62,8 +91,10 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
-// Bounded wait for the phase with parity `parity` to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Bounded wait for the phase with parity `parity` to complete.  Gives up
+// early when another role has raised the CTA's abort flag; raises it itself
+// when the poll limit is reached.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort) {
     const uint32_t addr = smem_u32(bar);
     for (uint32_t i = 0; i < kWaitLimit; ++i) {
         uint32_t done;
@@ -75,8 +106,42 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
+        if ((i & 63u) == 63u && *abort) return false;
     }
+    *abort = 1u;
     return false;
+}
+
+// Warp-uniform form: lane 0 waits, the result is broadcast.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, volatile uint32_t *abort) {
+    uint32_t ok = 0;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1u : 0u;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    return ok != 0;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// 2-D TMA tile load (no multicast) completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 1-D bulk copy global -> shared (no multicast) completing on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
 // K-major, 128B-swizzled shared-memory matrix descriptor (sm_100 format:
@@ -94,16 +159,19 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
 }
 
 // Instruction descriptor: F32 accumulate, BF16 A and B, both K-major,
-// N = kUN, M = kUM.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kUN >> 3) << 17) |
-                            ((uint32_t)(kUM >> 4) << 24);
+// M = kUM, N = n.
+constexpr uint32_t idesc_for(uint32_t n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((uint32_t)(kUM >> 4) << 24);
+}
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+// D (TMEM) += A (TMEM, 128 lanes x 16 K) * B (shared memory descriptor).
+template <uint32_t N>
+__device__ __forceinline__ void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(b), "n"(idesc_for(N)), "r"(accumulate));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
@@ -141,119 +209,302 @@ __device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t chunk) {
 }
 
 
-// Raw bytes per weight row and chunk staged in shared memory.
-template <uint32_t T> struct RawRow;
-template <> struct RawRow<kTypeQ4_K> { static constexpr uint32_t bytes = 48; };   // header 16 + quants 32
-template <> struct RawRow<kTypeQ6_K> { static constexpr uint32_t bytes = 128; };  // ql 64, qh 32, sc 16, d 16
-template <> struct RawRow<kTypeQ8_0> { static constexpr uint32_t bytes = 80; };   // codes 64, d 16
-template <> struct RawRow<kTypeBF16> { static constexpr uint32_t bytes = 128; };  // 64 values
-
-__device__ __forceinline__ void cp16(uint32_t smem_addr, const void *gmem) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gmem) : "memory");
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
 }
 
-// 16-byte piece `p` of row `row` for chunk `c` (same piece numbering as the
-// raw row layout above).  Returns false past the last piece.
-template <uint32_t T>
-__device__ __forceinline__ const uint8_t *raw_piece(const uint8_t *row, uint32_t cols, uint32_t c, uint32_t p) {
-    if constexpr (T == kTypeQ4_K) {
-        const uint8_t *b = row + (c >> 2) * 144u;           // 4 chunks per super-block
-        if (p == 0) return b;                               // d, dmin, scales
-        return b + 16u + (c & 3u) * 32u + (p - 1u) * 16u;   // quants of the 64-group
-    } else if constexpr (T == kTypeQ6_K) {
-        const uint32_t nsb = cols >> 8, sb = c >> 2, half = (c & 3u) >> 1;
-        if (p < 4) return row + sb * 128u + half * 64u + p * 16u;            // ql
-        if (p < 6) return row + nsb * 128u + sb * 64u + half * 32u + (p - 4u) * 16u;  // qh
-        if (p == 6) return row + nsb * 192u + sb * 16u;                     // scales
-        return row + ((nsb * 208u + sb * 2u) & ~15u);                        // d chunk
-    } else if constexpr (T == kTypeQ8_0) {
-        const uint32_t nb = cols >> 5;
-        if (p < 4) return row + (2u * c) * 32u + p * 16u;                    // codes of 2 blocks
-        return row + ((nb * 32u + 2u * c * 2u) & ~15u);                      // d chunk
-    } else {   // BF16
-        return row + (size_t)c * 128u + p * 16u;
-    }
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Matrix description with the weight type fixed at compile time, so the
-// decoders keep only the branch of that type.
-template <uint32_t T> struct TypedQ {
-    static constexpr uint32_t type = T;
-    uint32_t layout, cols, row_bytes;
+// Load from the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ float ld_dsmem(uint32_t local_addr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote));
+    return v;
+}
+
+// ---- exact decode into bf16 hi/lo pairs (f32x2 arithmetic)
+
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unf2(uint64_t v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// Splits a pair into bf16 hi (rounded half away from zero by an integer
+// add on the bits) and bf16 lo = w - hi (exact in F32 by Sterbenz, then
+// truncated: |error| <= 2^-16 |w|).  The residual is taken from the rounded
+// bits, not from an FP cancellation, so no compiler contraction can remove it.
+__device__ __forceinline__ void split_pair(uint64_t w, uint32_t &hi, uint32_t &lo) {
+    float w0, w1;
+    unf2(w, w0, w1);
+    const uint32_t b0 = __float_as_uint(w0) + 0x8000u, b1 = __float_as_uint(w1) + 0x8000u;
+    hi = __byte_perm(b0, b1, 0x7632u);
+    const uint64_t l = sub2(w, f2(__uint_as_float(b0 & 0xFFFF0000u), __uint_as_float(b1 & 0xFFFF0000u)));
+    float l0, l1;
+    unf2(l, l0, l1);
+    lo = __byte_perm(__float_as_uint(l0), __float_as_uint(l1), 0x7632u);
+}
+
+// f = 0.5 + u / 256 for the byte u = byte b of w (u < 128): one PRMT builds
+// the bit pattern 0x3Fuu0000 (exponent of 0.5, u in the mantissa's top 7
+// bits).
+__device__ __forceinline__ float half_plus_byte(uint32_t w, uint32_t b) {
+    return __uint_as_float(__byte_perm(w, 0x3F000000u, 0x7054u | (b << 8)));
+}
+// f = 0.5 + u / 65536 for any byte u = byte b of w (bit pattern 0x3F00uu00).
+__device__ __forceinline__ float half_plus_byte16(uint32_t w, uint32_t b) {
+    return __uint_as_float(__byte_perm(w, 0x3F000000u, 0x7504u | (b << 4)));
+}
+
+// f16 bits -> F32 with the hardware conversion (exact for every f16 value,
+// the same result as the reference's bit-level conversion).
+__device__ __forceinline__ float h2f(uint32_t bits) {
+    return __half2float(__ushort_as_half((unsigned short)bits));
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 &v, uint32_t i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Raw bytes of one super-block step (SC chunks of 64) for 128 rows, as the
+// TMA boxes leave them in shared memory.  Wide boxes keep the TMA engine
+// efficient; 128- and 64-byte boxes use the TMA swizzle so that a warp
+// reading 32 consecutive rows at the same column is free of bank conflicts.
+//   Q4_K (SC 4): [128][144]            whole super-blocks, no swizzle
+//   Q6_K (SC 4): ql [128][128] SW128 | qh [128][64] SW64 | sc [128][16] |
+//                d window [128][16]
+//   Q8_0 (SC 4): codes 2 x [128][128] SW128 | d [128][16]
+//   BF16 (SC 2): values 2 x [128][128] SW128
+template <uint32_t T> struct TypeCfg;
+template <> struct TypeCfg<kTypeQ4_K> { static constexpr uint32_t sc = 4, raw = 128 * 144; };
+template <> struct TypeCfg<kTypeQ6_K> { static constexpr uint32_t sc = 4, raw = 128 * 224; };
+template <> struct TypeCfg<kTypeQ8_0> { static constexpr uint32_t sc = 4, raw = 128 * 272; };
+template <> struct TypeCfg<kTypeBF16> { static constexpr uint32_t sc = 2, raw = 128 * 256; };
+
+// Ring depths per type within the shared-memory budget.
+template <uint32_t T> struct Ring {
+    static constexpr uint32_t raw = TypeCfg<T>::raw;
+    static constexpr uint32_t xdepth_fit = (kSmemBudget - kRawRing * raw) / kXSlot;
+    static constexpr uint32_t xdepth = xdepth_fit < (uint32_t)kMaxXRing ? xdepth_fit : kMaxXRing;
+    static constexpr uint32_t smem = kRawRing * raw + xdepth * kXSlot + 1024 /*align*/;
+    static_assert(xdepth >= (uint32_t)kABufs, "the A-buffer wait relies on xdepth >= kABufs");
+    static_assert(raw % 1024 == 0, "slots keep the 1024-byte swizzle alignment");
 };
 
+__device__ __forceinline__ uint4 lds16(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+// 16-byte chunk j of row r in a TMA 128B-swizzled box of 128-byte rows.
+__device__ __forceinline__ uint32_t sw128_at(uint32_t r, uint32_t j) { return r * 128u + ((j ^ (r & 7u)) << 4); }
+// 16-byte chunk j of row r in a TMA 64B-swizzled box of 64-byte rows.
+__device__ __forceinline__ uint32_t sw64_at(uint32_t r, uint32_t j) { return r * 64u + ((j ^ ((r >> 1) & 3u)) << 4); }
+
+// Decodes the 16 values [16q, 16q + 16) of chunk c of one staged row into
+// packed bf16 hi/lo pairs.  The decoded F32 values equal the reference
+// decoder's (src/kq_numeric.c): each is one correctly rounded FMA of exactly
+// representable operands, for example Q4_K: dl*code - ml = (256 dl) * f -
+// (128 dl + ml) with f = 0.5 + code/256.  BF16 values are their own hi part
+// and get a zero lo part (the MMA skips it).
 template <uint32_t T>
-__device__ __forceinline__ void raw_to_regs(const uint8_t *raw, uint32_t cols, uint32_t c, uint32_t half_,
-                                            Raw32 &r) {
-    r.fast = 1u;
+__device__ __forceinline__ void decode16(const uint8_t *raw, uint32_t row, uint32_t cols, uint32_t c, uint32_t q,
+                                         uint32_t (&hi)[8], uint32_t (&lo)[8]) {
     if constexpr (T == kTypeQ4_K) {
-        r.v[0] = *reinterpret_cast<const uint4 *>(raw);
-        r.v[1] = *reinterpret_cast<const uint4 *>(raw + 16);
-        r.v[2] = *reinterpret_cast<const uint4 *>(raw + 32);
+        // quants: nibble (q >> 1) of bytes 16*(q&1).. of the 64-group
+        const uint8_t *blk = raw + row * 144u;
+        const uint4 hdr = lds16(blk);
+        const uint4 qs = lds16(blk + 16u + (c & 3u) * 32u + 16u * (q & 1u));
+        const uint32_t high = q >> 1, j = 2u * (c & 3u) + high;
+        const float d = h2f(hdr.x & 0xFFFFu);
+        const float dmin = h2f(hdr.x >> 16);
+        auto sbyte = [&](uint32_t k) { return (word_of(hdr, 1u + (k >> 2)) >> (8u * (k & 3u))) & 0xFFu; };
+        uint32_t sc, mn;
+        if (j < 4) {
+            sc = sbyte(j) & 63u;
+            mn = sbyte(j + 4) & 63u;
+        } else {
+            sc = (sbyte(j + 4) & 15u) | ((sbyte(j - 4) >> 6) << 4);
+            mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
+        }
+        const float dl = __fmul_rn(d, (float)sc), ml = __fmul_rn(dmin, (float)mn);
+        const float a = __fmul_rn(dl, 256.0f), c0 = __fadd_rn(__fmul_rn(dl, 128.0f), ml);
+        const uint64_t A = f2(a, a), C0 = f2(-c0, -c0);
+        const uint32_t wq[4] = {qs.x, qs.y, qs.z, qs.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t nib = high ? (wq[k] >> 4) & 0x0F0F0F0Fu : wq[k] & 0x0F0F0F0Fu;
+            split_pair(fma2(A, f2(half_plus_byte(nib, 0), half_plus_byte(nib, 1)), C0), hi[2 * k], lo[2 * k]);
+            split_pair(fma2(A, f2(half_plus_byte(nib, 2), half_plus_byte(nib, 3)), C0), hi[2 * k + 1],
+                       lo[2 * k + 1]);
+        }
     } else if constexpr (T == kTypeQ6_K) {
+        // code = (ql nibble | qh 2 bits << 4) - 32, value = (d * sc) * code
         const uint32_t nsb = cols >> 8, sb = c >> 2, half = (c & 3u) >> 1;
-        const uint32_t s = 2u * (c & 1u) + half_;
-        r.v[0] = *reinterpret_cast<const uint4 *>(raw + 32u * half_);
-        r.v[1] = *reinterpret_cast<const uint4 *>(raw + 32u * half_ + 16u);
-        r.v[2] = *reinterpret_cast<const uint4 *>(raw + 64);
-        r.v[3] = *reinterpret_cast<const uint4 *>(raw + 80);
-        const uint32_t scp = *reinterpret_cast<const uint16_t *>(raw + 96u + half * 8u + 2u * s);
-        const uint32_t dp = *reinterpret_cast<const uint16_t *>(raw + 112u + ((nsb * 208u + sb * 2u) & 15u));
-        r.e = scp | (dp << 16);
+        const uint32_t h = q >> 1, s = 2u * (c & 1u) + h, part = q & 1u;
+        const uint4 ql = lds16(raw + sw128_at(row, 4u * half + 2u * h + part));
+        const uint4 qh = lds16(raw + 16384u + sw64_at(row, 2u * half + part));
+        const uint32_t scb = raw[24576u + row * 16u + half * 8u + 2u * s + part];
+        const uint32_t dbits =
+            *reinterpret_cast<const uint16_t *>(raw + 26624u + row * 16u + ((nsb * 208u + sb * 2u) & 15u));
+        const float scale = __fmul_rn(h2f(dbits), (float)(int8_t)scb);
+        const float a = __fmul_rn(scale, 256.0f), c0 = __fmul_rn(scale, 160.0f);   // both exact
+        const uint64_t A = f2(a, a), C0 = f2(-c0, -c0);
+        const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t nib = (c & 1u) ? (wl[k] >> 4) & 0x0F0F0F0Fu : wl[k] & 0x0F0F0F0Fu;
+            const uint32_t bw = nib | (((wh[k] >> (2u * s)) & 0x03030303u) << 4);
+            split_pair(fma2(A, f2(half_plus_byte(bw, 0), half_plus_byte(bw, 1)), C0), hi[2 * k], lo[2 * k]);
+            split_pair(fma2(A, f2(half_plus_byte(bw, 2), half_plus_byte(bw, 3)), C0), hi[2 * k + 1],
+                       lo[2 * k + 1]);
+        }
     } else if constexpr (T == kTypeQ8_0) {
-        const uint32_t nb = cols >> 5, blk = 2u * c + half_;
-        r.v[0] = *reinterpret_cast<const uint4 *>(raw + 32u * half_);
-        r.v[1] = *reinterpret_cast<const uint4 *>(raw + 32u * half_ + 16u);
-        r.e = *reinterpret_cast<const uint16_t *>(raw + 64u + ((nb * 32u + blk * 2u) & 15u));
-    } else {
-        const uint8_t *p = raw + 64u * half_;
-        r.v[0] = *reinterpret_cast<const uint4 *>(p);
-        r.v[1] = *reinterpret_cast<const uint4 *>(p + 16);
-        r.v[2] = *reinterpret_cast<const uint4 *>(p + 32);
-        r.v[3] = *reinterpret_cast<const uint4 *>(p + 48);
+        // value = code * d with code = (byte ^ 0x80) - 128
+        const uint32_t nb = cols >> 5, h = q >> 1, blk = 2u * c + h;
+        const uint4 cw = lds16(raw + ((c & 3u) >> 1) * 16384u + sw128_at(row, 4u * (c & 1u) + 2u * h + (q & 1u)));
+        const uint32_t dbits =
+            *reinterpret_cast<const uint16_t *>(raw + 32768u + row * 16u + ((nb * 32u + blk * 2u) & 15u));
+        const float d = h2f(dbits);
+        const float a = __fmul_rn(d, 65536.0f), c0 = __fmul_rn(d, 32896.0f);   // both exact
+        const uint64_t A = f2(a, a), C0 = f2(-c0, -c0);
+        const uint32_t wc[4] = {cw.x ^ 0x80808080u, cw.y ^ 0x80808080u, cw.z ^ 0x80808080u, cw.w ^ 0x80808080u};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            split_pair(fma2(A, f2(half_plus_byte16(wc[k], 0), half_plus_byte16(wc[k], 1)), C0), hi[2 * k],
+                       lo[2 * k]);
+            split_pair(fma2(A, f2(half_plus_byte16(wc[k], 2), half_plus_byte16(wc[k], 3)), C0), hi[2 * k + 1],
+                       lo[2 * k + 1]);
+        }
+    } else {   // BF16: the values are the hi part, no low part
+        const uint8_t *box = raw + (c & 1u) * 16384u;
+        const uint4 v0 = lds16(box + sw128_at(row, 2u * q)), v1 = lds16(box + sw128_at(row, 2u * q + 1u));
+        hi[0] = v0.x; hi[1] = v0.y; hi[2] = v0.z; hi[3] = v0.w;
+        hi[4] = v1.x; hi[5] = v1.y; hi[6] = v1.z; hi[7] = v1.w;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) lo[i] = 0u;
     }
 }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+                   "r"(r[7])
+                 : "memory");
+}
+
 
 }  // namespace
 
+// Tensor maps of the segments' raw bytes: 2-D uint8 [rows][row_bytes],
+// boxes of (width, box_rows); up to three widths per type (see TypeCfg).
+struct TmapSet {
+    CUtensorMap map[kMaxSegments][3];
+    uint32_t box_rows[kMaxSegments];
+};
+
 // Activations to bf16 hi/lo tiles in the MMA's shared-memory image:
 // out[btile][chunk] = { hi: 64 rows x 128 B swizzled, lo: same }.
-__global__ void xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t cols,
-                             uint32_t nchunks, uint8_t *__restrict__ out) {
-    const uint32_t bt = blockIdx.y, c = blockIdx.x;
-    const uint32_t r = threadIdx.x >> 2, q = threadIdx.x & 3;   // 64 rows x 4 quarters of 16
-    const uint32_t b = bt * kUN + r;
-    float v[16];
+// One CTA converts 16 rows of one chunk; one thread 8 values.
+__global__ void __launch_bounds__(128)
+xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t cols, uint32_t nchunks,
+             uint8_t *__restrict__ out) {
+    const uint32_t c = blockIdx.x >> 2, bt = blockIdx.y;
+    const uint32_t r = (blockIdx.x & 3u) * 16u + (threadIdx.x >> 3), q8 = threadIdx.x & 7u;
+    const uint32_t b = bt * kUN + r, k0 = c * kUK + q8 * 8u;
+    float v[8];
+    const float *src = x + (size_t)b * ldx + k0;
+    if (b < batch && k0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
+        const float4 a = *reinterpret_cast<const float4 *>(src);
+        const float4 e = *reinterpret_cast<const float4 *>(src + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = e.x; v[5] = e.y; v[6] = e.z; v[7] = e.w;
+    } else {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const uint32_t k = c * kUK + q * 16 + i;
-        v[i] = (b < batch && k < cols) ? x[(size_t)b * ldx + k] : 0.0f;
+        for (int i = 0; i < 8; ++i) v[i] = (b < batch && k0 + i < cols) ? src[i] : 0.0f;
     }
+    uint4 hi, lo;
+    pack8(v, hi, lo);
     uint8_t *tile = out + ((size_t)bt * nchunks + c) * (2 * kBTile);
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        uint4 hi, lo;
-        pack8(v + 8 * j, hi, lo);
-        const uint32_t off = sw128_off(r, q * 2 + j);
-        *reinterpret_cast<uint4 *>(tile + off) = hi;
-        *reinterpret_cast<uint4 *>(tile + kBTile + off) = lo;
+    const uint32_t off = sw128_off(r, q8);
+    *reinterpret_cast<uint4 *>(tile + off) = hi;
+    *reinterpret_cast<uint4 *>(tile + kBTile + off) = lo;
+}
+
+
+// TMA loads of super-block step `sb` (SC chunks) of 128 rows from row0.
+template <uint32_t T>
+__device__ __forceinline__ void load_raw(uint32_t dst, const CUtensorMap *maps, uint32_t cols, uint32_t sb,
+                                         int row0, uint64_t *bar) {
+    if constexpr (T == kTypeQ4_K) {
+        tma_load_2d(dst, &maps[0], (int)(sb * 144u), row0, bar);
+    } else if constexpr (T == kTypeQ6_K) {
+        const uint32_t nsb = cols >> 8;
+        tma_load_2d(dst, &maps[0], (int)(sb * 128u), row0, bar);                          // ql
+        tma_load_2d(dst + 16384u, &maps[1], (int)(nsb * 128u + sb * 64u), row0, bar);    // qh
+        tma_load_2d(dst + 24576u, &maps[2], (int)(nsb * 192u + sb * 16u), row0, bar);    // scales
+        tma_load_2d(dst + 26624u, &maps[2], (int)((nsb * 208u + sb * 2u) & ~15u), row0, bar);   // d window
+    } else if constexpr (T == kTypeQ8_0) {
+        const uint32_t nb = cols >> 5;
+        tma_load_2d(dst, &maps[0], (int)(sb * 256u), row0, bar);                          // codes, blocks 8sb..
+        tma_load_2d(dst + 16384u, &maps[0], (int)(sb * 256u + 128u), row0, bar);
+        tma_load_2d(dst + 32768u, &maps[1], (int)(nb * 32u + sb * 16u), row0, bar);       // d of 8 blocks
+    } else {
+        tma_load_2d(dst, &maps[0], (int)(sb * 256u), row0, bar);                          // 2 chunks of values
+        tma_load_2d(dst + 16384u, &maps[0], (int)(sb * 256u + 128u), row0, bar);
     }
 }
 
+// Bytes one load_raw delivers (full boxes, out-of-range rows zero-filled).
 template <uint32_t T>
-__global__ void __launch_bounds__(256, 1)
-proj_umma_kernel(ProjSegments segs, const uint8_t *__restrict__ xtiles, uint32_t nchunks_x,
-                 float *__restrict__ y, uint32_t ldy, uint32_t batch,
-                 float *__restrict__ partial, uint32_t kchunks_per_split, ErrorWord err) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ uint64_t bars[kRing];
-    __shared__ uint32_t tmem_base_slot;
-    if (*reinterpret_cast<volatile unsigned long long *>(err.word) != 0ull) return;
-    static_assert(RawRow<T>::bytes * kUM <= kRawBytes, "raw slot too small");
+__device__ __forceinline__ uint32_t raw_tx(uint32_t box_rows) {
+    if constexpr (T == kTypeQ4_K) return 144u * box_rows;
+    else if constexpr (T == kTypeQ6_K) return 224u * box_rows;
+    else if constexpr (T == kTypeQ8_0) return 272u * box_rows;
+    else return 256u * box_rows;
+}
 
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *ring = smem;                                   // kRing x [B hi | B lo | raw]
-    uint8_t *dec = smem + kRing * kSlotBytes;               // kDec x [A hi | A lo]
+template <uint32_t T>
+__global__ void __launch_bounds__(kThreads, 1)
+proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const uint8_t *__restrict__ xtiles,
+                 uint32_t nchunks_x, float *__restrict__ y, uint32_t ldy, uint32_t batch,
+                 uint32_t kchunks_per_split, ErrorWord err) {
+    constexpr uint32_t SC = TypeCfg<T>::sc, kRawBytes = Ring<T>::raw, kX = Ring<T>::xdepth;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ uint64_t rfull[kRawRing], rfree[kRawRing], xfull[kMaxXRing], mdone[kMaxXRing];
+    __shared__ uint64_t aready[kABufs], accum;
+    __shared__ uint32_t tmem_base_slot;
+    __shared__ volatile uint32_t abort_flag;
+    static_assert(kUM * kAccStride * 4 <= kX * kXSlot, "exchange tile does not fit");
+    // No early return anywhere: every CTA of a split-K cluster must reach
+    // both cluster barriers.
+    const bool skip = *reinterpret_cast<volatile unsigned long long *>(err.word) != 0ull;
+
+    uint8_t *raw_ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *x_ring = raw_ring + kRawRing * kRawBytes;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     int seg = 0;
@@ -262,15 +513,26 @@ proj_umma_kernel(ProjSegments segs, const uint8_t *__restrict__ xtiles, uint32_t
     const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * kUM;
     const uint32_t b0 = blockIdx.y * kUN;
     const uint32_t nchunks_total = (m.cols + kUK - 1) / kUK;
+    // kchunks_per_split is a multiple of SC, so c_begin starts a super-block step
     const uint32_t c_begin = blockIdx.z * kchunks_per_split;
     const uint32_t c_end = min(nchunks_total, c_begin + kchunks_per_split);
-    const uint32_t nchunks = c_end > c_begin ? c_end - c_begin : 0;
+    const uint32_t nchunks = (c_end > c_begin && !skip) ? c_end - c_begin : 0;
 
     if (tid == 0) {
-        for (int s = 0; s < kRing; ++s) mbar_init(&bars[s], 1);
+        for (int s = 0; s < kRawRing; ++s) {
+            mbar_init(&rfull[s], 1);
+            mbar_init(&rfree[s], 1);
+        }
+        for (uint32_t s = 0; s < kX; ++s) {
+            mbar_init(&xfull[s], 1);
+            mbar_init(&mdone[s], 1);
+        }
+        for (int b = 0; b < kABufs; ++b) mbar_init(&aready[b], kDecodeWarps);
+        mbar_init(&accum, 1);
+        abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(&tmem_base_slot)), "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -280,147 +542,155 @@ proj_umma_kernel(ProjSegments segs, const uint8_t *__restrict__ xtiles, uint32_t
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_slot;
 
-    // staging roles: pieces of the 128 raw rows, then the 16 KB x tile
-    constexpr uint32_t kPieces = RawRow<T>::bytes / 16;
-    auto stage_chunk = [&](uint32_t it) {
-        const uint32_t c = c_begin + it;
-        uint8_t *slot = ring + (it % kRing) * kSlotBytes;
-        const uint32_t raw_base = smem_u32(slot + 2 * kBTile);
-        for (uint32_t i = tid; i < kUM * kPieces; i += blockDim.x) {
-            const uint32_t r = i / kPieces, p = i % kPieces;
-            const uint32_t grow = min(row0 + r, m.rows - 1);   // rows past the end decode unused data
-            cp16(raw_base + r * RawRow<T>::bytes + p * 16u,
-                 raw_piece<T>(m.data + (size_t)grow * m.row_bytes, m.cols, c, p));
+    if (warp == kTmaWarp) {
+        // ---- producer: one thread issues every copy
+        if (lane == 0 && nchunks > 0) {
+            const CUtensorMap *maps = tmaps.map[seg];
+            const uint32_t rtx = raw_tx<T>(tmaps.box_rows[seg]);
+            const uint32_t sb0 = c_begin / SC;
+            for (uint32_t it = 0; it < nchunks; ++it) {
+                if (it % SC == 0) {
+                    // raw slot of step j was last used by step j - kRawRing
+                    const uint32_t j = it / SC, rs = j % kRawRing;
+                    if (j >= kRawRing && !mbar_wait(&rfree[rs], ((j - kRawRing) / kRawRing) & 1u, &abort_flag))
+                        break;
+                    mbar_expect_tx(&rfull[rs], rtx);
+                    load_raw<T>(smem_u32(raw_ring + rs * kRawBytes), maps, m.cols, sb0 + j, (int)row0, &rfull[rs]);
+                }
+                const uint32_t xs = it % kX;
+                if (it >= kX && !mbar_wait(&mdone[xs], ((it - kX) / kX) & 1u, &abort_flag)) break;
+                mbar_expect_tx(&xfull[xs], (uint32_t)kXSlot);
+                bulk_load(smem_u32(x_ring + xs * kXSlot),
+                          xtiles + ((size_t)blockIdx.y * nchunks_x + c_begin + it) * kXSlot, (uint32_t)kXSlot,
+                          &xfull[xs]);
+            }
         }
-        const uint8_t *xsrc = xtiles + ((size_t)blockIdx.y * nchunks_x + c) * (2 * kBTile);
-        const uint32_t xdst = smem_u32(slot);
-        for (uint32_t i = tid; i < 2 * kBTile / 16; i += blockDim.x) cp16(xdst + i * 16u, xsrc + i * 16u);
-    };
-    auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
+    } else if (warp == kMmaWarp) {
+        // ---- MMA issue: one thread
+        if (lane == 0) {
+            // x slot i's descriptor = slot 0's + i * kXSlot / 16 in the
+            // address field (shared addresses stay below 256 KB: no carry)
+            const uint64_t desc0 = sw128_desc(smem_u32(x_ring));
+            for (uint32_t it = 0; it < nchunks; ++it) {
+                const uint32_t xs = it % kX, b = it % kABufs;
+                if (!mbar_wait(&aready[b], (it / kABufs) & 1u, &abort_flag)) break;
+                if (!mbar_wait(&xfull[xs], (it / kX) & 1u, &abort_flag)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                // B: the slot's 128 swizzled rows are [xh (64 rows) | xl (64 rows)]
+                const uint64_t db = desc0 + (uint64_t)(xs * (kXSlot >> 4));
+                const uint32_t ah = tmem + kABase + b * 64u, al = ah + 32u;
+                const uint32_t first = it == 0 ? 0u : 1u;
+#pragma unroll
+                for (uint32_t kk = 0; kk < kUK / 16; ++kk) {
+                    // +32 bytes of K per step = +2 in the descriptor's address field
+                    umma_ts<2 * kUN>(tmem, ah + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
+                    if constexpr (T != kTypeBF16)
+                        umma_ts<kUN>(tmem + kAccLo, al + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
+                }
+                umma_commit(&mdone[xs]);
+                if (it % SC == SC - 1) umma_commit(&rfree[(it / SC) % kRawRing]);
+            }
+            umma_commit(&accum);   // completes once every MMA issued above has
+        }
+    } else {
+        // ---- decode warps: lane = weight row within the warp's TMEM quarter
+        const uint32_t quarter = warp & 3, q = warp >> 2;
+        const uint32_t row = quarter * 32u + lane;
+        const uint32_t lane_addr = (quarter * 32u) << 16;
+        for (uint32_t it = 0; it < nchunks; ++it) {
+            const uint32_t j = it / SC, rs = j % kRawRing, b = it % kABufs;
+            if (!mbar_wait_warp(&rfull[rs], (j / kRawRing) & 1u, &abort_flag)) break;
+            // A buffer b was last read by the MMAs of chunk it - kABufs
+            if (it >= kABufs && !mbar_wait_warp(&mdone[(it - kABufs) % kX], ((it - kABufs) / kX) & 1u,
+                                                &abort_flag))
+                break;
+            uint32_t hi[8], lo[8];
+            decode16<T>(raw_ring + rs * kRawBytes, row, m.cols, c_begin + it, q, hi, lo);
+            const uint32_t ta = tmem + lane_addr + kABase + b * 64u + q * 8u;
+            tmem_st8(ta, hi);
+            if constexpr (T != kTypeBF16) tmem_st8(ta + 32u, lo);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&aready[b]);
+        }
+    }
 
-    const uint32_t a_row = tid >> 1, a_half = tid & 1;
-    const bool a_live = row0 + a_row < m.rows;
-    bool ok = true;
-    uint32_t issued = 0;
-    if (nchunks > 0) stage_chunk(0);
-    commit();
-    if (nchunks > 1) stage_chunk(1);
-    commit();
-    for (uint32_t it = 0; it < nchunks; ++it) {
-        if (it >= 2) {
-            // MMAs of chunk it-2 read decode tile it%2 and ring slot (it+2)%4
-            const bool got = mbar_wait(&bars[(it - 2) % kRing], ((it - 2) / kRing) & 1u);
-            if (!__syncthreads_and(got)) { ok = false; break; }
-        }
-        if (it + 2 < nchunks) stage_chunk(it + 2);
-        commit();
-        asm volatile("cp.async.wait_group 2;" ::: "memory");
-        __syncthreads();
-        const uint32_t c = c_begin + it;
-        uint8_t *slot = ring + (it % kRing) * kSlotBytes;
-        uint8_t *A_hi = dec + (it % kDec) * 2 * kATile;
-        uint8_t *A_lo = A_hi + kATile;
-        {
-            float w[32];
-            if (a_live) {
-                Raw32 r;
-                raw_to_regs<T>(slot + 2 * kBTile + a_row * RawRow<T>::bytes, m.cols, c, a_half, r);
-                const TypedQ<T> tq{m.layout, m.cols, m.row_bytes};
-                decode_raw32(tq, r, nullptr, c * kUK + a_half * 32, w);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) w[i] = 0.0f;
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint4 hi, lo;
-                pack8(w + 8 * j, hi, lo);
-                const uint32_t off = sw128_off(a_row, a_half * 4 + j);
-                *reinterpret_cast<uint4 *>(A_hi + off) = hi;
-                *reinterpret_cast<uint4 *>(A_lo + off) = lo;
-            }
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t ah = smem_u32(A_hi), al = smem_u32(A_lo);
-            const uint32_t bh = smem_u32(slot), bl = smem_u32(slot + kBTile);
-#pragma unroll
-            for (int kk = 0; kk < kUK / 16; ++kk) {
-                const uint32_t koff = kk * 32;
-                const uint64_t dah = sw128_desc(ah + koff), dal = sw128_desc(al + koff);
-                const uint64_t dbh = sw128_desc(bh + koff), dbl = sw128_desc(bl + koff);
-                umma_bf16(tmem, dah, dbh, (it > 0 || kk > 0) ? 1u : 0u);
-                umma_bf16(tmem, dah, dbl, 1u);
-                umma_bf16(tmem, dal, dbh, 1u);
-            }
-            umma_commit(&bars[it % kRing]);
-        }
-        ++issued;
+    // ---- epilogue
+    bool ok = false;
+    if (warp < kDecodeWarps) {
+        ok = mbar_wait_warp(&accum, 0, &abort_flag);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (ok && issued > 0) {
-        const uint32_t last = issued - 1;
-        if (!mbar_wait(&bars[last % kRing], (last / kRing) & 1u)) ok = false;
-    }
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const bool all_ok = __syncthreads_and(ok);
-
-    const uint32_t lane_base = 32u * (warp & 3);
-    const uint32_t col_base = (uint32_t)(warp >> 2) * 32u;
-    const uint32_t row = row0 + lane_base + lane;
-    float *dst = partial ? partial + (size_t)blockIdx.z * batch * ldy : y;
-    if (all_ok && issued > 0) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem + (lane_base << 16) + col_base;
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-              "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-              "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-              "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (row < m.rows) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const uint32_t b = b0 + col_base + j;
-                if (b < batch) dst[(size_t)b * ldy + segs.out_offset[seg] + row] = __uint_as_float(r[j]);
-            }
-        }
-    } else if (all_ok && partial != nullptr && row < m.rows) {
-        // an empty split still owns its slice of the partial buffer
-        for (int j = 0; j < 32; ++j) {
-            const uint32_t b = b0 + col_base + j;
-            if (b < batch) dst[(size_t)b * ldy + segs.out_offset[seg] + row] = 0.0f;
-        }
-    }
-    if (!all_ok && tid == 0) {
+    const bool all_ok = __syncthreads_and(warp >= kDecodeWarps || ok) && abort_flag == 0u;
+    if (!all_ok && tid == 0)
         atomicCAS(err.word, 0ull, ((unsigned long long)kErrTimeout << 32) | err.call_id);
-        for (uint32_t s = 0; s < kRing; ++s) (void)mbar_wait(&bars[s], 0), (void)mbar_wait(&bars[s], 1);
+
+    // accumulator: decode warp w reads TMEM lanes 32*(w&3).., columns 16*(w>>2)..
+    const uint32_t lane_base = 32u * (warp & 3);
+    const uint32_t col_base = (uint32_t)(warp >> 2) * 16u;
+    const uint32_t trow = lane_base + lane;
+    float acc[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] = 0.0f;   // empty split: contributes zero
+    if (warp < kDecodeWarps && all_ok && nchunks > 0) {
+        // y = wh*xh + wh*xl + wl*xh, summed in that order
+        uint32_t r0[16], r1[16], r2[16];
+        const uint32_t taddr = tmem + (lane_base << 16) + col_base;
+        tmem_ld16(taddr, r0);
+        tmem_ld16(taddr + kUN, r1);
+        if constexpr (T != kTypeBF16) tmem_ld16(taddr + kAccLo, r2);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            acc[j] = __fadd_rn(__uint_as_float(r0[j]), __uint_as_float(r1[j]));
+            if constexpr (T != kTypeBF16) acc[j] = __fadd_rn(acc[j], __uint_as_float(r2[j]));
+        }
+    }
+    const bool write = all_ok && !skip;
+    const uint32_t nsplit = gridDim.z;
+    if (nsplit == 1) {
+        const uint32_t row = row0 + trow;
+        if (warp < kDecodeWarps && write && row < m.rows) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const uint32_t b = b0 + col_base + j;
+                if (b < batch) y[(size_t)b * ldy + segs.out_offset[seg] + row] = acc[j];
+            }
+        }
+    } else {
+        // exchange tile in the drained activation ring: [128 rows][kAccStride]
+        float *xt = reinterpret_cast<float *>(x_ring);
+        if (warp < kDecodeWarps) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xt[trow * kAccStride + col_base + j] = acc[j];
+        }
+        cluster_sync();
+        const uint32_t rank = cluster_rank();
+        const uint32_t rows_per = kUM / nsplit;
+        const uint32_t base = smem_u32(xt);
+        for (uint32_t i = tid; i < rows_per * kUN; i += kThreads) {
+            const uint32_t rr = i % rows_per, bb = i / rows_per;
+            const uint32_t lr = rank * rows_per + rr;
+            const uint32_t off = base + (lr * kAccStride + bb) * 4u;
+            float v[8];
+#pragma unroll
+            for (uint32_t z = 0; z < 8; ++z) v[z] = z < nsplit ? ld_dsmem(off, z) : 0.0f;
+            float sum = v[0];
+#pragma unroll
+            for (uint32_t z = 1; z < 8; ++z)
+                if (z < nsplit) sum = __fadd_rn(sum, v[z]);
+            const uint32_t row = row0 + lr, b = b0 + bb;
+            if (write && row < m.rows && b < batch) y[(size_t)b * ldy + segs.out_offset[seg] + row] = sum;
+        }
+        cluster_sync();   // peers finish reading this CTA's tile before it exits
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
-}
-
-// Sums the split-K partial tiles in split order (deterministic).
-__global__ void splitk_reduce_kernel(const float *__restrict__ partial, uint32_t splits, uint32_t batch,
-                                     uint32_t ldy, float *__restrict__ y, uint32_t col0, uint32_t cols) {
-    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (uint64_t)batch * cols) return;
-    const uint32_t b = (uint32_t)(i / cols), c = col0 + (uint32_t)(i % cols);
-    const size_t off = (size_t)b * ldy + c;
-    float s = partial[off];
-    for (uint32_t z = 1; z < splits; ++z) s += partial[(size_t)z * batch * ldy + off];
-    y[off] = s;
 }
 
 bool umma_supported(const QMatrix &m) {
@@ -439,53 +709,216 @@ size_t umma_xtile_bytes(uint32_t batch, uint32_t cols) {
     return (size_t)((batch + kUN - 1) / kUN) * ((cols + kUK - 1) / kUK) * 2 * kBTile;
 }
 
-// Launches one group of segments that share a weight type.
-static void launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, uint32_t nchunks_x, float *y,
-                         uint32_t ldy, uint32_t batch, float *partial, size_t partial_floats, ErrorWord err,
+
+// ---- tensor maps (host)
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        (void)cudaGetLastError();
+    });
+    return fn;
+}
+
+struct MapKey {
+    const uint8_t *data;
+    uint32_t rows, row_bytes, width, swizzle;
+    bool operator==(const MapKey &o) const {
+        return data == o.data && rows == o.rows && row_bytes == o.row_bytes && width == o.width &&
+               swizzle == o.swizzle;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        return std::hash<const void *>()(k.data) ^ ((size_t)k.rows << 20) ^ ((size_t)k.row_bytes << 40) ^
+               ((size_t)k.width << 8) ^ (size_t)k.swizzle;
+    }
+};
+
+// Tensor map of a matrix's raw bytes with boxes `width` bytes wide (cached:
+// provider matrices live as long as the provider, and a reused address with
+// the same shape encodes the same map).
+static bool tensor_map(const QMatrix &m, uint32_t width, CUtensorMapSwizzle swizzle, CUtensorMap *out) {
+    static std::mutex mu;
+    static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{m.data, m.rows, m.row_bytes, width, (uint32_t)swizzle};
+    std::lock_guard<std::mutex> lk(mu);
+    auto itr = cache.find(key);
+    if (itr != cache.end()) {
+        *out = itr->second;
+        return true;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return false;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {m.row_bytes, m.rows};
+    const cuuint64_t strides[1] = {m.row_bytes};
+    const cuuint32_t box[2] = {width, std::min<uint32_t>(m.rows, kUM)};
+    const cuuint32_t estr[2] = {1u, 1u};
+    if (fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(m.data), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (cache.size() > 4096) cache.clear();
+    cache.emplace(key, map);
+    *out = map;
+    return true;
+}
+
+// The maps one segment of type T needs (the box widths of TypeCfg).
+template <uint32_t T>
+static bool segment_maps(const QMatrix &m, CUtensorMap (&maps)[3]) {
+    if constexpr (T == kTypeQ4_K) {
+        return tensor_map(m, 144, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[0]);
+    } else if constexpr (T == kTypeQ6_K) {
+        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0]) &&
+               tensor_map(m, 64, CU_TENSOR_MAP_SWIZZLE_64B, &maps[1]) &&
+               tensor_map(m, 16, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[2]);
+    } else if constexpr (T == kTypeQ8_0) {
+        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0]) &&
+               tensor_map(m, 16, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[1]);
+    } else {
+        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0]);
+    }
+}
+
+static bool maps_for(const QMatrix &m, CUtensorMap (&maps)[3]) {
+    switch (m.type) {
+    case kTypeQ4_K: return segment_maps<kTypeQ4_K>(m, maps);
+    case kTypeQ6_K: return segment_maps<kTypeQ6_K>(m, maps);
+    case kTypeQ8_0: return segment_maps<kTypeQ8_0>(m, maps);
+    default: return segment_maps<kTypeBF16>(m, maps);
+    }
+}
+
+// Split count: 1, 2, 4 or 8 (a cluster of that many CTAs along z, at most
+// `max_splits`), chosen to minimise waves x (chunks per CTA + ~8 chunks of
+// pipeline fill and epilogue) + 2 per cluster member for the
+// distributed-shared-memory reduction, with one CTA per SM.  The constants
+// are fitted to measured B200 times of the in-/out-projection shapes.
+static uint32_t choose_splits(uint32_t tiles, uint32_t nchunks, uint32_t max_splits) {
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    uint32_t best = 1;
+    double best_cost = 1e30;
+    for (uint32_t s = 1; s <= max_splits; s *= 2) {
+        if (s > 1 && nchunks < 4 * s) break;
+        const double waves = std::ceil((double)tiles * s / sms);
+        const double cost = waves * ((nchunks + s - 1) / s + 8.0) + (s > 1 ? 2.0 * s : 0.0);
+        if (cost < best_cost - 1e-9) { best_cost = cost; best = s; }
+    }
+    return best;
+}
+
+// Largest split cluster (8, 4, 2 or 1) the device can co-schedule for this
+// kernel; queried once per type.
+template <uint32_t T>
+static uint32_t max_splits_for() {
+    static uint32_t cached = 0;
+    if (cached == 0) {
+        cudaFuncSetAttribute(proj_umma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Ring<T>::smem);
+        uint32_t best = 1;
+        for (uint32_t s = 8; s >= 2; s /= 2) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(1, 1, s);
+            cfg.blockDim = dim3(kThreads);
+            cfg.dynamicSmemBytes = Ring<T>::smem;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = 1;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = s;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, proj_umma_kernel<T>, &cfg) == cudaSuccess && n > 0) {
+                best = s;
+                break;
+            }
+        }
+        (void)cudaGetLastError();
+        cached = best;
+    }
+    return cached;
+}
+
+template <uint32_t T>
+static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &segs, const uint8_t *xt,
+                         uint32_t nchunks_x, float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
                          cudaStream_t stream) {
-    uint32_t acc = 0, cols = 0, col_lo = UINT32_MAX, col_hi = 0, covered = 0;
+    TmapSet maps;
+    for (int i = 0; i < segs.count; ++i) {
+        if (!segment_maps<T>(segs.m[i], maps.map[i])) return false;
+        maps.box_rows[i] = std::min<uint32_t>(segs.m[i].rows, kUM);
+    }
+    const uint32_t btiles = (batch + kUN - 1) / kUN;
+    static const int forced = [] {
+        const char *e = getenv("KQ_B200_PROJ_SPLITS");   // tuning: fixed split count
+        return e ? atoi(e) : 0;
+    }();
+    uint32_t splits = choose_splits(tiles * btiles, nchunks, max_splits_for<T>());
+    if (forced == 1 || forced == 2 || forced == 4 || forced == 8)
+        splits = std::min<uint32_t>((uint32_t)forced, max_splits_for<T>());
+    // chunks per split: whole super-block steps
+    constexpr uint32_t SC = TypeCfg<T>::sc;
+    const uint32_t per = ((nchunks + splits - 1) / splits + SC - 1) / SC * SC;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(tiles, btiles, splits);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Ring<T>::smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = splits;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, proj_umma_kernel<T>, maps, segs, xt, nchunks_x, y, ldy, batch, per, err);
+    return true;
+}
+
+// Launches one group of segments that share a weight type.
+static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, uint32_t nchunks_x, float *y,
+                         uint32_t ldy, uint32_t batch, ErrorWord err, cudaStream_t stream) {
+    uint32_t acc = 0, cols = 0;
     for (int i = 0; i < segs.count; ++i) {
         segs.tile_start[i] = acc;
         acc += (segs.m[i].rows + kUM - 1) / kUM;
         cols = std::max(cols, segs.m[i].cols);
-        col_lo = std::min(col_lo, segs.out_offset[i]);
-        col_hi = std::max(col_hi, segs.out_offset[i] + segs.m[i].rows);
-        covered += segs.m[i].rows;
     }
     segs.tile_start[segs.count] = acc;
-    const uint32_t btiles = (batch + kUN - 1) / kUN;
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
-    // split K until there are about two CTAs per SM, keeping >= 4 chunks
-    uint32_t splits = 1;
-    while (splits < kProjPartialSplits && acc * btiles * splits < 2 * 148 && nchunks / (splits * 2) >= 4)
-        splits *= 2;
-    if (splits > 1 && (partial == nullptr || partial_floats < (size_t)splits * batch * ldy)) splits = 1;
-    if (covered != col_hi - col_lo) splits = 1;   // the reduce covers one contiguous range
-    const uint32_t per = (nchunks + splits - 1) / splits;
-    dim3 grid(acc, btiles, splits);
-    float *part = splits > 1 ? partial : nullptr;
-#define KQB_LAUNCH(TT)                                                                              \
-    cudaFuncSetAttribute(proj_umma_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes); \
-    proj_umma_kernel<TT><<<grid, 256, kSmemBytes, stream>>>(segs, xt, nchunks_x, y, ldy, batch, part, per, err)
+    bool ok;
     switch (type) {
-    case kTypeQ4_K: KQB_LAUNCH(kTypeQ4_K); break;
-    case kTypeQ6_K: KQB_LAUNCH(kTypeQ6_K); break;
-    case kTypeQ8_0: KQB_LAUNCH(kTypeQ8_0); break;
-    default: KQB_LAUNCH(kTypeBF16); break;
+    case kTypeQ4_K: ok = launch_typed<kTypeQ4_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream); break;
+    case kTypeQ6_K: ok = launch_typed<kTypeQ6_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream); break;
+    case kTypeQ8_0: ok = launch_typed<kTypeQ8_0>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream); break;
+    default: ok = launch_typed<kTypeBF16>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream); break;
     }
-#undef KQB_LAUNCH
-    count_launch();
-    if (splits > 1) {
-        const uint64_t n = (uint64_t)batch * (col_hi - col_lo);
-        splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(partial, splits, batch, ldy, y,
-                                                                            col_lo, col_hi - col_lo);
-        count_launch();
-    }
+    if (ok) count_launch();
+    return ok;
 }
 
 bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx, float *y, uint32_t ldy,
-                            uint32_t batch, float *partial, size_t partial_floats, uint8_t *xtiles,
-                            size_t xtile_bytes, ErrorWord err, cudaStream_t stream) {
+                            uint32_t batch, uint8_t *xtiles, size_t xtile_bytes, ErrorWord err,
+                            cudaStream_t stream) {
     uint32_t cols = 0;
     for (int i = 0; i < in.count; ++i) {
         if (!umma_supported(in.m[i])) return false;
@@ -494,11 +927,16 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
     for (int i = 1; i < in.count; ++i)
         if (in.m[i].cols != cols) return false;
     if (xtiles == nullptr || xtile_bytes < umma_xtile_bytes(batch, cols)) return false;
+    // tensor maps first, so that a failure launches nothing
+    for (int i = 0; i < in.count; ++i) {
+        CUtensorMap maps[3];
+        if (!maps_for(in.m[i], maps)) return false;
+    }
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
-    dim3 xg(nchunks, (batch + kUN - 1) / kUN);
-    xconv_kernel<<<xg, 256, 0, stream>>>(x, ldx, batch, cols, nchunks, xtiles);
+    const dim3 xg(nchunks * 4, (batch + kUN - 1) / kUN);
+    xconv_kernel<<<xg, 128, 0, stream>>>(x, ldx, batch, cols, nchunks, xtiles);
     count_launch();
-    // one launch per weight type; the partial buffer is reused in order
+    // one launch per weight type present
     bool done[kMaxSegments] = {};
     for (int i = 0; i < in.count; ++i) {
         if (done[i]) continue;
@@ -510,7 +948,7 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
             ++g.count;
             done[j] = true;
         }
-        launch_group(in.m[i].type, g, xtiles, nchunks, y, ldy, batch, partial, partial_floats, err, stream);
+        launch_group(in.m[i].type, g, xtiles, nchunks, y, ldy, batch, err, stream);
     }
     return true;
 }
