@@ -153,6 +153,35 @@ kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
                                             float *y,
                                             kq_diagnostic *diagnostic);
 
+/* Allocation-free form of kq_b200_provider_linear_batch_f32; it has no
+ * counterpart in the reference.  For callers that cannot call cudaMalloc:
+ * a serving loop whose HBM is fully committed (KV cache, fixed budget), a
+ * host framework whose caching allocator owns device memory, or a
+ * latency-bound loop where cudaMalloc/cudaFree would synchronise the device.
+ * It allocates nothing: its scratch is one 4 MiB array compiled into the
+ * library (held on every GPU that loads it until exit), and it calls no
+ * cudaMalloc, cudaFree or other allocating routine.
+ *   - Limit: batches above 8 need ceil(batch/64) * ceil(columns/64) * 16 KiB
+ *     of activation tiles, at most 4 MiB - 256 B; larger calls return
+ *     KQ_STATUS_LIMIT_EXCEEDED.
+ *   - Runs on `cuda_stream` (NULL: the legacy default stream) and waits for
+ *     it before returning, so non-finite input is reported by this call
+ *     (KQ_STATUS_NUMERIC_DOMAIN).
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that call before any stream capture.
+ *   - Every call on a device shares the array (the last call's contents
+ *     stay in it): calls whose kernels overlap on the GPU race.
+ * The caller's current device is restored on return. */
+kq_status kq_b200_provider_linear_batch_f32_static(kq_weight_provider *provider,
+                                                   const kq_semantic_tensor *semantic,
+                                                   uint64_t rows,
+                                                   uint64_t columns,
+                                                   const float *x,
+                                                   uint32_t batch,
+                                                   float *y,
+                                                   void *cuda_stream,
+                                                   kq_diagnostic *diagnostic);
+
 typedef struct kq_b200_gdn_tensors {
     const kq_semantic_tensor *a_log;    /* F32 [Hv] */
     const kq_semantic_tensor *conv;     /* F32 [C*K] */

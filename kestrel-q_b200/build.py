@@ -35,6 +35,7 @@ SOURCES = [
     "api_provider.cpp",
     "api_gdn.cpp",
     "api_qsa.cpp",
+    "api_static.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -59,10 +59,13 @@ void launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
                        size_t partial_floats = 0);
 // Tensor-core path (kernels_umma.cu), used for batches above 8.  Returns
 // false (nothing launched) for shapes / types it does not cover.  `xtiles`
-// is work space of umma_xtile_bytes(batch, cols) bytes.
+// is work space of umma_xtile_bytes(batch, cols) bytes.  `cache_maps`
+// false encodes the TMA descriptors on the stack instead of the host-side
+// descriptor cache (no host allocation).
 bool launch_projection_umma(const ProjSegments &segs, const float *x, uint32_t ldx,
                             float *y, uint32_t ldy, uint32_t batch, uint8_t *xtiles,
-                            size_t xtile_bytes, ErrorWord err, cudaStream_t stream);
+                            size_t xtile_bytes, ErrorWord err, cudaStream_t stream,
+                            bool cache_maps = true);
 size_t umma_xtile_bytes(uint32_t batch, uint32_t cols);
 // Work space (in floats) that launch_projection uses for `batch` rows of
 // input with `cols` columns: the activation tiles of the tensor-core path.

@@ -746,18 +746,23 @@ struct MapKeyHash {
     }
 };
 
-// Tensor map of a matrix's raw bytes with boxes `width` bytes wide (cached:
-// provider matrices live as long as the provider, and a reused address with
-// the same shape encodes the same map).
-static bool tensor_map(const QMatrix &m, uint32_t width, CUtensorMapSwizzle swizzle, CUtensorMap *out) {
+// Tensor map of a matrix's raw bytes with boxes `width` bytes wide, cached
+// when `cache` is set (provider matrices live as long as the provider, and a
+// reused address with the same shape encodes the same map); without it the
+// map is encoded straight into *out and no host memory is allocated.
+static bool tensor_map(const QMatrix &m, uint32_t width, CUtensorMapSwizzle swizzle, CUtensorMap *out,
+                       bool cache_maps = true) {
     static std::mutex mu;
     static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
     const MapKey key{m.data, m.rows, m.row_bytes, width, (uint32_t)swizzle};
-    std::lock_guard<std::mutex> lk(mu);
-    auto itr = cache.find(key);
-    if (itr != cache.end()) {
-        *out = itr->second;
-        return true;
+    std::unique_lock<std::mutex> lk(mu, std::defer_lock);
+    if (cache_maps) {
+        lk.lock();
+        auto itr = cache.find(key);
+        if (itr != cache.end()) {
+            *out = itr->second;
+            return true;
+        }
     }
     EncodeTiledFn fn = encode_fn();
     if (fn == nullptr) return false;
@@ -770,35 +775,37 @@ static bool tensor_map(const QMatrix &m, uint32_t width, CUtensorMapSwizzle swiz
            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
-    if (cache.size() > 4096) cache.clear();
-    cache.emplace(key, map);
+    if (cache_maps) {
+        if (cache.size() > 4096) cache.clear();
+        cache.emplace(key, map);
+    }
     *out = map;
     return true;
 }
 
 // The maps one segment of type T needs (the box widths of TypeCfg).
 template <uint32_t T>
-static bool segment_maps(const QMatrix &m, CUtensorMap (&maps)[3]) {
+static bool segment_maps(const QMatrix &m, CUtensorMap (&maps)[3], bool cache = true) {
     if constexpr (T == kTypeQ4_K) {
-        return tensor_map(m, 144, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[0]);
+        return tensor_map(m, 144, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[0], cache);
     } else if constexpr (T == kTypeQ6_K) {
-        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0]) &&
-               tensor_map(m, 64, CU_TENSOR_MAP_SWIZZLE_64B, &maps[1]) &&
-               tensor_map(m, 16, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[2]);
+        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0], cache) &&
+               tensor_map(m, 64, CU_TENSOR_MAP_SWIZZLE_64B, &maps[1], cache) &&
+               tensor_map(m, 16, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[2], cache);
     } else if constexpr (T == kTypeQ8_0) {
-        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0]) &&
-               tensor_map(m, 16, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[1]);
+        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0], cache) &&
+               tensor_map(m, 16, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[1], cache);
     } else {
-        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0]);
+        return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0], cache);
     }
 }
 
-static bool maps_for(const QMatrix &m, CUtensorMap (&maps)[3]) {
+static bool maps_for(const QMatrix &m, CUtensorMap (&maps)[3], bool cache = true) {
     switch (m.type) {
-    case kTypeQ4_K: return segment_maps<kTypeQ4_K>(m, maps);
-    case kTypeQ6_K: return segment_maps<kTypeQ6_K>(m, maps);
-    case kTypeQ8_0: return segment_maps<kTypeQ8_0>(m, maps);
-    default: return segment_maps<kTypeBF16>(m, maps);
+    case kTypeQ4_K: return segment_maps<kTypeQ4_K>(m, maps, cache);
+    case kTypeQ6_K: return segment_maps<kTypeQ6_K>(m, maps, cache);
+    case kTypeQ8_0: return segment_maps<kTypeQ8_0>(m, maps, cache);
+    default: return segment_maps<kTypeBF16>(m, maps, cache);
     }
 }
 
@@ -861,10 +868,10 @@ static uint32_t max_splits_for() {
 template <uint32_t T>
 static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &segs, const uint8_t *xt,
                          uint32_t nchunks_x, float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, bool cache_maps) {
     TmapSet maps;
     for (int i = 0; i < segs.count; ++i) {
-        if (!segment_maps<T>(segs.m[i], maps.map[i])) return false;
+        if (!segment_maps<T>(segs.m[i], maps.map[i], cache_maps)) return false;
         maps.box_rows[i] = std::min<uint32_t>(segs.m[i].rows, kUM);
     }
     const uint32_t btiles = (batch + kUN - 1) / kUN;
@@ -896,7 +903,7 @@ static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &s
 
 // Launches one group of segments that share a weight type.
 static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, uint32_t nchunks_x, float *y,
-                         uint32_t ldy, uint32_t batch, ErrorWord err, cudaStream_t stream) {
+                         uint32_t ldy, uint32_t batch, ErrorWord err, cudaStream_t stream, bool cache_maps) {
     uint32_t acc = 0, cols = 0;
     for (int i = 0; i < segs.count; ++i) {
         segs.tile_start[i] = acc;
@@ -907,10 +914,10 @@ static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, ui
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
     bool ok;
     switch (type) {
-    case kTypeQ4_K: ok = launch_typed<kTypeQ4_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream); break;
-    case kTypeQ6_K: ok = launch_typed<kTypeQ6_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream); break;
-    case kTypeQ8_0: ok = launch_typed<kTypeQ8_0>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream); break;
-    default: ok = launch_typed<kTypeBF16>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream); break;
+    case kTypeQ4_K: ok = launch_typed<kTypeQ4_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream, cache_maps); break;
+    case kTypeQ6_K: ok = launch_typed<kTypeQ6_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream, cache_maps); break;
+    case kTypeQ8_0: ok = launch_typed<kTypeQ8_0>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream, cache_maps); break;
+    default: ok = launch_typed<kTypeBF16>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream, cache_maps); break;
     }
     if (ok) count_launch();
     return ok;
@@ -918,7 +925,7 @@ static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, ui
 
 bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx, float *y, uint32_t ldy,
                             uint32_t batch, uint8_t *xtiles, size_t xtile_bytes, ErrorWord err,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, bool cache_maps) {
     uint32_t cols = 0;
     for (int i = 0; i < in.count; ++i) {
         if (!umma_supported(in.m[i])) return false;
@@ -930,7 +937,7 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
     // tensor maps first, so that a failure launches nothing
     for (int i = 0; i < in.count; ++i) {
         CUtensorMap maps[3];
-        if (!maps_for(in.m[i], maps)) return false;
+        if (!maps_for(in.m[i], maps, cache_maps)) return false;
     }
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
     const dim3 xg(nchunks * 4, (batch + kUN - 1) / kUN);
@@ -948,7 +955,7 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
             ++g.count;
             done[j] = true;
         }
-        launch_group(in.m[i].type, g, xtiles, nchunks, y, ldy, batch, err, stream);
+        launch_group(in.m[i].type, g, xtiles, nchunks, y, ldy, batch, err, stream, cache_maps);
     }
     return true;
 }

@@ -130,6 +130,7 @@ _SIGNATURES = {
     "kq_weight_provider_linear_f32": (C.c_int, [vp, vp, C.c_int, u32, u64, u64, vp, vp, u64, vp, u64, vp]),
     "kq_weight_provider_vector_f32": (C.c_int, [vp, vp, u64, vp, u64, vp, u64, vp]),
     "kq_b200_provider_linear_batch_f32": (C.c_int, [vp, vp, u64, u64, vp, u32, vp, vp]),
+    "kq_b200_provider_linear_batch_f32_static": (C.c_int, [vp, vp, u64, u64, vp, u32, vp, vp, vp]),
     "kq_b200_profile_kernel": (None, [C.c_char_p]),
     "kq_b200_profile_read": (None, [C.POINTER(u64), C.POINTER(C.c_double)]),
     "kq_gdn_test_config_create": (C.c_int, [C.POINTER(GdnDimensions), C.POINTER(vp), vp]),
