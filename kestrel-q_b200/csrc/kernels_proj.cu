@@ -198,62 +198,163 @@ proj_warp_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
 // weights are decoded once into shared memory (read back as broadcasts) and
 // the activations are staged transposed (one conflict-free load per lane).
 
-constexpr int kExRows = 16;          // rows per CTA (4 per warp)
-constexpr int kExBatch = 32;         // batch rows per CTA (one per lane)
-constexpr int kExK = 128;            // columns per chunk
+// Exact projection: every output is the reference's sequential F32 row dot,
+// acc = acc + w[k]*x[k] for k = 0..cols-1 with separately rounded products and
+// sums (src/kq_numeric.c:420-503), so results are bit-identical.  The chain is
+// inherently serial; throughput comes from running many chains at once and
+// from keeping their operands in flight.  A CTA owns 8 weight rows x 64 batch
+// rows (512 chains); each thread two chains (a row pair, one batch row), so
+// two independent add chains hide the add latency.  K chunks of 128 are staged
+// in shared memory by cp.async four chunks deep (raw F32 or BF16 weight bytes,
+// F32 activations) and read as 16-byte vectors, four chain steps per load.
+// Other weight types are decoded into the stage synchronously (slow path).
+constexpr int kExRows = 8;            // weight rows per CTA
+constexpr int kExBatch = 64;          // batch rows per CTA
+constexpr int kExK = 128;             // K per staged chunk
+constexpr int kExStages = 4;
+constexpr int kExXStride = kExK + 4;  // padded activation row (conflict-free float4 reads)
+constexpr int kExThreads = 256;
+constexpr size_t kExXBytes = (size_t)kExBatch * kExXStride * 4;   // per stage
+constexpr size_t kExWBytes = (size_t)kExRows * kExK * 4;          // per stage (F32 room)
+constexpr size_t kExSmem = kExStages * (kExXBytes + kExWBytes);
 
-__global__ void __launch_bounds__(128)
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(a), "l"(gmem) : "memory");
+}
+
+// MODE 0: F32 weights, 1: BF16 weights (both staged raw by cp.async);
+// 2: any type, decoded into F32 by the staging threads.
+template <int MODE>
+__global__ void __launch_bounds__(kExThreads)
 proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                   float *__restrict__ y, uint32_t ldy, uint32_t batch,
                   ErrorWord err) {
-    __shared__ __align__(16) float ws[kExRows][kExK];
-    __shared__ float xs[kExK][kExBatch + 1];
+    extern __shared__ __align__(16) uint8_t ex_smem[];
     if (error_raised(err)) return;
+    float *xs_base = reinterpret_cast<float *>(ex_smem);
+    uint8_t *ws_base = ex_smem + kExStages * kExXBytes;
     int seg = 0;
     while (seg + 1 < segs.count && blockIdx.x >= segs.tile_start[seg + 1]) ++seg;
     const QMatrix m = segs.m[seg];
     const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * kExRows;
     const uint32_t b0 = blockIdx.y * kExBatch;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (uint32_t k0 = 0; k0 < m.cols; k0 += kExK) {
-        const uint32_t kc = min((uint32_t)kExK, m.cols - k0);
-        // decode: thread t owns row t/8, 16-element run (t%8)*16 of the chunk
-        {
-            const int r = threadIdx.x >> 3, run = (threadIdx.x & 7) * 16;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rp = warp >> 1;                        // row pair 0..3
+    const int bl = (warp & 1) * 32 + lane;           // batch row within the tile
+    const uint32_t nchunks = (m.cols + kExK - 1) / kExK;
+    const bool xvec = (ldx % 4u) == 0u && (reinterpret_cast<uintptr_t>(x) & 15u) == 0u;
+    constexpr uint32_t kElem = MODE == 1 ? 2u : 4u;   // staged weight bytes per value
+
+    auto stage = [&](uint32_t c) {
+        const int buf = c % kExStages;
+        const uint32_t k0 = c * kExK;
+        float *xs = xs_base + (size_t)buf * kExBatch * kExXStride;
+        uint8_t *ws = ws_base + (size_t)buf * kExWBytes;
+        // weights: 8 rows x 128 values
+        if constexpr (MODE == 2) {
+            const int r = tid >> 5, kk = (tid & 31) * 4;
             const uint32_t grow = row0 + r;
-            float w[16];
-            uint32_t cnt = 0;
-            if ((uint32_t)run < kc) cnt = min(16u, kc - run);
-            if (grow < m.rows && cnt > 0)
-                decode_any(m, m.data + (size_t)grow * m.row_bytes, k0 + run, cnt, w);
-            for (int i = 0; i < 16; ++i) ws[r][run + i] = (grow < m.rows && (uint32_t)i < cnt) ? w[i] : 0.0f;
+            float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (grow < m.rows && k0 + kk < m.cols)
+                decode_any(m, m.data + (size_t)grow * m.row_bytes, k0 + kk, min(4u, m.cols - (k0 + kk)), w);
+            for (int e = 0; e < 4; ++e)
+                reinterpret_cast<float *>(ws)[r * kExK + kk + e] = (k0 + kk + e < m.cols) ? w[e] : 0.0f;
+        } else {
+            constexpr int kPieces = kExK * kElem / 16;   // 16-byte pieces per row
+            for (int i = tid; i < kExRows * kPieces; i += kExThreads) {
+                const int r = i / kPieces, pc = i % kPieces;
+                const uint32_t grow = row0 + r, k = k0 + pc * (16 / kElem);
+                uint8_t *dst = ws + (size_t)r * kExK * kElem + pc * 16;
+                if (grow < m.rows && k + 16 / kElem <= m.cols) {
+                    cp_async16(dst, m.data + (size_t)grow * m.row_bytes + (size_t)k * kElem);
+                } else {
+                    for (uint32_t e = 0; e < 16 / kElem; ++e) {
+                        const bool in = grow < m.rows && k + e < m.cols;
+                        if constexpr (MODE == 1) {
+                            reinterpret_cast<uint16_t *>(dst)[e] =
+                                in ? reinterpret_cast<const uint16_t *>(m.data + (size_t)grow * m.row_bytes)[k + e] : 0;
+                        } else {
+                            reinterpret_cast<float *>(dst)[e] =
+                                in ? reinterpret_cast<const float *>(m.data + (size_t)grow * m.row_bytes)[k + e] : 0.0f;
+                        }
+                    }
+                }
+            }
         }
-        // activations, transposed: xs[k][b]
-        for (int idx = threadIdx.x; idx < kExBatch * kExK; idx += blockDim.x) {
-            const int bb = idx / kExK, kk = idx % kExK;
-            const uint32_t gb = b0 + bb;
-            xs[kk][bb] = (gb < batch && (uint32_t)kk < kc) ? x[(size_t)gb * ldx + k0 + kk] : 0.0f;
+        // activations: 64 rows x 128 values
+        for (int i = tid; i < kExBatch * (kExK / 4); i += kExThreads) {
+            const int bb = i / (kExK / 4), q4 = (i % (kExK / 4)) * 4;
+            const uint32_t gb = b0 + bb, k = k0 + q4;
+            float *dst = xs + (size_t)bb * kExXStride + q4;
+            if (xvec && gb < batch && k + 4 <= m.cols) {
+                cp_async16(dst, x + (size_t)gb * ldx + k);
+            } else {
+                for (int e = 0; e < 4; ++e)
+                    dst[e] = (gb < batch && k + e < m.cols) ? x[(size_t)gb * ldx + k + e] : 0.0f;
+            }
         }
+    };
+    auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
+
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (uint32_t c = 0; c < kExStages - 1; ++c) {
+        if (c < nchunks) stage(c);
+        commit();
+    }
+    for (uint32_t c = 0; c < nchunks; ++c) {
+        if (c + kExStages - 1 < nchunks) stage(c + kExStages - 1);
+        commit();
+        asm volatile("cp.async.wait_group %0;" ::"n"(kExStages - 1) : "memory");
         __syncthreads();
-        const float *w0 = ws[warp * 4 + 0], *w1 = ws[warp * 4 + 1];
-        const float *w2 = ws[warp * 4 + 2], *w3 = ws[warp * 4 + 3];
-        for (uint32_t k = 0; k < kc; ++k) {
-            const float xv = xs[k][lane];
-            acc[0] = __fadd_rn(acc[0], __fmul_rn(w0[k], xv));
-            acc[1] = __fadd_rn(acc[1], __fmul_rn(w1[k], xv));
-            acc[2] = __fadd_rn(acc[2], __fmul_rn(w2[k], xv));
-            acc[3] = __fadd_rn(acc[3], __fmul_rn(w3[k], xv));
+        const int buf = c % kExStages;
+        const uint32_t kc = min((uint32_t)kExK, m.cols - c * kExK);
+        const float *xv = xs_base + (size_t)buf * kExBatch * kExXStride + (size_t)bl * kExXStride;
+        const uint8_t *ws = ws_base + (size_t)buf * kExWBytes;
+        const uint8_t *w0 = ws + (size_t)(2 * rp) * kExK * kElem, *w1 = w0 + (size_t)kExK * kElem;
+        auto wq = [&](const uint8_t *row, int k) {   // 4 F32 weights at k
+            if constexpr (MODE == 1) {
+                const uint2 u = *reinterpret_cast<const uint2 *>(row + (size_t)k * 2);
+                return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                   __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+            } else {
+                return *reinterpret_cast<const float4 *>(row + (size_t)k * 4);
+            }
+        };
+        if (kc == (uint32_t)kExK) {
+#pragma unroll 4
+            for (int k = 0; k < kExK; k += 4) {
+                const float4 a = wq(w0, k), b = wq(w1, k);
+                const float4 v = *reinterpret_cast<const float4 *>(xv + k);
+                acc0 = __fadd_rn(acc0, __fmul_rn(a.x, v.x));
+                acc1 = __fadd_rn(acc1, __fmul_rn(b.x, v.x));
+                acc0 = __fadd_rn(acc0, __fmul_rn(a.y, v.y));
+                acc1 = __fadd_rn(acc1, __fmul_rn(b.y, v.y));
+                acc0 = __fadd_rn(acc0, __fmul_rn(a.z, v.z));
+                acc1 = __fadd_rn(acc1, __fmul_rn(b.z, v.z));
+                acc0 = __fadd_rn(acc0, __fmul_rn(a.w, v.w));
+                acc1 = __fadd_rn(acc1, __fmul_rn(b.w, v.w));
+            }
+        } else {
+            for (uint32_t k = 0; k < kc; k += 4) {
+                const float4 a = wq(w0, (int)k), b = wq(w1, (int)k);
+                const float4 v = *reinterpret_cast<const float4 *>(xv + k);
+                const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+                const float vv[4] = {v.x, v.y, v.z, v.w};
+                for (uint32_t e = 0; e < 4 && k + e < kc; ++e) {
+                    acc0 = __fadd_rn(acc0, __fmul_rn(av[e], vv[e]));
+                    acc1 = __fadd_rn(acc1, __fmul_rn(bv[e], vv[e]));
+                }
+            }
         }
         __syncthreads();
     }
-    const uint32_t b = b0 + lane;
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    const uint32_t b = b0 + bl;
     if (b >= batch) return;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t row = row0 + warp * 4 + i;
-        if (row < m.rows) y[(size_t)b * ldy + segs.out_offset[seg] + row] = acc[i];
-    }
+    const uint32_t r0 = row0 + 2 * rp;
+    if (r0 < m.rows) y[(size_t)b * ldy + segs.out_offset[seg] + r0] = acc0;
+    if (r0 + 1 < m.rows) y[(size_t)b * ldy + segs.out_offset[seg] + r0 + 1] = acc1;
 }
 
 static void fill_tile_starts(ProjSegments &s, uint32_t unit) {
@@ -305,7 +406,27 @@ void launch_projection_exact(const ProjSegments &in, const float *x,
     KernelTimer timer("proj_exact", stream);
     fill_tile_starts(segs, kExRows);
     dim3 grid(segs.tile_start[segs.count], (batch + kExBatch - 1) / kExBatch);
-    proj_exact_kernel<<<grid, 128, 0, stream>>>(segs, x, ldx, y, ldy, batch, err);
+    // one launch per mode; segments of mixed types go through the generic mode
+    int mode = 0;
+    for (int i = 0; i < segs.count; ++i) {
+        const QMatrix &q = segs.m[i];
+        const bool aligned = (q.row_bytes % 16u) == 0u && (reinterpret_cast<uintptr_t>(q.data) & 15u) == 0u;
+        const int mi = !aligned ? 2 : q.type == kTypeF32 ? 0 : q.type == kTypeBF16 ? 1 : 2;
+        mode = i == 0 ? mi : (mode == mi ? mode : 2);
+    }
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(proj_exact_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kExSmem);
+        cudaFuncSetAttribute(proj_exact_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kExSmem);
+        cudaFuncSetAttribute(proj_exact_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kExSmem);
+        attr = true;
+    }
+    if (mode == 0)
+        proj_exact_kernel<0><<<grid, kExThreads, kExSmem, stream>>>(segs, x, ldx, y, ldy, batch, err);
+    else if (mode == 1)
+        proj_exact_kernel<1><<<grid, kExThreads, kExSmem, stream>>>(segs, x, ldx, y, ldy, batch, err);
+    else
+        proj_exact_kernel<2><<<grid, kExThreads, kExSmem, stream>>>(segs, x, ldx, y, ldy, batch, err);
     count_launch();
 }
 
