@@ -195,11 +195,12 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     uint32_t max_blocks = 1;
     for (uint32_t b = 0; b < batch; ++b)
         max_blocks = std::max<uint32_t>(max_blocks, (uint32_t)((states[b]->length + tokens) / d.block));
-    // about 8 tiles of 16 selected tokens per split, and at least two waves
+    // about 16 tiles of 16 selected tokens per split, and at least two waves
     // of CTAs over the 148 SMs for small batches
     const uint32_t tiles = (d.sel_capacity + 15) / 16;
     const uint32_t per_seq = std::min<uint32_t>(batch, kMaxBatch) * d.kv_heads;
-    uint32_t splits = std::max<uint32_t>((tiles + 7) / 8, (3 * 148 + per_seq - 1) / per_seq);
+    // (the head-blocked attention kernel takes at most 32 tiles per split)
+    uint32_t splits = std::max<uint32_t>((tiles + 15) / 16, (3 * 148 + per_seq - 1) / per_seq);
     splits = std::max<uint32_t>(1, std::min<uint32_t>(splits, tiles));
     const size_t need = Carve::round(items * ldp * 4) + Carve::round(items * ldi * 4) +
                         Carve::round(items * qw * 4) + Carve::round((size_t)batch * qw * 4) +

@@ -697,6 +697,231 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     }
 }
 
+// Head-blocked form for head_dim 256 and up to 8 query heads per KV head
+// (the BASELINE geometry: 16 query heads over 2 KV heads).  Every K and V
+// element of a tile is read from shared memory once and used for all the KV
+// head's query heads:
+//   QK  warp w scores tokens 2w, 2w+1 of the 16-token tile; lane l holds the
+//       8 features [8l, 8l+8) of every query head in registers, forms 8
+//       partial dots per token and reduces them with a 9-shuffle
+//       reduce-scatter (4 lanes end up with each head's sum);
+//   softmax  warp h keeps head h's running max / sum (online softmax);
+//   PV  warp w owns features [32w, 32w+32), one per lane, for every head.
+// K/V tiles stream through a 3-stage cp.async ring (96 KB), two CTAs per SM.
+constexpr int kMhStages = 3;
+constexpr int kMhHD = 256;
+constexpr int kMhMaxTiles = 32;           // tiles per CTA (the launcher sizes splits for it)
+constexpr size_t kMhSmem = (size_t)kMhStages * 2 * kAtTile * kMhHD * 4 + 2 * kAtTile * 8 * 4 + 8 * 4 +
+                           (size_t)kMhMaxTiles * kAtTile * 4;
+
+__global__ void __launch_bounds__(256, 2)
+qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
+                     const uint32_t *__restrict__ selected,
+                     const uint32_t *__restrict__ selected_count,
+                     float *__restrict__ part_o, float *__restrict__ part_ml,
+                     uint32_t splits, ErrorWord err) {
+    constexpr int HD = kMhHD;
+    extern __shared__ __align__(16) float sm[];
+    float *kbuf = sm;                                        // [S][16][HD]
+    float *vbuf = kbuf + kMhStages * kAtTile * HD;           // [S][16][HD]
+    float *lg = vbuf + kMhStages * kAtTile * HD;             // [16][8] logits
+    float *pw = lg + kAtTile * 8;                            // [16][8] weights
+    float *corr_s = pw + kAtTile * 8;                        // [8]
+    uint32_t *tok_s = reinterpret_cast<uint32_t *>(corr_s + 8);   // [kMhMaxTiles * 16] cache rows
+    if (qsa_error_raised(err)) return;
+    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const QsaSeq s = bt.s[b];
+    const uint32_t pos = s.length;
+    const uint32_t nblocks = (pos + 1) / d.block;
+    const uint32_t tail = (pos + 1) % d.block;
+    const uint32_t ksel = min(selected_count[b], min(nblocks, d.topk));
+    const uint32_t ntok = ksel * d.block + tail;
+    const uint32_t ntiles = (ntok + kAtTile - 1) / kAtTile;
+    const uint32_t per = (ntiles + splits - 1) / splits;
+    const uint32_t tile0 = split * per, tile1 = min(ntiles, tile0 + per);
+    const uint32_t heads = d.repeat;   // <= 8 (checked by the launcher)
+    const uint32_t kvw = d.kv_heads * HD;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t *selb = selected + (size_t)b * d.topk;
+
+    auto token_of = [&](uint32_t i, bool &ok) -> uint32_t {
+        ok = i < ntok;
+        if (!ok) return 0;
+        if (i < ksel * d.block) {
+            const uint32_t blk = selb[i / d.block];
+            ok = blk < nblocks;
+            return ok ? blk * d.block + i % d.block : 0;
+        }
+        return nblocks * d.block + (i - ksel * d.block);
+    };
+    // cache row of every token this CTA attends to (UINT32_MAX: none); a
+    // split past the sequence's last tile has no tiles (tile1 <= tile0)
+    const uint32_t my_tiles = tile1 > tile0 ? tile1 - tile0 : 0u;
+    if (my_tiles > (uint32_t)kMhMaxTiles) {
+        if (threadIdx.x == 0) qsa_raise(err, kErrSelection);
+        return;
+    }
+    for (uint32_t i = threadIdx.x; i < my_tiles * kAtTile; i += blockDim.x) {
+        bool ok;
+        const uint32_t tok = token_of(tile0 * kAtTile + i, ok);
+        tok_s[i] = ok ? tok : 0xFFFFFFFFu;
+    }
+    __syncthreads();
+    auto load_tile = [&](uint32_t tile) {
+        const int buf = (tile - tile0) % kMhStages;
+        float *kd = kbuf + buf * kAtTile * HD;
+        float *vd = vbuf + buf * kAtTile * HD;
+        const uint32_t *tt = tok_s + (tile - tile0) * kAtTile;
+        // 16 tokens x 64 chunks of 16 bytes, K and V: 4 + 4 per thread
+        for (int c = threadIdx.x; c < kAtTile * (HD / 4); c += blockDim.x) {
+            const int t = c >> 6, col = (c & 63) * 4;
+            const uint32_t tok = tt[t];
+            if (tok != 0xFFFFFFFFu) {
+                const size_t off = (size_t)tok * kvw + kvh * HD + col;
+                cp_async16(kd + t * HD + col, s.key + off);
+                cp_async16(vd + t * HD + col, s.value + off);
+            } else {
+                *reinterpret_cast<float4 *>(kd + t * HD + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4 *>(vd + t * HD + col) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+    };
+
+    // query features [8 lane, 8 lane + 8) of every head, in registers
+    float qr[8][8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+        if ((uint32_t)h < heads) {
+            const float *qp = q + ((size_t)b * d.q_heads + kvh * heads + h) * HD + 8 * lane;
+            const float4 a = *reinterpret_cast<const float4 *>(qp);
+            const float4 c = *reinterpret_cast<const float4 *>(qp + 4);
+            qr[h][0] = a.x; qr[h][1] = a.y; qr[h][2] = a.z; qr[h][3] = a.w;
+            qr[h][4] = c.x; qr[h][5] = c.y; qr[h][6] = c.z; qr[h][7] = c.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) qr[h][j] = 0.0f;
+        }
+    }
+    float acc[8];
+#pragma unroll
+    for (int h = 0; h < 8; ++h) acc[h] = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f;   // head `warp`'s running softmax state
+    const float scale = d.sqrt_head_dim;
+    // reduce-scatter: after the three exchange steps lanes {4g..4g+3} hold
+    // head g's partial sums, with g = bit4*4 + bit3*2 + bit2 of the lane
+    const int my_head = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+
+    for (uint32_t t = tile0; t < tile0 + kMhStages - 1; ++t) {
+        if (t < tile1) load_tile(t);
+        cp_async_commit();
+    }
+    for (uint32_t tile = tile0; tile < tile1; ++tile) {
+        if (tile + kMhStages - 1 < tile1) load_tile(tile + kMhStages - 1);
+        cp_async_commit();
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(kMhStages - 1));
+        __syncthreads();
+        const int buf = (tile - tile0) % kMhStages;
+        const float *kt = kbuf + buf * kAtTile * HD;
+        const float *vt = vbuf + buf * kAtTile * HD;
+        // ---- QK: tokens 2 warp, 2 warp + 1
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+            const int tk = 2 * warp + tt;
+            const float4 k0 = *reinterpret_cast<const float4 *>(kt + tk * HD + 8 * lane);
+            const float4 k1 = *reinterpret_cast<const float4 *>(kt + tk * HD + 8 * lane + 4);
+            const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+            float v[8];
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+                float a = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) a = fmaf(qr[h][j], kv[j], a);
+                v[h] = a;
+            }
+            float w4[4], w2[2];
+            const bool u16 = (lane & 16) != 0, u8 = (lane & 8) != 0, u4 = (lane & 4) != 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float send = u16 ? v[i] : v[i + 4];
+                const float keep = u16 ? v[i + 4] : v[i];
+                w4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const float send = u8 ? w4[i] : w4[i + 2];
+                const float keep = u8 ? w4[i + 2] : w4[i];
+                w2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            }
+            float w1;
+            {
+                const float send = u4 ? w2[0] : w2[1];
+                const float keep = u4 ? w2[1] : w2[0];
+                w1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+            w1 += __shfl_xor_sync(0xffffffffu, w1, 2);
+            w1 += __shfl_xor_sync(0xffffffffu, w1, 1);
+            if ((lane & 3) == 0)
+                lg[tk * 8 + my_head] = tok_s[(tile - tile0) * kAtTile + tk] != 0xFFFFFFFFu ? w1 / scale : -INFINITY;
+        }
+        __syncthreads();
+        // ---- online softmax: warp h for head h, lanes 0..15 one token each
+        if ((uint32_t)warp < heads) {
+            const float logit = lane < kAtTile ? lg[lane * 8 + warp] : -INFINITY;
+            float mt = logit;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            const float m_new = fmaxf(m_run, mt);
+            const float corr = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
+            const float p = (logit == -INFINITY) ? 0.0f : expf(logit - m_new);
+            float ps = p;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            l_run = l_run * corr + ps;
+            m_run = m_new;
+            if (lane < kAtTile) pw[lane * 8 + warp] = p;
+            if (lane == 0) corr_s[warp] = corr;
+        }
+        __syncthreads();
+        // ---- PV: feature 32 warp + lane of every head
+        {
+            const int f = 32 * warp + lane;
+            const float4 c0 = *reinterpret_cast<const float4 *>(corr_s);
+            const float4 c1 = *reinterpret_cast<const float4 *>(corr_s + 4);
+            acc[0] *= c0.x; acc[1] *= c0.y; acc[2] *= c0.z; acc[3] *= c0.w;
+            acc[4] *= c1.x; acc[5] *= c1.y; acc[6] *= c1.z; acc[7] *= c1.w;
+#pragma unroll 4
+            for (int t = 0; t < kAtTile; ++t) {
+                const float vv = vt[t * HD + f];
+                const float4 p0 = *reinterpret_cast<const float4 *>(pw + t * 8);
+                const float4 p1 = *reinterpret_cast<const float4 *>(pw + t * 8 + 4);
+                acc[0] = fmaf(p0.x, vv, acc[0]);
+                acc[1] = fmaf(p0.y, vv, acc[1]);
+                acc[2] = fmaf(p0.z, vv, acc[2]);
+                acc[3] = fmaf(p0.w, vv, acc[3]);
+                acc[4] = fmaf(p1.x, vv, acc[4]);
+                acc[5] = fmaf(p1.y, vv, acc[5]);
+                acc[6] = fmaf(p1.z, vv, acc[6]);
+                acc[7] = fmaf(p1.w, vv, acc[7]);
+            }
+        }
+        __syncthreads();
+    }
+    asm volatile("cp.async.wait_group 0;\n" ::);
+    const int f = 32 * warp + lane;
+#pragma unroll
+    for (int h = 0; h < 8; ++h) {
+        if ((uint32_t)h < heads) {
+            const size_t slot = ((size_t)b * d.q_heads + kvh * heads + h) * splits + split;
+            part_o[slot * HD + f] = acc[h];
+        }
+    }
+    if ((uint32_t)warp < heads && lane == 0) {
+        const size_t slot = ((size_t)b * d.q_heads + kvh * heads + warp) * splits + split;
+        part_ml[slot * 2] = m_run;
+        part_ml[slot * 2 + 1] = l_run;
+    }
+}
+
 void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const float *q, const uint32_t *selected,
                        const uint32_t *selected_count, float *partial_o,
@@ -704,7 +929,15 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        ErrorWord err, cudaStream_t stream) {
     dim3 grid(splits, d.kv_heads, batch);
     KernelTimer timer("qsa_attend", stream);
-    if (d.head_dim == 256 || d.head_dim == 128) {
+    if (d.head_dim == 256 && d.repeat <= 8 && (d.kv_heads * 256u) % 4u == 0u) {
+        static bool attr = false;
+        if (!attr) {
+            cudaFuncSetAttribute(qsa_attend_mh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMhSmem);
+            attr = true;
+        }
+        qsa_attend_mh_kernel<<<grid, 256, kMhSmem, stream>>>(d, b, q, selected, selected_count, partial_o,
+                                                             partial_ml, splits, err);
+    } else if (d.head_dim == 256 || d.head_dim == 128) {
         const int hd = (int)d.head_dim;
         const size_t smem = (size_t)(8 * hd + 2 * kAtTile * (hd + 4) + 2 * kAtTile * hd) * sizeof(float);
         if (hd == 256) {
