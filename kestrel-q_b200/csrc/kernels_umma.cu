@@ -9,7 +9,7 @@
 // term and the rounding of the low parts are ~2^-16 relative.  BF16
 // weights are exact in bf16 and take two terms (w*xh + w*xl).
 //
-// Warp roles (576 threads, one CTA per SM):
+// Warp roles (608 threads, one CTA per SM):
 //   TMA warp     per K chunk of 64: 2-D TMA loads of the chunk's raw GGUF
 //                bytes (16-byte columns x 128 rows: Q4_K header + quants,
 //                Q6_K/Q8_0 planes, BF16 values) and a 1-D bulk copy of the
@@ -23,15 +23,15 @@
 //                same values as the reference decoder, src/kq_numeric.c),
 //                splits them into bf16 hi/lo and stores both
 //                straight into TMEM with tcgen05.st: the A operand never
-//                touches shared memory.  Four A buffers in TMEM.
-//   MMA warp     one thread issues, per K-step of 16, one N=128 MMA
+//                touches shared memory.  Six A buffers in TMEM.
+//   MMA warp     per K-step of 16, one thread issues an N=128 MMA
 //                wh * [xh | xl] (the activation tile's hi and lo halves are
-//                adjacent, so one instruction covers both terms) and one
-//                N=64 MMA wl * xh into a second accumulator, A from TMEM and
-//                B from shared memory, and commits to the chunk's mbarrier,
-//                which frees both the ring slot and the TMEM A buffer.
-//                (An M=128 tcgen05.mma costs about the same issue time for
-//                N=64 and N=128, so merging terms halves the MMA time.)
+//                adjacent, so one instruction covers both terms) and an N=64
+//                MMA wl * xh into the first 64 columns of the same
+//                accumulator; A from TMEM, B from shared memory.  It commits
+//                to the chunk's mbarrier, which frees the ring slot and the
+//                TMEM A buffer.  (An M=128 tcgen05.mma costs about the same
+//                issue time for N=64 and N=128.)
 // Epilogue: the decode warps read the three partial products with
 // tcgen05.ld and add them.
 // Split-K runs as a thread-block cluster along gridDim.z: every CTA leaves
@@ -68,17 +68,22 @@ constexpr int kXSlot = 2 * kBTile;        // activation tile of one chunk: [xh |
 constexpr int kMaxXRing = 10;
 constexpr int kRawRing = 3;               // raw super-block slots
 constexpr int kSmemBudget = 200 * 1024;
-constexpr int kABufs = 4;                 // decoded A buffers in TMEM
+constexpr int kABufs = 6;                 // decoded A buffers in TMEM
 constexpr int kDecodeWarps = 16;
-constexpr int kTmaWarp = kDecodeWarps;
+// The single-thread roles sit on different schedulers (scheduler = warp % 4),
+// because their TMA / MMA instructions take issue time from the decode warps
+// that share a scheduler with them: warp 16 (scheduler 0) owns TMEM, 17
+// (scheduler 1) issues the MMAs, 18 (scheduler 2) the TMA loads.
+constexpr int kAllocWarp = kDecodeWarps;
 constexpr int kMmaWarp = kDecodeWarps + 1;
-constexpr int kThreads = (kDecodeWarps + 2) * 32;
+constexpr int kTmaWarp = kDecodeWarps + 2;
+constexpr int kThreads = (kDecodeWarps + 3) * 32;
 constexpr int kAccStride = kUN + 1;       // floats per row of the split-K exchange tile
-// TMEM columns: [0, 128) wh * [xh | xl] (N = 128), [128, 192) wl * xh,
-// A buffer b at 192 + 64 b: hi 32 | lo 32.
+// TMEM columns: [0, 128) accumulator, wh * [xh | xl] (N = 128) with wl * xh
+// (N = 64) added into its first 64 columns; A buffer b at 128 + 64 b:
+// hi 32 | lo 32.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccLo = 128;
-constexpr uint32_t kABase = 192;
+constexpr uint32_t kABase = 128;
 static_assert(kABase + 64 * kABufs <= kTmemCols, "TMEM budget");
 constexpr uint32_t kWaitLimit = 1u << 22;  // mbarrier polls before giving up
 constexpr uint32_t kErrTimeout = 4;
@@ -493,6 +498,7 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
                  uint32_t nchunks_x, float *__restrict__ y, uint32_t ldy, uint32_t batch,
                  uint32_t kchunks_per_split, ErrorWord err) {
     constexpr uint32_t SC = TypeCfg<T>::sc, kRawBytes = Ring<T>::raw, kX = Ring<T>::xdepth;
+    constexpr uint32_t kIssuers = 1u;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t rfull[kRawRing], rfree[kRawRing], xfull[kMaxXRing], mdone[kMaxXRing];
     __shared__ uint64_t aready[kABufs], accum;
@@ -519,20 +525,18 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     const uint32_t nchunks = (c_end > c_begin && !skip) ? c_end - c_begin : 0;
 
     if (tid == 0) {
-        for (int s = 0; s < kRawRing; ++s) {
-            mbar_init(&rfull[s], 1);
-            mbar_init(&rfree[s], 1);
-        }
+        for (int s = 0; s < kRawRing; ++s) mbar_init(&rfull[s], 1);
         for (uint32_t s = 0; s < kX; ++s) {
             mbar_init(&xfull[s], 1);
-            mbar_init(&mdone[s], 1);
+            mbar_init(&mdone[s], kIssuers);
         }
+        for (int s = 0; s < kRawRing; ++s) mbar_init(&rfree[s], kIssuers);
         for (int b = 0; b < kABufs; ++b) mbar_init(&aready[b], kDecodeWarps);
-        mbar_init(&accum, 1);
+        mbar_init(&accum, kIssuers);
         abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == kMmaWarp) {
+    if (warp == kAllocWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(&tmem_base_slot)), "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
@@ -581,18 +585,16 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
                 const uint32_t ah = tmem + kABase + b * 64u, al = ah + 32u;
                 const uint32_t first = it == 0 ? 0u : 1u;
 #pragma unroll
-                for (uint32_t kk = 0; kk < kUK / 16; ++kk) {
-                    // +32 bytes of K per step = +2 in the descriptor's address field
+                for (uint32_t kk = 0; kk < kUK / 16; ++kk) {   // +32 bytes of K per step = +2 in the address field
                     umma_ts<2 * kUN>(tmem, ah + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
-                    if constexpr (T != kTypeBF16)
-                        umma_ts<kUN>(tmem + kAccLo, al + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
+                    if constexpr (T != kTypeBF16) umma_ts<kUN>(tmem, al + kk * 8u, db + 2u * kk, 1u);
                 }
                 umma_commit(&mdone[xs]);
                 if (it % SC == SC - 1) umma_commit(&rfree[(it / SC) % kRawRing]);
             }
-            umma_commit(&accum);   // completes once every MMA issued above has
+            umma_commit(&accum);   // completes once every MMA this thread issued has
         }
-    } else {
+    } else if (warp < kDecodeWarps) {
         // ---- decode warps: lane = weight row within the warp's TMEM quarter
         const uint32_t quarter = warp & 3, q = warp >> 2;
         const uint32_t row = quarter * 32u + lane;
@@ -634,18 +636,14 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
 #pragma unroll
     for (int j = 0; j < 16; ++j) acc[j] = 0.0f;   // empty split: contributes zero
     if (warp < kDecodeWarps && all_ok && nchunks > 0) {
-        // y = wh*xh + wh*xl + wl*xh, summed in that order
-        uint32_t r0[16], r1[16], r2[16];
+        // y = (wh*xh + wl*xh) + wh*xl
+        uint32_t r0[16], r1[16];
         const uint32_t taddr = tmem + (lane_base << 16) + col_base;
         tmem_ld16(taddr, r0);
         tmem_ld16(taddr + kUN, r1);
-        if constexpr (T != kTypeBF16) tmem_ld16(taddr + kAccLo, r2);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            acc[j] = __fadd_rn(__uint_as_float(r0[j]), __uint_as_float(r1[j]));
-            if constexpr (T != kTypeBF16) acc[j] = __fadd_rn(acc[j], __uint_as_float(r2[j]));
-        }
+        for (int j = 0; j < 16; ++j) acc[j] = __fadd_rn(__uint_as_float(r0[j]), __uint_as_float(r1[j]));
     }
     const bool write = all_ok && !skip;
     const uint32_t nsplit = gridDim.z;
@@ -687,7 +685,7 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == kMmaWarp) {
+    if (warp == kAllocWarp) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     }
