@@ -64,13 +64,30 @@ def contexts(rank: int, n: int = BATCH, ctx_max: int = CTX_RANGE[1]):
     return rng.integers(CTX_RANGE[0], ctx_max + 1, size=n)
 
 
-def layer_weights(rank: int):
+def layer_weights():
+    """The block's weights: one model, replicated on every rank."""
     from kqb200 import synth
     gd, qd = dims()
-    gdn = [synth.gdn_layer(1000 * rank + l, gd, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_Q4_K)
+    gdn = [synth.gdn_layer(l, gd, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_Q4_K)
            for l in range(GDN_LAYERS)]
-    qsa = synth.qsa_layer(1000 * rank + 7, qd, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_BF16)
+    qsa = synth.qsa_layer(7, qd, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_BF16)
     return gdn, qsa
+
+
+def max_over_ranks(values, world: int, device):
+    """Per-rank device times -> their maximum over all ranks (every rank
+    calls this, in the same order, with the same number of values)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def job_tokens_per_s(world: int, batch_per_rank: int, ms_per_step: float) -> float:
+    """Whole-job throughput: every rank decodes batch_per_rank tokens per step."""
+    return world * batch_per_rank * 1000.0 / ms_per_step
 
 
 def algorithmic_bytes(gdn, qsa, ctx, batch):
@@ -169,7 +186,7 @@ def cpu_block_sample(n_seqs: int, threads: int, rank: int = 0):
     from oracle import oracle as O
     impl = "reference" if O.ref_available() else "port"
     gd, qd = dims()
-    gdn, qsa = layer_weights(rank)
+    gdn, qsa = layer_weights()
     gw = [O.gdn_weights_f32(L) for L in gdn]
     qw = O.qsa_weights_f32(qsa)
     ctx = contexts(rank)[:n_seqs]
@@ -259,7 +276,7 @@ def run_b200(args, rank, world, local_rank):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local_rank))
     gd, qd = dims()
-    gdn_w, qsa_w = layer_weights(rank)
+    gdn_w, qsa_w = layer_weights()
     ctx = contexts(rank, ctx_max=args.ctx_max)
     B = BATCH
     steps_total = args.warmup + 2 * args.steps + 40
@@ -371,10 +388,7 @@ def run_b200(args, rank, world, local_rank):
     e2e_ms = f0.elapsed_time(f1) / args.steps
     assert torch.isfinite(yh).all(), "non-finite block output"
 
-    t = torch.tensor([ms, e2e_ms], device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = float(t[0]), float(t[1])
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world, torch.device("cuda", local_rank))
 
     step_bytes, parts = algorithmic_bytes(gdn_w, qsa_w, ctx, B)
     hbm, peak_kind = peaks()
@@ -387,7 +401,7 @@ def run_b200(args, rank, world, local_rank):
         traffic = json.loads(tf.read_text()).get("bytes_per_launch_b64")
     line = {
         "metric": METRIC,
-        "value": world * B * 1000.0 / ms,
+        "value": job_tokens_per_s(world, B, ms),
         "unit": "tok/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -422,7 +436,7 @@ def run_b200(args, rank, world, local_rank):
             "avg_launch_ms": rec_avg_ms,
             "launches_timed": rec_n.value,
         },
-        "e2e": {"value": world * B * 1000.0 / e2e_ms, "unit": "tok/s",
+        "e2e": {"value": job_tokens_per_s(world, B, e2e_ms), "unit": "tok/s",
                 "h2d_bytes_per_step": B * gd.hidden * 4, "d2h_bytes_per_step": B * gd.hidden * 4},
         "gpu_launches": int(launches),
         **({"kernel_breakdown": breakdown} if breakdown else {}),
