@@ -28,6 +28,7 @@ LIB = HERE / "lib" / "libkqb200.so"
 SOURCES = [
     "kernels_proj.cu",
     "kernels_gdn.cu",
+    "kernels_gdn_chunk.cu",
     "kernels_qsa.cu",
     "kernels_umma.cu",
     "runtime.cpp",

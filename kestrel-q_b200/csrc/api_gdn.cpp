@@ -23,6 +23,7 @@ namespace {
 constexpr uint32_t kGdnConfigMagic = 0x4b514743u;
 constexpr uint32_t kGdnStateMagic = 0x4b514753u;
 constexpr uint32_t kPrefillChunk = 2048;   // tokens per device pass
+constexpr uint32_t kChunkedMinTokens = 32;  // prefill passes from this length use the chunked recurrence
 }  // namespace
 
 struct kq_gdn_config {
@@ -150,6 +151,10 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
     const size_t partial_floats = std::max(projection_workspace_floats((uint32_t)items, ldp, H),
                                            projection_workspace_floats((uint32_t)items, H, Vd));
     need += Carve::round(partial_floats * 4);
+    // prefill of one sequence: chunked (WY-form) recurrence
+    const bool chunked = batch == 1 && chunk_tokens >= kChunkedMinTokens && gdn_chunked_supported(gd);
+    const size_t chunk_floats = chunked ? gdn_chunk_workspace_floats(gd, chunk_tokens) : 0;
+    if (chunked) need += Carve::round(items * Hv * 4) + Carve::round(chunk_floats * 4);
     void *ws;
     kq_status st = c->workspace(need, &ws, diag);
     if (st != KQ_STATUS_OK) return st;
@@ -162,6 +167,8 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
     float *decay = cv.take<float>(items * Hv);
     float *xm = mask ? cv.take<float>(items * H) : nullptr;
     float *partial = partial_floats ? cv.take<float>(partial_floats) : nullptr;
+    float *logdecay = chunked ? cv.take<float>(items * Hv) : nullptr;
+    float *chunk_work = chunked ? cv.take<float>(chunk_floats) : nullptr;
 
     ProjSegments in{};
     in.count = 4;
@@ -194,9 +201,13 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
             }
             const uint32_t n_items = gb * tc;
             launch_projection(in, xin, H, proj, ldp, n_items, err, c->stream, partial, partial_floats);
-            launch_gdn_conv_gates(gd, w.vec, p, gb, tc, proj, ldp, qk, v, beta, decay, err, c->stream);
-            launch_gdn_recurrence(gd, w.vec, p, gb, tc, qk, v, beta, decay, proj, ldp, gated, err,
-                                  c->stream);
+            launch_gdn_conv_gates(gd, w.vec, p, gb, tc, proj, ldp, qk, v, beta, decay, err, c->stream, logdecay);
+            if (chunked && tc >= kChunkedMinTokens)
+                launch_gdn_chunked(gd, w.vec, p, tc, qk, v, beta, logdecay, proj, ldp, gated, chunk_work, err,
+                                   c->stream);
+            else
+                launch_gdn_recurrence(gd, w.vec, p, gb, tc, qk, v, beta, decay, proj, ldp, gated, err,
+                                      c->stream);
             launch_projection(out, gated, Vd, y + row0 * H, H, n_items, err, c->stream, partial, partial_floats);
             launch_check_finite(y + row0 * H, (uint64_t)n_items * H, err, c->stream);
             for (uint32_t b = 0; b < gb; ++b) {

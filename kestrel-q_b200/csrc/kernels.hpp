@@ -109,17 +109,28 @@ struct GdnWeightsDev {
 };
 
 // proj: [B*T][ldp] (qkv | gate | beta | alpha), item = b*T + t.
+// `logdecay` (may be null) receives g as well as decay = exp(g).
 void launch_gdn_conv_gates(const GdnDims &d, const GdnWeightsDev &w,
                            const GdnBatchPtrs &p, uint32_t batch,
                            uint32_t tokens, const float *proj, uint32_t ldp,
                            float *qk, float *v, float *beta, float *decay,
-                           ErrorWord err, cudaStream_t stream);
+                           ErrorWord err, cudaStream_t stream, float *logdecay = nullptr);
 void launch_gdn_recurrence(const GdnDims &d, const GdnWeightsDev &w,
                            const GdnBatchPtrs &p, uint32_t batch,
                            uint32_t tokens, const float *qk, const float *v,
                            const float *beta, const float *decay,
                            const float *proj, uint32_t ldp, float *gated,
                            ErrorWord err, cudaStream_t stream);
+
+// Chunked (WY-form) prefill of one sequence (kernels_gdn_chunk.cu), for
+// dk = dv = 128: same inputs as the recurrence plus the log decays; `work`
+// holds gdn_chunk_workspace_floats(d, tokens) floats.
+bool gdn_chunked_supported(const GdnDims &d);
+size_t gdn_chunk_workspace_floats(const GdnDims &d, uint32_t tokens);
+void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatchPtrs &p, uint32_t tokens,
+                        const float *qk, const float *v, const float *beta, const float *logdecay,
+                        const float *proj, uint32_t ldp, float *gated, float *work, ErrorWord err,
+                        cudaStream_t stream);
 
 // ---- QSA (kernels_qsa.cu)
 struct QsaDims {

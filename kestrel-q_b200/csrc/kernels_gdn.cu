@@ -77,7 +77,7 @@ gdn_conv_gates_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t token
                       const float *__restrict__ proj, uint32_t ldp,
                       float *__restrict__ qk, float *__restrict__ vout,
                       float *__restrict__ beta, float *__restrict__ decay,
-                      ErrorWord err) {
+                      float *__restrict__ logdecay, ErrorWord err) {
     __shared__ float red[kConvThreads / 32];
     if (gdn_error_raised(err)) return;
     const uint32_t kh = blockIdx.x;
@@ -141,6 +141,7 @@ gdn_conv_gates_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t token
             }
             beta[(size_t)item * d.value_heads + h] = bt;
             decay[(size_t)item * d.value_heads + h] = expf(g);
+            if (logdecay) logdecay[(size_t)item * d.value_heads + h] = g;
         }
     }
     if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
@@ -326,11 +327,11 @@ void launch_gdn_conv_gates(const GdnDims &d, const GdnWeightsDev &w,
                            const GdnBatchPtrs &p, uint32_t batch,
                            uint32_t tokens, const float *proj, uint32_t ldp,
                            float *qk, float *v, float *beta, float *decay,
-                           ErrorWord err, cudaStream_t stream) {
+                           ErrorWord err, cudaStream_t stream, float *logdecay) {
     dim3 grid(d.key_heads, batch * tokens);
     KernelTimer timer("gdn_conv", stream);
     gdn_conv_gates_kernel<<<grid, kConvThreads, 0, stream>>>(d, w, p, tokens, proj, ldp, qk, v,
-                                                            beta, decay, err);
+                                                            beta, decay, logdecay, err);
     count_launch();
 }
 

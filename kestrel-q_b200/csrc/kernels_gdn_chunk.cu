@@ -1,0 +1,331 @@
+// Chunked (WY-form) gated delta-net prefill for dk = dv = 128.
+//
+// The reference runs the delta rule token by token (src/kq_gdn_qwen38.c:
+// 705-761): S <- e^g S; delta = beta (v - S^T k); S <- S + k delta^T;
+// o = S^T q.  Over a chunk of C tokens with S0 the state at its start and
+// G_i = g_1 + ... + g_i (log decays, all <= 0), the same recurrence is
+//   delta = U - W S0,                  (I + diag(beta) L) W = diag(beta e^G) K
+//                                      (I + diag(beta) L) U = diag(beta) V
+//   O     = diag(e^G) Q S0 + P delta,  P_ij  = (q_i . k_j) e^(G_i - G_j), j <= i
+//   S_C   = e^(G_C) S0 + (diag(e^(G_C - G)) K)^T delta,
+// with L_ij = (k_i . k_j) e^(G_i - G_j) for j < i.  Every decay factor is a
+// difference G_i - G_j <= 0, so nothing overflows however strong the decay.
+//
+// Phase 1 (gdn_chunk_prep_kernel), one CTA per (value head, chunk): the
+// chunk's L and P (64 x 64 dot products of 128-vectors), then W and U by
+// forward substitution (one thread per column), written to work space.
+// Phase 2 (gdn_chunk_state_kernel), one CTA per (value head, 32-column slice
+// of S): walks the chunks in order with its S slice in shared memory and
+// produces delta, O and the next S with three small matrix products per
+// chunk.  The state columns are independent, so the four slices of a head
+// run in parallel.  Phase 3 (gdn_gate_norm_kernel): gated RMSNorm of every
+// token, as the recurrence kernel's epilogue.
+//
+// Arithmetic is F32 (FMA); the result differs from the token-by-token order
+// only by rounding.
+#include "kernels.hpp"
+
+#include <cmath>
+
+namespace kqb {
+
+namespace {
+
+constexpr int kC = 64;       // tokens per chunk
+constexpr int kD = 128;      // dk = dv
+constexpr int kSlice = 32;   // state columns per phase-2 CTA
+
+__device__ __forceinline__ bool chunk_error_raised(const ErrorWord &e) {
+    return *reinterpret_cast<volatile unsigned long long *>(e.word) != 0ull;
+}
+__device__ __forceinline__ void chunk_raise(const ErrorWord &e, uint32_t code) {
+    atomicCAS(e.word, 0ull, ((unsigned long long)code << 32) | e.call_id);
+}
+
+__device__ __forceinline__ float chunk_sigmoid(float x) {
+    if (x >= 0.0f) {
+        const float e = expf(-x);
+        return 1.0f / (1.0f + e);
+    }
+    const float e = expf(x);
+    return e / (1.0f + e);
+}
+
+}  // namespace
+
+// Work-space layout per (value head, chunk), in floats.
+constexpr size_t kChunkW = 0;                       // W [64][128]
+constexpr size_t kChunkU = kChunkW + kC * kD;       // U [64][128]
+constexpr size_t kChunkP = kChunkU + kC * kD;       // P [64][64]
+constexpr size_t kChunkEG = kChunkP + kC * kC;      // e^G_i [64]
+constexpr size_t kChunkEGC = kChunkEG + kC;         // e^(G_C - G_i) [64]
+constexpr size_t kChunkTot = kChunkEGC + kC;        // e^G_C at [0], padding
+constexpr size_t kChunkFloats = kChunkTot + 64;
+
+size_t gdn_chunk_workspace_floats(const GdnDims &d, uint32_t tokens) {
+    const size_t chunks = (tokens + kC - 1) / kC;
+    return chunks * d.value_heads * kChunkFloats + (size_t)tokens * d.value_width;   // + O
+}
+
+bool gdn_chunked_supported(const GdnDims &d) { return d.key_dim == kD && d.value_dim == kD; }
+
+// ---------------------------------------------------------------- phase 1
+__global__ void __launch_bounds__(256)
+gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, const float *__restrict__ vin,
+                      const float *__restrict__ beta, const float *__restrict__ logdecay,
+                      float *__restrict__ work, ErrorWord err) {
+    extern __shared__ __align__(16) float cs[];
+    float *Ks = cs;                        // [64][128 + 4]
+    float *Qs = Ks + kC * (kD + 4);        // [64][128 + 4]
+    float *Ls = Qs + kC * (kD + 4);        // [64][65]
+    float *Gs = Ls + kC * (kC + 1);        // [64]
+    float *Bs = Gs + kC;                   // [64]
+    float *Xs = Bs + kC;                   // W then U staging [64][128]
+    if (chunk_error_raised(err)) return;
+    const uint32_t h = blockIdx.x, c = blockIdx.y;
+    const uint32_t kh = h / d.repeat;
+    const uint32_t t0 = c * kC;
+    const uint32_t n = min((uint32_t)kC, tokens - t0);
+    const int tid = threadIdx.x;
+    float *wk = work + ((size_t)c * d.value_heads + h) * kChunkFloats;
+
+    // q, k rows of key head kh (zero past the end of the sequence)
+    for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
+        const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
+        float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f), k4 = q4;
+        if ((uint32_t)r < n) {
+            const size_t item = t0 + r;
+            q4 = *reinterpret_cast<const float4 *>(qk + (item * 2 + 0) * d.key_width + kh * kD + c4);
+            k4 = *reinterpret_cast<const float4 *>(qk + (item * 2 + 1) * d.key_width + kh * kD + c4);
+        }
+        *reinterpret_cast<float4 *>(Qs + r * (kD + 4) + c4) = q4;
+        *reinterpret_cast<float4 *>(Ks + r * (kD + 4) + c4) = k4;
+    }
+    if (tid < kC) {
+        const bool in = (uint32_t)tid < n;
+        Bs[tid] = in ? beta[(size_t)(t0 + tid) * d.value_heads + h] : 0.0f;
+        Gs[tid] = in ? logdecay[(size_t)(t0 + tid) * d.value_heads + h] : 0.0f;
+    }
+    __syncthreads();
+    if (tid == 0) {   // cumulative log decay, in token order
+        float acc = 0.0f;
+        for (int i = 0; i < kC; ++i) {
+            acc += Gs[i];
+            Gs[i] = acc;
+        }
+    }
+    __syncthreads();
+    // L (strictly lower) and P (lower incl. diagonal): thread -> row i, 16 columns
+    {
+        const int i = tid >> 2, j0 = (tid & 3) * 16;
+        float lk[16], pq[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) { lk[r] = 0.f; pq[r] = 0.f; }
+        for (int kk = 0; kk < kD; kk += 4) {
+            const float4 ki = *reinterpret_cast<const float4 *>(Ks + i * (kD + 4) + kk);
+            const float4 qi = *reinterpret_cast<const float4 *>(Qs + i * (kD + 4) + kk);
+#pragma unroll
+            for (int r = 0; r < 16; ++r) {
+                const float4 kj = *reinterpret_cast<const float4 *>(Ks + (j0 + r) * (kD + 4) + kk);
+                lk[r] = fmaf(ki.x, kj.x, fmaf(ki.y, kj.y, fmaf(ki.z, kj.z, fmaf(ki.w, kj.w, lk[r]))));
+                pq[r] = fmaf(qi.x, kj.x, fmaf(qi.y, kj.y, fmaf(qi.z, kj.z, fmaf(qi.w, kj.w, pq[r]))));
+            }
+        }
+        const float gi = Gs[i];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+            const int j = j0 + r;
+            const float f = j <= i ? expf(gi - Gs[j]) : 0.0f;
+            Ls[i * (kC + 1) + j] = j < i ? lk[r] * f : 0.0f;
+            wk[kChunkP + i * kC + j] = pq[r] * f;
+        }
+    }
+    const float gc = Gs[n - 1];
+    if (tid < kC) {
+        wk[kChunkEG + tid] = expf(Gs[tid]);
+        wk[kChunkEGC + tid] = (uint32_t)tid < n ? expf(gc - Gs[tid]) : 0.0f;
+    }
+    if (tid == 0) wk[kChunkTot] = expf(gc);
+    __syncthreads();
+    // forward substitution, one column per thread: threads 0..127 W, 128..255 U
+    {
+        const bool is_w = tid < kD;
+        const int f = tid & (kD - 1);
+        for (int i = 0; i < kC; ++i) {
+            float base;
+            if (is_w) {
+                base = expf(Gs[i]) * Ks[i * (kD + 4) + f];
+            } else {
+                base = (uint32_t)i < n ? vin[(size_t)(t0 + i) * d.value_width + h * kD + f] : 0.0f;
+            }
+            float acc = 0.0f;
+            for (int j = 0; j < i; ++j) acc = fmaf(Ls[i * (kC + 1) + j], Xs[(is_w ? 0 : kC * kD) + j * kD + f], acc);
+            // Xs holds W in [0, 64*128) and U in [64*128, 2*64*128)
+            Xs[(is_w ? 0 : kC * kD) + i * kD + f] = Bs[i] * (base - acc);
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < kC * kD; i += blockDim.x) {
+        wk[kChunkW + i] = Xs[i];
+        wk[kChunkU + i] = Xs[kC * kD + i];
+    }
+}
+
+// ---------------------------------------------------------------- phase 2
+__global__ void __launch_bounds__(256)
+gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *__restrict__ qk,
+                       const float *__restrict__ work, float *__restrict__ obuf, ErrorWord err) {
+    extern __shared__ __align__(16) float cs[];
+    float *S = cs;                            // [128][32]
+    float *Ws = S + kD * kSlice;              // [64][128 + 4]
+    float *Qs = Ws + kC * (kD + 4);           // [64][128 + 4] (scaled by e^G)
+    float *Ks = Qs + kC * (kD + 4);           // [64][128 + 4] (scaled by e^(G_C - G))
+    float *Ps = Ks + kC * (kD + 4);           // [64][64 + 1]
+    float *Ds = Ps + kC * (kC + 1);           // delta [64][32]
+    if (chunk_error_raised(err)) return;
+    const uint32_t h = blockIdx.x, sl = blockIdx.y;
+    const uint32_t kh = h / d.repeat;
+    const uint32_t col0 = sl * kSlice;
+    const int tid = threadIdx.x, f = tid & 31, grp = tid >> 5;   // 8 groups of 32 threads
+    const float *sin_ = p.rec_in[0] + (size_t)h * kD * kD;
+    float *sout = p.rec_out[0] + (size_t)h * kD * kD;
+    for (int i = tid; i < kD * kSlice; i += blockDim.x) S[i] = sin_[(size_t)(i / kSlice) * kD + col0 + i % kSlice];
+    const uint32_t nchunks = (tokens + kC - 1) / kC;
+    bool bad = false;
+    for (uint32_t c = 0; c < nchunks; ++c) {
+        const float *wk = work + ((size_t)c * d.value_heads + h) * kChunkFloats;
+        const uint32_t t0 = c * kC, n = min((uint32_t)kC, tokens - t0);
+        __syncthreads();   // previous chunk done with the tiles
+        for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
+            const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
+            const float eg = wk[kChunkEG + r], egc = wk[kChunkEGC + r];
+            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f), k4 = q4;
+            if ((uint32_t)r < n) {
+                const size_t item = t0 + r;
+                q4 = *reinterpret_cast<const float4 *>(qk + (item * 2 + 0) * d.key_width + kh * kD + c4);
+                k4 = *reinterpret_cast<const float4 *>(qk + (item * 2 + 1) * d.key_width + kh * kD + c4);
+            }
+            q4.x *= eg; q4.y *= eg; q4.z *= eg; q4.w *= eg;
+            k4.x *= egc; k4.y *= egc; k4.z *= egc; k4.w *= egc;
+            *reinterpret_cast<float4 *>(Qs + r * (kD + 4) + c4) = q4;
+            *reinterpret_cast<float4 *>(Ks + r * (kD + 4) + c4) = k4;
+            *reinterpret_cast<float4 *>(Ws + r * (kD + 4) + c4) =
+                *reinterpret_cast<const float4 *>(wk + kChunkW + r * kD + c4);
+        }
+        for (int i = tid; i < kC * kC; i += blockDim.x) Ps[(i / kC) * (kC + 1) + i % kC] = wk[kChunkP + i];
+        __syncthreads();
+        // delta = U - W S : thread -> column f, rows 8 grp .. 8 grp + 7
+        {
+            float acc[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+            for (int k = 0; k < kD; ++k) {
+                const float sv = S[k * kSlice + f];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) acc[r] = fmaf(Ws[(8 * grp + r) * (kD + 4) + k], sv, acc[r]);
+            }
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const int i = 8 * grp + r;
+                Ds[i * kSlice + f] = wk[kChunkU + i * kD + col0 + f] - acc[r];
+            }
+        }
+        __syncthreads();
+        // O = (e^G Q) S + P delta for the same rows / column
+        {
+            float acc[8];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+            for (int k = 0; k < kD; ++k) {
+                const float sv = S[k * kSlice + f];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) acc[r] = fmaf(Qs[(8 * grp + r) * (kD + 4) + k], sv, acc[r]);
+            }
+            for (int j = 0; j < kC; ++j) {
+                const float dv = Ds[j * kSlice + f];
+#pragma unroll
+                for (int r = 0; r < 8; ++r) acc[r] = fmaf(Ps[(8 * grp + r) * (kC + 1) + j], dv, acc[r]);
+            }
+#pragma unroll
+            for (int r = 0; r < 8; ++r) {
+                const uint32_t i = 8 * grp + r;
+                if (i < n) {
+                    bad |= !isfinite(acc[r]);
+                    obuf[(size_t)(t0 + i) * d.value_width + h * kD + col0 + f] = acc[r];
+                }
+            }
+        }
+        __syncthreads();   // every read of the old S is done
+        // S = e^(G_C) S + (e^(G_C - G) K)^T delta : thread -> column f, rows 16 grp .. 16 grp + 15
+        {
+            const float eg_c = wk[kChunkTot];
+            float acc[16];
+#pragma unroll
+            for (int r = 0; r < 16; ++r) acc[r] = eg_c * S[(16 * grp + r) * kSlice + f];
+            for (int i = 0; i < kC; ++i) {
+                const float dv = Ds[i * kSlice + f];
+#pragma unroll
+                for (int r = 0; r < 16; ++r) acc[r] = fmaf(Ks[i * (kD + 4) + 16 * grp + r], dv, acc[r]);
+            }
+#pragma unroll
+            for (int r = 0; r < 16; ++r) S[(16 * grp + r) * kSlice + f] = acc[r];
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < kD * kSlice; i += blockDim.x) {
+        const float v = S[i];
+        bad |= !isfinite(v);
+        sout[(size_t)(i / kSlice) * kD + col0 + i % kSlice] = v;
+    }
+    if (__syncthreads_or(bad) && tid == 0) chunk_raise(err, kErrNonFinite);
+}
+
+// ---------------------------------------------------------------- phase 3
+// grid (Hv, T), 128 threads: o * rsqrt(mean(o^2) + eps) * norm_w * sigmoid(z).
+__global__ void __launch_bounds__(128)
+gdn_gate_norm_kernel(GdnDims d, GdnWeightsDev w, const float *__restrict__ obuf, const float *__restrict__ proj,
+                     uint32_t ldp, float *__restrict__ gated, ErrorWord err) {
+    __shared__ float red[4];
+    if (chunk_error_raised(err)) return;
+    const uint32_t h = blockIdx.x, t = blockIdx.y;
+    const int f = threadIdx.x;
+    const float o = obuf[(size_t)t * d.value_width + h * kD + f];
+    float v = o * o;
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+    if ((f & 31) == 0) red[f >> 5] = v;
+    __syncthreads();
+    const float sumsq = red[0] + red[1] + red[2] + red[3];
+    const float inv = 1.0f / sqrtf(sumsq / (float)kD + d.eps);
+    const float z = proj[(size_t)t * ldp + d.conv_channels + h * kD + f];
+    const float g = (w.norm[f] * (o * inv)) * chunk_sigmoid(z);
+    if (!isfinite(g)) chunk_raise(err, kErrNonFinite);
+    gated[(size_t)t * d.value_width + h * kD + f] = g;
+}
+
+void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatchPtrs &p, uint32_t tokens,
+                        const float *qk, const float *v, const float *beta, const float *logdecay,
+                        const float *proj, uint32_t ldp, float *gated, float *work, ErrorWord err,
+                        cudaStream_t stream) {
+    KernelTimer timer("gdn_recurrence", stream);
+    const uint32_t chunks = (tokens + kC - 1) / kC;
+    float *obuf = work + (size_t)chunks * d.value_heads * kChunkFloats;
+    const size_t smem1 = (size_t)(2 * kC * (kD + 4) + kC * (kC + 1) + 2 * kC + 2 * kC * kD) * sizeof(float);
+    const size_t smem2 = (size_t)(kD * kSlice + 3 * kC * (kD + 4) + kC * (kC + 1) + kC * kSlice) * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+        cudaFuncSetAttribute(gdn_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+        attr = true;
+    }
+    gdn_chunk_prep_kernel<<<dim3(d.value_heads, chunks), 256, smem1, stream>>>(d, tokens, qk, v, beta, logdecay,
+                                                                              work, err);
+    count_launch();
+    gdn_chunk_state_kernel<<<dim3(d.value_heads, kD / kSlice), 256, smem2, stream>>>(d, p, tokens, qk, work, obuf,
+                                                                                     err);
+    count_launch();
+    gdn_gate_norm_kernel<<<dim3(d.value_heads, tokens), 128, 0, stream>>>(d, w, obuf, proj, ldp, gated, err);
+    count_launch();
+}
+
+}  // namespace kqb

@@ -185,6 +185,36 @@ def _gdn_setup(kq, oracle, dims, seed, in_type, out_type, gate_type):
     return weights, prov, layer, oracle.gdn_weights_f32(weights)
 
 
+@pytest.mark.parametrize("hidden,kh,vh,T,seed", [(512, 16, 32, 300, 61), (256, 2, 4, 2100, 62)])
+def test_gdn_chunked_prefill(kq, oracle, hidden, kh, vh, T, seed):
+    """Prefill long enough for the chunked (WY-form) recurrence: 64-token
+    chunks with a partial last chunk, a padding mask, a non-zero initial
+    state, and (T = 2100) two device passes; outputs and both states against
+    the reference's token-by-token recurrence."""
+    from kqb200 import synth
+    dims = synth.GdnDims(hidden=hidden, key_heads=kh, value_heads=vh)
+    weights, prov, layer, w = _gdn_setup(kq, oracle, dims, seed, synth.TYPE_Q6_K, synth.TYPE_Q6_K, synth.TYPE_Q4_K)
+    try:
+        conv0, rec0 = synth.gdn_state(seed + 1, dims)
+        x = synth.hidden(seed + 2, T, dims.hidden)
+        mask = np.ones(T, np.uint8)
+        mask[5:9] = 0
+        mask[T - 3:] = 0
+        s = kq.GdnState(layer)
+        s.load(conv0, rec0)
+        y = s.execute_quantized(x, mask)
+        conv, rec, _ = s.save()
+        st, yo, convo, reco = oracle.gdn_run(dims, w, x, conv0, rec0, mask)
+        assert st == 0
+        assert_close(y, yo, "output")
+        assert_close(rec, reco, "recurrent state")
+        assert_close(conv, convo, "conv state")
+        s.close()
+    finally:
+        layer.close()
+        prov.close()
+
+
 def test_gdn_config0_decode_quantized(kq, oracle):
     """one decode step, hidden 2048, 16x128 key heads,
     32x128 value heads, Q8_0 qkv/z/out, F32 alpha/beta, N(0,1) conv state,
