@@ -172,9 +172,32 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
             s.raw[(size_t)pos * di + i] = v;
         }
         __syncthreads();
-        // the token completes a block: cache that block's key
-        if ((pos + 1) % d.block == 0 && threadIdx.x == 0) {
-            if (!exact_block_key(d, w, s, pos / d.block, vec)) bad = true;
+        // the token completes a block: cache that block's key (the steps of
+        // exact_block_key, spread over the CTA; only the RMS sum is serial)
+        if ((pos + 1) % d.block == 0) {
+            const uint32_t bi = pos / d.block;
+            for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) {
+                float sum = 0.0f;
+                for (uint32_t o = 0; o < d.block; ++o)
+                    sum = __fadd_rn(sum, s.raw[(size_t)(bi * d.block + o) * di + f]);
+                vec[f] = __fdiv_rn(sum, (float)d.block);
+            }
+            __syncthreads();
+            if (threadIdx.x == 0) *inv_slot = exact_rms_inverse(vec, di, d.eps);
+            __syncthreads();
+            const float inv = *inv_slot;
+            if (!isfinite(inv)) bad = true;
+            for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) vec[f] = exact_norm_apply(vec[f], inv, w.ik_norm[f]);
+            __syncthreads();
+            const uint32_t half = d.rotary / 2, bpos = bi * d.block;
+            for (uint32_t i = threadIdx.x; i < half; i += blockDim.x)
+                exact_rope_pair(vec, i, half, w.rope_cos[(size_t)bpos * half + i], w.rope_sin[(size_t)bpos * half + i]);
+            __syncthreads();
+            const uint32_t ld = s.capacity / d.block;
+            for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) {
+                if (!isfinite(vec[f])) bad = true;
+                s.block_keys[(size_t)f * ld + bi] = vec[f];
+            }
         }
     }
     if (__syncthreads_or(bad) && threadIdx.x == 0) qsa_raise(err, kErrNonFinite);
@@ -252,6 +275,7 @@ qsa_score_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ iq,
     for (uint32_t h0 = 0; h0 < d.index_heads; h0 += 4) {
         const uint32_t nh = min(4u, d.index_heads - h0);
         float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
         for (uint32_t f = 0; f < d.index_dim; ++f) {
             const float kv = key[(size_t)f * ld];
 #pragma unroll
@@ -327,14 +351,32 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
                 if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
             }
             __syncthreads();
-            if (tid == 0) {
-                uint32_t need = s_need, acc = 0, bin = 255;
-                for (int bb = 255; bb >= 0; --bb) {
-                    if (acc + hist[bb] >= need) { bin = (uint32_t)bb; break; }
-                    acc += hist[bb];
+            if (tid < 32) {
+                // highest bin whose suffix count reaches `need`: lane l owns
+                // bins 255-8l .. 248-8l (descending), a warp scan finds the lane
+                const uint32_t need = s_need;
+                uint32_t part = 0;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) part += hist[255 - 8 * tid - e];
+                uint32_t incl = part;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t up = __shfl_up_sync(0xffffffffu, incl, o);
+                    if ((int)tid >= o) incl += up;
                 }
-                s_need = need - acc;
-                s_prefix = prefix | (bin << shift);
+                const uint32_t excl = incl - part;
+                const unsigned hit = __ballot_sync(0xffffffffu, incl >= need);
+                const int lane_hit = hit ? __ffs(hit) - 1 : 31;
+                if ((int)tid == lane_hit) {
+                    uint32_t acc = excl, bin = 255 - 8 * tid - 7;
+                    for (int e = 0; e < 8; ++e) {
+                        const uint32_t bb = 255 - 8 * tid - e;
+                        if (acc + hist[bb] >= need) { bin = bb; break; }
+                        acc += hist[bb];
+                    }
+                    s_need = need - acc;
+                    s_prefix = prefix | (bin << shift);
+                }
             }
             mask |= 255u << shift;
             __syncthreads();
