@@ -134,10 +134,12 @@ struct GdnResolved {
 // device arrays [batch*tokens][H]; mask (device, may be null) is [tokens]
 // for batch == 1.  States flip optimistically and are registered for
 // roll-back; the caller synchronises.
+// `check_input`: the caller has not checked x for non-finite values; the
+// in-projection (or a separate pass) does.
 static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const GdnResolved &w,
                              kq_gdn_state *const *states, uint32_t batch, uint32_t tokens,
                              const float *x, const uint8_t *mask, float *y, ErrorWord err,
-                             kq_diagnostic *diag) {
+                             kq_diagnostic *diag, bool check_input = false) {
     const GdnDims gd = kernel_dims(cfg);
     const uint32_t H = gd.hidden, C = gd.conv_channels, Vd = gd.value_width, Hv = gd.value_heads;
     const uint32_t ldp = C + Vd + 2 * Hv;
@@ -200,7 +202,9 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
                 p.rec_out[b] = s->rec[1 - s->cur];
             }
             const uint32_t n_items = gb * tc;
-            launch_projection(in, xin, H, proj, ldp, n_items, err, c->stream, partial, partial_floats);
+            if (!launch_projection(in, xin, H, proj, ldp, n_items, err, c->stream, partial, partial_floats) &&
+                check_input)
+                launch_check_finite(xin, (uint64_t)n_items * H, err, c->stream);
             launch_gdn_conv_gates(gd, w.vec, p, gb, tc, proj, ldp, qk, v, beta, decay, err, c->stream, logdecay);
             if (chunked && tc >= kChunkedMinTokens)
                 launch_gdn_chunked(gd, w.vec, p, tc, qk, v, beta, logdecay, proj, ldp, gated, chunk_work, err,
@@ -208,8 +212,9 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
             else
                 launch_gdn_recurrence(gd, w.vec, p, gb, tc, qk, v, beta, decay, proj, ldp, gated, err,
                                       c->stream);
-            launch_projection(out, gated, Vd, y + row0 * H, H, n_items, err, c->stream, partial, partial_floats);
-            launch_check_finite(y + row0 * H, (uint64_t)n_items * H, err, c->stream);
+            if (!launch_projection(out, gated, Vd, y + row0 * H, H, n_items, err, c->stream, partial,
+                                   partial_floats))
+                launch_check_finite(y + row0 * H, (uint64_t)n_items * H, err, c->stream);
             for (uint32_t b = 0; b < gb; ++b) {
                 kq_gdn_state *s = states[g0 + b];
                 s->cur = 1 - s->cur;
@@ -718,8 +723,8 @@ kq_status kq_b200_gdn_decode_batch(const kq_gdn_config *config, kq_gdn_state *co
     if (st != KQ_STATUS_OK) return st;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     ErrorWord err = c->begin_call();
-    launch_check_finite(hidden, (uint64_t)batch * config->dims.hidden_size, err, c->stream);
-    return gdn_enqueue(c, config, w, states, batch, 1, hidden, nullptr, output, err, diagnostic);
+    return gdn_enqueue(c, config, w, states, batch, 1, hidden, nullptr, output, err, diagnostic,
+                       /*check_input=*/true);
 }
 
 const char *kq_gdn_checkpoint_kind_name(kq_gdn_checkpoint_kind kind) {

@@ -182,10 +182,12 @@ struct SelectionCopy {
 // or tokens == 1).  x / y are device [batch*tokens][H].  When `selection` is
 // non-null (batch == 1) the stream is synchronised after every token and the
 // selection of each token is copied out.
+// `check_input`: the caller has not checked x for non-finite values; the
+// main projection (or a separate pass) does.
 static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const QsaResolved &w,
                              kq_qsa_state *const *states, uint32_t batch, uint32_t tokens, const float *x,
                              float *y, ErrorWord err, std::vector<SelectionCopy> *selection,
-                             kq_diagnostic *diag) {
+                             kq_diagnostic *diag, bool check_input = false) {
     const QsaDims d = kernel_dims(cfg);
     const uint32_t H = d.hidden, hd = d.head_dim;
     const uint32_t qw = d.q_heads * hd, kvw = d.kv_heads * hd;
@@ -254,8 +256,10 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
         const uint32_t gb = std::min<uint32_t>(kMaxBatch, batch - g0);
         const size_t row0 = (size_t)g0 * tokens;
         const size_t n_items = (size_t)gb * tokens;
-        launch_projection(main, x + row0 * H, H, proj, ldp, (uint32_t)n_items, err, c->stream, partial,
-                          partial_floats);
+        if (!launch_projection(main, x + row0 * H, H, proj, ldp, (uint32_t)n_items, err, c->stream, partial,
+                               partial_floats) &&
+            check_input)
+            launch_check_finite(x + row0 * H, n_items * H, err, c->stream);
         launch_projection_exact(index, x + row0 * H, H, iproj, ldi, (uint32_t)n_items, err, c->stream);
         for (uint32_t b = 0; b < gb; ++b) {
             kq_qsa_state *s = states[g0 + b];
@@ -299,9 +303,9 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 selection->push_back(std::move(sc));
             }
         }
-        launch_projection(out, gated, qw, y + row0 * H, H, (uint32_t)n_items, err, c->stream, partial,
-                          partial_floats);
-        launch_check_finite(y + row0 * H, n_items * H, err, c->stream);
+        if (!launch_projection(out, gated, qw, y + row0 * H, H, (uint32_t)n_items, err, c->stream, partial,
+                               partial_floats))
+            launch_check_finite(y + row0 * H, n_items * H, err, c->stream);
         for (uint32_t b = 0; b < gb; ++b) {
             kq_qsa_state *s = states[g0 + b];
             s->length += tokens;
@@ -884,8 +888,8 @@ kq_status kq_b200_qsa_decode_batch(const kq_qsa_config *config, kq_qsa_state *co
     QsaResolved w{config->q, config->k, config->v, config->o, config->iq, config->ik,
                   config->q_norm, config->k_norm, config->iq_norm, config->ik_norm};
     ErrorWord err = c->begin_call();
-    launch_check_finite(hidden, (uint64_t)batch * config->dims.hidden_size, err, c->stream);
-    return qsa_enqueue(c, config, w, states, batch, 1, hidden, output, err, nullptr, diagnostic);
+    return qsa_enqueue(c, config, w, states, batch, 1, hidden, output, err, nullptr, diagnostic,
+                       /*check_input=*/true);
 }
 
 const char *kq_qsa_checkpoint_kind_name(kq_qsa_checkpoint_kind kind) {

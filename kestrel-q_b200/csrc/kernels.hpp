@@ -52,13 +52,16 @@ struct ErrorWord {
 
 // ---- projections (kernels_proj.cu)
 // `partial` (may be null) is work space of partial_floats floats; the
-// tensor-core path runs when it holds projection_workspace_floats().
-void launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
+// tensor-core path runs when it holds projection_workspace_floats().  Returns
+// true when the tensor-core path ran: it checks its input and its output for
+// non-finite values on the device, so callers need no separate check.
+bool launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
                        float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
                        cudaStream_t stream, float *partial = nullptr,
                        size_t partial_floats = 0);
 // Tensor-core path (kernels_umma.cu), used for batches above 8.  Returns
-// false (nothing launched) for shapes / types it does not cover.  `xtiles`
+// false (nothing launched) for shapes / types it does not cover (true: the
+// input and output were checked for non-finite values).  `xtiles`
 // is work space of umma_xtile_bytes(batch, cols) bytes.  `cache_maps`
 // false encodes the TMA descriptors on the stack instead of the host-side
 // descriptor cache (no host allocation).

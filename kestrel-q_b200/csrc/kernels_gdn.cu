@@ -72,6 +72,37 @@ __device__ __forceinline__ float conv_history(const GdnDims &d, const float *con
     return conv_in[(size_t)c * d.kernel + (uint32_t)(t + 1 + j)];
 }
 
+// conv + SiLU of channel c for token t: taps in the reference's order
+// (sum = sum + w_j * h_j, j = 0..K-1).  KT > 0 fixes the kernel size so that
+// the K history loads and weight loads are all issued before the sum.
+template <int KT>
+__device__ __forceinline__ float conv_channel(const GdnDims &d, const GdnWeightsDev &w, const float *conv_in,
+                                             float *conv_out, bool last, const float *proj, uint32_t ldp,
+                                             uint32_t item0, int t, uint32_t c) {
+    float s = 0.0f;
+    if constexpr (KT > 0) {
+        float hv[KT], wv[KT];
+#pragma unroll
+        for (int j = 0; j < KT; ++j) {
+            hv[j] = conv_history(d, conv_in, proj, ldp, item0, t, j, c);
+            wv[j] = w.conv[(size_t)c * KT + j];
+        }
+#pragma unroll
+        for (int j = 0; j < KT; ++j) {
+            s = __fadd_rn(s, __fmul_rn(wv[j], hv[j]));
+            if (last) conv_out[(size_t)c * KT + j] = hv[j];
+        }
+    } else {
+        for (uint32_t j = 0; j < d.kernel; ++j) {
+            const float h = conv_history(d, conv_in, proj, ldp, item0, t, (int)j, c);
+            s = __fadd_rn(s, __fmul_rn(w.conv[(size_t)c * d.kernel + j], h));
+            if (last) conv_out[(size_t)c * d.kernel + j] = h;
+        }
+    }
+    return s;
+}
+
+template <int KT>
 __global__ void __launch_bounds__(kConvThreads)
 gdn_conv_gates_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t tokens,
                       const float *__restrict__ proj, uint32_t ldp,
@@ -97,12 +128,7 @@ gdn_conv_gates_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t token
         const uint32_t i = threadIdx.x;
         if (i < d.key_dim) {
             uint32_t c = which * d.key_width + kh * d.key_dim + i;
-            float s = 0.0f;
-            for (uint32_t j = 0; j < d.kernel; ++j) {
-                float h = conv_history(d, conv_in, proj, ldp, item0, t, (int)j, c);
-                s = __fadd_rn(s, __fmul_rn(w.conv[(size_t)c * d.kernel + j], h));
-                if (last) conv_out[(size_t)c * d.kernel + j] = h;
-            }
+            const float s = conv_channel<KT>(d, w, conv_in, conv_out, last, proj, ldp, item0, t, c);
             val = s * stable_sigmoid(s);
             bad |= !isfinite(val);
         }
@@ -119,12 +145,7 @@ gdn_conv_gates_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t token
         uint32_t h = kh * d.repeat + r;
         for (uint32_t i = threadIdx.x; i < d.value_dim; i += blockDim.x) {
             uint32_t c = 2 * d.key_width + h * d.value_dim + i;
-            float s = 0.0f;
-            for (uint32_t j = 0; j < d.kernel; ++j) {
-                float hv = conv_history(d, conv_in, proj, ldp, item0, t, (int)j, c);
-                s = __fadd_rn(s, __fmul_rn(w.conv[(size_t)c * d.kernel + j], hv));
-                if (last) conv_out[(size_t)c * d.kernel + j] = hv;
-            }
+            const float s = conv_channel<KT>(d, w, conv_in, conv_out, last, proj, ldp, item0, t, c);
             float val = s * stable_sigmoid(s);
             bad |= !isfinite(val);
             vout[(size_t)item * d.value_width + h * d.value_dim + i] = val;
@@ -330,8 +351,12 @@ void launch_gdn_conv_gates(const GdnDims &d, const GdnWeightsDev &w,
                            ErrorWord err, cudaStream_t stream, float *logdecay) {
     dim3 grid(d.key_heads, batch * tokens);
     KernelTimer timer("gdn_conv", stream);
-    gdn_conv_gates_kernel<<<grid, kConvThreads, 0, stream>>>(d, w, p, tokens, proj, ldp, qk, v,
-                                                            beta, decay, logdecay, err);
+    if (d.kernel == 4)
+        gdn_conv_gates_kernel<4><<<grid, kConvThreads, 0, stream>>>(d, w, p, tokens, proj, ldp, qk, v,
+                                                                   beta, decay, logdecay, err);
+    else
+        gdn_conv_gates_kernel<0><<<grid, kConvThreads, 0, stream>>>(d, w, p, tokens, proj, ldp, qk, v,
+                                                                   beta, decay, logdecay, err);
     count_launch();
 }
 

@@ -371,7 +371,7 @@ size_t projection_workspace_floats(uint32_t batch, uint32_t /*ldy*/, uint32_t co
     return ((umma_xtile_bytes(batch, cols) + 255) & ~size_t(255)) / 4;
 }
 
-void launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
+bool launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
                        float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
                        cudaStream_t stream, float *partial, size_t partial_floats) {
     ProjSegments segs = in;
@@ -379,7 +379,7 @@ void launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
     if (batch > 8 && !force_simt_projection() && partial != nullptr &&
         launch_projection_umma(segs, x, ldx, y, ldy, batch, reinterpret_cast<uint8_t *>(partial),
                                partial_floats * 4, err, stream))
-        return;
+        return true;
     if (batch <= 8) {
         fill_tile_starts(segs, 1);
         uint32_t rows = segs.tile_start[segs.count];
@@ -396,6 +396,7 @@ void launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
         proj_tiled_kernel<<<grid, 256, 0, stream>>>(segs, x, ldx, y, ldy, batch, err);
     }
     count_launch();
+    return false;
 }
 
 void launch_projection_exact(const ProjSegments &in, const float *x,

@@ -437,7 +437,7 @@ struct TmapSet {
 // One CTA converts 16 rows of one chunk; one thread 8 values.
 __global__ void __launch_bounds__(128)
 xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t cols, uint32_t nchunks,
-             uint8_t *__restrict__ out) {
+             uint8_t *__restrict__ out, ErrorWord err) {
     const uint32_t c = blockIdx.x >> 2, bt = blockIdx.y;
     const uint32_t r = (blockIdx.x & 3u) * 16u + (threadIdx.x >> 3), q8 = threadIdx.x & 7u;
     const uint32_t b = bt * kUN + r, k0 = c * kUK + q8 * 8u;
@@ -451,6 +451,12 @@ xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = (b < batch && k0 + i < cols) ? src[i] : 0.0f;
     }
+    // the projection's input check (non-finite input -> NUMERIC_DOMAIN)
+    bool bad = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) bad |= !isfinite(v[i]);
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0)
+        atomicCAS(err.word, 0ull, ((unsigned long long)kErrNonFinite << 32) | err.call_id);
     uint4 hi, lo;
     pack8(v, hi, lo);
     uint8_t *tile = out + ((size_t)bt * nchunks + c) * (2 * kBTile);
@@ -647,13 +653,17 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     }
     const bool write = all_ok && !skip;
     const uint32_t nsplit = gridDim.z;
+    bool out_bad = false;   // the projection's output check
     if (nsplit == 1) {
         const uint32_t row = row0 + trow;
         if (warp < kDecodeWarps && write && row < m.rows) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const uint32_t b = b0 + col_base + j;
-                if (b < batch) y[(size_t)b * ldy + segs.out_offset[seg] + row] = acc[j];
+                if (b < batch) {
+                    out_bad |= !isfinite(acc[j]);
+                    y[(size_t)b * ldy + segs.out_offset[seg] + row] = acc[j];
+                }
             }
         }
     } else {
@@ -679,10 +689,14 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
             for (uint32_t z = 1; z < 8; ++z)
                 if (z < nsplit) sum = __fadd_rn(sum, v[z]);
             const uint32_t row = row0 + lr, b = b0 + bb;
-            if (write && row < m.rows && b < batch) y[(size_t)b * ldy + segs.out_offset[seg] + row] = sum;
+            if (write && row < m.rows && b < batch) {
+                out_bad |= !isfinite(sum);
+                y[(size_t)b * ldy + segs.out_offset[seg] + row] = sum;
+            }
         }
         cluster_sync();   // peers finish reading this CTA's tile before it exits
     }
+    if (out_bad) atomicCAS(err.word, 0ull, ((unsigned long long)kErrNonFinite << 32) | err.call_id);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == kAllocWarp) {
@@ -939,7 +953,7 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
     }
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
     const dim3 xg(nchunks * 4, (batch + kUN - 1) / kUN);
-    xconv_kernel<<<xg, 128, 0, stream>>>(x, ldx, batch, cols, nchunks, xtiles);
+    xconv_kernel<<<xg, 128, 0, stream>>>(x, ldx, batch, cols, nchunks, xtiles, err);
     count_launch();
     // one launch per weight type present
     bool done[kMaxSegments] = {};

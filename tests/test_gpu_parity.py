@@ -301,6 +301,56 @@ def test_gdn_decode_batch_matches_per_sequence_oracle(kq, oracle):
         prov.close()
 
 
+@pytest.mark.parametrize("B", [5, 40])
+def test_decode_batch_rejects_non_finite_input(kq, oracle, B):
+    """A NaN in one sequence's hidden state makes the batched decode of both
+    operators fail with NUMERIC_DOMAIN and roll every state back; B = 40 runs
+    the tensor-core projections (input check fused into their activation
+    staging), B = 5 the warp GEMV (separate check)."""
+    import torch
+    from kqb200 import synth
+    gdims = synth.GdnDims(hidden=512, key_heads=2, value_heads=4, key_dim=128, value_dim=128)
+    _, gprov, glayer, _ = _gdn_setup(kq, oracle, gdims, 21, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_Q4_K)
+    qdims = synth.QsaDims(hidden=512, query_heads=8, kv_heads=2, head_dim=256, index_heads=4, index_dim=128,
+                          block=4, budget=256, max_context=4096, rotary=64)
+    _, qprov, qlayer, _ = _qsa_setup(kq, oracle, qdims, 22)
+    try:
+        gstates, qstates, g0, q0 = [], [], [], []
+        for b in range(B):
+            s = kq.GdnState(glayer)
+            c0, r0 = synth.gdn_state(300 + b, gdims)
+            s.load(c0, r0)
+            gstates.append(s)
+            g0.append((c0, r0))
+            q = kq.QsaState(qlayer, 64)
+            k, v, r = synth.qsa_cache(400 + b, qdims, 9)
+            q.load(k, v, r)
+            qstates.append(q)
+            q0.append(len(k))
+        x = synth.hidden(23, B, 512)
+        x[B // 2, 7] = np.nan
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty_like(xd)
+        torch.cuda.synchronize()
+        for call in (lambda: kq.gdn_decode_batch(glayer, gstates, xd.data_ptr(), yd.data_ptr()),
+                     lambda: kq.qsa_decode_batch(qlayer, qstates, xd.data_ptr(), yd.data_ptr())):
+            call()
+            with pytest.raises(kq.KQError) as e:
+                kq.synchronize()
+            assert e.value.status == kq.abi.NUMERIC_DOMAIN
+        for b in (0, B // 2, B - 1):
+            c1, r1, _ = gstates[b].save()
+            assert np.array_equal(bits(c1), bits(g0[b][0])) and np.array_equal(bits(r1), bits(g0[b][1]))
+            assert kq.lib().kq_qsa_state_length(qstates[b].handle) == q0[b]
+        for s in gstates + qstates:
+            s.close()
+    finally:
+        glayer.close()
+        qlayer.close()
+        gprov.close()
+        qprov.close()
+
+
 def test_gdn_failure_leaves_state_unchanged(kq, oracle):
     from kqb200 import synth
     dims = synth.GdnDims(hidden=256, key_heads=2, value_heads=4, key_dim=128, value_dim=128)
