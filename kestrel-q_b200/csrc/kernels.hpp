@@ -7,6 +7,31 @@
 
 namespace kqb {
 
+// Programmatic dependent launch: every kernel of the library is launched
+// with launch_pdl, which lets the GPU set it up while the previous kernel
+// on the stream is still finishing, and every kernel starts with pdl_wait(),
+// which blocks until that previous kernel has completed and its writes are
+// visible.  Nothing is read or written before the wait.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<Args &&>(args)...);
+}
+
+#ifdef __CUDACC__
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+#endif
+
 // Error word shared by every kernel of one device.  0 = no error; otherwise
 // the id of the first failing call (see Runtime::next_call_id) in the low
 // 32 bits and a kernel error code in the high 32 bits.

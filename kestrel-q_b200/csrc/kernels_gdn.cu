@@ -109,6 +109,7 @@ gdn_conv_gates_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t token
                       float *__restrict__ qk, float *__restrict__ vout,
                       float *__restrict__ beta, float *__restrict__ decay,
                       float *__restrict__ logdecay, ErrorWord err) {
+    pdl_wait();
     __shared__ float red[kConvThreads / 32];
     if (gdn_error_raised(err)) return;
     const uint32_t kh = blockIdx.x;
@@ -187,6 +188,7 @@ gdn_recurrence128_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t to
                          const float *__restrict__ beta, const float *__restrict__ decay,
                          const float *__restrict__ proj, uint32_t ldp,
                          float *__restrict__ gated, ErrorWord err) {
+    pdl_wait();
     __shared__ __align__(16) float ks[kDim];
     __shared__ __align__(16) float qs[kDim];
     __shared__ __align__(16) float part[kRecThreads / 32][kDim];
@@ -291,6 +293,7 @@ gdn_recurrence_generic_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32
                               const float *__restrict__ beta, const float *__restrict__ decay,
                               const float *__restrict__ proj, uint32_t ldp,
                               float *__restrict__ gated, ErrorWord err) {
+    pdl_wait();
     __shared__ float red[4];
     if (gdn_error_raised(err)) return;
     const uint32_t h = blockIdx.x, b = blockIdx.y;
@@ -352,10 +355,10 @@ void launch_gdn_conv_gates(const GdnDims &d, const GdnWeightsDev &w,
     dim3 grid(d.key_heads, batch * tokens);
     KernelTimer timer("gdn_conv", stream);
     if (d.kernel == 4)
-        gdn_conv_gates_kernel<4><<<grid, kConvThreads, 0, stream>>>(d, w, p, tokens, proj, ldp, qk, v,
+        launch_pdl(gdn_conv_gates_kernel<4>, grid, kConvThreads, 0, stream, d, w, p, tokens, proj, ldp, qk, v,
                                                                    beta, decay, logdecay, err);
     else
-        gdn_conv_gates_kernel<0><<<grid, kConvThreads, 0, stream>>>(d, w, p, tokens, proj, ldp, qk, v,
+        launch_pdl(gdn_conv_gates_kernel<0>, grid, kConvThreads, 0, stream, d, w, p, tokens, proj, ldp, qk, v,
                                                                    beta, decay, logdecay, err);
     count_launch();
 }
@@ -369,10 +372,10 @@ void launch_gdn_recurrence(const GdnDims &d, const GdnWeightsDev &w,
     dim3 grid(d.value_heads, batch);
     KernelTimer timer("gdn_recurrence", stream);
     if (d.key_dim == kDim && d.value_dim == kDim) {
-        gdn_recurrence128_kernel<<<grid, kRecThreads, 0, stream>>>(d, w, p, tokens, qk, v, beta,
+        launch_pdl(gdn_recurrence128_kernel, grid, kRecThreads, 0, stream, d, w, p, tokens, qk, v, beta,
                                                                   decay, proj, ldp, gated, err);
     } else {
-        gdn_recurrence_generic_kernel<<<grid, 128, 0, stream>>>(d, w, p, tokens, qk, v, beta,
+        launch_pdl(gdn_recurrence_generic_kernel, grid, 128, 0, stream, d, w, p, tokens, qk, v, beta,
                                                                decay, proj, ldp, gated, err);
     }
     count_launch();

@@ -74,6 +74,7 @@ __global__ void __launch_bounds__(256)
 gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, const float *__restrict__ vin,
                       const float *__restrict__ beta, const float *__restrict__ logdecay,
                       float *__restrict__ work, ErrorWord err) {
+    pdl_wait();
     extern __shared__ __align__(16) float cs[];
     float *Ks = cs;                        // [64][128 + 4]
     float *Qs = Ks + kC * (kD + 4);        // [64][128 + 4]
@@ -175,6 +176,7 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
 __global__ void __launch_bounds__(256)
 gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *__restrict__ qk,
                        const float *__restrict__ work, float *__restrict__ obuf, ErrorWord err) {
+    pdl_wait();
     extern __shared__ __align__(16) float cs[];
     float *S = cs;                            // [128][32]
     float *Ws = S + kD * kSlice;              // [64][128 + 4]
@@ -285,6 +287,7 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
 __global__ void __launch_bounds__(128)
 gdn_gate_norm_kernel(GdnDims d, GdnWeightsDev w, const float *__restrict__ obuf, const float *__restrict__ proj,
                      uint32_t ldp, float *__restrict__ gated, ErrorWord err) {
+    pdl_wait();
     __shared__ float red[4];
     if (chunk_error_raised(err)) return;
     const uint32_t h = blockIdx.x, t = blockIdx.y;
@@ -318,13 +321,13 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
         cudaFuncSetAttribute(gdn_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
         attr = true;
     }
-    gdn_chunk_prep_kernel<<<dim3(d.value_heads, chunks), 256, smem1, stream>>>(d, tokens, qk, v, beta, logdecay,
+    launch_pdl(gdn_chunk_prep_kernel, dim3(d.value_heads, chunks), 256, smem1, stream, d, tokens, qk, v, beta, logdecay,
                                                                               work, err);
     count_launch();
-    gdn_chunk_state_kernel<<<dim3(d.value_heads, kD / kSlice), 256, smem2, stream>>>(d, p, tokens, qk, work, obuf,
+    launch_pdl(gdn_chunk_state_kernel, dim3(d.value_heads, kD / kSlice), 256, smem2, stream, d, p, tokens, qk, work, obuf,
                                                                                      err);
     count_launch();
-    gdn_gate_norm_kernel<<<dim3(d.value_heads, tokens), 128, 0, stream>>>(d, w, obuf, proj, ldp, gated, err);
+    launch_pdl(gdn_gate_norm_kernel, dim3(d.value_heads, tokens), 128, 0, stream, d, w, obuf, proj, ldp, gated, err);
     count_launch();
 }
 

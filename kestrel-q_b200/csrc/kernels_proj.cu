@@ -56,6 +56,7 @@ __global__ void __launch_bounds__(256)
 proj_tiled_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                   float *__restrict__ y, uint32_t ldy, uint32_t batch,
                   ErrorWord err) {
+    pdl_wait();
     __shared__ __align__(16) float ws[kTileK][kLd];
     __shared__ __align__(16) float xs[kTileK][kLd];
     if (error_raised(err)) return;
@@ -133,6 +134,7 @@ __global__ void __launch_bounds__(256)
 proj_warp_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                  float *__restrict__ y, uint32_t ldy, uint32_t batch,
                  ErrorWord err) {
+    pdl_wait();
     if (error_raised(err)) return;
     const int lane = threadIdx.x & 31;
     const uint32_t warp_global = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -230,6 +232,7 @@ __global__ void __launch_bounds__(kExThreads)
 proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                   float *__restrict__ y, uint32_t ldy, uint32_t batch,
                   ErrorWord err) {
+    pdl_wait();
     extern __shared__ __align__(16) uint8_t ex_smem[];
     if (error_raised(err)) return;
     float *xs_base = reinterpret_cast<float *>(ex_smem);
@@ -385,15 +388,15 @@ bool launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
         uint32_t rows = segs.tile_start[segs.count];
         dim3 grid((rows + 7) / 8);
         if (batch <= 1)
-            proj_warp_kernel<1><<<grid, 256, 0, stream>>>(segs, x, ldx, y, ldy, batch, err);
+            launch_pdl(proj_warp_kernel<1>, grid, 256, 0, stream, segs, x, ldx, y, ldy, batch, err);
         else if (batch <= 4)
-            proj_warp_kernel<4><<<grid, 256, 0, stream>>>(segs, x, ldx, y, ldy, batch, err);
+            launch_pdl(proj_warp_kernel<4>, grid, 256, 0, stream, segs, x, ldx, y, ldy, batch, err);
         else
-            proj_warp_kernel<8><<<grid, 256, 0, stream>>>(segs, x, ldx, y, ldy, batch, err);
+            launch_pdl(proj_warp_kernel<8>, grid, 256, 0, stream, segs, x, ldx, y, ldy, batch, err);
     } else {
         fill_tile_starts(segs, kTileR);
         dim3 grid(segs.tile_start[segs.count], (batch + kTileB - 1) / kTileB);
-        proj_tiled_kernel<<<grid, 256, 0, stream>>>(segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_tiled_kernel, grid, 256, 0, stream, segs, x, ldx, y, ldy, batch, err);
     }
     count_launch();
     return false;
@@ -423,11 +426,11 @@ void launch_projection_exact(const ProjSegments &in, const float *x,
         attr = true;
     }
     if (mode == 0)
-        proj_exact_kernel<0><<<grid, kExThreads, kExSmem, stream>>>(segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<0>, grid, kExThreads, kExSmem, stream, segs, x, ldx, y, ldy, batch, err);
     else if (mode == 1)
-        proj_exact_kernel<1><<<grid, kExThreads, kExSmem, stream>>>(segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<1>, grid, kExThreads, kExSmem, stream, segs, x, ldx, y, ldy, batch, err);
     else
-        proj_exact_kernel<2><<<grid, kExThreads, kExSmem, stream>>>(segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<2>, grid, kExThreads, kExSmem, stream, segs, x, ldx, y, ldy, batch, err);
     count_launch();
 }
 
@@ -435,6 +438,7 @@ void launch_projection_exact(const ProjSegments &in, const float *x,
 
 __global__ void dequantize_kernel(uint32_t type, const uint8_t *packed,
                                   uint64_t elements, float *out) {
+    pdl_wait();
     uint64_t run = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     uint64_t first = run * 32u;
     if (first >= elements) return;
@@ -453,13 +457,14 @@ __global__ void dequantize_kernel(uint32_t type, const uint8_t *packed,
 void launch_dequantize(uint32_t type, const uint8_t *packed, uint64_t elements,
                        float *out, cudaStream_t stream) {
     uint64_t runs = (elements + 31) / 32;
-    dequantize_kernel<<<(unsigned)((runs + 255) / 256), 256, 0, stream>>>(type, packed, elements, out);
+    launch_pdl(dequantize_kernel, (unsigned)((runs + 255) / 256), 256, 0, stream, type, packed, elements, out);
     count_launch();
 }
 
 __global__ void row_dot_kernel(uint32_t type, const uint8_t *packed,
                                uint64_t elements, const float *x, float *out,
                                int *status) {
+    pdl_wait();
     uint32_t be, bb;
     block_geometry(type, be, bb);
     float acc = 0.0f;
@@ -482,11 +487,12 @@ __global__ void row_dot_kernel(uint32_t type, const uint8_t *packed,
 void launch_row_dot(uint32_t type, const uint8_t *packed, uint64_t elements,
                     const float *x, float *out, int *status,
                     cudaStream_t stream) {
-    row_dot_kernel<<<1, 1, 0, stream>>>(type, packed, elements, x, out, status);
+    launch_pdl(row_dot_kernel, 1, 1, 0, stream, type, packed, elements, x, out, status);
     count_launch();
 }
 
 __global__ void check_finite_kernel(const float *x, uint64_t count, ErrorWord err) {
+    pdl_wait();
     uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     bool bad = false;
@@ -498,12 +504,13 @@ void launch_check_finite(const float *x, uint64_t count, ErrorWord err,
                          cudaStream_t stream) {
     uint64_t blocks = std::min<uint64_t>((count + 255) / 256, 1184);
     if (blocks == 0) blocks = 1;
-    check_finite_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, count, err);
+    launch_pdl(check_finite_kernel, (unsigned)blocks, 256, 0, stream, x, count, err);
     count_launch();
 }
 
 __global__ void mask_rows_kernel(const float *x, const uint8_t *mask, uint32_t rows,
                                  uint32_t cols, float *y) {
+    pdl_wait();
     uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (uint64_t)rows * cols) return;
     y[i] = x[i] * (float)mask[i / cols];
@@ -512,7 +519,7 @@ __global__ void mask_rows_kernel(const float *x, const uint8_t *mask, uint32_t r
 void launch_mask_rows(const float *x, const uint8_t *mask, uint32_t rows,
                       uint32_t cols, float *y, cudaStream_t stream) {
     uint64_t n = (uint64_t)rows * cols;
-    mask_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(x, mask, rows, cols, y);
+    launch_pdl(mask_rows_kernel, (unsigned)((n + 255) / 256), 256, 0, stream, x, mask, rows, cols, y);
     count_launch();
 }
 

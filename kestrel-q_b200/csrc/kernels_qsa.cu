@@ -122,6 +122,7 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
                    const float *__restrict__ iproj, uint32_t ldi,
                    float *__restrict__ q_out, float *__restrict__ iq_out,
                    ErrorWord err) {
+    pdl_wait();
     extern __shared__ float sh[];   // max(d, di) floats + 1
     if (qsa_error_raised(err)) return;
     const uint32_t b = blockIdx.x;
@@ -211,7 +212,7 @@ void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
     size_t smem = (std::max(d.head_dim, d.index_dim) + 1) * sizeof(float);
     dim3 grid(batch, d.q_heads + d.kv_heads + d.index_heads + 1);
     KernelTimer timer("qsa_prepare", stream);
-    qsa_prepare_kernel<<<grid, kPrepThreads, smem, stream>>>(d, w, b, proj, ldp, iproj, ldi,
+    launch_pdl(qsa_prepare_kernel, grid, kPrepThreads, smem, stream, d, w, b, proj, ldp, iproj, ldi,
                                                             q_out, iq_out, err);
     count_launch();
 }
@@ -219,6 +220,7 @@ void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
 // ------------------------------------------------------------ block keys
 __global__ void qsa_block_keys_kernel(QsaDims d, QsaWeightsDev w, QsaSeq s,
                                       uint32_t first, uint32_t end, ErrorWord err) {
+    pdl_wait();
     extern __shared__ float tmp_all[];
     uint32_t bi = first + blockIdx.x * blockDim.x + threadIdx.x;
     bool bad = false;
@@ -240,7 +242,7 @@ void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(qsa_block_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem);
-    qsa_block_keys_kernel<<<(n + threads - 1) / threads, threads, smem, stream>>>(
+    launch_pdl(qsa_block_keys_kernel, (n + threads - 1) / threads, threads, smem, stream, 
         d, w, s, first_block, end_block, err);
     count_launch();
 }
@@ -254,6 +256,7 @@ void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
 __global__ void __launch_bounds__(128)
 qsa_score_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ iq,
                  float *__restrict__ scores, uint32_t ld_scores, ErrorWord err) {
+    pdl_wait();
     extern __shared__ float qsh[];   // [Hi * di]
     if (qsa_error_raised(err)) return;
     const uint32_t b = blockIdx.y;
@@ -297,7 +300,7 @@ void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
     dim3 grid((max_blocks + 127) / 128, batch);
     size_t smem = (size_t)d.index_heads * d.index_dim * sizeof(float);
     KernelTimer timer("qsa_score", stream);
-    qsa_score_kernel<<<grid, 128, smem, stream>>>(d, b, iq, scores, ld_scores, err);
+    launch_pdl(qsa_score_kernel, grid, 128, smem, stream, d, b, iq, scores, ld_scores, err);
     count_launch();
 }
 
@@ -322,6 +325,7 @@ __global__ void __launch_bounds__(kSelThreads)
 qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
                   uint32_t ld_scores, uint32_t *__restrict__ selected,
                   uint32_t *__restrict__ selected_count, ErrorWord err) {
+    pdl_wait();
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_prefix, s_need, s_taken, s_tie_base;
     __shared__ unsigned long long cand[kSelMax];
@@ -443,7 +447,7 @@ void launch_qsa_select(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        uint32_t *selected, uint32_t *selected_count,
                        ErrorWord err, cudaStream_t stream) {
     KernelTimer timer("qsa_select", stream);
-    qsa_select_kernel<<<batch, kSelThreads, 0, stream>>>(d, b, scores, ld_scores, selected,
+    launch_pdl(qsa_select_kernel, batch, kSelThreads, 0, stream, d, b, scores, ld_scores, selected,
                                                         selected_count, err);
     count_launch();
 }
@@ -464,6 +468,7 @@ qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
                   const uint32_t *__restrict__ selected_count,
                   float *__restrict__ part_o, float *__restrict__ part_ml,
                   uint32_t splits, ErrorWord err) {
+    pdl_wait();
     extern __shared__ float smem[];   // [8 warps][HPW][hd + 2]
     if (qsa_error_raised(err)) return;
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -601,6 +606,7 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
                         const uint32_t *__restrict__ selected_count,
                         float *__restrict__ part_o, float *__restrict__ part_ml,
                         uint32_t splits, ErrorWord err) {
+    pdl_wait();
     constexpr int KLD = HD + 4;          // padded K row (conflict-free float4 reads)
     constexpr int HALF = HD / 2;
     constexpr int CH = HD / 4;           // 16-byte chunks per row
@@ -762,6 +768,7 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
                      const uint32_t *__restrict__ selected_count,
                      float *__restrict__ part_o, float *__restrict__ part_ml,
                      uint32_t splits, ErrorWord err) {
+    pdl_wait();
     constexpr int HD = kMhHD;
     extern __shared__ __align__(16) float sm[];
     float *kbuf = sm;                                        // [S][16][HD]
@@ -977,7 +984,7 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
             cudaFuncSetAttribute(qsa_attend_mh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMhSmem);
             attr = true;
         }
-        qsa_attend_mh_kernel<<<grid, 256, kMhSmem, stream>>>(d, b, q, selected, selected_count, partial_o,
+        launch_pdl(qsa_attend_mh_kernel, grid, 256, kMhSmem, stream, d, b, q, selected, selected_count, partial_o,
                                                              partial_ml, splits, err);
     } else if (d.head_dim == 256 || d.head_dim == 128) {
         const int hd = (int)d.head_dim;
@@ -985,22 +992,22 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
         if (hd == 256) {
             cudaFuncSetAttribute(qsa_attend_tiled_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
-            qsa_attend_tiled_kernel<256><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+            launch_pdl(qsa_attend_tiled_kernel<256>, grid, 256, smem, stream, d, b, q, selected, selected_count,
                                                                     partial_o, partial_ml, splits, err);
         } else {
             cudaFuncSetAttribute(qsa_attend_tiled_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
-            qsa_attend_tiled_kernel<128><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+            launch_pdl(qsa_attend_tiled_kernel<128>, grid, 256, smem, stream, d, b, q, selected, selected_count,
                                                                     partial_o, partial_ml, splits, err);
         }
     } else {
         // small heads (reduced test shapes): warp-per-token kernel
         size_t smem = (size_t)8 * 8 * (d.head_dim + 2) * sizeof(float);
         if (d.head_dim <= 32) {
-            qsa_attend_kernel<1, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+            launch_pdl(qsa_attend_kernel<1, 8>, grid, 256, smem, stream, d, b, q, selected, selected_count,
                                                                partial_o, partial_ml, splits, err);
         } else {
-            qsa_attend_kernel<2, 8><<<grid, 256, smem, stream>>>(d, b, q, selected, selected_count,
+            launch_pdl(qsa_attend_kernel<2, 8>, grid, 256, smem, stream, d, b, q, selected, selected_count,
                                                                partial_o, partial_ml, splits, err);
         }
     }
@@ -1016,6 +1023,7 @@ __global__ void qsa_combine_kernel(QsaDims d, const float *__restrict__ part_o,
                                    const float *__restrict__ part_ml, uint32_t splits,
                                    const float *__restrict__ proj, uint32_t ldp,
                                    float *__restrict__ gated, ErrorWord err) {
+    pdl_wait();
     if (qsa_error_raised(err)) return;
     const uint32_t h = blockIdx.x, b = blockIdx.y;
     const uint32_t hd = d.head_dim;
@@ -1047,7 +1055,7 @@ void launch_qsa_combine(const QsaDims &d, uint32_t batch,
                         float *gated, ErrorWord err, cudaStream_t stream) {
     dim3 grid(d.q_heads, batch);
     KernelTimer timer("qsa_combine", stream);
-    qsa_combine_kernel<<<grid, 256, 0, stream>>>(d, partial_o, partial_ml, splits, proj, ldp,
+    launch_pdl(qsa_combine_kernel, grid, 256, 0, stream, d, partial_o, partial_ml, splits, proj, ldp,
                                                  gated, err);
     count_launch();
 }

@@ -438,6 +438,7 @@ struct TmapSet {
 __global__ void __launch_bounds__(128)
 xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t cols, uint32_t nchunks,
              uint8_t *__restrict__ out, ErrorWord err) {
+    pdl_wait();
     const uint32_t c = blockIdx.x >> 2, bt = blockIdx.y;
     const uint32_t r = (blockIdx.x & 3u) * 16u + (threadIdx.x >> 3), q8 = threadIdx.x & 7u;
     const uint32_t b = bt * kUN + r, k0 = c * kUK + q8 * 8u;
@@ -503,6 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const uint8_t *__restrict__ xtiles,
                  uint32_t nchunks_x, float *__restrict__ y, uint32_t ldy, uint32_t batch,
                  uint32_t kchunks_per_split, ErrorWord err) {
+    pdl_wait();
     constexpr uint32_t SC = TypeCfg<T>::sc, kRawBytes = Ring<T>::raw, kX = Ring<T>::xdepth;
     constexpr uint32_t kIssuers = 1u;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -902,13 +904,15 @@ static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &s
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = Ring<T>::smem;
     cfg.stream = stream;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 1;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = splits;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see launch_pdl
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     cudaLaunchKernelEx(&cfg, proj_umma_kernel<T>, maps, segs, xt, nchunks_x, y, ldy, batch, per, err);
     return true;
 }
@@ -953,7 +957,7 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
     }
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
     const dim3 xg(nchunks * 4, (batch + kUN - 1) / kUN);
-    xconv_kernel<<<xg, 128, 0, stream>>>(x, ldx, batch, cols, nchunks, xtiles, err);
+    launch_pdl(xconv_kernel, xg, 128, 0, stream, x, ldx, batch, cols, nchunks, xtiles, err);
     count_launch();
     // one launch per weight type present
     bool done[kMaxSegments] = {};
