@@ -114,9 +114,17 @@ def algorithmic_bytes(gdn, qsa, ctx, batch):
 
 
 def recurrence_bytes_per_launch(batch):
+    """Algorithmic HBM bytes of one launch of the fused decode kernel
+    (conv / gates + delta-rule recurrence + gated RMSNorm) for `batch`
+    sequences: the recurrent state read and written, the conv state read and
+    written, the projected row read (q | k | v | gate | beta | alpha) and the
+    gated output written, each once."""
     gd, _ = dims()
-    per_head = gd.key_dim * gd.value_dim * 4 * 2 + 5 * gd.value_dim * 4
-    return batch * gd.value_heads * per_head
+    state = gd.value_heads * gd.key_dim * gd.value_dim * 4 * 2
+    conv = gd.conv_channels * gd.conv_kernel * 4 * 2
+    proj_row = (gd.conv_channels + gd.value_width + 2 * gd.value_heads) * 4
+    out = gd.value_width * 4
+    return batch * (state + conv + proj_row + out)
 
 
 class ClockSampler:
@@ -424,7 +432,7 @@ def run_b200(args, rank, world, local_rank):
             "step_hbm_frac": step_bytes / (ms * 1e-3) / 1e9 / hbm,
         },
         "roofline": {
-            "kernel": "gdn_recurrence128 (B=64, one GDN layer)",
+            "kernel": "gdn_decode_fused (conv/gates + recurrence + gated norm; B=64, one GDN layer)",
             "bound": "hbm",
             "achieved": achieved,
             "peak": hbm,

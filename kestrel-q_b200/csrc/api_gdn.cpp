@@ -205,6 +205,9 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
             if (!launch_projection(in, xin, H, proj, ldp, n_items, err, c->stream, partial, partial_floats) &&
                 check_input)
                 launch_check_finite(xin, (uint64_t)n_items * H, err, c->stream);
+            if (tc == 1 && gdn_decode_fused_supported(gd)) {
+                launch_gdn_decode_fused(gd, w.vec, p, gb, proj, ldp, gated, err, c->stream);
+            } else {
             launch_gdn_conv_gates(gd, w.vec, p, gb, tc, proj, ldp, qk, v, beta, decay, err, c->stream, logdecay);
             if (chunked && tc >= kChunkedMinTokens)
                 launch_gdn_chunked(gd, w.vec, p, tc, qk, v, beta, logdecay, proj, ldp, gated, chunk_work, err,
@@ -212,6 +215,7 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
             else
                 launch_gdn_recurrence(gd, w.vec, p, gb, tc, qk, v, beta, decay, proj, ldp, gated, err,
                                       c->stream);
+            }
             if (!launch_projection(out, gated, Vd, y + row0 * H, H, n_items, err, c->stream, partial,
                                    partial_floats))
                 launch_check_finite(y + row0 * H, (uint64_t)n_items * H, err, c->stream);

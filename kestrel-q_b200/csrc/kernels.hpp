@@ -150,6 +150,12 @@ void launch_gdn_recurrence(const GdnDims &d, const GdnWeightsDev &w,
                            const float *proj, uint32_t ldp, float *gated,
                            ErrorWord err, cudaStream_t stream);
 
+// Decode (one token per sequence) with the conv / gate stage fused into the
+// recurrence, for dk = dv = 128 and conv kernel 4.
+bool gdn_decode_fused_supported(const GdnDims &d);
+void launch_gdn_decode_fused(const GdnDims &d, const GdnWeightsDev &w, const GdnBatchPtrs &p, uint32_t batch,
+                             const float *proj, uint32_t ldp, float *gated, ErrorWord err, cudaStream_t stream);
+
 // Chunked (WY-form) prefill of one sequence (kernels_gdn_chunk.cu), for
 // dk = dv = 128: same inputs as the recurrence plus the log decays; `work`
 // holds gdn_chunk_workspace_floats(d, tokens) floats.

@@ -285,6 +285,157 @@ gdn_recurrence128_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t to
     if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
 }
 
+// Decode (one token per sequence), dk = dv = 128, conv kernel 4: the conv /
+// gate stage of gdn_conv_gates_kernel fused into the recurrence.  The CTA of
+// (value head h, sequence b) computes q and k of key head h / repeat (both
+// value heads of a key head compute them; the first writes their conv
+// state), v of head h, beta and the decay, then runs the recurrence as
+// gdn_recurrence128_kernel does.  Same arithmetic as the two kernels.
+__global__ void __launch_bounds__(kRecThreads, 2)
+gdn_decode_fused_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, const float *__restrict__ proj,
+                        uint32_t ldp, float *__restrict__ gated, ErrorWord err) {
+    pdl_wait();
+    __shared__ __align__(16) float ks[kDim];
+    __shared__ __align__(16) float qs[kDim];
+    __shared__ __align__(16) float vs[kDim];
+    __shared__ __align__(16) float part[kRecThreads / 32][kDim];
+    __shared__ __align__(16) float delta[kDim];
+    __shared__ float red[kRecThreads / 32];
+    __shared__ float gates[2];   // beta, decay
+    if (gdn_error_raised(err)) return;
+    const uint32_t h = blockIdx.x;
+    const uint32_t b = blockIdx.y;
+    const uint32_t kh = h / d.repeat;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *sin_ = p.rec_in[b] + (size_t)h * kDim * kDim;
+    float *sout = p.rec_out[b] + (size_t)h * kDim * kDim;
+    const float *prow = proj + (size_t)b * ldp;
+    const float *conv_in = p.conv_in[b];
+    float *conv_out = p.conv_out[b];
+    bool bad = false;
+
+    // state loads first: they are independent of the prologue
+    float4 s[kRows];
+#pragma unroll
+    for (int j = 0; j < kRows; ++j)
+        s[j] = *reinterpret_cast<const float4 *>(sin_ + (size_t)(warp + 8 * j) * kDim + 4 * lane);
+
+    // ---- prologue: threads 0..127 q (which 0) / 128..255 k (which 1)
+    {
+        const uint32_t which = threadIdx.x >> 7, i = threadIdx.x & (kDim - 1);
+        const uint32_t c = which * d.key_width + kh * kDim + i;
+        const bool writer = (h % d.repeat) == 0;
+        const float sconv = conv_channel<4>(d, w, conv_in, conv_out, writer, prow, ldp, 0, 0, c);
+        const float val = sconv * stable_sigmoid(sconv);
+        bad |= !isfinite(val);
+        // L2 norm of q and of k: two 128-thread halves
+        float v2 = val * val;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v2 += __shfl_xor_sync(0xffffffffu, v2, o);
+        if (lane == 0) red[warp] = v2;
+        __syncthreads();
+        const float sumsq = red[4 * which] + red[4 * which + 1] + red[4 * which + 2] + red[4 * which + 3];
+        const float inv = 1.0f / sqrtf(sumsq + 1.0e-6f);
+        float out = val * inv;
+        if (which == 0) out = out * (1.0f / sqrtf((float)d.key_dim));
+        (which == 0 ? qs : ks)[i] = out;
+        // v of head h and the gates
+        if (threadIdx.x < kDim) {
+            const uint32_t cv = 2 * d.key_width + h * kDim + threadIdx.x;
+            const float sv = conv_channel<4>(d, w, conv_in, conv_out, true, prow, ldp, 0, 0, cv);
+            const float vv = sv * stable_sigmoid(sv);
+            bad |= !isfinite(vv);
+            vs[threadIdx.x] = vv;
+        }
+        if (threadIdx.x == 0) {
+            const float pb = prow[d.conv_channels + d.value_width + h];
+            const float pa = prow[d.conv_channels + d.value_width + d.value_heads + h];
+            const float bt = stable_sigmoid(pb);
+            const float a = pa + w.dt_bias[h];
+            const float sp = a > 20.0f ? a : log1pf(expf(a));
+            const float g = -expf(w.a_log[h]) * sp;
+            if (!isfinite(g) || g > 0.0f || !isfinite(bt)) gdn_raise(err, kErrDecay);
+            gates[0] = bt;
+            gates[1] = expf(g);
+        }
+        __syncthreads();
+    }
+    // ---- recurrence (one token)
+    {
+        const float dec = gates[1];
+        const float bt = gates[0];
+        float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) {
+            s[j].x *= dec; s[j].y *= dec; s[j].z *= dec; s[j].w *= dec;
+            float kv = ks[warp + 8 * j];
+            r0 = fmaf(s[j].x, kv, r0);
+            r1 = fmaf(s[j].y, kv, r1);
+            r2 = fmaf(s[j].z, kv, r2);
+            r3 = fmaf(s[j].w, kv, r3);
+        }
+        *reinterpret_cast<float4 *>(&part[warp][4 * lane]) = make_float4(r0, r1, r2, r3);
+        __syncthreads();
+        if (threadIdx.x < kDim) {
+            float rd = 0.f;
+#pragma unroll
+            for (int wv = 0; wv < kRecThreads / 32; ++wv) rd += part[wv][threadIdx.x];
+            delta[threadIdx.x] = (vs[threadIdx.x] - rd) * bt;
+        }
+        __syncthreads();
+        const float4 dl = *reinterpret_cast<const float4 *>(&delta[4 * lane]);
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) {
+            float kv = ks[warp + 8 * j];
+            float qv = qs[warp + 8 * j];
+            s[j].x = fmaf(kv, dl.x, s[j].x);
+            s[j].y = fmaf(kv, dl.y, s[j].y);
+            s[j].z = fmaf(kv, dl.z, s[j].z);
+            s[j].w = fmaf(kv, dl.w, s[j].w);
+            o0 = fmaf(s[j].x, qv, o0);
+            o1 = fmaf(s[j].y, qv, o1);
+            o2 = fmaf(s[j].z, qv, o2);
+            o3 = fmaf(s[j].w, qv, o3);
+        }
+        *reinterpret_cast<float4 *>(&part[warp][4 * lane]) = make_float4(o0, o1, o2, o3);
+        __syncthreads();
+        float o = 0.f;
+        if (threadIdx.x < kDim) {
+#pragma unroll
+            for (int wv = 0; wv < kRecThreads / 32; ++wv) o += part[wv][threadIdx.x];
+            bad |= !isfinite(o);
+        }
+        float sumsq = block_sum<kRecThreads>(threadIdx.x < kDim ? o * o : 0.f, red);
+        if (threadIdx.x < kDim) {
+            float mean = sumsq / (float)kDim;
+            float inv = 1.0f / sqrtf(mean + d.eps);
+            float z = prow[d.conv_channels + h * kDim + threadIdx.x];
+            float g = (w.norm[threadIdx.x] * (o * inv)) * stable_sigmoid(z);
+            bad |= !isfinite(g);
+            gated[(size_t)b * d.value_width + h * kDim + threadIdx.x] = g;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) {
+        bad |= !isfinite(s[j].x) || !isfinite(s[j].y) || !isfinite(s[j].z) || !isfinite(s[j].w);
+        *reinterpret_cast<float4 *>(sout + (size_t)(warp + 8 * j) * kDim + 4 * lane) = s[j];
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
+}
+
+bool gdn_decode_fused_supported(const GdnDims &d) {
+    return d.key_dim == kDim && d.value_dim == kDim && d.kernel == 4;
+}
+
+void launch_gdn_decode_fused(const GdnDims &d, const GdnWeightsDev &w, const GdnBatchPtrs &p, uint32_t batch,
+                             const float *proj, uint32_t ldp, float *gated, ErrorWord err, cudaStream_t stream) {
+    KernelTimer timer("gdn_recurrence", stream);
+    launch_pdl(gdn_decode_fused_kernel, dim3(d.value_heads, batch), kRecThreads, 0, stream, d, w, p, proj, ldp,
+               gated, err);
+    count_launch();
+}
+
 // Generic dims (any dk, dv <= 1024): one thread per value feature f, state
 // streamed through global memory (rec_out doubles as the working copy).
 __global__ void __launch_bounds__(128)
