@@ -14,6 +14,12 @@ with the distributions BASELINE.json names.  The per-step working set
 (≈1.6 GB of state, KV and weights) is larger than the 126 MB L2, so no L2
 flush is needed between steps.
 
+`--workload prefill` runs BASELINE config 4 instead: one 131072-token
+prefill of the same block (all projections Q4_K, index BF16) with the layers
+tensor-parallel over the ranks (GDN by value-head group, QSA by query-head
+group, indexer replicated) and one NCCL all-reduce of the partial outputs
+after every layer's out-projection (strong scaling).
+
 Arms:
   default          the B200 library through its C-ABI (kestrel-q_b200)
   --impl reference the reference's own CPU operators (oracle/_ref, compiled
@@ -54,6 +60,14 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def tensor_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops_sustained"]), "measured (bf16, sustained)"
+    return 1400.0, "fallback (bf16, sustained)"
+
+
 def dims():
     from kqb200 import synth
     return synth.GdnDims(), synth.QsaDims()
@@ -72,6 +86,62 @@ def layer_weights():
            for l in range(GDN_LAYERS)]
     qsa = synth.qsa_layer(7, qd, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_BF16)
     return gdn, qsa
+
+
+PREFILL_TOKENS = 131072
+PREFILL_SLICE = 16384
+
+
+def prefill_weights():
+    """Config 4: the block with every projection Q4_K (index projections BF16)."""
+    from kqb200 import synth
+    gd, qd = dims()
+    gdn = [synth.gdn_layer(20 + l, gd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_Q4_K)
+           for l in range(GDN_LAYERS)]
+    qsa = synth.qsa_layer(27, qd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_BF16)
+    return gdn, qsa
+
+
+def wy_flops_per_chunk_head(C: int = 64, d: int = 128) -> int:
+    """FLOPs of the chunked WY form for one head and one chunk of C tokens
+    (dk = dv = d): K K^T and Q K^T (2 C^2 d each), the two triangular solves
+    for W and U (C^2 d each), the causal P delta (C^2 d), and W S, Q S,
+    K^T delta against the d x d state (2 C d^2 each)."""
+    return 7 * C * C * d + 6 * C * d * d
+
+
+def prefill_flops(T: int):
+    """Algorithmic FLOPs of one T-token prefill of the whole block (all
+    ranks together), by part."""
+    gd, qd = dims()
+    H, C, Vd, Hv = gd.hidden, gd.conv_channels, gd.value_width, gd.value_heads
+    gdn_proj = GDN_LAYERS * (2 * T * H * (C + Vd + 2 * Hv) + 2 * T * Vd * H)
+    chunks = (T + 63) // 64
+    wy = GDN_LAYERS * Hv * chunks * wy_flops_per_chunk_head(64, gd.key_dim)
+    qw, kvw = qd.q_width, qd.kv_width
+    iw = qd.index_heads * qd.index_dim + qd.index_dim
+    qsa_proj = 2 * T * H * (2 * qw + 2 * kvw) + 2 * T * qw * H + 2 * T * H * iw
+    pos = np.arange(T, dtype=np.int64)
+    nb = (pos + 1) // qd.block
+    ntok = np.minimum(nb, qd.budget // qd.block) * qd.block + (pos + 1) % qd.block
+    indexer = int(2 * qd.index_heads * qd.index_dim * nb.sum())
+    attention = int(4 * qd.query_heads * qd.head_dim * ntok.sum())
+    parts = {"gdn_proj": gdn_proj, "gdn_wy": wy, "qsa_proj": qsa_proj, "qsa_indexer": indexer,
+             "qsa_attention": attention}
+    return sum(parts.values()), parts
+
+
+def rank_tensor_core_flops(block, T: int) -> int:
+    """FLOPs of the projections this rank runs on the tensor cores (all but
+    the index projections, which take the exact CUDA-core path)."""
+    f = 0
+    for L in block.gdn_layers:
+        d = L.dims
+        f += 2 * T * d.hidden * (d.conv_channels + 2 * d.value_width + 2 * d.value_heads)
+    for L in block.qsa_layers:
+        d = L.dims
+        f += 2 * T * d.hidden * (3 * d.q_width + 2 * d.kv_width)
+    return f
 
 
 def max_over_ranks(values, world: int, device):
@@ -225,6 +295,33 @@ def cpu_block_sample(n_seqs: int, threads: int, rank: int = 0):
     return n_seqs / elapsed, impl, elapsed
 
 
+def cpu_prefill_sample(tokens: int):
+    """The reference's own F32 operators (oracle/_ref when built, else the
+    restatement) prefilling the first `tokens` tokens of the config-4 block
+    from empty states, one thread (the reference prefill of one sequence is
+    sequential).  Returns (tokens_per_second, kind, seconds)."""
+    from oracle import oracle as O
+    impl = "reference" if O.ref_available() else "port"
+    gd, qd = dims()
+    gdn, qsa = prefill_weights()
+    gw = [O.gdn_weights_f32(L) for L in gdn]
+    qw = O.qsa_weights_f32(qsa)
+    x = np.random.default_rng(99).normal(size=(tokens, gd.hidden)).astype(np.float32)
+    conv = np.zeros(gd.conv_channels * gd.conv_kernel, np.float32)
+    rec = np.zeros(gd.value_heads * gd.key_dim * gd.value_dim, np.float32)
+    z = np.zeros((tokens, qd.kv_width), np.float32)
+    zr = np.zeros((tokens, qd.index_dim), np.float32)
+    t0 = time.perf_counter()
+    h = x
+    for l in range(GDN_LAYERS):
+        st, h, _, _ = O.gdn_run(gd, gw[l], h, conv, rec, impl=impl)
+        assert st == 0
+    st, h, *_ = O.qsa_run(qd, qw, h, z, z, zr, 0, tokens, impl=impl)
+    assert st == 0
+    elapsed = time.perf_counter() - t0
+    return tokens / elapsed, impl, elapsed
+
+
 def cpu_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -232,9 +329,41 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
+def run_reference_prefill(args, rank, world):
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+    if not O.PORT_LIB.exists():
+        O.build()
+    n = args.cpu_tokens
+    cpu_prefill_sample(2)
+    vals, kind = [], "reference"
+    t_all = time.perf_counter()
+    for _ in range(args.steps):
+        v, impl, _ = cpu_prefill_sample(n)
+        kind = "reference" if impl == "reference" else "port"
+        vals.append(v)
+    elapsed = time.perf_counter() - t_all
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / max(1, args.steps),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config4: 4-layer GDN+QSA block prefill, batch 1, Q4_K",
+                   "sample": f"first {n} tokens of the prefill per step"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": 1, "kind": kind,
+                         "sample": f"first {n} tokens of the 4-layer block prefill from empty states, 1 thread"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
+    if args.workload == "prefill":
+        return run_reference_prefill(args, rank, world)
     threads = min(cpu_threads(), 16)
     n = threads
     from oracle import oracle as O
@@ -475,6 +604,174 @@ def run_b200(args, rank, world, local_rank):
     return 0
 
 
+def run_b200_prefill(args, rank, world, local_rank):
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    import kqb200
+    from kqb200 import tp
+
+    torch.cuda.set_device(local_rank)
+    d = kqb200.abi.Diagnostic()
+    kqb200.abi.check(kqb200.lib().kq_b200_set_device(local_rank, C.byref(d)), d)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    gd, qd = dims()
+    T = args.tokens
+    gdn_w, qsa_w = prefill_weights()
+    prov = kqb200.Provider(local_rank)
+    block = tp.TensorParallelBlock(kqb200, prov, gdn_w, [qsa_w], rank, world, capacity=T)
+    lib = kqb200.lib()
+    stream = torch.cuda.ExternalStream(lib.kq_b200_get_stream())
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4321)   # the same input on every rank (replicated activations)
+    x = torch.randn(T, gd.hidden, device="cuda", generator=gen)
+    bufs = [torch.empty(T, gd.hidden, device="cuda") for _ in range(block.layer_count)]
+    torch.cuda.synchronize()
+
+    def all_reduce(t):
+        return dist.all_reduce(t, async_op=True)
+
+    reduce = all_reduce if world > 1 else None
+
+    def step(inp):
+        block.reset()
+        block.prefill(inp, bufs, T, reduce, slice_tokens=args.slice_tokens)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step(x)
+    kqb200.synchronize()
+    torch.cuda.synchronize()
+
+    lib.kq_b200_profile_kernel(b"proj")
+    launches0 = lib.kq_b200_kernel_launch_count()
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                step(x)
+            e1.record(stream)
+        kqb200.synchronize()
+        torch.cuda.synchronize()
+        barrier()
+    launches = lib.kq_b200_kernel_launch_count() - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    proj_n, proj_ms = C.c_uint64(), C.c_double()
+    lib.kq_b200_profile_read(C.byref(proj_n), C.byref(proj_ms))
+    lib.kq_b200_profile_kernel(None)
+
+    breakdown = {}
+    if args.breakdown:
+        for fam in ("proj", "proj_exact", "gdn_conv", "gdn_recurrence", "qsa_prepare", "qsa_block_keys",
+                    "qsa_score", "qsa_select", "qsa_attend", "qsa_combine"):
+            lib.kq_b200_profile_kernel(fam.encode())
+            with torch.cuda.stream(stream):
+                step(x)
+            kqb200.synchronize()
+            torch.cuda.synchronize()
+            n_, t_ = C.c_uint64(), C.c_double()
+            lib.kq_b200_profile_read(C.byref(n_), C.byref(t_))
+            breakdown[fam] = {"ms_per_step": t_.value, "launches_per_step": n_.value}
+        lib.kq_b200_profile_kernel(None)
+
+    # ---- end-to-end: pinned host input -> block -> host output, every step
+    xh = torch.randn(T, gd.hidden, generator=torch.Generator().manual_seed(6)).pin_memory()
+    yh = torch.empty(T, gd.hidden).pin_memory()
+    xin = torch.empty_like(x)
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        for _ in range(args.steps):
+            xin.copy_(xh, non_blocking=True)
+            step(xin)
+            yh.copy_(bufs[-1], non_blocking=True)
+        f1.record(stream)
+    kqb200.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = f0.elapsed_time(f1) / args.steps
+    assert torch.isfinite(yh).all(), "non-finite block output"
+
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world, torch.device("cuda", local_rank))
+    total_flops, parts = prefill_flops(T)
+    tc_flops = rank_tensor_core_flops(block, T)
+    proj_step_ms = proj_ms.value / max(1, args.steps)
+    achieved = tc_flops / (proj_step_ms * 1e-3) / 1e12
+    peak, peak_kind = tensor_peak()
+    line = {
+        "metric": METRIC,
+        "value": T * 1000.0 / ms,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {
+            "workload": f"config4: 4-layer block (3 GDN + 1 QSA) prefill of {T} tokens, batch 1, "
+                        f"projections Q4_K, index BF16, F32 activations/state/KV",
+            "parallelism": f"tensor-parallel x{world}: GDN by value-head group, QSA by query-head group "
+                           f"(indexer replicated), NCCL all-reduce (f32) after each out-projection",
+            "slice_tokens": args.slice_tokens,
+            "l2": "working set per step (GBs of activations, KV, projections) >> 126 MB L2",
+            "step_algorithmic_flops": total_flops,
+            "step_flops_breakdown": parts,
+            "step_tflops": total_flops / (ms * 1e-3) / 1e12,
+        },
+        "roofline": {
+            "kernel": "proj (xconv + proj_umma: tcgen05 projection GEMMs of this rank's shards)",
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "TFLOP/s",
+            "frac": achieved / peak,
+            "traffic": None,
+            "algorithmic_flops_per_step": tc_flops,
+            "ms_per_step": proj_step_ms,
+            "launches_timed": proj_n.value,
+            "note": "F32 operands as bf16 hi/lo pairs: three MMAs per algorithmic product",
+        },
+        "e2e": {"value": T * 1000.0 / e2e_ms, "unit": "tok/s",
+                "h2d_bytes_per_step": T * gd.hidden * 4, "d2h_bytes_per_step": T * gd.hidden * 4},
+        "gpu_launches": int(launches),
+        **({"kernel_breakdown": breakdown} if breakdown else {}),
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, impl, secs = cpu_prefill_sample(args.cpu_tokens)
+        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": 1,
+                                "kind": "reference" if impl == "reference" else "port",
+                                "sample": f"first {args.cpu_tokens} tokens of the block prefill from empty "
+                                          f"states, 1 thread ({secs:.1f} s wall)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    block.close()
+    prov.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -485,12 +782,20 @@ def main():
     ap.add_argument("--breakdown", action="store_true", help="time every kernel family (extra steps)")
     ap.add_argument("--ctx-max", type=int, default=CTX_RANGE[1],
                     help="upper end of the context distribution (profiling runs use a small one)")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode: config 3 (default); prefill: config 4, tensor-parallel")
+    ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS, help="prefill length (config 4)")
+    ap.add_argument("--slice-tokens", type=int, default=PREFILL_SLICE,
+                    help="prefill tokens per layer call (all-reduce granularity)")
+    ap.add_argument("--cpu-tokens", type=int, default=16, help="prefill tokens of the CPU baseline sample")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload == "prefill":
+        return run_b200_prefill(args, rank, world, local_rank)
     return run_b200(args, rank, world, local_rank)
 
 

@@ -245,6 +245,27 @@ kq_status kq_b200_qsa_decode_batch(const kq_qsa_config *config,
                                    float *output,
                                    kq_diagnostic *diagnostic);
 
+/* T tokens of one sequence, like kq_gdn_execute_quantized /
+ * kq_qsa_execute_quantized (src/kq_gdn_internal.h:81-96,
+ * src/kq_qsa_internal.h:94-102) without a mask or observers, on device
+ * arrays [T][hidden_size] and asynchronous on the library stream (errors and
+ * the state roll-back as for the batched decode).  A tensor-parallel host
+ * binds one config per head group (a GDN config over its value/key heads, a
+ * QSA config over its query heads and their key/value head) and sums the
+ * groups' outputs, which are partial sums of the output projection. */
+kq_status kq_b200_gdn_prefill_async(const kq_gdn_config *config,
+                                    kq_gdn_state *state,
+                                    const float *hidden,
+                                    uint64_t T,
+                                    float *output,
+                                    kq_diagnostic *diagnostic);
+kq_status kq_b200_qsa_prefill_async(const kq_qsa_config *config,
+                                    kq_qsa_state *state,
+                                    const float *hidden,
+                                    uint64_t T,
+                                    float *output,
+                                    kq_diagnostic *diagnostic);
+
 /* Waits for the library stream and reports the first device-side error
  * raised since the previous synchronize. */
 kq_status kq_b200_synchronize(kq_diagnostic *diagnostic);

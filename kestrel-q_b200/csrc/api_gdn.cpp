@@ -208,13 +208,14 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
             if (tc == 1 && gdn_decode_fused_supported(gd)) {
                 launch_gdn_decode_fused(gd, w.vec, p, gb, proj, ldp, gated, err, c->stream);
             } else {
-            launch_gdn_conv_gates(gd, w.vec, p, gb, tc, proj, ldp, qk, v, beta, decay, err, c->stream, logdecay);
-            if (chunked && tc >= kChunkedMinTokens)
-                launch_gdn_chunked(gd, w.vec, p, tc, qk, v, beta, logdecay, proj, ldp, gated, chunk_work, err,
-                                   c->stream);
-            else
-                launch_gdn_recurrence(gd, w.vec, p, gb, tc, qk, v, beta, decay, proj, ldp, gated, err,
-                                      c->stream);
+                launch_gdn_conv_gates(gd, w.vec, p, gb, tc, proj, ldp, qk, v, beta, decay, err, c->stream,
+                                      logdecay);
+                if (chunked && tc >= kChunkedMinTokens)
+                    launch_gdn_chunked(gd, w.vec, p, tc, qk, v, beta, logdecay, proj, ldp, gated, chunk_work, err,
+                                       c->stream);
+                else
+                    launch_gdn_recurrence(gd, w.vec, p, gb, tc, qk, v, beta, decay, proj, ldp, gated, err,
+                                          c->stream);
             }
             if (!launch_projection(out, gated, Vd, y + row0 * H, H, n_items, err, c->stream, partial,
                                    partial_floats))
@@ -511,7 +512,8 @@ kq_status kq_gdn_state_create(const kq_gdn_config *config, kq_gdn_state **out_st
     const size_t cb = config->conv_state_elements * 4, rb = config->recurrent_elements * 4;
     for (int i = 0; i < 2; ++i) {
         if (cudaMalloc(&s->conv[i], cb) != cudaSuccess || cudaMalloc(&s->rec[i], rb) != cudaSuccess ||
-            cudaMemset(s->conv[i], 0, cb) != cudaSuccess || cudaMemset(s->rec[i], 0, rb) != cudaSuccess) {
+            cudaMemsetAsync(s->conv[i], 0, cb, c->stream) != cudaSuccess ||
+            cudaMemsetAsync(s->rec[i], 0, rb, c->stream) != cudaSuccess) {
             cudaGetLastError();
             for (int j = 0; j < 2; ++j) { cudaFree(s->conv[j]); cudaFree(s->rec[j]); }
             delete s;
@@ -546,8 +548,11 @@ kq_status kq_gdn_state_reset(kq_gdn_state *state, kq_diagnostic *diagnostic) {
     if (st != KQ_STATUS_OK) return st;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     c->synchronize(nullptr);
-    KQB_CUDA(cudaMemset(state->conv[state->cur], 0, state->config->conv_state_elements * 4), diagnostic, "reset");
-    KQB_CUDA(cudaMemset(state->rec[state->cur], 0, state->config->recurrent_elements * 4), diagnostic, "reset");
+    // on the library stream, so that later work on it sees the zeroed state
+    KQB_CUDA(cudaMemsetAsync(state->conv[state->cur], 0, state->config->conv_state_elements * 4, c->stream),
+             diagnostic, "reset");
+    KQB_CUDA(cudaMemsetAsync(state->rec[state->cur], 0, state->config->recurrent_elements * 4, c->stream),
+             diagnostic, "reset");
     state->initialized = 0;
     state->on_success();
     return KQ_STATUS_OK;
@@ -583,10 +588,10 @@ kq_status kq_gdn_state_export_f32(const kq_gdn_state *state, float *conv_state, 
     if (st != KQ_STATUS_OK) return st;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     c->synchronize(nullptr);
-    KQB_CUDA(cudaMemcpy(conv_state, state->conv[state->cur], cfg->conv_state_elements * 4, cudaMemcpyDefault),
-             diagnostic, "conv export");
-    KQB_CUDA(cudaMemcpy(recurrent_state, state->rec[state->cur], cfg->recurrent_elements * 4, cudaMemcpyDefault),
-             diagnostic, "recurrent export");
+    KQB_CUDA(copy_sync(conv_state, state->conv[state->cur], cfg->conv_state_elements * 4, cudaMemcpyDefault,
+                       c->stream), diagnostic, "conv export");
+    KQB_CUDA(copy_sync(recurrent_state, state->rec[state->cur], cfg->recurrent_elements * 4, cudaMemcpyDefault,
+                       c->stream), diagnostic, "recurrent export");
     *initialized = state->initialized;
     return KQ_STATUS_OK;
 }
@@ -614,10 +619,13 @@ kq_status kq_gdn_state_import_f32(kq_gdn_state *state, const float *conv_state, 
         launch_check_finite(recurrent_state, recurrent_count, err, c->stream);
         if (c->synchronize(nullptr) != KQ_STATUS_OK)
             return fail(diagnostic, KQ_STATUS_NUMERIC_DOMAIN, "GDN imported state must be finite");
-        KQB_CUDA(cudaMemcpy(state->conv[state->cur], conv_state, conv_count * 4, cudaMemcpyDeviceToDevice),
-                 diagnostic, "conv import");
-        KQB_CUDA(cudaMemcpy(state->rec[state->cur], recurrent_state, recurrent_count * 4, cudaMemcpyDeviceToDevice),
-                 diagnostic, "rec import");
+        // ordered on the library stream, and complete before the caller's
+        // buffers may be reused
+        KQB_CUDA(cudaMemcpyAsync(state->conv[state->cur], conv_state, conv_count * 4, cudaMemcpyDeviceToDevice,
+                                 c->stream), diagnostic, "conv import");
+        KQB_CUDA(cudaMemcpyAsync(state->rec[state->cur], recurrent_state, recurrent_count * 4,
+                                 cudaMemcpyDeviceToDevice, c->stream), diagnostic, "rec import");
+        KQB_CUDA(cudaStreamSynchronize(c->stream), diagnostic, "import");
         state->initialized = 1;
         state->on_success();
         return KQ_STATUS_OK;
@@ -642,8 +650,10 @@ kq_status kq_gdn_state_import_f32(kq_gdn_state *state, const float *conv_state, 
     if (st != KQ_STATUS_OK) return st;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     c->synchronize(nullptr);
-    KQB_CUDA(cudaMemcpy(state->conv[state->cur], conv_h.data(), conv_count * 4, cudaMemcpyHostToDevice), diagnostic, "conv import");
-    KQB_CUDA(cudaMemcpy(state->rec[state->cur], rec_h.data(), recurrent_count * 4, cudaMemcpyHostToDevice), diagnostic, "rec import");
+    KQB_CUDA(copy_sync(state->conv[state->cur], conv_h.data(), conv_count * 4, cudaMemcpyHostToDevice, c->stream),
+             diagnostic, "conv import");
+    KQB_CUDA(copy_sync(state->rec[state->cur], rec_h.data(), recurrent_count * 4, cudaMemcpyHostToDevice,
+                       c->stream), diagnostic, "rec import");
     state->initialized = initialized;
     state->on_success();
     return KQ_STATUS_OK;
@@ -728,6 +738,31 @@ kq_status kq_b200_gdn_decode_batch(const kq_gdn_config *config, kq_gdn_state *co
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     ErrorWord err = c->begin_call();
     return gdn_enqueue(c, config, w, states, batch, 1, hidden, nullptr, output, err, diagnostic,
+                       /*check_input=*/true);
+}
+
+kq_status kq_b200_gdn_prefill_async(const kq_gdn_config *config, kq_gdn_state *state, const float *hidden,
+                                    uint64_t T, float *output, kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (!config_valid(config) || !state_valid(state) || state->config != config || hidden == nullptr ||
+        output == nullptr || T == 0)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid config, state and device buffers are required");
+    if (T > UINT32_MAX || T * config->dims.hidden_size > SIZE_MAX / 4)
+        return fail(diagnostic, KQ_STATUS_ARITHMETIC_OVERFLOW, "GDN sequence element count is invalid or overflows");
+    if (config->dims.activation_dtype != KQ_GDN_ACTIVATION_F32)
+        return fail(diagnostic, KQ_STATUS_INCOMPATIBLE_GDN, "device prefill requires an F32 configuration");
+    if (!is_device_pointer(hidden) || !is_device_pointer(output))
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "device prefill takes device buffers");
+    GdnResolved w;
+    if (!resolve_bound(config, &w))
+        return fail(diagnostic, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "config has no bound provider weights");
+    DeviceContext *c;
+    kq_status st = context(&c, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    ErrorWord err = c->begin_call();
+    kq_gdn_state *states[1] = {state};
+    return gdn_enqueue(c, config, w, states, 1, (uint32_t)T, hidden, nullptr, output, err, diagnostic,
                        /*check_input=*/true);
 }
 

@@ -129,6 +129,9 @@ kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *
     void *dev = nullptr;
     KQB_CUDA(cudaMalloc(&dev, total), diagnostic, "weight allocation");
     cudaError_t e = cudaMemcpy(dev, src, total, cudaMemcpyHostToDevice);
+    // a pageable upload may return before its DMA lands; the library's
+    // streams do not wait for the legacy stream, so finish it here
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
     if (e != cudaSuccess) {
         cudaFree(dev);
         return cuda_fail(diagnostic, e, "weight upload");
@@ -167,6 +170,7 @@ kq_status kq_b200_provider_add_vector_f32(kq_weight_provider *provider, const ch
     void *dev = nullptr;
     KQB_CUDA(cudaMalloc(&dev, count * sizeof(float)), diagnostic, "vector allocation");
     cudaError_t e = cudaMemcpy(dev, values, count * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
     if (e != cudaSuccess) {
         cudaFree(dev);
         return cuda_fail(diagnostic, e, "vector upload");

@@ -194,23 +194,28 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     const uint32_t ldp = 2 * qw + 2 * kvw;
     const uint32_t ldi = d.index_heads * d.index_dim + d.index_dim;
     const size_t items = (size_t)batch * tokens;
+    // A prefill of one sequence without a selection observer runs up to
+    // kMaxBatch tokens per launch sequence, as batch entries over the same
+    // cache (entry i at position L + t0 + i).
+    const bool chunked = batch == 1 && tokens > 1 && selection == nullptr;
+    const uint32_t entries = chunked ? std::min<uint32_t>(tokens, kMaxBatch) : batch;
     uint32_t max_blocks = 1;
     for (uint32_t b = 0; b < batch; ++b)
         max_blocks = std::max<uint32_t>(max_blocks, (uint32_t)((states[b]->length + tokens) / d.block));
     // about 16 tiles of 16 selected tokens per split, and at least two waves
     // of CTAs over the 148 SMs for small batches
     const uint32_t tiles = (d.sel_capacity + 15) / 16;
-    const uint32_t per_seq = std::min<uint32_t>(batch, kMaxBatch) * d.kv_heads;
+    const uint32_t per_seq = std::min<uint32_t>(entries, kMaxBatch) * d.kv_heads;
     // (the head-blocked attention kernel takes at most 32 tiles per split)
     uint32_t splits = std::max<uint32_t>((tiles + 15) / 16, (3 * 148 + per_seq - 1) / per_seq);
     splits = std::max<uint32_t>(1, std::min<uint32_t>(splits, tiles));
     const size_t need = Carve::round(items * ldp * 4) + Carve::round(items * ldi * 4) +
-                        Carve::round(items * qw * 4) + Carve::round((size_t)batch * qw * 4) +
-                        Carve::round((size_t)batch * d.index_heads * d.index_dim * 4) +
-                        Carve::round((size_t)batch * max_blocks * 4) +
-                        Carve::round((size_t)batch * d.topk * 4) + Carve::round((size_t)batch * 4) +
-                        Carve::round((size_t)batch * d.q_heads * splits * hd * 4) +
-                        Carve::round((size_t)batch * d.q_heads * splits * 2 * 4) + 8192;
+                        Carve::round(items * qw * 4) + Carve::round((size_t)entries * qw * 4) +
+                        Carve::round((size_t)entries * d.index_heads * d.index_dim * 4) +
+                        Carve::round((size_t)entries * max_blocks * 4) +
+                        Carve::round((size_t)entries * d.topk * 4) + Carve::round((size_t)entries * 4) +
+                        Carve::round((size_t)entries * d.q_heads * splits * hd * 4) +
+                        Carve::round((size_t)entries * d.q_heads * splits * 2 * 4) + 8192;
     const size_t partial_floats = std::max(projection_workspace_floats((uint32_t)items, ldp, H),
                                            projection_workspace_floats((uint32_t)items, H, qw));
     void *ws;
@@ -220,13 +225,13 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     float *proj = cv.take<float>(items * ldp);
     float *iproj = cv.take<float>(items * ldi);
     float *gated = cv.take<float>(items * qw);
-    float *qv = cv.take<float>((size_t)batch * qw);
-    float *iqv = cv.take<float>((size_t)batch * d.index_heads * d.index_dim);
-    float *scores = cv.take<float>((size_t)batch * max_blocks);
-    uint32_t *sel = cv.take<uint32_t>((size_t)batch * d.topk);
-    uint32_t *sel_count = cv.take<uint32_t>(batch);
-    float *part_o = cv.take<float>((size_t)batch * d.q_heads * splits * hd);
-    float *part_ml = cv.take<float>((size_t)batch * d.q_heads * splits * 2);
+    float *qv = cv.take<float>((size_t)entries * qw);
+    float *iqv = cv.take<float>((size_t)entries * d.index_heads * d.index_dim);
+    float *scores = cv.take<float>((size_t)entries * max_blocks);
+    uint32_t *sel = cv.take<uint32_t>((size_t)entries * d.topk);
+    uint32_t *sel_count = cv.take<uint32_t>(entries);
+    float *part_o = cv.take<float>((size_t)entries * d.q_heads * splits * hd);
+    float *part_ml = cv.take<float>((size_t)entries * d.q_heads * splits * 2);
     float *partial = partial_floats ? cv.take<float>(partial_floats) : nullptr;
 
     ProjSegments main{};
@@ -269,7 +274,31 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 launch_qsa_block_keys(d, wd, sq, (uint32_t)s->bk_valid, (uint32_t)complete, err, c->stream);
             }
         }
-        for (uint32_t t = 0; t < tokens; ++t) {
+        if (chunked) {
+            kq_qsa_state *s = states[0];
+            const QsaSeq seq{s->key, s->value, s->raw, s->block_keys, (uint32_t)s->length, (uint32_t)s->capacity};
+            for (uint32_t t0 = 0; t0 < tokens; t0 += kMaxBatch) {
+                const uint32_t n = std::min<uint32_t>(kMaxBatch, tokens - t0);
+                const uint32_t pos0 = (uint32_t)s->length + t0;
+                QsaBatch qb;
+                for (uint32_t i = 0; i < n; ++i) {
+                    qb.s[i] = seq;
+                    qb.s[i].length = pos0 + i;
+                }
+                const uint32_t nb_max = std::max<uint32_t>(1, (pos0 + n) / d.block);
+                const float *pt = proj + (size_t)t0 * ldp;
+                launch_qsa_prepare(d, wd, qb, n, pt, ldp, iproj + (size_t)t0 * ldi, ldi, qv, iqv, false, err,
+                                   c->stream);
+                // keys of the blocks this chunk completes, once all their raw rows are written
+                launch_qsa_block_keys(d, wd, seq, pos0 / d.block, (pos0 + n) / d.block, err, c->stream);
+                launch_qsa_score(d, qb, n, iqv, scores, max_blocks, nb_max, err, c->stream);
+                launch_qsa_select(d, qb, n, scores, max_blocks, sel, sel_count, err, c->stream);
+                launch_qsa_attend(d, qb, n, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);
+                launch_qsa_combine(d, n, part_o, part_ml, splits, pt, ldp, gated + (size_t)t0 * qw, err,
+                                   c->stream);
+            }
+        }
+        for (uint32_t t = 0; !chunked && t < tokens; ++t) {
             QsaBatch qb;
             uint32_t nb_max = 1;
             for (uint32_t b = 0; b < gb; ++b) {
@@ -284,7 +313,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
             }
             const float *pt = proj + (size_t)t * ldp;      // batch==1: token rows; tokens==1: t==0
             const float *it = iproj + (size_t)t * ldi;
-            launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, err, c->stream);
+            launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, true, err, c->stream);
             launch_qsa_score(d, qb, gb, iqv, scores, max_blocks, nb_max, err, c->stream);
             launch_qsa_select(d, qb, gb, scores, max_blocks, sel, sel_count, err, c->stream);
             launch_qsa_attend(d, qb, gb, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);
@@ -638,10 +667,10 @@ kq_status kq_qsa_state_create(const kq_qsa_config *config, uint64_t token_capaci
         delete s;
         return fail(diagnostic, KQ_STATUS_OUT_OF_MEMORY, "could not allocate bounded QSA cache buffers");
     }
-    cudaMemset(s->key, 0, kvb);
-    cudaMemset(s->value, 0, kvb);
-    cudaMemset(s->raw, 0, rb);
-    cudaMemset(s->block_keys, 0, bkb);
+    cudaMemsetAsync(s->key, 0, kvb, c->stream);
+    cudaMemsetAsync(s->value, 0, kvb, c->stream);
+    cudaMemsetAsync(s->raw, 0, rb, c->stream);
+    cudaMemsetAsync(s->block_keys, 0, bkb, c->stream);
     s->magic = kQsaStateMagic;
     s->config = config;
     s->capacity = token_capacity;
@@ -698,9 +727,12 @@ kq_status kq_qsa_state_export_f32(const kq_qsa_state *state, float *key_cache, u
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     c->synchronize(nullptr);
     if (kv_count) {
-        KQB_CUDA(cudaMemcpy(key_cache, state->key, kv_count * 4, cudaMemcpyDefault), diagnostic, "key export");
-        KQB_CUDA(cudaMemcpy(value_cache, state->value, kv_count * 4, cudaMemcpyDefault), diagnostic, "value export");
-        KQB_CUDA(cudaMemcpy(raw_cache, state->raw, raw_count * 4, cudaMemcpyDefault), diagnostic, "raw export");
+        KQB_CUDA(copy_sync(key_cache, state->key, kv_count * 4, cudaMemcpyDefault, c->stream), diagnostic,
+                 "key export");
+        KQB_CUDA(copy_sync(value_cache, state->value, kv_count * 4, cudaMemcpyDefault, c->stream), diagnostic,
+                 "value export");
+        KQB_CUDA(copy_sync(raw_cache, state->raw, raw_count * 4, cudaMemcpyDefault, c->stream), diagnostic,
+                 "raw export");
     }
     *length = state->length;
     return KQ_STATUS_OK;
@@ -731,9 +763,15 @@ kq_status kq_qsa_state_import_f32(kq_qsa_state *state, const float *key_cache, u
         launch_check_finite(raw_cache, eraw, err, c->stream);
         if (c->synchronize(nullptr) != KQ_STATUS_OK)
             return fail(diagnostic, KQ_STATUS_NUMERIC_DOMAIN, "QSA imported K/V state must be finite");
-        KQB_CUDA(cudaMemcpy(state->key, key_cache, ekv * 4, cudaMemcpyDeviceToDevice), diagnostic, "import");
-        KQB_CUDA(cudaMemcpy(state->value, value_cache, ekv * 4, cudaMemcpyDeviceToDevice), diagnostic, "import");
-        KQB_CUDA(cudaMemcpy(state->raw, raw_cache, eraw * 4, cudaMemcpyDeviceToDevice), diagnostic, "import");
+        // ordered on the library stream, and complete before the caller's
+        // buffers may be reused
+        KQB_CUDA(cudaMemcpyAsync(state->key, key_cache, ekv * 4, cudaMemcpyDeviceToDevice, c->stream), diagnostic,
+                 "import");
+        KQB_CUDA(cudaMemcpyAsync(state->value, value_cache, ekv * 4, cudaMemcpyDeviceToDevice, c->stream),
+                 diagnostic, "import");
+        KQB_CUDA(cudaMemcpyAsync(state->raw, raw_cache, eraw * 4, cudaMemcpyDeviceToDevice, c->stream), diagnostic,
+                 "import");
+        KQB_CUDA(cudaStreamSynchronize(c->stream), diagnostic, "import");
         state->bk_valid = 0;
         state->length = length;
         state->on_success();
@@ -768,9 +806,11 @@ kq_status kq_qsa_state_import_f32(kq_qsa_state *state, const float *key_cache, u
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     c->synchronize(nullptr);
     if (ekv) {
-        KQB_CUDA(cudaMemcpy(state->key, kh.data(), ekv * 4, cudaMemcpyHostToDevice), diagnostic, "import");
-        KQB_CUDA(cudaMemcpy(state->value, vh.data(), ekv * 4, cudaMemcpyHostToDevice), diagnostic, "import");
-        KQB_CUDA(cudaMemcpy(state->raw, rh.data(), eraw * 4, cudaMemcpyHostToDevice), diagnostic, "import");
+        KQB_CUDA(copy_sync(state->key, kh.data(), ekv * 4, cudaMemcpyHostToDevice, c->stream), diagnostic, "import");
+        KQB_CUDA(copy_sync(state->value, vh.data(), ekv * 4, cudaMemcpyHostToDevice, c->stream), diagnostic,
+                 "import");
+        KQB_CUDA(copy_sync(state->raw, rh.data(), eraw * 4, cudaMemcpyHostToDevice, c->stream), diagnostic,
+                 "import");
     }
     // cached block keys are rebuilt from the imported raw keys by the next
     // call, which knows the index-key norm weights
@@ -889,6 +929,33 @@ kq_status kq_b200_qsa_decode_batch(const kq_qsa_config *config, kq_qsa_state *co
                   config->q_norm, config->k_norm, config->iq_norm, config->ik_norm};
     ErrorWord err = c->begin_call();
     return qsa_enqueue(c, config, w, states, batch, 1, hidden, output, err, nullptr, diagnostic,
+                       /*check_input=*/true);
+}
+
+kq_status kq_b200_qsa_prefill_async(const kq_qsa_config *config, kq_qsa_state *state, const float *hidden,
+                                    uint64_t T, float *output, kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (!config_valid(config) || !state_valid(state) || state->config != config || hidden == nullptr ||
+        output == nullptr || T == 0)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid config, state and device buffers are required");
+    if (config->dims.activation_dtype != KQ_QSA_ACTIVATION_F32)
+        return fail(diagnostic, KQ_STATUS_INCOMPATIBLE_QSA, "device prefill requires an F32 configuration");
+    if (!config->bound)
+        return fail(diagnostic, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "config has no bound provider weights");
+    uint64_t total;
+    if (!add_ok(state->length, T, &total) || total > state->capacity || T > UINT32_MAX)
+        return fail(diagnostic, KQ_STATUS_LIMIT_EXCEEDED, "QSA sequence exceeds bounded state capacity");
+    if (!is_device_pointer(hidden) || !is_device_pointer(output))
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "device prefill takes device buffers");
+    DeviceContext *c;
+    kq_status st = context(&c, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    QsaResolved w{config->q, config->k, config->v, config->o, config->iq, config->ik,
+                  config->q_norm, config->k_norm, config->iq_norm, config->ik_norm};
+    ErrorWord err = c->begin_call();
+    kq_qsa_state *states[1] = {state};
+    return qsa_enqueue(c, config, w, states, 1, (uint32_t)T, hidden, output, err, nullptr, diagnostic,
                        /*check_input=*/true);
 }
 

@@ -197,11 +197,15 @@ struct QsaWeightsDev {
 
 // proj: [B][2*Hq*d + 2*Hkv*d] (q/gate interleaved | k | v);
 // iproj: [B][Hi*di + di] (index query | raw index key), exact order.
+// `inline_block_key`: an entry whose token completes a block also caches
+// that block's key.  Entries that share one cache (a prefill chunk) pass
+// false and run launch_qsa_block_keys afterwards, because the block's other
+// raw rows are written by other CTAs of the same launch.
 void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
                         const QsaBatch &b, uint32_t batch, const float *proj,
                         uint32_t ldp, const float *iproj, uint32_t ldi,
-                        float *q_out, float *iq_out, ErrorWord err,
-                        cudaStream_t stream);
+                        float *q_out, float *iq_out, bool inline_block_key,
+                        ErrorWord err, cudaStream_t stream);
 void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                       const float *iq, float *scores, uint32_t ld_scores,
                       uint32_t max_blocks, ErrorWord err, cudaStream_t stream);

@@ -78,32 +78,39 @@ __device__ void exact_norm_rope_shared(float *x, uint32_t n, const float *w, flo
     __syncthreads();
 }
 
-// Block key of block `bi` from raw index keys, exactly as :614-631; one
-// thread, result written feature-major into s.block_keys.  `tmp` holds di
-// floats of thread-private or shared storage.
-__device__ bool exact_block_key(const QsaDims &d, const QsaWeightsDev &w, const QsaSeq &s,
-                                uint32_t bi, float *tmp) {
+// Key of block `bi` from its raw index keys, exactly as :614-631, by the
+// whole CTA: per-feature means in parallel (each a sequential sum over the
+// block's rows), the RMS statistic by one thread in the reference's order,
+// then norm and RoPE in parallel; written feature-major into s.block_keys.
+// `vec` holds di floats of shared memory, `inv_slot` one more.  All threads
+// of the CTA must call it; returns false on a non-finite value.
+__device__ bool cta_block_key(const QsaDims &d, const QsaWeightsDev &w, const QsaSeq &s,
+                              uint32_t bi, float *vec, float *inv_slot) {
     const uint32_t di = d.index_dim;
-    for (uint32_t f = 0; f < di; ++f) {
+    bool bad = false;
+    for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) {
         float sum = 0.0f;
         for (uint32_t o = 0; o < d.block; ++o)
             sum = __fadd_rn(sum, s.raw[(size_t)(bi * d.block + o) * di + f]);
-        tmp[f] = __fdiv_rn(sum, (float)d.block);
+        vec[f] = __fdiv_rn(sum, (float)d.block);
     }
-    float inv = exact_rms_inverse(tmp, di, d.eps);
-    bool ok = isfinite(inv);
-    for (uint32_t f = 0; f < di; ++f) tmp[f] = exact_norm_apply(tmp[f], inv, w.ik_norm[f]);
-    const uint32_t half = d.rotary / 2;
-    const uint32_t pos = bi * d.block;
-    for (uint32_t i = 0; i < half; ++i)
-        exact_rope_pair(tmp, i, half, w.rope_cos[(size_t)pos * half + i],
-                        w.rope_sin[(size_t)pos * half + i]);
+    __syncthreads();
+    if (threadIdx.x == 0) *inv_slot = exact_rms_inverse(vec, di, d.eps);
+    __syncthreads();
+    const float inv = *inv_slot;
+    if (!isfinite(inv)) bad = true;
+    for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) vec[f] = exact_norm_apply(vec[f], inv, w.ik_norm[f]);
+    __syncthreads();
+    const uint32_t half = d.rotary / 2, bpos = bi * d.block;
+    for (uint32_t i = threadIdx.x; i < half; i += blockDim.x)
+        exact_rope_pair(vec, i, half, w.rope_cos[(size_t)bpos * half + i], w.rope_sin[(size_t)bpos * half + i]);
+    __syncthreads();
     const uint32_t ld = s.capacity / d.block;
-    for (uint32_t f = 0; f < di; ++f) {
-        ok &= isfinite(tmp[f]);
-        s.block_keys[(size_t)f * ld + bi] = tmp[f];
+    for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) {
+        if (!isfinite(vec[f])) bad = true;
+        s.block_keys[(size_t)f * ld + bi] = vec[f];
     }
-    return ok;
+    return !bad;
 }
 
 // ------------------------------------------------------------ prepare
@@ -121,7 +128,7 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
                    const float *__restrict__ proj, uint32_t ldp,
                    const float *__restrict__ iproj, uint32_t ldi,
                    float *__restrict__ q_out, float *__restrict__ iq_out,
-                   ErrorWord err) {
+                   bool inline_block_key, ErrorWord err) {
     pdl_wait();
     extern __shared__ float sh[];   // max(d, di) floats + 1
     if (qsa_error_raised(err)) return;
@@ -173,33 +180,9 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
             s.raw[(size_t)pos * di + i] = v;
         }
         __syncthreads();
-        // the token completes a block: cache that block's key (the steps of
-        // exact_block_key, spread over the CTA; only the RMS sum is serial)
-        if ((pos + 1) % d.block == 0) {
-            const uint32_t bi = pos / d.block;
-            for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) {
-                float sum = 0.0f;
-                for (uint32_t o = 0; o < d.block; ++o)
-                    sum = __fadd_rn(sum, s.raw[(size_t)(bi * d.block + o) * di + f]);
-                vec[f] = __fdiv_rn(sum, (float)d.block);
-            }
-            __syncthreads();
-            if (threadIdx.x == 0) *inv_slot = exact_rms_inverse(vec, di, d.eps);
-            __syncthreads();
-            const float inv = *inv_slot;
-            if (!isfinite(inv)) bad = true;
-            for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) vec[f] = exact_norm_apply(vec[f], inv, w.ik_norm[f]);
-            __syncthreads();
-            const uint32_t half = d.rotary / 2, bpos = bi * d.block;
-            for (uint32_t i = threadIdx.x; i < half; i += blockDim.x)
-                exact_rope_pair(vec, i, half, w.rope_cos[(size_t)bpos * half + i], w.rope_sin[(size_t)bpos * half + i]);
-            __syncthreads();
-            const uint32_t ld = s.capacity / d.block;
-            for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) {
-                if (!isfinite(vec[f])) bad = true;
-                s.block_keys[(size_t)f * ld + bi] = vec[f];
-            }
-        }
+        // the token completes a block: cache that block's key
+        if (inline_block_key && (pos + 1) % d.block == 0)
+            if (!cta_block_key(d, w, s, pos / d.block, vec, inv_slot)) bad = true;
     }
     if (__syncthreads_or(bad) && threadIdx.x == 0) qsa_raise(err, kErrNonFinite);
 }
@@ -207,28 +190,25 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
 void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
                         const QsaBatch &b, uint32_t batch, const float *proj,
                         uint32_t ldp, const float *iproj, uint32_t ldi,
-                        float *q_out, float *iq_out, ErrorWord err,
-                        cudaStream_t stream) {
+                        float *q_out, float *iq_out, bool inline_block_key,
+                        ErrorWord err, cudaStream_t stream) {
     size_t smem = (std::max(d.head_dim, d.index_dim) + 1) * sizeof(float);
     dim3 grid(batch, d.q_heads + d.kv_heads + d.index_heads + 1);
     KernelTimer timer("qsa_prepare", stream);
     launch_pdl(qsa_prepare_kernel, grid, kPrepThreads, smem, stream, d, w, b, proj, ldp, iproj, ldi,
-                                                            q_out, iq_out, err);
+               q_out, iq_out, inline_block_key, err);
     count_launch();
 }
 
 // ------------------------------------------------------------ block keys
-__global__ void qsa_block_keys_kernel(QsaDims d, QsaWeightsDev w, QsaSeq s,
-                                      uint32_t first, uint32_t end, ErrorWord err) {
+//
+// grid (end - first); 128 threads; one CTA per block key.
+__global__ void __launch_bounds__(kPrepThreads)
+qsa_block_keys_kernel(QsaDims d, QsaWeightsDev w, QsaSeq s, uint32_t first, ErrorWord err) {
     pdl_wait();
-    extern __shared__ float tmp_all[];
-    uint32_t bi = first + blockIdx.x * blockDim.x + threadIdx.x;
-    bool bad = false;
-    if (bi < end) {
-        float *tmp = tmp_all + (size_t)threadIdx.x * d.index_dim;
-        bad = !exact_block_key(d, w, s, bi, tmp);
-    }
-    if (__syncthreads_or(bad) && threadIdx.x == 0) qsa_raise(err, kErrNonFinite);
+    extern __shared__ float vec[];   // di floats + 1
+    const bool ok = cta_block_key(d, w, s, first + blockIdx.x, vec, vec + d.index_dim);
+    if (__syncthreads_or(!ok) && threadIdx.x == 0) qsa_raise(err, kErrNonFinite);
 }
 
 void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
@@ -236,14 +216,10 @@ void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
                            uint32_t end_block, ErrorWord err,
                            cudaStream_t stream) {
     if (end_block <= first_block) return;
-    const uint32_t threads = 64;
-    uint32_t n = end_block - first_block;
-    size_t smem = (size_t)threads * d.index_dim * sizeof(float);
-    if (smem > 48 * 1024)
-        cudaFuncSetAttribute(qsa_block_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem);
-    launch_pdl(qsa_block_keys_kernel, (n + threads - 1) / threads, threads, smem, stream, 
-        d, w, s, first_block, end_block, err);
+    const size_t smem = (d.index_dim + 1) * sizeof(float);
+    KernelTimer timer("qsa_block_keys", stream);
+    launch_pdl(qsa_block_keys_kernel, end_block - first_block, kPrepThreads, smem, stream, d, w, s, first_block,
+               err);
     count_launch();
 }
 

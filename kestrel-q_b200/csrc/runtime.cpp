@@ -48,6 +48,12 @@ bool ranges_overlap(const void *a, uint64_t an, const void *b, uint64_t bn) {
     return x < y + bn && y < x + an;
 }
 
+cudaError_t copy_sync(void *dst, const void *src, size_t bytes, cudaMemcpyKind kind, cudaStream_t stream) {
+    if (bytes == 0) return cudaSuccess;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, kind, stream);
+    return e != cudaSuccess ? e : cudaStreamSynchronize(stream);
+}
+
 bool is_device_pointer(const void *p) {
     if (p == nullptr) return false;
     cudaPointerAttributes attr;
@@ -165,7 +171,7 @@ kq_status DeviceContext::synchronize(kq_diagnostic *d) {
         uint32_t code = (uint32_t)(word >> 32);
         for (Rollbackable *r : dirty) r->on_error(failing);
         dirty.clear();
-        KQB_CUDA(cudaMemset(err_word, 0, sizeof(unsigned long long)), d, "error word reset");
+        KQB_CUDA(cudaMemsetAsync(err_word, 0, sizeof(unsigned long long), stream), d, "error word reset");
         kq_status s = code == kErrSelection ? KQ_STATUS_INVALID_QSA_STATE : KQ_STATUS_NUMERIC_DOMAIN;
         diag_set(d, s, "device reported %s (call %u); state rolled back", error_text(code), failing);
         return s;

@@ -40,6 +40,10 @@ bool ranges_overlap(const void *a, uint64_t a_bytes, const void *b, uint64_t b_b
 // True when `p` is device memory (or managed memory) of any device.
 bool is_device_pointer(const void *p);
 
+// A copy ordered on `stream` (the library's streams do not synchronise with
+// the legacy default stream), complete when it returns.
+cudaError_t copy_sync(void *dst, const void *src, size_t bytes, cudaMemcpyKind kind, cudaStream_t stream);
+
 // An object whose device-resident value can be rolled back when an
 // asynchronous call fails (GDN and QSA states).
 struct Rollbackable {

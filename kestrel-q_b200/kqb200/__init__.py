@@ -297,6 +297,19 @@ def qsa_decode_batch(layer: QsaLayer, states: Sequence[QsaState], x_ptr: int, y_
     abi.check(lib().kq_b200_qsa_decode_batch(layer.handle, arr, len(states), x_ptr, y_ptr, C.byref(d)), d)
 
 
+def gdn_prefill_async(state: GdnState, x_ptr: int, tokens: int, y_ptr: int) -> None:
+    """T tokens of one sequence on device buffers, asynchronous on the library stream."""
+    d = abi.Diagnostic()
+    abi.check(lib().kq_b200_gdn_prefill_async(state.layer.handle, state.handle, x_ptr, tokens, y_ptr,
+                                              C.byref(d)), d)
+
+
+def qsa_prefill_async(state: QsaState, x_ptr: int, tokens: int, y_ptr: int) -> None:
+    d = abi.Diagnostic()
+    abi.check(lib().kq_b200_qsa_prefill_async(state.layer.handle, state.handle, x_ptr, tokens, y_ptr,
+                                              C.byref(d)), d)
+
+
 def synchronize() -> None:
     d = abi.Diagnostic()
     abi.check(lib().kq_b200_synchronize(C.byref(d)), d)

@@ -175,6 +175,8 @@ _SIGNATURES = {
     "kq_qsa_execute_quantized": (C.c_int, [vp, vp, vp, u64, vp, u64, vp, vp, u64, vp, u64,
                                            SELECTION_OBSERVER, vp, vp, vp]),
     "kq_b200_qsa_decode_batch": (C.c_int, [vp, C.POINTER(vp), u32, vp, vp, vp]),
+    "kq_b200_gdn_prefill_async": (C.c_int, [vp, vp, vp, u64, vp, vp]),
+    "kq_b200_qsa_prefill_async": (C.c_int, [vp, vp, vp, u64, vp, vp]),
     "kq_gdn_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
     "kq_qsa_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
 }

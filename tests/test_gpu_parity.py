@@ -501,6 +501,44 @@ def test_qsa_prefill_then_decode_selection_exact(kq, oracle):
         prov.close()
 
 
+@pytest.mark.parametrize("hidden,qh,hd,budget,L0,T,seed", [
+    (512, 8, 128, 64, 37, 150, 71),       # three chunks (64, 64, 22), prior context mid-block
+    (2048, 16, 256, 512, 1001, 130, 72),  # config-1 head geometry, head-blocked attention
+])
+def test_qsa_chunked_prefill(kq, oracle, hidden, qh, hd, budget, L0, T, seed):
+    """A prefill without a selection observer runs 64 tokens per launch
+    sequence as batch entries over one cache; its outputs, caches and the
+    block keys it writes (checked through the bit-exact scores of the next
+    decode token) must match the per-token reference."""
+    from kqb200 import synth
+    dims = synth.QsaDims(hidden=hidden, query_heads=qh, kv_heads=2, head_dim=hd, index_heads=4, index_dim=128,
+                         block=4, budget=budget, max_context=4096, rotary=64)
+    weights, prov, layer, w = _qsa_setup(kq, oracle, dims, seed, proj_type=8)
+    try:
+        cap = 2048
+        k0, v0, r0 = synth.qsa_cache(seed + 100, dims, L0)
+        s = kq.QsaState(layer, cap)
+        s.load(k0, v0, r0)
+        x = synth.hidden(seed + 200, T + 1, dims.hidden)
+        y = s.execute_quantized(x[:T])
+        st, yo, ko, vo, ro, n, _ = oracle.qsa_run(dims, w, x[:T], k0, v0, r0, L0, cap)
+        assert st == 0 and s.length == n == L0 + T
+        assert_close(y, yo, "chunked prefill")
+        k, v, r = s.save()
+        assert np.array_equal(bits(r), bits(ro[:n]))
+        assert_close(k, ko[:n], "keys")
+        y1, sels = s.execute_quantized(x[T:], want_selection=True)
+        st, yo1, *_, osel = oracle.qsa_run(dims, w, x[T:], ko, vo, ro, n, cap)
+        assert st == 0
+        assert np.array_equal(bits(sels[0]["scores"]), bits(osel[0]["scores"]))
+        assert np.array_equal(sels[0]["selected"], osel[0]["selected"])
+        assert_close(y1, yo1, "decode after chunked prefill")
+        s.close()
+    finally:
+        layer.close()
+        prov.close()
+
+
 def test_qsa_decode_batch_ragged_contexts(kq, oracle):
     import torch
     from kqb200 import synth
