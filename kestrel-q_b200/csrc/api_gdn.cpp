@@ -22,7 +22,7 @@ using namespace kqb;
 namespace {
 constexpr uint32_t kGdnConfigMagic = 0x4b514743u;
 constexpr uint32_t kGdnStateMagic = 0x4b514753u;
-constexpr uint32_t kPrefillChunk = 2048;   // tokens per device pass
+constexpr uint32_t kPrefillChunk = 8192;   // tokens per device pass
 constexpr uint32_t kChunkedMinTokens = 32;  // prefill passes from this length use the chunked recurrence
 }  // namespace
 

@@ -94,7 +94,7 @@ kq_status kq_b200_provider_linear_batch_f32_static(kq_weight_provider *provider,
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "batched linear takes device buffers");
     if (ranges_overlap(x, (uint64_t)batch * columns * 4, y, (uint64_t)batch * rows * 4))
         return fail(diagnostic, KQ_STATUS_ALIASING_VIOLATION, "linear input and output overlap");
-    const size_t tiles = batch > 8 ? umma_xtile_bytes(batch, (uint32_t)columns) : 0;
+    const size_t tiles = batch > 8 ? umma_xtile_bytes(batch, (uint32_t)columns, /*allow_wide=*/false) : 0;
     if (tiles > kStaticScratchBytes - kErrorBytes) {
         char msg[160];
         snprintf(msg, sizeof msg, "batch %u x %llu columns needs %zu bytes of activation tiles; the static scratch "
@@ -117,7 +117,7 @@ kq_status kq_b200_provider_linear_batch_f32_static(kq_weight_provider *provider,
     const bool tensor_cores = batch > 8 && !force_simt_projection() &&
                               launch_projection_umma(segs, x, (uint32_t)columns, y, (uint32_t)rows, batch,
                                                      scratch + kErrorBytes, kStaticScratchBytes - kErrorBytes,
-                                                     err, stream, /*cache_maps=*/false);
+                                                     err, stream, /*cache_maps=*/false, /*allow_wide=*/false);
     if (!tensor_cores)   // warp GEMV / SIMT tiles: no scratch
         launch_projection(segs, x, (uint32_t)columns, y, (uint32_t)rows, batch, err, stream, nullptr, 0);
     KQB_CUDA(cudaGetLastError(), diagnostic, "linear launch");

@@ -40,6 +40,7 @@ enum DeviceError : uint32_t {
     kErrNonFinite = 1,   // non-finite input, state or result
     kErrDecay = 2,       // GDN log-decay not finite or positive
     kErrSelection = 3,   // QSA selected-token count invalid
+    kErrTimeout = 4,     // a bounded wait gave up (wait site in bits 8..15)
 };
 
 // One quantized (or F32/BF16) matrix in HBM: `rows` consecutive GGUF rows.
@@ -87,14 +88,15 @@ bool launch_projection(const ProjSegments &segs, const float *x, uint32_t ldx,
 // Tensor-core path (kernels_umma.cu), used for batches above 8.  Returns
 // false (nothing launched) for shapes / types it does not cover (true: the
 // input and output were checked for non-finite values).  `xtiles`
-// is work space of umma_xtile_bytes(batch, cols) bytes.  `cache_maps`
-// false encodes the TMA descriptors on the stack instead of the host-side
-// descriptor cache (no host allocation).
+// is work space of umma_xtile_bytes(batch, cols, allow_wide) bytes.
+// `cache_maps` false encodes the TMA descriptors on the stack instead of the
+// host-side descriptor cache (no host allocation).  `allow_wide` false keeps
+// the 64-row activation tile for every batch (smaller work space).
 bool launch_projection_umma(const ProjSegments &segs, const float *x, uint32_t ldx,
                             float *y, uint32_t ldy, uint32_t batch, uint8_t *xtiles,
                             size_t xtile_bytes, ErrorWord err, cudaStream_t stream,
-                            bool cache_maps = true);
-size_t umma_xtile_bytes(uint32_t batch, uint32_t cols);
+                            bool cache_maps = true, bool allow_wide = true);
+size_t umma_xtile_bytes(uint32_t batch, uint32_t cols, bool allow_wide = true);
 // Work space (in floats) that launch_projection uses for `batch` rows of
 // input with `cols` columns: the activation tiles of the tensor-core path.
 size_t projection_workspace_floats(uint32_t batch, uint32_t ldy, uint32_t cols);

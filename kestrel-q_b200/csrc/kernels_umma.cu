@@ -61,14 +61,12 @@ namespace kqb {
 namespace {
 
 constexpr int kUM = 128;                  // weight rows per CTA (MMA M)
-constexpr int kUN = 64;                   // batch rows per CTA (MMA N)
+constexpr int kUN = 64;                   // batch rows per CTA, small batches (MMA N)
+constexpr int kUNWide = 256;              // batch rows per CTA, large batches (prefill)
 constexpr int kUK = 64;                   // K per chunk (one 128-byte swizzle row of bf16)
-constexpr int kBTile = kUN * kUK * 2;     // bytes of one bf16 B tile (8 KB)
-constexpr int kXSlot = 2 * kBTile;        // activation tile of one chunk: [xh | xl]
 constexpr int kMaxXRing = 10;
-constexpr int kRawRing = 3;               // raw super-block slots
-constexpr int kSmemBudget = 200 * 1024;
-constexpr int kABufs = 6;                 // decoded A buffers in TMEM
+constexpr int kMaxRawRing = 3;
+constexpr int kMaxABufs = 6;
 constexpr int kDecodeWarps = 16;
 // The single-thread roles sit on different schedulers (scheduler = warp % 4),
 // because their TMA / MMA instructions take issue time from the decode warps
@@ -79,14 +77,43 @@ constexpr int kMmaWarp = kDecodeWarps + 1;
 constexpr int kTmaWarp = kDecodeWarps + 2;
 constexpr int kThreads = (kDecodeWarps + 3) * 32;
 constexpr int kAccStride = kUN + 1;       // floats per row of the split-K exchange tile
-// TMEM columns: [0, 128) accumulator, wh * [xh | xl] (N = 128) with wl * xh
-// (N = 64) added into its first 64 columns; A buffer b at 128 + 64 b:
-// hi 32 | lo 32.
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kABase = 128;
-static_assert(kABase + 64 * kABufs <= kTmemCols, "TMEM budget");
-constexpr uint32_t kWaitLimit = 1u << 22;  // mbarrier polls before giving up
-constexpr uint32_t kErrTimeout = 4;
+
+// Geometry of a tile of NT batch rows.
+//  NT = 64: TMEM columns [0, 128) hold the accumulator: wh * [xh | xl]
+//           (N = 128) with wl * xh (N = 64) added into its first 64 columns;
+//           six A buffers follow.
+//  NT = 256: the activation tile is [xh (256 rows) | xl (256 rows)] and all
+//           three products go into one accumulator of 256 columns (three
+//           N = 256 MMAs per K step); four A buffers follow.  Each decoded
+//           weight chunk then feeds four times the MMA work, which is what
+//           a prefill needs (decode time per chunk is the same).
+// An A buffer is 64 columns: hi 32 | lo 32 (64 bf16 K values each).
+template <uint32_t NT> struct Tile {
+    static_assert(NT == 64 || NT == 256, "tile widths");
+    static constexpr uint32_t xslot = 2u * NT * kUK * 2u;       // bytes: [xh | xl]
+    static constexpr uint32_t raw_ring = NT == 64 ? 3u : 2u;    // raw super-block slots
+    static constexpr uint32_t budget = (NT == 64 ? 200u : 220u) * 1024u;
+    static constexpr uint32_t dcols = NT == 64 ? 128u : NT;
+    static constexpr uint32_t abase = dcols;
+    static constexpr uint32_t abufs = (kTmemCols - dcols) / 64u < (uint32_t)kMaxABufs
+                                          ? (kTmemCols - dcols) / 64u : (uint32_t)kMaxABufs;
+    static_assert(abase + 64u * abufs <= kTmemCols, "TMEM budget");
+};
+constexpr uint32_t kWaitLimit = 1u << 26;           // mbarrier polls before giving up
+constexpr uint64_t kWaitNs = 2000000000ull;          // or 2 s of global time, whichever comes first
+
+// Wait sites, recorded in the abort flag by the first wait that gives up
+// and reported in the error code (kErrTimeout | site << 8).
+enum WaitSite : uint32_t {
+    kSiteRawFree = 1, kSiteXFree, kSiteAReady, kSiteXFull, kSiteRawFull, kSiteADone, kSiteAccum
+};
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -98,9 +125,11 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 
 // Bounded wait for the phase with parity `parity` to complete.  Gives up
 // early when another role has raised the CTA's abort flag; raises it itself
-// when the poll limit is reached.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort) {
+// (with its site) when the poll limit or the time limit is reached.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort,
+                                          uint32_t site) {
     const uint32_t addr = smem_u32(bar);
+    const uint64_t t0 = global_ns();
     for (uint32_t i = 0; i < kWaitLimit; ++i) {
         uint32_t done;
         asm volatile(
@@ -111,16 +140,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
-        if ((i & 63u) == 63u && *abort) return false;
+        if ((i & 63u) == 63u) {
+            if (*abort) return false;
+            if (global_ns() - t0 > kWaitNs) break;
+        }
     }
-    *abort = 1u;
+    atomicCAS(const_cast<uint32_t *>(abort), 0u, site);
     return false;
 }
 
 // Warp-uniform form: lane 0 waits, the result is broadcast.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, volatile uint32_t *abort) {
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, volatile uint32_t *abort,
+                                               uint32_t site) {
     uint32_t ok = 0;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort) ? 1u : 0u;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, site) ? 1u : 0u;
     ok = __shfl_sync(0xffffffffu, ok, 0);
     return ok != 0;
 }
@@ -305,14 +338,17 @@ template <> struct TypeCfg<kTypeQ6_K> { static constexpr uint32_t sc = 4, raw = 
 template <> struct TypeCfg<kTypeQ8_0> { static constexpr uint32_t sc = 4, raw = 128 * 272; };
 template <> struct TypeCfg<kTypeBF16> { static constexpr uint32_t sc = 2, raw = 128 * 256; };
 
-// Ring depths per type within the shared-memory budget.
-template <uint32_t T> struct Ring {
+// Ring depths per type and tile width within the shared-memory budget.
+template <uint32_t T, uint32_t NT> struct Ring {
     static constexpr uint32_t raw = TypeCfg<T>::raw;
-    static constexpr uint32_t xdepth_fit = (kSmemBudget - kRawRing * raw) / kXSlot;
+    static constexpr uint32_t rr = Tile<NT>::raw_ring;
+    static constexpr uint32_t xdepth_fit = (Tile<NT>::budget - rr * raw) / Tile<NT>::xslot;
     static constexpr uint32_t xdepth = xdepth_fit < (uint32_t)kMaxXRing ? xdepth_fit : kMaxXRing;
-    static constexpr uint32_t smem = kRawRing * raw + xdepth * kXSlot + 1024 /*align*/;
-    static_assert(xdepth >= (uint32_t)kABufs, "the A-buffer wait relies on xdepth >= kABufs");
+    static constexpr uint32_t smem = rr * raw + xdepth * Tile<NT>::xslot + 1024 /*align*/;
+    static_assert(xdepth >= 2, "double-buffered activations");
+    static_assert(rr <= (uint32_t)kMaxRawRing, "raw ring");
     static_assert(raw % 1024 == 0, "slots keep the 1024-byte swizzle alignment");
+    static_assert(smem <= 227u * 1024u, "shared memory per CTA");
 };
 
 __device__ __forceinline__ uint4 lds16(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
@@ -433,15 +469,17 @@ struct TmapSet {
 };
 
 // Activations to bf16 hi/lo tiles in the MMA's shared-memory image:
-// out[btile][chunk] = { hi: 64 rows x 128 B swizzled, lo: same }.
+// out[btile][chunk] = { hi: NT rows x 128 B swizzled, lo: same }.
 // One CTA converts 16 rows of one chunk; one thread 8 values.
+template <uint32_t NT>
 __global__ void __launch_bounds__(128)
 xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t cols, uint32_t nchunks,
              uint8_t *__restrict__ out, ErrorWord err) {
     pdl_wait();
-    const uint32_t c = blockIdx.x >> 2, bt = blockIdx.y;
-    const uint32_t r = (blockIdx.x & 3u) * 16u + (threadIdx.x >> 3), q8 = threadIdx.x & 7u;
-    const uint32_t b = bt * kUN + r, k0 = c * kUK + q8 * 8u;
+    constexpr uint32_t kGroups = NT / 16u;
+    const uint32_t c = blockIdx.x / kGroups, bt = blockIdx.y;
+    const uint32_t r = (blockIdx.x % kGroups) * 16u + (threadIdx.x >> 3), q8 = threadIdx.x & 7u;
+    const uint32_t b = bt * NT + r, k0 = c * kUK + q8 * 8u;
     float v[8];
     const float *src = x + (size_t)b * ldx + k0;
     if (b < batch && k0 + 8 <= cols && ((reinterpret_cast<uintptr_t>(src) & 15u) == 0)) {
@@ -460,10 +498,10 @@ xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t
         atomicCAS(err.word, 0ull, ((unsigned long long)kErrNonFinite << 32) | err.call_id);
     uint4 hi, lo;
     pack8(v, hi, lo);
-    uint8_t *tile = out + ((size_t)bt * nchunks + c) * (2 * kBTile);
+    uint8_t *tile = out + ((size_t)bt * nchunks + c) * Tile<NT>::xslot;
     const uint32_t off = sw128_off(r, q8);
     *reinterpret_cast<uint4 *>(tile + off) = hi;
-    *reinterpret_cast<uint4 *>(tile + kBTile + off) = lo;
+    *reinterpret_cast<uint4 *>(tile + Tile<NT>::xslot / 2 + off) = lo;
 }
 
 
@@ -499,20 +537,22 @@ __device__ __forceinline__ uint32_t raw_tx(uint32_t box_rows) {
     else return 256u * box_rows;
 }
 
-template <uint32_t T>
+template <uint32_t T, uint32_t NT>
 __global__ void __launch_bounds__(kThreads, 1)
 proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const uint8_t *__restrict__ xtiles,
                  uint32_t nchunks_x, float *__restrict__ y, uint32_t ldy, uint32_t batch,
                  uint32_t kchunks_per_split, ErrorWord err) {
     pdl_wait();
-    constexpr uint32_t SC = TypeCfg<T>::sc, kRawBytes = Ring<T>::raw, kX = Ring<T>::xdepth;
+    using R = Ring<T, NT>;
+    constexpr uint32_t SC = TypeCfg<T>::sc, kRawBytes = R::raw, kX = R::xdepth, kRawRing = R::rr;
+    constexpr uint32_t kXSlot = Tile<NT>::xslot, kABufs = Tile<NT>::abufs, kABase = Tile<NT>::abase;
     constexpr uint32_t kIssuers = 1u;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    __shared__ uint64_t rfull[kRawRing], rfree[kRawRing], xfull[kMaxXRing], mdone[kMaxXRing];
-    __shared__ uint64_t aready[kABufs], accum;
+    __shared__ uint64_t rfull[kMaxRawRing], rfree[kMaxRawRing], xfull[kMaxXRing], mdone[kMaxXRing];
+    __shared__ uint64_t aready[kMaxABufs], adone[kMaxABufs], accum;
     __shared__ uint32_t tmem_base_slot;
     __shared__ volatile uint32_t abort_flag;
-    static_assert(kUM * kAccStride * 4 <= kX * kXSlot, "exchange tile does not fit");
+    static_assert(NT != 64 || kUM * kAccStride * 4 <= kX * kXSlot, "exchange tile does not fit");
     // No early return anywhere: every CTA of a split-K cluster must reach
     // both cluster barriers.
     const bool skip = *reinterpret_cast<volatile unsigned long long *>(err.word) != 0ull;
@@ -525,7 +565,7 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     while (seg + 1 < segs.count && blockIdx.x >= segs.tile_start[seg + 1]) ++seg;
     const QMatrix m = segs.m[seg];
     const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * kUM;
-    const uint32_t b0 = blockIdx.y * kUN;
+    const uint32_t b0 = blockIdx.y * NT;
     const uint32_t nchunks_total = (m.cols + kUK - 1) / kUK;
     // kchunks_per_split is a multiple of SC, so c_begin starts a super-block step
     const uint32_t c_begin = blockIdx.z * kchunks_per_split;
@@ -533,13 +573,16 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     const uint32_t nchunks = (c_end > c_begin && !skip) ? c_end - c_begin : 0;
 
     if (tid == 0) {
-        for (int s = 0; s < kRawRing; ++s) mbar_init(&rfull[s], 1);
+        for (uint32_t s = 0; s < kRawRing; ++s) mbar_init(&rfull[s], 1);
         for (uint32_t s = 0; s < kX; ++s) {
             mbar_init(&xfull[s], 1);
             mbar_init(&mdone[s], kIssuers);
         }
-        for (int s = 0; s < kRawRing; ++s) mbar_init(&rfree[s], kIssuers);
-        for (int b = 0; b < kABufs; ++b) mbar_init(&aready[b], kDecodeWarps);
+        for (uint32_t s = 0; s < kRawRing; ++s) mbar_init(&rfree[s], kIssuers);
+        for (uint32_t b = 0; b < kABufs; ++b) {
+            mbar_init(&aready[b], kDecodeWarps);
+            mbar_init(&adone[b], kIssuers);
+        }
         mbar_init(&accum, kIssuers);
         abort_flag = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -564,17 +607,16 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
                 if (it % SC == 0) {
                     // raw slot of step j was last used by step j - kRawRing
                     const uint32_t j = it / SC, rs = j % kRawRing;
-                    if (j >= kRawRing && !mbar_wait(&rfree[rs], ((j - kRawRing) / kRawRing) & 1u, &abort_flag))
+                    if (j >= kRawRing && !mbar_wait(&rfree[rs], ((j - kRawRing) / kRawRing) & 1u, &abort_flag, kSiteRawFree))
                         break;
                     mbar_expect_tx(&rfull[rs], rtx);
                     load_raw<T>(smem_u32(raw_ring + rs * kRawBytes), maps, m.cols, sb0 + j, (int)row0, &rfull[rs]);
                 }
                 const uint32_t xs = it % kX;
-                if (it >= kX && !mbar_wait(&mdone[xs], ((it - kX) / kX) & 1u, &abort_flag)) break;
-                mbar_expect_tx(&xfull[xs], (uint32_t)kXSlot);
+                if (it >= kX && !mbar_wait(&mdone[xs], ((it - kX) / kX) & 1u, &abort_flag, kSiteXFree)) break;
+                mbar_expect_tx(&xfull[xs], kXSlot);
                 bulk_load(smem_u32(x_ring + xs * kXSlot),
-                          xtiles + ((size_t)blockIdx.y * nchunks_x + c_begin + it) * kXSlot, (uint32_t)kXSlot,
-                          &xfull[xs]);
+                          xtiles + ((size_t)blockIdx.y * nchunks_x + c_begin + it) * kXSlot, kXSlot, &xfull[xs]);
             }
         }
     } else if (warp == kMmaWarp) {
@@ -585,19 +627,27 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
             const uint64_t desc0 = sw128_desc(smem_u32(x_ring));
             for (uint32_t it = 0; it < nchunks; ++it) {
                 const uint32_t xs = it % kX, b = it % kABufs;
-                if (!mbar_wait(&aready[b], (it / kABufs) & 1u, &abort_flag)) break;
-                if (!mbar_wait(&xfull[xs], (it / kX) & 1u, &abort_flag)) break;
+                if (!mbar_wait(&aready[b], (it / kABufs) & 1u, &abort_flag, kSiteAReady)) break;
+                if (!mbar_wait(&xfull[xs], (it / kX) & 1u, &abort_flag, kSiteXFull)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                // B: the slot's 128 swizzled rows are [xh (64 rows) | xl (64 rows)]
+                // B: the slot's swizzled rows are [xh (NT rows) | xl (NT rows)]
                 const uint64_t db = desc0 + (uint64_t)(xs * (kXSlot >> 4));
                 const uint32_t ah = tmem + kABase + b * 64u, al = ah + 32u;
                 const uint32_t first = it == 0 ? 0u : 1u;
 #pragma unroll
                 for (uint32_t kk = 0; kk < kUK / 16; ++kk) {   // +32 bytes of K per step = +2 in the address field
-                    umma_ts<2 * kUN>(tmem, ah + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
-                    if constexpr (T != kTypeBF16) umma_ts<kUN>(tmem, al + kk * 8u, db + 2u * kk, 1u);
+                    if constexpr (NT == 64) {
+                        umma_ts<2 * NT>(tmem, ah + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
+                        if constexpr (T != kTypeBF16) umma_ts<NT>(tmem, al + kk * 8u, db + 2u * kk, 1u);
+                    } else {
+                        const uint64_t dlo = db + (uint64_t)((kXSlot / 2) >> 4);
+                        umma_ts<NT>(tmem, ah + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
+                        umma_ts<NT>(tmem, ah + kk * 8u, dlo + 2u * kk, 1u);
+                        if constexpr (T != kTypeBF16) umma_ts<NT>(tmem, al + kk * 8u, db + 2u * kk, 1u);
+                    }
                 }
                 umma_commit(&mdone[xs]);
+                umma_commit(&adone[b]);
                 if (it % SC == SC - 1) umma_commit(&rfree[(it / SC) % kRawRing]);
             }
             umma_commit(&accum);   // completes once every MMA this thread issued has
@@ -609,10 +659,9 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
         const uint32_t lane_addr = (quarter * 32u) << 16;
         for (uint32_t it = 0; it < nchunks; ++it) {
             const uint32_t j = it / SC, rs = j % kRawRing, b = it % kABufs;
-            if (!mbar_wait_warp(&rfull[rs], (j / kRawRing) & 1u, &abort_flag)) break;
+            if (!mbar_wait_warp(&rfull[rs], (j / kRawRing) & 1u, &abort_flag, kSiteRawFull)) break;
             // A buffer b was last read by the MMAs of chunk it - kABufs
-            if (it >= kABufs && !mbar_wait_warp(&mdone[(it - kABufs) % kX], ((it - kABufs) / kX) & 1u,
-                                                &abort_flag))
+            if (it >= kABufs && !mbar_wait_warp(&adone[b], ((it - kABufs) / kABufs) & 1u, &abort_flag, kSiteADone))
                 break;
             uint32_t hi[8], lo[8];
             decode16<T>(raw_ring + rs * kRawBytes, row, m.cols, c_begin + it, q, hi, lo);
@@ -629,17 +678,43 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     // ---- epilogue
     bool ok = false;
     if (warp < kDecodeWarps) {
-        ok = mbar_wait_warp(&accum, 0, &abort_flag);
+        ok = mbar_wait_warp(&accum, 0, &abort_flag, kSiteAccum);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     }
     const bool all_ok = __syncthreads_and(warp >= kDecodeWarps || ok) && abort_flag == 0u;
     if (!all_ok && tid == 0)
-        atomicCAS(err.word, 0ull, ((unsigned long long)kErrTimeout << 32) | err.call_id);
+        atomicCAS(err.word, 0ull, ((unsigned long long)(kErrTimeout | (abort_flag << 8)) << 32) | err.call_id);
 
-    // accumulator: decode warp w reads TMEM lanes 32*(w&3).., columns 16*(w>>2)..
+    // accumulator: decode warp w reads TMEM lanes 32*(w&3).., its quarter of the columns
     const uint32_t lane_base = 32u * (warp & 3);
-    const uint32_t col_base = (uint32_t)(warp >> 2) * 16u;
     const uint32_t trow = lane_base + lane;
+    const bool write = all_ok && !skip;
+    bool out_bad = false;   // the projection's output check
+    if constexpr (NT != 64) {
+        // one accumulator holds all three products; no split-K
+        const uint32_t col_base = (uint32_t)(warp >> 2) * (NT / 4u);
+        const uint32_t row = row0 + trow;
+        // warp-uniform condition: tcgen05.ld is a .sync.aligned warp
+        // instruction; rows past the matrix only skip their stores
+        if (warp < kDecodeWarps && write && nchunks > 0) {
+#pragma unroll 1
+            for (uint32_t g = 0; g < NT / 4u; g += 16u) {
+                uint32_t r0[16];
+                tmem_ld16(tmem + (lane_base << 16) + col_base + g, r0);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const uint32_t b = b0 + col_base + g + j;
+                    const float v = __uint_as_float(r0[j]);
+                    if (b < batch && row < m.rows) {
+                        out_bad |= !isfinite(v);
+                        y[(size_t)b * ldy + segs.out_offset[seg] + row] = v;
+                    }
+                }
+            }
+        }
+    } else {
+    const uint32_t col_base = (uint32_t)(warp >> 2) * 16u;
     float acc[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) acc[j] = 0.0f;   // empty split: contributes zero
@@ -653,9 +728,7 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[j] = __fadd_rn(__uint_as_float(r0[j]), __uint_as_float(r1[j]));
     }
-    const bool write = all_ok && !skip;
     const uint32_t nsplit = gridDim.z;
-    bool out_bad = false;   // the projection's output check
     if (nsplit == 1) {
         const uint32_t row = row0 + trow;
         if (warp < kDecodeWarps && write && row < m.rows) {
@@ -698,6 +771,7 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
         }
         cluster_sync();   // peers finish reading this CTA's tile before it exits
     }
+    }
     if (out_bad) atomicCAS(err.word, 0ull, ((unsigned long long)kErrNonFinite << 32) | err.call_id);
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -719,8 +793,12 @@ bool umma_supported(const QMatrix &m) {
     }
 }
 
-size_t umma_xtile_bytes(uint32_t batch, uint32_t cols) {
-    return (size_t)((batch + kUN - 1) / kUN) * ((cols + kUK - 1) / kUK) * 2 * kBTile;
+size_t umma_xtile_bytes(uint32_t batch, uint32_t cols, bool allow_wide) {
+    const size_t nch = (cols + kUK - 1) / kUK;
+    const size_t narrow = (size_t)((batch + kUN - 1) / kUN) * nch * Tile<kUN>::xslot;
+    if (batch <= (uint32_t)kUN || !allow_wide) return narrow;
+    const size_t wide = (size_t)((batch + kUNWide - 1) / kUNWide) * nch * Tile<kUNWide>::xslot;
+    return std::max(narrow, wide);
 }
 
 
@@ -828,7 +906,7 @@ static bool maps_for(const QMatrix &m, CUtensorMap (&maps)[3], bool cache = true
 // pipeline fill and epilogue) + 2 per cluster member for the
 // distributed-shared-memory reduction, with one CTA per SM.  The constants
 // are fitted to measured B200 times of the in-/out-projection shapes.
-static uint32_t choose_splits(uint32_t tiles, uint32_t nchunks, uint32_t max_splits) {
+static int sm_count() {
     static int sms = 0;
     if (sms == 0) {
         int dev = 0;
@@ -836,6 +914,11 @@ static uint32_t choose_splits(uint32_t tiles, uint32_t nchunks, uint32_t max_spl
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (sms <= 0) sms = 148;
     }
+    return sms;
+}
+
+static uint32_t choose_splits(uint32_t tiles, uint32_t nchunks, uint32_t max_splits, double *cost_out = nullptr) {
+    const int sms = sm_count();
     uint32_t best = 1;
     double best_cost = 1e30;
     for (uint32_t s = 1; s <= max_splits; s *= 2) {
@@ -844,7 +927,23 @@ static uint32_t choose_splits(uint32_t tiles, uint32_t nchunks, uint32_t max_spl
         const double cost = waves * ((nchunks + s - 1) / s + 8.0) + (s > 1 ? 2.0 * s : 0.0);
         if (cost < best_cost - 1e-9) { best_cost = cost; best = s; }
     }
+    if (cost_out) *cost_out = best_cost;
     return best;
+}
+
+// The wide tile (256 batch rows per CTA, no split) against the narrow one
+// (64 rows, split-K): a CTA spends about the same time per weight chunk
+// either way (the decode of the weights bounds it), so the wide tile wins
+// once it still fills the SMs; 1.15 covers its longer MMA issue per chunk.
+static bool choose_wide(uint32_t tiles, uint32_t nchunks, uint32_t batch) {
+    const char *env = getenv("KQ_B200_PROJ_WIDE");   // tuning and tests: 0 narrow, 1 wide
+    const int forced = env ? atoi(env) : -1;
+    if (batch <= (uint32_t)kUN) return false;
+    if (forced == 0 || forced == 1) return forced == 1;
+    double narrow;
+    choose_splits(tiles * ((batch + kUN - 1) / kUN), nchunks, 8, &narrow);
+    const double waves = std::ceil((double)tiles * ((batch + kUNWide - 1) / kUNWide) / sm_count());
+    return waves * (nchunks + 8.0) * 1.15 < narrow;
 }
 
 // Largest split cluster (8, 4, 2 or 1) the device can co-schedule for this
@@ -853,13 +952,14 @@ template <uint32_t T>
 static uint32_t max_splits_for() {
     static uint32_t cached = 0;
     if (cached == 0) {
-        cudaFuncSetAttribute(proj_umma_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Ring<T>::smem);
+        cudaFuncSetAttribute(proj_umma_kernel<T, kUN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Ring<T, kUN>::smem);
         uint32_t best = 1;
         for (uint32_t s = 8; s >= 2; s /= 2) {
             cudaLaunchConfig_t cfg{};
             cfg.gridDim = dim3(1, 1, s);
             cfg.blockDim = dim3(kThreads);
-            cfg.dynamicSmemBytes = Ring<T>::smem;
+            cfg.dynamicSmemBytes = Ring<T, kUN>::smem;
             cudaLaunchAttribute at[1];
             at[0].id = cudaLaunchAttributeClusterDimension;
             at[0].val.clusterDim.x = 1;
@@ -868,7 +968,7 @@ static uint32_t max_splits_for() {
             cfg.attrs = at;
             cfg.numAttrs = 1;
             int n = 0;
-            if (cudaOccupancyMaxActiveClusters(&n, proj_umma_kernel<T>, &cfg) == cudaSuccess && n > 0) {
+            if (cudaOccupancyMaxActiveClusters(&n, proj_umma_kernel<T, kUN>, &cfg) == cudaSuccess && n > 0) {
                 best = s;
                 break;
             }
@@ -881,12 +981,33 @@ static uint32_t max_splits_for() {
 
 template <uint32_t T>
 static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &segs, const uint8_t *xt,
-                         uint32_t nchunks_x, float *y, uint32_t ldy, uint32_t batch, ErrorWord err,
+                         uint32_t nchunks_x, float *y, uint32_t ldy, uint32_t batch, bool wide, ErrorWord err,
                          cudaStream_t stream, bool cache_maps) {
     TmapSet maps;
     for (int i = 0; i < segs.count; ++i) {
         if (!segment_maps<T>(segs.m[i], maps.map[i], cache_maps)) return false;
         maps.box_rows[i] = std::min<uint32_t>(segs.m[i].rows, kUM);
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see launch_pdl
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    if (wide) {
+        static bool attr = false;
+        if (!attr) {
+            cudaFuncSetAttribute(proj_umma_kernel<T, kUNWide>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Ring<T, kUNWide>::smem);
+            attr = true;
+        }
+        cfg.gridDim = dim3(tiles, (batch + kUNWide - 1) / kUNWide, 1);
+        cfg.dynamicSmemBytes = Ring<T, kUNWide>::smem;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, proj_umma_kernel<T, kUNWide>, maps, segs, xt, nchunks_x, y, ldy, batch, nchunks,
+                           err);
+        return true;
     }
     const uint32_t btiles = (batch + kUN - 1) / kUN;
     static const int forced = [] {
@@ -899,27 +1020,21 @@ static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &s
     // chunks per split: whole super-block steps
     constexpr uint32_t SC = TypeCfg<T>::sc;
     const uint32_t per = ((nchunks + splits - 1) / splits + SC - 1) / SC * SC;
-    cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(tiles, btiles, splits);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = Ring<T>::smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute at[2];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 1;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = splits;
-    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;   // see launch_pdl
-    at[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
+    cfg.dynamicSmemBytes = Ring<T, kUN>::smem;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = 1;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = splits;
     cfg.numAttrs = 2;
-    cudaLaunchKernelEx(&cfg, proj_umma_kernel<T>, maps, segs, xt, nchunks_x, y, ldy, batch, per, err);
+    cudaLaunchKernelEx(&cfg, proj_umma_kernel<T, kUN>, maps, segs, xt, nchunks_x, y, ldy, batch, per, err);
     return true;
 }
 
 // Launches one group of segments that share a weight type.
 static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, uint32_t nchunks_x, float *y,
-                         uint32_t ldy, uint32_t batch, ErrorWord err, cudaStream_t stream, bool cache_maps) {
+                         uint32_t ldy, uint32_t batch, bool wide, ErrorWord err, cudaStream_t stream,
+                         bool cache_maps) {
     uint32_t acc = 0, cols = 0;
     for (int i = 0; i < segs.count; ++i) {
         segs.tile_start[i] = acc;
@@ -930,10 +1045,10 @@ static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, ui
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
     bool ok;
     switch (type) {
-    case kTypeQ4_K: ok = launch_typed<kTypeQ4_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream, cache_maps); break;
-    case kTypeQ6_K: ok = launch_typed<kTypeQ6_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream, cache_maps); break;
-    case kTypeQ8_0: ok = launch_typed<kTypeQ8_0>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream, cache_maps); break;
-    default: ok = launch_typed<kTypeBF16>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, err, stream, cache_maps); break;
+    case kTypeQ4_K: ok = launch_typed<kTypeQ4_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, wide, err, stream, cache_maps); break;
+    case kTypeQ6_K: ok = launch_typed<kTypeQ6_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, wide, err, stream, cache_maps); break;
+    case kTypeQ8_0: ok = launch_typed<kTypeQ8_0>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, wide, err, stream, cache_maps); break;
+    default: ok = launch_typed<kTypeBF16>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, wide, err, stream, cache_maps); break;
     }
     if (ok) count_launch();
     return ok;
@@ -941,7 +1056,7 @@ static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, ui
 
 bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx, float *y, uint32_t ldy,
                             uint32_t batch, uint8_t *xtiles, size_t xtile_bytes, ErrorWord err,
-                            cudaStream_t stream, bool cache_maps) {
+                            cudaStream_t stream, bool cache_maps, bool allow_wide) {
     uint32_t cols = 0;
     for (int i = 0; i < in.count; ++i) {
         if (!umma_supported(in.m[i])) return false;
@@ -949,15 +1064,23 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
     }
     for (int i = 1; i < in.count; ++i)
         if (in.m[i].cols != cols) return false;
-    if (xtiles == nullptr || xtile_bytes < umma_xtile_bytes(batch, cols)) return false;
+    if (xtiles == nullptr || xtile_bytes < umma_xtile_bytes(batch, cols, allow_wide)) return false;
     // tensor maps first, so that a failure launches nothing
     for (int i = 0; i < in.count; ++i) {
         CUtensorMap maps[3];
         if (!maps_for(in.m[i], maps, cache_maps)) return false;
     }
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
-    const dim3 xg(nchunks * 4, (batch + kUN - 1) / kUN);
-    launch_pdl(xconv_kernel, xg, 128, 0, stream, x, ldx, batch, cols, nchunks, xtiles, err);
+    uint32_t tiles = 0;
+    for (int i = 0; i < in.count; ++i) tiles += (in.m[i].rows + kUM - 1) / kUM;
+    const bool wide = allow_wide && choose_wide(tiles, nchunks, batch);
+    if (wide) {
+        const dim3 xg(nchunks * (kUNWide / 16), (batch + kUNWide - 1) / kUNWide);
+        launch_pdl(xconv_kernel<kUNWide>, xg, 128, 0, stream, x, ldx, batch, cols, nchunks, xtiles, err);
+    } else {
+        const dim3 xg(nchunks * (kUN / 16), (batch + kUN - 1) / kUN);
+        launch_pdl(xconv_kernel<kUN>, xg, 128, 0, stream, x, ldx, batch, cols, nchunks, xtiles, err);
+    }
     count_launch();
     // one launch per weight type present
     bool done[kMaxSegments] = {};
@@ -971,7 +1094,7 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
             ++g.count;
             done[j] = true;
         }
-        launch_group(in.m[i].type, g, xtiles, nchunks, y, ldy, batch, err, stream, cache_maps);
+        launch_group(in.m[i].type, g, xtiles, nchunks, y, ldy, batch, wide, err, stream, cache_maps);
     }
     return true;
 }

@@ -148,10 +148,11 @@ kq_status DeviceContext::workspace(size_t bytes, void **out, kq_diagnostic *d) {
 }
 
 static const char *error_text(uint32_t code) {
-    switch (code) {
+    switch (code & 0xFFu) {
     case kErrNonFinite: return "a non-finite input, state or intermediate value";
     case kErrDecay: return "GDN log decay must be finite and non-positive";
     case kErrSelection: return "QSA selected-token count is invalid";
+    case kErrTimeout: return "a tensor-core pipeline wait that timed out";
     default: return "device error";
     }
 }
@@ -173,7 +174,8 @@ kq_status DeviceContext::synchronize(kq_diagnostic *d) {
         dirty.clear();
         KQB_CUDA(cudaMemsetAsync(err_word, 0, sizeof(unsigned long long), stream), d, "error word reset");
         kq_status s = code == kErrSelection ? KQ_STATUS_INVALID_QSA_STATE : KQ_STATUS_NUMERIC_DOMAIN;
-        diag_set(d, s, "device reported %s (call %u); state rolled back", error_text(code), failing);
+        diag_set(d, s, "device reported %s (code 0x%x, call %u); state rolled back", error_text(code), code,
+                 failing);
         return s;
     }
     for (Rollbackable *r : dirty) r->on_success();

@@ -99,14 +99,19 @@ def test_provider_linear(kq, oracle, type_id):
         p.close()
 
 
-@pytest.mark.parametrize("type_id,rows,cols,batch", [
-    (12, 520, 2048, 64), (14, 2048, 4096, 64), (8, 300, 2048, 9), (30, 640, 2048, 100),
-    (0, 200, 512, 33), (12, 12352, 2048, 64), (14, 130, 256, 129)])
-def test_tensor_core_projection(kq, oracle, type_id, rows, cols, batch):
+@pytest.mark.parametrize("type_id,rows,cols,batch,wide", [
+    (12, 520, 2048, 64, None), (14, 2048, 4096, 64, None), (8, 300, 2048, 9, None), (30, 640, 2048, 100, None),
+    (0, 200, 512, 33, None), (12, 12352, 2048, 64, None), (14, 130, 256, 129, None),
+    # the 256-row activation tile of prefill batches, forced on and off
+    (12, 12352, 2048, 600, "1"), (12, 12352, 2048, 600, "0"), (14, 2048, 4096, 513, "1"),
+    (8, 300, 2048, 257, "1"), (30, 640, 2048, 300, "1"), (14, 130, 256, 65, "1")])
+def test_tensor_core_projection(kq, oracle, type_id, rows, cols, batch, wide, monkeypatch):
     """Dequant-fused tcgen05 GEMM (three-term BF16 split) against the
     reference's sequential F32 row dots: ragged rows, batches and K."""
     import torch
     from kqb200 import synth
+    if wide is not None:
+        monkeypatch.setenv("KQ_B200_PROJ_WIDE", wide)
     rng = np.random.default_rng(rows + cols + batch)
     q = synth.pack(type_id, rng, rows, cols)
     p = kq.Provider(0)
