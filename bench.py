@@ -624,9 +624,10 @@ def run_b200_prefill(args, rank, world, local_rank):
     T = args.tokens
     gdn_w, qsa_w = prefill_weights()
     prov = kqb200.Provider(local_rank)
-    block = tp.TensorParallelBlock(kqb200, prov, gdn_w, [qsa_w], rank, world, capacity=T)
     lib = kqb200.lib()
     stream = torch.cuda.ExternalStream(lib.kq_b200_get_stream())
+    exchange = tp.torch_exchange(stream) if world > 1 and not args.replicated_indexer else None
+    block = tp.TensorParallelBlock(kqb200, prov, gdn_w, [qsa_w], rank, world, capacity=T, exchange=exchange)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(4321)   # the same input on every rank (replicated activations)
     x = torch.randn(T, gd.hidden, device="cuda", generator=gen)
@@ -674,8 +675,9 @@ def run_b200_prefill(args, rank, world, local_rank):
 
     breakdown = {}
     if args.breakdown:
-        for fam in ("proj", "proj_exact", "gdn_conv", "gdn_recurrence", "qsa_prepare", "qsa_block_keys",
-                    "qsa_score", "qsa_select", "qsa_attend", "qsa_combine"):
+        for fam in ("proj", "proj_exact", "gdn_conv", "gdn_recurrence", "gdn_chunk_prep", "gdn_chunk_state",
+                    "gdn_gate_norm", "qsa_prepare", "qsa_block_keys", "qsa_score", "qsa_select", "qsa_attend",
+                    "qsa_combine"):
             lib.kq_b200_profile_kernel(fam.encode())
             with torch.cuda.stream(stream):
                 step(x)
@@ -729,7 +731,8 @@ def run_b200_prefill(args, rank, world, local_rank):
             "workload": f"config4: 4-layer block (3 GDN + 1 QSA) prefill of {T} tokens, batch 1, "
                         f"projections Q4_K, index BF16, F32 activations/state/KV",
             "parallelism": f"tensor-parallel x{world}: GDN by value-head group, QSA by query-head group "
-                           f"(indexer replicated), NCCL all-reduce (f32) after each out-projection",
+                           f"(indexer {'replicated' if exchange is None else 'scores/top-k split by 64-token chunk, one all-reduce of the selections'}), "
+                           f"NCCL all-reduce (f32) after each out-projection",
             "slice_tokens": args.slice_tokens,
             "l2": "working set per step (GBs of activations, KV, projections) >> 126 MB L2",
             "step_algorithmic_flops": total_flops,
@@ -788,6 +791,8 @@ def main():
     ap.add_argument("--slice-tokens", type=int, default=PREFILL_SLICE,
                     help="prefill tokens per layer call (all-reduce granularity)")
     ap.add_argument("--cpu-tokens", type=int, default=16, help="prefill tokens of the CPU baseline sample")
+    ap.add_argument("--replicated-indexer", action="store_true",
+                    help="prefill at N > 1: every rank selects for every token (no selection exchange)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

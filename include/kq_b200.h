@@ -266,6 +266,30 @@ kq_status kq_b200_qsa_prefill_async(const kq_qsa_config *config,
                                     float *output,
                                     kq_diagnostic *diagnostic);
 
+/* Completes the token selections of a sharded QSA prefill across the ranks:
+ * `words` is a device array of `count` uint32 (every token's selected block
+ * ids, then every token's selection count) that is zero outside the calling
+ * rank's chunks; the function must enqueue on `cuda_stream` a sum over all
+ * ranks into `words` (for example ncclAllReduce) and return 0, or non-zero
+ * on failure.  It is called once per call, on the calling thread. */
+typedef int (*kq_b200_exchange_fn)(void *words, uint64_t count, void *cuda_stream, void *user);
+
+/* kq_b200_qsa_prefill_async for one of `world` tensor-parallel ranks whose
+ * configs hold the same indexer: the block scores and top-k of the 64-token
+ * chunks c with c % world == rank are computed here, `exchange` shares them,
+ * then every chunk's attention runs with its query heads.  world == 1 is
+ * kq_b200_qsa_prefill_async (exchange may be NULL). */
+kq_status kq_b200_qsa_prefill_sharded_async(const kq_qsa_config *config,
+                                            kq_qsa_state *state,
+                                            const float *hidden,
+                                            uint64_t T,
+                                            float *output,
+                                            uint32_t rank,
+                                            uint32_t world,
+                                            kq_b200_exchange_fn exchange,
+                                            void *user,
+                                            kq_diagnostic *diagnostic);
+
 /* Waits for the library stream and reports the first device-side error
  * raised since the previous synchronize. */
 kq_status kq_b200_synchronize(kq_diagnostic *diagnostic);

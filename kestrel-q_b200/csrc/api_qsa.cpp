@@ -178,6 +178,16 @@ struct SelectionCopy {
     uint32_t count = 0;
 };
 
+// Token sharding of the indexer in a tensor-parallel prefill: this rank
+// scores and selects only the 64-token chunks c with c % world == rank, and
+// `exchange` completes the selection rows of every chunk (a sum over ranks
+// of buffers that are zero outside each rank's chunks).
+struct TokenShard {
+    uint32_t rank = 0, world = 1;
+    kq_b200_exchange_fn exchange = nullptr;
+    void *user = nullptr;
+};
+
 // Enqueues the operator for `batch` sequences x `tokens` tokens (batch == 1
 // or tokens == 1).  x / y are device [batch*tokens][H].  When `selection` is
 // non-null (batch == 1) the stream is synchronised after every token and the
@@ -187,7 +197,7 @@ struct SelectionCopy {
 static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const QsaResolved &w,
                              kq_qsa_state *const *states, uint32_t batch, uint32_t tokens, const float *x,
                              float *y, ErrorWord err, std::vector<SelectionCopy> *selection,
-                             kq_diagnostic *diag, bool check_input = false) {
+                             kq_diagnostic *diag, bool check_input = false, const TokenShard *shard = nullptr) {
     const QsaDims d = kernel_dims(cfg);
     const uint32_t H = d.hidden, hd = d.head_dim;
     const uint32_t qw = d.q_heads * hd, kvw = d.kv_heads * hd;
@@ -198,6 +208,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     // kMaxBatch tokens per launch sequence, as batch entries over the same
     // cache (entry i at position L + t0 + i).
     const bool chunked = batch == 1 && tokens > 1 && selection == nullptr;
+    // two passes (index / attention) around the selection exchange
+    const bool sharded = chunked && shard != nullptr && shard->world > 1;
     const uint32_t entries = chunked ? std::min<uint32_t>(tokens, kMaxBatch) : batch;
     uint32_t max_blocks = 1;
     for (uint32_t b = 0; b < batch; ++b)
@@ -215,7 +227,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                         Carve::round((size_t)entries * max_blocks * 4) +
                         Carve::round((size_t)entries * d.topk * 4) + Carve::round((size_t)entries * 4) +
                         Carve::round((size_t)entries * d.q_heads * splits * hd * 4) +
-                        Carve::round((size_t)entries * d.q_heads * splits * 2 * 4) + 8192;
+                        Carve::round((size_t)entries * d.q_heads * splits * 2 * 4) + 8192 +
+                        (sharded ? Carve::round(items * (d.topk + 1) * 4) + Carve::round(items * qw * 4) : 0);
     const size_t partial_floats = std::max(projection_workspace_floats((uint32_t)items, ldp, H),
                                            projection_workspace_floats((uint32_t)items, H, qw));
     void *ws;
@@ -233,6 +246,9 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     float *part_o = cv.take<float>((size_t)entries * d.q_heads * splits * hd);
     float *part_ml = cv.take<float>((size_t)entries * d.q_heads * splits * 2);
     float *partial = partial_floats ? cv.take<float>(partial_floats) : nullptr;
+    // sharded: every token's selection ([T][topk] then [T] counts) and query
+    uint32_t *sel_all = sharded ? cv.take<uint32_t>(items * (d.topk + 1)) : nullptr;
+    float *q_all = sharded ? cv.take<float>(items * qw) : nullptr;
 
     ProjSegments main{};
     main.count = 3;
@@ -274,7 +290,47 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 launch_qsa_block_keys(d, wd, sq, (uint32_t)s->bk_valid, (uint32_t)complete, err, c->stream);
             }
         }
-        if (chunked) {
+        if (sharded) {
+            kq_qsa_state *s = states[0];
+            const QsaSeq seq{s->key, s->value, s->raw, s->block_keys, (uint32_t)s->length, (uint32_t)s->capacity};
+            uint32_t *cnt_all = sel_all + (size_t)tokens * d.topk;
+            KQB_CUDA(cudaMemsetAsync(sel_all, 0, (size_t)tokens * (d.topk + 1) * 4, c->stream), diag, "selection");
+            auto chunk_batch = [&](uint32_t t0, uint32_t n, QsaBatch &qb) {
+                for (uint32_t i = 0; i < n; ++i) {
+                    qb.s[i] = seq;
+                    qb.s[i].length = (uint32_t)s->length + t0 + i;
+                }
+            };
+            // pass 1: cache rows, queries and block keys of every chunk; the
+            // scores and top-k of this rank's chunks
+            for (uint32_t t0 = 0, ci = 0; t0 < tokens; t0 += kMaxBatch, ++ci) {
+                const uint32_t n = std::min<uint32_t>(kMaxBatch, tokens - t0);
+                const uint32_t pos0 = (uint32_t)s->length + t0;
+                QsaBatch qb;
+                chunk_batch(t0, n, qb);
+                launch_qsa_prepare(d, wd, qb, n, proj + (size_t)t0 * ldp, ldp, iproj + (size_t)t0 * ldi, ldi,
+                                   q_all + (size_t)t0 * qw, iqv, false, err, c->stream);
+                launch_qsa_block_keys(d, wd, seq, pos0 / d.block, (pos0 + n) / d.block, err, c->stream);
+                if (ci % shard->world != shard->rank) continue;
+                const uint32_t nb_max = std::max<uint32_t>(1, (pos0 + n) / d.block);
+                launch_qsa_score(d, qb, n, iqv, scores, max_blocks, nb_max, true, err, c->stream);
+                launch_qsa_select(d, qb, n, scores, max_blocks, sel_all + (size_t)t0 * d.topk, cnt_all + t0, err,
+                                  c->stream);
+            }
+            KQB_CUDA(cudaGetLastError(), diag, "QSA index pass");
+            if (shard->exchange(sel_all, (uint64_t)tokens * (d.topk + 1), c->stream, shard->user) != 0)
+                return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "QSA selection exchange failed");
+            // pass 2: attention of every chunk with the exchanged selections
+            for (uint32_t t0 = 0; t0 < tokens; t0 += kMaxBatch) {
+                const uint32_t n = std::min<uint32_t>(kMaxBatch, tokens - t0);
+                QsaBatch qb;
+                chunk_batch(t0, n, qb);
+                launch_qsa_attend(d, qb, n, q_all + (size_t)t0 * qw, sel_all + (size_t)t0 * d.topk, cnt_all + t0,
+                                  part_o, part_ml, splits, err, c->stream);
+                launch_qsa_combine(d, n, part_o, part_ml, splits, proj + (size_t)t0 * ldp, ldp,
+                                   gated + (size_t)t0 * qw, err, c->stream);
+            }
+        } else if (chunked) {
             kq_qsa_state *s = states[0];
             const QsaSeq seq{s->key, s->value, s->raw, s->block_keys, (uint32_t)s->length, (uint32_t)s->capacity};
             for (uint32_t t0 = 0; t0 < tokens; t0 += kMaxBatch) {
@@ -291,7 +347,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                                    c->stream);
                 // keys of the blocks this chunk completes, once all their raw rows are written
                 launch_qsa_block_keys(d, wd, seq, pos0 / d.block, (pos0 + n) / d.block, err, c->stream);
-                launch_qsa_score(d, qb, n, iqv, scores, max_blocks, nb_max, err, c->stream);
+                launch_qsa_score(d, qb, n, iqv, scores, max_blocks, nb_max, true, err, c->stream);
                 launch_qsa_select(d, qb, n, scores, max_blocks, sel, sel_count, err, c->stream);
                 launch_qsa_attend(d, qb, n, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);
                 launch_qsa_combine(d, n, part_o, part_ml, splits, pt, ldp, gated + (size_t)t0 * qw, err,
@@ -314,7 +370,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
             const float *pt = proj + (size_t)t * ldp;      // batch==1: token rows; tokens==1: t==0
             const float *it = iproj + (size_t)t * ldi;
             launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, true, err, c->stream);
-            launch_qsa_score(d, qb, gb, iqv, scores, max_blocks, nb_max, err, c->stream);
+            launch_qsa_score(d, qb, gb, iqv, scores, max_blocks, nb_max, false, err, c->stream);
             launch_qsa_select(d, qb, gb, scores, max_blocks, sel, sel_count, err, c->stream);
             launch_qsa_attend(d, qb, gb, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);
             launch_qsa_combine(d, gb, part_o, part_ml, splits, pt, ldp * tokens, gated + (size_t)t * qw, err,
@@ -659,7 +715,8 @@ kq_status kq_qsa_state_create(const kq_qsa_config *config, uint64_t token_capaci
     if (s == nullptr) return fail(diagnostic, KQ_STATUS_OUT_OF_MEMORY, "could not allocate QSA state object");
     s->device = c->device;
     const size_t kvb = token_capacity * config->kv_per_token * 4, rb = token_capacity * config->raw_per_token * 4;
-    const size_t bkb = std::max<uint64_t>(1, token_capacity / config->dims.block_size) * config->raw_per_token * 4;
+    const size_t bkb = std::max<uint64_t>(4, block_key_ld((uint32_t)token_capacity, config->dims.block_size)) *
+                       config->raw_per_token * 4;
     if (cudaMalloc(&s->key, kvb) != cudaSuccess || cudaMalloc(&s->value, kvb) != cudaSuccess ||
         cudaMalloc(&s->raw, rb) != cudaSuccess || cudaMalloc(&s->block_keys, bkb) != cudaSuccess) {
         cudaGetLastError();
@@ -934,7 +991,15 @@ kq_status kq_b200_qsa_decode_batch(const kq_qsa_config *config, kq_qsa_state *co
 
 kq_status kq_b200_qsa_prefill_async(const kq_qsa_config *config, kq_qsa_state *state, const float *hidden,
                                     uint64_t T, float *output, kq_diagnostic *diagnostic) {
+    return kq_b200_qsa_prefill_sharded_async(config, state, hidden, T, output, 0, 1, nullptr, nullptr, diagnostic);
+}
+
+kq_status kq_b200_qsa_prefill_sharded_async(const kq_qsa_config *config, kq_qsa_state *state, const float *hidden,
+                                            uint64_t T, float *output, uint32_t rank, uint32_t world,
+                                            kq_b200_exchange_fn exchange, void *user, kq_diagnostic *diagnostic) {
     kq_diagnostic_clear(diagnostic);
+    if (world == 0 || rank >= world || (world > 1 && exchange == nullptr))
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "rank < world and an exchange function are required");
     if (!config_valid(config) || !state_valid(state) || state->config != config || hidden == nullptr ||
         output == nullptr || T == 0)
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid config, state and device buffers are required");
@@ -955,8 +1020,13 @@ kq_status kq_b200_qsa_prefill_async(const kq_qsa_config *config, kq_qsa_state *s
                   config->q_norm, config->k_norm, config->iq_norm, config->ik_norm};
     ErrorWord err = c->begin_call();
     kq_qsa_state *states[1] = {state};
+    TokenShard shard;
+    shard.rank = rank;
+    shard.world = world;
+    shard.exchange = exchange;
+    shard.user = user;
     return qsa_enqueue(c, config, w, states, 1, (uint32_t)T, hidden, output, err, nullptr, diagnostic,
-                       /*check_input=*/true);
+                       /*check_input=*/true, &shard);
 }
 
 const char *kq_qsa_checkpoint_kind_name(kq_qsa_checkpoint_kind kind) {

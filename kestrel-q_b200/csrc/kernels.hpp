@@ -191,6 +191,13 @@ struct QsaBatch {
     QsaSeq s[kMaxBatch];
 };
 
+// Row stride (in blocks) of a sequence's feature-major block-key cache
+// [di][ld]: the block count rounded up to a multiple of 4, so that four
+// consecutive blocks of one feature are one aligned 16-byte load.
+__host__ __device__ inline uint32_t block_key_ld(uint32_t capacity, uint32_t block) {
+    return ((capacity / block) + 3u) & ~3u;
+}
+
 struct QsaWeightsDev {
     const float *q_norm, *k_norm, *iq_norm, *ik_norm;
     const float *rope_cos, *rope_sin;   // [positions][rotary/2]
@@ -208,9 +215,12 @@ void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
                         uint32_t ldp, const float *iproj, uint32_t ldi,
                         float *q_out, float *iq_out, bool inline_block_key,
                         ErrorWord err, cudaStream_t stream);
+// `shared_sequence`: every entry is a token of the same sequence (one
+// cache, consecutive positions), so the entries share the block keys.
 void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                       const float *iq, float *scores, uint32_t ld_scores,
-                      uint32_t max_blocks, ErrorWord err, cudaStream_t stream);
+                      uint32_t max_blocks, bool shared_sequence, ErrorWord err,
+                      cudaStream_t stream);
 void launch_qsa_select(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const float *scores, uint32_t ld_scores,
                        uint32_t *selected, uint32_t *selected_count,

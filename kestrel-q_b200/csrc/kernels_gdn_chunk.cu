@@ -14,11 +14,11 @@
 // Phase 1 (gdn_chunk_prep_kernel), one CTA per (value head, chunk): the
 // chunk's L and P (64 x 64 dot products of 128-vectors), then W and U by
 // forward substitution (one thread per column), written to work space.
-// Phase 2 (gdn_chunk_state_kernel), one CTA per (value head, 32-column slice
+// Phase 2 (gdn_chunk_state_kernel), one CTA per (value head, column slice
 // of S): walks the chunks in order with its S slice in shared memory and
 // produces delta, O and the next S with three small matrix products per
-// chunk.  The state columns are independent, so the four slices of a head
-// run in parallel.  Phase 3 (gdn_gate_norm_kernel): gated RMSNorm of every
+// chunk.  The state columns are independent, so the slices of a head run in
+// parallel.  Phase 3 (gdn_gate_norm_kernel): gated RMSNorm of every
 // token, as the recurrence kernel's epilogue.
 //
 // Arithmetic is F32 (FMA); the result differs from the token-by-token order
@@ -33,7 +33,6 @@ namespace {
 
 constexpr int kC = 64;       // tokens per chunk
 constexpr int kD = 128;      // dk = dv
-constexpr int kSlice = 32;   // state columns per phase-2 CTA
 
 __device__ __forceinline__ bool chunk_error_raised(const ErrorWord &e) {
     return *reinterpret_cast<volatile unsigned long long *>(e.word) != 0ull;
@@ -78,8 +77,8 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
     extern __shared__ __align__(16) float cs[];
     float *Ks = cs;                        // [64][128 + 4]
     float *Qs = Ks + kC * (kD + 4);        // [64][128 + 4]
-    float *Ls = Qs + kC * (kD + 4);        // [64][65]
-    float *Gs = Ls + kC * (kC + 1);        // [64]
+    float *Ls = Qs + kC * (kD + 4);        // [64][68]
+    float *Gs = Ls + kC * (kC + 4);        // [64]
     float *Bs = Gs + kC;                   // [64]
     float *Xs = Bs + kC;                   // W then U staging [64][128]
     if (chunk_error_raised(err)) return;
@@ -137,7 +136,7 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
         for (int r = 0; r < 16; ++r) {
             const int j = j0 + r;
             const float f = j <= i ? expf(gi - Gs[j]) : 0.0f;
-            Ls[i * (kC + 1) + j] = j < i ? lk[r] * f : 0.0f;
+            Ls[i * (kC + 4) + j] = j < i ? lk[r] * f : 0.0f;
             wk[kChunkP + i * kC + j] = pq[r] * f;
         }
     }
@@ -148,21 +147,36 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
     }
     if (tid == 0) wk[kChunkTot] = expf(gc);
     __syncthreads();
-    // forward substitution, one column per thread: threads 0..127 W, 128..255 U
+    // right-hand sides, staged before the sequential solve: W rows start as
+    // e^G_i k_i, U rows as v_i (Xs holds W in [0, 64*128), U after it)
+    for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
+        const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
+        const float eg = expf(Gs[r]);
+        const float4 k4 = *reinterpret_cast<const float4 *>(Ks + r * (kD + 4) + c4);
+        *reinterpret_cast<float4 *>(Xs + r * kD + c4) = make_float4(eg * k4.x, eg * k4.y, eg * k4.z, eg * k4.w);
+        float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if ((uint32_t)r < n) v4 = *reinterpret_cast<const float4 *>(vin + (size_t)(t0 + r) * d.value_width + h * kD + c4);
+        *reinterpret_cast<float4 *>(Xs + kC * kD + r * kD + c4) = v4;
+    }
+    __syncthreads();
+    // forward substitution in place, one column per thread: threads 0..127 W,
+    // 128..255 U; row i = beta_i (rhs_i - sum_{j<i} L_ij row_j)
     {
-        const bool is_w = tid < kD;
+        float *X = Xs + (tid < kD ? 0 : kC * kD);
         const int f = tid & (kD - 1);
         for (int i = 0; i < kC; ++i) {
-            float base;
-            if (is_w) {
-                base = expf(Gs[i]) * Ks[i * (kD + 4) + f];
-            } else {
-                base = (uint32_t)i < n ? vin[(size_t)(t0 + i) * d.value_width + h * kD + f] : 0.0f;
-            }
+            const float *Li = Ls + i * (kC + 4);
             float acc = 0.0f;
-            for (int j = 0; j < i; ++j) acc = fmaf(Ls[i * (kC + 1) + j], Xs[(is_w ? 0 : kC * kD) + j * kD + f], acc);
-            // Xs holds W in [0, 64*128) and U in [64*128, 2*64*128)
-            Xs[(is_w ? 0 : kC * kD) + i * kD + f] = Bs[i] * (base - acc);
+            int j = 0;
+            for (; j + 4 <= i; j += 4) {
+                const float4 l4 = *reinterpret_cast<const float4 *>(Li + j);
+                acc = fmaf(l4.x, X[j * kD + f], acc);
+                acc = fmaf(l4.y, X[(j + 1) * kD + f], acc);
+                acc = fmaf(l4.z, X[(j + 2) * kD + f], acc);
+                acc = fmaf(l4.w, X[(j + 3) * kD + f], acc);
+            }
+            for (; j < i; ++j) acc = fmaf(Li[j], X[j * kD + f], acc);
+            X[i * kD + f] = Bs[i] * (X[i * kD + f] - acc);
         }
     }
     __syncthreads();
@@ -173,25 +187,37 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
 }
 
 // ---------------------------------------------------------------- phase 2
-__global__ void __launch_bounds__(256)
+// CW state columns per CTA (32, 16 or 8: fewer value heads per GPU take
+// narrower slices, so that the grid still covers the SMs); 256 threads =
+// CW columns x G = 256 / CW row groups.  The tiles are read as 16-byte
+// vectors along their rows (broadcast within a row group), four K steps per
+// vector.
+template <int CW>
+__global__ void __launch_bounds__(256, 1)
 gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *__restrict__ qk,
                        const float *__restrict__ work, float *__restrict__ obuf, ErrorWord err) {
+    constexpr int G = 256 / CW;      // row groups
+    constexpr int RD = kC / G;       // delta / O rows per thread
+    constexpr int RS = kD / G;       // state rows per thread
+    constexpr int LT = kD + 4;       // row stride of the W / Q / K tiles
+    constexpr int LP = kC + 4;       // row stride of P
+    static_assert(RS % 4 == 0, "state rows in 16-byte groups");
     pdl_wait();
     extern __shared__ __align__(16) float cs[];
-    float *S = cs;                            // [128][32]
-    float *Ws = S + kD * kSlice;              // [64][128 + 4]
-    float *Qs = Ws + kC * (kD + 4);           // [64][128 + 4] (scaled by e^G)
-    float *Ks = Qs + kC * (kD + 4);           // [64][128 + 4] (scaled by e^(G_C - G))
-    float *Ps = Ks + kC * (kD + 4);           // [64][64 + 1]
-    float *Ds = Ps + kC * (kC + 1);           // delta [64][32]
+    float *S = cs;                   // [128][CW]
+    float *Ws = S + kD * CW;         // [64][LT]
+    float *Qs = Ws + kC * LT;        // [64][LT] (scaled by e^G)
+    float *Ks = Qs + kC * LT;        // [64][LT] (scaled by e^(G_C - G))
+    float *Ps = Ks + kC * LT;        // [64][LP]
+    float *Ds = Ps + kC * LP;        // delta [64][CW]
     if (chunk_error_raised(err)) return;
     const uint32_t h = blockIdx.x, sl = blockIdx.y;
     const uint32_t kh = h / d.repeat;
-    const uint32_t col0 = sl * kSlice;
-    const int tid = threadIdx.x, f = tid & 31, grp = tid >> 5;   // 8 groups of 32 threads
+    const uint32_t col0 = sl * CW;
+    const int tid = threadIdx.x, f = tid % CW, grp = tid / CW;
     const float *sin_ = p.rec_in[0] + (size_t)h * kD * kD;
     float *sout = p.rec_out[0] + (size_t)h * kD * kD;
-    for (int i = tid; i < kD * kSlice; i += blockDim.x) S[i] = sin_[(size_t)(i / kSlice) * kD + col0 + i % kSlice];
+    for (int i = tid; i < kD * CW; i += blockDim.x) S[i] = sin_[(size_t)(i / CW) * kD + col0 + i % CW];
     const uint32_t nchunks = (tokens + kC - 1) / kC;
     bool bad = false;
     for (uint32_t c = 0; c < nchunks; ++c) {
@@ -209,48 +235,66 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
             }
             q4.x *= eg; q4.y *= eg; q4.z *= eg; q4.w *= eg;
             k4.x *= egc; k4.y *= egc; k4.z *= egc; k4.w *= egc;
-            *reinterpret_cast<float4 *>(Qs + r * (kD + 4) + c4) = q4;
-            *reinterpret_cast<float4 *>(Ks + r * (kD + 4) + c4) = k4;
-            *reinterpret_cast<float4 *>(Ws + r * (kD + 4) + c4) =
+            *reinterpret_cast<float4 *>(Qs + r * LT + c4) = q4;
+            *reinterpret_cast<float4 *>(Ks + r * LT + c4) = k4;
+            *reinterpret_cast<float4 *>(Ws + r * LT + c4) =
                 *reinterpret_cast<const float4 *>(wk + kChunkW + r * kD + c4);
         }
-        for (int i = tid; i < kC * kC; i += blockDim.x) Ps[(i / kC) * (kC + 1) + i % kC] = wk[kChunkP + i];
+        for (int i = tid; i < kC * (kC / 4); i += blockDim.x) {
+            const int r = i / (kC / 4), c4 = (i % (kC / 4)) * 4;
+            *reinterpret_cast<float4 *>(Ps + r * LP + c4) = *reinterpret_cast<const float4 *>(wk + kChunkP + r * kC + c4);
+        }
         __syncthreads();
-        // delta = U - W S : thread -> column f, rows 8 grp .. 8 grp + 7
+        // delta = U - W S : thread -> column f, rows RD grp .. RD grp + RD - 1
         {
-            float acc[8];
+            float acc[RD];
 #pragma unroll
-            for (int r = 0; r < 8; ++r) acc[r] = 0.f;
-            for (int k = 0; k < kD; ++k) {
-                const float sv = S[k * kSlice + f];
+            for (int r = 0; r < RD; ++r) acc[r] = 0.f;
+#pragma unroll 2
+            for (int k = 0; k < kD; k += 4) {
+                const float s0 = S[k * CW + f], s1 = S[(k + 1) * CW + f], s2 = S[(k + 2) * CW + f],
+                            s3 = S[(k + 3) * CW + f];
 #pragma unroll
-                for (int r = 0; r < 8; ++r) acc[r] = fmaf(Ws[(8 * grp + r) * (kD + 4) + k], sv, acc[r]);
+                for (int r = 0; r < RD; ++r) {
+                    const float4 w4 = *reinterpret_cast<const float4 *>(Ws + (RD * grp + r) * LT + k);
+                    acc[r] = fmaf(w4.w, s3, fmaf(w4.z, s2, fmaf(w4.y, s1, fmaf(w4.x, s0, acc[r]))));
+                }
             }
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const int i = 8 * grp + r;
-                Ds[i * kSlice + f] = wk[kChunkU + i * kD + col0 + f] - acc[r];
+            for (int r = 0; r < RD; ++r) {
+                const int i = RD * grp + r;
+                Ds[i * CW + f] = wk[kChunkU + i * kD + col0 + f] - acc[r];
             }
         }
         __syncthreads();
         // O = (e^G Q) S + P delta for the same rows / column
         {
-            float acc[8];
+            float acc[RD];
 #pragma unroll
-            for (int r = 0; r < 8; ++r) acc[r] = 0.f;
-            for (int k = 0; k < kD; ++k) {
-                const float sv = S[k * kSlice + f];
+            for (int r = 0; r < RD; ++r) acc[r] = 0.f;
+#pragma unroll 2
+            for (int k = 0; k < kD; k += 4) {
+                const float s0 = S[k * CW + f], s1 = S[(k + 1) * CW + f], s2 = S[(k + 2) * CW + f],
+                            s3 = S[(k + 3) * CW + f];
 #pragma unroll
-                for (int r = 0; r < 8; ++r) acc[r] = fmaf(Qs[(8 * grp + r) * (kD + 4) + k], sv, acc[r]);
+                for (int r = 0; r < RD; ++r) {
+                    const float4 q4 = *reinterpret_cast<const float4 *>(Qs + (RD * grp + r) * LT + k);
+                    acc[r] = fmaf(q4.w, s3, fmaf(q4.z, s2, fmaf(q4.y, s1, fmaf(q4.x, s0, acc[r]))));
+                }
             }
-            for (int j = 0; j < kC; ++j) {
-                const float dv = Ds[j * kSlice + f];
+#pragma unroll 2
+            for (int j = 0; j < kC; j += 4) {
+                const float d0 = Ds[j * CW + f], d1 = Ds[(j + 1) * CW + f], d2 = Ds[(j + 2) * CW + f],
+                            d3 = Ds[(j + 3) * CW + f];
 #pragma unroll
-                for (int r = 0; r < 8; ++r) acc[r] = fmaf(Ps[(8 * grp + r) * (kC + 1) + j], dv, acc[r]);
+                for (int r = 0; r < RD; ++r) {
+                    const float4 p4 = *reinterpret_cast<const float4 *>(Ps + (RD * grp + r) * LP + j);
+                    acc[r] = fmaf(p4.w, d3, fmaf(p4.z, d2, fmaf(p4.y, d1, fmaf(p4.x, d0, acc[r]))));
+                }
             }
 #pragma unroll
-            for (int r = 0; r < 8; ++r) {
-                const uint32_t i = 8 * grp + r;
+            for (int r = 0; r < RD; ++r) {
+                const uint32_t i = RD * grp + r;
                 if (i < n) {
                     bad |= !isfinite(acc[r]);
                     obuf[(size_t)(t0 + i) * d.value_width + h * kD + col0 + f] = acc[r];
@@ -258,28 +302,40 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
             }
         }
         __syncthreads();   // every read of the old S is done
-        // S = e^(G_C) S + (e^(G_C - G) K)^T delta : thread -> column f, rows 16 grp .. 16 grp + 15
+        // S = e^(G_C) S + (e^(G_C - G) K)^T delta : thread -> column f, rows RS grp .. RS grp + RS - 1
         {
             const float eg_c = wk[kChunkTot];
-            float acc[16];
+            float acc[RS];
 #pragma unroll
-            for (int r = 0; r < 16; ++r) acc[r] = eg_c * S[(16 * grp + r) * kSlice + f];
+            for (int r = 0; r < RS; ++r) acc[r] = eg_c * S[(RS * grp + r) * CW + f];
+#pragma unroll 2
             for (int i = 0; i < kC; ++i) {
-                const float dv = Ds[i * kSlice + f];
+                const float dv = Ds[i * CW + f];
 #pragma unroll
-                for (int r = 0; r < 16; ++r) acc[r] = fmaf(Ks[i * (kD + 4) + 16 * grp + r], dv, acc[r]);
+                for (int r = 0; r < RS; r += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(Ks + i * LT + RS * grp + r);
+                    acc[r] = fmaf(k4.x, dv, acc[r]);
+                    acc[r + 1] = fmaf(k4.y, dv, acc[r + 1]);
+                    acc[r + 2] = fmaf(k4.z, dv, acc[r + 2]);
+                    acc[r + 3] = fmaf(k4.w, dv, acc[r + 3]);
+                }
             }
 #pragma unroll
-            for (int r = 0; r < 16; ++r) S[(16 * grp + r) * kSlice + f] = acc[r];
+            for (int r = 0; r < RS; ++r) S[(RS * grp + r) * CW + f] = acc[r];
         }
     }
     __syncthreads();
-    for (int i = tid; i < kD * kSlice; i += blockDim.x) {
+    for (int i = tid; i < kD * CW; i += blockDim.x) {
         const float v = S[i];
         bad |= !isfinite(v);
-        sout[(size_t)(i / kSlice) * kD + col0 + i % kSlice] = v;
+        sout[(size_t)(i / CW) * kD + col0 + i % CW] = v;
     }
     if (__syncthreads_or(bad) && tid == 0) chunk_raise(err, kErrNonFinite);
+}
+
+template <int CW>
+static size_t state_smem() {
+    return (size_t)(kD * CW + 3 * kC * (kD + 4) + kC * (kC + 4) + kC * CW) * sizeof(float);
 }
 
 // ---------------------------------------------------------------- phase 3
@@ -313,22 +369,46 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
     KernelTimer timer("gdn_recurrence", stream);
     const uint32_t chunks = (tokens + kC - 1) / kC;
     float *obuf = work + (size_t)chunks * d.value_heads * kChunkFloats;
-    const size_t smem1 = (size_t)(2 * kC * (kD + 4) + kC * (kC + 1) + 2 * kC + 2 * kC * kD) * sizeof(float);
-    const size_t smem2 = (size_t)(kD * kSlice + 3 * kC * (kD + 4) + kC * (kC + 1) + kC * kSlice) * sizeof(float);
+    const size_t smem1 = (size_t)(2 * kC * (kD + 4) + kC * (kC + 4) + 2 * kC + 2 * kC * kD) * sizeof(float);
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
-        cudaFuncSetAttribute(gdn_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)state_smem<32>());
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)state_smem<16>());
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)state_smem<8>());
         attr = true;
     }
-    launch_pdl(gdn_chunk_prep_kernel, dim3(d.value_heads, chunks), 256, smem1, stream, d, tokens, qk, v, beta, logdecay,
-                                                                              work, err);
-    count_launch();
-    launch_pdl(gdn_chunk_state_kernel, dim3(d.value_heads, kD / kSlice), 256, smem2, stream, d, p, tokens, qk, work, obuf,
-                                                                                     err);
-    count_launch();
-    launch_pdl(gdn_gate_norm_kernel, dim3(d.value_heads, tokens), 128, 0, stream, d, w, obuf, proj, ldp, gated, err);
-    count_launch();
+    {
+        KernelTimer t1("gdn_chunk_prep", stream);
+        launch_pdl(gdn_chunk_prep_kernel, dim3(d.value_heads, chunks), 256, smem1, stream, d, tokens, qk, v, beta,
+                   logdecay, work, err);
+        count_launch();
+    }
+    {
+        // the sequential pass: (value heads x column slices) CTAs, slices
+        // narrow enough that the grid reaches about 128 CTAs
+        KernelTimer t2("gdn_chunk_state", stream);
+        if (d.value_heads >= 32) {
+            launch_pdl(gdn_chunk_state_kernel<32>, dim3(d.value_heads, kD / 32), 256, state_smem<32>(), stream, d, p,
+                       tokens, qk, work, obuf, err);
+        } else if (d.value_heads >= 16) {
+            launch_pdl(gdn_chunk_state_kernel<16>, dim3(d.value_heads, kD / 16), 256, state_smem<16>(), stream, d, p,
+                       tokens, qk, work, obuf, err);
+        } else {
+            launch_pdl(gdn_chunk_state_kernel<8>, dim3(d.value_heads, kD / 8), 256, state_smem<8>(), stream, d, p,
+                       tokens, qk, work, obuf, err);
+        }
+        count_launch();
+    }
+    {
+        KernelTimer t3("gdn_gate_norm", stream);
+        launch_pdl(gdn_gate_norm_kernel, dim3(d.value_heads, tokens), 128, 0, stream, d, w, obuf, proj, ldp, gated,
+                   err);
+        count_launch();
+    }
 }
 
 }  // namespace kqb

@@ -19,6 +19,8 @@
 // value from the raw keys on every token.
 #include "kernels.hpp"
 
+#include <cstdlib>
+
 #include <algorithm>
 #include <cmath>
 
@@ -105,7 +107,7 @@ __device__ bool cta_block_key(const QsaDims &d, const QsaWeightsDev &w, const Qs
     for (uint32_t i = threadIdx.x; i < half; i += blockDim.x)
         exact_rope_pair(vec, i, half, w.rope_cos[(size_t)bpos * half + i], w.rope_sin[(size_t)bpos * half + i]);
     __syncthreads();
-    const uint32_t ld = s.capacity / d.block;
+    const uint32_t ld = block_key_ld(s.capacity, d.block);
     for (uint32_t f = threadIdx.x; f < di; f += blockDim.x) {
         if (!isfinite(vec[f])) bad = true;
         s.block_keys[(size_t)f * ld + bi] = vec[f];
@@ -225,58 +227,131 @@ void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
 
 // ------------------------------------------------------------ score
 //
-// grid (ceil(max_blocks / 128), B); one thread per candidate block; the
-// index query of the sequence sits in shared memory.  Score of block bi:
-// sum over index heads of max(0, q_h . key_bi) (sequential dot), / sqrt(di).
+// Score of block bi for one entry: the sum over index heads of
+// max(0, q_h . key_bi) (each dot a sequential F32 sum over the features,
+// products and sums rounded separately as in the reference), / sqrt(di).
+//
+// grid (ceil(max_blocks / 128), ceil(B / E)), 128 threads, one block per
+// thread.  E = 4 when the entries are consecutive tokens of one sequence (a
+// prefill chunk: the same block keys), so each key value read from memory
+// feeds the products of four entries; else 1.  The features go in groups
+// of 8: the thread's 8 key values in registers, each (entry, head)'s 8 query
+// values as two 16-byte shared-memory loads.  Products and sums use the
+// correctly rounded scalar intrinsics in the reference's order (a paired
+// f32x2 multiply + add is not guaranteed to stay unfused, and the scores
+// decide a discrete selection).
 
-__global__ void __launch_bounds__(128)
-qsa_score_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ iq,
+constexpr uint32_t kScoreThreads = 128;
+constexpr uint32_t kScoreHeads = 4;      // index heads per pass
+
+template <int E>
+__global__ void __launch_bounds__(kScoreThreads)
+qsa_score_kernel(QsaDims d, QsaBatch bt, uint32_t batch, const float *__restrict__ iq,
                  float *__restrict__ scores, uint32_t ld_scores, ErrorWord err) {
     pdl_wait();
-    extern __shared__ float qsh[];   // [Hi * di]
+    extern __shared__ __align__(16) float qsh[];   // [E][Hi * di]
     if (qsa_error_raised(err)) return;
-    const uint32_t b = blockIdx.y;
-    const QsaSeq s = bt.s[b];
-    const uint32_t nblocks = (s.length + 1) / d.block;
-    const uint32_t base = blockIdx.x * blockDim.x;
-    if (base >= nblocks) return;
-    const uint32_t n = d.index_heads * d.index_dim;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) qsh[i] = iq[(size_t)b * n + i];
-    __syncthreads();
-    const uint32_t bi = base + threadIdx.x;
-    if (bi >= nblocks) return;
-    const uint32_t ld = s.capacity / d.block;
-    const float *key = s.block_keys + bi;
-    float score = 0.0f;
-    // the index heads' dot products are independent chains: walk them
-    // together (each key feature read once), each in the reference's
-    // sequential feature order; then add the positive ones in head order
-    for (uint32_t h0 = 0; h0 < d.index_heads; h0 += 4) {
-        const uint32_t nh = min(4u, d.index_heads - h0);
-        float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 8
-        for (uint32_t f = 0; f < d.index_dim; ++f) {
-            const float kv = key[(size_t)f * ld];
+    const uint32_t e0 = blockIdx.y * E;
+    const uint32_t ne = min((uint32_t)E, batch - e0);
+    uint32_t nb[E];
+    uint32_t nb_max = 0;
 #pragma unroll
-            for (uint32_t h = 0; h < 4; ++h)
-                if (h < nh) dot[h] = __fadd_rn(dot[h], __fmul_rn(qsh[(h0 + h) * d.index_dim + f], kv));
-        }
-        for (uint32_t h = 0; h < nh; ++h)
-            if (dot[h] > 0.0f) score = __fadd_rn(score, dot[h]);
+    for (int e = 0; e < E; ++e) {
+        nb[e] = (uint32_t)e < ne ? (bt.s[e0 + e].length + 1) / d.block : 0u;
+        nb_max = max(nb_max, nb[e]);
     }
-    score = __fdiv_rn(score, d.sqrt_index_dim);
-    if (!isfinite(score)) qsa_raise(err, kErrNonFinite);
-    scores[(size_t)b * ld_scores + bi] = score;
+    if (blockIdx.x * kScoreThreads >= nb_max) return;   // uniform over the CTA
+    const uint32_t n = d.index_heads * d.index_dim;
+    for (uint32_t i = threadIdx.x; i < E * n; i += kScoreThreads)
+        qsh[i] = i / n < ne ? iq[(size_t)e0 * n + i] : 0.0f;
+    __syncthreads();
+    const uint32_t bi = blockIdx.x * kScoreThreads + threadIdx.x;
+    if (bi >= nb_max) return;
+    const QsaSeq s = bt.s[e0];   // E > 1: every entry reads this sequence's keys
+    const uint32_t ld = block_key_ld(s.capacity, d.block);
+    const float *key = s.block_keys + bi;
+    float score[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) score[e] = 0.0f;
+    for (uint32_t h0 = 0; h0 < d.index_heads; h0 += kScoreHeads) {
+        const uint32_t nh = min(kScoreHeads, d.index_heads - h0);
+        float dot[E][kScoreHeads];
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+#pragma unroll
+            for (uint32_t h = 0; h < kScoreHeads; ++h) dot[e][h] = 0.0f;
+        const float *q0 = qsh + h0 * d.index_dim;
+        // 8-feature groups while the 16-byte query loads stay aligned
+        // (index_dim a multiple of 8), then one feature at a time
+        const uint32_t fvec = (d.index_dim & 7u) == 0 ? d.index_dim : 0u;
+        for (uint32_t f0 = 0; f0 < fvec; f0 += 8) {
+            float kv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) kv[j] = key[(size_t)(f0 + j) * ld];
+#pragma unroll
+            for (int e = 0; e < E; ++e)
+#pragma unroll
+                for (uint32_t h = 0; h < kScoreHeads; ++h) {
+                    if (h < nh) {
+                        const float *qp = q0 + (size_t)e * n + h * d.index_dim + f0;
+                        const float4 qa = *reinterpret_cast<const float4 *>(qp);
+                        const float4 qb = *reinterpret_cast<const float4 *>(qp + 4);
+                        const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                        float acc = dot[e][h];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, __fmul_rn(qv[j], kv[j]));
+                        dot[e][h] = acc;
+                    }
+                }
+        }
+        for (uint32_t f = fvec; f < d.index_dim; ++f) {
+            const float kvf = key[(size_t)f * ld];
+#pragma unroll
+            for (int e = 0; e < E; ++e)
+#pragma unroll
+                for (uint32_t h = 0; h < kScoreHeads; ++h)
+                    if (h < nh)
+                        dot[e][h] = __fadd_rn(dot[e][h], __fmul_rn(q0[(size_t)e * n + h * d.index_dim + f], kvf));
+        }
+        // positive dots, added in head order
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+#pragma unroll
+            for (uint32_t h = 0; h < kScoreHeads; ++h)
+                if (h < nh && dot[e][h] > 0.0f) score[e] = __fadd_rn(score[e], dot[e][h]);
+    }
+    bool bad = false;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        if ((uint32_t)e < ne && bi < nb[e]) {
+            const float sc = __fdiv_rn(score[e], d.sqrt_index_dim);
+            bad |= !isfinite(sc);
+            scores[(size_t)(e0 + e) * ld_scores + bi] = sc;
+        }
+    }
+    if (bad) qsa_raise(err, kErrNonFinite);
 }
 
 void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                       const float *iq, float *scores, uint32_t ld_scores,
-                      uint32_t max_blocks, ErrorWord err, cudaStream_t stream) {
+                      uint32_t max_blocks, bool shared_sequence, ErrorWord err, cudaStream_t stream) {
     if (max_blocks == 0) return;
-    dim3 grid((max_blocks + 127) / 128, batch);
-    size_t smem = (size_t)d.index_heads * d.index_dim * sizeof(float);
+    const size_t n = (size_t)d.index_heads * d.index_dim;
     KernelTimer timer("qsa_score", stream);
-    launch_pdl(qsa_score_kernel, grid, 128, smem, stream, d, b, iq, scores, ld_scores, err);
+    // entries of one sequence share each key load four ways, once that
+    // still leaves about four waves of CTAs
+    const uint32_t xblocks = (max_blocks + kScoreThreads - 1) / kScoreThreads;
+    const char *force = getenv("KQ_B200_SCORE_SHARED");   // tests: 1 = always share when possible
+    const bool big = xblocks * ((batch + 3) / 4) >= 4u * 148u || (force && atoi(force) == 1);
+    if (shared_sequence && batch > 1 && big) {
+        dim3 grid(xblocks, (batch + 3) / 4);
+        launch_pdl(qsa_score_kernel<4>, grid, kScoreThreads, 4 * n * sizeof(float), stream, d, b, batch, iq, scores,
+                   ld_scores, err);
+    } else {
+        dim3 grid((max_blocks + kScoreThreads - 1) / kScoreThreads, batch);
+        launch_pdl(qsa_score_kernel<1>, grid, kScoreThreads, n * sizeof(float), stream, d, b, batch, iq, scores,
+                   ld_scores, err);
+    }
     count_launch();
 }
 
@@ -954,14 +1029,14 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        ErrorWord err, cudaStream_t stream) {
     dim3 grid(splits, d.kv_heads, batch);
     KernelTimer timer("qsa_attend", stream);
-    if (d.head_dim == 256 && d.repeat <= 8 && (d.kv_heads * 256u) % 4u == 0u) {
+    if (d.head_dim == 256 && d.repeat <= 8) {
         static bool attr = false;
         if (!attr) {
             cudaFuncSetAttribute(qsa_attend_mh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMhSmem);
             attr = true;
         }
         launch_pdl(qsa_attend_mh_kernel, grid, 256, kMhSmem, stream, d, b, q, selected, selected_count, partial_o,
-                                                             partial_ml, splits, err);
+                   partial_ml, splits, err);
     } else if (d.head_dim == 256 || d.head_dim == 128) {
         const int hd = (int)d.head_dim;
         const size_t smem = (size_t)(8 * hd + 2 * kAtTile * (hd + 4) + 2 * kAtTile * hd) * sizeof(float);

@@ -310,6 +310,17 @@ def qsa_prefill_async(state: QsaState, x_ptr: int, tokens: int, y_ptr: int) -> N
                                               C.byref(d)), d)
 
 
+def qsa_prefill_sharded_async(state: QsaState, x_ptr: int, tokens: int, y_ptr: int, rank: int, world: int,
+                              exchange) -> None:
+    """Tensor-parallel QSA prefill of one rank: the indexer's scores and top-k
+    of the 64-token chunks c with c % world == rank, `exchange` (an
+    abi.EXCHANGE_FN, kept alive by the caller) sums the selection buffer
+    over the ranks, then attention for every chunk."""
+    d = abi.Diagnostic()
+    abi.check(lib().kq_b200_qsa_prefill_sharded_async(state.layer.handle, state.handle, x_ptr, tokens, y_ptr, rank,
+                                                      world, exchange, None, C.byref(d)), d)
+
+
 def synchronize() -> None:
     d = abi.Diagnostic()
     abi.check(lib().kq_b200_synchronize(C.byref(d)), d)

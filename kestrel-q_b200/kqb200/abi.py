@@ -105,6 +105,8 @@ class QsaSelection(C.Structure):
                 ("selected_token_count", u64), ("tail_count", u64)]
 
 
+# int (*)(void *words, uint64_t count, void *cuda_stream, void *user)
+EXCHANGE_FN = C.CFUNCTYPE(C.c_int, vp, u64, vp, vp)
 SELECTION_OBSERVER = C.CFUNCTYPE(None, C.POINTER(QsaSelection), vp)
 
 _SIGNATURES = {
@@ -177,6 +179,7 @@ _SIGNATURES = {
     "kq_b200_qsa_decode_batch": (C.c_int, [vp, C.POINTER(vp), u32, vp, vp, vp]),
     "kq_b200_gdn_prefill_async": (C.c_int, [vp, vp, vp, u64, vp, vp]),
     "kq_b200_qsa_prefill_async": (C.c_int, [vp, vp, vp, u64, vp, vp]),
+    "kq_b200_qsa_prefill_sharded_async": (C.c_int, [vp, vp, vp, u64, vp, u32, u32, vp, vp, vp]),
     "kq_gdn_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
     "kq_qsa_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
 }

@@ -15,9 +15,12 @@ A QSA layer is split by query-head group: rank r keeps query heads
 [r*Hq/N, (r+1)*Hq/N) with their interleaved [q | gate] rows
 (src/kq_qsa_qwen38.c:569-571) and the key/value heads they read (head h
 reads h // (Hq/Hkv)); ranks that share a key/value head both compute it.
-The indexer (index projections, block keys, scores and top-k) is replicated,
-so every rank selects the same blocks.  The out-projection columns of the
-group again give a partial sum (src/kq_qsa_qwen38.c:783-787).
+Every rank holds the whole indexer (index projections and block keys), so
+any rank can select for any token; with a selection exchange the block
+scores and top-k are split by 64-token chunk (chunk c on rank c % N) and one
+all-reduce of the selection rows gives every rank every token's blocks,
+otherwise each rank selects for every token itself.  The out-projection
+columns of the group again give a partial sum (src/kq_qsa_qwen38.c:783-787).
 
 Each shard is an ordinary layer of the smaller geometry, bound to the
 library through the same config API; only the partial outputs need the
@@ -177,9 +180,16 @@ class TensorParallelBlock:
 
     def __init__(self, kq, provider, gdn_weights: Sequence[synth.GdnLayerWeights],
                  qsa_weights: Sequence[synth.QsaLayerWeights], rank: int, world: int, capacity: int,
-                 layer_base: int = 0):
+                 layer_base: int = 0, exchange: Callable | None = None):
+        """`exchange(words_ptr, count, stream_ptr) -> int`, when given,
+        enqueues on the library stream a sum over the ranks of `count` int32
+        words at `words_ptr` (device memory) and returns 0; the QSA layers
+        then split the indexer's selections by token chunk."""
         self.kq = kq
         self.rank, self.world = rank, world
+        self._exchange = None
+        if exchange is not None and world > 1:
+            self._exchange = kq.abi.EXCHANGE_FN(lambda p, n, st, _u: int(exchange(p, n, st)))
         self.gdn_layers, self.gdn_states = [], []
         self.qsa_layers, self.qsa_states = [], []
         for i, w in enumerate(gdn_weights):
@@ -210,6 +220,9 @@ class TensorParallelBlock:
         """Partial output of layer `index` for `tokens` tokens (asynchronous)."""
         if index < len(self.gdn_states):
             self.kq.gdn_prefill_async(self.gdn_states[index], x_ptr, tokens, y_ptr)
+        elif self._exchange is not None:
+            self.kq.qsa_prefill_sharded_async(self.qsa_states[index - len(self.gdn_states)], x_ptr, tokens, y_ptr,
+                                              self.rank, self.world, self._exchange)
         else:
             self.kq.qsa_prefill_async(self.qsa_states[index - len(self.gdn_states)], x_ptr, tokens, y_ptr)
 
@@ -246,3 +259,26 @@ class TensorParallelBlock:
         for layer in self.gdn_layers + self.qsa_layers:
             layer.close()
         self.gdn_states, self.qsa_states, self.gdn_layers, self.qsa_layers = [], [], [], []
+
+
+class DeviceWords:
+    """A device array the library owns, seen by torch (CUDA array interface)."""
+
+    def __init__(self, ptr: int, count: int, typestr: str = "<i4"):
+        self.__cuda_array_interface__ = {"shape": (int(count),), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None, "stream": None}
+
+
+def torch_exchange(lib_stream):
+    """A selection exchange over torch.distributed (NCCL): an in-place
+    all-reduce (sum) of the words on the library stream."""
+    import torch
+    import torch.distributed as dist
+
+    def exchange(ptr: int, count: int, _stream: int) -> int:
+        t = torch.as_tensor(DeviceWords(ptr, count), device="cuda")
+        with torch.cuda.stream(lib_stream):
+            dist.all_reduce(t)
+        return 0
+
+    return exchange

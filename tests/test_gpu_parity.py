@@ -506,16 +506,18 @@ def test_qsa_prefill_then_decode_selection_exact(kq, oracle):
         prov.close()
 
 
-@pytest.mark.parametrize("hidden,qh,hd,budget,L0,T,seed", [
-    (512, 8, 128, 64, 37, 150, 71),       # three chunks (64, 64, 22), prior context mid-block
-    (2048, 16, 256, 512, 1001, 130, 72),  # config-1 head geometry, head-blocked attention
+@pytest.mark.parametrize("hidden,qh,hd,budget,L0,T,seed,shared", [
+    (512, 8, 128, 64, 37, 150, 71, "0"),       # three chunks (64, 64, 22), prior context mid-block
+    (2048, 16, 256, 512, 1001, 130, 72, "0"),  # config-1 head geometry, head-blocked attention
+    (2048, 16, 256, 512, 1001, 130, 73, "1"),  # scores of four entries per key load
 ])
-def test_qsa_chunked_prefill(kq, oracle, hidden, qh, hd, budget, L0, T, seed):
+def test_qsa_chunked_prefill(kq, oracle, hidden, qh, hd, budget, L0, T, seed, shared, monkeypatch):
     """A prefill without a selection observer runs 64 tokens per launch
     sequence as batch entries over one cache; its outputs, caches and the
     block keys it writes (checked through the bit-exact scores of the next
     decode token) must match the per-token reference."""
     from kqb200 import synth
+    monkeypatch.setenv("KQ_B200_SCORE_SHARED", shared)
     dims = synth.QsaDims(hidden=hidden, query_heads=qh, kv_heads=2, head_dim=hd, index_heads=4, index_dim=128,
                          block=4, budget=budget, max_context=4096, rotary=64)
     weights, prov, layer, w = _qsa_setup(kq, oracle, dims, seed, proj_type=8)

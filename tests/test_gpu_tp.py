@@ -80,3 +80,89 @@ def test_two_gpu_nccl_prefill_runs():
     assert out.returncode == 0, out.stderr[-3000:]
     line = json.loads([ln for ln in out.stdout.splitlines() if ln.startswith("{")][-1])
     assert line["n_gpus"] == 2 and line["value"] > 0 and line["scaling"] == "strong"
+
+
+def _tp_worker(rank, world, port, out_dir):
+    import os
+    import sys
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    for p in (REPO, REPO / "kestrel-q_b200"):
+        sys.path.insert(0, str(p))
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import kqb200 as kq
+    from kqb200 import synth, tp
+    torch.cuda.set_device(rank)
+    d = kq.abi.Diagnostic()
+    kq.abi.check(kq.lib().kq_b200_set_device(rank, __import__("ctypes").byref(d)), d)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    gd, qd, gdn_w, qsa_w, T = _small_block()
+    prov = kq.Provider(rank)
+    stream = torch.cuda.ExternalStream(kq.lib().kq_b200_get_stream())
+    block = tp.TensorParallelBlock(kq, prov, gdn_w, [qsa_w], rank, world, capacity=512,
+                                   exchange=tp.torch_exchange(stream))
+    x = torch.from_numpy(synth.hidden(96, T, gd.hidden)).cuda()
+    bufs = [torch.empty_like(x) for _ in range(block.layer_count)]
+    torch.cuda.synchronize()
+
+    def all_reduce(t):
+        return dist.all_reduce(t, async_op=True)
+
+    with torch.cuda.stream(stream):
+        block.prefill(x, bufs, T, all_reduce, slice_tokens=128)
+    kq.synchronize()
+    torch.cuda.synchronize()
+    if rank == 0:
+        for i, b in enumerate(bufs):
+            np.save(Path(out_dir) / f"layer{i}.npy", b.cpu().numpy())
+        np.save(Path(out_dir) / "x.npy", x.cpu().numpy())
+    block.close()
+    prov.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _small_block():
+    from kqb200 import synth
+    gd = synth.GdnDims(hidden=512, key_heads=4, value_heads=8, key_dim=128, value_dim=128)
+    qd = synth.QsaDims(hidden=512, query_heads=8, kv_heads=2, head_dim=256, index_heads=4, index_dim=128,
+                       block=4, budget=128, max_context=1024, rotary=64)
+    gdn_w = [synth.gdn_layer(90 + l, gd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_Q4_K) for l in range(2)]
+    qsa_w = synth.qsa_layer(95, qd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_BF16)
+    return gd, qd, gdn_w, qsa_w, 300
+
+
+def test_two_gpu_tensor_parallel_block_with_sharded_indexer(oracle, tmp_path):
+    """Two GPUs over NCCL: head-group shards, the QSA scores / top-k split by
+    64-token chunk with one exchange of the selections, an all-reduce after
+    every layer; each layer's reduced output against the oracle layer run on
+    the same input."""
+    import socket
+
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.spawn(_tp_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    gd, qd, gdn_w, qsa_w, T = _small_block()
+    src = np.load(tmp_path / "x.npy")
+    conv = np.zeros(gd.conv_channels * gd.conv_kernel, np.float32)
+    rec = np.zeros(gd.value_heads * gd.key_dim * gd.value_dim, np.float32)
+    for layer in range(3):
+        got = np.load(tmp_path / f"layer{layer}.npy")
+        if layer < 2:
+            st, yo, _, _ = oracle.gdn_run(gd, oracle.gdn_weights_f32(gdn_w[layer]), src, conv, rec)
+        else:
+            z = np.zeros((512, qd.kv_width), np.float32)
+            zr = np.zeros((512, qd.index_dim), np.float32)
+            st, yo, *_ = oracle.qsa_run(qd, oracle.qsa_weights_f32(qsa_w), src, z, z, zr, 0, 512)
+        assert st == 0
+        assert_close(got, yo, f"layer {layer}")
+        src = got
