@@ -281,7 +281,33 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                                partial_floats) &&
             check_input)
             launch_check_finite(x + row0 * H, n_items * H, err, c->stream);
-        launch_projection_exact(index, x + row0 * H, H, iproj, ldi, (uint32_t)n_items, err, c->stream);
+        // sharded: ownership of the index work in groups of `group` chunks,
+        // chunk c on rank (c / group) % world (balanced: later chunks score
+        // more blocks); raw index keys for every token, index queries only
+        // for this rank's chunks
+        const uint32_t nchunks = (tokens + kMaxBatch - 1) / kMaxBatch;
+        const uint32_t group = sharded ? std::max<uint32_t>(1, std::min<uint32_t>(8, nchunks / (4 * shard->world)))
+                                       : 1u;
+        auto owned = [&](uint32_t ci) { return !sharded || (ci / group) % shard->world == shard->rank; };
+        if (!sharded) {
+            launch_projection_exact(index, x + row0 * H, H, iproj, ldi, (uint32_t)n_items, err, c->stream);
+        } else {
+            ProjSegments raw_key{};
+            raw_key.count = 1;
+            raw_key.m[0] = w.ik;
+            raw_key.out_offset[0] = d.index_heads * d.index_dim;
+            launch_projection_exact(raw_key, x, H, iproj, ldi, tokens, err, c->stream);
+            ProjSegments queries{};
+            queries.count = 1;
+            queries.m[0] = w.iq;
+            queries.out_offset[0] = 0;
+            for (uint32_t ci = 0; ci < nchunks; ci += group) {
+                if (!owned(ci)) continue;
+                const uint32_t t0 = ci * kMaxBatch, t1 = std::min<uint32_t>(tokens, (ci + group) * kMaxBatch);
+                launch_projection_exact(queries, x + (size_t)t0 * H, H, iproj + (size_t)t0 * ldi, ldi, t1 - t0, err,
+                                        c->stream);
+            }
+        }
         for (uint32_t b = 0; b < gb; ++b) {
             kq_qsa_state *s = states[g0 + b];
             const uint64_t complete = s->length / d.block;
@@ -309,9 +335,9 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 QsaBatch qb;
                 chunk_batch(t0, n, qb);
                 launch_qsa_prepare(d, wd, qb, n, proj + (size_t)t0 * ldp, ldp, iproj + (size_t)t0 * ldi, ldi,
-                                   q_all + (size_t)t0 * qw, iqv, false, err, c->stream);
+                                   q_all + (size_t)t0 * qw, iqv, false, owned(ci), err, c->stream);
                 launch_qsa_block_keys(d, wd, seq, pos0 / d.block, (pos0 + n) / d.block, err, c->stream);
-                if (ci % shard->world != shard->rank) continue;
+                if (!owned(ci)) continue;
                 const uint32_t nb_max = std::max<uint32_t>(1, (pos0 + n) / d.block);
                 launch_qsa_score(d, qb, n, iqv, scores, max_blocks, nb_max, true, err, c->stream);
                 launch_qsa_select(d, qb, n, scores, max_blocks, sel_all + (size_t)t0 * d.topk, cnt_all + t0, err,
@@ -343,7 +369,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 }
                 const uint32_t nb_max = std::max<uint32_t>(1, (pos0 + n) / d.block);
                 const float *pt = proj + (size_t)t0 * ldp;
-                launch_qsa_prepare(d, wd, qb, n, pt, ldp, iproj + (size_t)t0 * ldi, ldi, qv, iqv, false, err,
+                launch_qsa_prepare(d, wd, qb, n, pt, ldp, iproj + (size_t)t0 * ldi, ldi, qv, iqv, false, true, err,
                                    c->stream);
                 // keys of the blocks this chunk completes, once all their raw rows are written
                 launch_qsa_block_keys(d, wd, seq, pos0 / d.block, (pos0 + n) / d.block, err, c->stream);
@@ -369,7 +395,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
             }
             const float *pt = proj + (size_t)t * ldp;      // batch==1: token rows; tokens==1: t==0
             const float *it = iproj + (size_t)t * ldi;
-            launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, true, err, c->stream);
+            launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, true, true, err,
+                               c->stream);
             launch_qsa_score(d, qb, gb, iqv, scores, max_blocks, nb_max, false, err, c->stream);
             launch_qsa_select(d, qb, gb, scores, max_blocks, sel, sel_count, err, c->stream);
             launch_qsa_attend(d, qb, gb, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);

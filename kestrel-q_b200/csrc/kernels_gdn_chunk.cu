@@ -115,9 +115,11 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
         }
     }
     __syncthreads();
-    // L (strictly lower) and P (lower incl. diagonal): thread -> row i, 16 columns
+    // L (strictly lower) and P (lower incl. diagonal): thread -> row i,
+    // columns j = (tid & 3) + 4 r (the four column groups of a warp read
+    // four consecutive K rows: different banks)
     {
-        const int i = tid >> 2, j0 = (tid & 3) * 16;
+        const int i = tid >> 2, j0 = tid & 3;
         float lk[16], pq[16];
 #pragma unroll
         for (int r = 0; r < 16; ++r) { lk[r] = 0.f; pq[r] = 0.f; }
@@ -126,7 +128,7 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
             const float4 qi = *reinterpret_cast<const float4 *>(Qs + i * (kD + 4) + kk);
 #pragma unroll
             for (int r = 0; r < 16; ++r) {
-                const float4 kj = *reinterpret_cast<const float4 *>(Ks + (j0 + r) * (kD + 4) + kk);
+                const float4 kj = *reinterpret_cast<const float4 *>(Ks + (j0 + 4 * r) * (kD + 4) + kk);
                 lk[r] = fmaf(ki.x, kj.x, fmaf(ki.y, kj.y, fmaf(ki.z, kj.z, fmaf(ki.w, kj.w, lk[r]))));
                 pq[r] = fmaf(qi.x, kj.x, fmaf(qi.y, kj.y, fmaf(qi.z, kj.z, fmaf(qi.w, kj.w, pq[r]))));
             }
@@ -134,7 +136,7 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
         const float gi = Gs[i];
 #pragma unroll
         for (int r = 0; r < 16; ++r) {
-            const int j = j0 + r;
+            const int j = j0 + 4 * r;
             const float f = j <= i ? expf(gi - Gs[j]) : 0.0f;
             Ls[i * (kC + 4) + j] = j < i ? lk[r] * f : 0.0f;
             wk[kChunkP + i * kC + j] = pq[r] * f;
@@ -191,7 +193,21 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
 // narrower slices, so that the grid still covers the SMs); 256 threads =
 // CW columns x G = 256 / CW row groups.  The tiles are read as 16-byte
 // vectors along their rows (broadcast within a row group), four K steps per
-// vector.
+// vector.  Tile loads are cp.async copies issued ahead of use: the next
+// chunk's W during the whole current chunk (two W buffers), the current
+// chunk's Q, P and decay factors during its delta phase, its K during the
+// O phase.  Q and K are stored unscaled; e^G scales a row's Q . S dot and
+// e^(G_C - G) scales delta in the state update.
+
+__device__ __forceinline__ void chunk_cp16(float *smem, const float *gmem, bool valid) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
+    const unsigned n = valid ? 16u : 0u;   // 0: zero fill
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void chunk_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void chunk_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
 template <int CW>
 __global__ void __launch_bounds__(256, 1)
 gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *__restrict__ qk,
@@ -205,11 +221,12 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
     pdl_wait();
     extern __shared__ __align__(16) float cs[];
     float *S = cs;                   // [128][CW]
-    float *Ws = S + kD * CW;         // [64][LT]
-    float *Qs = Ws + kC * LT;        // [64][LT] (scaled by e^G)
-    float *Ks = Qs + kC * LT;        // [64][LT] (scaled by e^(G_C - G))
+    float *Wb = S + kD * CW;         // [2][64][LT]
+    float *Qs = Wb + 2 * kC * LT;    // [64][LT]
+    float *Ks = Qs + kC * LT;        // [64][LT]
     float *Ps = Ks + kC * LT;        // [64][LP]
     float *Ds = Ps + kC * LP;        // delta [64][CW]
+    float *Eg = Ds + kC * CW;        // e^G_i [64], e^(G_C - G_i) [64], e^G_C [4]
     if (chunk_error_raised(err)) return;
     const uint32_t h = blockIdx.x, sl = blockIdx.y;
     const uint32_t kh = h / d.repeat;
@@ -217,34 +234,52 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
     const int tid = threadIdx.x, f = tid % CW, grp = tid / CW;
     const float *sin_ = p.rec_in[0] + (size_t)h * kD * kD;
     float *sout = p.rec_out[0] + (size_t)h * kD * kD;
-    for (int i = tid; i < kD * CW; i += blockDim.x) S[i] = sin_[(size_t)(i / CW) * kD + col0 + i % CW];
     const uint32_t nchunks = (tokens + kC - 1) / kC;
-    bool bad = false;
-    for (uint32_t c = 0; c < nchunks; ++c) {
-        const float *wk = work + ((size_t)c * d.value_heads + h) * kChunkFloats;
-        const uint32_t t0 = c * kC, n = min((uint32_t)kC, tokens - t0);
-        __syncthreads();   // previous chunk done with the tiles
+    auto chunk_work = [&](uint32_t c) { return work + ((size_t)c * d.value_heads + h) * kChunkFloats; };
+    auto load_w = [&](uint32_t c) {
+        const float *wk = chunk_work(c);
+        float *dst = Wb + (c & 1u) * kC * LT;
         for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
             const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
-            const float eg = wk[kChunkEG + r], egc = wk[kChunkEGC + r];
-            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f), k4 = q4;
-            if ((uint32_t)r < n) {
-                const size_t item = t0 + r;
-                q4 = *reinterpret_cast<const float4 *>(qk + (item * 2 + 0) * d.key_width + kh * kD + c4);
-                k4 = *reinterpret_cast<const float4 *>(qk + (item * 2 + 1) * d.key_width + kh * kD + c4);
-            }
-            q4.x *= eg; q4.y *= eg; q4.z *= eg; q4.w *= eg;
-            k4.x *= egc; k4.y *= egc; k4.z *= egc; k4.w *= egc;
-            *reinterpret_cast<float4 *>(Qs + r * LT + c4) = q4;
-            *reinterpret_cast<float4 *>(Ks + r * LT + c4) = k4;
-            *reinterpret_cast<float4 *>(Ws + r * LT + c4) =
-                *reinterpret_cast<const float4 *>(wk + kChunkW + r * kD + c4);
+            chunk_cp16(dst + r * LT + c4, wk + kChunkW + r * kD + c4, true);
+        }
+    };
+    for (int i = tid; i < kD * CW; i += blockDim.x) S[i] = sin_[(size_t)(i / CW) * kD + col0 + i % CW];
+    if (nchunks > 0) load_w(0);
+    chunk_commit();
+    bool bad = false;
+    for (uint32_t c = 0; c < nchunks; ++c) {
+        const float *wk = chunk_work(c);
+        const uint32_t t0 = c * kC, n = min((uint32_t)kC, tokens - t0);
+        __syncthreads();   // the previous chunk is done with Q, K, P, D and its W buffer
+        // group A: Q, P, decay factors of this chunk
+        for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
+            const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
+            const bool in = (uint32_t)r < n;
+            const size_t item = t0 + (in ? r : 0);
+            chunk_cp16(Qs + r * LT + c4, qk + (item * 2 + 0) * d.key_width + kh * kD + c4, in);
         }
         for (int i = tid; i < kC * (kC / 4); i += blockDim.x) {
             const int r = i / (kC / 4), c4 = (i % (kC / 4)) * 4;
-            *reinterpret_cast<float4 *>(Ps + r * LP + c4) = *reinterpret_cast<const float4 *>(wk + kChunkP + r * kC + c4);
+            chunk_cp16(Ps + r * LP + c4, wk + kChunkP + r * kC + c4, true);
         }
+        if (tid < 32) chunk_cp16(Eg + tid * 4, wk + kChunkEG + tid * 4, true);   // e^G, e^(G_C - G)
+        if (tid == 32) chunk_cp16(Eg + 128, wk + kChunkTot, true);                // e^G_C (+ padding)
+        chunk_commit();
+        // group B: K of this chunk
+        for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
+            const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
+            const bool in = (uint32_t)r < n;
+            const size_t item = t0 + (in ? r : 0);
+            chunk_cp16(Ks + r * LT + c4, qk + (item * 2 + 1) * d.key_width + kh * kD + c4, in);
+        }
+        chunk_commit();
+        // group C: W of the next chunk
+        if (c + 1 < nchunks) load_w(c + 1);
+        chunk_commit();
+        chunk_wait<3>();   // this chunk's W (committed one chunk earlier)
         __syncthreads();
+        const float *Ws = Wb + (c & 1u) * kC * LT;
         // delta = U - W S : thread -> column f, rows RD grp .. RD grp + RD - 1
         {
             float acc[RD];
@@ -266,8 +301,9 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
                 Ds[i * CW + f] = wk[kChunkU + i * kD + col0 + f] - acc[r];
             }
         }
+        chunk_wait<2>();   // Q, P, decay factors
         __syncthreads();
-        // O = (e^G Q) S + P delta for the same rows / column
+        // O = e^G (Q S) + P delta for the same rows / column
         {
             float acc[RD];
 #pragma unroll
@@ -282,6 +318,8 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
                     acc[r] = fmaf(q4.w, s3, fmaf(q4.z, s2, fmaf(q4.y, s1, fmaf(q4.x, s0, acc[r]))));
                 }
             }
+#pragma unroll
+            for (int r = 0; r < RD; ++r) acc[r] *= Eg[RD * grp + r];
 #pragma unroll 2
             for (int j = 0; j < kC; j += 4) {
                 const float d0 = Ds[j * CW + f], d1 = Ds[(j + 1) * CW + f], d2 = Ds[(j + 2) * CW + f],
@@ -301,16 +339,17 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
                 }
             }
         }
-        __syncthreads();   // every read of the old S is done
-        // S = e^(G_C) S + (e^(G_C - G) K)^T delta : thread -> column f, rows RS grp .. RS grp + RS - 1
+        chunk_wait<1>();   // K
+        __syncthreads();   // every read of the old S is done; K visible
+        // S = e^(G_C) S + K^T (e^(G_C - G) delta) : thread -> column f, rows RS grp .. RS grp + RS - 1
         {
-            const float eg_c = wk[kChunkTot];
+            const float eg_c = Eg[128];
             float acc[RS];
 #pragma unroll
             for (int r = 0; r < RS; ++r) acc[r] = eg_c * S[(RS * grp + r) * CW + f];
 #pragma unroll 2
             for (int i = 0; i < kC; ++i) {
-                const float dv = Ds[i * CW + f];
+                const float dv = Eg[64 + i] * Ds[i * CW + f];
 #pragma unroll
                 for (int r = 0; r < RS; r += 4) {
                     const float4 k4 = *reinterpret_cast<const float4 *>(Ks + i * LT + RS * grp + r);
@@ -324,6 +363,7 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
             for (int r = 0; r < RS; ++r) S[(RS * grp + r) * CW + f] = acc[r];
         }
     }
+    chunk_wait<0>();
     __syncthreads();
     for (int i = tid; i < kD * CW; i += blockDim.x) {
         const float v = S[i];
@@ -335,7 +375,7 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
 
 template <int CW>
 static size_t state_smem() {
-    return (size_t)(kD * CW + 3 * kC * (kD + 4) + kC * (kC + 4) + kC * CW) * sizeof(float);
+    return (size_t)(kD * CW + 4 * kC * (kD + 4) + kC * (kC + 4) + kC * CW + 2 * kC + 4) * sizeof(float);
 }
 
 // ---------------------------------------------------------------- phase 3

@@ -210,15 +210,24 @@ proj_warp_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
 // in shared memory by cp.async four chunks deep (raw F32 or BF16 weight bytes,
 // F32 activations) and read as 16-byte vectors, four chain steps per load.
 // Other weight types are decoded into the stage synchronously (slow path).
-constexpr int kExRows = 8;            // weight rows per CTA
 constexpr int kExBatch = 64;          // batch rows per CTA
 constexpr int kExK = 128;             // K per staged chunk
-constexpr int kExStages = 4;
 constexpr int kExXStride = kExK + 4;  // padded activation row (conflict-free float4 reads)
 constexpr int kExThreads = 256;
 constexpr size_t kExXBytes = (size_t)kExBatch * kExXStride * 4;   // per stage
-constexpr size_t kExWBytes = (size_t)kExRows * kExK * 4;          // per stage (F32 room)
-constexpr size_t kExSmem = kExStages * (kExXBytes + kExWBytes);
+
+// Tile of TR weight rows x 64 batch rows.  TR = 8 (small batches: more
+// CTAs): a thread owns 2 rows x 1 batch row; TR = 32 (large batches): 4
+// rows x 2 batch rows, eight independent sequential chains per thread, each
+// weight value read from shared memory feeding two of them.
+template <int TR> struct ExTile {
+    static constexpr int stages = TR == 8 ? 4 : 3;
+    static constexpr int rpt = TR == 8 ? 2 : 4;      // rows per thread
+    static constexpr int bpt = TR == 8 ? 1 : 2;      // batch rows per thread
+    static constexpr size_t wbytes = (size_t)TR * kExK * 4;   // per stage (F32 room)
+    static constexpr size_t smem = stages * (kExXBytes + wbytes);
+    static_assert(TR / rpt * (kExBatch / bpt) == kExThreads, "one output group per thread");
+};
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
@@ -226,46 +235,54 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 }
 
 // MODE 0: F32 weights, 1: BF16 weights (both staged raw by cp.async);
-// 2: any type, decoded into F32 by the staging threads.
-template <int MODE>
+// 2: any type, decoded into F32 by the staging threads.  Every output is one
+// sequential F32 chain over K in the reference's order (products and sums
+// rounded separately).
+template <int MODE, int TR>
 __global__ void __launch_bounds__(kExThreads)
 proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                   float *__restrict__ y, uint32_t ldy, uint32_t batch,
                   ErrorWord err) {
+    using TT = ExTile<TR>;
+    constexpr int kStages = TT::stages, RPT = TT::rpt, BPT = TT::bpt;
     pdl_wait();
     extern __shared__ __align__(16) uint8_t ex_smem[];
     if (error_raised(err)) return;
     float *xs_base = reinterpret_cast<float *>(ex_smem);
-    uint8_t *ws_base = ex_smem + kExStages * kExXBytes;
+    uint8_t *ws_base = ex_smem + kStages * kExXBytes;
     int seg = 0;
     while (seg + 1 < segs.count && blockIdx.x >= segs.tile_start[seg + 1]) ++seg;
     const QMatrix m = segs.m[seg];
-    const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * kExRows;
+    const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * TR;
     const uint32_t b0 = blockIdx.y * kExBatch;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rp = warp >> 1;                        // row pair 0..3
-    const int bl = (warp & 1) * 32 + lane;           // batch row within the tile
+    // the thread's rows rb .. rb + RPT - 1 (warp-uniform: broadcast weight
+    // reads) and batch rows bb + 32 j
+    const int rb = TR == 8 ? 2 * (warp >> 1) : 4 * warp;
+    const int bb = TR == 8 ? (warp & 1) * 32 + lane : lane;
     const uint32_t nchunks = (m.cols + kExK - 1) / kExK;
     const bool xvec = (ldx % 4u) == 0u && (reinterpret_cast<uintptr_t>(x) & 15u) == 0u;
     constexpr uint32_t kElem = MODE == 1 ? 2u : 4u;   // staged weight bytes per value
 
     auto stage = [&](uint32_t c) {
-        const int buf = c % kExStages;
+        const int buf = c % kStages;
         const uint32_t k0 = c * kExK;
         float *xs = xs_base + (size_t)buf * kExBatch * kExXStride;
-        uint8_t *ws = ws_base + (size_t)buf * kExWBytes;
-        // weights: 8 rows x 128 values
+        uint8_t *ws = ws_base + (size_t)buf * TT::wbytes;
+        // weights: TR rows x 128 values
         if constexpr (MODE == 2) {
-            const int r = tid >> 5, kk = (tid & 31) * 4;
-            const uint32_t grow = row0 + r;
-            float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (grow < m.rows && k0 + kk < m.cols)
-                decode_any(m, m.data + (size_t)grow * m.row_bytes, k0 + kk, min(4u, m.cols - (k0 + kk)), w);
-            for (int e = 0; e < 4; ++e)
-                reinterpret_cast<float *>(ws)[r * kExK + kk + e] = (k0 + kk + e < m.cols) ? w[e] : 0.0f;
+            for (int i = tid; i < TR * (kExK / 4); i += kExThreads) {
+                const int r = i / (kExK / 4), kk = (i % (kExK / 4)) * 4;
+                const uint32_t grow = row0 + r;
+                float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (grow < m.rows && k0 + kk < m.cols)
+                    decode_any(m, m.data + (size_t)grow * m.row_bytes, k0 + kk, min(4u, m.cols - (k0 + kk)), w);
+                for (int e = 0; e < 4; ++e)
+                    reinterpret_cast<float *>(ws)[r * kExK + kk + e] = (k0 + kk + e < m.cols) ? w[e] : 0.0f;
+            }
         } else {
             constexpr int kPieces = kExK * kElem / 16;   // 16-byte pieces per row
-            for (int i = tid; i < kExRows * kPieces; i += kExThreads) {
+            for (int i = tid; i < TR * kPieces; i += kExThreads) {
                 const int r = i / kPieces, pc = i % kPieces;
                 const uint32_t grow = row0 + r, k = k0 + pc * (16 / kElem);
                 uint8_t *dst = ws + (size_t)r * kExK * kElem + pc * 16;
@@ -287,9 +304,9 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
         }
         // activations: 64 rows x 128 values
         for (int i = tid; i < kExBatch * (kExK / 4); i += kExThreads) {
-            const int bb = i / (kExK / 4), q4 = (i % (kExK / 4)) * 4;
-            const uint32_t gb = b0 + bb, k = k0 + q4;
-            float *dst = xs + (size_t)bb * kExXStride + q4;
+            const int br = i / (kExK / 4), q4 = (i % (kExK / 4)) * 4;
+            const uint32_t gb = b0 + br, k = k0 + q4;
+            float *dst = xs + (size_t)br * kExXStride + q4;
             if (xvec && gb < batch && k + 4 <= m.cols) {
                 cp_async16(dst, x + (size_t)gb * ldx + k);
             } else {
@@ -300,22 +317,26 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
     };
     auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
 
-    float acc0 = 0.0f, acc1 = 0.0f;
-    for (uint32_t c = 0; c < kExStages - 1; ++c) {
+    float acc[RPT][BPT];
+#pragma unroll
+    for (int r = 0; r < RPT; ++r)
+#pragma unroll
+        for (int j = 0; j < BPT; ++j) acc[r][j] = 0.0f;
+    for (uint32_t c = 0; c < (uint32_t)kStages - 1; ++c) {
         if (c < nchunks) stage(c);
         commit();
     }
     for (uint32_t c = 0; c < nchunks; ++c) {
-        if (c + kExStages - 1 < nchunks) stage(c + kExStages - 1);
+        if (c + kStages - 1 < nchunks) stage(c + kStages - 1);
         commit();
-        asm volatile("cp.async.wait_group %0;" ::"n"(kExStages - 1) : "memory");
+        asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 1) : "memory");
         __syncthreads();
-        const int buf = c % kExStages;
+        const int buf = c % kStages;
         const uint32_t kc = min((uint32_t)kExK, m.cols - c * kExK);
-        const float *xv = xs_base + (size_t)buf * kExBatch * kExXStride + (size_t)bl * kExXStride;
-        const uint8_t *ws = ws_base + (size_t)buf * kExWBytes;
-        const uint8_t *w0 = ws + (size_t)(2 * rp) * kExK * kElem, *w1 = w0 + (size_t)kExK * kElem;
-        auto wq = [&](const uint8_t *row, int k) {   // 4 F32 weights at k
+        const float *xv = xs_base + (size_t)buf * kExBatch * kExXStride + (size_t)bb * kExXStride;
+        const uint8_t *ws = ws_base + (size_t)buf * TT::wbytes + (size_t)rb * kExK * kElem;
+        auto wq = [&](int r, int k) {   // 4 F32 weights of row rb + r at k
+            const uint8_t *row = ws + (size_t)r * kExK * kElem;
             if constexpr (MODE == 1) {
                 const uint2 u = *reinterpret_cast<const uint2 *>(row + (size_t)k * 2);
                 return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
@@ -325,39 +346,52 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
             }
         };
         if (kc == (uint32_t)kExK) {
-#pragma unroll 4
+#pragma unroll 2
             for (int k = 0; k < kExK; k += 4) {
-                const float4 a = wq(w0, k), b = wq(w1, k);
-                const float4 v = *reinterpret_cast<const float4 *>(xv + k);
-                acc0 = __fadd_rn(acc0, __fmul_rn(a.x, v.x));
-                acc1 = __fadd_rn(acc1, __fmul_rn(b.x, v.x));
-                acc0 = __fadd_rn(acc0, __fmul_rn(a.y, v.y));
-                acc1 = __fadd_rn(acc1, __fmul_rn(b.y, v.y));
-                acc0 = __fadd_rn(acc0, __fmul_rn(a.z, v.z));
-                acc1 = __fadd_rn(acc1, __fmul_rn(b.z, v.z));
-                acc0 = __fadd_rn(acc0, __fmul_rn(a.w, v.w));
-                acc1 = __fadd_rn(acc1, __fmul_rn(b.w, v.w));
+                float xv4[BPT][4];
+#pragma unroll
+                for (int j = 0; j < BPT; ++j) {
+                    const float4 v = *reinterpret_cast<const float4 *>(xv + (size_t)j * 32 * kExXStride + k);
+                    xv4[j][0] = v.x; xv4[j][1] = v.y; xv4[j][2] = v.z; xv4[j][3] = v.w;
+                }
+#pragma unroll
+                for (int r = 0; r < RPT; ++r) {
+                    const float4 a = wq(r, k);
+                    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+#pragma unroll
+                        for (int j = 0; j < BPT; ++j) acc[r][j] = __fadd_rn(acc[r][j], __fmul_rn(av[e], xv4[j][e]));
+                }
             }
         } else {
             for (uint32_t k = 0; k < kc; k += 4) {
-                const float4 a = wq(w0, (int)k), b = wq(w1, (int)k);
-                const float4 v = *reinterpret_cast<const float4 *>(xv + k);
-                const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
-                const float vv[4] = {v.x, v.y, v.z, v.w};
                 for (uint32_t e = 0; e < 4 && k + e < kc; ++e) {
-                    acc0 = __fadd_rn(acc0, __fmul_rn(av[e], vv[e]));
-                    acc1 = __fadd_rn(acc1, __fmul_rn(bv[e], vv[e]));
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) {
+                        const float4 a = wq(r, (int)k);
+                        const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                        for (int j = 0; j < BPT; ++j)
+                            acc[r][j] = __fadd_rn(acc[r][j],
+                                                  __fmul_rn(av[e], xv[(size_t)j * 32 * kExXStride + k + e]));
+                    }
                 }
             }
         }
         __syncthreads();
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    const uint32_t b = b0 + bl;
-    if (b >= batch) return;
-    const uint32_t r0 = row0 + 2 * rp;
-    if (r0 < m.rows) y[(size_t)b * ldy + segs.out_offset[seg] + r0] = acc0;
-    if (r0 + 1 < m.rows) y[(size_t)b * ldy + segs.out_offset[seg] + r0 + 1] = acc1;
+#pragma unroll
+    for (int j = 0; j < BPT; ++j) {
+        const uint32_t b = b0 + bb + 32 * j;
+        if (b >= batch) continue;
+#pragma unroll
+        for (int r = 0; r < RPT; ++r) {
+            const uint32_t row = row0 + rb + r;
+            if (row < m.rows) y[(size_t)b * ldy + segs.out_offset[seg] + row] = acc[r][j];
+        }
+    }
 }
 
 static void fill_tile_starts(ProjSegments &s, uint32_t unit) {
@@ -402,13 +436,11 @@ bool launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
     return false;
 }
 
-void launch_projection_exact(const ProjSegments &in, const float *x,
-                             uint32_t ldx, float *y, uint32_t ldy,
-                             uint32_t batch, ErrorWord err,
-                             cudaStream_t stream) {
+template <int TR>
+static void launch_exact_tiles(const ProjSegments &in, const float *x, uint32_t ldx, float *y, uint32_t ldy,
+                               uint32_t batch, ErrorWord err, cudaStream_t stream) {
     ProjSegments segs = in;
-    KernelTimer timer("proj_exact", stream);
-    fill_tile_starts(segs, kExRows);
+    fill_tile_starts(segs, TR);
     dim3 grid(segs.tile_start[segs.count], (batch + kExBatch - 1) / kExBatch);
     // one launch per mode; segments of mixed types go through the generic mode
     int mode = 0;
@@ -418,19 +450,32 @@ void launch_projection_exact(const ProjSegments &in, const float *x,
         const int mi = !aligned ? 2 : q.type == kTypeF32 ? 0 : q.type == kTypeBF16 ? 1 : 2;
         mode = i == 0 ? mi : (mode == mi ? mode : 2);
     }
+    constexpr size_t smem = ExTile<TR>::smem;
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(proj_exact_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kExSmem);
-        cudaFuncSetAttribute(proj_exact_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kExSmem);
-        cudaFuncSetAttribute(proj_exact_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kExSmem);
+        cudaFuncSetAttribute(proj_exact_kernel<0, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(proj_exact_kernel<1, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(proj_exact_kernel<2, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = true;
     }
     if (mode == 0)
-        launch_pdl(proj_exact_kernel<0>, grid, kExThreads, kExSmem, stream, segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<0, TR>, grid, kExThreads, smem, stream, segs, x, ldx, y, ldy, batch, err);
     else if (mode == 1)
-        launch_pdl(proj_exact_kernel<1>, grid, kExThreads, kExSmem, stream, segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<1, TR>, grid, kExThreads, smem, stream, segs, x, ldx, y, ldy, batch, err);
     else
-        launch_pdl(proj_exact_kernel<2>, grid, kExThreads, kExSmem, stream, segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<2, TR>, grid, kExThreads, smem, stream, segs, x, ldx, y, ldy, batch, err);
+}
+
+void launch_projection_exact(const ProjSegments &in, const float *x,
+                             uint32_t ldx, float *y, uint32_t ldy,
+                             uint32_t batch, ErrorWord err,
+                             cudaStream_t stream) {
+    KernelTimer timer("proj_exact", stream);
+    // 32-row tiles once the batch alone gives several CTAs per SM
+    if (batch >= 1024)
+        launch_exact_tiles<32>(in, x, ldx, y, ldy, batch, err, stream);
+    else
+        launch_exact_tiles<8>(in, x, ldx, y, ldy, batch, err, stream);
     count_launch();
 }
 

@@ -130,7 +130,7 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
                    const float *__restrict__ proj, uint32_t ldp,
                    const float *__restrict__ iproj, uint32_t ldi,
                    float *__restrict__ q_out, float *__restrict__ iq_out,
-                   bool inline_block_key, ErrorWord err) {
+                   bool inline_block_key, bool index_queries, ErrorWord err) {
     pdl_wait();
     extern __shared__ float sh[];   // max(d, di) floats + 1
     if (qsa_error_raised(err)) return;
@@ -168,6 +168,7 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
             s.value[(size_t)pos * kvw + h * hd + i] = v;
         }
     } else if ((role -= d.kv_heads) < d.index_heads) {
+        if (!index_queries) return;   // whole CTA: this entry is scored elsewhere
         const uint32_t h = role;
         for (uint32_t i = threadIdx.x; i < di; i += blockDim.x) vec[i] = irow[h * di + i];
         __syncthreads();
@@ -193,12 +194,12 @@ void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
                         const QsaBatch &b, uint32_t batch, const float *proj,
                         uint32_t ldp, const float *iproj, uint32_t ldi,
                         float *q_out, float *iq_out, bool inline_block_key,
-                        ErrorWord err, cudaStream_t stream) {
+                        bool index_queries, ErrorWord err, cudaStream_t stream) {
     size_t smem = (std::max(d.head_dim, d.index_dim) + 1) * sizeof(float);
     dim3 grid(batch, d.q_heads + d.kv_heads + d.index_heads + 1);
     KernelTimer timer("qsa_prepare", stream);
     launch_pdl(qsa_prepare_kernel, grid, kPrepThreads, smem, stream, d, w, b, proj, ldp, iproj, ldi,
-               q_out, iq_out, inline_block_key, err);
+               q_out, iq_out, inline_block_key, index_queries, err);
     count_launch();
 }
 

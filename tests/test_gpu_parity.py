@@ -510,6 +510,7 @@ def test_qsa_prefill_then_decode_selection_exact(kq, oracle):
     (512, 8, 128, 64, 37, 150, 71, "0"),       # three chunks (64, 64, 22), prior context mid-block
     (2048, 16, 256, 512, 1001, 130, 72, "0"),  # config-1 head geometry, head-blocked attention
     (2048, 16, 256, 512, 1001, 130, 73, "1"),  # scores of four entries per key load
+    (512, 8, 128, 64, 5, 1100, 74, "1"),       # >= 1024 tokens: 32-row tiles of the exact index projection
 ])
 def test_qsa_chunked_prefill(kq, oracle, hidden, qh, hd, budget, L0, T, seed, shared, monkeypatch):
     """A prefill without a selection observer runs 64 tokens per launch
