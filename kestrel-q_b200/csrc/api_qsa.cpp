@@ -182,6 +182,9 @@ struct SelectionCopy {
 // scores and selects only the 64-token chunks c with c % world == rank, and
 // `exchange` completes the selection rows of every chunk (a sum over ranks
 // of buffers that are zero outside each rank's chunks).
+// Tokens per launch sequence of a one-sequence prefill (uniform batches).
+constexpr uint32_t kPrefillEntries = 1024;
+
 struct TokenShard {
     uint32_t rank = 0, world = 1;
     kq_b200_exchange_fn exchange = nullptr;
@@ -204,20 +207,28 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     const uint32_t ldp = 2 * qw + 2 * kvw;
     const uint32_t ldi = d.index_heads * d.index_dim + d.index_dim;
     const size_t items = (size_t)batch * tokens;
-    // A prefill of one sequence without a selection observer runs up to
-    // kMaxBatch tokens per launch sequence, as batch entries over the same
+    // A prefill of one sequence without a selection observer runs `unit`
+    // tokens per launch sequence, as entries of a uniform batch over the same
     // cache (entry i at position L + t0 + i).
     const bool chunked = batch == 1 && tokens > 1 && selection == nullptr;
     // two passes (index / attention) around the selection exchange
     const bool sharded = chunked && shard != nullptr && shard->world > 1;
-    const uint32_t entries = chunked ? std::min<uint32_t>(tokens, kMaxBatch) : batch;
+    // sharded: the index work (index queries, scores, top-k) is owned in
+    // groups of `group` 64-token chunks, group u on rank u % world
+    // (interleaved: later chunks score more blocks); one launch sequence per
+    // group
+    const uint32_t nchunks = (tokens + 63) / 64;
+    const uint32_t group = sharded ? std::max<uint32_t>(1, std::min<uint32_t>(8, nchunks / (4 * shard->world))) : 1u;
+    const uint32_t unit = sharded ? group * 64u : kPrefillEntries;
+    auto owned = [&](uint32_t t0) { return !sharded || (t0 / unit) % shard->world == shard->rank; };
+    const uint32_t entries = chunked ? std::min<uint32_t>(tokens, unit) : batch;
     uint32_t max_blocks = 1;
     for (uint32_t b = 0; b < batch; ++b)
         max_blocks = std::max<uint32_t>(max_blocks, (uint32_t)((states[b]->length + tokens) / d.block));
     // about 16 tiles of 16 selected tokens per split, and at least two waves
     // of CTAs over the 148 SMs for small batches
     const uint32_t tiles = (d.sel_capacity + 15) / 16;
-    const uint32_t per_seq = std::min<uint32_t>(entries, kMaxBatch) * d.kv_heads;
+    const uint32_t per_seq = entries * d.kv_heads;
     // (the head-blocked attention kernel takes at most 32 tiles per split)
     uint32_t splits = std::max<uint32_t>((tiles + 15) / 16, (3 * 148 + per_seq - 1) / per_seq);
     splits = std::max<uint32_t>(1, std::min<uint32_t>(splits, tiles));
@@ -281,14 +292,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                                partial_floats) &&
             check_input)
             launch_check_finite(x + row0 * H, n_items * H, err, c->stream);
-        // sharded: ownership of the index work in groups of `group` chunks,
-        // chunk c on rank (c / group) % world (balanced: later chunks score
-        // more blocks); raw index keys for every token, index queries only
-        // for this rank's chunks
-        const uint32_t nchunks = (tokens + kMaxBatch - 1) / kMaxBatch;
-        const uint32_t group = sharded ? std::max<uint32_t>(1, std::min<uint32_t>(8, nchunks / (4 * shard->world)))
-                                       : 1u;
-        auto owned = [&](uint32_t ci) { return !sharded || (ci / group) % shard->world == shard->rank; };
+        // sharded: raw index keys for every token, index queries only for
+        // this rank's groups
         if (!sharded) {
             launch_projection_exact(index, x + row0 * H, H, iproj, ldi, (uint32_t)n_items, err, c->stream);
         } else {
@@ -301,10 +306,10 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
             queries.count = 1;
             queries.m[0] = w.iq;
             queries.out_offset[0] = 0;
-            for (uint32_t ci = 0; ci < nchunks; ci += group) {
-                if (!owned(ci)) continue;
-                const uint32_t t0 = ci * kMaxBatch, t1 = std::min<uint32_t>(tokens, (ci + group) * kMaxBatch);
-                launch_projection_exact(queries, x + (size_t)t0 * H, H, iproj + (size_t)t0 * ldi, ldi, t1 - t0, err,
+            for (uint32_t t0 = 0; t0 < tokens; t0 += unit) {
+                if (!owned(t0)) continue;
+                const uint32_t n = std::min<uint32_t>(unit, tokens - t0);
+                launch_projection_exact(queries, x + (size_t)t0 * H, H, iproj + (size_t)t0 * ldi, ldi, n, err,
                                         c->stream);
             }
         }
@@ -316,68 +321,54 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 launch_qsa_block_keys(d, wd, sq, (uint32_t)s->bk_valid, (uint32_t)complete, err, c->stream);
             }
         }
-        if (sharded) {
+        if (chunked) {
             kq_qsa_state *s = states[0];
             const QsaSeq seq{s->key, s->value, s->raw, s->block_keys, (uint32_t)s->length, (uint32_t)s->capacity};
-            uint32_t *cnt_all = sel_all + (size_t)tokens * d.topk;
-            KQB_CUDA(cudaMemsetAsync(sel_all, 0, (size_t)tokens * (d.topk + 1) * 4, c->stream), diag, "selection");
-            auto chunk_batch = [&](uint32_t t0, uint32_t n, QsaBatch &qb) {
-                for (uint32_t i = 0; i < n; ++i) {
-                    qb.s[i] = seq;
-                    qb.s[i].length = (uint32_t)s->length + t0 + i;
-                }
+            auto uniform_batch = [&](uint32_t t0) {
+                QsaBatch qb;
+                qb.s[0] = seq;
+                qb.s[0].length = (uint32_t)s->length + t0;
+                qb.uniform = 1;
+                return qb;
             };
-            // pass 1: cache rows, queries and block keys of every chunk; the
-            // scores and top-k of this rank's chunks
-            for (uint32_t t0 = 0, ci = 0; t0 < tokens; t0 += kMaxBatch, ++ci) {
-                const uint32_t n = std::min<uint32_t>(kMaxBatch, tokens - t0);
+            uint32_t *cnt_all = sharded ? sel_all + (size_t)tokens * d.topk : nullptr;
+            if (sharded)
+                KQB_CUDA(cudaMemsetAsync(sel_all, 0, (size_t)tokens * (d.topk + 1) * 4, c->stream), diag, "selection");
+            // pass 1 (the only pass without sharding): cache rows, queries and
+            // block keys of every group; scores and top-k of the owned ones
+            for (uint32_t t0 = 0; t0 < tokens; t0 += unit) {
+                const uint32_t n = std::min<uint32_t>(unit, tokens - t0);
                 const uint32_t pos0 = (uint32_t)s->length + t0;
-                QsaBatch qb;
-                chunk_batch(t0, n, qb);
-                launch_qsa_prepare(d, wd, qb, n, proj + (size_t)t0 * ldp, ldp, iproj + (size_t)t0 * ldi, ldi,
-                                   q_all + (size_t)t0 * qw, iqv, false, owned(ci), err, c->stream);
-                launch_qsa_block_keys(d, wd, seq, pos0 / d.block, (pos0 + n) / d.block, err, c->stream);
-                if (!owned(ci)) continue;
-                const uint32_t nb_max = std::max<uint32_t>(1, (pos0 + n) / d.block);
-                launch_qsa_score(d, qb, n, iqv, scores, max_blocks, nb_max, true, err, c->stream);
-                launch_qsa_select(d, qb, n, scores, max_blocks, sel_all + (size_t)t0 * d.topk, cnt_all + t0, err,
-                                  c->stream);
-            }
-            KQB_CUDA(cudaGetLastError(), diag, "QSA index pass");
-            if (shard->exchange(sel_all, (uint64_t)tokens * (d.topk + 1), c->stream, shard->user) != 0)
-                return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "QSA selection exchange failed");
-            // pass 2: attention of every chunk with the exchanged selections
-            for (uint32_t t0 = 0; t0 < tokens; t0 += kMaxBatch) {
-                const uint32_t n = std::min<uint32_t>(kMaxBatch, tokens - t0);
-                QsaBatch qb;
-                chunk_batch(t0, n, qb);
-                launch_qsa_attend(d, qb, n, q_all + (size_t)t0 * qw, sel_all + (size_t)t0 * d.topk, cnt_all + t0,
-                                  part_o, part_ml, splits, err, c->stream);
-                launch_qsa_combine(d, n, part_o, part_ml, splits, proj + (size_t)t0 * ldp, ldp,
-                                   gated + (size_t)t0 * qw, err, c->stream);
-            }
-        } else if (chunked) {
-            kq_qsa_state *s = states[0];
-            const QsaSeq seq{s->key, s->value, s->raw, s->block_keys, (uint32_t)s->length, (uint32_t)s->capacity};
-            for (uint32_t t0 = 0; t0 < tokens; t0 += kMaxBatch) {
-                const uint32_t n = std::min<uint32_t>(kMaxBatch, tokens - t0);
-                const uint32_t pos0 = (uint32_t)s->length + t0;
-                QsaBatch qb;
-                for (uint32_t i = 0; i < n; ++i) {
-                    qb.s[i] = seq;
-                    qb.s[i].length = pos0 + i;
-                }
-                const uint32_t nb_max = std::max<uint32_t>(1, (pos0 + n) / d.block);
+                const QsaBatch qb = uniform_batch(t0);
                 const float *pt = proj + (size_t)t0 * ldp;
-                launch_qsa_prepare(d, wd, qb, n, pt, ldp, iproj + (size_t)t0 * ldi, ldi, qv, iqv, false, true, err,
-                                   c->stream);
-                // keys of the blocks this chunk completes, once all their raw rows are written
+                float *qdst = sharded ? q_all + (size_t)t0 * qw : qv;
+                launch_qsa_prepare(d, wd, qb, n, pt, ldp, iproj + (size_t)t0 * ldi, ldi, qdst, iqv, false, owned(t0),
+                                   err, c->stream);
+                // keys of the blocks this group completes, once all their raw rows are written
                 launch_qsa_block_keys(d, wd, seq, pos0 / d.block, (pos0 + n) / d.block, err, c->stream);
+                if (!owned(t0)) continue;
+                const uint32_t nb_max = std::max<uint32_t>(1, (pos0 + n) / d.block);
+                uint32_t *sdst = sharded ? sel_all + (size_t)t0 * d.topk : sel;
+                uint32_t *cdst = sharded ? cnt_all + t0 : sel_count;
                 launch_qsa_score(d, qb, n, iqv, scores, max_blocks, nb_max, true, err, c->stream);
-                launch_qsa_select(d, qb, n, scores, max_blocks, sel, sel_count, err, c->stream);
+                launch_qsa_select(d, qb, n, scores, max_blocks, sdst, cdst, err, c->stream);
+                if (sharded) continue;
                 launch_qsa_attend(d, qb, n, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);
-                launch_qsa_combine(d, n, part_o, part_ml, splits, pt, ldp, gated + (size_t)t0 * qw, err,
-                                   c->stream);
+                launch_qsa_combine(d, n, part_o, part_ml, splits, pt, ldp, gated + (size_t)t0 * qw, err, c->stream);
+            }
+            if (sharded) {
+                KQB_CUDA(cudaGetLastError(), diag, "QSA index pass");
+                if (shard->exchange(sel_all, (uint64_t)tokens * (d.topk + 1), c->stream, shard->user) != 0)
+                    return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "QSA selection exchange failed");
+                // pass 2: attention of every group with the exchanged selections
+                for (uint32_t t0 = 0; t0 < tokens; t0 += unit) {
+                    const uint32_t n = std::min<uint32_t>(unit, tokens - t0);
+                    const QsaBatch qb = uniform_batch(t0);
+                    launch_qsa_attend(d, qb, n, q_all + (size_t)t0 * qw, sel_all + (size_t)t0 * d.topk,
+                                      cnt_all + t0, part_o, part_ml, splits, err, c->stream);
+                    launch_qsa_combine(d, n, part_o, part_ml, splits, proj + (size_t)t0 * ldp, ldp,
+                                       gated + (size_t)t0 * qw, err, c->stream);
+                }
             }
         }
         for (uint32_t t = 0; !chunked && t < tokens; ++t) {

@@ -187,9 +187,22 @@ struct QsaSeq {
     uint32_t capacity;
 };
 
+// Entries of one launch: up to kMaxBatch independent sequences, or (uniform
+// != 0) any number of consecutive tokens of one sequence: entry b is s[0]
+// with length s[0].length + b (a prefill; every entry shares the cache).
 struct QsaBatch {
     QsaSeq s[kMaxBatch];
+    uint32_t uniform = 0;
 };
+
+__host__ __device__ inline QsaSeq batch_seq(const QsaBatch &bt, uint32_t b) {
+    if (bt.uniform) {
+        QsaSeq s = bt.s[0];
+        s.length += b;
+        return s;
+    }
+    return bt.s[b];
+}
 
 // Row stride (in blocks) of a sequence's feature-major block-key cache
 // [di][ld]: the block count rounded up to a multiple of 4, so that four

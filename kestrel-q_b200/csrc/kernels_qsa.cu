@@ -136,7 +136,7 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
     if (qsa_error_raised(err)) return;
     const uint32_t b = blockIdx.x;
     uint32_t role = blockIdx.y;
-    const QsaSeq s = bt.s[b];
+    const QsaSeq s = batch_seq(bt, b);
     const uint32_t pos = s.length;
     const float *prow = proj + (size_t)b * ldp;
     const float *irow = iproj + (size_t)b * ldi;
@@ -258,7 +258,7 @@ qsa_score_kernel(QsaDims d, QsaBatch bt, uint32_t batch, const float *__restrict
     uint32_t nb_max = 0;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-        nb[e] = (uint32_t)e < ne ? (bt.s[e0 + e].length + 1) / d.block : 0u;
+        nb[e] = (uint32_t)e < ne ? (batch_seq(bt, e0 + e).length + 1) / d.block : 0u;
         nb_max = max(nb_max, nb[e]);
     }
     if (blockIdx.x * kScoreThreads >= nb_max) return;   // uniform over the CTA
@@ -268,7 +268,7 @@ qsa_score_kernel(QsaDims d, QsaBatch bt, uint32_t batch, const float *__restrict
     __syncthreads();
     const uint32_t bi = blockIdx.x * kScoreThreads + threadIdx.x;
     if (bi >= nb_max) return;
-    const QsaSeq s = bt.s[e0];   // E > 1: every entry reads this sequence's keys
+    const QsaSeq s = batch_seq(bt, e0);   // E > 1: every entry reads this sequence's keys
     const uint32_t ld = block_key_ld(s.capacity, d.block);
     const float *key = s.block_keys + bi;
     float score[E];
@@ -384,7 +384,7 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
     __shared__ uint32_t warp_tot[kSelThreads / 32];
     if (qsa_error_raised(err)) return;
     const uint32_t b = blockIdx.x;
-    const QsaSeq s = bt.s[b];
+    const QsaSeq s = batch_seq(bt, b);
     const uint32_t n = (s.length + 1) / d.block;
     const uint32_t k = min(n, d.topk);
     const float *sc = scores + (size_t)b * ld_scores;
@@ -524,7 +524,7 @@ qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     extern __shared__ float smem[];   // [8 warps][HPW][hd + 2]
     if (qsa_error_raised(err)) return;
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const QsaSeq s = bt.s[b];
+    const QsaSeq s = batch_seq(bt, b);
     const uint32_t pos = s.length;
     const uint32_t nblocks = (pos + 1) / d.block;
     const uint32_t tail = (pos + 1) % d.block;
@@ -668,7 +668,7 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     float *vs = ks + 2 * kAtTile * KLD;              // [2][16][HD]
     if (qsa_error_raised(err)) return;
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const QsaSeq s = bt.s[b];
+    const QsaSeq s = batch_seq(bt, b);
     const uint32_t pos = s.length;
     const uint32_t nblocks = (pos + 1) / d.block;
     const uint32_t tail = (pos + 1) % d.block;
@@ -808,6 +808,26 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
 //   softmax  warp h keeps head h's running max / sum (online softmax);
 //   PV  warp w owns features [32w, 32w+32), one per lane, for every head.
 // K/V tiles stream through a 3-stage cp.async ring (96 KB), two CTAs per SM.
+// f32 pairs for the attention arithmetic (fma.rn.f32x2 / mul.rn.f32x2)
+__device__ __forceinline__ uint64_t at_pair(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void at_unpair(uint64_t v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t at_fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t at_mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
 constexpr int kMhStages = 3;
 constexpr int kMhHD = 256;
 constexpr int kMhMaxTiles = 32;           // tiles per CTA (the launcher sizes splits for it)
@@ -831,7 +851,7 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     uint32_t *tok_s = reinterpret_cast<uint32_t *>(corr_s + 8);   // [kMhMaxTiles * 16] cache rows
     if (qsa_error_raised(err)) return;
     const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const QsaSeq s = bt.s[b];
+    const QsaSeq s = batch_seq(bt, b);
     const uint32_t pos = s.length;
     const uint32_t nblocks = (pos + 1) / d.block;
     const uint32_t tail = (pos + 1) % d.block;
@@ -889,23 +909,25 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     };
 
     // query features [8 lane, 8 lane + 8) of every head, in registers
-    float qr[8][8];
+    // query features as f32 pairs (paired FMAs: two lanes of math per
+    // instruction; attention is checked to tolerance, not bit-exact)
+    uint64_t qr[8][4];
 #pragma unroll
     for (int h = 0; h < 8; ++h) {
         if ((uint32_t)h < heads) {
             const float *qp = q + ((size_t)b * d.q_heads + kvh * heads + h) * HD + 8 * lane;
             const float4 a = *reinterpret_cast<const float4 *>(qp);
             const float4 c = *reinterpret_cast<const float4 *>(qp + 4);
-            qr[h][0] = a.x; qr[h][1] = a.y; qr[h][2] = a.z; qr[h][3] = a.w;
-            qr[h][4] = c.x; qr[h][5] = c.y; qr[h][6] = c.z; qr[h][7] = c.w;
+            qr[h][0] = at_pair(a.x, a.y); qr[h][1] = at_pair(a.z, a.w);
+            qr[h][2] = at_pair(c.x, c.y); qr[h][3] = at_pair(c.z, c.w);
         } else {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) qr[h][j] = 0.0f;
+            for (int j = 0; j < 4; ++j) qr[h][j] = 0ull;
         }
     }
-    float acc[8];
+    uint64_t acc2[4];   // heads (0,1), (2,3), (4,5), (6,7) of feature f
 #pragma unroll
-    for (int h = 0; h < 8; ++h) acc[h] = 0.0f;
+    for (int i = 0; i < 4; ++i) acc2[i] = 0ull;
     float m_run = -INFINITY, l_run = 0.0f;   // head `warp`'s running softmax state
     const float scale = d.sqrt_head_dim;
     // reduce-scatter: after the three exchange steps lanes {4g..4g+3} hold
@@ -930,14 +952,17 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
             const int tk = 2 * warp + tt;
             const float4 k0 = *reinterpret_cast<const float4 *>(kt + tk * HD + 8 * lane);
             const float4 k1 = *reinterpret_cast<const float4 *>(kt + tk * HD + 8 * lane + 4);
-            const float kv[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+            const uint64_t kp[4] = {at_pair(k0.x, k0.y), at_pair(k0.z, k0.w), at_pair(k1.x, k1.y),
+                                    at_pair(k1.z, k1.w)};
             float v[8];
 #pragma unroll
             for (int h = 0; h < 8; ++h) {
-                float a = 0.0f;
+                uint64_t a2 = 0ull;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) a = fmaf(qr[h][j], kv[j], a);
-                v[h] = a;
+                for (int j = 0; j < 4; ++j) a2 = at_fma2(qr[h][j], kp[j], a2);
+                float lo, hi;
+                at_unpair(a2, lo, hi);
+                v[h] = lo + hi;
             }
             float w4[4], w2[2];
             const bool u16 = (lane & 16) != 0, u8 = (lane & 8) != 0, u4 = (lane & 4) != 0;
@@ -988,27 +1013,29 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
             const int f = 32 * warp + lane;
             const float4 c0 = *reinterpret_cast<const float4 *>(corr_s);
             const float4 c1 = *reinterpret_cast<const float4 *>(corr_s + 4);
-            acc[0] *= c0.x; acc[1] *= c0.y; acc[2] *= c0.z; acc[3] *= c0.w;
-            acc[4] *= c1.x; acc[5] *= c1.y; acc[6] *= c1.z; acc[7] *= c1.w;
+            acc2[0] = at_mul2(acc2[0], at_pair(c0.x, c0.y));
+            acc2[1] = at_mul2(acc2[1], at_pair(c0.z, c0.w));
+            acc2[2] = at_mul2(acc2[2], at_pair(c1.x, c1.y));
+            acc2[3] = at_mul2(acc2[3], at_pair(c1.z, c1.w));
 #pragma unroll 4
             for (int t = 0; t < kAtTile; ++t) {
                 const float vv = vt[t * HD + f];
+                const uint64_t v2 = at_pair(vv, vv);
                 const float4 p0 = *reinterpret_cast<const float4 *>(pw + t * 8);
                 const float4 p1 = *reinterpret_cast<const float4 *>(pw + t * 8 + 4);
-                acc[0] = fmaf(p0.x, vv, acc[0]);
-                acc[1] = fmaf(p0.y, vv, acc[1]);
-                acc[2] = fmaf(p0.z, vv, acc[2]);
-                acc[3] = fmaf(p0.w, vv, acc[3]);
-                acc[4] = fmaf(p1.x, vv, acc[4]);
-                acc[5] = fmaf(p1.y, vv, acc[5]);
-                acc[6] = fmaf(p1.z, vv, acc[6]);
-                acc[7] = fmaf(p1.w, vv, acc[7]);
+                acc2[0] = at_fma2(at_pair(p0.x, p0.y), v2, acc2[0]);
+                acc2[1] = at_fma2(at_pair(p0.z, p0.w), v2, acc2[1]);
+                acc2[2] = at_fma2(at_pair(p1.x, p1.y), v2, acc2[2]);
+                acc2[3] = at_fma2(at_pair(p1.z, p1.w), v2, acc2[3]);
             }
         }
         __syncthreads();
     }
     asm volatile("cp.async.wait_group 0;\n" ::);
     const int f = 32 * warp + lane;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) at_unpair(acc2[i], acc[2 * i], acc[2 * i + 1]);
 #pragma unroll
     for (int h = 0; h < 8; ++h) {
         if ((uint32_t)h < heads) {
