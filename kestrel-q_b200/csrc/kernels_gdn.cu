@@ -169,6 +169,107 @@ gdn_conv_gates_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t token
     if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
 }
 
+// Prefill with dk = dv = 128 and a 4-tap conv: one warp per (token, key
+// head), 8 per CTA, REP value heads per key head.  Lane l owns channels
+// 4l .. 4l+3 of the head's q, k and v blocks (16-byte loads and stores; the
+// four history rows of a channel are re-read, mostly from L1/L2), and the
+// L2 norms are warp reductions, so nothing waits at a CTA barrier.  Same
+// arithmetic per value as gdn_conv_gates_kernel (taps in the reference's
+// order).
+template <int REP>
+__global__ void __launch_bounds__(256)
+gdn_conv_gates_warp_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t tokens,
+                           const float *__restrict__ proj, uint32_t ldp,
+                           float *__restrict__ qk, float *__restrict__ vout,
+                           float *__restrict__ beta, float *__restrict__ decay,
+                           float *__restrict__ logdecay, ErrorWord err) {
+    constexpr int K = 4, D = 128, NCH = 2 + REP;
+    pdl_wait();
+    if (gdn_error_raised(err)) return;
+    const uint32_t pair = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pair >= tokens * d.key_heads) return;
+    const uint32_t t = pair / d.key_heads, kh = pair % d.key_heads;
+    const int lane = threadIdx.x & 31;
+    const float *conv_in = p.conv_in[0];
+    float *conv_out = p.conv_out[0];
+    const bool last = t == tokens - 1;
+    float val[NCH][4];
+    bool bad = false;
+#pragma unroll
+    for (int cc = 0; cc < NCH; ++cc) {
+        const uint32_t c0 = (cc == 0 ? kh * D : cc == 1 ? d.key_width + kh * D
+                                                      : 2 * d.key_width + (kh * REP + (cc - 2)) * D) + 4 * lane;
+        float h[K][4];
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+            const int src = (int)t - (K - 1) + j;
+            if (src >= 0) {
+                const float4 x = *reinterpret_cast<const float4 *>(proj + (size_t)src * ldp + c0);
+                h[j][0] = x.x; h[j][1] = x.y; h[j][2] = x.z; h[j][3] = x.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) h[j][e] = conv_in[(size_t)(c0 + e) * K + (t + 1 + j)];
+            }
+        }
+        float wt[4][K];   // the four channels' taps: 16 consecutive weights
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float4 wq = *reinterpret_cast<const float4 *>(w.conv + (size_t)(c0 + e) * K);
+            wt[e][0] = wq.x; wt[e][1] = wq.y; wt[e][2] = wq.z; wt[e][3] = wq.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float sacc = 0.0f;
+#pragma unroll
+            for (int j = 0; j < K; ++j) sacc = __fadd_rn(sacc, __fmul_rn(wt[e][j], h[j][e]));
+            val[cc][e] = sacc * stable_sigmoid(sacc);
+            bad |= !isfinite(val[cc][e]);
+        }
+        if (last) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                *reinterpret_cast<float4 *>(conv_out + (size_t)(c0 + e) * K) = make_float4(h[0][e], h[1][e], h[2][e],
+                                                                                           h[3][e]);
+        }
+    }
+    float sq = 0.0f, sk = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        sq += val[0][e] * val[0][e];
+        sk += val[1][e] * val[1][e];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    }
+    const float iq = 1.0f / sqrtf(sq + 1.0e-6f), ik = 1.0f / sqrtf(sk + 1.0e-6f);
+    const float qscale = 1.0f / sqrtf((float)d.key_dim);
+    *reinterpret_cast<float4 *>(qk + ((size_t)t * 2 + 0) * d.key_width + kh * D + 4 * lane) =
+        make_float4(val[0][0] * iq * qscale, val[0][1] * iq * qscale, val[0][2] * iq * qscale, val[0][3] * iq * qscale);
+    *reinterpret_cast<float4 *>(qk + ((size_t)t * 2 + 1) * d.key_width + kh * D + 4 * lane) =
+        make_float4(val[1][0] * ik, val[1][1] * ik, val[1][2] * ik, val[1][3] * ik);
+#pragma unroll
+    for (int r = 0; r < REP; ++r)
+        *reinterpret_cast<float4 *>(vout + (size_t)t * d.value_width + (kh * REP + r) * D + 4 * lane) =
+            make_float4(val[2 + r][0], val[2 + r][1], val[2 + r][2], val[2 + r][3]);
+    if (lane < REP) {
+        const float *prow = proj + (size_t)t * ldp;
+        const uint32_t h = kh * REP + lane;
+        const float pb = prow[d.conv_channels + d.value_width + h];
+        const float pa = prow[d.conv_channels + d.value_width + d.value_heads + h];
+        const float bt = stable_sigmoid(pb);
+        const float a = pa + w.dt_bias[h];
+        const float sp = a > 20.0f ? a : log1pf(expf(a));
+        const float g = -expf(w.a_log[h]) * sp;
+        if (!isfinite(g) || g > 0.0f || !isfinite(bt)) gdn_raise(err, kErrDecay);
+        beta[(size_t)t * d.value_heads + h] = bt;
+        decay[(size_t)t * d.value_heads + h] = expf(g);
+        if (logdecay) logdecay[(size_t)t * d.value_heads + h] = g;
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) gdn_raise(err, kErrNonFinite);
+}
+
 // ------------------------------------------------------------ recurrence
 //
 // Fast path for dk = dv = 128: grid (Hv, B), 256 threads.  The head's
@@ -503,8 +604,25 @@ void launch_gdn_conv_gates(const GdnDims &d, const GdnWeightsDev &w,
                            uint32_t tokens, const float *proj, uint32_t ldp,
                            float *qk, float *v, float *beta, float *decay,
                            ErrorWord err, cudaStream_t stream, float *logdecay) {
-    dim3 grid(d.key_heads, batch * tokens);
     KernelTimer timer("gdn_conv", stream);
+    const bool aligned = (ldp % 4u) == 0u && (reinterpret_cast<uintptr_t>(proj) & 15u) == 0u &&
+                         (reinterpret_cast<uintptr_t>(w.conv) & 15u) == 0u;
+    if (batch == 1 && tokens >= 64 && d.kernel == 4 && d.key_dim == 128 && d.value_dim == 128 && aligned &&
+        (d.repeat == 1 || d.repeat == 2 || d.repeat == 4)) {
+        const dim3 wgrid((tokens * d.key_heads + 7) / 8);
+        if (d.repeat == 1)
+            launch_pdl(gdn_conv_gates_warp_kernel<1>, wgrid, 256, 0, stream, d, w, p, tokens, proj, ldp, qk, v, beta,
+                       decay, logdecay, err);
+        else if (d.repeat == 2)
+            launch_pdl(gdn_conv_gates_warp_kernel<2>, wgrid, 256, 0, stream, d, w, p, tokens, proj, ldp, qk, v, beta,
+                       decay, logdecay, err);
+        else
+            launch_pdl(gdn_conv_gates_warp_kernel<4>, wgrid, 256, 0, stream, d, w, p, tokens, proj, ldp, qk, v, beta,
+                       decay, logdecay, err);
+        count_launch();
+        return;
+    }
+    dim3 grid(d.key_heads, batch * tokens);
     if (d.kernel == 4)
         launch_pdl(gdn_conv_gates_kernel<4>, grid, kConvThreads, 0, stream, d, w, p, tokens, proj, ldp, qk, v,
                                                                    beta, decay, logdecay, err);

@@ -379,27 +379,28 @@ static size_t state_smem() {
 }
 
 // ---------------------------------------------------------------- phase 3
-// grid (Hv, T), 128 threads: o * rsqrt(mean(o^2) + eps) * norm_w * sigmoid(z).
-__global__ void __launch_bounds__(128)
+// One warp per (token, value head), 8 per CTA: lane l takes features
+// 4l .. 4l+3; o * rsqrt(mean(o^2) + eps) * norm_w * sigmoid(z).
+__global__ void __launch_bounds__(256)
 gdn_gate_norm_kernel(GdnDims d, GdnWeightsDev w, const float *__restrict__ obuf, const float *__restrict__ proj,
-                     uint32_t ldp, float *__restrict__ gated, ErrorWord err) {
+                     uint32_t ldp, float *__restrict__ gated, uint32_t tokens, ErrorWord err) {
     pdl_wait();
-    __shared__ float red[4];
     if (chunk_error_raised(err)) return;
-    const uint32_t h = blockIdx.x, t = blockIdx.y;
-    const int f = threadIdx.x;
-    const float o = obuf[(size_t)t * d.value_width + h * kD + f];
-    float v = o * o;
+    const uint32_t pair = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pair >= tokens * d.value_heads) return;
+    const uint32_t t = pair / d.value_heads, h = pair % d.value_heads;
+    const int lane = threadIdx.x & 31;
+    const float4 o = *reinterpret_cast<const float4 *>(obuf + (size_t)t * d.value_width + h * kD + 4 * lane);
+    float v = o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
-    if ((f & 31) == 0) red[f >> 5] = v;
-    __syncthreads();
-    const float sumsq = red[0] + red[1] + red[2] + red[3];
-    const float inv = 1.0f / sqrtf(sumsq / (float)kD + d.eps);
-    const float z = proj[(size_t)t * ldp + d.conv_channels + h * kD + f];
-    const float g = (w.norm[f] * (o * inv)) * chunk_sigmoid(z);
-    if (!isfinite(g)) chunk_raise(err, kErrNonFinite);
-    gated[(size_t)t * d.value_width + h * kD + f] = g;
+    const float inv = 1.0f / sqrtf(v / (float)kD + d.eps);
+    const float4 z = *reinterpret_cast<const float4 *>(proj + (size_t)t * ldp + d.conv_channels + h * kD + 4 * lane);
+    const float4 nw = *reinterpret_cast<const float4 *>(w.norm + 4 * lane);
+    const float4 g = make_float4((nw.x * (o.x * inv)) * chunk_sigmoid(z.x), (nw.y * (o.y * inv)) * chunk_sigmoid(z.y),
+                                 (nw.z * (o.z * inv)) * chunk_sigmoid(z.z), (nw.w * (o.w * inv)) * chunk_sigmoid(z.w));
+    if (!isfinite(g.x) || !isfinite(g.y) || !isfinite(g.z) || !isfinite(g.w)) chunk_raise(err, kErrNonFinite);
+    *reinterpret_cast<float4 *>(gated + (size_t)t * d.value_width + h * kD + 4 * lane) = g;
 }
 
 void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatchPtrs &p, uint32_t tokens,
@@ -445,8 +446,8 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
     }
     {
         KernelTimer t3("gdn_gate_norm", stream);
-        launch_pdl(gdn_gate_norm_kernel, dim3(d.value_heads, tokens), 128, 0, stream, d, w, obuf, proj, ldp, gated,
-                   err);
+        launch_pdl(gdn_gate_norm_kernel, dim3((tokens * d.value_heads + 7) / 8), 256, 0, stream, d, w, obuf, proj,
+                   ldp, gated, tokens, err);
         count_launch();
     }
 }
