@@ -230,7 +230,11 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     const uint32_t tiles = (d.sel_capacity + 15) / 16;
     const uint32_t per_seq = entries * d.kv_heads;
     // (the head-blocked attention kernel takes at most 32 tiles per split)
-    uint32_t splits = std::max<uint32_t>((tiles + 15) / 16, (3 * 148 + per_seq - 1) / per_seq);
+    // about 16 tiles of 16 selected tokens per split for decode batches, 32
+    // (the kernel's limit) for prefill batches, which have CTAs to spare
+    const uint32_t tiles_per_split = chunked ? 32u : 16u;
+    uint32_t splits = std::max<uint32_t>((tiles + tiles_per_split - 1) / tiles_per_split,
+                                         (3 * 148 + per_seq - 1) / per_seq);
     splits = std::max<uint32_t>(1, std::min<uint32_t>(splits, tiles));
     const size_t need = Carve::round(items * ldp * 4) + Carve::round(items * ldi * 4) +
                         Carve::round(items * qw * 4) + Carve::round((size_t)entries * qw * 4) +

@@ -69,18 +69,22 @@ size_t gdn_chunk_workspace_floats(const GdnDims &d, uint32_t tokens) {
 bool gdn_chunked_supported(const GdnDims &d) { return d.key_dim == kD && d.value_dim == kD; }
 
 // ---------------------------------------------------------------- phase 1
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, const float *__restrict__ vin,
                       const float *__restrict__ beta, const float *__restrict__ logdecay,
                       float *__restrict__ work, ErrorWord err) {
     pdl_wait();
+    // 112.5 KB: two CTAs per SM.  K and Q are [64][128] with their 16-byte
+    // chunks XOR-swizzled by row (8 consecutive rows hit 8 bank groups); the
+    // Q tile is dead after L and P and then holds W.
     extern __shared__ __align__(16) float cs[];
-    float *Ks = cs;                        // [64][128 + 4]
-    float *Qs = Ks + kC * (kD + 4);        // [64][128 + 4]
-    float *Ls = Qs + kC * (kD + 4);        // [64][68]
-    float *Gs = Ls + kC * (kC + 4);        // [64]
+    float *Ks = cs;                        // [64][128] swizzled
+    float *Qs = Ks + kC * kD;              // [64][128] swizzled, then W [64][128]
+    float *Us = Qs + kC * kD;              // U [64][128]
+    float *Ls = Us + kC * kD;              // [64][64]
+    float *Gs = Ls + kC * kC;              // [64]
     float *Bs = Gs + kC;                   // [64]
-    float *Xs = Bs + kC;                   // W then U staging [64][128]
+    auto sw = [](int r, int c4) { return r * kD + ((((c4 >> 2) ^ (r & 7))) << 2); };
     if (chunk_error_raised(err)) return;
     const uint32_t h = blockIdx.x, c = blockIdx.y;
     const uint32_t kh = h / d.repeat;
@@ -98,8 +102,8 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
             q4 = *reinterpret_cast<const float4 *>(qk + (item * 2 + 0) * d.key_width + kh * kD + c4);
             k4 = *reinterpret_cast<const float4 *>(qk + (item * 2 + 1) * d.key_width + kh * kD + c4);
         }
-        *reinterpret_cast<float4 *>(Qs + r * (kD + 4) + c4) = q4;
-        *reinterpret_cast<float4 *>(Ks + r * (kD + 4) + c4) = k4;
+        *reinterpret_cast<float4 *>(Qs + sw(r, c4)) = q4;
+        *reinterpret_cast<float4 *>(Ks + sw(r, c4)) = k4;
     }
     if (tid < kC) {
         const bool in = (uint32_t)tid < n;
@@ -124,11 +128,11 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
 #pragma unroll
         for (int r = 0; r < 16; ++r) { lk[r] = 0.f; pq[r] = 0.f; }
         for (int kk = 0; kk < kD; kk += 4) {
-            const float4 ki = *reinterpret_cast<const float4 *>(Ks + i * (kD + 4) + kk);
-            const float4 qi = *reinterpret_cast<const float4 *>(Qs + i * (kD + 4) + kk);
+            const float4 ki = *reinterpret_cast<const float4 *>(Ks + sw(i, kk));
+            const float4 qi = *reinterpret_cast<const float4 *>(Qs + sw(i, kk));
 #pragma unroll
             for (int r = 0; r < 16; ++r) {
-                const float4 kj = *reinterpret_cast<const float4 *>(Ks + (j0 + 4 * r) * (kD + 4) + kk);
+                const float4 kj = *reinterpret_cast<const float4 *>(Ks + sw(j0 + 4 * r, kk));
                 lk[r] = fmaf(ki.x, kj.x, fmaf(ki.y, kj.y, fmaf(ki.z, kj.z, fmaf(ki.w, kj.w, lk[r]))));
                 pq[r] = fmaf(qi.x, kj.x, fmaf(qi.y, kj.y, fmaf(qi.z, kj.z, fmaf(qi.w, kj.w, pq[r]))));
             }
@@ -138,7 +142,7 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
         for (int r = 0; r < 16; ++r) {
             const int j = j0 + 4 * r;
             const float f = j <= i ? expf(gi - Gs[j]) : 0.0f;
-            Ls[i * (kC + 4) + j] = j < i ? lk[r] * f : 0.0f;
+            Ls[i * kC + j] = j < i ? lk[r] * f : 0.0f;
             wk[kChunkP + i * kC + j] = pq[r] * f;
         }
     }
@@ -150,24 +154,25 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
     if (tid == 0) wk[kChunkTot] = expf(gc);
     __syncthreads();
     // right-hand sides, staged before the sequential solve: W rows start as
-    // e^G_i k_i, U rows as v_i (Xs holds W in [0, 64*128), U after it)
+    // e^G_i k_i (in the Q tile, dead now), U rows as v_i
+    float *Ws = Qs;
     for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
         const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
         const float eg = expf(Gs[r]);
-        const float4 k4 = *reinterpret_cast<const float4 *>(Ks + r * (kD + 4) + c4);
-        *reinterpret_cast<float4 *>(Xs + r * kD + c4) = make_float4(eg * k4.x, eg * k4.y, eg * k4.z, eg * k4.w);
+        const float4 k4 = *reinterpret_cast<const float4 *>(Ks + sw(r, c4));
+        *reinterpret_cast<float4 *>(Ws + r * kD + c4) = make_float4(eg * k4.x, eg * k4.y, eg * k4.z, eg * k4.w);
         float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
         if ((uint32_t)r < n) v4 = *reinterpret_cast<const float4 *>(vin + (size_t)(t0 + r) * d.value_width + h * kD + c4);
-        *reinterpret_cast<float4 *>(Xs + kC * kD + r * kD + c4) = v4;
+        *reinterpret_cast<float4 *>(Us + r * kD + c4) = v4;
     }
     __syncthreads();
     // forward substitution in place, one column per thread: threads 0..127 W,
     // 128..255 U; row i = beta_i (rhs_i - sum_{j<i} L_ij row_j)
     {
-        float *X = Xs + (tid < kD ? 0 : kC * kD);
+        float *X = tid < kD ? Ws : Us;
         const int f = tid & (kD - 1);
         for (int i = 0; i < kC; ++i) {
-            const float *Li = Ls + i * (kC + 4);
+            const float *Li = Ls + i * kC;
             float acc = 0.0f;
             int j = 0;
             for (; j + 4 <= i; j += 4) {
@@ -182,16 +187,16 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
         }
     }
     __syncthreads();
-    for (int i = tid; i < kC * kD; i += blockDim.x) {
-        wk[kChunkW + i] = Xs[i];
-        wk[kChunkU + i] = Xs[kC * kD + i];
+    for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
+        *reinterpret_cast<float4 *>(wk + kChunkW + 4 * i) = *reinterpret_cast<const float4 *>(Ws + 4 * i);
+        *reinterpret_cast<float4 *>(wk + kChunkU + 4 * i) = *reinterpret_cast<const float4 *>(Us + 4 * i);
     }
 }
 
 // ---------------------------------------------------------------- phase 2
 // CW state columns per CTA (32, 16 or 8: fewer value heads per GPU take
-// narrower slices, so that the grid still covers the SMs); 256 threads =
-// CW columns x G = 256 / CW row groups.  The tiles are read as 16-byte
+// narrower slices, so that the grid still covers the SMs); NT threads =
+// CW columns x G = NT / CW row groups.  The tiles are read as 16-byte
 // vectors along their rows (broadcast within a row group), four K steps per
 // vector.  Tile loads are cp.async copies issued ahead of use: the next
 // chunk's W during the whole current chunk (two W buffers), the current
@@ -208,11 +213,11 @@ __device__ __forceinline__ void chunk_commit() { asm volatile("cp.async.commit_g
 template <int N>
 __device__ __forceinline__ void chunk_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
-template <int CW>
-__global__ void __launch_bounds__(256, 1)
+template <int CW, int NT>
+__global__ void __launch_bounds__(NT, 1)
 gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *__restrict__ qk,
                        const float *__restrict__ work, float *__restrict__ obuf, ErrorWord err) {
-    constexpr int G = 256 / CW;      // row groups
+    constexpr int G = NT / CW;       // row groups
     constexpr int RD = kC / G;       // delta / O rows per thread
     constexpr int RS = kD / G;       // state rows per thread
     constexpr int LT = kD + 4;       // row stride of the W / Q / K tiles
@@ -373,6 +378,8 @@ gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *
     if (__syncthreads_or(bad) && tid == 0) chunk_raise(err, kErrNonFinite);
 }
 
+constexpr int kStateThreads = 256;   // 512 measured slower (register-limited, one CTA per SM either way)
+
 template <int CW>
 static size_t state_smem() {
     return (size_t)(kD * CW + 4 * kC * (kD + 4) + kC * (kC + 4) + kC * CW + 2 * kC + 4) * sizeof(float);
@@ -410,15 +417,15 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
     KernelTimer timer("gdn_recurrence", stream);
     const uint32_t chunks = (tokens + kC - 1) / kC;
     float *obuf = work + (size_t)chunks * d.value_heads * kChunkFloats;
-    const size_t smem1 = (size_t)(2 * kC * (kD + 4) + kC * (kC + 4) + 2 * kC + 2 * kC * kD) * sizeof(float);
+    const size_t smem1 = (size_t)(3 * kC * kD + kC * kC + 2 * kC) * sizeof(float);
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
-        cudaFuncSetAttribute(gdn_chunk_state_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)state_smem<32>());
-        cudaFuncSetAttribute(gdn_chunk_state_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)state_smem<16>());
-        cudaFuncSetAttribute(gdn_chunk_state_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<32, kStateThreads>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)state_smem<32>());
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<16, kStateThreads>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)state_smem<16>());
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<8, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)state_smem<8>());
         attr = true;
     }
@@ -433,14 +440,14 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
         // narrow enough that the grid reaches about 128 CTAs
         KernelTimer t2("gdn_chunk_state", stream);
         if (d.value_heads >= 32) {
-            launch_pdl(gdn_chunk_state_kernel<32>, dim3(d.value_heads, kD / 32), 256, state_smem<32>(), stream, d, p,
-                       tokens, qk, work, obuf, err);
+            launch_pdl(gdn_chunk_state_kernel<32, kStateThreads>, dim3(d.value_heads, kD / 32), kStateThreads,
+                       state_smem<32>(), stream, d, p, tokens, qk, work, obuf, err);
         } else if (d.value_heads >= 16) {
-            launch_pdl(gdn_chunk_state_kernel<16>, dim3(d.value_heads, kD / 16), 256, state_smem<16>(), stream, d, p,
-                       tokens, qk, work, obuf, err);
+            launch_pdl(gdn_chunk_state_kernel<16, kStateThreads>, dim3(d.value_heads, kD / 16), kStateThreads,
+                       state_smem<16>(), stream, d, p, tokens, qk, work, obuf, err);
         } else {
-            launch_pdl(gdn_chunk_state_kernel<8>, dim3(d.value_heads, kD / 8), 256, state_smem<8>(), stream, d, p,
-                       tokens, qk, work, obuf, err);
+            launch_pdl(gdn_chunk_state_kernel<8, 256>, dim3(d.value_heads, kD / 8), 256, state_smem<8>(), stream, d,
+                       p, tokens, qk, work, obuf, err);
         }
         count_launch();
     }
