@@ -355,7 +355,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 uint32_t *sdst = sharded ? sel_all + (size_t)t0 * d.topk : sel;
                 uint32_t *cdst = sharded ? cnt_all + t0 : sel_count;
                 launch_qsa_score(d, qb, n, iqv, scores, max_blocks, nb_max, true, err, c->stream);
-                launch_qsa_select(d, qb, n, scores, max_blocks, sdst, cdst, err, c->stream);
+                launch_qsa_select(d, qb, n, scores, max_blocks, sdst, cdst, false, err, c->stream);
                 if (sharded) continue;
                 launch_qsa_attend(d, qb, n, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);
                 launch_qsa_combine(d, n, part_o, part_ml, splits, pt, ldp, gated + (size_t)t0 * qw, err, c->stream);
@@ -393,7 +393,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
             launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, true, true, err,
                                c->stream);
             launch_qsa_score(d, qb, gb, iqv, scores, max_blocks, nb_max, false, err, c->stream);
-            launch_qsa_select(d, qb, gb, scores, max_blocks, sel, sel_count, err, c->stream);
+            launch_qsa_select(d, qb, gb, scores, max_blocks, sel, sel_count, selection != nullptr, err, c->stream);
             launch_qsa_attend(d, qb, gb, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);
             launch_qsa_combine(d, gb, part_o, part_ml, splits, pt, ldp * tokens, gated + (size_t)t * qw, err,
                                c->stream);

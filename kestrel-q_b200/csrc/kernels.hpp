@@ -236,10 +236,12 @@ void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                       const float *iq, float *scores, uint32_t ld_scores,
                       uint32_t max_blocks, bool shared_sequence, ErrorWord err,
                       cudaStream_t stream);
+// `rank_order`: the selected ids in the reference's rank order (score
+// descending, id ascending), else in ascending id order (same set).
 void launch_qsa_select(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const float *scores, uint32_t ld_scores,
                        uint32_t *selected, uint32_t *selected_count,
-                       ErrorWord err, cudaStream_t stream);
+                       bool rank_order, ErrorWord err, cudaStream_t stream);
 void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const float *q, const uint32_t *selected,
                        const uint32_t *selected_count, float *partial_o,

@@ -376,7 +376,7 @@ __device__ __forceinline__ uint32_t order_key(float v) {
 __global__ void __launch_bounds__(kSelThreads)
 qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
                   uint32_t ld_scores, uint32_t *__restrict__ selected,
-                  uint32_t *__restrict__ selected_count, ErrorWord err) {
+                  uint32_t *__restrict__ selected_count, uint32_t rank_order, ErrorWord err) {
     pdl_wait();
     __shared__ uint32_t hist[256];
     __shared__ uint32_t s_prefix, s_need, s_taken, s_tie_base;
@@ -472,7 +472,9 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
         }
         __syncthreads();
     }
-    // bitonic sort, descending
+    // bitonic sort, descending: by (score, -id) = the reference's rank
+    // order, or by -id alone (ascending block ids) when only the set matters
+    const unsigned long long key_mask = rank_order ? ~0ull : 0xffffffffull;
     for (uint32_t size = 2; size <= kSelMax; size <<= 1) {
         for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
             for (uint32_t i = tid; i < kSelMax; i += blockDim.x) {
@@ -480,7 +482,7 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
                 if (j > i) {
                     bool desc = (i & size) == 0;
                     unsigned long long a = cand[i], c = cand[j];
-                    if ((a < c) == desc) { cand[i] = c; cand[j] = a; }
+                    if (((a & key_mask) < (c & key_mask)) == desc) { cand[i] = c; cand[j] = a; }
                 }
             }
             __syncthreads();
@@ -497,16 +499,16 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
 void launch_qsa_select(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const float *scores, uint32_t ld_scores,
                        uint32_t *selected, uint32_t *selected_count,
-                       ErrorWord err, cudaStream_t stream) {
+                       bool rank_order, ErrorWord err, cudaStream_t stream) {
     KernelTimer timer("qsa_select", stream);
     launch_pdl(qsa_select_kernel, batch, kSelThreads, 0, stream, d, b, scores, ld_scores, selected,
-                                                        selected_count, err);
+               selected_count, rank_order ? 1u : 0u, err);
     count_launch();
 }
 
 // ------------------------------------------------------------ attend
 //
-// grid (splits, Hkv, B); 256 threads = 8 warps.  A split owns a contiguous
+// grid (B, Hkv, splits); 256 threads = 8 warps.  A split owns a contiguous
 // range of the selected-token list.  Each warp takes every 8th token of the
 // range, one token at a time: its lanes hold FPL features of the K and V
 // rows, compute the logits of all query heads sharing the KV head (warp
@@ -523,7 +525,7 @@ qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     pdl_wait();
     extern __shared__ float smem[];   // [8 warps][HPW][hd + 2]
     if (qsa_error_raised(err)) return;
-    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const uint32_t b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
     const QsaSeq s = batch_seq(bt, b);
     const uint32_t pos = s.length;
     const uint32_t nblocks = (pos + 1) / d.block;
@@ -631,7 +633,7 @@ qsa_attend_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
 }
 
 // Tiled variant for head dimensions 128 / 256 (the BASELINE shapes).
-// grid (splits, Hkv, B); 256 threads = 8 warps; warp h owns query head
+// grid (B, Hkv, splits); 256 threads = 8 warps; warp h owns query head
 // kvh*repeat + h.  The split's token range is walked in tiles of 16
 // selected tokens whose K and V rows are staged with cp.async into
 // double-buffered shared memory (the next tile loads while the current one
@@ -667,7 +669,7 @@ qsa_attend_tiled_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     float *ks = qs + 8 * HD;                         // [2][16][KLD]
     float *vs = ks + 2 * kAtTile * KLD;              // [2][16][HD]
     if (qsa_error_raised(err)) return;
-    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const uint32_t b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
     const QsaSeq s = batch_seq(bt, b);
     const uint32_t pos = s.length;
     const uint32_t nblocks = (pos + 1) / d.block;
@@ -850,7 +852,7 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     float *corr_s = pw + kAtTile * 8;                        // [8]
     uint32_t *tok_s = reinterpret_cast<uint32_t *>(corr_s + 8);   // [kMhMaxTiles * 16] cache rows
     if (qsa_error_raised(err)) return;
-    const uint32_t split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const uint32_t b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
     const QsaSeq s = batch_seq(bt, b);
     const uint32_t pos = s.length;
     const uint32_t nblocks = (pos + 1) / d.block;
@@ -1055,7 +1057,10 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const uint32_t *selected_count, float *partial_o,
                        float *partial_ml, uint32_t splits,
                        ErrorWord err, cudaStream_t stream) {
-    dim3 grid(splits, d.kv_heads, batch);
+    // entries fastest: the CTAs in flight together take the same split of
+    // many entries, which (with selections in block order) read nearby
+    // parts of a shared cache
+    dim3 grid(batch, d.kv_heads, splits);
     KernelTimer timer("qsa_attend", stream);
     if (d.head_dim == 256 && d.repeat <= 8) {
         static bool attr = false;
