@@ -290,6 +290,26 @@ kq_status kq_b200_qsa_prefill_sharded_async(const kq_qsa_config *config,
                                             void *user,
                                             kq_diagnostic *diagnostic);
 
+/* kq_b200_qsa_prefill_sharded_async where more ranks than key/value heads
+ * share the attention: `config` holds every query head of one key/value
+ * head, and this rank runs the attention, gate and out-projection of token
+ * part `token_part` of `token_parts` (contiguous ranges of whole 64-token
+ * chunk groups), writing zero rows of `output` for the other tokens, so that
+ * the sum over ranks is the layer's output.  token_parts == 1 is
+ * kq_b200_qsa_prefill_sharded_async. */
+kq_status kq_b200_qsa_prefill_split_async(const kq_qsa_config *config,
+                                          kq_qsa_state *state,
+                                          const float *hidden,
+                                          uint64_t T,
+                                          float *output,
+                                          uint32_t rank,
+                                          uint32_t world,
+                                          uint32_t token_part,
+                                          uint32_t token_parts,
+                                          kq_b200_exchange_fn exchange,
+                                          void *user,
+                                          kq_diagnostic *diagnostic);
+
 /* Waits for the library stream and reports the first device-side error
  * raised since the previous synchronize. */
 kq_status kq_b200_synchronize(kq_diagnostic *diagnostic);

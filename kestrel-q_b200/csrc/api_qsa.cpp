@@ -185,10 +185,15 @@ struct SelectionCopy {
 // Tokens per launch sequence of a one-sequence prefill (uniform batches).
 constexpr uint32_t kPrefillEntries = 1024;
 
+// With `parts` > 1 the attention is split by token as well: this rank's
+// config holds every query head of one key/value head, and it runs the
+// attention, gate and out-projection only for token part `part` of `parts`
+// (contiguous, in whole launch groups), writing zero output rows elsewhere.
 struct TokenShard {
     uint32_t rank = 0, world = 1;
     kq_b200_exchange_fn exchange = nullptr;
     void *user = nullptr;
+    uint32_t part = 0, parts = 1;
 };
 
 // Enqueues the operator for `batch` sequences x `tokens` tokens (batch == 1
@@ -221,6 +226,12 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     const uint32_t group = sharded ? std::max<uint32_t>(1, std::min<uint32_t>(8, nchunks / (4 * shard->world))) : 1u;
     const uint32_t unit = sharded ? group * 64u : kPrefillEntries;
     auto owned = [&](uint32_t t0) { return !sharded || (t0 / unit) % shard->world == shard->rank; };
+    // the rank's token range for attention: launch groups [u0, u1)
+    const uint32_t parts = sharded ? shard->parts : 1u, part = sharded ? shard->part : 0u;
+    const uint32_t ngroups = (tokens + unit - 1) / unit;
+    const uint32_t tb = std::min<uint32_t>(tokens, (uint32_t)((uint64_t)ngroups * part / parts) * unit);
+    const uint32_t te = std::min<uint32_t>(tokens, (uint32_t)((uint64_t)ngroups * (part + 1) / parts) * unit);
+    auto attends = [&](uint32_t t0) { return t0 >= tb && t0 < te; };
     const uint32_t entries = chunked ? std::min<uint32_t>(tokens, unit) : batch;
     uint32_t max_blocks = 1;
     for (uint32_t b = 0; b < batch; ++b)
@@ -292,10 +303,27 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
         const uint32_t gb = std::min<uint32_t>(kMaxBatch, batch - g0);
         const size_t row0 = (size_t)g0 * tokens;
         const size_t n_items = (size_t)gb * tokens;
-        if (!launch_projection(main, x + row0 * H, H, proj, ldp, (uint32_t)n_items, err, c->stream, partial,
-                               partial_floats) &&
-            check_input)
-            launch_check_finite(x + row0 * H, n_items * H, err, c->stream);
+        if (parts == 1) {
+            if (!launch_projection(main, x + row0 * H, H, proj, ldp, (uint32_t)n_items, err, c->stream, partial,
+                                   partial_floats) &&
+                check_input)
+                launch_check_finite(x + row0 * H, n_items * H, err, c->stream);
+        } else {
+            // keys and values of every token, queries / gates of this rank's tokens
+            ProjSegments kv{};
+            kv.count = 2;
+            kv.m[0] = w.k; kv.out_offset[0] = 2 * qw;
+            kv.m[1] = w.v; kv.out_offset[1] = 2 * qw + kvw;
+            if (!launch_projection(kv, x, H, proj, ldp, tokens, err, c->stream, partial, partial_floats) &&
+                check_input)
+                launch_check_finite(x, (uint64_t)tokens * H, err, c->stream);
+            ProjSegments qg{};
+            qg.count = 1;
+            qg.m[0] = w.q; qg.out_offset[0] = 0;
+            if (te > tb)
+                launch_projection(qg, x + (size_t)tb * H, H, proj + (size_t)tb * ldp, ldp, te - tb, err, c->stream,
+                                  partial, partial_floats);
+        }
         // sharded: raw index keys for every token, index queries only for
         // this rank's groups
         if (!sharded) {
@@ -347,7 +375,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 const float *pt = proj + (size_t)t0 * ldp;
                 float *qdst = sharded ? q_all + (size_t)t0 * qw : qv;
                 launch_qsa_prepare(d, wd, qb, n, pt, ldp, iproj + (size_t)t0 * ldi, ldi, qdst, iqv, false, owned(t0),
-                                   err, c->stream);
+                                   attends(t0), err, c->stream);
                 // keys of the blocks this group completes, once all their raw rows are written
                 launch_qsa_block_keys(d, wd, seq, pos0 / d.block, (pos0 + n) / d.block, err, c->stream);
                 if (!owned(t0)) continue;
@@ -364,8 +392,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 KQB_CUDA(cudaGetLastError(), diag, "QSA index pass");
                 if (shard->exchange(sel_all, (uint64_t)tokens * (d.topk + 1), c->stream, shard->user) != 0)
                     return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "QSA selection exchange failed");
-                // pass 2: attention of every group with the exchanged selections
-                for (uint32_t t0 = 0; t0 < tokens; t0 += unit) {
+                // pass 2: attention of this rank's groups with the exchanged selections
+                for (uint32_t t0 = tb; t0 < te; t0 += unit) {
                     const uint32_t n = std::min<uint32_t>(unit, tokens - t0);
                     const QsaBatch qb = uniform_batch(t0);
                     launch_qsa_attend(d, qb, n, q_all + (size_t)t0 * qw, sel_all + (size_t)t0 * d.topk,
@@ -390,7 +418,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
             }
             const float *pt = proj + (size_t)t * ldp;      // batch==1: token rows; tokens==1: t==0
             const float *it = iproj + (size_t)t * ldi;
-            launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, true, true, err,
+            launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, true, true, true, err,
                                c->stream);
             launch_qsa_score(d, qb, gb, iqv, scores, max_blocks, nb_max, false, err, c->stream);
             launch_qsa_select(d, qb, gb, scores, max_blocks, sel, sel_count, selection != nullptr, err, c->stream);
@@ -410,9 +438,21 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 selection->push_back(std::move(sc));
             }
         }
-        if (!launch_projection(out, gated, qw, y + row0 * H, H, (uint32_t)n_items, err, c->stream, partial,
-                               partial_floats))
-            launch_check_finite(y + row0 * H, n_items * H, err, c->stream);
+        if (parts == 1) {
+            if (!launch_projection(out, gated, qw, y + row0 * H, H, (uint32_t)n_items, err, c->stream, partial,
+                                   partial_floats))
+                launch_check_finite(y + row0 * H, n_items * H, err, c->stream);
+        } else {
+            // this rank's rows; zeros elsewhere (other ranks add theirs)
+            if (tb > 0) KQB_CUDA(cudaMemsetAsync(y, 0, (size_t)tb * H * 4, c->stream), diag, "output rows");
+            if (te < tokens)
+                KQB_CUDA(cudaMemsetAsync(y + (size_t)te * H, 0, (size_t)(tokens - te) * H * 4, c->stream), diag,
+                         "output rows");
+            if (te > tb &&
+                !launch_projection(out, gated + (size_t)tb * qw, qw, y + (size_t)tb * H, H, te - tb, err, c->stream,
+                                   partial, partial_floats))
+                launch_check_finite(y + (size_t)tb * H, (uint64_t)(te - tb) * H, err, c->stream);
+        }
         for (uint32_t b = 0; b < gb; ++b) {
             kq_qsa_state *s = states[g0 + b];
             s->length += tokens;
@@ -1019,9 +1059,19 @@ kq_status kq_b200_qsa_prefill_async(const kq_qsa_config *config, kq_qsa_state *s
 kq_status kq_b200_qsa_prefill_sharded_async(const kq_qsa_config *config, kq_qsa_state *state, const float *hidden,
                                             uint64_t T, float *output, uint32_t rank, uint32_t world,
                                             kq_b200_exchange_fn exchange, void *user, kq_diagnostic *diagnostic) {
+    return kq_b200_qsa_prefill_split_async(config, state, hidden, T, output, rank, world, 0, 1, exchange, user,
+                                           diagnostic);
+}
+
+kq_status kq_b200_qsa_prefill_split_async(const kq_qsa_config *config, kq_qsa_state *state, const float *hidden,
+                                          uint64_t T, float *output, uint32_t rank, uint32_t world,
+                                          uint32_t token_part, uint32_t token_parts, kq_b200_exchange_fn exchange,
+                                          void *user, kq_diagnostic *diagnostic) {
     kq_diagnostic_clear(diagnostic);
     if (world == 0 || rank >= world || (world > 1 && exchange == nullptr))
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "rank < world and an exchange function are required");
+    if (token_parts == 0 || token_part >= token_parts || (token_parts > 1 && world == 1))
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "token_part < token_parts (split only across ranks)");
     if (!config_valid(config) || !state_valid(state) || state->config != config || hidden == nullptr ||
         output == nullptr || T == 0)
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid config, state and device buffers are required");
@@ -1047,6 +1097,8 @@ kq_status kq_b200_qsa_prefill_sharded_async(const kq_qsa_config *config, kq_qsa_
     shard.world = world;
     shard.exchange = exchange;
     shard.user = user;
+    shard.part = token_part;
+    shard.parts = token_parts;
     return qsa_enqueue(c, config, w, states, 1, (uint32_t)T, hidden, output, err, nullptr, diagnostic,
                        /*check_input=*/true, &shard);
 }

@@ -224,12 +224,14 @@ struct QsaWeightsDev {
 // false and run launch_qsa_block_keys afterwards, because the block's other
 // raw rows are written by other CTAs of the same launch.
 // `index_queries` false: the entries' index queries are neither read nor
-// written (their scores are computed on another rank).
+// written (their scores are computed on another rank); `queries` false: the
+// same for the attention queries (their attention runs on another rank).
 void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
                         const QsaBatch &b, uint32_t batch, const float *proj,
                         uint32_t ldp, const float *iproj, uint32_t ldi,
                         float *q_out, float *iq_out, bool inline_block_key,
-                        bool index_queries, ErrorWord err, cudaStream_t stream);
+                        bool index_queries, bool queries, ErrorWord err,
+                        cudaStream_t stream);
 // `shared_sequence`: every entry is a token of the same sequence (one
 // cache, consecutive positions), so the entries share the block keys.
 void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,

@@ -130,7 +130,7 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
                    const float *__restrict__ proj, uint32_t ldp,
                    const float *__restrict__ iproj, uint32_t ldi,
                    float *__restrict__ q_out, float *__restrict__ iq_out,
-                   bool inline_block_key, bool index_queries, ErrorWord err) {
+                   bool inline_block_key, bool index_queries, bool queries, ErrorWord err) {
     pdl_wait();
     extern __shared__ float sh[];   // max(d, di) floats + 1
     if (qsa_error_raised(err)) return;
@@ -147,6 +147,7 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
     bool bad = false;
 
     if (role < d.q_heads) {
+        if (!queries) return;   // whole CTA: this entry's attention runs on another rank
         // query head: q part of the interleaved [q | gate] rows of the head
         const uint32_t h = role;
         for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) vec[i] = prow[(size_t)h * 2 * hd + i];
@@ -194,12 +195,12 @@ void launch_qsa_prepare(const QsaDims &d, const QsaWeightsDev &w,
                         const QsaBatch &b, uint32_t batch, const float *proj,
                         uint32_t ldp, const float *iproj, uint32_t ldi,
                         float *q_out, float *iq_out, bool inline_block_key,
-                        bool index_queries, ErrorWord err, cudaStream_t stream) {
+                        bool index_queries, bool queries, ErrorWord err, cudaStream_t stream) {
     size_t smem = (std::max(d.head_dim, d.index_dim) + 1) * sizeof(float);
     dim3 grid(batch, d.q_heads + d.kv_heads + d.index_heads + 1);
     KernelTimer timer("qsa_prepare", stream);
     launch_pdl(qsa_prepare_kernel, grid, kPrepThreads, smem, stream, d, w, b, proj, ldp, iproj, ldi,
-               q_out, iq_out, inline_block_key, index_queries, err);
+               q_out, iq_out, inline_block_key, index_queries, queries, err);
     count_launch();
 }
 

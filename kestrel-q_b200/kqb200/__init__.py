@@ -311,14 +311,15 @@ def qsa_prefill_async(state: QsaState, x_ptr: int, tokens: int, y_ptr: int) -> N
 
 
 def qsa_prefill_sharded_async(state: QsaState, x_ptr: int, tokens: int, y_ptr: int, rank: int, world: int,
-                              exchange) -> None:
+                              exchange, token_part: int = 0, token_parts: int = 1) -> None:
     """Tensor-parallel QSA prefill of one rank: the indexer's scores and top-k
-    of the 64-token chunks c with c % world == rank, `exchange` (an
-    abi.EXCHANGE_FN, kept alive by the caller) sums the selection buffer
-    over the ranks, then attention for every chunk."""
+    of this rank's 64-token chunk groups, `exchange` (an abi.EXCHANGE_FN,
+    kept alive by the caller) sums the selection buffer over the ranks, then
+    attention for every chunk, or with token_parts > 1 for token part
+    `token_part` only (zero output rows elsewhere)."""
     d = abi.Diagnostic()
-    abi.check(lib().kq_b200_qsa_prefill_sharded_async(state.layer.handle, state.handle, x_ptr, tokens, y_ptr, rank,
-                                                      world, exchange, None, C.byref(d)), d)
+    abi.check(lib().kq_b200_qsa_prefill_split_async(state.layer.handle, state.handle, x_ptr, tokens, y_ptr, rank,
+                                                    world, token_part, token_parts, exchange, None, C.byref(d)), d)
 
 
 def synchronize() -> None:

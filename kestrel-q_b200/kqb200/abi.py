@@ -180,6 +180,7 @@ _SIGNATURES = {
     "kq_b200_gdn_prefill_async": (C.c_int, [vp, vp, vp, u64, vp, vp]),
     "kq_b200_qsa_prefill_async": (C.c_int, [vp, vp, vp, u64, vp, vp]),
     "kq_b200_qsa_prefill_sharded_async": (C.c_int, [vp, vp, vp, u64, vp, u32, u32, vp, vp, vp]),
+    "kq_b200_qsa_prefill_split_async": (C.c_int, [vp, vp, vp, u64, vp, u32, u32, u32, u32, vp, vp, vp]),
     "kq_gdn_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
     "kq_qsa_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
 }

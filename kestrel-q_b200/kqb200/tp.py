@@ -21,6 +21,12 @@ scores and top-k are split by 64-token chunk (chunk c on rank c % N) and one
 all-reduce of the selection rows gives every rank every token's blocks,
 otherwise each rank selects for every token itself.  The out-projection
 columns of the group again give a partial sum (src/kq_qsa_qwen38.c:783-787).
+With more ranks than key/value heads (and a selection exchange), the ranks
+that share a key/value head split the tokens instead of the query heads:
+each holds every query head of its key/value head and runs the attention,
+gate and out-projection for its contiguous share of the tokens, writing
+zero rows elsewhere, so every rank reads only its share of the KV cache and
+the same all-reduce completes the output.
 
 Each shard is an ordinary layer of the smaller geometry, bound to the
 library through the same config API; only the partial outputs need the
@@ -155,6 +161,16 @@ def shard_qsa(w: synth.QsaLayerWeights, rank: int, world: int) -> synth.QsaLayer
     )
 
 
+def qsa_token_part(dims: synth.QsaDims, rank: int, world: int):
+    """(key/value head group, member, members) when `world` ranks split a QSA
+    layer's tokens within key/value-head groups (world a multiple of the
+    key/value head count and larger than it), else None."""
+    if world <= dims.kv_heads or world % dims.kv_heads:
+        return None
+    members = world // dims.kv_heads
+    return rank // members, rank % members, members
+
+
 def shard_qsa_cache(dims: synth.QsaDims, key: np.ndarray, value: np.ndarray, raw: np.ndarray,
                     rank: int, world: int):
     """Cache rows of a shard: its key/value heads, and the whole raw index keys."""
@@ -197,8 +213,16 @@ class TensorParallelBlock:
             layer = kq.GdnLayer(sw.dims, sw, provider, layer=layer_base + i)
             self.gdn_layers.append(layer)
             self.gdn_states.append(kq.GdnState(layer))
+        self.token_parts = []
         for i, w in enumerate(qsa_weights):
-            sw = shard_qsa(w, rank, world)
+            part = qsa_token_part(w.dims, rank, world) if self._exchange is not None else None
+            if part is None:
+                sw = shard_qsa(w, rank, world)
+                self.token_parts.append((0, 1))
+            else:
+                group, member, members = part
+                sw = shard_qsa(w, group, w.dims.kv_heads)
+                self.token_parts.append((member, members))
             layer = kq.QsaLayer(sw.dims, sw, provider, layer=layer_base + len(gdn_weights) + i)
             self.qsa_layers.append(layer)
             self.qsa_states.append(kq.QsaState(layer, capacity))
@@ -221,8 +245,10 @@ class TensorParallelBlock:
         if index < len(self.gdn_states):
             self.kq.gdn_prefill_async(self.gdn_states[index], x_ptr, tokens, y_ptr)
         elif self._exchange is not None:
-            self.kq.qsa_prefill_sharded_async(self.qsa_states[index - len(self.gdn_states)], x_ptr, tokens, y_ptr,
-                                              self.rank, self.world, self._exchange)
+            q = index - len(self.gdn_states)
+            part, parts = self.token_parts[q]
+            self.kq.qsa_prefill_sharded_async(self.qsa_states[q], x_ptr, tokens, y_ptr, self.rank, self.world,
+                                              self._exchange, part, parts)
         else:
             self.kq.qsa_prefill_async(self.qsa_states[index - len(self.gdn_states)], x_ptr, tokens, y_ptr)
 

@@ -82,7 +82,7 @@ def test_two_gpu_nccl_prefill_runs():
     assert line["n_gpus"] == 2 and line["value"] > 0 and line["scaling"] == "strong"
 
 
-def _tp_worker(rank, world, port, out_dir):
+def _tp_worker(rank, world, port, out_dir, kv_heads):
     import os
     import sys
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -100,7 +100,7 @@ def _tp_worker(rank, world, port, out_dir):
     kq.abi.check(kq.lib().kq_b200_set_device(rank, __import__("ctypes").byref(d)), d)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
                             device_id=torch.device("cuda", rank))
-    gd, qd, gdn_w, qsa_w, T = _small_block()
+    gd, qd, gdn_w, qsa_w, T = _small_block(kv_heads)
     prov = kq.Provider(rank)
     stream = torch.cuda.ExternalStream(kq.lib().kq_b200_get_stream())
     block = tp.TensorParallelBlock(kq, prov, gdn_w, [qsa_w], rank, world, capacity=512,
@@ -126,21 +126,23 @@ def _tp_worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def _small_block():
+def _small_block(kv_heads=2):
     from kqb200 import synth
     gd = synth.GdnDims(hidden=512, key_heads=4, value_heads=8, key_dim=128, value_dim=128)
-    qd = synth.QsaDims(hidden=512, query_heads=8, kv_heads=2, head_dim=256, index_heads=4, index_dim=128,
+    qd = synth.QsaDims(hidden=512, query_heads=8, kv_heads=kv_heads, head_dim=256, index_heads=4, index_dim=128,
                        block=4, budget=128, max_context=1024, rotary=64)
     gdn_w = [synth.gdn_layer(90 + l, gd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_Q4_K) for l in range(2)]
     qsa_w = synth.qsa_layer(95, qd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_BF16)
     return gd, qd, gdn_w, qsa_w, 300
 
 
-def test_two_gpu_tensor_parallel_block_with_sharded_indexer(oracle, tmp_path):
+@pytest.mark.parametrize("kv_heads", [2, 1])
+def test_two_gpu_tensor_parallel_block_with_sharded_indexer(oracle, tmp_path, kv_heads):
     """Two GPUs over NCCL: head-group shards, the QSA scores / top-k split by
     64-token chunk with one exchange of the selections, an all-reduce after
     every layer; each layer's reduced output against the oracle layer run on
-    the same input."""
+    the same input.  With one key/value head the two ranks split the QSA
+    attention by token instead of by query head."""
     import socket
 
     import torch
@@ -150,8 +152,8 @@ def test_two_gpu_tensor_parallel_block_with_sharded_indexer(oracle, tmp_path):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.spawn(_tp_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True)
-    gd, qd, gdn_w, qsa_w, T = _small_block()
+    mp.spawn(_tp_worker, args=(2, port, str(tmp_path), kv_heads), nprocs=2, join=True)
+    gd, qd, gdn_w, qsa_w, T = _small_block(kv_heads)
     src = np.load(tmp_path / "x.npy")
     conv = np.zeros(gd.conv_channels * gd.conv_kernel, np.float32)
     rec = np.zeros(gd.value_heads * gd.key_dim * gd.value_dim, np.float32)

@@ -123,6 +123,9 @@ def test_shard_geometry_and_rejections():
     assert np.array_equal(part.data.reshape(4, -1), t.data.reshape(4, -1)[:, 144:432])
     with pytest.raises(ValueError):
         tp.cols(t, 128, 512)
+    # more ranks than key/value heads: ranks split the tokens within a head group
+    assert tp.qsa_token_part(q, 5, 8) == (1, 1, 4)
+    assert tp.qsa_token_part(q, 1, 2) is None
 
 
 def _free_port() -> int:
