@@ -216,18 +216,21 @@ constexpr int kExXStride = kExK + 4;  // padded activation row (conflict-free fl
 constexpr int kExThreads = 256;
 constexpr size_t kExXBytes = (size_t)kExBatch * kExXStride * 4;   // per stage
 
-// Tile of TR weight rows x 64 batch rows.  TR = 8 (small batches: more
-// CTAs): a thread owns 2 rows x 1 batch row; TR = 32 (large batches): 4
-// rows x 2 batch rows, eight independent sequential chains per thread, each
+// Tile of TR weight rows x 64 batch rows.  TR = 4 (one batch tile: twice
+// the CTAs of TR = 8, all resident at two per SM): a thread owns 1 row x 1
+// batch row; TR = 8: 2 rows x 1 batch row; TR = 32 (large batches): 4 rows
+// x 2 batch rows, eight independent sequential chains per thread, each
 // weight value read from shared memory feeding two of them.
 template <int TR> struct ExTile {
     static constexpr int stages = TR == 8 ? 4 : 3;
-    static constexpr int rpt = TR == 8 ? 2 : 4;      // rows per thread
-    static constexpr int bpt = TR == 8 ? 1 : 2;      // batch rows per thread
+    static constexpr int rpt = TR == 4 ? 1 : TR == 8 ? 2 : 4;    // rows per thread
+    static constexpr int bpt = TR == 32 ? 2 : 1;                  // batch rows per thread
     static constexpr size_t wbytes = (size_t)TR * kExK * 4;   // per stage (F32 room)
     static constexpr size_t smem = stages * (kExXBytes + wbytes);
     static_assert(TR / rpt * (kExBatch / bpt) == kExThreads, "one output group per thread");
 };
+
+template <int TR> __host__ __device__ constexpr int rpt_of() { return ExTile<TR>::rpt; }
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
@@ -258,8 +261,8 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // the thread's rows rb .. rb + RPT - 1 (warp-uniform: broadcast weight
     // reads) and batch rows bb + 32 j
-    const int rb = TR == 8 ? 2 * (warp >> 1) : 4 * warp;
-    const int bb = TR == 8 ? (warp & 1) * 32 + lane : lane;
+    const int rb = TR == 32 ? 4 * warp : rpt_of<TR>() * (warp >> 1);
+    const int bb = TR == 32 ? lane : (warp & 1) * 32 + lane;
     const uint32_t nchunks = (m.cols + kExK - 1) / kExK;
     const bool xvec = (ldx % 4u) == 0u && (reinterpret_cast<uintptr_t>(x) & 15u) == 0u;
     constexpr uint32_t kElem = MODE == 1 ? 2u : 4u;   // staged weight bytes per value
@@ -471,9 +474,12 @@ void launch_projection_exact(const ProjSegments &in, const float *x,
                              uint32_t batch, ErrorWord err,
                              cudaStream_t stream) {
     KernelTimer timer("proj_exact", stream);
-    // 32-row tiles once the batch alone gives several CTAs per SM
+    // 32-row tiles once the batch alone gives several CTAs per SM; 4-row
+    // tiles for one batch tile (decode), so that the rows alone fill the SMs
     if (batch >= 1024)
         launch_exact_tiles<32>(in, x, ldx, y, ldy, batch, err, stream);
+    else if (batch <= (uint32_t)kExBatch)
+        launch_exact_tiles<4>(in, x, ldx, y, ldy, batch, err, stream);
     else
         launch_exact_tiles<8>(in, x, ldx, y, ldy, batch, err, stream);
     count_launch();

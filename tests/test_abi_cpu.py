@@ -153,3 +153,24 @@ def test_compute_entry_points_fail_loudly_without_gpu(kq):
     d = abi.Diagnostic()
     st = lib.kq_b200_provider_create(0, C.byref(p), C.byref(d))
     assert st != 0 and p.value is None
+
+
+def test_prefill_entry_points_validate_before_any_device_work(kq):
+    """The device prefill entry points reject bad arguments on the host, with
+    the reference's status codes, before touching a device."""
+    lib, abi = kq.lib(), kq.abi
+    d = abi.Diagnostic()
+    exch = abi.EXCHANGE_FN(lambda p, n, s, u: 0)
+    # no config / state
+    assert lib.kq_b200_gdn_prefill_async(None, None, None, 16, None, C.byref(d)) == abi.INVALID_ARGUMENT
+    assert lib.kq_b200_qsa_prefill_async(None, None, None, 16, None, C.byref(d)) == abi.INVALID_ARGUMENT
+    # rank outside the world, a world without an exchange, a token part outside its parts
+    assert lib.kq_b200_qsa_prefill_split_async(None, None, None, 16, None, 2, 2, 0, 1, exch, None,
+                                               C.byref(d)) == abi.INVALID_ARGUMENT
+    assert lib.kq_b200_qsa_prefill_split_async(None, None, None, 16, None, 0, 2, 0, 1, None, None,
+                                               C.byref(d)) == abi.INVALID_ARGUMENT
+    assert lib.kq_b200_qsa_prefill_split_async(None, None, None, 16, None, 0, 2, 2, 2, exch, None,
+                                               C.byref(d)) == abi.INVALID_ARGUMENT
+    assert lib.kq_b200_qsa_prefill_split_async(None, None, None, 16, None, 0, 1, 0, 2, exch, None,
+                                               C.byref(d)) == abi.INVALID_ARGUMENT
+    assert b"token_part" in d.message or b"rank" in d.message or b"valid" in d.message
