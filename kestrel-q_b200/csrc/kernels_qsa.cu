@@ -380,9 +380,9 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
                   uint32_t *__restrict__ selected_count, uint32_t rank_order, ErrorWord err) {
     pdl_wait();
     __shared__ uint32_t hist[256];
-    __shared__ uint32_t s_prefix, s_need, s_taken, s_tie_base;
+    __shared__ uint32_t s_prefix, s_need, s_tie_base, s_abv_base;
     __shared__ unsigned long long cand[kSelMax];
-    __shared__ uint32_t warp_tot[kSelThreads / 32];
+    __shared__ uint32_t warp_tot[kSelThreads / 32], warp_abv[kSelThreads / 32];
     if (qsa_error_raised(err)) return;
     const uint32_t b = blockIdx.x;
     const QsaSeq s = batch_seq(bt, b);
@@ -394,7 +394,7 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
         if (tid == 0) qsa_raise(err, kErrSelection);
         return;
     }
-    if (tid == 0) { s_prefix = 0; s_need = k; s_taken = 0; s_tie_base = 0; }
+    if (tid == 0) { s_prefix = 0; s_need = k; s_tie_base = 0; s_abv_base = 0; }
     uint32_t mask = 0;
     __syncthreads();
     if (k > 0 && k < n) {
@@ -439,12 +439,19 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
             __syncthreads();
         }
     }
-    // gather: keys above the threshold, then the s_need lowest-id ties
+    // gather: keys above the threshold, then the s_need lowest-id ties.
+    // Every selected id's position in id order is (#above before it) +
+    // min(#ties before it, ties needed), from block-wide prefix counts, so
+    // the id-ordered output needs no sort; the rank-ordered one is sorted.
     const bool take_all = (k == n);
     const uint32_t thr = s_prefix;
     const uint32_t ties_needed = take_all ? 0 : s_need;
-    for (uint32_t i = tid; i < kSelMax; i += blockDim.x) cand[i] = 0ull;
+    if (rank_order) {
+        for (uint32_t i = tid; i < kSelMax; i += blockDim.x) cand[i] = 0ull;
+    }
     __syncthreads();
+    const uint32_t lane = tid & 31, warp = tid >> 5;
+    const unsigned lt = (1u << lane) - 1u;
     for (uint32_t start = 0; start < n; start += blockDim.x) {
         uint32_t i = start + tid;
         uint32_t key = 0;
@@ -452,48 +459,61 @@ qsa_select_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ scores,
         if (valid) key = order_key(sc[i]);
         bool above = valid && (take_all || key > thr);
         bool tie = valid && !take_all && key == thr;
-        // ordered rank of ties within this chunk (ascending id)
-        unsigned ballot = __ballot_sync(0xffffffffu, tie);
-        uint32_t lane = tid & 31, warp = tid >> 5;
-        uint32_t before_in_warp = __popc(ballot & ((1u << lane) - 1u));
-        if (lane == 0) warp_tot[warp] = __popc(ballot);
+        const unsigned tb = __ballot_sync(0xffffffffu, tie), ab = __ballot_sync(0xffffffffu, above);
+        if (lane == 0) {
+            warp_tot[warp] = __popc(tb);
+            warp_abv[warp] = __popc(ab);
+        }
         __syncthreads();
-        uint32_t before = 0;
-        for (uint32_t w = 0; w < warp; ++w) before += warp_tot[w];
-        uint32_t tie_rank = s_tie_base + before + before_in_warp;
+        uint32_t tbefore = 0, abefore = 0;
+        for (uint32_t w = 0; w < warp; ++w) {
+            tbefore += warp_tot[w];
+            abefore += warp_abv[w];
+        }
+        const uint32_t tie_rank = s_tie_base + tbefore + __popc(tb & lt);
+        const uint32_t abv_rank = s_abv_base + abefore + __popc(ab & lt);
         if (above || (tie && tie_rank < ties_needed)) {
-            uint32_t slot = atomicAdd(&s_taken, 1u);
-            if (slot < kSelMax) cand[slot] = ((unsigned long long)key << 32) | (uint32_t)(~i);
+            if (rank_order) {
+                const uint32_t slot = abv_rank + min(tie_rank, ties_needed);
+                if (slot < kSelMax) cand[slot] = ((unsigned long long)key << 32) | (uint32_t)(~i);
+            } else {
+                selected[(size_t)b * d.topk + abv_rank + min(tie_rank, ties_needed)] = i;
+            }
         }
         __syncthreads();
         if (tid == 0) {
-            uint32_t tot = 0;
-            for (uint32_t w = 0; w < blockDim.x / 32; ++w) tot += warp_tot[w];
-            s_tie_base += tot;
+            uint32_t tt = 0, ta = 0;
+            for (uint32_t w = 0; w < blockDim.x / 32; ++w) {
+                tt += warp_tot[w];
+                ta += warp_abv[w];
+            }
+            s_tie_base += tt;
+            s_abv_base += ta;
         }
         __syncthreads();
     }
-    // bitonic sort, descending: by (score, -id) = the reference's rank
-    // order, or by -id alone (ascending block ids) when only the set matters
-    const unsigned long long key_mask = rank_order ? ~0ull : 0xffffffffull;
-    for (uint32_t size = 2; size <= kSelMax; size <<= 1) {
-        for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-            for (uint32_t i = tid; i < kSelMax; i += blockDim.x) {
-                uint32_t j = i ^ stride;
-                if (j > i) {
-                    bool desc = (i & size) == 0;
-                    unsigned long long a = cand[i], c = cand[j];
-                    if (((a & key_mask) < (c & key_mask)) == desc) { cand[i] = c; cand[j] = a; }
+    const uint32_t taken = s_abv_base + min(s_tie_base, ties_needed);
+    if (rank_order) {
+        // bitonic sort, descending by (score, -id): the reference's rank order
+        for (uint32_t size = 2; size <= kSelMax; size <<= 1) {
+            for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
+                for (uint32_t i = tid; i < kSelMax; i += blockDim.x) {
+                    uint32_t j = i ^ stride;
+                    if (j > i) {
+                        bool desc = (i & size) == 0;
+                        unsigned long long a = cand[i], c = cand[j];
+                        if ((a < c) == desc) { cand[i] = c; cand[j] = a; }
+                    }
                 }
+                __syncthreads();
             }
-            __syncthreads();
         }
+        for (uint32_t i = tid; i < k; i += blockDim.x)
+            selected[(size_t)b * d.topk + i] = ~(uint32_t)(cand[i] & 0xffffffffull);
     }
-    for (uint32_t i = tid; i < k; i += blockDim.x)
-        selected[(size_t)b * d.topk + i] = ~(uint32_t)(cand[i] & 0xffffffffull);
     if (tid == 0) {
         selected_count[b] = k;
-        if (s_taken != k) qsa_raise(err, kErrSelection);
+        if (taken != k) qsa_raise(err, kErrSelection);
     }
 }
 
