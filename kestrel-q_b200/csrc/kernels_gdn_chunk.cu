@@ -27,6 +27,8 @@
 
 #include <cmath>
 
+#include <cuda_bf16.h>
+
 namespace kqb {
 
 namespace {
@@ -52,14 +54,37 @@ __device__ __forceinline__ float chunk_sigmoid(float x) {
 
 }  // namespace
 
-// Work-space layout per (value head, chunk), in floats.
-constexpr size_t kChunkW = 0;                       // W [64][128]
-constexpr size_t kChunkU = kChunkW + kC * kD;       // U [64][128]
-constexpr size_t kChunkP = kChunkU + kC * kD;       // P [64][64]
-constexpr size_t kChunkEG = kChunkP + kC * kC;      // e^G_i [64]
+// Work-space layout per (value head, chunk), in floats.  The operands of
+// the phase-2 tensor-core products are stored as bf16 hi / lo pairs
+// (v = hi + lo, both bf16) in the padded row layouts the MMA fragments are
+// read from (rows of 136 or 72 bf16: conflict-free 32-bit fragment loads):
+//   W [64 tokens][128 features], Q [64][128], K^T [128 features][64 tokens],
+//   P [64][64]; U stays F32 [64][128].
+constexpr int kLK = 136;                            // bf16 row stride, K = 128
+constexpr int kLT = 72;                             // bf16 row stride, K = 64
+constexpr size_t kTileW = (size_t)kC * kLK / 2;     // floats of one bf16 [64][136] tile
+constexpr size_t kTileKT = (size_t)kD * kLT / 2;    // [128][72]
+constexpr size_t kTileP = (size_t)kC * kLT / 2;     // [64][72]
+constexpr size_t kChunkWh = 0;
+constexpr size_t kChunkWl = kChunkWh + kTileW;
+constexpr size_t kChunkQh = kChunkWl + kTileW;
+constexpr size_t kChunkQl = kChunkQh + kTileW;
+constexpr size_t kChunkKTh = kChunkQl + kTileW;
+constexpr size_t kChunkKTl = kChunkKTh + kTileKT;
+constexpr size_t kChunkPh = kChunkKTl + kTileKT;
+constexpr size_t kChunkPl = kChunkPh + kTileP;
+constexpr size_t kChunkU = kChunkPl + kTileP;       // U [64][128] F32
+constexpr size_t kChunkEG = kChunkU + kC * kD;      // e^G_i [64]
 constexpr size_t kChunkEGC = kChunkEG + kC;         // e^(G_C - G_i) [64]
 constexpr size_t kChunkTot = kChunkEGC + kC;        // e^G_C at [0], padding
 constexpr size_t kChunkFloats = kChunkTot + 64;
+static_assert(kChunkU % 4 == 0 && kChunkFloats % 64 == 0, "16-byte aligned regions");
+
+__device__ __forceinline__ void split_store(uint16_t *hi, uint16_t *lo, size_t i, float v) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = __bfloat16_as_ushort(h);
+    lo[i] = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(h)));
+}
 
 size_t gdn_chunk_workspace_floats(const GdnDims &d, uint32_t tokens) {
     const size_t chunks = (tokens + kC - 1) / kC;
@@ -143,7 +168,19 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
             const int j = j0 + 4 * r;
             const float f = j <= i ? expf(gi - Gs[j]) : 0.0f;
             Ls[i * kC + j] = j < i ? lk[r] * f : 0.0f;
-            wk[kChunkP + i * kC + j] = pq[r] * f;
+            split_store(reinterpret_cast<uint16_t *>(wk + kChunkPh), reinterpret_cast<uint16_t *>(wk + kChunkPl),
+                        (size_t)i * kLT + j, pq[r] * f);
+        }
+    }
+    // Q [64][136] and K^T [128][72] as bf16 pairs for the tensor-core pass
+    {
+        uint16_t *qh = reinterpret_cast<uint16_t *>(wk + kChunkQh), *ql = reinterpret_cast<uint16_t *>(wk + kChunkQl);
+        uint16_t *kh2 = reinterpret_cast<uint16_t *>(wk + kChunkKTh), *kl2 = reinterpret_cast<uint16_t *>(wk + kChunkKTl);
+        for (int e = tid; e < kC * kD; e += blockDim.x) {
+            const int r = e / kD, f = e % kD;
+            split_store(qh, ql, (size_t)r * kLK + f, Qs[sw(r, f & ~3) + (f & 3)]);
+            const int fi = e / kC, ti = e % kC;   // K^T row fi, column ti: coalesced along tokens
+            split_store(kh2, kl2, (size_t)fi * kLT + ti, Ks[sw(ti, fi & ~3) + (fi & 3)]);
         }
     }
     const float gc = Gs[n - 1];
@@ -187,202 +224,219 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
         }
     }
     __syncthreads();
-    for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
-        *reinterpret_cast<float4 *>(wk + kChunkW + 4 * i) = *reinterpret_cast<const float4 *>(Ws + 4 * i);
-        *reinterpret_cast<float4 *>(wk + kChunkU + 4 * i) = *reinterpret_cast<const float4 *>(Us + 4 * i);
+    {
+        uint16_t *wh = reinterpret_cast<uint16_t *>(wk + kChunkWh), *wl = reinterpret_cast<uint16_t *>(wk + kChunkWl);
+        for (int e = tid; e < kC * kD; e += blockDim.x) split_store(wh, wl, (size_t)(e / kD) * kLK + e % kD, Ws[e]);
     }
+    for (int i = tid; i < kC * (kD / 4); i += blockDim.x)
+        *reinterpret_cast<float4 *>(wk + kChunkU + 4 * i) = *reinterpret_cast<const float4 *>(Us + 4 * i);
 }
 
 // ---------------------------------------------------------------- phase 2
-// CW state columns per CTA (32, 16 or 8: fewer value heads per GPU take
-// narrower slices, so that the grid still covers the SMs); NT threads =
-// CW columns x G = NT / CW row groups.  The tiles are read as 16-byte
-// vectors along their rows (broadcast within a row group), four K steps per
-// vector.  Tile loads are cp.async copies issued ahead of use: the next
-// chunk's W during the whole current chunk (two W buffers), the current
-// chunk's Q, P and decay factors during its delta phase, its K during the
-// O phase.  Q and K are stored unscaled; e^G scales a row's Q . S dot and
-// e^(G_C - G) scales delta in the state update.
+// One CTA per (value head, slice of CW state columns), 256 threads, walking
+// the chunks in order.  The three products of a chunk run on the tensor
+// cores as warp MMAs (mma.sync m16n8k16, bf16 operands, F32 accumulate),
+// each with the three-term split a b ~ a_hi b_hi + a_hi b_lo + a_lo b_hi:
+//   delta = U - W S              (64 x CW, K = 128)
+//   O     = e^G (Q S) + P delta  (64 x CW, K = 128 and 64)
+//   S     = e^G_C S + K^T delta' (128 x CW, K = 64; delta' = e^(G_C - G) delta)
+// Warp w keeps rows 16w .. 16w+15 of the F32 state in its accumulator
+// registers for the whole pass; after each update the state is written back
+// to shared memory as bf16 pairs, transposed ([column][row]), as the B
+// operand of the next chunk.  W is prefetched one chunk ahead; Q, P and the
+// decay factors load during the delta products, K^T during the O products.
 
-__device__ __forceinline__ void chunk_cp16(float *smem, const float *gmem, bool valid) {
+__device__ __forceinline__ void chunk_cp16(void *smem, const void *gmem) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(smem);
-    const unsigned n = valid ? 16u : 0u;   // 0: zero fill
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gmem), "r"(n));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gmem));
 }
 __device__ __forceinline__ void chunk_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
 __device__ __forceinline__ void chunk_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
-template <int CW, int NT>
-__global__ void __launch_bounds__(NT, 1)
-gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *__restrict__ qk,
-                       const float *__restrict__ work, float *__restrict__ obuf, ErrorWord err) {
-    constexpr int G = NT / CW;       // row groups
-    constexpr int RD = kC / G;       // delta / O rows per thread
-    constexpr int RS = kD / G;       // state rows per thread
-    constexpr int LT = kD + 4;       // row stride of the W / Q / K tiles
-    constexpr int LP = kC + 4;       // row stride of P
-    static_assert(RS % 4 == 0, "state rows in 16-byte groups");
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// A fragment (rows m0 .. m0+15, K k0 .. k0+15) of a row-major bf16 tile with
+// row stride ld; B fragment (columns n0 .. n0+7) of a [n][k] bf16 tile.
+__device__ __forceinline__ void frag_a(const uint16_t *t, int ld, int m0, int k0, int g, int q, uint32_t (&a)[4]) {
+    a[0] = *reinterpret_cast<const uint32_t *>(t + (m0 + g) * ld + k0 + 2 * q);
+    a[1] = *reinterpret_cast<const uint32_t *>(t + (m0 + g + 8) * ld + k0 + 2 * q);
+    a[2] = *reinterpret_cast<const uint32_t *>(t + (m0 + g) * ld + k0 + 2 * q + 8);
+    a[3] = *reinterpret_cast<const uint32_t *>(t + (m0 + g + 8) * ld + k0 + 2 * q + 8);
+}
+__device__ __forceinline__ void frag_b(const uint16_t *t, int ld, int n0, int k0, int g, int q, uint32_t &b0,
+                                       uint32_t &b1) {
+    b0 = *reinterpret_cast<const uint32_t *>(t + (n0 + g) * ld + k0 + 2 * q);
+    b1 = *reinterpret_cast<const uint32_t *>(t + (n0 + g) * ld + k0 + 2 * q + 8);
+}
+// acc += A B over K = 16 * KS steps, three-term split
+template <int KS>
+__device__ __forceinline__ void mma3(float (&acc)[4], const uint16_t *ah, const uint16_t *al, int lda, int m0,
+                                     const uint16_t *bh, const uint16_t *bl, int ldb, int n0, int g, int q) {
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+        uint32_t a[4], b0, b1;
+        frag_a(ah, lda, m0, 16 * kk, g, q, a);
+        frag_b(bh, ldb, n0, 16 * kk, g, q, b0, b1);
+        mma_bf16(acc, a, b0, b1);
+        uint32_t c0, c1;
+        frag_b(bl, ldb, n0, 16 * kk, g, q, c0, c1);
+        mma_bf16(acc, a, c0, c1);
+        frag_a(al, lda, m0, 16 * kk, g, q, a);
+        mma_bf16(acc, a, b0, b1);
+    }
+}
+
+template <int CW>
+struct StateSmem {
+    static constexpr size_t st = (size_t)CW * kLK;       // bf16 elements of one S^T part
+    static constexpr size_t w = (size_t)kC * kLK;        // one W / Q part
+    static constexpr size_t kt = (size_t)kD * kLT;       // one K^T part
+    static constexpr size_t p = (size_t)kC * kLT;        // one P part
+    static constexpr size_t dt = (size_t)CW * kLT;       // one delta^T part
+    static constexpr size_t bytes = (2 * st + 4 * w + 2 * w + 2 * kt + 2 * p + 4 * dt) * 2 + (2 * kC + 4) * 4;
+};
+
+template <int CW>
+__global__ void __launch_bounds__(256, 1)
+gdn_chunk_state_kernel(GdnDims d, GdnBatchPtrs p, uint32_t tokens, const float *__restrict__ work,
+                       float *__restrict__ obuf, ErrorWord err) {
+    constexpr int NT = CW / 8;        // n8 tiles of the slice
+    using SM = StateSmem<CW>;
     pdl_wait();
-    extern __shared__ __align__(16) float cs[];
-    float *S = cs;                   // [128][CW]
-    float *Wb = S + kD * CW;         // [2][64][LT]
-    float *Qs = Wb + 2 * kC * LT;    // [64][LT]
-    float *Ks = Qs + kC * LT;        // [64][LT]
-    float *Ps = Ks + kC * LT;        // [64][LP]
-    float *Ds = Ps + kC * LP;        // delta [64][CW]
-    float *Eg = Ds + kC * CW;        // e^G_i [64], e^(G_C - G_i) [64], e^G_C [4]
+    extern __shared__ __align__(16) uint16_t sm16[];
+    uint16_t *STh = sm16, *STl = STh + SM::st;                 // S^T [CW][136]
+    uint16_t *Wb = STl + SM::st;                               // [2 buffers][hi, lo][64][136]
+    uint16_t *Qh = Wb + 4 * SM::w, *Ql = Qh + SM::w;           // [64][136]
+    uint16_t *KTh = Ql + SM::w, *KTl = KTh + SM::kt;           // [128][72]
+    uint16_t *Ph = KTl + SM::kt, *Pl = Ph + SM::p;             // [64][72]
+    uint16_t *DTh = Pl + SM::p, *DTl = DTh + SM::dt;           // delta^T [CW][72]
+    uint16_t *D2h = DTl + SM::dt, *D2l = D2h + SM::dt;         // (e^(G_C - G) delta)^T
+    float *Eg = reinterpret_cast<float *>(D2l + SM::dt);       // e^G [64], e^(G_C - G) [64], e^G_C
     if (chunk_error_raised(err)) return;
     const uint32_t h = blockIdx.x, sl = blockIdx.y;
-    const uint32_t kh = h / d.repeat;
     const uint32_t col0 = sl * CW;
-    const int tid = threadIdx.x, f = tid % CW, grp = tid / CW;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
     const float *sin_ = p.rec_in[0] + (size_t)h * kD * kD;
     float *sout = p.rec_out[0] + (size_t)h * kD * kD;
     const uint32_t nchunks = (tokens + kC - 1) / kC;
     auto chunk_work = [&](uint32_t c) { return work + ((size_t)c * d.value_heads + h) * kChunkFloats; };
+    auto copy = [&](void *dst, const float *src, size_t bytes) {
+        for (size_t i = tid; i < bytes / 16; i += blockDim.x)
+            chunk_cp16(reinterpret_cast<uint8_t *>(dst) + 16 * i, reinterpret_cast<const uint8_t *>(src) + 16 * i);
+    };
     auto load_w = [&](uint32_t c) {
         const float *wk = chunk_work(c);
-        float *dst = Wb + (c & 1u) * kC * LT;
-        for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
-            const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
-            chunk_cp16(dst + r * LT + c4, wk + kChunkW + r * kD + c4, true);
+        uint16_t *dst = Wb + (c & 1u) * 2 * SM::w;
+        copy(dst, wk + kChunkWh, SM::w * 2);
+        copy(dst + SM::w, wk + kChunkWl, SM::w * 2);
+    };
+    // the state rows of warp w, columns of the slice, in accumulator layout
+    float sacc[NT][4];
+    const int r0 = 16 * warp + g;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int c = 8 * nt + 2 * q;
+        sacc[nt][0] = sin_[(size_t)r0 * kD + col0 + c];
+        sacc[nt][1] = sin_[(size_t)r0 * kD + col0 + c + 1];
+        sacc[nt][2] = sin_[(size_t)(r0 + 8) * kD + col0 + c];
+        sacc[nt][3] = sin_[(size_t)(r0 + 8) * kD + col0 + c + 1];
+    }
+    auto store_st = [&]() {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int c = 8 * nt + 2 * q;
+            split_store(STh, STl, (size_t)c * kLK + r0, sacc[nt][0]);
+            split_store(STh, STl, (size_t)(c + 1) * kLK + r0, sacc[nt][1]);
+            split_store(STh, STl, (size_t)c * kLK + r0 + 8, sacc[nt][2]);
+            split_store(STh, STl, (size_t)(c + 1) * kLK + r0 + 8, sacc[nt][3]);
         }
     };
-    for (int i = tid; i < kD * CW; i += blockDim.x) S[i] = sin_[(size_t)(i / CW) * kD + col0 + i % CW];
+    store_st();
     if (nchunks > 0) load_w(0);
     chunk_commit();
     bool bad = false;
     for (uint32_t c = 0; c < nchunks; ++c) {
         const float *wk = chunk_work(c);
         const uint32_t t0 = c * kC, n = min((uint32_t)kC, tokens - t0);
-        __syncthreads();   // the previous chunk is done with Q, K, P, D and its W buffer
-        // group A: Q, P, decay factors of this chunk
-        for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
-            const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
-            const bool in = (uint32_t)r < n;
-            const size_t item = t0 + (in ? r : 0);
-            chunk_cp16(Qs + r * LT + c4, qk + (item * 2 + 0) * d.key_width + kh * kD + c4, in);
-        }
-        for (int i = tid; i < kC * (kC / 4); i += blockDim.x) {
-            const int r = i / (kC / 4), c4 = (i % (kC / 4)) * 4;
-            chunk_cp16(Ps + r * LP + c4, wk + kChunkP + r * kC + c4, true);
-        }
-        if (tid < 32) chunk_cp16(Eg + tid * 4, wk + kChunkEG + tid * 4, true);   // e^G, e^(G_C - G)
-        if (tid == 32) chunk_cp16(Eg + 128, wk + kChunkTot, true);                // e^G_C (+ padding)
+        __syncthreads();   // the previous chunk is done with Q, K^T, P, delta, decay factors and its W
+        copy(Qh, wk + kChunkQh, SM::w * 2);          // group A: Q, P, decay factors
+        copy(Ql, wk + kChunkQl, SM::w * 2);
+        copy(Ph, wk + kChunkPh, SM::p * 2);
+        copy(Pl, wk + kChunkPl, SM::p * 2);
+        copy(Eg, wk + kChunkEG, (2 * kC + 4) * 4);
         chunk_commit();
-        // group B: K of this chunk
-        for (int i = tid; i < kC * (kD / 4); i += blockDim.x) {
-            const int r = i / (kD / 4), c4 = (i % (kD / 4)) * 4;
-            const bool in = (uint32_t)r < n;
-            const size_t item = t0 + (in ? r : 0);
-            chunk_cp16(Ks + r * LT + c4, qk + (item * 2 + 1) * d.key_width + kh * kD + c4, in);
-        }
+        copy(KTh, wk + kChunkKTh, SM::kt * 2);       // group B: K^T
+        copy(KTl, wk + kChunkKTl, SM::kt * 2);
         chunk_commit();
-        // group C: W of the next chunk
-        if (c + 1 < nchunks) load_w(c + 1);
+        if (c + 1 < nchunks) load_w(c + 1);          // group C: the next chunk's W
         chunk_commit();
         chunk_wait<3>();   // this chunk's W (committed one chunk earlier)
-        __syncthreads();
-        const float *Ws = Wb + (c & 1u) * kC * LT;
-        // delta = U - W S : thread -> column f, rows RD grp .. RD grp + RD - 1
-        {
-            float acc[RD];
+        __syncthreads();   // ... and S^T of the previous update, visible to every warp
+        const uint16_t *Wh = Wb + (c & 1u) * 2 * SM::w, *Wl = Wh + SM::w;
+        // ---- delta = U - W S, and delta' = e^(G_C - G) delta, both stored transposed as bf16 pairs
+        for (int tt = warp; tt < 4 * NT; tt += 8) {
+            const int mt = tt / NT, nt = tt % NT;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            mma3<kD / 16>(acc, Wh, Wl, kLK, 16 * mt, STh, STl, kLK, 8 * nt, g, q);
 #pragma unroll
-            for (int r = 0; r < RD; ++r) acc[r] = 0.f;
-#pragma unroll 2
-            for (int k = 0; k < kD; k += 4) {
-                const float s0 = S[k * CW + f], s1 = S[(k + 1) * CW + f], s2 = S[(k + 2) * CW + f],
-                            s3 = S[(k + 3) * CW + f];
-#pragma unroll
-                for (int r = 0; r < RD; ++r) {
-                    const float4 w4 = *reinterpret_cast<const float4 *>(Ws + (RD * grp + r) * LT + k);
-                    acc[r] = fmaf(w4.w, s3, fmaf(w4.z, s2, fmaf(w4.y, s1, fmaf(w4.x, s0, acc[r]))));
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < RD; ++r) {
-                const int i = RD * grp + r;
-                Ds[i * CW + f] = wk[kChunkU + i * kD + col0 + f] - acc[r];
+            for (int e = 0; e < 4; ++e) {
+                const int row = 16 * mt + g + (e >> 1) * 8, col = 8 * nt + 2 * q + (e & 1);
+                const float dl = wk[kChunkU + row * kD + col0 + col] - acc[e];
+                split_store(DTh, DTl, (size_t)col * kLT + row, dl);
+                split_store(D2h, D2l, (size_t)col * kLT + row, wk[kChunkEGC + row] * dl);
             }
         }
         chunk_wait<2>();   // Q, P, decay factors
-        __syncthreads();
-        // O = e^G (Q S) + P delta for the same rows / column
-        {
-            float acc[RD];
+        __syncthreads();   // ... and delta^T from every warp
+        // ---- O = e^G (Q S) + P delta
+        for (int tt = warp; tt < 4 * NT; tt += 8) {
+            const int mt = tt / NT, nt = tt % NT;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            mma3<kD / 16>(acc, Qh, Ql, kLK, 16 * mt, STh, STl, kLK, 8 * nt, g, q);
 #pragma unroll
-            for (int r = 0; r < RD; ++r) acc[r] = 0.f;
-#pragma unroll 2
-            for (int k = 0; k < kD; k += 4) {
-                const float s0 = S[k * CW + f], s1 = S[(k + 1) * CW + f], s2 = S[(k + 2) * CW + f],
-                            s3 = S[(k + 3) * CW + f];
+            for (int e = 0; e < 4; ++e) acc[e] *= Eg[16 * mt + g + (e >> 1) * 8];
+            mma3<kC / 16>(acc, Ph, Pl, kLT, 16 * mt, DTh, DTl, kLT, 8 * nt, g, q);
 #pragma unroll
-                for (int r = 0; r < RD; ++r) {
-                    const float4 q4 = *reinterpret_cast<const float4 *>(Qs + (RD * grp + r) * LT + k);
-                    acc[r] = fmaf(q4.w, s3, fmaf(q4.z, s2, fmaf(q4.y, s1, fmaf(q4.x, s0, acc[r]))));
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < RD; ++r) acc[r] *= Eg[RD * grp + r];
-#pragma unroll 2
-            for (int j = 0; j < kC; j += 4) {
-                const float d0 = Ds[j * CW + f], d1 = Ds[(j + 1) * CW + f], d2 = Ds[(j + 2) * CW + f],
-                            d3 = Ds[(j + 3) * CW + f];
-#pragma unroll
-                for (int r = 0; r < RD; ++r) {
-                    const float4 p4 = *reinterpret_cast<const float4 *>(Ps + (RD * grp + r) * LP + j);
-                    acc[r] = fmaf(p4.w, d3, fmaf(p4.z, d2, fmaf(p4.y, d1, fmaf(p4.x, d0, acc[r]))));
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < RD; ++r) {
-                const uint32_t i = RD * grp + r;
-                if (i < n) {
-                    bad |= !isfinite(acc[r]);
-                    obuf[(size_t)(t0 + i) * d.value_width + h * kD + col0 + f] = acc[r];
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t row = 16 * mt + g + (e >> 1) * 8, col = 8 * nt + 2 * q + (e & 1);
+                if (row < n) {
+                    bad |= !isfinite(acc[e]);
+                    obuf[(size_t)(t0 + row) * d.value_width + h * kD + col0 + col] = acc[e];
                 }
             }
         }
-        chunk_wait<1>();   // K
-        __syncthreads();   // every read of the old S is done; K visible
-        // S = e^(G_C) S + K^T (e^(G_C - G) delta) : thread -> column f, rows RS grp .. RS grp + RS - 1
+        chunk_wait<1>();   // K^T
+        __syncthreads();   // every read of S^T is done; K^T visible
+        // ---- S = e^G_C S + K^T delta'
         {
-            const float eg_c = Eg[128];
-            float acc[RS];
+            const float eg_c = Eg[2 * kC];
 #pragma unroll
-            for (int r = 0; r < RS; ++r) acc[r] = eg_c * S[(RS * grp + r) * CW + f];
-#pragma unroll 2
-            for (int i = 0; i < kC; ++i) {
-                const float dv = Eg[64 + i] * Ds[i * CW + f];
+            for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
-                for (int r = 0; r < RS; r += 4) {
-                    const float4 k4 = *reinterpret_cast<const float4 *>(Ks + i * LT + RS * grp + r);
-                    acc[r] = fmaf(k4.x, dv, acc[r]);
-                    acc[r + 1] = fmaf(k4.y, dv, acc[r + 1]);
-                    acc[r + 2] = fmaf(k4.z, dv, acc[r + 2]);
-                    acc[r + 3] = fmaf(k4.w, dv, acc[r + 3]);
-                }
+                for (int e = 0; e < 4; ++e) sacc[nt][e] *= eg_c;
+                mma3<kC / 16>(sacc[nt], KTh, KTl, kLT, 16 * warp, D2h, D2l, kLT, 8 * nt, g, q);
             }
-#pragma unroll
-            for (int r = 0; r < RS; ++r) S[(RS * grp + r) * CW + f] = acc[r];
+            store_st();
         }
     }
     chunk_wait<0>();
-    __syncthreads();
-    for (int i = tid; i < kD * CW; i += blockDim.x) {
-        const float v = S[i];
-        bad |= !isfinite(v);
-        sout[(size_t)(i / CW) * kD + col0 + i % CW] = v;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const int c = 8 * nt + 2 * q;
+        bad |= !isfinite(sacc[nt][0]) || !isfinite(sacc[nt][1]) || !isfinite(sacc[nt][2]) || !isfinite(sacc[nt][3]);
+        sout[(size_t)r0 * kD + col0 + c] = sacc[nt][0];
+        sout[(size_t)r0 * kD + col0 + c + 1] = sacc[nt][1];
+        sout[(size_t)(r0 + 8) * kD + col0 + c] = sacc[nt][2];
+        sout[(size_t)(r0 + 8) * kD + col0 + c + 1] = sacc[nt][3];
     }
     if (__syncthreads_or(bad) && tid == 0) chunk_raise(err, kErrNonFinite);
-}
-
-constexpr int kStateThreads = 256;   // 512 measured slower (register-limited, one CTA per SM either way)
-
-template <int CW>
-static size_t state_smem() {
-    return (size_t)(kD * CW + 4 * kC * (kD + 4) + kC * (kC + 4) + kC * CW + 2 * kC + 4) * sizeof(float);
 }
 
 // ---------------------------------------------------------------- phase 3
@@ -421,12 +475,12 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
-        cudaFuncSetAttribute(gdn_chunk_state_kernel<32, kStateThreads>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)state_smem<32>());
-        cudaFuncSetAttribute(gdn_chunk_state_kernel<16, kStateThreads>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)state_smem<16>());
-        cudaFuncSetAttribute(gdn_chunk_state_kernel<8, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)state_smem<8>());
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)StateSmem<32>::bytes);
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)StateSmem<16>::bytes);
+        cudaFuncSetAttribute(gdn_chunk_state_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)StateSmem<8>::bytes);
         attr = true;
     }
     {
@@ -439,16 +493,15 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
         // the sequential pass: (value heads x column slices) CTAs, slices
         // narrow enough that the grid reaches about 128 CTAs
         KernelTimer t2("gdn_chunk_state", stream);
-        if (d.value_heads >= 32) {
-            launch_pdl(gdn_chunk_state_kernel<32, kStateThreads>, dim3(d.value_heads, kD / 32), kStateThreads,
-                       state_smem<32>(), stream, d, p, tokens, qk, work, obuf, err);
-        } else if (d.value_heads >= 16) {
-            launch_pdl(gdn_chunk_state_kernel<16, kStateThreads>, dim3(d.value_heads, kD / 16), kStateThreads,
-                       state_smem<16>(), stream, d, p, tokens, qk, work, obuf, err);
-        } else {
-            launch_pdl(gdn_chunk_state_kernel<8, 256>, dim3(d.value_heads, kD / 8), 256, state_smem<8>(), stream, d,
-                       p, tokens, qk, work, obuf, err);
-        }
+        if (d.value_heads >= 32)
+            launch_pdl(gdn_chunk_state_kernel<32>, dim3(d.value_heads, kD / 32), 256, StateSmem<32>::bytes, stream,
+                       d, p, tokens, work, obuf, err);
+        else if (d.value_heads >= 16)
+            launch_pdl(gdn_chunk_state_kernel<16>, dim3(d.value_heads, kD / 16), 256, StateSmem<16>::bytes, stream,
+                       d, p, tokens, work, obuf, err);
+        else
+            launch_pdl(gdn_chunk_state_kernel<8>, dim3(d.value_heads, kD / 8), 256, StateSmem<8>::bytes, stream,
+                       d, p, tokens, work, obuf, err);
         count_launch();
     }
     {
