@@ -47,6 +47,9 @@ struct kq_qsa_state final : Rollbackable {
     int device = 0;
     uint64_t capacity = 0, length = 0;
     float *key = nullptr, *value = nullptr, *raw = nullptr, *block_keys = nullptr;
+    // bf16 hi / lo copies of the K / V rows for the tensor-core attention
+    // (null when it does not cover the geometry)
+    uint16_t *key_split = nullptr, *value_split = nullptr;
     uint64_t owned_bytes = 0;
     uint64_t synced_length = 0;
     std::vector<std::pair<uint32_t, uint64_t>> history;
@@ -355,7 +358,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
         }
         if (chunked) {
             kq_qsa_state *s = states[0];
-            const QsaSeq seq{s->key, s->value, s->raw, s->block_keys, (uint32_t)s->length, (uint32_t)s->capacity};
+            const QsaSeq seq{s->key,    s->value,       s->raw,         s->block_keys, (uint32_t)s->length,
+                             (uint32_t)s->capacity, s->key_split, s->value_split};
             auto uniform_batch = [&](uint32_t t0) {
                 QsaBatch qb;
                 qb.s[0] = seq;
@@ -410,6 +414,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                 kq_qsa_state *s = states[g0 + b];
                 qb.s[b].key = s->key;
                 qb.s[b].value = s->value;
+                qb.s[b].key_split = s->key_split;
+                qb.s[b].value_split = s->value_split;
                 qb.s[b].raw = s->raw;
                 qb.s[b].block_keys = s->block_keys;
                 qb.s[b].length = (uint32_t)(s->length + t);
@@ -786,6 +792,21 @@ kq_status kq_qsa_state_create(const kq_qsa_config *config, uint64_t token_capaci
         delete s;
         return fail(diagnostic, KQ_STATUS_OUT_OF_MEMORY, "could not allocate bounded QSA cache buffers");
     }
+    size_t split_bytes = 0;
+    if (qsa_split_cache_used(kernel_dims(config))) {
+        // hi + lo bf16 (1040-byte rows of 256 features)
+        split_bytes = token_capacity * config->dims.key_value_head_count * kQsaSplitRow * 2;
+        if (cudaMalloc(&s->key_split, split_bytes) != cudaSuccess ||
+            cudaMalloc(&s->value_split, split_bytes) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(s->key); cudaFree(s->value); cudaFree(s->raw); cudaFree(s->block_keys);
+            cudaFree(s->key_split); cudaFree(s->value_split);
+            delete s;
+            return fail(diagnostic, KQ_STATUS_OUT_OF_MEMORY, "could not allocate bounded QSA cache buffers");
+        }
+        cudaMemsetAsync(s->key_split, 0, split_bytes, c->stream);
+        cudaMemsetAsync(s->value_split, 0, split_bytes, c->stream);
+    }
     cudaMemsetAsync(s->key, 0, kvb, c->stream);
     cudaMemsetAsync(s->value, 0, kvb, c->stream);
     cudaMemsetAsync(s->raw, 0, rb, c->stream);
@@ -793,7 +814,7 @@ kq_status kq_qsa_state_create(const kq_qsa_config *config, uint64_t token_capaci
     s->magic = kQsaStateMagic;
     s->config = config;
     s->capacity = token_capacity;
-    s->owned_bytes = sizeof(*s) + 2 * kvb + rb + bkb;
+    s->owned_bytes = sizeof(*s) + 2 * kvb + rb + bkb + 2 * split_bytes;
     *out_state = s;
     return KQ_STATUS_OK;
 }
@@ -807,6 +828,7 @@ void kq_qsa_state_close(kq_qsa_state *state) {
         c->dirty.erase(state);
     }
     cudaFree(state->key); cudaFree(state->value); cudaFree(state->raw); cudaFree(state->block_keys);
+    cudaFree(state->key_split); cudaFree(state->value_split);
     state->magic = 0;
     delete state;
 }
@@ -857,6 +879,15 @@ kq_status kq_qsa_state_export_f32(const kq_qsa_state *state, float *key_cache, u
     return KQ_STATUS_OK;
 }
 
+// The hi / lo copies of imported K / V rows (the appends of later calls
+// write their own).
+static void split_imported_rows(kq_qsa_state *s, uint64_t length, cudaStream_t stream) {
+    if (s->key_split == nullptr || length == 0) return;
+    const uint32_t kvh = s->config->dims.key_value_head_count;
+    launch_qsa_split_rows(s->key, s->key_split, length, kvh, s->capacity, stream);
+    launch_qsa_split_rows(s->value, s->value_split, length, kvh, s->capacity, stream);
+}
+
 kq_status kq_qsa_state_import_f32(kq_qsa_state *state, const float *key_cache, uint64_t key_count,
                                   const float *value_cache, uint64_t value_count, const float *raw_cache,
                                   uint64_t raw_count, uint64_t length, kq_diagnostic *diagnostic) {
@@ -890,6 +921,7 @@ kq_status kq_qsa_state_import_f32(kq_qsa_state *state, const float *key_cache, u
                  diagnostic, "import");
         KQB_CUDA(cudaMemcpyAsync(state->raw, raw_cache, eraw * 4, cudaMemcpyDeviceToDevice, c->stream), diagnostic,
                  "import");
+        split_imported_rows(state, length, c->stream);
         KQB_CUDA(cudaStreamSynchronize(c->stream), diagnostic, "import");
         state->bk_valid = 0;
         state->length = length;
@@ -930,6 +962,8 @@ kq_status kq_qsa_state_import_f32(kq_qsa_state *state, const float *key_cache, u
                  "import");
         KQB_CUDA(copy_sync(state->raw, rh.data(), eraw * 4, cudaMemcpyHostToDevice, c->stream), diagnostic,
                  "import");
+        split_imported_rows(state, length, c->stream);
+        KQB_CUDA(cudaStreamSynchronize(c->stream), diagnostic, "import");
     }
     // cached block keys are rebuilt from the imported raw keys by the next
     // call, which knows the index-key norm weights

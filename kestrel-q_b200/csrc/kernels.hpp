@@ -185,7 +185,17 @@ struct QsaSeq {
     float *block_keys;   // [di][capacity/block] feature-major
     uint32_t length;     // committed length before this token
     uint32_t capacity;
+    // bf16 hi / lo copies of the key and value rows (v = hi + lo), written
+    // beside the F32 rows, KV-head major: [Hkv][capacity][kQsaSplitRow]
+    // uint16 with a row = [hi 256 | lo 256 | 8 unused]; null when the
+    // tensor-core attention does not cover the geometry (head_dim != 256)
+    uint16_t *key_split = nullptr;
+    uint16_t *value_split = nullptr;
 };
+
+// uint16 elements per row of the split cache: 1040 bytes, so that rows
+// copied back to back into shared memory start in 8 different bank groups
+constexpr uint32_t kQsaSplitRow = 520;
 
 // Entries of one launch: up to kMaxBatch independent sequences, or (uniform
 // != 0) any number of consecutive tokens of one sequence: entry b is s[0]
@@ -253,6 +263,15 @@ void launch_qsa_combine(const QsaDims &d, uint32_t batch,
                         const float *partial_o, const float *partial_ml,
                         uint32_t splits, const float *proj, uint32_t ldp,
                         float *gated, ErrorWord err, cudaStream_t stream);
+// True when the attention runs on the tensor cores (head_dim 256, at most 8
+// query heads per KV head), which reads the bf16 hi / lo copies of the
+// cache rows; the state then keeps them.
+bool qsa_split_cache_used(const QsaDims &d);
+bool force_simt_attention();
+// Writes the hi / lo copies of tokens [0, length) of an F32 cache
+// [token][kv_heads][256] into the split layout of a `capacity`-token cache.
+void launch_qsa_split_rows(const float *src, uint16_t *dst, uint64_t length, uint32_t kv_heads,
+                           uint64_t capacity, cudaStream_t stream);
 // Recomputes the block-key cache entries [first_block, end_block) of one
 // sequence from its raw index keys (after an import).
 void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,

@@ -210,17 +210,18 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
         const int f = tid & (kD - 1);
         for (int i = 0; i < kC; ++i) {
             const float *Li = Ls + i * kC;
-            float acc = 0.0f;
+            // four independent partial sums: a quarter of the dependent chain
+            float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
             int j = 0;
             for (; j + 4 <= i; j += 4) {
                 const float4 l4 = *reinterpret_cast<const float4 *>(Li + j);
-                acc = fmaf(l4.x, X[j * kD + f], acc);
-                acc = fmaf(l4.y, X[(j + 1) * kD + f], acc);
-                acc = fmaf(l4.z, X[(j + 2) * kD + f], acc);
-                acc = fmaf(l4.w, X[(j + 3) * kD + f], acc);
+                a0 = fmaf(l4.x, X[j * kD + f], a0);
+                a1 = fmaf(l4.y, X[(j + 1) * kD + f], a1);
+                a2 = fmaf(l4.z, X[(j + 2) * kD + f], a2);
+                a3 = fmaf(l4.w, X[(j + 3) * kD + f], a3);
             }
-            for (; j < i; ++j) acc = fmaf(Li[j], X[j * kD + f], acc);
-            X[i * kD + f] = Bs[i] * (X[i * kD + f] - acc);
+            for (; j < i; ++j) a0 = fmaf(Li[j], X[j * kD + f], a0);
+            X[i * kD + f] = Bs[i] * (X[i * kD + f] - ((a0 + a1) + (a2 + a3)));
         }
     }
     __syncthreads();

@@ -21,6 +21,8 @@
 
 #include <cstdlib>
 
+#include <cuda_bf16.h>
+
 #include <algorithm>
 #include <cmath>
 
@@ -115,6 +117,33 @@ __device__ bool cta_block_key(const QsaDims &d, const QsaWeightsDev &w, const Qs
     return !bad;
 }
 
+// bf16 hi (round to nearest) and lo (the residual, rounded) of v at
+// row[i] and row[width + i].
+__device__ __forceinline__ void split_store16(uint16_t *row, uint32_t i, uint32_t width, float v) {
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    row[i] = __bfloat16_as_ushort(hi);
+    row[width + i] = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(hi)));
+}
+
+__global__ void qsa_split_rows_kernel(const float *__restrict__ src, uint16_t *__restrict__ dst, uint64_t length,
+                                      uint32_t kv_heads, uint64_t capacity) {
+    const uint64_t n = length * kv_heads * 256u;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < n; e += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t t = e / (kv_heads * 256u);
+        const uint32_t h = (uint32_t)(e / 256u % kv_heads), i = (uint32_t)(e % 256u);
+        split_store16(dst + ((uint64_t)h * capacity + t) * kQsaSplitRow, i, 256u, src[e]);
+    }
+}
+
+void launch_qsa_split_rows(const float *src, uint16_t *dst, uint64_t length, uint32_t kv_heads, uint64_t capacity,
+                           cudaStream_t stream) {
+    if (length == 0) return;
+    const uint64_t n = length * kv_heads * 256u;
+    const uint32_t blocks = (uint32_t)std::min<uint64_t>((n + 255) / 256, 148ull * 16);
+    qsa_split_rows_kernel<<<blocks, 256, 0, stream>>>(src, dst, length, kv_heads, capacity);
+    count_launch();
+}
+
 // ------------------------------------------------------------ prepare
 //
 // grid (B, Hq + Hkv + Hi + 1); 128 threads.  blockIdx.y selects one head:
@@ -162,11 +191,16 @@ qsa_prepare_kernel(QsaDims d, QsaWeightsDev w, QsaBatch bt,
         for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) vec[i] = kproj[h * hd + i];
         __syncthreads();
         exact_norm_rope_shared(vec, hd, w.k_norm, d.eps, w, d.rotary, pos, inv_slot, bad);
+        const size_t split_row = ((size_t)h * s.capacity + pos) * kQsaSplitRow;   // used when hd == 256
         for (uint32_t i = threadIdx.x; i < hd; i += blockDim.x) {
             s.key[(size_t)pos * kvw + h * hd + i] = vec[i];
             const float v = vproj[h * hd + i];
             if (!isfinite(v)) bad = true;
             s.value[(size_t)pos * kvw + h * hd + i] = v;
+            if (s.key_split != nullptr) {
+                split_store16(s.key_split + split_row, i, hd, vec[i]);
+                split_store16(s.value_split + split_row, i, hd, v);
+            }
         }
     } else if ((role -= d.kv_heads) < d.index_heads) {
         if (!index_queries) return;   // whole CTA: this entry is scored elsewhere
@@ -1073,6 +1107,410 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
     }
 }
 
+// ------------------------------------------------ tensor-core attention
+//
+// head_dim 256, up to 8 query heads per KV head; grid (entries, kv_heads,
+// splits), 288 threads: eight consumer warps and one producer warp.  Reads
+// the bf16 hi / lo copies of the cache rows (QsaSeq::key_split /
+// value_split: rows [hi 256 | lo 256] per token, KV-head major).  Per tile
+// of 16 selected tokens:
+//   logits^T [16 tokens][8 heads] = K [16][256] . Q^T [256][8]
+//   O^T [256][8] += V^T [256][16] . P^T [16][8]
+// as warp MMAs (m16n8k16, bf16 operands, F32 accumulate) with the
+// three-term split a b ~ a_hi b_hi + a_hi b_lo + a_lo b_hi, each term in
+// its own accumulator; the heads are the n = 8 side, so no MMA row is
+// padding.  Warp w owns features [32 w, 32 w + 32): its partial logits over
+// them are summed across the eight warps through shared memory (in warp
+// order, so every warp sees the same logits and takes the same softmax
+// decisions), then each warp multiplies its features of V.  One barrier
+// of the consumer warps per tile.  The softmax reference point m is raised only when a
+// logit exceeds it by more than kTcRescale (the weights exp(logit - m) then
+// stay below e^8, and O and l are rescaled rarely); O / l is the same
+// quotient for any m.  P^T reaches the B operand layout by movmatrix
+// transposes.  The producer warp refills a stage as soon as the eight
+// consumers have released it (an mbarrier per stage each way), with one
+// bulk copy per run of consecutive cache rows (the tokens of a selected
+// block); rows of a tile past the selection load cache row 0 and get
+// weight 0.
+
+namespace {
+
+constexpr int kTcTile = 16;                               // tokens per tile
+constexpr int kTcStages = 3;
+constexpr int kTcWarps = 8;                               // consumers; warp 8 produces
+constexpr int kTcThreads = 32 * (kTcWarps + 1);
+constexpr uint32_t kTcRow = 1040;                         // 1 KB row + 16 B: 8 rows hit 8 bank groups
+constexpr uint32_t kTcStage = 2 * kTcTile * kTcRow;       // K rows, then V rows
+static_assert(kTcRow == 2 * kQsaSplitRow, "shared-memory rows are split-cache rows");
+constexpr int kTcMaxTiles = 32;
+constexpr float kTcRescale = 8.0f;
+constexpr size_t kTcLogOff = (size_t)kTcStages * kTcStage;
+constexpr size_t kTcTokOff = kTcLogOff + 2 * kTcWarps * 32 * 4 * 4;
+constexpr size_t kTcBarOff = kTcTokOff + (size_t)kTcMaxTiles * kTcTile * 4;
+constexpr size_t kTcSmem = kTcBarOff + 2 * kTcStages * 8 + 16;   // full[], empty[], abort flag
+static_assert(kTcLogOff % 16 == 0 && kTcTokOff % 16 == 0 && kTcBarOff % 8 == 0, "shared-memory alignment");
+constexpr uint32_t kTcWaitSite = 8;                        // reported as kErrTimeout | 8 << 8
+constexpr uint32_t kTcWaitPolls = 1u << 26;
+constexpr uint64_t kTcWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t tc_smem(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t tc_now() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool tc_poll(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait by lane 0 of the warp, result broadcast.  Gives up at once
+// when another warp has raised the CTA's abort flag; raises it itself after
+// the poll or time limit.
+__device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, volatile uint32_t *abort_flag) {
+    uint32_t ok = 1;
+    if ((threadIdx.x & 31) == 0) {
+        const uint32_t a = tc_smem(bar);
+        const uint64_t t0 = tc_now();
+        ok = 0;
+        for (uint32_t i = 0; i < kTcWaitPolls; ++i) {
+            if (tc_poll(a, parity)) {
+                ok = 1;
+                break;
+            }
+            if ((i & 63u) == 63u) {
+                if (*abort_flag) break;
+                if (tc_now() - t0 > kTcWaitNs) {
+                    atomicCAS(const_cast<uint32_t *>(abort_flag), 0u, kTcWaitSite);
+                    break;
+                }
+            }
+        }
+        if (!ok) atomicCAS(const_cast<uint32_t *>(abort_flag), 0u, kTcWaitSite);
+    }
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ void tc_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// 1-D bulk copy global -> shared (no multicast) completing on `bar`
+__device__ __forceinline__ void tc_bulk(uint32_t dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(tc_smem(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_ldsm(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_ldsm_t(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// (x0, x1) -> bf16x2 hi (round to nearest) and bf16x2 lo of the residuals;
+// x0 in the low half (the lower k index of an MMA operand pair)
+__device__ __forceinline__ void tc_split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+// 8x8 b16 transpose of a fragment (row T / 4, columns 2 (T % 4), +1)
+__device__ __forceinline__ uint32_t tc_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+}  // namespace
+
+bool qsa_split_cache_used(const QsaDims &d) { return d.head_dim == 256 && d.repeat <= 8; }
+
+// KQ_B200_SIMT_ATTENTION=1 selects the F32 CUDA-core attention kernel for
+// head_dim 256 as well (used by the tests to cross-check the two).
+bool force_simt_attention() {
+    const char *e = getenv("KQ_B200_SIMT_ATTENTION");
+    return e != nullptr && e[0] == '1';
+}
+
+__global__ void __launch_bounds__(kTcThreads, 2)
+qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const uint32_t *__restrict__ selected,
+                     const uint32_t *__restrict__ selected_count, float *__restrict__ part_o,
+                     float *__restrict__ part_ml, uint32_t splits, ErrorWord err) {
+    pdl_wait();
+    extern __shared__ __align__(128) uint8_t tsm[];
+    float *plog = reinterpret_cast<float *>(tsm + kTcLogOff);                  // [2][8 warps][32 lanes][4]
+    uint32_t *tok_s = reinterpret_cast<uint32_t *>(tsm + kTcTokOff);          // cache row per selected token
+    uint64_t *full = reinterpret_cast<uint64_t *>(tsm + kTcBarOff);
+    uint64_t *empty = full + kTcStages;
+    volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(empty + kTcStages);
+    if (qsa_error_raised(err)) return;
+    const uint32_t b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+    const QsaSeq s = batch_seq(bt, b);
+    const uint32_t pos = s.length;
+    const uint32_t nblocks = (pos + 1) / d.block;
+    const uint32_t tail = (pos + 1) % d.block;
+    const uint32_t ksel = min(selected_count[b], min(nblocks, d.topk));
+    const uint32_t ntok = ksel * d.block + tail;
+    const uint32_t ntiles = (ntok + kTcTile - 1) / kTcTile;
+    const uint32_t per = (ntiles + splits - 1) / splits;
+    const uint32_t tile0 = split * per, tile1 = min(ntiles, tile0 + per);
+    const uint32_t heads = d.repeat;   // <= 8 (checked by the launcher)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, qd = lane & 3;
+    const uint32_t *selb = selected + (size_t)b * d.topk;
+    const uint32_t my_tiles = tile1 > tile0 ? tile1 - tile0 : 0u;
+    if (my_tiles > (uint32_t)kTcMaxTiles) {
+        if (tid == 0) qsa_raise(err, kErrSelection);
+        return;
+    }
+    // cache row of every token of this CTA's tiles (UINT32_MAX: none)
+    for (uint32_t i = tid; i < my_tiles * kTcTile; i += kTcThreads) {
+        const uint32_t t = tile0 * kTcTile + i;
+        uint32_t tok = 0xFFFFFFFFu;
+        if (t < ksel * d.block) {
+            const uint32_t blk = selb[t / d.block];
+            if (blk < nblocks) tok = blk * d.block + t % d.block;
+        } else if (t < ntok) {
+            tok = nblocks * d.block + (t - ksel * d.block);
+        }
+        tok_s[i] = tok;
+    }
+    if (tid == 0) {
+        for (int st = 0; st < kTcStages; ++st) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&full[st])), "r"(1u));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem(&empty[st])), "r"((uint32_t)kTcWarps));
+        }
+        *abort_flag = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    const uint16_t *ksplit = s.key_split + (size_t)kvh * s.capacity * kQsaSplitRow;
+    const uint16_t *vsplit = s.value_split + (size_t)kvh * s.capacity * kQsaSplitRow;
+    // producer: bulk copies of tile j (relative to tile0).  Lane l < 16 takes
+    // token l's key row, lane 16 + l its value row; consecutive cache rows
+    // (the tokens of one selected block) go as one copy of the whole run,
+    // issued by the lane of its first token.  A row past the selection
+    // loads cache row 0.
+    auto issue = [&](uint32_t j) {
+        const uint32_t st = j % kTcStages;
+        if (lane == 0) tc_expect_tx(&full[st], 2u * kTcTile * kTcRow);
+        __syncwarp();
+        const uint32_t r = lane & 15u, which = (uint32_t)lane >> 4;
+        const uint32_t *tt = tok_s + j * kTcTile;
+        const uint32_t tok = tt[r];
+        const bool start = tok == 0xFFFFFFFFu || r == 0 || tt[r - 1] == 0xFFFFFFFFu || tt[r - 1] + 1 != tok;
+        if (start) {
+            uint32_t n = 1;
+            if (tok != 0xFFFFFFFFu)
+                while (r + n < (uint32_t)kTcTile && tt[r + n] == tok + n) ++n;
+            const uint16_t *src = (which ? vsplit : ksplit) + (size_t)(tok == 0xFFFFFFFFu ? 0u : tok) * kQsaSplitRow;
+            const uint32_t dst = tc_smem(tsm + st * kTcStage + which * kTcTile * kTcRow + r * kTcRow);
+            tc_bulk(dst, src, n * kTcRow, &full[st]);
+        }
+    };
+    if (warp == kTcWarps) {
+        // producer: a stage is refilled once every consumer has released it
+        uint32_t j = 0;
+        for (; j < my_tiles; ++j) {
+            const uint32_t st = j % kTcStages;
+            if (j >= (uint32_t)kTcStages && !tc_wait_warp(&empty[st], (j / kTcStages - 1) & 1u, abort_flag)) break;
+            issue(j);
+        }
+        if (*abort_flag && lane == 0) {
+            // let the copies in flight land (bounded) before the CTA exits
+            for (uint32_t st = 0; st < (uint32_t)kTcStages && st < j; ++st) {
+                const uint32_t last = st + ((j - 1 - st) / kTcStages) * kTcStages;
+                const uint32_t a = tc_smem(&full[st]);
+                const uint64_t t0 = tc_now();
+                while (!tc_poll(a, (last / kTcStages) & 1u) && tc_now() - t0 < kTcWaitNs) {
+                }
+            }
+        }
+        return;
+    }
+
+    // Q^T fragments of this warp's features (B operand: k = feature, n = head g)
+    uint32_t qh[2][2], ql[2][2];
+    {
+        const bool hv = (uint32_t)g < heads;
+        const float *qp = q + ((size_t)b * d.q_heads + kvh * heads + (hv ? g : 0)) * 256u;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            const int f = 32 * warp + 16 * kk + 2 * qd;
+            float2 x0 = make_float2(0.f, 0.f), x1 = x0;
+            if (hv) {
+                x0 = *reinterpret_cast<const float2 *>(qp + f);
+                x1 = *reinterpret_cast<const float2 *>(qp + f + 8);
+            }
+            tc_split2(x0.x, x0.y, qh[kk][0], ql[kk][0]);
+            tc_split2(x1.x, x1.y, qh[kk][1], ql[kk][1]);
+        }
+    }
+    // softmax state of heads 2 qd, 2 qd + 1 (l: this lane's tokens only)
+    float m_run[2] = {-INFINITY, -INFINITY}, l_part[2] = {0.f, 0.f};
+    // O^T of m-tile mt, one accumulator per split term:
+    // (feature g, head 2qd | 2qd+1), (feature g + 8, ...)
+    float o[3][2][4];
+#pragma unroll
+    for (int a = 0; a < 3; ++a)
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[a][mt][i] = 0.f;
+    bool failed = false;
+    const float scale = d.sqrt_head_dim;
+    const uint32_t base = tc_smem(tsm);
+    // ldmatrix row addresses: K as the A operand (rows = tokens), V as the
+    // transposed A operand (rows = features)
+    const uint32_t k_lane = ((lane & 7) + ((lane >> 3) & 1) * 8) * kTcRow + (32 * warp + (lane >> 4) * 8) * 2;
+    const uint32_t v_lane =
+        kTcTile * kTcRow + ((lane & 7) + (lane >> 4) * 8) * kTcRow + (32 * warp + ((lane >> 3) & 1) * 8) * 2;
+
+    for (uint32_t j = 0; j < my_tiles; ++j) {
+        const uint32_t st = j % kTcStages;
+        if (!tc_wait_warp(&full[st], (j / kTcStages) & 1u, abort_flag)) failed = true;
+        const uint32_t stage = base + st * kTcStage;
+        // ---- partial logits over this warp's features: six independent products
+        float a[6][4];
+#pragma unroll
+        for (int i = 0; i < 6; ++i) a[i][0] = a[i][1] = a[i][2] = a[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+            uint32_t ah[4], al[4];
+            tc_ldsm(stage + k_lane + kk * 32, ah);
+            tc_ldsm(stage + k_lane + kk * 32 + 512, al);
+            tc_mma(a[3 * kk + 0], ah, qh[kk][0], qh[kk][1]);
+            tc_mma(a[3 * kk + 1], ah, ql[kk][0], ql[kk][1]);
+            tc_mma(a[3 * kk + 2], al, qh[kk][0], qh[kk][1]);
+        }
+        float *pl = plog + (j & 1u) * kTcWarps * 32 * 4;
+        float4 mine;
+        mine.x = ((a[0][0] + a[1][0]) + a[2][0]) + ((a[3][0] + a[4][0]) + a[5][0]);
+        mine.y = ((a[0][1] + a[1][1]) + a[2][1]) + ((a[3][1] + a[4][1]) + a[5][1]);
+        mine.z = ((a[0][2] + a[1][2]) + a[2][2]) + ((a[3][2] + a[4][2]) + a[5][2]);
+        mine.w = ((a[0][3] + a[1][3]) + a[2][3]) + ((a[3][3] + a[4][3]) + a[5][3]);
+        *reinterpret_cast<float4 *>(pl + (warp * 32 + lane) * 4) = mine;
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * kTcWarps) : "memory");
+        float4 acc = *reinterpret_cast<const float4 *>(pl + lane * 4);
+#pragma unroll
+        for (int w = 1; w < kTcWarps; ++w) {
+            const float4 x = *reinterpret_cast<const float4 *>(pl + (w * 32 + lane) * 4);
+            acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+        }
+        const uint32_t *tt = tok_s + j * kTcTile;
+        const bool v0 = tt[g] != 0xFFFFFFFFu, v1 = tt[g + 8] != 0xFFFFFFFFu;
+        // (token g, head 2qd), (g, 2qd + 1), (g + 8, 2qd), (g + 8, 2qd + 1)
+        const float lg[4] = {v0 ? acc.x / scale : -INFINITY, v0 ? acc.y / scale : -INFINITY,
+                             v1 ? acc.z / scale : -INFINITY, v1 ? acc.w / scale : -INFINITY};
+        const bool high = lg[0] > m_run[0] + kTcRescale || lg[2] > m_run[0] + kTcRescale ||
+                          lg[1] > m_run[1] + kTcRescale || lg[3] > m_run[1] + kTcRescale;
+        if (__any_sync(0xffffffffu, high)) {
+            // new reference point: the running maximum of each head
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                float mt = fmaxf(lg[c], lg[c + 2]);
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+                const float m_new = fmaxf(m_run[c], mt);
+                const float corr = (m_run[c] == -INFINITY) ? 0.0f : expf(m_run[c] - m_new);
+                l_part[c] *= corr;
+#pragma unroll
+                for (int t3 = 0; t3 < 3; ++t3)
+#pragma unroll
+                    for (int mt2 = 0; mt2 < 2; ++mt2) {
+                        o[t3][mt2][c] *= corr;
+                        o[t3][mt2][c + 2] *= corr;
+                    }
+                m_run[c] = m_new;
+            }
+        }
+        float p[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) p[i] = (lg[i] == -INFINITY) ? 0.0f : expf(lg[i] - m_run[i & 1]);
+        l_part[0] += p[0] + p[2];
+        l_part[1] += p[1] + p[3];
+        // P^T as the B operand (k = token, n = head): the fragments of P
+        // (token g | g + 8, heads 2qd, 2qd + 1) transposed
+        uint32_t h01, l01, h23, l23;
+        tc_split2(p[0], p[1], h01, l01);
+        tc_split2(p[2], p[3], h23, l23);
+        const uint32_t pb0h = tc_trans(h01), pb1h = tc_trans(h23);
+        const uint32_t pb0l = tc_trans(l01), pb1l = tc_trans(l23);
+        // ---- O^T += V^T P^T over this warp's features
+#pragma unroll
+        for (int mt2 = 0; mt2 < 2; ++mt2) {
+            uint32_t ah[4], al[4];
+            tc_ldsm_t(stage + v_lane + mt2 * 32, ah);
+            tc_ldsm_t(stage + v_lane + mt2 * 32 + 512, al);
+            tc_mma(o[0][mt2], ah, pb0h, pb1h);
+            tc_mma(o[1][mt2], ah, pb0l, pb1l);
+            tc_mma(o[2][mt2], al, pb0h, pb1h);
+        }
+        // this warp is done with the stage
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc_smem(&empty[st])) : "memory");
+    }
+    if (failed || *abort_flag) {
+        if (tid == 0)
+            atomicCAS(err.word, 0ull, ((unsigned long long)(kErrTimeout | (kTcWaitSite << 8)) << 32) | err.call_id);
+        return;
+    }
+    // l over the 16 token rows of the lanes with this qd
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        l_part[c] += __shfl_xor_sync(0xffffffffu, l_part[c], 4);
+        l_part[c] += __shfl_xor_sync(0xffffffffu, l_part[c], 8);
+        l_part[c] += __shfl_xor_sync(0xffffffffu, l_part[c], 16);
+    }
+    // partial results of this split: O (features 32 w + 16 mt + g (+ 8)) and m, l
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        const uint32_t h = 2 * qd + c;
+        if (h >= heads) continue;
+        const size_t slot = ((size_t)b * d.q_heads + kvh * heads + h) * splits + split;
+        float *po = part_o + slot * 256u + 32 * warp + g;
+#pragma unroll
+        for (int mt2 = 0; mt2 < 2; ++mt2) {
+            po[16 * mt2] = (o[0][mt2][c] + o[1][mt2][c]) + o[2][mt2][c];
+            po[16 * mt2 + 8] = (o[0][mt2][c + 2] + o[1][mt2][c + 2]) + o[2][mt2][c + 2];
+        }
+        if (warp == 0 && g == 0) {
+            part_ml[slot * 2] = m_run[c];
+            part_ml[slot * 2 + 1] = l_part[c];
+        }
+    }
+}
+
 void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const float *q, const uint32_t *selected,
                        const uint32_t *selected_count, float *partial_o,
@@ -1083,7 +1521,18 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
     // parts of a shared cache
     dim3 grid(batch, d.kv_heads, splits);
     KernelTimer timer("qsa_attend", stream);
-    if (d.head_dim == 256 && d.repeat <= 8) {
+    bool split_rows = qsa_split_cache_used(d) && !force_simt_attention();
+    for (uint32_t e = 0; split_rows && e < (b.uniform ? 1u : batch); ++e)
+        split_rows = b.s[e].key_split != nullptr && b.s[e].value_split != nullptr;
+    if (split_rows) {
+        static bool attr = false;
+        if (!attr) {
+            cudaFuncSetAttribute(qsa_attend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+            attr = true;
+        }
+        launch_pdl(qsa_attend_tc_kernel, grid, kTcThreads, kTcSmem, stream, d, b, q, selected, selected_count,
+                   partial_o, partial_ml, splits, err);
+    } else if (d.head_dim == 256 && d.repeat <= 8) {
         static bool attr = false;
         if (!attr) {
             cudaFuncSetAttribute(qsa_attend_mh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMhSmem);

@@ -448,12 +448,16 @@ def _qsa_setup(kq, oracle, dims, seed, proj_type=12, index_type=30):
     return weights, prov, layer, oracle.qsa_weights_f32(weights)
 
 
-def test_qsa_config1_decode_context_4096(kq, oracle):
+@pytest.mark.parametrize("simt", ["0", "1"])
+def test_qsa_config1_decode_context_4096(kq, oracle, simt, monkeypatch):
     """decode at context 4096 (4095 prior positions),
     hidden 2048, 16 q heads / 2 KV heads of 256, partial RoPE 64, theta 1e7,
     Q4_K q/k/v/o, BF16 index projections, N(0,1) caches.  Block selection
-    (512 of 1024 blocks) must match the reference exactly."""
+    (512 of 1024 blocks) must match the reference exactly.  The attention
+    runs on the tensor cores (bf16 hi / lo cache copies) and, with
+    KQ_B200_SIMT_ATTENTION=1, on the F32 CUDA-core kernel."""
     from kqb200 import synth
+    monkeypatch.setenv("KQ_B200_SIMT_ATTENTION", simt)
     dims = synth.QsaDims(max_context=8192)
     weights, prov, layer, w = _qsa_setup(kq, oracle, dims, 21)
     try:
