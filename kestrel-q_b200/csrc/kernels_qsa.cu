@@ -1124,9 +1124,11 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
 // order, so every warp sees the same logits and takes the same softmax
 // decisions), then each warp multiplies its features of V.  One barrier
 // of the consumer warps per tile.  The softmax reference point m is raised only when a
-// logit exceeds it by more than kTcRescale (the weights exp(logit - m) then
-// stay below e^8, and O and l are rescaled rarely); O / l is the same
-// quotient for any m.  P^T reaches the B operand layout by movmatrix
+// logit exceeds it by more than kTcRescale (the weights then stay below
+// 2^12, and O and l are rescaled rarely); O / l is the same quotient for
+// any m.  The logits are kept in base-2 units (Q is scaled by
+// log2(e) / sqrt(d) before the split, so the weights are exp2(logit - m));
+// m is written back in natural units.  P^T reaches the B operand layout by movmatrix
 // transposes.  The producer warp refills a stage as soon as the eight
 // consumers have released it (an mbarrier per stage each way), with one
 // bulk copy per run of consecutive cache rows (the tokens of a selected
@@ -1136,19 +1138,25 @@ qsa_attend_mh_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q,
 namespace {
 
 constexpr int kTcTile = 16;                               // tokens per tile
-constexpr int kTcStages = 3;
 constexpr int kTcWarps = 8;                               // consumers; warp 8 produces
 constexpr int kTcThreads = 32 * (kTcWarps + 1);
 constexpr uint32_t kTcRow = 1040;                         // 1 KB row + 16 B: 8 rows hit 8 bank groups
 constexpr uint32_t kTcStage = 2 * kTcTile * kTcRow;       // K rows, then V rows
 static_assert(kTcRow == 2 * kQsaSplitRow, "shared-memory rows are split-cache rows");
 constexpr int kTcMaxTiles = 32;
-constexpr float kTcRescale = 8.0f;
-constexpr size_t kTcLogOff = (size_t)kTcStages * kTcStage;
-constexpr size_t kTcTokOff = kTcLogOff + 2 * kTcWarps * 32 * 4 * 4;
-constexpr size_t kTcBarOff = kTcTokOff + (size_t)kTcMaxTiles * kTcTile * 4;
-constexpr size_t kTcSmem = kTcBarOff + 2 * kTcStages * 8 + 16;   // full[], empty[], abort flag
-static_assert(kTcLogOff % 16 == 0 && kTcTokOff % 16 == 0 && kTcBarOff % 8 == 0, "shared-memory alignment");
+constexpr float kTcRescale = 12.0f;                       // base-2 units
+constexpr float kTcLog2e = 1.44269504088896340736f;
+constexpr float kTcLn2 = 0.69314718055994530942f;
+// shared memory of the S-stage kernel: stages, partial logits, cache rows,
+// full[S], empty[S], abort flag
+template <int S>
+struct TcLayout {
+    static constexpr size_t log_off = (size_t)S * kTcStage;
+    static constexpr size_t tok_off = log_off + 2 * kTcWarps * 32 * 4 * 4;
+    static constexpr size_t bar_off = tok_off + (size_t)kTcMaxTiles * kTcTile * 4;
+    static constexpr size_t bytes = bar_off + 2 * S * 8 + 16;
+    static_assert(log_off % 16 == 0 && tok_off % 16 == 0 && bar_off % 8 == 0, "shared-memory alignment");
+};
 constexpr uint32_t kTcWaitSite = 8;                        // reported as kErrTimeout | 8 << 8
 constexpr uint32_t kTcWaitPolls = 1u << 26;
 constexpr uint64_t kTcWaitNs = 2000000000ull;
@@ -1261,15 +1269,17 @@ bool force_simt_attention() {
     return e != nullptr && e[0] == '1';
 }
 
-__global__ void __launch_bounds__(kTcThreads, 2)
+template <int kTcStages, int kMinBlocks>
+__global__ void __launch_bounds__(kTcThreads, kMinBlocks)
 qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const uint32_t *__restrict__ selected,
                      const uint32_t *__restrict__ selected_count, float *__restrict__ part_o,
                      float *__restrict__ part_ml, uint32_t splits, ErrorWord err) {
     pdl_wait();
     extern __shared__ __align__(128) uint8_t tsm[];
-    float *plog = reinterpret_cast<float *>(tsm + kTcLogOff);                  // [2][8 warps][32 lanes][4]
-    uint32_t *tok_s = reinterpret_cast<uint32_t *>(tsm + kTcTokOff);          // cache row per selected token
-    uint64_t *full = reinterpret_cast<uint64_t *>(tsm + kTcBarOff);
+    using L = TcLayout<kTcStages>;
+    float *plog = reinterpret_cast<float *>(tsm + L::log_off);                 // [2][8 warps][32 lanes][4]
+    uint32_t *tok_s = reinterpret_cast<uint32_t *>(tsm + L::tok_off);         // cache row per selected token
+    uint64_t *full = reinterpret_cast<uint64_t *>(tsm + L::bar_off);
     uint64_t *empty = full + kTcStages;
     volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(empty + kTcStages);
     if (qsa_error_raised(err)) return;
@@ -1360,6 +1370,7 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
 
     // Q^T fragments of this warp's features (B operand: k = feature, n = head g)
     uint32_t qh[2][2], ql[2][2];
+    const float qscale = kTcLog2e / d.sqrt_head_dim;
     {
         const bool hv = (uint32_t)g < heads;
         const float *qp = q + ((size_t)b * d.q_heads + kvh * heads + (hv ? g : 0)) * 256u;
@@ -1370,6 +1381,7 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
             if (hv) {
                 x0 = *reinterpret_cast<const float2 *>(qp + f);
                 x1 = *reinterpret_cast<const float2 *>(qp + f + 8);
+                x0.x *= qscale; x0.y *= qscale; x1.x *= qscale; x1.y *= qscale;
             }
             tc_split2(x0.x, x0.y, qh[kk][0], ql[kk][0]);
             tc_split2(x1.x, x1.y, qh[kk][1], ql[kk][1]);
@@ -1387,7 +1399,6 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
 #pragma unroll
             for (int i = 0; i < 4; ++i) o[a][mt][i] = 0.f;
     bool failed = false;
-    const float scale = d.sqrt_head_dim;
     const uint32_t base = tc_smem(tsm);
     // ldmatrix row addresses: K as the A operand (rows = tokens), V as the
     // transposed A operand (rows = features)
@@ -1399,25 +1410,25 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
         const uint32_t st = j % kTcStages;
         if (!tc_wait_warp(&full[st], (j / kTcStages) & 1u, abort_flag)) failed = true;
         const uint32_t stage = base + st * kTcStage;
-        // ---- partial logits over this warp's features: six independent products
-        float a[6][4];
+        // ---- partial logits over this warp's features, one accumulator per split term
+        float a[3][4];
 #pragma unroll
-        for (int i = 0; i < 6; ++i) a[i][0] = a[i][1] = a[i][2] = a[i][3] = 0.f;
+        for (int i = 0; i < 3; ++i) a[i][0] = a[i][1] = a[i][2] = a[i][3] = 0.f;
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
             uint32_t ah[4], al[4];
             tc_ldsm(stage + k_lane + kk * 32, ah);
             tc_ldsm(stage + k_lane + kk * 32 + 512, al);
-            tc_mma(a[3 * kk + 0], ah, qh[kk][0], qh[kk][1]);
-            tc_mma(a[3 * kk + 1], ah, ql[kk][0], ql[kk][1]);
-            tc_mma(a[3 * kk + 2], al, qh[kk][0], qh[kk][1]);
+            tc_mma(a[0], ah, qh[kk][0], qh[kk][1]);
+            tc_mma(a[1], ah, ql[kk][0], ql[kk][1]);
+            tc_mma(a[2], al, qh[kk][0], qh[kk][1]);
         }
         float *pl = plog + (j & 1u) * kTcWarps * 32 * 4;
         float4 mine;
-        mine.x = ((a[0][0] + a[1][0]) + a[2][0]) + ((a[3][0] + a[4][0]) + a[5][0]);
-        mine.y = ((a[0][1] + a[1][1]) + a[2][1]) + ((a[3][1] + a[4][1]) + a[5][1]);
-        mine.z = ((a[0][2] + a[1][2]) + a[2][2]) + ((a[3][2] + a[4][2]) + a[5][2]);
-        mine.w = ((a[0][3] + a[1][3]) + a[2][3]) + ((a[3][3] + a[4][3]) + a[5][3]);
+        mine.x = (a[0][0] + a[1][0]) + a[2][0];
+        mine.y = (a[0][1] + a[1][1]) + a[2][1];
+        mine.z = (a[0][2] + a[1][2]) + a[2][2];
+        mine.w = (a[0][3] + a[1][3]) + a[2][3];
         *reinterpret_cast<float4 *>(pl + (warp * 32 + lane) * 4) = mine;
         asm volatile("bar.sync 1, %0;" ::"n"(32 * kTcWarps) : "memory");
         float4 acc = *reinterpret_cast<const float4 *>(pl + lane * 4);
@@ -1429,8 +1440,8 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
         const uint32_t *tt = tok_s + j * kTcTile;
         const bool v0 = tt[g] != 0xFFFFFFFFu, v1 = tt[g + 8] != 0xFFFFFFFFu;
         // (token g, head 2qd), (g, 2qd + 1), (g + 8, 2qd), (g + 8, 2qd + 1)
-        const float lg[4] = {v0 ? acc.x / scale : -INFINITY, v0 ? acc.y / scale : -INFINITY,
-                             v1 ? acc.z / scale : -INFINITY, v1 ? acc.w / scale : -INFINITY};
+        const float lg[4] = {v0 ? acc.x : -INFINITY, v0 ? acc.y : -INFINITY, v1 ? acc.z : -INFINITY,
+                             v1 ? acc.w : -INFINITY};
         const bool high = lg[0] > m_run[0] + kTcRescale || lg[2] > m_run[0] + kTcRescale ||
                           lg[1] > m_run[1] + kTcRescale || lg[3] > m_run[1] + kTcRescale;
         if (__any_sync(0xffffffffu, high)) {
@@ -1442,7 +1453,7 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
                 const float m_new = fmaxf(m_run[c], mt);
-                const float corr = (m_run[c] == -INFINITY) ? 0.0f : expf(m_run[c] - m_new);
+                const float corr = (m_run[c] == -INFINITY) ? 0.0f : exp2f(m_run[c] - m_new);
                 l_part[c] *= corr;
 #pragma unroll
                 for (int t3 = 0; t3 < 3; ++t3)
@@ -1456,7 +1467,7 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
         }
         float p[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) p[i] = (lg[i] == -INFINITY) ? 0.0f : expf(lg[i] - m_run[i & 1]);
+        for (int i = 0; i < 4; ++i) p[i] = (lg[i] == -INFINITY) ? 0.0f : exp2f(lg[i] - m_run[i & 1]);
         l_part[0] += p[0] + p[2];
         l_part[1] += p[1] + p[3];
         // P^T as the B operand (k = token, n = head): the fragments of P
@@ -1505,7 +1516,7 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
             po[16 * mt2 + 8] = (o[0][mt2][c + 2] + o[1][mt2][c + 2]) + o[2][mt2][c + 2];
         }
         if (warp == 0 && g == 0) {
-            part_ml[slot * 2] = m_run[c];
+            part_ml[slot * 2] = m_run[c] * kTcLn2;
             part_ml[slot * 2 + 1] = l_part[c];
         }
     }
@@ -1525,13 +1536,28 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
     for (uint32_t e = 0; split_rows && e < (b.uniform ? 1u : batch); ++e)
         split_rows = b.s[e].key_split != nullptr && b.s[e].value_split != nullptr;
     if (split_rows) {
-        static bool attr = false;
-        if (!attr) {
-            cudaFuncSetAttribute(qsa_attend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
-            attr = true;
+        // three stages and two CTAs per SM, or (KQ_B200_ATTEND_STAGES=6) six
+        // stages and one CTA
+        const char *e = getenv("KQ_B200_ATTEND_STAGES");
+        if (e != nullptr && e[0] == '6') {
+            static bool attr6 = false;
+            if (!attr6) {
+                cudaFuncSetAttribute(qsa_attend_tc_kernel<6, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)TcLayout<6>::bytes);
+                attr6 = true;
+            }
+            launch_pdl(qsa_attend_tc_kernel<6, 1>, grid, kTcThreads, TcLayout<6>::bytes, stream, d, b, q, selected,
+                       selected_count, partial_o, partial_ml, splits, err);
+        } else {
+            static bool attr3 = false;
+            if (!attr3) {
+                cudaFuncSetAttribute(qsa_attend_tc_kernel<3, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)TcLayout<3>::bytes);
+                attr3 = true;
+            }
+            launch_pdl(qsa_attend_tc_kernel<3, 2>, grid, kTcThreads, TcLayout<3>::bytes, stream, d, b, q, selected,
+                       selected_count, partial_o, partial_ml, splits, err);
         }
-        launch_pdl(qsa_attend_tc_kernel, grid, kTcThreads, kTcSmem, stream, d, b, q, selected, selected_count,
-                   partial_o, partial_ml, splits, err);
     } else if (d.head_dim == 256 && d.repeat <= 8) {
         static bool attr = false;
         if (!attr) {
