@@ -368,6 +368,121 @@ qsa_score_kernel(QsaDims d, QsaBatch bt, uint32_t batch, const float *__restrict
     if (bad) qsa_raise(err, kErrNonFinite);
 }
 
+// f32x2 forms of a separately rounded product and sum (two lanes per
+// instruction, each lane rounded exactly as __fmul_rn / __fadd_rn; the
+// explicit .rn keeps them from being contracted into a fused multiply-add)
+__device__ __forceinline__ uint64_t sc_pair(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void sc_unpair(uint64_t v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t sc_mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t sc_add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// Block scores of E consecutive entries of one sequence (E a multiple of 4)
+// per thread: every block-key load serves E entries, and the E dots of one
+// (head, feature) step run as E / 2 paired products and sums.  The queries
+// sit in shared memory as [head][feature][entry].  Same arithmetic, in the
+// same order, per entry as qsa_score_kernel.
+template <int E>
+__global__ void __launch_bounds__(kScoreThreads)
+qsa_score_pair_kernel(QsaDims d, QsaBatch bt, uint32_t batch, const float *__restrict__ iq,
+                      float *__restrict__ scores, uint32_t ld_scores, ErrorWord err) {
+    static_assert(E % 4 == 0, "entries come in float4 groups");
+    pdl_wait();
+    extern __shared__ __align__(16) float qsh[];   // [Hi][di][E]
+    if (qsa_error_raised(err)) return;
+    const uint32_t e0 = blockIdx.y * E;
+    const uint32_t ne = min((uint32_t)E, batch - e0);
+    uint32_t nb[E];
+    uint32_t nb_max = 0;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        nb[e] = (uint32_t)e < ne ? (batch_seq(bt, e0 + e).length + 1) / d.block : 0u;
+        nb_max = max(nb_max, nb[e]);
+    }
+    if (blockIdx.x * kScoreThreads >= nb_max) return;   // uniform over the CTA
+    const uint32_t di = d.index_dim, n = d.index_heads * di;
+    for (uint32_t i = threadIdx.x; i < E * n; i += kScoreThreads) {
+        const uint32_t e = i % E, hf = i / E;
+        qsh[i] = e < ne ? iq[(size_t)(e0 + e) * n + hf] : 0.0f;
+    }
+    __syncthreads();
+    const uint32_t bi = blockIdx.x * kScoreThreads + threadIdx.x;
+    if (bi >= nb_max) return;
+    const QsaSeq s = batch_seq(bt, e0);
+    const uint32_t ld = block_key_ld(s.capacity, d.block);
+    const float *key = s.block_keys + bi;
+    float score[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) score[e] = 0.0f;
+    for (uint32_t h0 = 0; h0 < d.index_heads; h0 += kScoreHeads) {
+        const uint32_t nh = min(kScoreHeads, d.index_heads - h0);
+        uint64_t dot[kScoreHeads][E / 2];
+#pragma unroll
+        for (uint32_t h = 0; h < kScoreHeads; ++h)
+#pragma unroll
+            for (int p = 0; p < E / 2; ++p) dot[h][p] = 0ull;   // (+0.0f, +0.0f)
+        auto step = [&](uint32_t f, float kf) {
+            const uint64_t k2 = sc_pair(kf, kf);
+#pragma unroll
+            for (uint32_t h = 0; h < kScoreHeads; ++h) {
+                if (h < nh) {
+                    const float *qp = qsh + ((size_t)(h0 + h) * di + f) * E;
+#pragma unroll
+                    for (int p = 0; p < E / 4; ++p) {
+                        const float4 q4 = *reinterpret_cast<const float4 *>(qp + 4 * p);
+                        dot[h][2 * p] = sc_add2(dot[h][2 * p], sc_mul2(sc_pair(q4.x, q4.y), k2));
+                        dot[h][2 * p + 1] = sc_add2(dot[h][2 * p + 1], sc_mul2(sc_pair(q4.z, q4.w), k2));
+                    }
+                }
+            }
+        };
+        uint32_t f = 0;
+        for (; f + 8 <= di; f += 8) {
+            float kv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) kv[j] = key[(size_t)(f + j) * ld];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) step(f + j, kv[j]);
+        }
+        for (; f < di; ++f) step(f, key[(size_t)f * ld]);
+        // positive dots, added in head order
+#pragma unroll
+        for (uint32_t h = 0; h < kScoreHeads; ++h) {
+            if (h >= nh) continue;
+#pragma unroll
+            for (int p = 0; p < E / 2; ++p) {
+                float lo, hi;
+                sc_unpair(dot[h][p], lo, hi);
+                if (lo > 0.0f) score[2 * p] = __fadd_rn(score[2 * p], lo);
+                if (hi > 0.0f) score[2 * p + 1] = __fadd_rn(score[2 * p + 1], hi);
+            }
+        }
+    }
+    bool bad = false;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        if ((uint32_t)e < ne && bi < nb[e]) {
+            const float sc = __fdiv_rn(score[e], d.sqrt_index_dim);
+            bad |= !isfinite(sc);
+            scores[(size_t)(e0 + e) * ld_scores + bi] = sc;
+        }
+    }
+    if (bad) qsa_raise(err, kErrNonFinite);
+}
+
 void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                       const float *iq, float *scores, uint32_t ld_scores,
                       uint32_t max_blocks, bool shared_sequence, ErrorWord err, cudaStream_t stream) {
@@ -379,7 +494,13 @@ void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
     const uint32_t xblocks = (max_blocks + kScoreThreads - 1) / kScoreThreads;
     const char *force = getenv("KQ_B200_SCORE_SHARED");   // tests: 1 = always share when possible
     const bool big = xblocks * ((batch + 3) / 4) >= 4u * 148u || (force && atoi(force) == 1);
-    if (shared_sequence && batch > 1 && big) {
+    const bool big8 = xblocks * ((batch + 7) / 8) >= 4u * 148u || (force && atoi(force) == 1);
+    if (shared_sequence && batch > 1 && big8) {
+        // eight entries per key load, paired products
+        dim3 grid(xblocks, (batch + 7) / 8);
+        launch_pdl(qsa_score_pair_kernel<8>, grid, kScoreThreads, 8 * n * sizeof(float), stream, d, b, batch, iq,
+                   scores, ld_scores, err);
+    } else if (shared_sequence && batch > 1 && big) {
         dim3 grid(xblocks, (batch + 3) / 4);
         launch_pdl(qsa_score_kernel<4>, grid, kScoreThreads, 4 * n * sizeof(float), stream, d, b, batch, iq, scores,
                    ld_scores, err);

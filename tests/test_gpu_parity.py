@@ -551,6 +551,33 @@ def test_qsa_chunked_prefill(kq, oracle, hidden, qh, hd, budget, L0, T, seed, sh
         prov.close()
 
 
+def test_qsa_paired_scores_select_like_single_entry_scores(kq, oracle, monkeypatch):
+    """The eight-entry score kernel (f32x2 products and sums, each lane
+    rounded like the scalar ones) gives bit-identical block scores to the
+    one-entry kernel: a chunked prefill run with either produces the same
+    outputs and caches bit for bit."""
+    from kqb200 import synth
+    dims = synth.QsaDims(hidden=2048, query_heads=16, kv_heads=2, head_dim=256, index_heads=4, index_dim=128,
+                         block=4, budget=512, max_context=4096, rotary=64)
+    weights, prov, layer, w = _qsa_setup(kq, oracle, dims, 77, proj_type=8)
+    try:
+        k0, v0, r0 = synth.qsa_cache(177, dims, 1500)
+        x = synth.hidden(277, 200, dims.hidden)
+        runs = []
+        for shared in ("0", "1"):
+            monkeypatch.setenv("KQ_B200_SCORE_SHARED", shared)
+            s = kq.QsaState(layer, 2048)
+            s.load(k0, v0, r0)
+            y = s.execute_quantized(x)
+            runs.append((y, *s.save()))
+            s.close()
+        for a, b in zip(*runs):
+            assert np.array_equal(bits(a), bits(b))
+    finally:
+        layer.close()
+        prov.close()
+
+
 def test_qsa_decode_batch_ragged_contexts(kq, oracle):
     import torch
     from kqb200 import synth
