@@ -391,11 +391,13 @@ __device__ __forceinline__ uint64_t sc_add2(uint64_t a, uint64_t b) {
 }
 
 // Block scores of E consecutive entries of one sequence (E a multiple of 4)
-// per thread: every block-key load serves E entries, and the E dots of one
-// (head, feature) step run as E / 2 paired products and sums.  The queries
-// sit in shared memory as [head][feature][entry].  Same arithmetic, in the
-// same order, per entry as qsa_score_kernel.
-template <int E>
+// for NB blocks per thread (blocks bi + j * kScoreThreads): every block-key
+// load serves E entries, every query read from shared memory serves NB
+// blocks, and the E dots of one (head, feature) step run as E / 2 paired
+// products and sums.  The queries sit in shared memory as
+// [head][feature][entry].  Same arithmetic, in the same order, per entry
+// and block as qsa_score_kernel.
+template <int E, int NB>
 __global__ void __launch_bounds__(kScoreThreads)
 qsa_score_pair_kernel(QsaDims d, QsaBatch bt, uint32_t batch, const float *__restrict__ iq,
                       float *__restrict__ scores, uint32_t ld_scores, ErrorWord err) {
@@ -412,30 +414,43 @@ qsa_score_pair_kernel(QsaDims d, QsaBatch bt, uint32_t batch, const float *__res
         nb[e] = (uint32_t)e < ne ? (batch_seq(bt, e0 + e).length + 1) / d.block : 0u;
         nb_max = max(nb_max, nb[e]);
     }
-    if (blockIdx.x * kScoreThreads >= nb_max) return;   // uniform over the CTA
+    const uint32_t cta_blocks = NB * kScoreThreads;
+    if (blockIdx.x * cta_blocks >= nb_max) return;   // uniform over the CTA
     const uint32_t di = d.index_dim, n = d.index_heads * di;
     for (uint32_t i = threadIdx.x; i < E * n; i += kScoreThreads) {
         const uint32_t e = i % E, hf = i / E;
         qsh[i] = e < ne ? iq[(size_t)(e0 + e) * n + hf] : 0.0f;
     }
     __syncthreads();
-    const uint32_t bi = blockIdx.x * kScoreThreads + threadIdx.x;
-    if (bi >= nb_max) return;
+    const uint32_t bi0 = blockIdx.x * cta_blocks + threadIdx.x;
+    if (bi0 >= nb_max) return;
     const QsaSeq s = batch_seq(bt, e0);
     const uint32_t ld = block_key_ld(s.capacity, d.block);
-    const float *key = s.block_keys + bi;
-    float score[E];
+    bool live[NB];
+    const float *key[NB];
 #pragma unroll
-    for (int e = 0; e < E; ++e) score[e] = 0.0f;
+    for (int j = 0; j < NB; ++j) {
+        live[j] = bi0 + j * kScoreThreads < nb_max;
+        key[j] = s.block_keys + (live[j] ? bi0 + j * kScoreThreads : bi0);
+    }
+    float score[NB][E];
+#pragma unroll
+    for (int j = 0; j < NB; ++j)
+#pragma unroll
+        for (int e = 0; e < E; ++e) score[j][e] = 0.0f;
     for (uint32_t h0 = 0; h0 < d.index_heads; h0 += kScoreHeads) {
         const uint32_t nh = min(kScoreHeads, d.index_heads - h0);
-        uint64_t dot[kScoreHeads][E / 2];
+        uint64_t dot[NB][kScoreHeads][E / 2];
 #pragma unroll
-        for (uint32_t h = 0; h < kScoreHeads; ++h)
+        for (int j = 0; j < NB; ++j)
 #pragma unroll
-            for (int p = 0; p < E / 2; ++p) dot[h][p] = 0ull;   // (+0.0f, +0.0f)
-        auto step = [&](uint32_t f, float kf) {
-            const uint64_t k2 = sc_pair(kf, kf);
+            for (uint32_t h = 0; h < kScoreHeads; ++h)
+#pragma unroll
+                for (int p = 0; p < E / 2; ++p) dot[j][h][p] = 0ull;   // (+0.0f, +0.0f)
+        auto step = [&](uint32_t f, const float (&kf)[NB]) {
+            uint64_t k2[NB];
+#pragma unroll
+            for (int j = 0; j < NB; ++j) k2[j] = sc_pair(kf[j], kf[j]);
 #pragma unroll
             for (uint32_t h = 0; h < kScoreHeads; ++h) {
                 if (h < nh) {
@@ -443,41 +458,59 @@ qsa_score_pair_kernel(QsaDims d, QsaBatch bt, uint32_t batch, const float *__res
 #pragma unroll
                     for (int p = 0; p < E / 4; ++p) {
                         const float4 q4 = *reinterpret_cast<const float4 *>(qp + 4 * p);
-                        dot[h][2 * p] = sc_add2(dot[h][2 * p], sc_mul2(sc_pair(q4.x, q4.y), k2));
-                        dot[h][2 * p + 1] = sc_add2(dot[h][2 * p + 1], sc_mul2(sc_pair(q4.z, q4.w), k2));
+                        const uint64_t qa = sc_pair(q4.x, q4.y), qb = sc_pair(q4.z, q4.w);
+#pragma unroll
+                        for (int j = 0; j < NB; ++j) {
+                            dot[j][h][2 * p] = sc_add2(dot[j][h][2 * p], sc_mul2(qa, k2[j]));
+                            dot[j][h][2 * p + 1] = sc_add2(dot[j][h][2 * p + 1], sc_mul2(qb, k2[j]));
+                        }
                     }
                 }
             }
         };
         uint32_t f = 0;
-        for (; f + 8 <= di; f += 8) {
-            float kv[8];
+        for (; f + 4 <= di; f += 4) {
+            float kv[4][NB];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) kv[j] = key[(size_t)(f + j) * ld];
+            for (int t = 0; t < 4; ++t)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) step(f + j, kv[j]);
+                for (int j = 0; j < NB; ++j) kv[t][j] = key[j][(size_t)(f + t) * ld];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) step(f + t, kv[t]);
         }
-        for (; f < di; ++f) step(f, key[(size_t)f * ld]);
+        for (; f < di; ++f) {
+            float kv[NB];
+#pragma unroll
+            for (int j = 0; j < NB; ++j) kv[j] = key[j][(size_t)f * ld];
+            step(f, kv);
+        }
         // positive dots, added in head order
 #pragma unroll
-        for (uint32_t h = 0; h < kScoreHeads; ++h) {
-            if (h >= nh) continue;
+        for (int j = 0; j < NB; ++j)
 #pragma unroll
-            for (int p = 0; p < E / 2; ++p) {
-                float lo, hi;
-                sc_unpair(dot[h][p], lo, hi);
-                if (lo > 0.0f) score[2 * p] = __fadd_rn(score[2 * p], lo);
-                if (hi > 0.0f) score[2 * p + 1] = __fadd_rn(score[2 * p + 1], hi);
+            for (uint32_t h = 0; h < kScoreHeads; ++h) {
+                if (h >= nh) continue;
+#pragma unroll
+                for (int p = 0; p < E / 2; ++p) {
+                    float lo, hi;
+                    sc_unpair(dot[j][h][p], lo, hi);
+                    if (lo > 0.0f) score[j][2 * p] = __fadd_rn(score[j][2 * p], lo);
+                    if (hi > 0.0f) score[j][2 * p + 1] = __fadd_rn(score[j][2 * p + 1], hi);
+                }
             }
-        }
     }
     bool bad = false;
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-        if ((uint32_t)e < ne && bi < nb[e]) {
-            const float sc = __fdiv_rn(score[e], d.sqrt_index_dim);
-            bad |= !isfinite(sc);
-            scores[(size_t)(e0 + e) * ld_scores + bi] = sc;
+    for (int j = 0; j < NB; ++j) {
+        const uint32_t bi = bi0 + j * kScoreThreads;
+        if (!live[j]) continue;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            if ((uint32_t)e < ne && bi < nb[e]) {
+                const float sc = __fdiv_rn(score[j][e], d.sqrt_index_dim);
+                bad |= !isfinite(sc);
+                scores[(size_t)(e0 + e) * ld_scores + bi] = sc;
+            }
         }
     }
     if (bad) qsa_raise(err, kErrNonFinite);
@@ -496,10 +529,10 @@ void launch_qsa_score(const QsaDims &d, const QsaBatch &b, uint32_t batch,
     const bool big = xblocks * ((batch + 3) / 4) >= 4u * 148u || (force && atoi(force) == 1);
     const bool big8 = xblocks * ((batch + 7) / 8) >= 4u * 148u || (force && atoi(force) == 1);
     if (shared_sequence && batch > 1 && big8) {
-        // eight entries per key load, paired products
-        dim3 grid(xblocks, (batch + 7) / 8);
-        launch_pdl(qsa_score_pair_kernel<8>, grid, kScoreThreads, 8 * n * sizeof(float), stream, d, b, batch, iq,
-                   scores, ld_scores, err);
+        // eight entries per key load, two blocks per query read, paired products
+        dim3 grid((max_blocks + 2 * kScoreThreads - 1) / (2 * kScoreThreads), (batch + 7) / 8);
+        launch_pdl(qsa_score_pair_kernel<8, 2>, grid, kScoreThreads, 8 * n * sizeof(float), stream, d, b, batch,
+                   iq, scores, ld_scores, err);
     } else if (shared_sequence && batch > 1 && big) {
         dim3 grid(xblocks, (batch + 3) / 4);
         launch_pdl(qsa_score_kernel<4>, grid, kScoreThreads, 4 * n * sizeof(float), stream, d, b, batch, iq, scores,
