@@ -86,6 +86,30 @@ __device__ __forceinline__ void split_store(uint16_t *hi, uint16_t *lo, size_t i
     lo[i] = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(h)));
 }
 
+// TF32 hi (round to nearest, ties away) and lo (the residual, rounded) of x
+__device__ __forceinline__ void tf32_split(float x, uint32_t &hi, uint32_t &lo) {
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(hi) : "f"(x));
+    const float r = x - __uint_as_float(hi);
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(lo) : "f"(r));
+}
+
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// (x0, x1) -> bf16x2 hi and bf16x2 lo of the residuals, x0 in the low half
+__device__ __forceinline__ void bf16_split2(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
 size_t gdn_chunk_workspace_floats(const GdnDims &d, uint32_t tokens) {
     const size_t chunks = (tokens + kC - 1) / kC;
     return chunks * d.value_heads * kChunkFloats + (size_t)tokens * d.value_width;   // + O
@@ -144,33 +168,67 @@ gdn_chunk_prep_kernel(GdnDims d, uint32_t tokens, const float *__restrict__ qk, 
         }
     }
     __syncthreads();
-    // L (strictly lower) and P (lower incl. diagonal): thread -> row i,
-    // columns j = (tid & 3) + 4 r (the four column groups of a warp read
-    // four consecutive K rows: different banks)
+    // L (strictly lower) and P (lower incl. diagonal) on the tensor cores:
+    // warp w computes rows 16 (w & 3) .. +15 and columns 32 (w >> 2) .. +31
+    // of both with m16n8k8 TF32 MMAs and the three-term split (hi = tf32(x),
+    // lo = tf32(x - hi); a b ~ a_hi b_hi + a_hi b_lo + a_lo b_hi, relative
+    // error ~ 2^-22).  Fragments come from the swizzled F32 tiles (the 8
+    // rows of a fragment read 8 different 16-byte chunks).
     {
-        const int i = tid >> 2, j0 = tid & 3;
-        float lk[16], pq[16];
+        const int warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
+        const int m0 = 16 * (warp & 3), n0 = 32 * (warp >> 2);
+        auto at = [&](const float *T, int r, int f) { return T[sw(r, f & ~3) + (f & 3)]; };
+        float lacc[4][4], pacc[4][4];
 #pragma unroll
-        for (int r = 0; r < 16; ++r) { lk[r] = 0.f; pq[r] = 0.f; }
-        for (int kk = 0; kk < kD; kk += 4) {
-            const float4 ki = *reinterpret_cast<const float4 *>(Ks + sw(i, kk));
-            const float4 qi = *reinterpret_cast<const float4 *>(Qs + sw(i, kk));
+        for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                const float4 kj = *reinterpret_cast<const float4 *>(Ks + sw(j0 + 4 * r, kk));
-                lk[r] = fmaf(ki.x, kj.x, fmaf(ki.y, kj.y, fmaf(ki.z, kj.z, fmaf(ki.w, kj.w, lk[r]))));
-                pq[r] = fmaf(qi.x, kj.x, fmaf(qi.y, kj.y, fmaf(qi.z, kj.z, fmaf(qi.w, kj.w, pq[r]))));
+            for (int e = 0; e < 4; ++e) lacc[nt][e] = pacc[nt][e] = 0.0f;
+#pragma unroll 2
+        for (int k0 = 0; k0 < kD; k0 += 8) {
+            uint32_t kh[4], kl[4], qh[4], ql[4];
+            const int ar[4] = {m0 + g, m0 + g + 8, m0 + g, m0 + g + 8};
+            const int ac[4] = {k0 + q, k0 + q, k0 + q + 4, k0 + q + 4};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                tf32_split(at(Ks, ar[e], ac[e]), kh[e], kl[e]);
+                tf32_split(at(Qs, ar[e], ac[e]), qh[e], ql[e]);
+            }
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+                const int j = n0 + 8 * nt + g;
+                uint32_t bh0, bl0, bh1, bl1;
+                tf32_split(at(Ks, j, k0 + q), bh0, bl0);
+                tf32_split(at(Ks, j, k0 + q + 4), bh1, bl1);
+                mma_tf32(lacc[nt], kh, bh0, bh1);
+                mma_tf32(pacc[nt], qh, bh0, bh1);
+                mma_tf32(lacc[nt], kh, bl0, bl1);
+                mma_tf32(pacc[nt], qh, bl0, bl1);
+                mma_tf32(lacc[nt], kl, bh0, bh1);
+                mma_tf32(pacc[nt], ql, bh0, bh1);
             }
         }
-        const float gi = Gs[i];
+        // decay factors; accumulator element e is row m0 + g (+ 8 for e >= 2),
+        // column n0 + 8 nt + 2 q + (e & 1)
+        uint32_t *ph = reinterpret_cast<uint32_t *>(wk + kChunkPh), *pl = reinterpret_cast<uint32_t *>(wk + kChunkPl);
 #pragma unroll
-        for (int r = 0; r < 16; ++r) {
-            const int j = j0 + 4 * r;
-            const float f = j <= i ? expf(gi - Gs[j]) : 0.0f;
-            Ls[i * kC + j] = j < i ? lk[r] * f : 0.0f;
-            split_store(reinterpret_cast<uint16_t *>(wk + kChunkPh), reinterpret_cast<uint16_t *>(wk + kChunkPl),
-                        (size_t)i * kLT + j, pq[r] * f);
-        }
+        for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int i = m0 + g + 8 * half, j = n0 + 8 * nt + 2 * q;
+                const float gi = Gs[i];
+                float pv[2];
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int jj = j + c;
+                    const float f = jj <= i ? expf(gi - Gs[jj]) : 0.0f;
+                    Ls[i * kC + jj] = jj < i ? lacc[nt][2 * half + c] * f : 0.0f;
+                    pv[c] = pacc[nt][2 * half + c] * f;
+                }
+                uint32_t hi, lo;
+                bf16_split2(pv[0], pv[1], hi, lo);
+                ph[((size_t)i * kLT + j) / 2] = hi;
+                pl[((size_t)i * kLT + j) / 2] = lo;
+            }
     }
     // Q [64][136] and K^T [128][72] as bf16 pairs for the tensor-core pass
     {
