@@ -1,4 +1,5 @@
-// QSA (gated block-sparse grouped-query attention) decode kernels.
+// QSA (gated block-sparse grouped-query attention) kernels: decode batches
+// and uniform prefill groups (consecutive tokens of one sequence).
 //
 // Math follows the per-token loop of kq_qsa_execute_common
 // (src/kq_qsa_qwen38.c:524-828 of Kestrel-Q):
@@ -16,7 +17,9 @@
 // the selected blocks - are bit-identical to the reference given identical
 // inputs.  The block key of a block is computed once, when the block
 // completes, and cached feature-major; the reference recomputes the same
-// value from the raw keys on every token.
+// value from the raw keys on every token.  The attention over the selected
+// tokens is checked to tolerance instead: for head_dim 256 it runs on the
+// tensor cores over bf16 hi / lo copies of the cache rows.
 #include "kernels.hpp"
 
 #include <cstdlib>
