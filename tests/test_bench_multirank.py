@@ -67,3 +67,23 @@ def test_reference_arm_runs_on_rank_zero_only():
     import bench
     # a non-zero rank returns at once, without touching the oracle
     assert bench.run_reference(None, rank=1, world=2) == 0
+
+
+def test_reference_arm_prints_the_contract_line():
+    """`bench.py --impl reference` times the reference's own CPU operators
+    (oracle/_ref, else the restatement) on this host and prints one JSON
+    line with the fields the driver reads."""
+    import subprocess
+    out = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", "1",
+                          "--warmup", "1"], capture_output=True, text=True, cwd=REPO, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["unit"] == "tok/s" and line["higher_is_better"] is True
+    assert line["steps"] == 1 and line["warmup"] == 1 and line["n_gpus"] == 1
+    assert line["value"] > 0 and line["config"]["workload"].startswith("config3")
+    cb = line["cpu_baseline"]
+    assert cb["value"] == line["value"] and cb["kind"] in ("reference", "port") and cb["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
