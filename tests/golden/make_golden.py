@@ -1,8 +1,8 @@
 """Extracts the reference's own golden vectors into compact test fixtures.
 
-Run once in a checkout that has the Kestrel-Q tree (default
-/root/reference); the outputs are committed so that tests never read the
-reference at run time:
+Run once on a machine that has the Kestrel-Q tree (its location is the
+--reference argument); the outputs are committed so that tests never read
+the reference at run time:
 
   gdn_golden.npz / gdn_golden.json   research/operators/.../gdn-{contract,
                                      calibration,holdout,state-vectors,
@@ -15,7 +15,7 @@ reference at run time:
 Expected values in those files come from pinned Transformers / llama.cpp
 oracles (never from Kestrel-Q itself); the calibrated abs / rel / ULP
 contracts are copied alongside.  Usage:
-  python tests/golden/make_golden.py [--reference /root/reference]
+  python tests/golden/make_golden.py [--reference <Kestrel-Q checkout>]
 """
 from __future__ import annotations
 
