@@ -161,16 +161,21 @@ kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
  * It allocates nothing: its scratch is one 4 MiB array compiled into the
  * library (held on every GPU that loads it until exit), and it calls no
  * cudaMalloc, cudaFree or other allocating routine.
- *   - Limit: batches above 8 need ceil(batch/64) * ceil(columns/64) * 16 KiB
- *     of activation tiles, at most 4 MiB - 256 B; larger calls return
- *     KQ_STATUS_LIMIT_EXCEEDED.
+ *   - Limit: on the tensor-core path (batches above 8, weight types it
+ *     covers) a call needs ceil(batch/64) * ceil(columns/64) * 16 KiB of
+ *     activation tiles, at most 4 MiB - 256 B; larger calls return
+ *     KQ_STATUS_LIMIT_EXCEEDED.  The warp GEMV (batches up to 8) and the
+ *     CUDA-core tiles use no scratch and have no such limit.
  *   - Runs on `cuda_stream` (NULL: the legacy default stream) and waits for
  *     it before returning, so non-finite input is reported by this call
  *     (KQ_STATUS_NUMERIC_DOMAIN).
- *   - The first call on a device looks up the array's device address
- *     (cudaGetSymbolAddress); make that call before any stream capture.
+ *   - kq_b200_provider_create looks up the array's device address on its
+ *     device (cudaGetSymbolAddress), which makes the driver load the array
+ *     there: create the provider before committing the rest of HBM.
  *   - Every call on a device shares the array (the last call's contents
- *     stay in it): calls whose kernels overlap on the GPU race.
+ *     stay in it, and its first word is the call's error word): calls whose
+ *     kernels overlap on the GPU race, on the tiles and on that word, so one
+ *     such call can also report another's KQ_STATUS_NUMERIC_DOMAIN.
  * The caller's current device is restored on return. */
 kq_status kq_b200_provider_linear_batch_f32_static(kq_weight_provider *provider,
                                                    const kq_semantic_tensor *semantic,

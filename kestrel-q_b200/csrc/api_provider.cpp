@@ -59,6 +59,8 @@ kq_status kq_b200_provider_create(int device, kq_weight_provider **out, kq_diagn
     DeviceContext *c;
     st = context(&c, diagnostic);
     if (st != KQ_STATUS_OK) return st;
+    st = static_scratch_prepare(device, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
     auto *p = new kq_weight_provider();
     p->device = device;
     *out = p;

@@ -20,8 +20,15 @@
 // the GPU (different streams, or several host threads) race on it.
 //
 // The device address of the array is looked up once per device, with that
-// device current, on the first call that runs there (cudaGetSymbolAddress);
-// that first call should come before any stream capture.
+// device current, when a provider is created on it (kq_b200_provider_create
+// calls static_scratch_prepare).  The lookup is what makes the driver load
+// the array, so it happens at provider creation, before the host commits the
+// rest of HBM, and not on a later call: under lazy module loading the first
+// use of this file's code would otherwise allocate the 4 MiB then.
+//
+// The limit applies to the tensor-core path only (batches above 8 on a
+// weight type the tensor-core GEMM covers); the warp GEMV and the CUDA-core
+// tiles use no scratch.
 #include "kernels.hpp"
 #include "provider.hpp"
 #include "runtime.hpp"
@@ -43,6 +50,8 @@ static __device__ __align__(256) uint8_t g_linear_scratch[kStaticScratchBytes];
 std::mutex g_scratch_mu;
 uint8_t *g_scratch_addr[kMaxStaticDevices];   // device address of g_linear_scratch, per device
 
+}  // namespace
+
 // Device address of the scratch array on the current device `device`.
 kq_status static_scratch(int device, uint8_t **out, kq_diagnostic *d) {
     if (device < 0 || device >= kMaxStaticDevices)
@@ -57,6 +66,13 @@ kq_status static_scratch(int device, uint8_t **out, kq_diagnostic *d) {
     *out = g_scratch_addr[device];
     return KQ_STATUS_OK;
 }
+
+kq_status static_scratch_prepare(int device, kq_diagnostic *d) {
+    uint8_t *p = nullptr;
+    return static_scratch(device, &p, d);
+}
+
+namespace {
 
 // Runs on `device`, then restores the caller's current device.
 struct DeviceScope {
@@ -94,7 +110,8 @@ kq_status kq_b200_provider_linear_batch_f32_static(kq_weight_provider *provider,
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "batched linear takes device buffers");
     if (ranges_overlap(x, (uint64_t)batch * columns * 4, y, (uint64_t)batch * rows * 4))
         return fail(diagnostic, KQ_STATUS_ALIASING_VIOLATION, "linear input and output overlap");
-    const size_t tiles = batch > 8 ? umma_xtile_bytes(batch, (uint32_t)columns, /*allow_wide=*/false) : 0;
+    const bool umma_path = batch > 8 && !force_simt_projection() && umma_supported(t->m);
+    const size_t tiles = umma_path ? umma_xtile_bytes(batch, (uint32_t)columns, /*allow_wide=*/false) : 0;
     if (tiles > kStaticScratchBytes - kErrorBytes) {
         char msg[160];
         snprintf(msg, sizeof msg, "batch %u x %llu columns needs %zu bytes of activation tiles; the static scratch "
@@ -114,7 +131,7 @@ kq_status kq_b200_provider_linear_batch_f32_static(kq_weight_provider *provider,
     ProjSegments segs{};
     segs.count = 1;
     segs.m[0] = t->m;
-    const bool tensor_cores = batch > 8 && !force_simt_projection() &&
+    const bool tensor_cores = umma_path &&
                               launch_projection_umma(segs, x, (uint32_t)columns, y, (uint32_t)rows, batch,
                                                      scratch + kErrorBytes, kStaticScratchBytes - kErrorBytes,
                                                      err, stream, /*cache_maps=*/false, /*allow_wide=*/false);

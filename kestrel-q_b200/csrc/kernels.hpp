@@ -1,17 +1,50 @@
 // Internal launch interface between the host ABI layer and the CUDA kernels.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
+#include <mutex>
 
 #include <cuda_runtime.h>
 
 namespace kqb {
 
+// Runs a set-up step (cudaFuncSetAttribute and the like) once per device.
+// Function attributes belong to the current device's context, so a launcher
+// used on several devices of one process must set them on each; the step
+// has completed on a device before any caller on that device goes past run().
+struct DeviceOnce {
+    std::atomic<uint64_t> done{0};
+    std::mutex mu;
+    template <typename F>
+    void run(F &&f) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+            f();
+            return;
+        }
+        const uint64_t bit = 1ull << dev;
+        if (done.load(std::memory_order_acquire) & bit) return;
+        std::lock_guard<std::mutex> lk(mu);
+        if (done.load(std::memory_order_relaxed) & bit) return;
+        f();
+        done.fetch_or(bit, std::memory_order_release);
+    }
+};
+
 // Programmatic dependent launch: every kernel of the library is launched
-// with launch_pdl, which lets the GPU set it up while the previous kernel
-// on the stream is still finishing, and every kernel starts with pdl_wait(),
-// which blocks until that previous kernel has completed and its writes are
-// visible.  Nothing is read or written before the wait.
+// with launch_pdl (or the same attribute), and every kernel calls pdl_wait()
+// before it touches anything the previous kernel on the stream may write.
+// pdl_wait() blocks until that previous kernel has completed and its writes
+// are visible, then lets the next kernel's CTAs start (launch_dependents).
+// Because every kernel triggers only after its own wait, a kernel whose
+// CTAs are running knows that every kernel before its predecessor has
+// completed: work that depends only on such older kernels, or on nothing
+// written by a kernel (uploaded weights), may run before pdl_wait() and so
+// overlap the predecessor.  Two kernels use that: the tensor-core projection
+// issues its first weight loads, the fused GDN decode loads its recurrent
+// state (written by the previous decode step, never by the projection just
+// before it), with L2-only loads.
 template <typename... KArgs, typename... Args>
 inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                        Args &&...args) {
@@ -29,7 +62,10 @@ inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 
 #ifdef __CUDACC__
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 #endif
 
 // Error word shared by every kernel of one device.  0 = no error; otherwise
@@ -97,6 +133,8 @@ bool launch_projection_umma(const ProjSegments &segs, const float *x, uint32_t l
                             size_t xtile_bytes, ErrorWord err, cudaStream_t stream,
                             bool cache_maps = true, bool allow_wide = true);
 size_t umma_xtile_bytes(uint32_t batch, uint32_t cols, bool allow_wide = true);
+// True when the tensor-core path covers this matrix's type and layout.
+bool umma_supported(const QMatrix &m);
 // Work space (in floats) that launch_projection uses for `batch` rows of
 // input with `cols` columns: the activation tiles of the tensor-core path.
 size_t projection_workspace_floats(uint32_t batch, uint32_t ldy, uint32_t cols);

@@ -534,8 +534,8 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
     const uint32_t chunks = (tokens + kC - 1) / kC;
     float *obuf = work + (size_t)chunks * d.value_heads * kChunkFloats;
     const size_t smem1 = (size_t)(3 * kC * kD + kC * kC + 2 * kC) * sizeof(float);
-    static bool attr = false;
-    if (!attr) {
+    static DeviceOnce attr;
+    attr.run([&] {
         cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
         cudaFuncSetAttribute(gdn_chunk_state_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)StateSmem<32>::bytes);
@@ -543,8 +543,7 @@ void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatch
                              (int)StateSmem<16>::bytes);
         cudaFuncSetAttribute(gdn_chunk_state_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)StateSmem<8>::bytes);
-        attr = true;
-    }
+    });
     {
         KernelTimer t1("gdn_chunk_prep", stream);
         launch_pdl(gdn_chunk_prep_kernel, dim3(d.value_heads, chunks), 256, smem1, stream, d, tokens, qk, v, beta,

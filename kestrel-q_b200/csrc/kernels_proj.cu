@@ -454,13 +454,12 @@ static void launch_exact_tiles(const ProjSegments &in, const float *x, uint32_t 
         mode = i == 0 ? mi : (mode == mi ? mode : 2);
     }
     constexpr size_t smem = ExTile<TR>::smem;
-    static bool attr = false;
-    if (!attr) {
+    static DeviceOnce attr;
+    attr.run([] {
         cudaFuncSetAttribute(proj_exact_kernel<0, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaFuncSetAttribute(proj_exact_kernel<1, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         cudaFuncSetAttribute(proj_exact_kernel<2, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-    }
+    });
     if (mode == 0)
         launch_pdl(proj_exact_kernel<0, TR>, grid, kExThreads, smem, stream, segs, x, ldx, y, ldy, batch, err);
     else if (mode == 1)

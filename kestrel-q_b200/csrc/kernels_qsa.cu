@@ -1697,30 +1697,27 @@ void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
         // stages and one CTA
         const char *e = getenv("KQ_B200_ATTEND_STAGES");
         if (e != nullptr && e[0] == '6') {
-            static bool attr6 = false;
-            if (!attr6) {
+            static DeviceOnce attr6;
+            attr6.run([] {
                 cudaFuncSetAttribute(qsa_attend_tc_kernel<6, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)TcLayout<6>::bytes);
-                attr6 = true;
-            }
+            });
             launch_pdl(qsa_attend_tc_kernel<6, 1>, grid, kTcThreads, TcLayout<6>::bytes, stream, d, b, q, selected,
                        selected_count, partial_o, partial_ml, splits, err);
         } else {
-            static bool attr3 = false;
-            if (!attr3) {
+            static DeviceOnce attr3;
+            attr3.run([] {
                 cudaFuncSetAttribute(qsa_attend_tc_kernel<3, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)TcLayout<3>::bytes);
-                attr3 = true;
-            }
+            });
             launch_pdl(qsa_attend_tc_kernel<3, 2>, grid, kTcThreads, TcLayout<3>::bytes, stream, d, b, q, selected,
                        selected_count, partial_o, partial_ml, splits, err);
         }
     } else if (d.head_dim == 256 && d.repeat <= 8) {
-        static bool attr = false;
-        if (!attr) {
+        static DeviceOnce attr;
+        attr.run([] {
             cudaFuncSetAttribute(qsa_attend_mh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMhSmem);
-            attr = true;
-        }
+        });
         launch_pdl(qsa_attend_mh_kernel, grid, 256, kMhSmem, stream, d, b, q, selected, selected_count, partial_o,
                    partial_ml, splits, err);
     } else if (d.head_dim == 256 || d.head_dim == 128) {

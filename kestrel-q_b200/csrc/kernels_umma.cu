@@ -542,7 +542,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const uint8_t *__restrict__ xtiles,
                  uint32_t nchunks_x, float *__restrict__ y, uint32_t ldy, uint32_t batch,
                  uint32_t kchunks_per_split, ErrorWord err) {
-    pdl_wait();
     using R = Ring<T, NT>;
     constexpr uint32_t SC = TypeCfg<T>::sc, kRawBytes = R::raw, kX = R::xdepth, kRawRing = R::rr;
     constexpr uint32_t kXSlot = Tile<NT>::xslot, kABufs = Tile<NT>::abufs, kABase = Tile<NT>::abase;
@@ -550,12 +549,11 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ uint64_t rfull[kMaxRawRing], rfree[kMaxRawRing], xfull[kMaxXRing], mdone[kMaxXRing];
     __shared__ uint64_t aready[kMaxABufs], adone[kMaxABufs], accum;
-    __shared__ uint32_t tmem_base_slot;
+    __shared__ uint32_t tmem_base_slot, skip_slot;
     __shared__ volatile uint32_t abort_flag;
     static_assert(NT != 64 || kUM * kAccStride * 4 <= kX * kXSlot, "exchange tile does not fit");
     // No early return anywhere: every CTA of a split-K cluster must reach
     // both cluster barriers.
-    const bool skip = *reinterpret_cast<volatile unsigned long long *>(err.word) != 0ull;
 
     uint8_t *raw_ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *x_ring = raw_ring + kRawRing * kRawBytes;
@@ -570,7 +568,7 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     // kchunks_per_split is a multiple of SC, so c_begin starts a super-block step
     const uint32_t c_begin = blockIdx.z * kchunks_per_split;
     const uint32_t c_end = min(nchunks_total, c_begin + kchunks_per_split);
-    const uint32_t nchunks = (c_end > c_begin && !skip) ? c_end - c_begin : 0;
+    const uint32_t nchunks_planned = c_end > c_begin ? c_end - c_begin : 0;
 
     if (tid == 0) {
         for (uint32_t s = 0; s < kRawRing; ++s) mbar_init(&rfull[s], 1);
@@ -597,20 +595,50 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base_slot;
 
+    // The weights of the first raw slots are requested before the wait: they
+    // are uploaded by the host and never written by a kernel, so their loads
+    // overlap the previous kernel (see pdl_wait).
+    uint32_t prefetched = 0;   // raw steps already issued (producer thread)
+    const CUtensorMap *maps = tmaps.map[seg];
+    const uint32_t rtx = raw_tx<T>(tmaps.box_rows[seg]);
+    const uint32_t sb0 = c_begin / SC;
+    if (warp == kTmaWarp && lane == 0 && nchunks_planned > 0) {
+        prefetched = min((nchunks_planned + SC - 1) / SC, kRawRing);
+        for (uint32_t j = 0; j < prefetched; ++j) {
+            mbar_expect_tx(&rfull[j], rtx);
+            load_raw<T>(smem_u32(raw_ring + j * kRawBytes), maps, m.cols, sb0 + j, (int)row0, &rfull[j]);
+        }
+    }
+    pdl_wait();
+    // one read of the error word for the whole CTA, so that every role
+    // agrees on the chunk count
+    if (tid == 0) skip_slot = *reinterpret_cast<volatile unsigned long long *>(err.word) != 0ull ? 1u : 0u;
+    __syncthreads();
+    const bool skip = skip_slot != 0u;
+    const uint32_t nchunks = skip ? 0u : nchunks_planned;
+
     if (warp == kTmaWarp) {
         // ---- producer: one thread issues every copy
+        if (lane == 0 && skip) {
+            // an earlier kernel failed: only let the weight loads already in
+            // flight land before the CTA exits
+            for (uint32_t j = 0; j < prefetched; ++j)
+                if (!mbar_wait(&rfull[j], 0u, &abort_flag, kSiteRawFull)) break;
+        }
         if (lane == 0 && nchunks > 0) {
-            const CUtensorMap *maps = tmaps.map[seg];
-            const uint32_t rtx = raw_tx<T>(tmaps.box_rows[seg]);
-            const uint32_t sb0 = c_begin / SC;
             for (uint32_t it = 0; it < nchunks; ++it) {
                 if (it % SC == 0) {
-                    // raw slot of step j was last used by step j - kRawRing
+                    // raw slot of step j was last used by step j - kRawRing;
+                    // steps below `prefetched` were issued before the wait
                     const uint32_t j = it / SC, rs = j % kRawRing;
-                    if (j >= kRawRing && !mbar_wait(&rfree[rs], ((j - kRawRing) / kRawRing) & 1u, &abort_flag, kSiteRawFree))
-                        break;
-                    mbar_expect_tx(&rfull[rs], rtx);
-                    load_raw<T>(smem_u32(raw_ring + rs * kRawBytes), maps, m.cols, sb0 + j, (int)row0, &rfull[rs]);
+                    if (j >= prefetched) {
+                        if (j >= kRawRing &&
+                            !mbar_wait(&rfree[rs], ((j - kRawRing) / kRawRing) & 1u, &abort_flag, kSiteRawFree))
+                            break;
+                        mbar_expect_tx(&rfull[rs], rtx);
+                        load_raw<T>(smem_u32(raw_ring + rs * kRawBytes), maps, m.cols, sb0 + j, (int)row0,
+                                    &rfull[rs]);
+                    }
                 }
                 const uint32_t xs = it % kX;
                 if (it >= kX && !mbar_wait(&mdone[xs], ((it - kX) / kX) & 1u, &abort_flag, kSiteXFree)) break;
@@ -947,10 +975,14 @@ static bool choose_wide(uint32_t tiles, uint32_t nchunks, uint32_t batch) {
 }
 
 // Largest split cluster (8, 4, 2 or 1) the device can co-schedule for this
-// kernel; queried once per type.
+// kernel; queried once per type and device (the attribute it sets belongs to
+// the current device).
 template <uint32_t T>
 static uint32_t max_splits_for() {
-    static uint32_t cached = 0;
+    static std::atomic<uint32_t> per_device[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 63;
+    uint32_t cached = per_device[dev].load(std::memory_order_acquire);
     if (cached == 0) {
         cudaFuncSetAttribute(proj_umma_kernel<T, kUN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Ring<T, kUN>::smem);
@@ -975,6 +1007,7 @@ static uint32_t max_splits_for() {
         }
         (void)cudaGetLastError();
         cached = best;
+        per_device[dev].store(cached, std::memory_order_release);
     }
     return cached;
 }
@@ -996,12 +1029,11 @@ static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &s
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     if (wide) {
-        static bool attr = false;
-        if (!attr) {
+        static DeviceOnce attr;
+        attr.run([] {
             cudaFuncSetAttribute(proj_umma_kernel<T, kUNWide>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  Ring<T, kUNWide>::smem);
-            attr = true;
-        }
+        });
         cfg.gridDim = dim3(tiles, (batch + kUNWide - 1) / kUNWide, 1);
         cfg.dynamicSmemBytes = Ring<T, kUNWide>::smem;
         cfg.numAttrs = 1;

@@ -32,3 +32,11 @@ struct kq_weight_provider {
 // descriptor was not created by `provider`.
 ProviderTensor *provider_lookup(const kq_weight_provider *provider,
                                 const kq_semantic_tensor *semantic);
+
+// Makes the allocation-free linear's static scratch array resident on the
+// current device `device` and records its device address (api_static.cu).
+// Called when a provider is created, so that the array is in place before
+// the host commits the rest of HBM.
+namespace kqb {
+kq_status static_scratch_prepare(int device, kq_diagnostic *diagnostic);
+}  // namespace kqb

@@ -1,9 +1,9 @@
 """Allocation-free batched linear (kq_b200_provider_linear_batch_f32_static).
 
 Collected last on purpose: it must give the allocating entry point's results
-both in a fresh process and after every other test has run.  Each shape is
-called twice in a row, because the entry point's scratch array keeps the
-previous call's contents.
+(and the CPU oracle's) both in a fresh process and after every other test has
+run.  Each shape is called twice in a row, because the entry point's scratch
+array keeps the previous call's contents.
 """
 import ctypes as C
 
@@ -24,7 +24,12 @@ def _close(a, b, what):
 
 
 @pytest.mark.parametrize("type_id,rows,cols,batch", [(12, 520, 2048, 64), (14, 2048, 4096, 100), (8, 96, 512, 5)])
-def test_static_linear_matches_allocating_entry(kq, type_id, rows, cols, batch):
+def test_static_linear_matches_allocating_entry(kq, oracle, type_id, rows, cols, batch):
+    """Two calls in a row: each must equal the allocating entry point and the
+    CPU oracle's row dots, batches above 8 must have run the tensor-core GEMM
+    (check + activation tiles + GEMM = three launches; the CUDA-core
+    fallback would be two), and a warmed-up call must leave the device's free
+    memory unchanged."""
     import torch
     from kqb200 import synth
     rng = np.random.default_rng(rows * 7 + batch)
@@ -34,7 +39,8 @@ def test_static_linear_matches_allocating_entry(kq, type_id, rows, cols, batch):
     try:
         h = p.add_matrix("m", 11, q)
         for call in range(2):
-            x = torch.from_numpy(rng.normal(size=(batch, cols)).astype(np.float32)).cuda()
+            xn = rng.normal(size=(batch, cols)).astype(np.float32)
+            x = torch.from_numpy(xn).cuda()
             y_ref = torch.full((batch, rows), float("nan"), device="cuda")
             y_static = torch.full((batch, rows), float("nan"), device="cuda")
             torch.cuda.synchronize()
@@ -43,10 +49,20 @@ def test_static_linear_matches_allocating_entry(kq, type_id, rows, cols, batch):
                                                        y_ref.data_ptr(), C.byref(d))
             assert st == 0, d.text()
             kq.synchronize()
+            free0 = torch.cuda.mem_get_info()[0]
+            n0 = lib.kq_b200_kernel_launch_count()
             st = lib.kq_b200_provider_linear_batch_f32_static(p.handle, h, rows, cols, x.data_ptr(), batch,
                                                               y_static.data_ptr(), None, C.byref(d))
             assert st == 0, d.text()
-            _close(y_static.cpu().numpy(), y_ref.cpu().numpy(), f"type {type_id} call {call}")
+            launched = lib.kq_b200_kernel_launch_count() - n0
+            free1 = torch.cuda.mem_get_info()[0]
+            if batch > 8:
+                assert launched == 3, f"tensor-core path did not run ({launched} launches)"
+            if call == 1:
+                assert free1 == free0, f"free device memory changed by {free0 - free1} bytes"
+            ys = y_static.cpu().numpy()
+            _close(ys, y_ref.cpu().numpy(), f"type {type_id} call {call} vs allocating entry")
+            _close(ys, oracle.matvec(type_id, q, rows, cols, xn), f"type {type_id} call {call} vs oracle")
     finally:
         p.close()
 
