@@ -1,24 +1,41 @@
-"""GDN+QSA layer-block decode benchmark on B200.
+"""GDN+QSA layer-block benchmark on B200: decode B=64 as
+the headline, with the prefill configurations (2 and 4) as sub-records.
 
-Workload per GPU: a 4-layer hybrid block (3 GDN layers + 1 QSA layer, hidden
-2048, GDN 16x128 key / 32x128 value heads, QSA 16 query / 2 KV heads of 256,
-block 4, budget 2048) decoding one token for each of 64 independent
-sequences whose contexts are drawn uniformly from [1k, 32k] (seed 0 + rank).
-In-projections Q4_K, out-projections Q6_K, index projections BF16; F32 state
-and KV caches.  A step = one token through the whole block for all 64
-sequences.  Multi-GPU: one process per GPU, each rank serves its own 64
-sequences (sequence sharding, no data-path collective; weak scaling).
+Headline workload per GPU: a 4-layer hybrid block (3 GDN layers + 1 QSA
+layer, hidden 2048, GDN 16x128 key / 32x128 value heads, QSA 16 query / 2 KV
+heads of 256, block 4, budget 2048) decoding one token for each of 64
+independent sequences whose contexts are drawn uniformly from [1k, 32k]
+(seed 0 + rank).  In-projections Q4_K, out-projections Q6_K, index
+projections BF16; F32 state and KV caches.  A step = one token through the
+whole block for all 64 sequences.  Multi-GPU: one process per GPU, each rank
+serves its own 64 sequences (sequence sharding, no data-path collective;
+weak scaling).
+
+Sub-records of the same JSON line (default run; `--no-prefill` skips them):
+  prefill_8k.gdn_layer  config 2: one GDN layer, Q6_K projections, 8192
+                        tokens from a zero state (chunked WY-form recurrence)
+  prefill_8k.block      the 4-layer block of config 4 on 8192 tokens
+  prefill_131k          config 4: the 4-layer block (all projections Q4_K,
+                        index BF16) on 131072 tokens
+Every prefill runs tensor-parallel over the run's ranks (GDN by value-head
+group, QSA by query-head group or by token within a KV-head group, the
+indexer's selections exchanged once per layer call) with one NCCL
+all-reduce of the partial outputs after every layer's out-projection
+(strong scaling); at one GPU it is the plain layer.
 
 Inputs are synthetic and seeded (no dataset): weights and states are drawn
-with the distributions BASELINE.json names.  The per-step working set
-(≈1.6 GB of state, KV and weights) is larger than the 126 MB L2, so no L2
-flush is needed between steps.
+with the distributions BASELINE.json names.  Every timed step's working set
+(GBs of state, KV, weights and activations) is larger than the 126 MB L2, so
+no L2 flush is needed between steps.
 
-`--workload prefill` runs BASELINE config 4 instead: one 131072-token
-prefill of the same block (all projections Q4_K, index BF16) with the layers
-tensor-parallel over the ranks (GDN by value-head group, QSA by query-head
-group, indexer replicated) and one NCCL all-reduce of the partial outputs
-after every layer's out-projection (strong scaling).
+Timing: W warm-up steps, then exactly K steps between barrier +
+synchronize on both sides, CUDA events on the library stream, max over
+ranks.  The per-kernel timing behind `roofline` is a separate pass of the
+same steps with events around that kernel family's launches (events between
+kernels break the programmatic-dependent-launch overlap, so they stay out of
+the headline region).  `e2e` repeats the step through the public API with
+the step's inputs copied from pinned host memory and its outputs read back
+inside the timed region.
 
 Arms:
   default          the B200 library through its C-ABI (kestrel-q_b200)
@@ -50,6 +67,9 @@ METRIC = "GDN+QSA block tok/s (decode B=64, prefill 8k) at 1-8 B200; % HBM/TC ro
 BATCH = 64
 CTX_RANGE = (1024, 32768)
 GDN_LAYERS = 3
+PREFILL_TOKENS = 131072
+PREFILL_SLICE = 16384
+CPU_PREFILL_TOKENS = 16
 
 
 def peaks():
@@ -79,17 +99,13 @@ def contexts(rank: int, n: int = BATCH, ctx_max: int = CTX_RANGE[1]):
 
 
 def layer_weights():
-    """The block's weights: one model, replicated on every rank."""
+    """Config 3: the block's weights (one model, replicated on every rank)."""
     from kqb200 import synth
     gd, qd = dims()
     gdn = [synth.gdn_layer(l, gd, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_Q4_K)
            for l in range(GDN_LAYERS)]
     qsa = synth.qsa_layer(7, qd, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_BF16)
     return gdn, qsa
-
-
-PREFILL_TOKENS = 131072
-PREFILL_SLICE = 16384
 
 
 def prefill_weights():
@@ -99,7 +115,22 @@ def prefill_weights():
     gdn = [synth.gdn_layer(20 + l, gd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_Q4_K)
            for l in range(GDN_LAYERS)]
     qsa = synth.qsa_layer(27, qd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_BF16)
-    return gdn, qsa
+    return gdn, [qsa]
+
+
+def gdn_prefill_weights():
+    """Config 2: one GDN layer with every projection Q6_K."""
+    from kqb200 import synth
+    gd, _ = dims()
+    return [synth.gdn_layer(202, gd, synth.TYPE_Q6_K, synth.TYPE_Q6_K, synth.TYPE_Q6_K)], []
+
+
+PREFILL_KINDS = {
+    "gdn_layer": ("config2: one GDN layer prefill from a zero state, batch 1, Q6_K projections, F32 state",
+                  gdn_prefill_weights),
+    "block": ("config4: 4-layer block (3 GDN + 1 QSA) prefill, batch 1, projections Q4_K, index BF16, "
+              "F32 activations/state/KV", prefill_weights),
+}
 
 
 def wy_flops_per_chunk_head(C: int = 64, d: int = 128) -> int:
@@ -110,24 +141,23 @@ def wy_flops_per_chunk_head(C: int = 64, d: int = 128) -> int:
     return 7 * C * C * d + 6 * C * d * d
 
 
-def prefill_flops(T: int):
-    """Algorithmic FLOPs of one T-token prefill of the whole block (all
-    ranks together), by part."""
+def prefill_flops(T: int, gdn_layers: int = GDN_LAYERS, qsa_layers: int = 1):
+    """Algorithmic FLOPs of one T-token prefill (all ranks together), by part."""
     gd, qd = dims()
     H, C, Vd, Hv = gd.hidden, gd.conv_channels, gd.value_width, gd.value_heads
-    gdn_proj = GDN_LAYERS * (2 * T * H * (C + Vd + 2 * Hv) + 2 * T * Vd * H)
+    gdn_proj = gdn_layers * (2 * T * H * (C + Vd + 2 * Hv) + 2 * T * Vd * H)
     chunks = (T + 63) // 64
-    wy = GDN_LAYERS * Hv * chunks * wy_flops_per_chunk_head(64, gd.key_dim)
-    qw, kvw = qd.q_width, qd.kv_width
-    iw = qd.index_heads * qd.index_dim + qd.index_dim
-    qsa_proj = 2 * T * H * (2 * qw + 2 * kvw) + 2 * T * qw * H + 2 * T * H * iw
-    pos = np.arange(T, dtype=np.int64)
-    nb = (pos + 1) // qd.block
-    ntok = np.minimum(nb, qd.budget // qd.block) * qd.block + (pos + 1) % qd.block
-    indexer = int(2 * qd.index_heads * qd.index_dim * nb.sum())
-    attention = int(4 * qd.query_heads * qd.head_dim * ntok.sum())
-    parts = {"gdn_proj": gdn_proj, "gdn_wy": wy, "qsa_proj": qsa_proj, "qsa_indexer": indexer,
-             "qsa_attention": attention}
+    wy = gdn_layers * Hv * chunks * wy_flops_per_chunk_head(64, gd.key_dim)
+    parts = {"gdn_proj": gdn_proj, "gdn_wy": wy}
+    if qsa_layers:
+        qw, kvw = qd.q_width, qd.kv_width
+        iw = qd.index_heads * qd.index_dim + qd.index_dim
+        pos = np.arange(T, dtype=np.int64)
+        nb = (pos + 1) // qd.block
+        ntok = np.minimum(nb, qd.budget // qd.block) * qd.block + (pos + 1) % qd.block
+        parts["qsa_proj"] = qsa_layers * (2 * T * H * (2 * qw + 2 * kvw) + 2 * T * qw * H + 2 * T * H * iw)
+        parts["qsa_indexer"] = qsa_layers * int(2 * qd.index_heads * qd.index_dim * nb.sum())
+        parts["qsa_attention"] = qsa_layers * int(4 * qd.query_heads * qd.head_dim * ntok.sum())
     return sum(parts.values()), parts
 
 
@@ -161,10 +191,10 @@ def job_tokens_per_s(world: int, batch_per_rank: int, ms_per_step: float) -> flo
 
 
 def algorithmic_bytes(gdn, qsa, ctx, batch):
-    """HBM bytes one step must move at minimum (per GPU): every weight once,
-    GDN state and conv state read + written once, QSA K/V read only for the
-    selected tokens, cached block keys once, new K/V/raw rows written, and
-    the block's activations."""
+    """HBM bytes one decode step must move at minimum (per GPU): every
+    weight once, GDN state and conv state read + written once, QSA K/V read
+    only for the selected tokens, cached block keys once, new K/V/raw rows
+    written, and the block's activations."""
     gd, qd = dims()
     w = sum(t.nbytes for L in gdn for t in (L.qkv, L.gate, L.beta, L.alpha, L.output))
     w += sum(t.nbytes for t in (qsa.query, qsa.key, qsa.value, qsa.output, qsa.index_query, qsa.index_key))
@@ -211,10 +241,11 @@ class ClockSampler:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            time.sleep(0.3)   # let the sampler start before the timed work
         except FileNotFoundError:
             self.proc = None
         return self
@@ -255,12 +286,18 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- CPU arm
 
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_block_sample(n_seqs: int, threads: int, rank: int = 0):
     """The reference's own F32 operators (oracle/_ref when built, else the
     restatement) decoding one token of the 4-layer block for `n_seqs`
     sequences of the workload, `threads` sequences in parallel.
     Returns (tokens_per_second, kind, seconds)."""
-    from kqb200 import synth
     from oracle import oracle as O
     impl = "reference" if O.ref_available() else "port"
     gd, qd = dims()
@@ -295,17 +332,17 @@ def cpu_block_sample(n_seqs: int, threads: int, rank: int = 0):
     return n_seqs / elapsed, impl, elapsed
 
 
-def cpu_prefill_sample(tokens: int):
+def cpu_prefill_sample(kind: str, tokens: int):
     """The reference's own F32 operators (oracle/_ref when built, else the
-    restatement) prefilling the first `tokens` tokens of the config-4 block
-    from empty states, one thread (the reference prefill of one sequence is
-    sequential).  Returns (tokens_per_second, kind, seconds)."""
+    restatement) prefilling the first `tokens` tokens of a prefill workload
+    (PREFILL_KINDS) from empty states, one thread (the reference's prefill
+    of one sequence is sequential).  Returns (tokens_per_second, kind, seconds)."""
     from oracle import oracle as O
     impl = "reference" if O.ref_available() else "port"
     gd, qd = dims()
-    gdn, qsa = prefill_weights()
+    gdn, qsa = PREFILL_KINDS[kind][1]()
     gw = [O.gdn_weights_f32(L) for L in gdn]
-    qw = O.qsa_weights_f32(qsa)
+    qw = [O.qsa_weights_f32(L) for L in qsa]
     x = np.random.default_rng(99).normal(size=(tokens, gd.hidden)).astype(np.float32)
     conv = np.zeros(gd.conv_channels * gd.conv_kernel, np.float32)
     rec = np.zeros(gd.value_heads * gd.key_dim * gd.value_dim, np.float32)
@@ -313,64 +350,36 @@ def cpu_prefill_sample(tokens: int):
     zr = np.zeros((tokens, qd.index_dim), np.float32)
     t0 = time.perf_counter()
     h = x
-    for l in range(GDN_LAYERS):
-        st, h, _, _ = O.gdn_run(gd, gw[l], h, conv, rec, impl=impl)
+    for w in gw:
+        st, h, _, _ = O.gdn_run(gd, w, h, conv, rec, impl=impl)
         assert st == 0
-    st, h, *_ = O.qsa_run(qd, qw, h, z, z, zr, 0, tokens, impl=impl)
-    assert st == 0
+    for w in qw:
+        st, h, *_ = O.qsa_run(qd, w, h, z, z, zr, 0, tokens, impl=impl)
+        assert st == 0
     elapsed = time.perf_counter() - t0
     return tokens / elapsed, impl, elapsed
 
 
-def cpu_threads():
-    try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
-
-
-def run_reference_prefill(args, rank, world):
-    if rank != 0:
-        return 0
-    from oracle import oracle as O
-    if not O.PORT_LIB.exists():
-        O.build()
-    n = args.cpu_tokens
-    cpu_prefill_sample(2)
-    vals, kind = [], "reference"
-    t_all = time.perf_counter()
-    for _ in range(args.steps):
-        v, impl, _ = cpu_prefill_sample(n)
-        kind = "reference" if impl == "reference" else "port"
-        vals.append(v)
-    elapsed = time.perf_counter() - t_all
-    value = statistics.median(vals)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / max(1, args.steps),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config4: 4-layer GDN+QSA block prefill, batch 1, Q4_K",
-                   "sample": f"first {n} tokens of the prefill per step"},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": 1, "kind": kind,
-                         "sample": f"first {n} tokens of the 4-layer block prefill from empty states, 1 thread"},
-        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+def cpu_prefill_record(kind: str, tokens: int = CPU_PREFILL_TOKENS):
+    v, impl, secs = cpu_prefill_sample(kind, tokens)
+    return {"value": v, "unit": "tok/s", "cores": 1, "kind": "reference" if impl == "reference" else "port",
+            "sample": f"first {tokens} tokens of the {kind} prefill from empty states, 1 thread "
+                      f"({secs:.1f} s wall)"}
 
 
 def run_reference(args, rank, world):
+    """The reference arm: rank 0 alone times the reference's CPU operators on
+    every host core it may use; other ranks exit at once."""
     if rank != 0:
         return 0
-    if args.workload == "prefill":
-        return run_reference_prefill(args, rank, world)
-    threads = min(cpu_threads(), 16)
-    n = threads
     from oracle import oracle as O
     if not O.PORT_LIB.exists():
         O.build()
-    for _ in range(args.warmup if args.warmup < 1 else 1):
-        cpu_block_sample(min(2, n), min(2, threads))
+    threads = cpu_threads()
+    if args.workload == "prefill":
+        return run_reference_prefill(args, world)
+    n = threads
+    cpu_block_sample(min(2, n), min(2, threads))
     vals = []
     kind = "reference"
     t_all = time.perf_counter()
@@ -387,7 +396,37 @@ def run_reference(args, rank, world):
         "config": {"workload": "config3: 4-layer GDN+QSA block decode, B=64, ctx U[1k,32k]",
                    "sample": f"{n} sequences x 1 token per step"},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": kind,
-                         "sample": f"{n} sequences x 1 token of the 4-layer block, {threads} threads"},
+                         "sample": f"{n} sequences x 1 token of the 4-layer block, {threads} threads "
+                                   f"(one sequence per thread)"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    if not args.no_prefill:
+        line["prefill_8k"] = {k: {"impl": "reference", "cpu_baseline": cpu_prefill_record(k)}
+                              for k in ("gdn_layer", "block")}
+        line["prefill_131k"] = {"impl": "reference", "cpu_baseline": cpu_prefill_record("block")}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_prefill(args, world):
+    vals, kind = [], "reference"
+    cpu_prefill_sample("block", 2)
+    t_all = time.perf_counter()
+    for _ in range(args.steps):
+        v, impl, _ = cpu_prefill_sample("block", args.cpu_tokens)
+        kind = "reference" if impl == "reference" else "port"
+        vals.append(v)
+    elapsed = time.perf_counter() - t_all
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / max(1, args.steps),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": PREFILL_KINDS["block"][0],
+                   "sample": f"first {args.cpu_tokens} tokens of the prefill per step"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": 1, "kind": kind,
+                         "sample": f"first {args.cpu_tokens} tokens of the 4-layer block prefill from empty "
+                                   f"states, 1 thread"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -396,28 +435,84 @@ def run_reference(args, rank, world):
 
 # ---------------------------------------------------------------- B200 arm
 
-def run_b200(args, rank, world, local_rank):
+class Ctx:
+    """Per-rank plumbing: device, library stream, process group."""
+
+    def __init__(self, rank, world, local_rank):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        import kqb200
+        self.rank, self.world, self.local_rank = rank, world, local_rank
+        self.torch, self.dist, self.kq = torch, dist, kqb200
+        torch.cuda.set_device(local_rank)
+        d = kqb200.abi.Diagnostic()
+        kqb200.abi.check(kqb200.lib().kq_b200_set_device(local_rank, C.byref(d)), d)
+        if world > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local_rank))
+        self.lib = kqb200.lib()
+        self.stream = torch.cuda.ExternalStream(self.lib.kq_b200_get_stream())
+        self.device = torch.device("cuda", local_rank)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def sync(self):
+        self.kq.synchronize()
+        self.torch.cuda.synchronize()
+
+    def timed(self, steps, fn):
+        """Device time of `steps` calls of fn() on the library stream (ms per
+        step), bracketed by barrier + synchronize on both sides."""
+        torch = self.torch
+        self.barrier()
+        self.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(self.stream):
+            e0.record(self.stream)
+            for _ in range(steps):
+                fn()
+            e1.record(self.stream)
+        self.sync()
+        self.barrier()
+        return e0.elapsed_time(e1) / steps
+
+    def family_ms(self, family, steps, fn):
+        """Per-step device time of one kernel family (events around its
+        launches), over `steps` extra calls of fn(); returns (ms, launches)."""
+        import ctypes as C
+        self.lib.kq_b200_profile_kernel(family.encode())
+        with self.torch.cuda.stream(self.stream):
+            for _ in range(steps):
+                fn()
+        self.sync()
+        n_, t_ = C.c_uint64(), C.c_double()
+        self.lib.kq_b200_profile_read(C.byref(n_), C.byref(t_))
+        self.lib.kq_b200_profile_kernel(None)
+        return t_.value / steps, n_.value / steps
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def decode_record(args, cx: Ctx):
+    """Config 3 decode: the headline record."""
     import ctypes as C
-
-    import torch
-    import torch.distributed as dist
-
-    import kqb200
-    from kqb200 import synth
-
-    torch.cuda.set_device(local_rank)
-    d = kqb200.abi.Diagnostic()
-    kqb200.abi.check(kqb200.lib().kq_b200_set_device(local_rank, C.byref(d)), d)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local_rank))
+    torch, kqb200 = cx.torch, cx.kq
+    rank, world = cx.rank, cx.world
     gd, qd = dims()
     gdn_w, qsa_w = layer_weights()
     ctx = contexts(rank, ctx_max=args.ctx_max)
     B = BATCH
-    steps_total = args.warmup + 2 * args.steps + 40
-    prov = kqb200.Provider(local_rank)
+    steps_total = args.warmup + 3 * args.steps + 40
+    prov = kqb200.Provider(cx.local_rank)
     gdn_layers = [kqb200.GdnLayer(gd, w, prov, layer=l) for l, w in enumerate(gdn_w)]
     qsa_layer = kqb200.QsaLayer(qd, qsa_w, prov, layer=3)
 
@@ -432,8 +527,8 @@ def run_b200(args, rank, world, local_rank):
             rec = torch.randn(gd.value_heads * gd.key_dim * gd.value_dim, device="cuda", generator=gen) * 0.02
             torch.cuda.synchronize()
             dd = kqb200.abi.Diagnostic()
-            kqb200.abi.check(kqb200.lib().kq_gdn_state_import_f32(s.handle, conv.data_ptr(), conv.numel(),
-                                                                  rec.data_ptr(), rec.numel(), 1, C.byref(dd)), dd)
+            kqb200.abi.check(cx.lib.kq_gdn_state_import_f32(s.handle, conv.data_ptr(), conv.numel(),
+                                                            rec.data_ptr(), rec.numel(), 1, C.byref(dd)), dd)
             row.append(s)
         gdn_states.append(row)
     qsa_states = []
@@ -445,14 +540,11 @@ def run_b200(args, rank, world, local_rank):
         r = torch.randn(L, qd.index_dim, device="cuda", generator=gen)
         torch.cuda.synchronize()
         dd = kqb200.abi.Diagnostic()
-        kqb200.abi.check(kqb200.lib().kq_qsa_state_import_f32(s.handle, k.data_ptr(), k.numel(), v.data_ptr(),
-                                                              v.numel(), r.data_ptr(), r.numel(), L, C.byref(dd)), dd)
+        kqb200.abi.check(cx.lib.kq_qsa_state_import_f32(s.handle, k.data_ptr(), k.numel(), v.data_ptr(),
+                                                        v.numel(), r.data_ptr(), r.numel(), L, C.byref(dd)), dd)
         del k, v, r
         qsa_states.append(s)
     torch.cuda.synchronize()
-
-    lib = kqb200.lib()
-    stream = torch.cuda.ExternalStream(lib.kq_b200_get_stream())
     bufs = [torch.randn(B, gd.hidden, device="cuda", generator=gen) for _ in range(GDN_LAYERS + 2)]
     torch.cuda.synchronize()
 
@@ -464,72 +556,42 @@ def run_b200(args, rank, world, local_rank):
         kqb200.qsa_decode_batch(qsa_layer, qsa_states, h_in, y_ptr)
 
     x0, y0 = bufs[0].data_ptr(), bufs[GDN_LAYERS + 1].data_ptr()
-    for _ in range(args.warmup):
-        step(x0, y0)
-    kqb200.synchronize()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    # ---- device-resident timed region
-    lib.kq_b200_profile_kernel(b"gdn_recurrence")
-    launches0 = lib.kq_b200_kernel_launch_count()
-    with ClockSampler(local_rank) as clocks:
-        barrier()
-        torch.cuda.synchronize()
-        kqb200.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
+    with torch.cuda.stream(cx.stream):
+        for _ in range(args.warmup):
             step(x0, y0)
-        e1.record(stream)
-        kqb200.synchronize()
-        torch.cuda.synchronize()
-        barrier()
-    launches = lib.kq_b200_kernel_launch_count() - launches0
-    ms = e0.elapsed_time(e1) / args.steps
-    rec_n, rec_ms = C.c_uint64(), C.c_double()
-    lib.kq_b200_profile_read(C.byref(rec_n), C.byref(rec_ms))
-    lib.kq_b200_profile_kernel(None)
+    cx.sync()
 
+    # ---- device-resident timed region (no per-launch events)
+    launches0 = cx.lib.kq_b200_kernel_launch_count()
+    with ClockSampler(cx.local_rank) as clocks:
+        ms = cx.timed(args.steps, lambda: step(x0, y0))
+    launches = cx.lib.kq_b200_kernel_launch_count() - launches0
+
+    # ---- the roofline kernel, timed in a pass of its own
+    rec_ms, rec_n = cx.family_ms("gdn_recurrence", args.steps, lambda: step(x0, y0))
     breakdown = {}
     if args.breakdown:
-        for fam in ("proj", "proj_exact", "gdn_conv", "gdn_recurrence", "qsa_prepare", "qsa_score",
-                    "qsa_select", "qsa_attend", "qsa_combine"):
-            lib.kq_b200_profile_kernel(fam.encode())
-            for _ in range(3):
-                step(x0, y0)
-            kqb200.synchronize()
-            n_, t_ = C.c_uint64(), C.c_double()
-            lib.kq_b200_profile_read(C.byref(n_), C.byref(t_))
-            breakdown[fam] = {"ms_per_step": t_.value / 3, "launches_per_step": n_.value / 3}
-        lib.kq_b200_profile_kernel(None)
+        for fam in ("proj", "proj_exact", "gdn_recurrence", "qsa_prepare", "qsa_score", "qsa_select",
+                    "qsa_attend", "qsa_combine"):
+            t, n = cx.family_ms(fam, 5, lambda: step(x0, y0))
+            breakdown[fam] = {"ms_per_step": t, "launches_per_step": n}
 
     # ---- end-to-end: pinned host input -> block -> host result, every step
     xh = torch.randn(B, gd.hidden, generator=torch.Generator().manual_seed(5)).pin_memory()
     yh = torch.empty(B, gd.hidden).pin_memory()
-    barrier()
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    with torch.cuda.stream(stream):
-        for _ in range(args.steps):
-            bufs[0].copy_(xh, non_blocking=True)
-            step(x0, y0)
-            yh.copy_(bufs[GDN_LAYERS + 1], non_blocking=True)
-    f1.record(stream)
-    kqb200.synchronize()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = f0.elapsed_time(f1) / args.steps
+
+    def e2e_step():
+        bufs[0].copy_(xh, non_blocking=True)
+        step(x0, y0)
+        yh.copy_(bufs[GDN_LAYERS + 1], non_blocking=True)
+
+    e2e_ms = cx.timed(args.steps, e2e_step)
     assert torch.isfinite(yh).all(), "non-finite block output"
 
-    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world, torch.device("cuda", local_rank))
-
+    ms, e2e_ms, rec_ms = max_over_ranks([ms, e2e_ms, rec_ms], world, cx.device)
     step_bytes, parts = algorithmic_bytes(gdn_w, qsa_w, ctx, B)
     hbm, peak_kind = peaks()
-    rec_avg_ms = rec_ms.value / max(1, rec_n.value)
+    rec_avg_ms = rec_ms / max(1.0, rec_n)
     rec_bytes = recurrence_bytes_per_launch(B)
     achieved = rec_bytes / (rec_avg_ms * 1e-3) / 1e9
     traffic = None
@@ -571,7 +633,8 @@ def run_b200(args, rank, world, local_rank):
             "traffic": traffic,
             "algorithmic_bytes_per_launch": rec_bytes,
             "avg_launch_ms": rec_avg_ms,
-            "launches_timed": rec_n.value,
+            "launches_timed": int(rec_n * args.steps),
+            "timing": "CUDA events around each launch of the kernel, in a pass of its own after the timed region",
         },
         "e2e": {"value": job_tokens_per_s(world, B, e2e_ms), "unit": "tok/s",
                 "h2d_bytes_per_step": B * gd.hidden * 4, "d2h_bytes_per_step": B * gd.hidden * 4},
@@ -579,16 +642,6 @@ def run_b200(args, rank, world, local_rank):
         **({"kernel_breakdown": breakdown} if breakdown else {}),
         "clocks": clocks.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        threads = min(cpu_threads(), 16)
-        v, impl, secs = cpu_block_sample(threads, threads, rank)
-        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads,
-                                "kind": "reference" if impl == "reference" else "port",
-                                "sample": f"{threads} sequences x 1 token of the 4-layer block "
-                                          f"({secs:.1f} s wall)"}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    # release
     for row in gdn_states:
         for s in row:
             s.close()
@@ -598,160 +651,99 @@ def run_b200(args, rank, world, local_rank):
         L.close()
     qsa_layer.close()
     prov.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    return line
 
 
-def run_b200_prefill(args, rank, world, local_rank):
-    import ctypes as C
-
-    import torch
-    import torch.distributed as dist
-
-    import kqb200
+def prefill_record(args, cx: Ctx, kind: str, T: int, steps: int, warmup: int, cpu: bool):
+    """One prefill workload (PREFILL_KINDS) of T tokens, tensor-parallel over
+    the ranks; returns its record (every rank takes the same collective
+    steps)."""
+    torch, kqb200 = cx.torch, cx.kq
     from kqb200 import tp
-
-    torch.cuda.set_device(local_rank)
-    d = kqb200.abi.Diagnostic()
-    kqb200.abi.check(kqb200.lib().kq_b200_set_device(local_rank, C.byref(d)), d)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local_rank))
-    gd, qd = dims()
-    T = args.tokens
-    gdn_w, qsa_w = prefill_weights()
-    prov = kqb200.Provider(local_rank)
-    lib = kqb200.lib()
-    stream = torch.cuda.ExternalStream(lib.kq_b200_get_stream())
-    exchange = tp.torch_exchange(stream) if world > 1 and not args.replicated_indexer else None
-    block = tp.TensorParallelBlock(kqb200, prov, gdn_w, [qsa_w], rank, world, capacity=T, exchange=exchange)
+    rank, world = cx.rank, cx.world
+    gd, _ = dims()
+    gdn_w, qsa_w = PREFILL_KINDS[kind][1]()
+    prov = kqb200.Provider(cx.local_rank)
+    exchange = tp.torch_exchange(cx.stream) if world > 1 and not args.replicated_indexer else None
+    block = tp.TensorParallelBlock(kqb200, prov, gdn_w, qsa_w, rank, world, capacity=T, exchange=exchange)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(4321)   # the same input on every rank (replicated activations)
     x = torch.randn(T, gd.hidden, device="cuda", generator=gen)
     bufs = [torch.empty(T, gd.hidden, device="cuda") for _ in range(block.layer_count)]
     torch.cuda.synchronize()
-
-    def all_reduce(t):
-        return dist.all_reduce(t, async_op=True)
-
-    reduce = all_reduce if world > 1 else None
+    reduce = (lambda t: cx.dist.all_reduce(t, async_op=True)) if world > 1 else None
+    slice_tokens = min(args.slice_tokens, T)
 
     def step(inp):
         block.reset()
-        block.prefill(inp, bufs, T, reduce, slice_tokens=args.slice_tokens)
+        block.prefill(inp, bufs, T, reduce, slice_tokens=slice_tokens)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
+    with torch.cuda.stream(cx.stream):
+        for _ in range(warmup):
             step(x)
-    kqb200.synchronize()
-    torch.cuda.synchronize()
-
-    lib.kq_b200_profile_kernel(b"proj")
-    launches0 = lib.kq_b200_kernel_launch_count()
-    with ClockSampler(local_rank) as clocks:
-        barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(args.steps):
-                step(x)
-            e1.record(stream)
-        kqb200.synchronize()
-        torch.cuda.synchronize()
-        barrier()
-    launches = lib.kq_b200_kernel_launch_count() - launches0
-    ms = e0.elapsed_time(e1) / args.steps
-    proj_n, proj_ms = C.c_uint64(), C.c_double()
-    lib.kq_b200_profile_read(C.byref(proj_n), C.byref(proj_ms))
-    lib.kq_b200_profile_kernel(None)
-
+    cx.sync()
+    launches0 = cx.lib.kq_b200_kernel_launch_count()
+    with ClockSampler(cx.local_rank) as clocks:
+        ms = cx.timed(steps, lambda: step(x))
+    launches = cx.lib.kq_b200_kernel_launch_count() - launches0
+    proj_ms, proj_n = cx.family_ms("proj", steps, lambda: step(x))
     breakdown = {}
     if args.breakdown:
-        for fam in ("proj", "proj_exact", "gdn_conv", "gdn_recurrence", "gdn_chunk_prep", "gdn_chunk_state",
-                    "gdn_gate_norm", "qsa_prepare", "qsa_block_keys", "qsa_score", "qsa_select", "qsa_attend",
-                    "qsa_combine"):
-            lib.kq_b200_profile_kernel(fam.encode())
-            with torch.cuda.stream(stream):
-                step(x)
-            kqb200.synchronize()
-            torch.cuda.synchronize()
-            n_, t_ = C.c_uint64(), C.c_double()
-            lib.kq_b200_profile_read(C.byref(n_), C.byref(t_))
-            breakdown[fam] = {"ms_per_step": t_.value, "launches_per_step": n_.value}
-        lib.kq_b200_profile_kernel(None)
+        for fam in ("proj", "proj_exact", "gdn_conv", "gdn_chunk_prep", "gdn_chunk_state", "gdn_gate_norm",
+                    "qsa_prepare", "qsa_block_keys", "qsa_score", "qsa_select", "qsa_attend", "qsa_combine"):
+            t, n = cx.family_ms(fam, 1, lambda: step(x))
+            breakdown[fam] = {"ms_per_step": t, "launches_per_step": n}
 
-    # ---- end-to-end: pinned host input -> block -> host output, every step
     xh = torch.randn(T, gd.hidden, generator=torch.Generator().manual_seed(6)).pin_memory()
     yh = torch.empty(T, gd.hidden).pin_memory()
     xin = torch.empty_like(x)
-    barrier()
-    torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        f0.record(stream)
-        for _ in range(args.steps):
-            xin.copy_(xh, non_blocking=True)
-            step(xin)
-            yh.copy_(bufs[-1], non_blocking=True)
-        f1.record(stream)
-    kqb200.synchronize()
-    torch.cuda.synchronize()
-    barrier()
-    e2e_ms = f0.elapsed_time(f1) / args.steps
-    assert torch.isfinite(yh).all(), "non-finite block output"
 
-    ms, e2e_ms = max_over_ranks([ms, e2e_ms], world, torch.device("cuda", local_rank))
-    total_flops, parts = prefill_flops(T)
+    def e2e_step():
+        xin.copy_(xh, non_blocking=True)
+        step(xin)
+        yh.copy_(bufs[-1], non_blocking=True)
+
+    e2e_ms = cx.timed(steps, e2e_step)
+    assert torch.isfinite(yh).all(), "non-finite prefill output"
+    ms, e2e_ms, proj_ms = max_over_ranks([ms, e2e_ms, proj_ms], world, cx.device)
+    n_gdn, n_qsa = len(gdn_w), len(qsa_w)
+    total_flops, parts = prefill_flops(T, n_gdn, n_qsa)
     tc_flops = rank_tensor_core_flops(block, T)
-    proj_step_ms = proj_ms.value / max(1, args.steps)
-    achieved = tc_flops / (proj_step_ms * 1e-3) / 1e12
+    achieved = tc_flops / (proj_ms * 1e-3) / 1e12
     peak, peak_kind = tensor_peak()
-    line = {
-        "metric": METRIC,
+    qsa_split = ("" if not n_qsa else
+                 f", QSA by query-head group (indexer "
+                 f"{'replicated' if exchange is None else 'scores/top-k split by 64-token chunk, selections all-reduced'})")
+    rec = {
         "value": T * 1000.0 / ms,
         "unit": "tok/s",
         "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
+        "steps": steps,
+        "warmup": warmup,
         "ms_per_step": ms,
-        "higher_is_better": True,
         "scaling": "strong",
-        "vs_baseline": None,
-        "dtype": "f32",
-        "data": "synthetic",
-        "config": {
-            "workload": f"config4: 4-layer block (3 GDN + 1 QSA) prefill of {T} tokens, batch 1, "
-                        f"projections Q4_K, index BF16, F32 activations/state/KV",
-            "parallelism": f"tensor-parallel x{world}: GDN by value-head group, QSA by query-head group "
-                           f"(indexer {'replicated' if exchange is None else 'scores/top-k split by 64-token chunk, one all-reduce of the selections'}), "
-                           f"NCCL all-reduce (f32) after each out-projection",
-            "slice_tokens": args.slice_tokens,
-            "l2": "working set per step (GBs of activations, KV, projections) >> 126 MB L2",
-            "step_algorithmic_flops": total_flops,
-            "step_flops_breakdown": parts,
-            "step_tflops": total_flops / (ms * 1e-3) / 1e12,
-        },
+        "workload": f"{PREFILL_KINDS[kind][0]}, {T} tokens",
+        "parallelism": (f"tensor-parallel x{world}: GDN by value-head group{qsa_split}, "
+                        f"NCCL all-reduce (f32) after each out-projection" if world > 1 else "one GPU"),
+        "slice_tokens": slice_tokens,
+        "step_algorithmic_flops": total_flops,
+        "step_flops_breakdown": parts,
+        "step_tflops": total_flops / (ms * 1e-3) / 1e12,
         "roofline": {
-            "kernel": "proj (xconv + proj_umma: tcgen05 projection GEMMs of this rank's shards)",
+            "kernel": "proj (activation tiles + proj_umma: tcgen05 projection GEMMs of this rank's shards)",
             "bound": "tensor",
             "achieved": achieved,
             "peak": peak,
             "peak_kind": peak_kind,
             "unit": "TFLOP/s",
             "frac": achieved / peak,
+            "bf16_pipe_frac": 3.0 * achieved / peak,
             "traffic": None,
             "algorithmic_flops_per_step": tc_flops,
-            "ms_per_step": proj_step_ms,
-            "launches_timed": proj_n.value,
-            "note": "F32 operands as bf16 hi/lo pairs: three MMAs per algorithmic product",
+            "ms_per_step": proj_ms,
+            "launches_per_step": proj_n,
+            "note": "F32 operands as bf16 hi/lo pairs: three bf16 MMAs per algorithmic product "
+                    "(bf16_pipe_frac = 3 x frac)",
         },
         "e2e": {"value": T * 1000.0 / e2e_ms, "unit": "tok/s",
                 "h2d_bytes_per_step": T * gd.hidden * 4, "d2h_bytes_per_step": T * gd.hidden * 4},
@@ -759,38 +751,70 @@ def run_b200_prefill(args, rank, world, local_rank):
         **({"kernel_breakdown": breakdown} if breakdown else {}),
         "clocks": clocks.summary(),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, impl, secs = cpu_prefill_sample(args.cpu_tokens)
-        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": 1,
-                                "kind": "reference" if impl == "reference" else "port",
-                                "sample": f"first {args.cpu_tokens} tokens of the block prefill from empty "
-                                          f"states, 1 thread ({secs:.1f} s wall)"}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    if cpu and rank == 0 and world == 1:
+        rec["cpu_baseline"] = cpu_prefill_record(kind, args.cpu_tokens)
     block.close()
     prov.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    del x, bufs, xin
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_b200(args, rank, world, local_rank):
+    cx = Ctx(rank, world, local_rank)
+    cpu = not args.no_cpu_baseline
+    if args.workload == "prefill":
+        rec = prefill_record(args, cx, "block", args.tokens, args.steps, args.warmup, cpu)
+        line = {"metric": METRIC, "value": rec["value"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": rec["workload"], "parallelism": rec["parallelism"],
+                           "slice_tokens": rec["slice_tokens"],
+                           "l2": "working set per step (GBs of activations, KV, projections) >> 126 MB L2",
+                           "step_algorithmic_flops": rec["step_algorithmic_flops"],
+                           "step_flops_breakdown": rec["step_flops_breakdown"], "step_tflops": rec["step_tflops"]},
+                **{k: rec[k] for k in ("roofline", "e2e", "gpu_launches", "clocks", "kernel_breakdown",
+                                       "cpu_baseline") if k in rec}}
+    else:
+        line = decode_record(args, cx)
+        if rank == 0 and world == 1 and cpu:
+            threads = cpu_threads()
+            v, impl, secs = cpu_block_sample(threads, threads, rank)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads,
+                                    "kind": "reference" if impl == "reference" else "port",
+                                    "sample": f"{threads} sequences x 1 token of the 4-layer block, one sequence "
+                                              f"per thread ({secs:.1f} s wall)"}
+        if not args.no_prefill:
+            ps, pw = args.prefill_steps, args.prefill_warmup
+            line["prefill_8k"] = {k: prefill_record(args, cx, k, 8192, ps, pw, cpu) for k in ("gdn_layer", "block")}
+            line["prefill_131k"] = prefill_record(args, cx, "block", PREFILL_TOKENS, ps, pw, cpu)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    cx.close()
     return 0
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--breakdown", action="store_true", help="time every kernel family (extra steps)")
+    ap.add_argument("--no-prefill", action="store_true", help="headline decode record only")
+    ap.add_argument("--breakdown", action="store_true", help="time every kernel family (extra passes)")
     ap.add_argument("--ctx-max", type=int, default=CTX_RANGE[1],
                     help="upper end of the context distribution (profiling runs use a small one)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode: config 3 (default); prefill: config 4, tensor-parallel")
-    ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS, help="prefill length (config 4)")
+                    help="decode: config 3 headline with the prefill sub-records (default); "
+                         "prefill: config 4 alone (--tokens) as the line's own record")
+    ap.add_argument("--tokens", type=int, default=PREFILL_TOKENS, help="prefill length (--workload prefill)")
+    ap.add_argument("--prefill-steps", type=int, default=3, help="timed steps of each prefill sub-record")
+    ap.add_argument("--prefill-warmup", type=int, default=3, help="warm-up steps of each prefill sub-record")
     ap.add_argument("--slice-tokens", type=int, default=PREFILL_SLICE,
                     help="prefill tokens per layer call (all-reduce granularity)")
-    ap.add_argument("--cpu-tokens", type=int, default=16, help="prefill tokens of the CPU baseline sample")
+    ap.add_argument("--cpu-tokens", type=int, default=CPU_PREFILL_TOKENS,
+                    help="prefill tokens of the CPU baseline sample")
     ap.add_argument("--replicated-indexer", action="store_true",
                     help="prefill at N > 1: every rank selects for every token (no selection exchange)")
     args = ap.parse_args()
@@ -799,8 +823,6 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
-    if args.workload == "prefill":
-        return run_b200_prefill(args, rank, world, local_rank)
     return run_b200(args, rank, world, local_rank)
 
 

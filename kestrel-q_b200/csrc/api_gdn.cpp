@@ -288,7 +288,7 @@ static kq_status gdn_execute_sync(const kq_gdn_config *cfg, const GdnResolved *w
             if (views[i].owned == nullptr) launch_check_finite(views[i].ptr, counts[i], err, c->stream);
         }
         auto dense = [](const float *p, uint32_t rows, uint32_t cols) {
-            QMatrix m;
+            QMatrix m{};
             m.data = reinterpret_cast<const uint8_t *>(p);
             m.type = 0;
             m.rows = rows;

@@ -1,6 +1,7 @@
 // Device-resident weight provider: the GEMV seam of the operator ABI
 // (kq_weight_provider_linear_f32, src/kq_weight_provider.c:378-509 of
 // Kestrel-Q) over GGUF blocks uploaded once to HBM.
+#include <algorithm>
 #include <cfenv>
 #include <cmath>
 #include <cstring>
@@ -12,6 +13,58 @@
 #include "quant.cuh"
 
 using namespace kqb;
+
+namespace kqb {
+
+// |value| of an IEEE half stored little-endian at p (inf for inf / NaN).
+static double half_abs(const uint8_t *p) {
+    const uint32_t h = (uint32_t)p[0] | ((uint32_t)p[1] << 8);
+    const uint32_t e = (h >> 10) & 31u, m = h & 0x3ffu;
+    if (e == 31u) return INFINITY;
+    return e == 0u ? std::ldexp((double)m, -24) : std::ldexp((double)(m | 0x400u), (int)e - 25);
+}
+
+double weight_abs_bound(uint32_t type, const uint8_t *p, uint64_t rows, uint64_t row_bytes) {
+    const uint64_t total = rows * row_bytes;
+    double b = 0.0;
+    switch (type) {
+    case kTypeQ4_K:   // d * sc * q - dmin * m, sc and m 6-bit, q 4-bit
+        for (uint64_t o = 0; o + 144 <= total; o += 144)
+            b = std::max(b, half_abs(p + o) * 63.0 * 15.0 + half_abs(p + o + 2) * 63.0);
+        break;
+    case kTypeQ6_K:   // d * sc * (q - 32), sc int8, q 6-bit
+        for (uint64_t o = 0; o + 210 <= total; o += 210) b = std::max(b, half_abs(p + o + 208) * 128.0 * 32.0);
+        break;
+    case kTypeQ8_0:   // d * code, code int8
+        for (uint64_t o = 0; o + 34 <= total; o += 34) b = std::max(b, half_abs(p + o) * 128.0);
+        break;
+    case kTypeBF16:
+        for (uint64_t o = 0; o + 2 <= total; o += 2) {
+            const uint32_t bits = ((uint32_t)p[o] | ((uint32_t)p[o + 1] << 8)) << 16;
+            float v;
+            std::memcpy(&v, &bits, 4);
+            b = std::max(b, std::fabs((double)v));
+        }
+        break;
+    default:
+        for (uint64_t o = 0; o + 4 <= total; o += 4) {
+            float v;
+            std::memcpy(&v, p + o, 4);
+            b = std::max(b, std::fabs((double)v));
+        }
+        break;
+    }
+    return b;
+}
+
+int32_t weight_scale_exponent(double bound) {
+    if (!(bound > 0.0) || !std::isfinite(bound)) return 0;
+    int k = 0;
+    std::frexp(bound, &k);   // bound < 2^k
+    return std::min(64, std::max(-64, 14 - k));
+}
+
+}  // namespace kqb
 
 ProviderTensor *provider_lookup(const kq_weight_provider *provider,
                                 const kq_semantic_tensor *semantic) {
@@ -147,6 +200,8 @@ kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *
     t->m.cols = (uint32_t)columns;
     t->m.row_bytes = (uint32_t)row_bytes;
     t->m.layout = layout;
+    t->m.scale_exp = weight_scale_exponent(
+        weight_abs_bound(type_id, static_cast<const uint8_t *>(packed), rows, row_bytes));
     t->desc.canonical_rank = 2;
     t->desc.canonical_dimensions[0] = rows;
     t->desc.canonical_dimensions[1] = columns;

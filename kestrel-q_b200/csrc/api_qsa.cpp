@@ -621,7 +621,7 @@ static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w
             if (views[i].owned == nullptr) launch_check_finite(views[i].ptr, counts[i], err, c->stream);
         }
         auto dense = [](const float *p, uint32_t rows, uint32_t cols) {
-            QMatrix m;
+            QMatrix m{};
             m.data = reinterpret_cast<const uint8_t *>(p);
             m.type = 0;
             m.rows = rows;

@@ -33,18 +33,14 @@ struct DeviceOnce {
 };
 
 // Programmatic dependent launch: every kernel of the library is launched
-// with launch_pdl (or the same attribute), and every kernel calls pdl_wait()
-// before it touches anything the previous kernel on the stream may write.
-// pdl_wait() blocks until that previous kernel has completed and its writes
-// are visible, then lets the next kernel's CTAs start (launch_dependents).
-// Because every kernel triggers only after its own wait, a kernel whose
-// CTAs are running knows that every kernel before its predecessor has
-// completed: work that depends only on such older kernels, or on nothing
-// written by a kernel (uploaded weights), may run before pdl_wait() and so
-// overlap the predecessor.  Two kernels use that: the tensor-core projection
-// issues its first weight loads, the fused GDN decode loads its recurrent
-// state (written by the previous decode step, never by the projection just
-// before it), with L2-only loads.
+// with launch_pdl (or the same attribute), which lets the GPU set it up while
+// the previous kernel on the stream is still finishing, and every kernel
+// calls pdl_wait() before it touches anything the previous kernel may write;
+// pdl_wait() blocks until that kernel has completed and its writes are
+// visible.  Only data no kernel writes (uploaded weights) is requested before
+// the wait: the tensor-core projection issues its first weight loads there.
+// (Triggering dependents early, right after the wait, and loading the GDN
+// recurrent state before it were both measured slower on the decode step.)
 template <typename... KArgs, typename... Args>
 inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                        Args &&...args) {
@@ -62,10 +58,7 @@ inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 
 #ifdef __CUDACC__
-__device__ __forceinline__ void pdl_wait() {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 #endif
 
 // Error word shared by every kernel of one device.  0 = no error; otherwise
@@ -77,6 +70,7 @@ enum DeviceError : uint32_t {
     kErrDecay = 2,       // GDN log-decay not finite or positive
     kErrSelection = 3,   // QSA selected-token count invalid
     kErrTimeout = 4,     // a bounded wait gave up (wait site in bits 8..15)
+    kErrRange = 5,       // an activation beyond the tensor-core projection's range (|x| >= 2^18)
 };
 
 // One quantized (or F32/BF16) matrix in HBM: `rows` consecutive GGUF rows.
@@ -87,6 +81,10 @@ enum DeviceError : uint32_t {
 //   Q6_K: [ql nsb*128][qh nsb*64][scales nsb*16][d nsb*2]
 //   Q8_0: [codes nb*32][d nb*2]
 // (Q4_K's 144-byte super-blocks are already 16-byte aligned and stay GGUF.)
+// `scale_exp`: the tensor-core projection multiplies the decoded weights by
+// 2^scale_exp (exact) before splitting them into fp16 hi/lo parts, so that
+// every value of the matrix lies inside the fp16 range, and divides the
+// result by it again (weight_scale_exponent() picks it at upload).
 struct QMatrix {
     const uint8_t *data;
     uint32_t type;
@@ -94,7 +92,16 @@ struct QMatrix {
     uint32_t cols;
     uint32_t row_bytes;
     uint32_t layout;
+    int32_t scale_exp;
 };
+
+// Power-of-two exponent e for a matrix whose decoded values are bounded by
+// |w| <= bound: bound * 2^e < 2^14, clamped to [-64, 64] (0 for a zero or
+// non-finite bound).
+int32_t weight_scale_exponent(double bound);
+// Upper bound of |decoded value| over `rows` GGUF rows of `type` blocks
+// (read from the block headers: scales, minima, codes' ranges).
+double weight_abs_bound(uint32_t type, const uint8_t *packed, uint64_t rows, uint64_t row_bytes);
 
 constexpr int kMaxSegments = 6;
 

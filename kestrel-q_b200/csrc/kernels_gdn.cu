@@ -395,6 +395,7 @@ gdn_recurrence128_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t to
 __global__ void __launch_bounds__(kRecThreads, 2)
 gdn_decode_fused_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, const float *__restrict__ proj,
                         uint32_t ldp, float *__restrict__ gated, ErrorWord err) {
+    pdl_wait();
     __shared__ __align__(16) float ks[kDim];
     __shared__ __align__(16) float qs[kDim];
     __shared__ __align__(16) float vs[kDim];
@@ -402,6 +403,7 @@ gdn_decode_fused_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, const float 
     __shared__ __align__(16) float delta[kDim];
     __shared__ float red[kRecThreads / 32];
     __shared__ float gates[2];   // beta, decay
+    if (gdn_error_raised(err)) return;
     const uint32_t h = blockIdx.x;
     const uint32_t b = blockIdx.y;
     const uint32_t kh = h / d.repeat;
@@ -413,16 +415,11 @@ gdn_decode_fused_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, const float 
     float *conv_out = p.conv_out[b];
     bool bad = false;
 
-    // State loads first, before the wait: the state was written by an
-    // earlier decode step, never by the projection this kernel follows (see
-    // pdl_wait), so the 64 KiB per CTA stream in while the projection
-    // finishes.  L2-only loads (no stale L1 line can be hit).
+    // state loads first: they are independent of the prologue
     float4 s[kRows];
 #pragma unroll
     for (int j = 0; j < kRows; ++j)
-        s[j] = __ldcg(reinterpret_cast<const float4 *>(sin_ + (size_t)(warp + 8 * j) * kDim + 4 * lane));
-    pdl_wait();
-    if (gdn_error_raised(err)) return;
+        s[j] = *reinterpret_cast<const float4 *>(sin_ + (size_t)(warp + 8 * j) * kDim + 4 * lane);
 
     // ---- prologue: threads 0..127 q (which 0) / 128..255 k (which 1)
     {

@@ -3,11 +3,17 @@
 //   y[b][n] = sum_k W[n][k] * x[b][k]      (W: GGUF blocks in HBM, x: F32)
 //
 // One CTA computes a 128 (weight rows, MMA M) x 64 (batch rows, MMA N) tile
-// of y^T with tcgen05.mma (kind::f16, BF16 operands, F32 accumulator in
+// of y^T with tcgen05.mma (kind::f16, FP16 operands, F32 accumulator in
 // TMEM).  F32 accuracy is kept with a three-term split: w = wh + wl and
-// x = xh + xl (bf16 each), y ~= wh*xh + wh*xl + wl*xh; the dropped wl*xl
-// term and the rounding of the low parts are ~2^-16 relative.  BF16
-// weights are exact in bf16 and take two terms (w*xh + w*xl).
+// x = xh + xl (fp16 each, both parts rounded to nearest, so each pair holds
+// 22 significant bits), y ~= wh*xh + wh*xl + wl*xh; the dropped wl*xl term
+// and the rounding of the low parts are ~2^-22 relative per product (a
+// bf16 split, 8 bits per part, left ~2^-16, which over K = 4096 products of
+// outputs of a few hundred exceeded a 2e-3 absolute tolerance).  fp16's
+// range is kept by exact power-of-two scales: the weights of a matrix by
+// 2^scale_exp (chosen at upload from the block headers so that every value
+// is below 2^14), the activations by 2^-2 (inputs must stay below 2^18 in
+// magnitude; larger ones raise a range error); the epilogue undoes both.
 //
 // Warp roles (608 threads, one CTA per SM):
 //   TMA warp     per K chunk of 64: 2-D TMA loads of the chunk's raw GGUF
@@ -78,6 +84,11 @@ constexpr int kTmaWarp = kDecodeWarps + 2;
 constexpr int kThreads = (kDecodeWarps + 3) * 32;
 constexpr int kAccStride = kUN + 1;       // floats per row of the split-K exchange tile
 constexpr uint32_t kTmemCols = 512;
+// Activations enter the MMA as fp16 hi/lo parts of x * kXScale (exact);
+// |x| must stay below kXRangeLimit, where x / 4 would round to fp16 infinity
+// beyond 65504.  The epilogue multiplies by 2^(2 - scale_exp).
+constexpr float kXScale = 0.25f;
+constexpr float kXRangeLimit = 262016.0f;
 
 // Geometry of a tile of NT batch rows.
 //  NT = 64: TMEM columns [0, 128) hold the accumulator: wh * [xh | xl]
@@ -196,10 +207,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_addr) {
     return d;
 }
 
-// Instruction descriptor: F32 accumulate, BF16 A and B, both K-major,
-// M = kUM, N = n.
+// Instruction descriptor: F32 accumulate (c_format 1, bits [4,6)), FP16 A
+// and B (a_format = b_format = 0, bits [7,10) and [10,13)), both K-major,
+// N >> 3 in [17,23), M >> 4 in [24,29).
 constexpr uint32_t idesc_for(uint32_t n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((n >> 3) << 17) | ((uint32_t)(kUM >> 4) << 24);
+    return (1u << 4) | ((n >> 3) << 17) | ((uint32_t)(kUM >> 4) << 24);
 }
 
 // D (TMEM) += A (TMEM, 128 lanes x 16 K) * B (shared memory descriptor).
@@ -217,28 +229,24 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
                  ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Splits an F32 value into bf16 hi (round to nearest) and bf16 lo of the
-// exact residual.  Returns (lo << 16) | hi.
-__device__ __forceinline__ uint32_t split_bf16(float v) {
-    __nv_bfloat16 hi = __float2bfloat16_rn(v);
-    float r = v - __bfloat162float(hi);
-    __nv_bfloat16 lo = __float2bfloat16_rn(r);
-    return (uint32_t)__bfloat16_as_ushort(hi) | ((uint32_t)__bfloat16_as_ushort(lo) << 16);
+// Splits two F32 values into fp16 hi = RN(w) and fp16 lo = RN(w - hi) (the
+// residual is exact in F32), packed with w0 in the low half of each word:
+// |w - hi - lo| <= 2^-22 |w| for |w| in the fp16 normal range, and at most
+// 2^-25 absolute below it.
+__device__ __forceinline__ void split_f16(float w0, float w1, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(w0, w1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(__fsub_rn(w0, hf.x), __fsub_rn(w1, hf.y));
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
 }
 
-// Packs 8 values into two 16-byte chunks (hi, lo) of bf16.
+// Packs 8 values into two 16-byte chunks (hi, lo) of fp16.
 __device__ __forceinline__ void pack8(const float *v, uint4 &hi, uint4 &lo) {
-    uint32_t s[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s[i] = split_bf16(v[i]);
-    hi.x = (s[0] & 0xFFFFu) | (s[1] << 16);
-    hi.y = (s[2] & 0xFFFFu) | (s[3] << 16);
-    hi.z = (s[4] & 0xFFFFu) | (s[5] << 16);
-    hi.w = (s[6] & 0xFFFFu) | (s[7] << 16);
-    lo.x = (s[0] >> 16) | (s[1] & 0xFFFF0000u);
-    lo.y = (s[2] >> 16) | (s[3] & 0xFFFF0000u);
-    lo.z = (s[4] >> 16) | (s[5] & 0xFFFF0000u);
-    lo.w = (s[6] >> 16) | (s[7] & 0xFFFF0000u);
+    split_f16(v[0], v[1], hi.x, lo.x);
+    split_f16(v[2], v[3], hi.y, lo.y);
+    split_f16(v[4], v[5], hi.z, lo.z);
+    split_f16(v[6], v[7], hi.w, lo.w);
 }
 
 // Byte offset of 16-byte chunk `chunk` (0..7) of row `r` in a SW128 tile.
@@ -287,19 +295,11 @@ __device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
     return r;
 }
 
-// Splits a pair into bf16 hi (rounded half away from zero by an integer
-// add on the bits) and bf16 lo = w - hi (exact in F32 by Sterbenz, then
-// truncated: |error| <= 2^-16 |w|).  The residual is taken from the rounded
-// bits, not from an FP cancellation, so no compiler contraction can remove it.
+// fp16 hi/lo split of a pair of (already scaled) decoded weights.
 __device__ __forceinline__ void split_pair(uint64_t w, uint32_t &hi, uint32_t &lo) {
     float w0, w1;
     unf2(w, w0, w1);
-    const uint32_t b0 = __float_as_uint(w0) + 0x8000u, b1 = __float_as_uint(w1) + 0x8000u;
-    hi = __byte_perm(b0, b1, 0x7632u);
-    const uint64_t l = sub2(w, f2(__uint_as_float(b0 & 0xFFFF0000u), __uint_as_float(b1 & 0xFFFF0000u)));
-    float l0, l1;
-    unf2(l, l0, l1);
-    lo = __byte_perm(__float_as_uint(l0), __float_as_uint(l1), 0x7632u);
+    split_f16(w0, w1, hi, lo);
 }
 
 // f = 0.5 + u / 256 for the byte u = byte b of w (u < 128): one PRMT builds
@@ -357,15 +357,16 @@ __device__ __forceinline__ uint32_t sw128_at(uint32_t r, uint32_t j) { return r 
 // 16-byte chunk j of row r in a TMA 64B-swizzled box of 64-byte rows.
 __device__ __forceinline__ uint32_t sw64_at(uint32_t r, uint32_t j) { return r * 64u + ((j ^ ((r >> 1) & 3u)) << 4); }
 
-// Decodes the 16 values [16q, 16q + 16) of chunk c of one staged row into
-// packed bf16 hi/lo pairs.  The decoded F32 values equal the reference
-// decoder's (src/kq_numeric.c): each is one correctly rounded FMA of exactly
-// representable operands, for example Q4_K: dl*code - ml = (256 dl) * f -
-// (128 dl + ml) with f = 0.5 + code/256.  BF16 values are their own hi part
-// and get a zero lo part (the MMA skips it).
+// Decodes the 16 values [16q, 16q + 16) of chunk c of one staged row, scaled
+// by `wscale` (the matrix's power of two), into packed fp16 hi/lo pairs.  The
+// decoded F32 values equal the reference decoder's (src/kq_numeric.c) times
+// wscale: each is one correctly rounded FMA of exactly representable
+// operands, for example Q4_K: dl*code - ml = (256 dl) * f - (128 dl + ml)
+// with f = 0.5 + code/256, and scaling both operands by a power of two
+// scales the rounded result exactly.
 template <uint32_t T>
 __device__ __forceinline__ void decode16(const uint8_t *raw, uint32_t row, uint32_t cols, uint32_t c, uint32_t q,
-                                         uint32_t (&hi)[8], uint32_t (&lo)[8]) {
+                                         float wscale, uint32_t (&hi)[8], uint32_t (&lo)[8]) {
     if constexpr (T == kTypeQ4_K) {
         // quants: nibble (q >> 1) of bytes 16*(q&1).. of the 64-group
         const uint8_t *blk = raw + row * 144u;
@@ -384,7 +385,8 @@ __device__ __forceinline__ void decode16(const uint8_t *raw, uint32_t row, uint3
             mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
         }
         const float dl = __fmul_rn(d, (float)sc), ml = __fmul_rn(dmin, (float)mn);
-        const float a = __fmul_rn(dl, 256.0f), c0 = __fadd_rn(__fmul_rn(dl, 128.0f), ml);
+        const float a = __fmul_rn(__fmul_rn(dl, 256.0f), wscale);
+        const float c0 = __fmul_rn(__fadd_rn(__fmul_rn(dl, 128.0f), ml), wscale);
         const uint64_t A = f2(a, a), C0 = f2(-c0, -c0);
         const uint32_t wq[4] = {qs.x, qs.y, qs.z, qs.w};
 #pragma unroll
@@ -404,7 +406,8 @@ __device__ __forceinline__ void decode16(const uint8_t *raw, uint32_t row, uint3
         const uint32_t dbits =
             *reinterpret_cast<const uint16_t *>(raw + 26624u + row * 16u + ((nsb * 208u + sb * 2u) & 15u));
         const float scale = __fmul_rn(h2f(dbits), (float)(int8_t)scb);
-        const float a = __fmul_rn(scale, 256.0f), c0 = __fmul_rn(scale, 160.0f);   // both exact
+        const float a = __fmul_rn(__fmul_rn(scale, 256.0f), wscale);   // all exact
+        const float c0 = __fmul_rn(__fmul_rn(scale, 160.0f), wscale);
         const uint64_t A = f2(a, a), C0 = f2(-c0, -c0);
         const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
@@ -422,7 +425,8 @@ __device__ __forceinline__ void decode16(const uint8_t *raw, uint32_t row, uint3
         const uint32_t dbits =
             *reinterpret_cast<const uint16_t *>(raw + 32768u + row * 16u + ((nb * 32u + blk * 2u) & 15u));
         const float d = h2f(dbits);
-        const float a = __fmul_rn(d, 65536.0f), c0 = __fmul_rn(d, 32896.0f);   // both exact
+        const float a = __fmul_rn(__fmul_rn(d, 65536.0f), wscale);   // all exact
+        const float c0 = __fmul_rn(__fmul_rn(d, 32896.0f), wscale);
         const uint64_t A = f2(a, a), C0 = f2(-c0, -c0);
         const uint32_t wc[4] = {cw.x ^ 0x80808080u, cw.y ^ 0x80808080u, cw.z ^ 0x80808080u, cw.w ^ 0x80808080u};
 #pragma unroll
@@ -432,13 +436,14 @@ __device__ __forceinline__ void decode16(const uint8_t *raw, uint32_t row, uint3
             split_pair(fma2(A, f2(half_plus_byte16(wc[k], 2), half_plus_byte16(wc[k], 3)), C0), hi[2 * k + 1],
                        lo[2 * k + 1]);
         }
-    } else {   // BF16: the values are the hi part, no low part
+    } else {   // BF16: each value is its bits << 16 as F32, scaled exactly
         const uint8_t *box = raw + (c & 1u) * 16384u;
         const uint4 v0 = lds16(box + sw128_at(row, 2u * q)), v1 = lds16(box + sw128_at(row, 2u * q + 1u));
-        hi[0] = v0.x; hi[1] = v0.y; hi[2] = v0.z; hi[3] = v0.w;
-        hi[4] = v1.x; hi[5] = v1.y; hi[6] = v1.z; hi[7] = v1.w;
+        const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) lo[i] = 0u;
+        for (int i = 0; i < 8; ++i)
+            split_f16(__fmul_rn(__uint_as_float(w[i] << 16), wscale),
+                      __fmul_rn(__uint_as_float(w[i] & 0xFFFF0000u), wscale), hi[i], lo[i]);
     }
 }
 
@@ -468,7 +473,7 @@ struct TmapSet {
     uint32_t box_rows[kMaxSegments];
 };
 
-// Activations to bf16 hi/lo tiles in the MMA's shared-memory image:
+// Activations x 2^-2 to fp16 hi/lo tiles in the MMA's shared-memory image:
 // out[btile][chunk] = { hi: NT rows x 128 B swizzled, lo: same }.
 // One CTA converts 16 rows of one chunk; one thread 8 values.
 template <uint32_t NT>
@@ -490,12 +495,19 @@ xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = (b < batch && k0 + i < cols) ? src[i] : 0.0f;
     }
-    // the projection's input check (non-finite input -> NUMERIC_DOMAIN)
-    bool bad = false;
+    // the projection's input check (non-finite input -> NUMERIC_DOMAIN), and
+    // the fp16 range of the scaled activations (|x| / 4 < 65504)
+    bool bad = false, big = false;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) bad |= !isfinite(v[i]);
+    for (int i = 0; i < 8; ++i) {
+        bad |= !isfinite(v[i]);
+        big |= isfinite(v[i]) && !(fabsf(v[i]) < kXRangeLimit);
+        v[i] = __fmul_rn(v[i], kXScale);
+    }
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0)
         atomicCAS(err.word, 0ull, ((unsigned long long)kErrNonFinite << 32) | err.call_id);
+    if (__any_sync(0xffffffffu, big) && (threadIdx.x & 31) == 0)
+        atomicCAS(err.word, 0ull, ((unsigned long long)kErrRange << 32) | err.call_id);
     uint4 hi, lo;
     pack8(v, hi, lo);
     uint8_t *tile = out + ((size_t)bt * nchunks + c) * Tile<NT>::xslot;
@@ -562,6 +574,10 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     int seg = 0;
     while (seg + 1 < segs.count && blockIdx.x >= segs.tile_start[seg + 1]) ++seg;
     const QMatrix m = segs.m[seg];
+    // decoded weights x 2^scale_exp, result x 2^(2 - scale_exp): exact powers
+    // of two built from their exponent bits (scale_exp is within [-64, 64])
+    const float wscale = __uint_as_float((uint32_t)(127 + m.scale_exp) << 23);
+    const float oscale = __uint_as_float((uint32_t)(127 + 2 - m.scale_exp) << 23);
     const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * kUM;
     const uint32_t b0 = blockIdx.y * NT;
     const uint32_t nchunks_total = (m.cols + kUK - 1) / kUK;
@@ -596,8 +612,7 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     const uint32_t tmem = tmem_base_slot;
 
     // The weights of the first raw slots are requested before the wait: they
-    // are uploaded by the host and never written by a kernel, so their loads
-    // overlap the previous kernel (see pdl_wait).
+    // are uploaded by the host and never written by a kernel.
     uint32_t prefetched = 0;   // raw steps already issued (producer thread)
     const CUtensorMap *maps = tmaps.map[seg];
     const uint32_t rtx = raw_tx<T>(tmaps.box_rows[seg]);
@@ -666,12 +681,12 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
                 for (uint32_t kk = 0; kk < kUK / 16; ++kk) {   // +32 bytes of K per step = +2 in the address field
                     if constexpr (NT == 64) {
                         umma_ts<2 * NT>(tmem, ah + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
-                        if constexpr (T != kTypeBF16) umma_ts<NT>(tmem, al + kk * 8u, db + 2u * kk, 1u);
+                        umma_ts<NT>(tmem, al + kk * 8u, db + 2u * kk, 1u);
                     } else {
                         const uint64_t dlo = db + (uint64_t)((kXSlot / 2) >> 4);
                         umma_ts<NT>(tmem, ah + kk * 8u, db + 2u * kk, kk == 0 ? first : 1u);
                         umma_ts<NT>(tmem, ah + kk * 8u, dlo + 2u * kk, 1u);
-                        if constexpr (T != kTypeBF16) umma_ts<NT>(tmem, al + kk * 8u, db + 2u * kk, 1u);
+                        umma_ts<NT>(tmem, al + kk * 8u, db + 2u * kk, 1u);
                     }
                 }
                 umma_commit(&mdone[xs]);
@@ -692,10 +707,10 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
             if (it >= kABufs && !mbar_wait_warp(&adone[b], ((it - kABufs) / kABufs) & 1u, &abort_flag, kSiteADone))
                 break;
             uint32_t hi[8], lo[8];
-            decode16<T>(raw_ring + rs * kRawBytes, row, m.cols, c_begin + it, q, hi, lo);
+            decode16<T>(raw_ring + rs * kRawBytes, row, m.cols, c_begin + it, q, wscale, hi, lo);
             const uint32_t ta = tmem + lane_addr + kABase + b * 64u + q * 8u;
             tmem_st8(ta, hi);
-            if constexpr (T != kTypeBF16) tmem_st8(ta + 32u, lo);
+            tmem_st8(ta + 32u, lo);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
@@ -733,7 +748,7 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const uint32_t b = b0 + col_base + g + j;
-                    const float v = __uint_as_float(r0[j]);
+                    const float v = __fmul_rn(__uint_as_float(r0[j]), oscale);
                     if (b < batch && row < m.rows) {
                         out_bad |= !isfinite(v);
                         y[(size_t)b * ldy + segs.out_offset[seg] + row] = v;
@@ -754,7 +769,8 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
         tmem_ld16(taddr + kUN, r1);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = __fadd_rn(__uint_as_float(r0[j]), __uint_as_float(r1[j]));
+        for (int j = 0; j < 16; ++j)
+            acc[j] = __fmul_rn(__fadd_rn(__uint_as_float(r0[j]), __uint_as_float(r1[j])), oscale);
     }
     const uint32_t nsplit = gridDim.z;
     if (nsplit == 1) {

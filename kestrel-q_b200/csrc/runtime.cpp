@@ -153,6 +153,7 @@ static const char *error_text(uint32_t code) {
     case kErrDecay: return "GDN log decay must be finite and non-positive";
     case kErrSelection: return "QSA selected-token count is invalid";
     case kErrTimeout: return "a tensor-core pipeline wait that timed out";
+    case kErrRange: return "a projection input is beyond the tensor-core range (|x| >= 2^18)";
     default: return "device error";
     }
 }

@@ -356,6 +356,52 @@ def test_decode_batch_rejects_non_finite_input(kq, oracle, B):
         qprov.close()
 
 
+def test_decode_batch_rejects_activation_beyond_fp16_range(kq, oracle):
+    """The tensor-core projection carries activations as fp16 hi/lo parts of
+    x / 4, so |x| must stay below 2^18: a batch (B = 40, tensor-core path)
+    with one such value fails with NUMERIC_DOMAIN naming the range, and every
+    GDN state rolls back; a value just below the limit decodes normally."""
+    import torch
+    from kqb200 import synth
+    gdims = synth.GdnDims(hidden=512, key_heads=2, value_heads=4, key_dim=128, value_dim=128)
+    _, gprov, glayer, w = _gdn_setup(kq, oracle, gdims, 24, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_Q4_K)
+    try:
+        B = 40
+        states, init = [], []
+        for b in range(B):
+            s = kq.GdnState(glayer)
+            c0, r0 = synth.gdn_state(500 + b, gdims)
+            s.load(c0, r0)
+            states.append(s)
+            init.append((c0, r0))
+        x = synth.hidden(25, B, 512)
+        x[3, 100] = 3.0e5
+        xd = torch.from_numpy(x).cuda()
+        yd = torch.empty_like(xd)
+        torch.cuda.synchronize()
+        kq.gdn_decode_batch(glayer, states, xd.data_ptr(), yd.data_ptr())
+        with pytest.raises(kq.KQError) as e:
+            kq.synchronize()
+        assert e.value.status == kq.abi.NUMERIC_DOMAIN and "range" in str(e.value)
+        for b in (0, 3, B - 1):
+            c1, r1, _ = states[b].save()
+            assert np.array_equal(bits(c1), bits(init[b][0])) and np.array_equal(bits(r1), bits(init[b][1]))
+        x[3, 100] = 2.5e5   # inside the range
+        xd.copy_(torch.from_numpy(x))
+        torch.cuda.synchronize()
+        kq.gdn_decode_batch(glayer, states, xd.data_ptr(), yd.data_ptr())
+        kq.synchronize()
+        st, yo, _, reco = oracle.gdn_run(gdims, w, x[3:4], *init[3])
+        assert st == 0
+        assert_close(yd.cpu().numpy()[3], yo, "decode with a large activation")
+        assert_close(states[3].save()[1], reco, "state after a large activation")
+        for s in states:
+            s.close()
+    finally:
+        glayer.close()
+        gprov.close()
+
+
 def test_gdn_failure_leaves_state_unchanged(kq, oracle):
     from kqb200 import synth
     dims = synth.GdnDims(hidden=256, key_heads=2, value_heads=4, key_dim=128, value_dim=128)

@@ -62,7 +62,7 @@ def test_static_linear_matches_allocating_entry(kq, oracle, type_id, rows, cols,
                 assert free1 == free0, f"free device memory changed by {free0 - free1} bytes"
             ys = y_static.cpu().numpy()
             _close(ys, y_ref.cpu().numpy(), f"type {type_id} call {call} vs allocating entry")
-            _close(ys, oracle.matvec(type_id, q, rows, cols, xn), f"type {type_id} call {call} vs oracle")
+            _close(ys, oracle.matvec(type_id, q.data, rows, cols, xn), f"type {type_id} call {call} vs oracle")
     finally:
         p.close()
 
