@@ -11,7 +11,11 @@ whole block for all 64 sequences.  Multi-GPU: one process per GPU, each rank
 serves its own 64 sequences (sequence sharding, no data-path collective;
 weak scaling).
 
-Sub-records of the same JSON line (default run; `--no-prefill` skips them):
+Sub-records of the same JSON line (default run; `--no-prefill` skips the
+prefill ones):
+  e2e_per_sequence      the decode step through the reference-shaped entry
+                        points, one sequence per call with host buffers
+  decode_b1             configs 0 and 1: batch-1 decode latency (one GPU)
   prefill_8k.gdn_layer  config 2: one GDN layer, Q6_K projections, 8192
                         tokens from a zero state (chunked WY-form recurrence)
   prefill_8k.block      the 4-layer block of config 4 on 8192 tokens
@@ -502,6 +506,53 @@ class Ctx:
             self.dist.destroy_process_group()
 
 
+class RefShaped:
+    """The reference-shaped synchronous entry points (kq_gdn_execute_quantized,
+    kq_qsa_execute_quantized: src/kq_gdn_internal.h:81-96,
+    src/kq_qsa_internal.h:94-102) called the way the reference's layer code
+    calls them (src/kq_layer.c:746-765): one sequence per call, host buffers,
+    caller-owned scratch, which this keeps allocated across calls."""
+
+    def __init__(self, cx: Ctx):
+        self.cx = cx
+        self.lib = cx.lib
+        self.abi = cx.kq.abi
+        self.buffers = {}
+
+    def _buf(self, key, floats):
+        b = self.buffers.get(key)
+        if b is None or b.size < floats:
+            b = np.empty(max(1, floats), np.float32)
+            self.buffers[key] = b
+        return b
+
+    def gdn(self, layer, state, x: np.ndarray, y: np.ndarray):
+        import ctypes as C
+        dm = layer.dims
+        scratch = self._buf(("gs", id(layer)), self.lib.kq_gdn_config_scratch_bytes(layer.handle) // 4 + 1)
+        conv = dm.conv_channels * dm.conv_kernel
+        wscratch = self._buf(("gw", id(layer)), 2 * dm.value_heads + 2 * conv + dm.value_dim + 65536 // 4 + 64)
+        d = self.abi.Diagnostic()
+        self.abi.check(self.lib.kq_gdn_execute_quantized(
+            layer.handle, layer.provider.handle, x.ctypes.data, x.shape[0], None, y.ctypes.data, y.size,
+            state.handle, scratch.ctypes.data, scratch.nbytes, wscratch.ctypes.data, wscratch.nbytes, None, None,
+            C.byref(d)), d)
+
+    def qsa(self, layer, state, x: np.ndarray, y: np.ndarray):
+        import ctypes as C
+        dm = layer.dims
+        need = C.c_uint64()
+        d = self.abi.Diagnostic()
+        self.abi.check(self.lib.kq_qsa_required_scratch_bytes(layer.handle, state.handle, x.shape[0],
+                                                               C.byref(need), C.byref(d)), d)
+        scratch = self._buf(("qs", id(layer)), need.value // 4 + 1)
+        wscratch = self._buf(("qw", id(layer)), (65536 + 8 * (dm.head_dim + dm.index_dim) * 4) // 4 + 64)
+        self.abi.check(self.lib.kq_qsa_execute_quantized(
+            layer.handle, layer.provider.handle, x.ctypes.data, x.shape[0], y.ctypes.data, y.size, state.handle,
+            scratch.ctypes.data, scratch.nbytes, wscratch.ctypes.data, wscratch.nbytes,
+            self.abi.SELECTION_OBSERVER(), None, None, C.byref(d)), d)
+
+
 def decode_record(args, cx: Ctx):
     """Config 3 decode: the headline record."""
     import ctypes as C
@@ -511,7 +562,7 @@ def decode_record(args, cx: Ctx):
     gdn_w, qsa_w = layer_weights()
     ctx = contexts(rank, ctx_max=args.ctx_max)
     B = BATCH
-    steps_total = args.warmup + 3 * args.steps + 40
+    steps_total = args.warmup + 3 * args.steps + 80
     prov = kqb200.Provider(cx.local_rank)
     gdn_layers = [kqb200.GdnLayer(gd, w, prov, layer=l) for l, w in enumerate(gdn_w)]
     qsa_layer = kqb200.QsaLayer(qd, qsa_w, prov, layer=3)
@@ -588,7 +639,27 @@ def decode_record(args, cx: Ctx):
     e2e_ms = cx.timed(args.steps, e2e_step)
     assert torch.isfinite(yh).all(), "non-finite block output"
 
-    ms, e2e_ms, rec_ms = max_over_ranks([ms, e2e_ms, rec_ms], world, cx.device)
+    # ---- end-to-end through the reference-shaped entry points, one
+    # sequence per call (the drop-in path a reference host takes)
+    rs = RefShaped(cx)
+    xs = np.random.default_rng(7).normal(size=(B, 1, gd.hidden)).astype(np.float32)
+    hs = [np.empty((1, gd.hidden), np.float32) for _ in range(GDN_LAYERS + 1)]
+
+    def per_sequence_step():
+        for b in range(B):
+            h = xs[b]
+            for l in range(GDN_LAYERS):
+                rs.gdn(gdn_layers[l], gdn_states[l][b], h, hs[l])
+                h = hs[l]
+            rs.qsa(qsa_layer, qsa_states[b], h, hs[GDN_LAYERS])
+
+    per_seq_step_ms = 0.0
+    if args.per_sequence_steps > 0:
+        per_sequence_step()
+        per_seq_step_ms = cx.timed(args.per_sequence_steps, per_sequence_step)
+        assert np.isfinite(hs[GDN_LAYERS]).all(), "non-finite per-sequence output"
+
+    ms, e2e_ms, rec_ms, per_seq_step_ms = max_over_ranks([ms, e2e_ms, rec_ms, per_seq_step_ms], world, cx.device)
     step_bytes, parts = algorithmic_bytes(gdn_w, qsa_w, ctx, B)
     hbm, peak_kind = peaks()
     rec_avg_ms = rec_ms / max(1.0, rec_n)
@@ -638,6 +709,14 @@ def decode_record(args, cx: Ctx):
         },
         "e2e": {"value": job_tokens_per_s(world, B, e2e_ms), "unit": "tok/s",
                 "h2d_bytes_per_step": B * gd.hidden * 4, "d2h_bytes_per_step": B * gd.hidden * 4},
+        **({"e2e_per_sequence": {
+            "value": job_tokens_per_s(world, B, per_seq_step_ms), "unit": "tok/s",
+            "ms_per_step": per_seq_step_ms, "steps": args.per_sequence_steps,
+            "calls_per_step": B * (GDN_LAYERS + 1),
+            "api": "kq_gdn_execute_quantized / kq_qsa_execute_quantized, one sequence per call, host "
+                   "activations, synchronous (the reference layer's calling pattern)",
+            "h2d_bytes_per_step": B * (GDN_LAYERS + 1) * gd.hidden * 4,
+            "d2h_bytes_per_step": B * (GDN_LAYERS + 1) * gd.hidden * 4}} if args.per_sequence_steps > 0 else {}),
         "gpu_launches": int(launches),
         **({"kernel_breakdown": breakdown} if breakdown else {}),
         "clocks": clocks.summary(),
@@ -652,6 +731,99 @@ def decode_record(args, cx: Ctx):
     qsa_layer.close()
     prov.close()
     return line
+
+
+def decode_b1_record(args, cx: Ctx, cpu: bool):
+    """BASELINE configs 0 and 1: one decode token at batch 1, as latency.
+    `device_ms`: the batched device entry point with one sequence (inputs in
+    HBM); `api_ms`: the reference-shaped synchronous entry point with host
+    buffers; `cpu_ms`: the reference's own operator on one host core."""
+    import ctypes as C
+    torch, kqb200 = cx.torch, cx.kq
+    from kqb200 import synth
+    gd, qd = dims()
+    hbm, peak_kind = peaks()
+    steps = args.b1_steps
+    out = {}
+    prov = kqb200.Provider(cx.local_rank)
+    rs = RefShaped(cx)
+    try:
+        # config 0: GDN, Q8_0 qkv / gate / out, F32 alpha / beta
+        gw = synth.gdn_layer(0, gd, synth.TYPE_Q8_0, synth.TYPE_Q8_0, synth.TYPE_F32)
+        layer = kqb200.GdnLayer(gd, gw, prov, layer=0)
+        st = kqb200.GdnState(layer)
+        conv0, rec0 = synth.gdn_state(1, gd)
+        st.load(conv0, rec0)
+        x = torch.from_numpy(synth.hidden(2, 1, gd.hidden)).cuda()
+        y = torch.empty_like(x)
+        torch.cuda.synchronize()
+        run = lambda: kqb200.gdn_decode_batch(layer, [st], x.data_ptr(), y.data_ptr())
+        for _ in range(args.warmup):
+            run()
+        dev_ms = cx.timed(steps, run)
+        xh, yh = synth.hidden(3, 1, gd.hidden), np.empty((1, gd.hidden), np.float32)
+        rs.gdn(layer, st, xh, yh)
+        api_ms = cx.timed(steps, lambda: rs.gdn(layer, st, xh, yh))
+        w_bytes = sum(t.nbytes for t in (gw.qkv, gw.gate, gw.beta, gw.alpha, gw.output))
+        tok_bytes = w_bytes + 2 * 4 * (gd.value_heads * gd.key_dim * gd.value_dim + gd.conv_channels * 4)
+        rec = {"workload": "config0: GDN layer decode, batch 1, Q8_0 qkv/gate/out, F32 alpha/beta, F32 state",
+               "device_ms": dev_ms, "device_tok_s": 1000.0 / dev_ms, "api_ms": api_ms,
+               "api_tok_s": 1000.0 / api_ms, "steps": steps,
+               "algorithmic_bytes_per_token": tok_bytes,
+               "hbm_frac": tok_bytes / (dev_ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind}
+        if cpu:
+            from oracle import oracle as O
+            impl = "reference" if O.ref_available() else "port"
+            wf = O.gdn_weights_f32(gw)
+            xs = synth.hidden(4, 3, gd.hidden)
+            t0 = time.perf_counter()
+            for i in range(3):
+                assert O.gdn_run(gd, wf, xs[i:i + 1], conv0, rec0, impl=impl)[0] == 0
+            rec["cpu_ms"] = (time.perf_counter() - t0) * 1000.0 / 3
+            rec["cpu_kind"] = impl
+        out["config0_gdn"] = rec
+        st.close()
+        layer.close()
+
+        # config 1: QSA, context 4096 (4095 prior positions), Q4_K q/k/v/o, BF16 index
+        qw = synth.qsa_layer(2, qd, synth.TYPE_Q4_K, synth.TYPE_Q4_K, synth.TYPE_BF16)
+        qlayer = kqb200.QsaLayer(qd, qw, prov, layer=3)
+        L = 4095
+        qs = kqb200.QsaState(qlayer, L + 2 * steps + args.warmup + 8)
+        k0, v0, r0 = synth.qsa_cache(5, qd, L)
+        qs.load(k0, v0, r0)
+        xq = torch.from_numpy(synth.hidden(6, 1, qd.hidden)).cuda()
+        yq = torch.empty_like(xq)
+        torch.cuda.synchronize()
+        run = lambda: kqb200.qsa_decode_batch(qlayer, [qs], xq.data_ptr(), yq.data_ptr())
+        for _ in range(args.warmup):
+            run()
+        dev_ms = cx.timed(steps, run)
+        xh, yh = synth.hidden(7, 1, qd.hidden), np.empty((1, qd.hidden), np.float32)
+        api_ms = cx.timed(steps, lambda: rs.qsa(qlayer, qs, xh, yh))
+        w_bytes = sum(t.nbytes for t in (qw.query, qw.key, qw.value, qw.output, qw.index_query, qw.index_key))
+        tok_bytes = w_bytes + qd.budget * 2 * qd.kv_width * 4 + (L + 1) // qd.block * qd.index_dim * 4
+        rec = {"workload": "config1: QSA layer decode, batch 1, context 4096, Q4_K q/k/v/o, BF16 index, F32 KV",
+               "device_ms": dev_ms, "device_tok_s": 1000.0 / dev_ms, "api_ms": api_ms,
+               "api_tok_s": 1000.0 / api_ms, "steps": steps,
+               "algorithmic_bytes_per_token": tok_bytes,
+               "hbm_frac": tok_bytes / (dev_ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind}
+        if cpu:
+            from oracle import oracle as O
+            impl = "reference" if O.ref_available() else "port"
+            wf = O.qsa_weights_f32(qw)
+            xs = synth.hidden(8, 3, qd.hidden)
+            t0 = time.perf_counter()
+            for i in range(3):
+                assert O.qsa_run(qd, wf, xs[i:i + 1], k0, v0, r0, L, L + 1, impl=impl)[0] == 0
+            rec["cpu_ms"] = (time.perf_counter() - t0) * 1000.0 / 3
+            rec["cpu_kind"] = impl
+        out["config1_qsa"] = rec
+        qs.close()
+        qlayer.close()
+    finally:
+        prov.close()
+    return out
 
 
 def prefill_record(args, cx: Ctx, kind: str, T: int, steps: int, warmup: int, cpu: bool):
@@ -784,6 +956,8 @@ def run_b200(args, rank, world, local_rank):
                                     "kind": "reference" if impl == "reference" else "port",
                                     "sample": f"{threads} sequences x 1 token of the 4-layer block, one sequence "
                                               f"per thread ({secs:.1f} s wall)"}
+        if world == 1 and args.b1_steps > 0:
+            line["decode_b1"] = decode_b1_record(args, cx, cpu)
         if not args.no_prefill:
             ps, pw = args.prefill_steps, args.prefill_warmup
             line["prefill_8k"] = {k: prefill_record(args, cx, k, 8192, ps, pw, cpu) for k in ("gdn_layer", "block")}
@@ -813,6 +987,9 @@ def main():
     ap.add_argument("--prefill-warmup", type=int, default=3, help="warm-up steps of each prefill sub-record")
     ap.add_argument("--slice-tokens", type=int, default=PREFILL_SLICE,
                     help="prefill tokens per layer call (all-reduce granularity)")
+    ap.add_argument("--per-sequence-steps", type=int, default=3,
+                    help="decode steps timed through the reference-shaped entry points, one sequence per call")
+    ap.add_argument("--b1-steps", type=int, default=50, help="steps of the batch-1 latency records (configs 0, 1)")
     ap.add_argument("--cpu-tokens", type=int, default=CPU_PREFILL_TOKENS,
                     help="prefill tokens of the CPU baseline sample")
     ap.add_argument("--replicated-indexer", action="store_true",

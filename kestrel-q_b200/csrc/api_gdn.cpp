@@ -233,12 +233,135 @@ static kq_status gdn_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const G
     return KQ_STATUS_OK;
 }
 
+// Checkpoint path (an observer is attached): token by token, every
+// intermediate the reference's observer sees (src/kq_gdn_qwen38.c:554-838,
+// the 21 kinds of include/kq_gdn.h) computed on the device by the debug
+// kernel, copied to the host and handed to the observer in the reference's
+// order once the token has run without a device error.  The projections are
+// the product's own.  The state keeps the call's contract: the caller's final
+// synchronize commits it, or rolls the whole call back if a token failed (the
+// observer has then seen the tokens before the failing one, as with the
+// reference).
+static kq_status gdn_debug_run(DeviceContext *c, const kq_gdn_config *cfg, const GdnResolved &w, kq_gdn_state *s,
+                               uint32_t T, const float *x, const uint8_t *mask, float *y, ErrorWord err,
+                               kq_gdn_checkpoint_observer observer, void *user, kq_diagnostic *diag) {
+    const GdnDims gd = kernel_dims(cfg);
+    const uint32_t H = gd.hidden, C = gd.conv_channels, Vd = gd.value_width, Hv = gd.value_heads;
+    const uint32_t dk = gd.key_dim, dv = gd.value_dim, K = gd.kernel;
+    const uint32_t ldp = C + Vd + 2 * Hv;
+    const size_t rk = (size_t)Hv * dk, rec_n = cfg->recurrent_elements;
+    const size_t need = Carve::round((size_t)H * 4) + Carve::round((size_t)ldp * 4) + Carve::round((size_t)C * 4) +
+                        Carve::round((size_t)C * K * 4) + 4 * Carve::round(rk * 4) + 5 * Carve::round((size_t)Vd * 4) +
+                        2 * Carve::round((size_t)Hv * 4) + 4096;
+    void *ws;
+    kq_status st = c->workspace(need, &ws, diag);
+    if (st != KQ_STATUS_OK) return st;
+    Carve cv(ws);
+    float *xm = cv.take<float>(H);
+    float *proj = cv.take<float>(ldp);
+    GdnDebugBufs b;
+    b.conv_out = cv.take<float>(C);
+    b.conv_state = cv.take<float>((size_t)C * K);
+    b.q_raw = cv.take<float>(rk);
+    b.k_raw = cv.take<float>(rk);
+    b.q_norm = cv.take<float>(rk);
+    b.k_norm = cv.take<float>(rk);
+    b.v = cv.take<float>(Vd);
+    b.read = cv.take<float>(Vd);
+    b.delta = cv.take<float>(Vd);
+    b.core = cv.take<float>(Vd);
+    b.gated = cv.take<float>(Vd);
+    b.log_decay = cv.take<float>(Hv);
+    b.beta = cv.take<float>(Hv);
+    ProjSegments in{};
+    in.count = 4;
+    in.m[0] = w.qkv; in.out_offset[0] = 0;
+    in.m[1] = w.gate; in.out_offset[1] = C;
+    in.m[2] = w.beta; in.out_offset[2] = C + Vd;
+    in.m[3] = w.alpha; in.out_offset[3] = C + Vd + Hv;
+    ProjSegments out{};
+    out.count = 1;
+    out.m[0] = w.out;
+    out.out_offset[0] = 0;
+    std::vector<float> hx(H), hp(ldp), hco(C), hcs((size_t)C * K), hqr(rk), hkr(rk), hqn(rk), hkn(rk), hv(Vd),
+        hrd(Vd), hdl(Vd), hcr(Vd), hgt(Vd), hg(Hv), hb(Hv), hst(rec_n), hy(H);
+    for (uint32_t t = 0; t < T; ++t) {
+        const float *xt = x + (size_t)t * H;
+        const float *xin = xt;
+        if (mask) {
+            launch_mask_rows(xt, mask + t, 1, H, xm, c->stream);
+            xin = xm;
+        }
+        launch_projection(in, xin, H, proj, ldp, 1, err, c->stream);
+        const int cur = s->cur;
+        launch_gdn_debug_token(gd, w.vec, s->conv[cur], s->conv[1 - cur], s->rec[cur], s->rec[1 - cur], proj, b,
+                               err, c->stream);
+        float *yt = y + (size_t)t * H;
+        if (!launch_projection(out, b.gated, Vd, yt, H, 1, err, c->stream))
+            launch_check_finite(yt, H, err, c->stream);
+        s->cur = 1 - cur;
+        s->initialized = 1;
+        s->on_step(err.call_id);
+        c->dirty.insert(s);
+        KQB_CUDA(cudaGetLastError(), diag, "GDN checkpoint launch");
+        KQB_CUDA(cudaStreamSynchronize(c->stream), diag, "GDN checkpoint sync");
+        unsigned long long word = 0;
+        KQB_CUDA(cudaMemcpy(&word, c->err_word, sizeof word, cudaMemcpyDeviceToHost), diag, "error word read");
+        if (word != 0ull) return KQ_STATUS_OK;   // reported and rolled back by the caller's synchronize
+        struct Copy { float *dst; const float *src; size_t n; } copies[] = {
+            {hx.data(), xin, H}, {hp.data(), proj, ldp}, {hco.data(), b.conv_out, C},
+            {hcs.data(), b.conv_state, (size_t)C * K}, {hqr.data(), b.q_raw, rk}, {hkr.data(), b.k_raw, rk},
+            {hv.data(), b.v, Vd}, {hqn.data(), b.q_norm, rk}, {hkn.data(), b.k_norm, rk},
+            {hg.data(), b.log_decay, Hv}, {hb.data(), b.beta, Hv}, {hrd.data(), b.read, Vd},
+            {hdl.data(), b.delta, Vd}, {hcr.data(), b.core, Vd}, {hst.data(), s->rec[s->cur], rec_n},
+            {hgt.data(), b.gated, Vd}, {hy.data(), yt, H}};
+        for (const Copy &cp : copies)
+            KQB_CUDA(cudaMemcpy(cp.dst, cp.src, cp.n * 4, cudaMemcpyDeviceToHost), diag, "checkpoint copy");
+        auto emit = [&](kq_gdn_checkpoint_kind kind, uint32_t rank, uint64_t d0, uint64_t d1, uint64_t d2,
+                        const float *v, uint64_t count) {
+            kq_gdn_checkpoint cp;
+            std::memset(&cp, 0, sizeof(cp));
+            cp.kind = kind;
+            cp.token_index = t;
+            cp.rank = rank;
+            cp.dimensions[0] = d0;
+            cp.dimensions[1] = d1;
+            cp.dimensions[2] = d2;
+            cp.values = v;
+            cp.value_count = count;
+            observer(&cp, user);
+        };
+        emit(KQ_GDN_CHECKPOINT_MASKED_INPUT, 1, H, 0, 0, hx.data(), H);
+        emit(KQ_GDN_CHECKPOINT_PROJECTED_QKV, 1, C, 0, 0, hp.data(), C);
+        emit(KQ_GDN_CHECKPOINT_PROJECTED_GATE, 2, Hv, dv, 0, hp.data() + C, Vd);
+        emit(KQ_GDN_CHECKPOINT_PROJECTED_BETA, 1, Hv, 0, 0, hp.data() + C + Vd, Hv);
+        emit(KQ_GDN_CHECKPOINT_PROJECTED_ALPHA, 1, Hv, 0, 0, hp.data() + C + Vd + Hv, Hv);
+        emit(KQ_GDN_CHECKPOINT_CONV_INPUT, 1, C, 0, 0, hp.data(), C);
+        emit(KQ_GDN_CHECKPOINT_CONV_OUTPUT, 1, C, 0, 0, hco.data(), C);
+        emit(KQ_GDN_CHECKPOINT_CONV_STATE, 2, C, K, 0, hcs.data(), (uint64_t)C * K);
+        emit(KQ_GDN_CHECKPOINT_QUERY_BEFORE_NORM, 2, Hv, dk, 0, hqr.data(), rk);
+        emit(KQ_GDN_CHECKPOINT_KEY_BEFORE_NORM, 2, Hv, dk, 0, hkr.data(), rk);
+        emit(KQ_GDN_CHECKPOINT_VALUE, 2, Hv, dv, 0, hv.data(), Vd);
+        emit(KQ_GDN_CHECKPOINT_NORMALIZED_SCALED_QUERY, 2, Hv, dk, 0, hqn.data(), rk);
+        emit(KQ_GDN_CHECKPOINT_NORMALIZED_KEY, 2, Hv, dk, 0, hkn.data(), rk);
+        emit(KQ_GDN_CHECKPOINT_LOG_DECAY, 1, Hv, 0, 0, hg.data(), Hv);
+        emit(KQ_GDN_CHECKPOINT_BETA, 1, Hv, 0, 0, hb.data(), Hv);
+        emit(KQ_GDN_CHECKPOINT_RECURRENT_READ, 2, Hv, dv, 0, hrd.data(), Vd);
+        emit(KQ_GDN_CHECKPOINT_RECURRENT_DELTA, 2, Hv, dv, 0, hdl.data(), Vd);
+        emit(KQ_GDN_CHECKPOINT_RECURRENT_OUTPUT, 2, Hv, dv, 0, hcr.data(), Vd);
+        emit(KQ_GDN_CHECKPOINT_RECURRENT_STATE, 3, Hv, dk, dv, hst.data(), rec_n);
+        emit(KQ_GDN_CHECKPOINT_GATED_NORM_OUTPUT, 2, Hv, dv, 0, hgt.data(), Vd);
+        emit(KQ_GDN_CHECKPOINT_OPERATOR_OUTPUT, 1, H, 0, 0, hy.data(), H);
+    }
+    return KQ_STATUS_OK;
+}
+
 // Host/device staging + synchronous execution shared by the F32 and the
-// provider entry points.
+// provider entry points (`observer` non-null: the checkpoint path).
 static kq_status gdn_execute_sync(const kq_gdn_config *cfg, const GdnResolved *w_in,
                                   const kq_gdn_weights_f32 *wf, const float *hidden, uint64_t T,
                                   const uint8_t *mask, float *output, kq_gdn_state *state,
-                                  kq_diagnostic *diag) {
+                                  kq_gdn_checkpoint_observer observer, void *user, kq_diagnostic *diag) {
     DeviceContext *c;
     kq_status st = context(&c, diag);
     if (st != KQ_STATUS_OK) return st;
@@ -249,30 +372,32 @@ static kq_status gdn_execute_sync(const kq_gdn_config *cfg, const GdnResolved *w
     const uint64_t n = T * H;
     ErrorWord err = c->begin_call();
 
-    // inputs on the device (separate allocation: the arena is reused by the
-    // operator itself)
-    DeviceView xview;
-    st = xview.bind(hidden, n, c->stream, diag);
+    // host inputs and the output go through the context's staging arena (no
+    // allocation once it has grown to this call's size; the operator's own
+    // work space is a separate arena)
+    const bool x_host = !is_device_pointer(hidden);
+    const bool m_host = mask != nullptr && !is_device_pointer(mask);
+    void *stage;
+    st = c->staging(Carve::round(n * 4) + (x_host ? Carve::round(n * 4) : 0) + (m_host ? Carve::round(T) : 0),
+                    &stage, diag);
     if (st != KQ_STATUS_OK) return st;
-    launch_check_finite(xview.ptr, n, err, c->stream);
-    uint8_t *dmask = nullptr;
-    float *dy = nullptr;
-    struct Free {
-        void *p[2] = {nullptr, nullptr};
-        ~Free() { for (void *q : p) if (q) cudaFree(q); }
-    } frees;
-    if (mask) {
-        KQB_CUDA(cudaMalloc(&dmask, T), diag, "mask staging");
-        frees.p[0] = dmask;
-        KQB_CUDA(cudaMemcpyAsync(dmask, mask, T, is_device_pointer(mask) ? cudaMemcpyDeviceToDevice
-                                                                         : cudaMemcpyHostToDevice,
-                                 c->stream), diag, "mask copy");
+    Carve sc(stage);
+    float *dy = sc.take<float>(n);
+    const float *dx = hidden;
+    if (x_host) {
+        float *t = sc.take<float>(n);
+        KQB_CUDA(cudaMemcpyAsync(t, hidden, n * 4, cudaMemcpyHostToDevice, c->stream), diag, "input copy");
+        dx = t;
     }
-    KQB_CUDA(cudaMalloc(&dy, n * 4), diag, "output staging");
-    frees.p[1] = dy;
+    launch_check_finite(dx, n, err, c->stream);
+    const uint8_t *dmask = mask;
+    if (m_host) {
+        uint8_t *t = sc.take<uint8_t>(T);
+        KQB_CUDA(cudaMemcpyAsync(t, mask, T, cudaMemcpyHostToDevice, c->stream), diag, "mask copy");
+        dmask = t;
+    }
 
     GdnResolved w;
-    DeviceView views[9];
     if (w_in) {
         w = *w_in;
     } else {
@@ -282,10 +407,17 @@ static kq_status gdn_execute_sync(const kq_gdn_config *cfg, const GdnResolved *w
         const uint64_t counts[9] = {wf->a_log_count, wf->conv_count, wf->dt_bias_count,
                                     wf->alpha_count, wf->beta_count, wf->qkv_count,
                                     wf->gate_count, wf->norm_count, wf->output_count};
+        // host weights: uploaded once and reused while their contents stay
+        // the same; device weights: used in place, checked on the device
+        const float *dev[9];
         for (int i = 0; i < 9; ++i) {
-            st = views[i].bind(ptrs[i], counts[i], c->stream, diag);
-            if (st != KQ_STATUS_OK) return st;
-            if (views[i].owned == nullptr) launch_check_finite(views[i].ptr, counts[i], err, c->stream);
+            if (is_device_pointer(ptrs[i])) {
+                dev[i] = ptrs[i];
+                launch_check_finite(dev[i], counts[i], err, c->stream);
+            } else {
+                st = c->upload_cached(ptrs[i], counts[i], &dev[i], diag);
+                if (st != KQ_STATUS_OK) return st;
+            }
         }
         auto dense = [](const float *p, uint32_t rows, uint32_t cols) {
             QMatrix m{};
@@ -297,18 +429,20 @@ static kq_status gdn_execute_sync(const kq_gdn_config *cfg, const GdnResolved *w
             m.layout = 0;
             return m;
         };
-        w.vec.a_log = views[0].ptr;
-        w.vec.conv = views[1].ptr;
-        w.vec.dt_bias = views[2].ptr;
-        w.alpha = dense(views[3].ptr, Hv, Hh);
-        w.beta = dense(views[4].ptr, Hv, Hh);
-        w.qkv = dense(views[5].ptr, C, Hh);
-        w.gate = dense(views[6].ptr, Vd, Hh);
-        w.vec.norm = views[7].ptr;
-        w.out = dense(views[8].ptr, Hh, Vd);
+        w.vec.a_log = dev[0];
+        w.vec.conv = dev[1];
+        w.vec.dt_bias = dev[2];
+        w.alpha = dense(dev[3], Hv, Hh);
+        w.beta = dense(dev[4], Hv, Hh);
+        w.qkv = dense(dev[5], C, Hh);
+        w.gate = dense(dev[6], Vd, Hh);
+        w.vec.norm = dev[7];
+        w.out = dense(dev[8], Hh, Vd);
     }
     kq_gdn_state *states[1] = {state};
-    st = gdn_enqueue(c, cfg, w, states, 1, (uint32_t)T, xview.ptr, dmask, dy, err, diag);
+    st = observer != nullptr
+             ? gdn_debug_run(c, cfg, w, state, (uint32_t)T, dx, dmask, dy, err, observer, user, diag)
+             : gdn_enqueue(c, cfg, w, states, 1, (uint32_t)T, dx, dmask, dy, err, diag);
     if (st != KQ_STATUS_OK) {
         c->synchronize(nullptr);
         return st;
@@ -664,16 +798,12 @@ kq_status kq_gdn_prefill_f32(const kq_gdn_config *config, const kq_gdn_weights_f
                              float *output, uint64_t output_capacity, kq_gdn_state *state, void *scratch,
                              uint64_t scratch_bytes, kq_gdn_checkpoint_observer observer, void *observer_user_data,
                              kq_diagnostic *diagnostic) {
-    (void)observer_user_data;
     kq_diagnostic_clear(diagnostic);
     kq_status st = validate_call(config, weights, hidden_states, sequence_length, padding_mask, output,
                                  output_capacity, state, scratch, scratch_bytes, false, diagnostic);
     if (st != KQ_STATUS_OK) return st;
-    if (observer != nullptr)
-        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT,
-                    "checkpoint observers are not supported by the B200 GDN path");
     return gdn_execute_sync(config, nullptr, weights, hidden_states, sequence_length, padding_mask, output,
-                            state, diagnostic);
+                            state, observer, observer_user_data, diagnostic);
 }
 
 kq_status kq_gdn_decode_f32(const kq_gdn_config *config, const kq_gdn_weights_f32 *weights,
@@ -692,7 +822,6 @@ kq_status kq_gdn_execute_quantized(const kq_gdn_config *config, kq_weight_provid
                                    void *weight_scratch, uint64_t weight_scratch_bytes,
                                    kq_gdn_checkpoint_observer observer, void *observer_user_data,
                                    kq_diagnostic *diagnostic) {
-    (void)observer_user_data;
     kq_diagnostic_clear(diagnostic);
     if (!config_valid(config))
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid compatible GDN call arguments are required");
@@ -709,11 +838,8 @@ kq_status kq_gdn_execute_quantized(const kq_gdn_config *config, kq_weight_provid
     GdnResolved w;
     if (!resolve_bound(config, &w) || config->provider != provider)
         return fail(diagnostic, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "GDN provider matrix semantic is missing");
-    if (observer != nullptr)
-        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT,
-                    "checkpoint observers are not supported by the B200 GDN path");
     return gdn_execute_sync(config, &w, nullptr, hidden_states, sequence_length, padding_mask, output, state,
-                            diagnostic);
+                            observer, observer_user_data, diagnostic);
 }
 
 kq_status kq_b200_gdn_decode_batch(const kq_gdn_config *config, kq_gdn_state *const *states, uint32_t batch,

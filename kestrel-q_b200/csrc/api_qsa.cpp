@@ -181,6 +181,13 @@ struct SelectionCopy {
     uint32_t count = 0;
 };
 
+// Device arrays of one token's checkpoint data, filled by qsa_enqueue on the
+// per-token path when the checkpoint observer is attached.
+struct QsaDebugOut {
+    const float *q = nullptr, *iq = nullptr, *gated = nullptr;
+    float *logits = nullptr, *probs = nullptr, *context = nullptr;
+};
+
 // Token sharding of the indexer in a tensor-parallel prefill: this rank
 // scores and selects only the 64-token chunks c with c % world == rank, and
 // `exchange` completes the selection rows of every chunk (a sum over ranks
@@ -208,7 +215,8 @@ struct TokenShard {
 static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const QsaResolved &w,
                              kq_qsa_state *const *states, uint32_t batch, uint32_t tokens, const float *x,
                              float *y, ErrorWord err, std::vector<SelectionCopy> *selection,
-                             kq_diagnostic *diag, bool check_input = false, const TokenShard *shard = nullptr) {
+                             kq_diagnostic *diag, bool check_input = false, const TokenShard *shard = nullptr,
+                             QsaDebugOut *debug = nullptr) {
     const QsaDims d = kernel_dims(cfg);
     const uint32_t H = d.hidden, hd = d.head_dim;
     const uint32_t qw = d.q_heads * hd, kvw = d.kv_heads * hd;
@@ -218,7 +226,7 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     // A prefill of one sequence without a selection observer runs `unit`
     // tokens per launch sequence, as entries of a uniform batch over the same
     // cache (entry i at position L + t0 + i).
-    const bool chunked = batch == 1 && tokens > 1 && selection == nullptr;
+    const bool chunked = batch == 1 && tokens > 1 && selection == nullptr && debug == nullptr;
     // two passes (index / attention) around the selection exchange
     const bool sharded = chunked && shard != nullptr && shard->world > 1;
     // sharded: the index work (index queries, scores, top-k) is owned in
@@ -257,7 +265,8 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
                         Carve::round((size_t)entries * d.topk * 4) + Carve::round((size_t)entries * 4) +
                         Carve::round((size_t)entries * d.q_heads * splits * hd * 4) +
                         Carve::round((size_t)entries * d.q_heads * splits * 2 * 4) + 8192 +
-                        (sharded ? Carve::round(items * (d.topk + 1) * 4) + Carve::round(items * qw * 4) : 0);
+                        (sharded ? Carve::round(items * (d.topk + 1) * 4) + Carve::round(items * qw * 4) : 0) +
+                        (debug ? 2 * Carve::round((size_t)d.q_heads * d.sel_capacity * 4) + Carve::round(qw * 4) : 0);
     const size_t partial_floats = std::max(projection_workspace_floats((uint32_t)items, ldp, H),
                                            projection_workspace_floats((uint32_t)items, H, qw));
     void *ws;
@@ -278,6 +287,14 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
     // sharded: every token's selection ([T][topk] then [T] counts) and query
     uint32_t *sel_all = sharded ? cv.take<uint32_t>(items * (d.topk + 1)) : nullptr;
     float *q_all = sharded ? cv.take<float>(items * qw) : nullptr;
+    if (debug) {
+        debug->logits = cv.take<float>((size_t)d.q_heads * d.sel_capacity);
+        debug->probs = cv.take<float>((size_t)d.q_heads * d.sel_capacity);
+        debug->context = cv.take<float>(qw);
+        debug->q = qv;
+        debug->iq = iqv;
+        debug->gated = gated;
+    }
 
     ProjSegments main{};
     main.count = 3;
@@ -427,10 +444,14 @@ static kq_status qsa_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const Q
             launch_qsa_prepare(d, wd, qb, gb, pt, ldp * tokens, it, ldi * tokens, qv, iqv, true, true, true, err,
                                c->stream);
             launch_qsa_score(d, qb, gb, iqv, scores, max_blocks, nb_max, false, err, c->stream);
-            launch_qsa_select(d, qb, gb, scores, max_blocks, sel, sel_count, selection != nullptr, err, c->stream);
+            launch_qsa_select(d, qb, gb, scores, max_blocks, sel, sel_count, selection != nullptr || debug != nullptr,
+                              err, c->stream);
             launch_qsa_attend(d, qb, gb, qv, sel, sel_count, part_o, part_ml, splits, err, c->stream);
             launch_qsa_combine(d, gb, part_o, part_ml, splits, pt, ldp * tokens, gated + (size_t)t * qw, err,
                                c->stream);
+            if (debug)
+                launch_qsa_debug_attention(d, qb, qv, sel, sel_count, debug->logits, debug->probs, debug->context,
+                                           err, c->stream);
             if (selection != nullptr) {
                 KQB_CUDA(cudaStreamSynchronize(c->stream), diag, "selection sync");
                 SelectionCopy sc;
@@ -556,7 +577,7 @@ static kq_status validate_call(const kq_qsa_config *config, const kq_qsa_weights
 }
 
 static void emit_selections(const kq_qsa_config *cfg, uint64_t L0, const std::vector<SelectionCopy> &sels,
-                            kq_qsa_selection_observer obs, void *user) {
+                            kq_qsa_selection_observer obs, void *user, uint64_t token0 = 0) {
     const uint32_t blk = cfg->dims.block_size;
     for (size_t t = 0; t < sels.size(); ++t) {
         const SelectionCopy &s = sels[t];
@@ -569,7 +590,7 @@ static void emit_selections(const kq_qsa_config *cfg, uint64_t L0, const std::ve
         for (uint64_t i = 0; i < tail; ++i) toks.push_back((uint32_t)(nb * blk + i));
         kq_qsa_selection sel;
         std::memset(&sel, 0, sizeof(sel));
-        sel.token_index = t;
+        sel.token_index = token0 + t;
         sel.absolute_position = pos;
         sel.candidate_block_ids = ids.data();
         sel.candidate_scores = s.scores.data();
@@ -583,9 +604,90 @@ static void emit_selections(const kq_qsa_config *cfg, uint64_t L0, const std::ve
     }
 }
 
+// Checkpoint path (a checkpoint observer is attached): one token per launch
+// sequence through the product kernels, with the selection in the reference's
+// rank order and the attention's logits, probabilities and ungated context
+// from the debug kernel; after each token the 12 checkpoints of
+// include/kq_qsa.h are copied to the host and handed to the observer in the
+// reference's order (src/kq_qsa_qwen38.c:687-815), after the token's
+// selection observer call.  A device error stops the emission; the caller's
+// final synchronize rolls the whole call back.
+static kq_status qsa_debug_run(DeviceContext *c, const kq_qsa_config *cfg, const QsaResolved &w, kq_qsa_state *s,
+                               uint32_t T, const float *x, float *y, ErrorWord err,
+                               kq_qsa_selection_observer sel_obs, kq_qsa_checkpoint_observer ck_obs, void *user,
+                               kq_diagnostic *diag) {
+    const QsaDims d = kernel_dims(cfg);
+    const uint32_t H = d.hidden, hd = d.head_dim, qw = d.q_heads * hd, kvw = d.kv_heads * hd;
+    const uint32_t di = d.index_dim, iqw = d.index_heads * di;
+    const uint32_t ld = block_key_ld((uint32_t)s->capacity, d.block);
+    std::vector<float> hiq(iqw), hraw(di), hq(qw), hk(kvw), hv(kvw), hctx(qw), hgt(qw), hy(H), hbk, hbkt,
+        hlg, hpr;
+    for (uint32_t t = 0; t < T; ++t) {
+        const uint64_t pos = s->length;
+        std::vector<SelectionCopy> sels;
+        QsaDebugOut dbg;
+        kq_qsa_state *states[1] = {s};
+        kq_status st = qsa_enqueue(c, cfg, w, states, 1, 1, x + (size_t)t * H, y + (size_t)t * H, err, &sels, diag,
+                                   false, nullptr, &dbg);
+        if (st != KQ_STATUS_OK) return st;
+        KQB_CUDA(cudaStreamSynchronize(c->stream), diag, "QSA checkpoint sync");
+        unsigned long long word = 0;
+        KQB_CUDA(cudaMemcpy(&word, c->err_word, sizeof word, cudaMemcpyDeviceToHost), diag, "error word read");
+        if (word != 0ull) return KQ_STATUS_OK;   // reported and rolled back by the caller's synchronize
+        const uint64_t nb = (pos + 1) / d.block, tail = (pos + 1) % d.block;
+        const uint64_t ntok = (uint64_t)sels[0].count * d.block + tail;
+        hbk.resize(nb * di);
+        hbkt.resize(nb * di);
+        hlg.resize((size_t)d.q_heads * ntok);
+        hpr.resize((size_t)d.q_heads * ntok);
+        struct Copy { float *dst; const float *src; size_t n; } copies[] = {
+            {hiq.data(), dbg.iq, iqw}, {hraw.data(), s->raw + pos * di, di}, {hq.data(), dbg.q, qw},
+            {hk.data(), s->key + pos * kvw, kvw}, {hv.data(), s->value + pos * kvw, kvw},
+            {hlg.data(), dbg.logits, hlg.size()}, {hpr.data(), dbg.probs, hpr.size()},
+            {hctx.data(), dbg.context, qw}, {hgt.data(), dbg.gated, qw}, {hy.data(), y + (size_t)t * H, H}};
+        for (const Copy &cp : copies)
+            if (cp.n) KQB_CUDA(cudaMemcpy(cp.dst, cp.src, cp.n * 4, cudaMemcpyDeviceToHost), diag, "checkpoint copy");
+        if (nb) {
+            // the cached block keys are feature-major [di][ld]: rows of nb, then transposed
+            KQB_CUDA(cudaMemcpy2D(hbkt.data(), nb * 4, s->block_keys, (size_t)ld * 4, nb * 4, di,
+                                  cudaMemcpyDeviceToHost), diag, "block key copy");
+            for (uint64_t b = 0; b < nb; ++b)
+                for (uint32_t f = 0; f < di; ++f) hbk[b * di + f] = hbkt[(size_t)f * nb + b];
+        }
+        if (sel_obs) emit_selections(cfg, pos, sels, sel_obs, user, t);
+        auto emit = [&](kq_qsa_checkpoint_kind kind, uint32_t rank, uint64_t d0, uint64_t d1, const float *v,
+                        uint64_t count) {
+            kq_qsa_checkpoint cp;
+            std::memset(&cp, 0, sizeof(cp));
+            cp.kind = kind;
+            cp.token_index = t;
+            cp.rank = rank;
+            cp.dimensions[0] = d0;
+            cp.dimensions[1] = d1;
+            cp.values = v;
+            cp.value_count = count;
+            ck_obs(&cp, user);
+        };
+        emit(KQ_QSA_CHECKPOINT_INDEX_QUERY, 2, d.index_heads, di, hiq.data(), iqw);
+        emit(KQ_QSA_CHECKPOINT_RAW_INDEX_KEY, 1, di, 0, hraw.data(), di);
+        emit(KQ_QSA_CHECKPOINT_BLOCK_KEYS, 2, nb, di, hbk.data(), nb * di);
+        emit(KQ_QSA_CHECKPOINT_CANDIDATE_SCORES, 1, nb, 0, sels[0].scores.data(), nb);
+        emit(KQ_QSA_CHECKPOINT_QUERY, 2, d.q_heads, hd, hq.data(), qw);
+        emit(KQ_QSA_CHECKPOINT_KEY, 2, d.kv_heads, hd, hk.data(), kvw);
+        emit(KQ_QSA_CHECKPOINT_VALUE, 2, d.kv_heads, hd, hv.data(), kvw);
+        emit(KQ_QSA_CHECKPOINT_ATTENTION_LOGITS, 2, d.q_heads, ntok, hlg.data(), hlg.size());
+        emit(KQ_QSA_CHECKPOINT_ATTENTION_PROBABILITIES, 2, d.q_heads, ntok, hpr.data(), hpr.size());
+        emit(KQ_QSA_CHECKPOINT_HEAD_CONTEXT, 2, d.q_heads, hd, hctx.data(), qw);
+        emit(KQ_QSA_CHECKPOINT_GATED_CONTEXT, 2, d.q_heads, hd, hgt.data(), qw);
+        emit(KQ_QSA_CHECKPOINT_OPERATOR_OUTPUT, 1, H, 0, hy.data(), H);
+    }
+    return KQ_STATUS_OK;
+}
+
 static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w_in, const kq_qsa_weights_f32 *wf,
                                   const float *hidden, uint64_t T, float *output, kq_qsa_state *state,
-                                  kq_qsa_selection_observer sel_obs, void *user, kq_diagnostic *diag) {
+                                  kq_qsa_selection_observer sel_obs, kq_qsa_checkpoint_observer ck_obs, void *user,
+                                  kq_diagnostic *diag) {
     DeviceContext *c;
     kq_status st = context(&c, diag);
     if (st != KQ_STATUS_OK) return st;
@@ -595,16 +697,23 @@ static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w
     const uint32_t H = cfg->dims.hidden_size;
     const uint64_t n = T * H;
     ErrorWord err = c->begin_call();
-    DeviceView xview;
-    st = xview.bind(hidden, n, c->stream, diag);
+    // host input and the output go through the context's staging arena (no
+    // allocation once it has grown to this call's size)
+    const bool x_host = !is_device_pointer(hidden);
+    void *stage;
+    st = c->staging(Carve::round(n * 4) + (x_host ? Carve::round(n * 4) : 0), &stage, diag);
     if (st != KQ_STATUS_OK) return st;
-    launch_check_finite(xview.ptr, n, err, c->stream);
-    float *dy = nullptr;
-    KQB_CUDA(cudaMalloc(&dy, n * 4), diag, "output staging");
-    struct Free { void *p; ~Free() { if (p) cudaFree(p); } } fy{dy};
+    Carve sc(stage);
+    float *dy = sc.take<float>(n);
+    const float *dx = hidden;
+    if (x_host) {
+        float *t = sc.take<float>(n);
+        KQB_CUDA(cudaMemcpyAsync(t, hidden, n * 4, cudaMemcpyHostToDevice, c->stream), diag, "input copy");
+        dx = t;
+    }
+    launch_check_finite(dx, n, err, c->stream);
 
     QsaResolved w;
-    DeviceView views[10];
     if (w_in) {
         w = *w_in;
     } else {
@@ -615,10 +724,17 @@ static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w
         const uint64_t counts[10] = {wf->query_count, wf->key_count, wf->value_count, wf->output_count,
                                      wf->query_norm_count, wf->key_norm_count, wf->index_query_count,
                                      wf->index_key_count, wf->index_query_norm_count, wf->index_key_norm_count};
+        // host weights: uploaded once and reused while their contents stay
+        // the same; device weights: used in place, checked on the device
+        const float *dev[10];
         for (int i = 0; i < 10; ++i) {
-            st = views[i].bind(ptrs[i], counts[i], c->stream, diag);
-            if (st != KQ_STATUS_OK) return st;
-            if (views[i].owned == nullptr) launch_check_finite(views[i].ptr, counts[i], err, c->stream);
+            if (is_device_pointer(ptrs[i])) {
+                dev[i] = ptrs[i];
+                launch_check_finite(dev[i], counts[i], err, c->stream);
+            } else {
+                st = c->upload_cached(ptrs[i], counts[i], &dev[i], diag);
+                if (st != KQ_STATUS_OK) return st;
+            }
         }
         auto dense = [](const float *p, uint32_t rows, uint32_t cols) {
             QMatrix m{};
@@ -630,16 +746,16 @@ static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w
             m.layout = 0;
             return m;
         };
-        w.q = dense(views[0].ptr, 2 * qw, H);
-        w.k = dense(views[1].ptr, kvw, H);
-        w.v = dense(views[2].ptr, kvw, H);
-        w.o = dense(views[3].ptr, H, qw);
-        w.q_norm = views[4].ptr;
-        w.k_norm = views[5].ptr;
-        w.iq = dense(views[6].ptr, d.index_query_head_count * d.index_head_dimension, H);
-        w.ik = dense(views[7].ptr, d.index_head_dimension, H);
-        w.iq_norm = views[8].ptr;
-        w.ik_norm = views[9].ptr;
+        w.q = dense(dev[0], 2 * qw, H);
+        w.k = dense(dev[1], kvw, H);
+        w.v = dense(dev[2], kvw, H);
+        w.o = dense(dev[3], H, qw);
+        w.q_norm = dev[4];
+        w.k_norm = dev[5];
+        w.iq = dense(dev[6], d.index_query_head_count * d.index_head_dimension, H);
+        w.ik = dense(dev[7], d.index_head_dimension, H);
+        w.iq_norm = dev[8];
+        w.ik_norm = dev[9];
     }
     {
         std::vector<float> norm(cfg->dims.index_head_dimension);
@@ -652,7 +768,9 @@ static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w
     const uint64_t L0 = state->length;
     std::vector<SelectionCopy> sels;
     kq_qsa_state *states[1] = {state};
-    st = qsa_enqueue(c, cfg, w, states, 1, (uint32_t)T, xview.ptr, dy, err, sel_obs ? &sels : nullptr, diag);
+    st = ck_obs != nullptr
+             ? qsa_debug_run(c, cfg, w, state, (uint32_t)T, dx, dy, err, sel_obs, ck_obs, user, diag)
+             : qsa_enqueue(c, cfg, w, states, 1, (uint32_t)T, dx, dy, err, sel_obs ? &sels : nullptr, diag);
     if (st != KQ_STATUS_OK) {
         c->synchronize(nullptr);
         return st;
@@ -662,7 +780,7 @@ static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w
     KQB_CUDA(cudaMemcpy(output, dy, n * 4,
                         is_device_pointer(output) ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost),
              diag, "output copy");
-    if (sel_obs) emit_selections(cfg, L0, sels, sel_obs, user);
+    if (sel_obs && ck_obs == nullptr) emit_selections(cfg, L0, sels, sel_obs, user);
     return KQ_STATUS_OK;
 }
 
@@ -1011,11 +1129,8 @@ kq_status kq_qsa_prefill_f32(const kq_qsa_config *config, const kq_qsa_weights_f
     kq_status st = validate_call(config, weights, hidden_states, sequence_length, output, output_capacity, state,
                                  scratch, scratch_bytes, false, diagnostic);
     if (st != KQ_STATUS_OK) return st;
-    if (checkpoint_observer != nullptr)
-        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT,
-                    "checkpoint observers are not supported by the B200 QSA path");
     return qsa_execute_sync(config, nullptr, weights, hidden_states, sequence_length, output, state,
-                            selection_observer, observer_user_data, diagnostic);
+                            selection_observer, checkpoint_observer, observer_user_data, diagnostic);
 }
 
 kq_status kq_qsa_decode_f32(const kq_qsa_config *config, const kq_qsa_weights_f32 *weights,
@@ -1048,13 +1163,10 @@ kq_status kq_qsa_execute_quantized(const kq_qsa_config *config, kq_weight_provid
     if (st != KQ_STATUS_OK) return st;
     if (!config->bound || config->provider != provider)
         return fail(diagnostic, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "required QSA semantic tensor is missing");
-    if (checkpoint_observer != nullptr)
-        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT,
-                    "checkpoint observers are not supported by the B200 QSA path");
     QsaResolved w{config->q, config->k, config->v, config->o, config->iq, config->ik,
                   config->q_norm, config->k_norm, config->iq_norm, config->ik_norm};
     return qsa_execute_sync(config, &w, nullptr, hidden_states, sequence_length, output, state, selection_observer,
-                            observer_user_data, diagnostic);
+                            checkpoint_observer, observer_user_data, diagnostic);
 }
 
 kq_status kq_b200_qsa_decode_batch(const kq_qsa_config *config, kq_qsa_state *const *states, uint32_t batch,

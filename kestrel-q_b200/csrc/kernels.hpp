@@ -203,6 +203,23 @@ bool gdn_decode_fused_supported(const GdnDims &d);
 void launch_gdn_decode_fused(const GdnDims &d, const GdnWeightsDev &w, const GdnBatchPtrs &p, uint32_t batch,
                              const float *proj, uint32_t ldp, float *gated, ErrorWord err, cudaStream_t stream);
 
+// Checkpoint path (an observer is attached): one token of one sequence with
+// every intermediate the reference's observer sees kept in device arrays.
+// The recurrent and conv states go from *_in to *_out as in the other paths.
+struct GdnDebugBufs {
+    float *conv_out;              // [C]     SiLU(conv)
+    float *conv_state;            // [C][K]  history after this token's shift
+    float *q_raw, *k_raw;         // [Hv][dk] before the L2 norm (key heads repeated)
+    float *v;                     // [Hv][dv]
+    float *q_norm, *k_norm;       // [Hv][dk] normalised (q also scaled by 1/sqrt(dk))
+    float *log_decay, *beta;      // [Hv]
+    float *read, *delta, *core;   // [Hv][dv] recurrence read, delta and output
+    float *gated;                 // [Hv][dv] gated RMSNorm output
+};
+void launch_gdn_debug_token(const GdnDims &d, const GdnWeightsDev &w, const float *conv_in, float *conv_out,
+                            const float *rec_in, float *rec_out, const float *proj, const GdnDebugBufs &b,
+                            ErrorWord err, cudaStream_t stream);
+
 // Chunked (WY-form) prefill of one sequence (kernels_gdn_chunk.cu), for
 // dk = dv = 128: same inputs as the recurrence plus the log decays; `work`
 // holds gdn_chunk_workspace_floats(d, tokens) floats.
@@ -308,6 +325,14 @@ void launch_qsa_combine(const QsaDims &d, uint32_t batch,
                         const float *partial_o, const float *partial_ml,
                         uint32_t splits, const float *proj, uint32_t ldp,
                         float *gated, ErrorWord err, cudaStream_t stream);
+// Checkpoint path: the attention of entry 0 of `b` (one token) for every
+// query head over its selected tokens in the reference's rank order (the
+// selection written with rank_order), with the logits [Hq][ntok], the
+// probabilities [Hq][ntok] and the ungated context [Hq][d] written out
+// (ntok = selected blocks x block + the tail; rows packed with that stride).
+void launch_qsa_debug_attention(const QsaDims &d, const QsaBatch &b, const float *q, const uint32_t *selected,
+                                const uint32_t *selected_count, float *logits, float *probs, float *context,
+                                ErrorWord err, cudaStream_t stream);
 // True when the attention runs on the tensor cores (head_dim 256, at most 8
 // query heads per KV head), which reads the bf16 hi / lo copies of the
 // cache rows; the state then keeps them.

@@ -525,6 +525,147 @@ gdn_decode_fused_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, const float 
     if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
 }
 
+// ------------------------------------------------------------ checkpoint path
+//
+// One token, grid (Hv), 128 threads, dynamic shared memory of 2 dk + 2 dv
+// floats.  The arithmetic follows the reference's scalar loop step by step
+// (src/kq_gdn_qwen38.c:602-815): products and sums separately rounded, the
+// dot products, L2 sums and RMS sum taken sequentially by one thread, the
+// recurrence one value feature per thread over the key features in order.
+// Every intermediate the reference's observer sees is written out.
+__global__ void __launch_bounds__(128)
+gdn_debug_token_kernel(GdnDims d, GdnWeightsDev w, const float *__restrict__ conv_in, float *__restrict__ conv_out,
+                       const float *__restrict__ rec_in, float *__restrict__ rec_out, const float *__restrict__ proj,
+                       GdnDebugBufs o, ErrorWord err) {
+    pdl_wait();
+    extern __shared__ float dsm[];
+    __shared__ float gates[2];   // beta, exp(g)
+    __shared__ float inv[2];     // q / k inverse norms, then the RMS inverse
+    if (gdn_error_raised(err)) return;
+    const uint32_t dk = d.key_dim, dv = d.value_dim, K = d.kernel;
+    float *sq = dsm, *sk = sq + dk, *sv = sk + dk, *sc = sv + dv;
+    const uint32_t h = blockIdx.x, kh = h / d.repeat;
+    const bool writer = (h % d.repeat) == 0;   // the key head's q / k channels are written once
+    bool bad = false;
+    // conv history shift (hist[j] = old hist[j + 1], hist[K-1] = projection),
+    // taps dot, SiLU = x * sigmoid(x) (:602-621)
+    auto conv = [&](uint32_t c, bool write) -> float {
+        float s = 0.0f;
+        for (uint32_t j = 0; j < K; ++j) {
+            const float hv = j + 1 < K ? conv_in[(size_t)c * K + j + 1] : proj[c];
+            s = __fadd_rn(s, __fmul_rn(w.conv[(size_t)c * K + j], hv));
+            if (write) {
+                conv_out[(size_t)c * K + j] = hv;
+                o.conv_state[(size_t)c * K + j] = hv;
+            }
+        }
+        return __fmul_rn(s, stable_sigmoid(s));
+    };
+    for (uint32_t i = threadIdx.x; i < dk; i += blockDim.x) {
+        const uint32_t cq = kh * dk + i, ck = d.key_width + kh * dk + i;
+        const float q = conv(cq, writer), k = conv(ck, writer);
+        if (writer) {
+            o.conv_out[cq] = q;
+            o.conv_out[ck] = k;
+        }
+        o.q_raw[(size_t)h * dk + i] = q;
+        o.k_raw[(size_t)h * dk + i] = k;
+        sq[i] = q;
+        sk[i] = k;
+        bad |= !isfinite(q) || !isfinite(k);
+    }
+    for (uint32_t i = threadIdx.x; i < dv; i += blockDim.x) {
+        const uint32_t cv = 2 * d.key_width + h * dv + i;
+        const float v = conv(cv, true);
+        o.conv_out[cv] = v;
+        o.v[(size_t)h * dv + i] = v;
+        sv[i] = v;
+        bad |= !isfinite(v);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // beta, log decay (:662-678), L2 sums (:338-360)
+        const float pb = proj[d.conv_channels + d.value_width + h];
+        const float pa = proj[d.conv_channels + d.value_width + d.value_heads + h];
+        const float bt = stable_sigmoid(pb);
+        const float a = __fadd_rn(pa, w.dt_bias[h]);
+        const float sp = a > 20.0f ? a : log1pf(expf(a));
+        const float g = __fmul_rn(-expf(w.a_log[h]), sp);
+        if (!isfinite(a) || !isfinite(sp) || !isfinite(g) || g > 0.0f) gdn_raise(err, kErrDecay);
+        o.log_decay[h] = g;
+        o.beta[h] = bt;
+        gates[0] = bt;
+        gates[1] = expf(g);
+        float s = 0.0f;
+        for (uint32_t i = 0; i < dk; ++i) s = __fadd_rn(s, __fmul_rn(sq[i], sq[i]));
+        inv[0] = 1.0f / sqrtf(__fadd_rn(s, 1.0e-6f));
+        s = 0.0f;
+        for (uint32_t i = 0; i < dk; ++i) s = __fadd_rn(s, __fmul_rn(sk[i], sk[i]));
+        inv[1] = 1.0f / sqrtf(__fadd_rn(s, 1.0e-6f));
+    }
+    __syncthreads();
+    const float qscale = 1.0f / sqrtf((float)dk);
+    for (uint32_t i = threadIdx.x; i < dk; i += blockDim.x) {
+        const float qn = __fmul_rn(__fmul_rn(sq[i], inv[0]), qscale);
+        const float kn = __fmul_rn(sk[i], inv[1]);
+        o.q_norm[(size_t)h * dk + i] = qn;
+        o.k_norm[(size_t)h * dk + i] = kn;
+        sq[i] = qn;
+        sk[i] = kn;
+    }
+    __syncthreads();
+    // delta rule (:705-761): S *= exp(g); read = S^T k; delta = (v - read) beta;
+    // S += k delta^T; out = S^T q
+    const float bt = gates[0], dec = gates[1];
+    const float *S0 = rec_in + (size_t)h * dk * dv;
+    float *S1 = rec_out + (size_t)h * dk * dv;
+    for (uint32_t f = threadIdx.x; f < dv; f += blockDim.x) {
+        float rd = 0.0f;
+        for (uint32_t kf = 0; kf < dk; ++kf) {
+            const float s = __fmul_rn(S0[(size_t)kf * dv + f], dec);
+            S1[(size_t)kf * dv + f] = s;
+            rd = __fadd_rn(rd, __fmul_rn(s, sk[kf]));
+        }
+        const float dl = __fmul_rn(__fsub_rn(sv[f], rd), bt);
+        float co = 0.0f;
+        for (uint32_t kf = 0; kf < dk; ++kf) {
+            const float s = __fadd_rn(S1[(size_t)kf * dv + f], __fmul_rn(sk[kf], dl));
+            S1[(size_t)kf * dv + f] = s;
+            bad |= !isfinite(s);
+            co = __fadd_rn(co, __fmul_rn(s, sq[kf]));
+        }
+        o.read[(size_t)h * dv + f] = rd;
+        o.delta[(size_t)h * dv + f] = dl;
+        o.core[(size_t)h * dv + f] = co;
+        sc[f] = co;
+        bad |= !isfinite(co);
+    }
+    __syncthreads();
+    // gated RMSNorm, norm weight applied directly (:787-815)
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (uint32_t f = 0; f < dv; ++f) s = __fadd_rn(s, __fmul_rn(sc[f], sc[f]));
+        inv[0] = 1.0f / sqrtf(__fadd_rn(s / (float)dv, d.eps));
+    }
+    __syncthreads();
+    for (uint32_t f = threadIdx.x; f < dv; f += blockDim.x) {
+        const float z = proj[d.conv_channels + h * dv + f];
+        const float g = __fmul_rn(__fmul_rn(w.norm[f], __fmul_rn(sc[f], inv[0])), stable_sigmoid(z));
+        o.gated[(size_t)h * dv + f] = g;
+        bad |= !isfinite(g);
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
+}
+
+void launch_gdn_debug_token(const GdnDims &d, const GdnWeightsDev &w, const float *conv_in, float *conv_out,
+                            const float *rec_in, float *rec_out, const float *proj, const GdnDebugBufs &b,
+                            ErrorWord err, cudaStream_t stream) {
+    const size_t smem = (size_t)(2 * d.key_dim + 2 * d.value_dim) * sizeof(float);
+    launch_pdl(gdn_debug_token_kernel, dim3(d.value_heads), 128, smem, stream, d, w, conv_in, conv_out, rec_in,
+               rec_out, proj, b, err);
+    count_launch();
+}
+
 bool gdn_decode_fused_supported(const GdnDims &d) {
     return d.key_dim == kDim && d.value_dim == kDim && d.kernel == 4;
 }

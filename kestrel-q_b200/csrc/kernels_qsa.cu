@@ -1679,6 +1679,89 @@ qsa_attend_tc_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const 
     }
 }
 
+// ------------------------------------------------------------ checkpoint path
+//
+// grid (Hq), 256 threads; dynamic shared memory: the token list and the
+// logits of one head (selected-token capacity each).  The reference's order
+// (src/kq_qsa_qwen38.c:716-773): dots over the features in order divided by
+// sqrt(d), the maximum, exp(logit - max) summed in token order by one
+// thread, the division, then each feature's context summed in token order.
+__global__ void __launch_bounds__(256)
+qsa_debug_attention_kernel(QsaDims d, QsaBatch bt, const float *__restrict__ q, const uint32_t *__restrict__ selected,
+                           const uint32_t *__restrict__ selected_count, float *__restrict__ logits,
+                           float *__restrict__ probs, float *__restrict__ context, ErrorWord err) {
+    pdl_wait();
+    extern __shared__ float dbg_sm[];
+    __shared__ float red[8];
+    __shared__ float sum_s;
+    if (qsa_error_raised(err)) return;
+    const QsaSeq s = batch_seq(bt, 0);
+    const uint32_t pos = s.length, h = blockIdx.x, hd = d.head_dim;
+    const uint32_t kvh = h / d.repeat, kvw = d.kv_heads * hd;
+    const uint32_t nblocks = (pos + 1) / d.block, tail = (pos + 1) % d.block;
+    const uint32_t ksel = min(selected_count[0], min(nblocks, d.topk));
+    const uint32_t ntok = ksel * d.block + tail;
+    uint32_t *tok = reinterpret_cast<uint32_t *>(dbg_sm);
+    float *lg = dbg_sm + d.sel_capacity;
+    for (uint32_t i = threadIdx.x; i < ntok; i += blockDim.x)
+        tok[i] = i < ksel * d.block ? selected[i / d.block] * d.block + i % d.block : nblocks * d.block + (i - ksel * d.block);
+    __syncthreads();
+    const float *qh = q + (size_t)h * hd;
+    float mx = -INFINITY;
+    for (uint32_t i = threadIdx.x; i < ntok; i += blockDim.x) {
+        const float *kr = s.key + (size_t)tok[i] * kvw + kvh * hd;
+        float dot = 0.0f;
+        for (uint32_t f = 0; f < hd; ++f) dot = __fadd_rn(dot, __fmul_rn(qh[f], kr[f]));
+        dot = __fdiv_rn(dot, d.sqrt_head_dim);
+        lg[i] = dot;
+        logits[(size_t)h * ntok + i] = dot;
+        mx = fmaxf(mx, dot);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float m = red[0];
+        for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+        float sum = 0.0f;
+        for (uint32_t i = 0; i < ntok; ++i) {
+            const float p = expf(__fsub_rn(lg[i], m));
+            lg[i] = p;
+            sum = __fadd_rn(sum, p);
+        }
+        if (!(sum > 0.0f) || !isfinite(sum)) qsa_raise(err, kErrNonFinite);
+        sum_s = sum;
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < ntok; i += blockDim.x) {
+        const float p = __fdiv_rn(lg[i], sum_s);
+        probs[(size_t)h * ntok + i] = p;
+    }
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < ntok; i += blockDim.x) lg[i] = __fdiv_rn(lg[i], sum_s);
+    __syncthreads();
+    for (uint32_t f = threadIdx.x; f < hd; f += blockDim.x) {
+        float acc = 0.0f;
+        for (uint32_t i = 0; i < ntok; ++i)
+            acc = __fadd_rn(acc, __fmul_rn(lg[i], s.value[(size_t)tok[i] * kvw + kvh * hd + f]));
+        context[(size_t)h * hd + f] = acc;
+    }
+}
+
+void launch_qsa_debug_attention(const QsaDims &d, const QsaBatch &b, const float *q, const uint32_t *selected,
+                                const uint32_t *selected_count, float *logits, float *probs, float *context,
+                                ErrorWord err, cudaStream_t stream) {
+    const size_t smem = (size_t)2 * d.sel_capacity * sizeof(float);
+    static DeviceOnce attr;
+    attr.run([&] {
+        cudaFuncSetAttribute(qsa_debug_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    });
+    launch_pdl(qsa_debug_attention_kernel, dim3(d.q_heads), 256, smem, stream, d, b, q, selected, selected_count,
+               logits, probs, context, err);
+    count_launch();
+}
+
 void launch_qsa_attend(const QsaDims &d, const QsaBatch &b, uint32_t batch,
                        const float *q, const uint32_t *selected,
                        const uint32_t *selected_count, float *partial_o,

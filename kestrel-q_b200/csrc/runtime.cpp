@@ -184,20 +184,74 @@ kq_status DeviceContext::synchronize(kq_diagnostic *d) {
     return KQ_STATUS_OK;
 }
 
-DeviceView::~DeviceView() {
-    if (owned) cudaFree(owned);
+kq_status DeviceContext::staging(size_t bytes, void **out, kq_diagnostic *d) {
+    if (bytes > stage_bytes) {
+        KQB_CUDA(cudaStreamSynchronize(stream), d, "staging growth sync");
+        if (stage_arena) cudaFree(stage_arena);
+        stage_arena = nullptr;
+        stage_bytes = 0;
+        const size_t want = bytes + bytes / 4 + (1u << 20);
+        KQB_CUDA(cudaMalloc(&stage_arena, want), d, "staging allocation");
+        stage_bytes = want;
+    }
+    *out = stage_arena;
+    return KQ_STATUS_OK;
 }
 
-kq_status DeviceView::bind(const float *src, uint64_t count, cudaStream_t s, kq_diagnostic *d) {
-    if (src == nullptr || count == 0) return fail(d, KQ_STATUS_INVALID_ARGUMENT, "array is required");
-    if (is_device_pointer(src)) {
-        ptr = src;
-        return KQ_STATUS_OK;
+uint64_t hash_bytes(const void *p, size_t bytes) {
+    const uint8_t *b = static_cast<const uint8_t *>(p);
+    uint64_t h = 0x243F6A8885A308D3ull ^ bytes;
+    size_t i = 0;
+    for (; i + 8 <= bytes; i += 8) {
+        uint64_t w;
+        std::memcpy(&w, b + i, 8);
+        h = (h ^ w) * 0x9E3779B97F4A7C15ull;
+        h ^= h >> 29;
     }
-    KQB_CUDA(cudaMalloc(&owned, count * sizeof(float)), d, "staging allocation");
-    KQB_CUDA(cudaMemcpyAsync(owned, src, count * sizeof(float), cudaMemcpyHostToDevice, s), d,
-             "host to device copy");
-    ptr = static_cast<const float *>(owned);
+    for (; i < bytes; ++i) h = (h ^ b[i]) * 0x100000001B3ull;
+    return h ^ (h >> 32);
+}
+
+kq_status DeviceContext::upload_cached(const float *host, uint64_t count, const float **out, kq_diagnostic *d) {
+    const size_t bytes = count * sizeof(float);
+    const uint64_t h = hash_bytes(host, bytes);
+    ++upload_clock;
+    for (auto &u : uploads) {
+        if (u.host == host && u.count == count) {
+            if (u.hash != h) {
+                // same array, new contents: refresh the device copy in place
+                KQB_CUDA(copy_sync(u.dev, host, bytes, cudaMemcpyHostToDevice, stream), d, "weight upload");
+                u.hash = h;
+            }
+            u.last_use = upload_clock;
+            *out = u.dev;
+            return KQ_STATUS_OK;
+        }
+    }
+    // make room: least recently used arrays leave first
+    while (!uploads.empty() && upload_bytes + bytes > kUploadCacheBytes) {
+        size_t oldest = 0;
+        for (size_t i = 1; i < uploads.size(); ++i)
+            if (uploads[i].last_use < uploads[oldest].last_use) oldest = i;
+        KQB_CUDA(cudaStreamSynchronize(stream), d, "upload cache eviction sync");
+        cudaFree(uploads[oldest].dev);
+        upload_bytes -= uploads[oldest].count * sizeof(float);
+        uploads.erase(uploads.begin() + (std::ptrdiff_t)oldest);
+    }
+    CachedUpload u;
+    u.host = host;
+    u.count = count;
+    u.hash = h;
+    u.last_use = upload_clock;
+    KQB_CUDA(cudaMalloc(&u.dev, bytes), d, "weight upload allocation");
+    const cudaError_t e = copy_sync(u.dev, host, bytes, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) {
+        cudaFree(u.dev);
+        return cuda_fail(d, e, "weight upload");
+    }
+    uploads.push_back(u);
+    upload_bytes += bytes;
+    *out = u.dev;
     return KQ_STATUS_OK;
 }
 

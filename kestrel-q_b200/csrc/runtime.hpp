@@ -56,6 +56,17 @@ struct Rollbackable {
     virtual void on_success() = 0;
 };
 
+// A host F32 array uploaded by a synchronous entry point and kept on the
+// device for later calls with the same array (same address, length and
+// contents, checked by a hash of the bytes on every call).
+struct CachedUpload {
+    const float *host = nullptr;
+    uint64_t count = 0;
+    uint64_t hash = 0;
+    float *dev = nullptr;
+    uint64_t last_use = 0;
+};
+
 struct DeviceContext {
     int device = 0;
     cudaStream_t own_stream = nullptr;
@@ -65,12 +76,25 @@ struct DeviceContext {
     uint32_t next_call = 1;
     void *arena = nullptr;
     size_t arena_bytes = 0;
+    void *stage_arena = nullptr;
+    size_t stage_bytes = 0;
+    std::vector<CachedUpload> uploads;
+    size_t upload_bytes = 0;
+    uint64_t upload_clock = 0;
     std::recursive_mutex mu;
     std::unordered_set<Rollbackable *> dirty;
 
     ErrorWord begin_call();
     // grow-only device workspace (synchronises when it has to grow)
     kq_status workspace(size_t bytes, void **out, kq_diagnostic *d);
+    // grow-only device staging for the synchronous entry points' host inputs
+    // and outputs, separate from the operators' workspace (synchronises when
+    // it has to grow; a call of a size seen before allocates nothing)
+    kq_status staging(size_t bytes, void **out, kq_diagnostic *d);
+    // device copy of the host F32 array [count], uploaded only when the
+    // array is new or its contents changed since the last call; the cache
+    // keeps up to kUploadCacheBytes, least recently used first out
+    kq_status upload_cached(const float *host, uint64_t count, const float **out, kq_diagnostic *d);
     // waits for the stream and resolves errors of the calls since the last
     // synchronize (rolling back dirty objects on failure)
     kq_status synchronize(kq_diagnostic *d);
@@ -97,13 +121,11 @@ struct Carve {
     static size_t round(size_t bytes) { return (bytes + 255) & ~size_t(255); }
 };
 
-// Host- or device-resident F32 array made available on the device for the
-// duration of one call (uploads host memory into a temporary device buffer).
-struct DeviceView {
-    const float *ptr = nullptr;
-    void *owned = nullptr;
-    ~DeviceView();
-    kq_status bind(const float *src, uint64_t count, cudaStream_t s, kq_diagnostic *d);
-};
+// Bytes of uploaded F32 weight arrays a device context keeps for the
+// synchronous F32 entry points.
+constexpr size_t kUploadCacheBytes = size_t(8) << 30;
+
+// 64-bit hash of a byte range (multiply-xorshift over 8-byte words).
+uint64_t hash_bytes(const void *p, size_t bytes);
 
 }  // namespace kqb

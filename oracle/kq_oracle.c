@@ -255,10 +255,31 @@ static float kqo_sigmoid(float x) {
 
 /* ------------------------------------------------------------------- GDN */
 
-/* Per-token loop of src/kq_gdn_qwen38.c:545-842 over F32 weights. */
+/* One checkpoint to the callback (src/kq_gdn_qwen38.c:248-271). */
+static void kqo_emit(kqo_checkpoint_fn cb, void *user, uint32_t kind, uint64_t token, uint32_t rank,
+                     uint64_t d0, uint64_t d1, uint64_t d2, const float *values, uint64_t count) {
+    uint64_t dims[4];
+    if (cb == NULL) return;
+    dims[0] = d0;
+    dims[1] = d1;
+    dims[2] = d2;
+    dims[3] = 0;
+    cb(kind, token, rank, dims, values, count, user);
+}
+
 int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
                 const float *hidden, uint64_t tokens, const uint8_t *mask,
                 float *output, float *conv_state, float *recurrent_state) {
+    return kqo_gdn_run_observed(dm, w, hidden, tokens, mask, output, conv_state, recurrent_state, NULL, NULL);
+}
+
+/* Per-token loop of src/kq_gdn_qwen38.c:545-842 over F32 weights; the
+ * checkpoint kinds follow include/kq_gdn.h:23-44 and are emitted where the
+ * reference emits them. */
+int kqo_gdn_run_observed(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
+                         const float *hidden, uint64_t tokens, const uint8_t *mask,
+                         float *output, float *conv_state, float *recurrent_state,
+                         kqo_checkpoint_fn cb, void *user) {
     const uint64_t H = dm->hidden_size, Hv = dm->value_heads,
                    dk = dm->key_dim, dv = dm->value_dim, K = dm->conv_kernel;
     const uint64_t key_width = (uint64_t)dm->key_heads * dk;
@@ -268,7 +289,7 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
     const uint64_t conv_n = C * K, rec_n = Hv * dk * dv;
     const float query_scale = 1.0f / sqrtf((float)dk);
     float *ws, *conv, *rec, *xin, *proj, *gate, *pb, *pa, *co, *q, *k, *v,
-          *beta, *g, *core, *sg, *y;
+          *beta, *g, *core, *sg, *y, *rd, *dl;
     uint64_t t, i, h, f, kf, c, j;
     int status = KQO_OK;
 
@@ -276,14 +297,14 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
         return KQO_INVALID_ARGUMENT;
     ws = (float *)malloc(sizeof(float) *
                          (conv_n + rec_n + H + C + Vd + 2 * Hv + C +
-                          2 * Hv * dk + Vd + 2 * Hv + Vd + Vd + H));
+                          2 * Hv * dk + Vd + 2 * Hv + Vd + Vd + H + 2 * Vd));
     if (ws == NULL) return KQO_INVALID_ARGUMENT;
     conv = ws;            rec = conv + conv_n;  xin = rec + rec_n;
     proj = xin + H;       gate = proj + C;      pb = gate + Vd;
     pa = pb + Hv;         co = pa + Hv;         q = co + C;
     k = q + Hv * dk;      v = k + Hv * dk;      beta = v + Vd;
     g = beta + Hv;        core = g + Hv;        sg = core + Vd;
-    y = sg + Vd;
+    y = sg + Vd;          rd = y + H;           dl = rd + Vd;
     /* transactional: work on a copy (src/kq_gdn_qwen38.c:532-536) */
     memcpy(conv, conv_state, sizeof(float) * conv_n);
     memcpy(rec, recurrent_state, sizeof(float) * rec_n);
@@ -292,11 +313,17 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
         const float *x = hidden + t * H;
         float m = mask == NULL ? 1.0f : (float)mask[t];
         for (i = 0; i < H; ++i) xin[i] = x[i] * m;
+        kqo_emit(cb, user, 0, t, 1, H, 0, 0, xin, H);                 /* MASKED_INPUT */
         /* projections (:558-579) */
         for (i = 0; i < C; ++i) proj[i] = kqo_dot(w->qkv + i * H, xin, H);
         for (i = 0; i < Vd; ++i) gate[i] = kqo_dot(w->gate + i * H, xin, H);
         for (i = 0; i < Hv; ++i) pb[i] = kqo_dot(w->beta + i * H, xin, H);
         for (i = 0; i < Hv; ++i) pa[i] = kqo_dot(w->alpha + i * H, xin, H);
+        kqo_emit(cb, user, 1, t, 1, C, 0, 0, proj, C);                /* PROJECTED_QKV */
+        kqo_emit(cb, user, 2, t, 2, Hv, dv, 0, gate, Vd);             /* PROJECTED_GATE */
+        kqo_emit(cb, user, 3, t, 1, Hv, 0, 0, pb, Hv);                /* PROJECTED_BETA */
+        kqo_emit(cb, user, 4, t, 1, Hv, 0, 0, pa, Hv);                /* PROJECTED_ALPHA */
+        kqo_emit(cb, user, 5, t, 1, C, 0, 0, proj, C);                /* CONV_INPUT */
         /* causal conv over pre-activation history, then SiLU (:602-621) */
         for (c = 0; c < C; ++c) {
             float *hist = conv + c * K;
@@ -306,6 +333,8 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
             s = kqo_dot(w->conv + c * K, hist, K);
             co[c] = s * kqo_sigmoid(s);
         }
+        kqo_emit(cb, user, 6, t, 1, C, 0, 0, co, C);                  /* CONV_OUTPUT */
+        kqo_emit(cb, user, 18, t, 2, C, K, 0, conv, conv_n);          /* CONV_STATE */
         /* head split with consecutive key-head repeat (:631-648) */
         for (h = 0; h < Hv; ++h) {
             uint64_t kh = h / repeat;
@@ -313,6 +342,9 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
             memcpy(k + h * dk, co + key_width + kh * dk, sizeof(float) * dk);
             memcpy(v + h * dv, co + 2 * key_width + h * dv, sizeof(float) * dv);
         }
+        kqo_emit(cb, user, 7, t, 2, Hv, dk, 0, q, Hv * dk);           /* QUERY_BEFORE_NORM */
+        kqo_emit(cb, user, 8, t, 2, Hv, dk, 0, k, Hv * dk);           /* KEY_BEFORE_NORM */
+        kqo_emit(cb, user, 9, t, 2, Hv, dv, 0, v, Vd);                /* VALUE */
         /* beta, log-decay, L2 norms (:662-687) */
         for (h = 0; h < Hv; ++h) {
             float sp, a = pa[h] + w->dt_bias[h];
@@ -338,12 +370,16 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
             }
         }
         if (status != KQO_OK) break;
+        kqo_emit(cb, user, 10, t, 2, Hv, dk, 0, q, Hv * dk);          /* NORMALIZED_SCALED_QUERY */
+        kqo_emit(cb, user, 11, t, 2, Hv, dk, 0, k, Hv * dk);          /* NORMALIZED_KEY */
+        kqo_emit(cb, user, 12, t, 1, Hv, 0, 0, g, Hv);                /* LOG_DECAY */
+        kqo_emit(cb, user, 13, t, 1, Hv, 0, 0, beta, Hv);             /* BETA */
         /* delta-rule recurrence (:705-761) */
         for (h = 0; h < Hv; ++h) {
             float decay = expf(g[h]);
             float *S = rec + h * dk * dv;
             const float *kh = k + h * dk, *qh = q + h * dk, *vh = v + h * dv;
-            float delta[1024];
+            float *delta = dl + h * dv;
             for (i = 0; i < dk * dv; ++i) S[i] = S[i] * decay;
             for (f = 0; f < dv; ++f) {
                 float sum = 0.0f;
@@ -351,6 +387,7 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
                     float product = S[kf * dv + f] * kh[kf];
                     sum = sum + product;
                 }
+                rd[h * dv + f] = sum;
                 delta[f] = (vh[f] - sum) * beta[h];
             }
             for (kf = 0; kf < dk; ++kf) {
@@ -371,6 +408,10 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
         for (i = 0; i < rec_n; ++i)
             if (!isfinite(rec[i])) { status = KQO_NUMERIC_DOMAIN; break; }
         if (status != KQO_OK) break;
+        kqo_emit(cb, user, 14, t, 2, Hv, dv, 0, rd, Vd);              /* RECURRENT_READ */
+        kqo_emit(cb, user, 15, t, 2, Hv, dv, 0, dl, Vd);              /* RECURRENT_DELTA */
+        kqo_emit(cb, user, 16, t, 2, Hv, dv, 0, core, Vd);            /* RECURRENT_OUTPUT */
+        kqo_emit(cb, user, 17, t, 3, Hv, dk, dv, rec, rec_n);         /* RECURRENT_STATE */
         /* gated RMSNorm (:787-815): norm weight applied directly */
         for (i = 0; i < Vd; ++i) sg[i] = kqo_sigmoid(gate[i]);
         for (h = 0; h < Hv; ++h) {
@@ -388,6 +429,7 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
                 cr[f] = wt * sg[h * dv + f];
             }
         }
+        kqo_emit(cb, user, 19, t, 2, Hv, dv, 0, core, Vd);            /* GATED_NORM_OUTPUT */
         /* output projection (:826-831) */
         for (i = 0; i < H; ++i) {
             y[i] = kqo_dot(w->output + i * Vd, core, Vd);
@@ -395,6 +437,7 @@ int kqo_gdn_run(const kqo_gdn_dims *dm, const kqo_gdn_weights *w,
         }
         if (status != KQO_OK) break;
         memcpy(output + t * H, y, sizeof(float) * H);
+        kqo_emit(cb, user, 20, t, 1, H, 0, 0, y, H);                  /* OPERATOR_OUTPUT */
     }
     if (status == KQO_OK) {
         memcpy(conv_state, conv, sizeof(float) * conv_n);
@@ -461,12 +504,24 @@ uint64_t kqo_select_blocks(const float *scores, uint64_t count, uint64_t limit,
     return n;
 }
 
-/* Per-token loop of src/kq_qsa_qwen38.c:524-828 over F32 weights. */
 int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
                 const float *hidden, uint64_t tokens, float *output,
                 float *kc, float *vc, float *rc, uint64_t capacity,
                 uint64_t *length, uint32_t *sel_out, uint32_t *sel_counts,
                 float *scores_out) {
+    return kqo_qsa_run_observed(dm, w, hidden, tokens, output, kc, vc, rc, capacity, length, sel_out, sel_counts,
+                                scores_out, NULL, NULL);
+}
+
+/* Per-token loop of src/kq_qsa_qwen38.c:524-828 over F32 weights; the
+ * checkpoint kinds follow include/kq_qsa.h:23-36 and are emitted where the
+ * reference emits them (:687-716 before the attention, :794-815 after the
+ * output projection). */
+int kqo_qsa_run_observed(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
+                         const float *hidden, uint64_t tokens, float *output,
+                         float *kc, float *vc, float *rc, uint64_t capacity,
+                         uint64_t *length, uint32_t *sel_out, uint32_t *sel_counts,
+                         float *scores_out, kqo_checkpoint_fn cb, void *user) {
     const uint64_t H = dm->hidden_size, Hq = dm->query_heads,
                    Hkv = dm->kv_heads, d = dm->head_dim, Hi = dm->index_heads,
                    di = dm->index_dim, blk = dm->block_size;
@@ -476,7 +531,7 @@ int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
     const uint64_t rep = Hq / Hkv;
     const uint64_t max_blocks = capacity / blk;
     uint64_t L0, t;
-    float *qg, *q, *kk, *vv, *iq, *rk, *bk, *sc, *logit, *ctx, *y, *staged;
+    float *qg, *q, *kk, *vv, *iq, *rk, *bk, *sc, *logit, *ctx, *y, *staged, *lg_all, *pr_all, *hctx;
     uint32_t *sel, *tok;
     int st = KQO_OK;
 
@@ -486,14 +541,15 @@ int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
     L0 = *length;
     qg = (float *)malloc(sizeof(float) * (2 * qw + qw + kvw + kvw + iqw + di +
                                           max_blocks * di + max_blocks +
-                                          sel_cap + qw + H + tokens * H));
+                                          sel_cap + qw + H + tokens * H + 2 * Hq * sel_cap + qw));
     sel = (uint32_t *)malloc(sizeof(uint32_t) * (topk + sel_cap + 1));
     if (qg == NULL || sel == NULL) { free(qg); free(sel); return KQO_INVALID_ARGUMENT; }
     tok = sel + topk;
     q = qg + 2 * qw;  kk = q + qw;   vv = kk + kvw;  iq = vv + kvw;
     rk = iq + iqw;    bk = rk + di;  sc = bk + max_blocks * di;
     logit = sc + max_blocks; ctx = logit + sel_cap; y = ctx + qw;
-    staged = y + H;
+    staged = y + H;   lg_all = staged + tokens * H; pr_all = lg_all + Hq * sel_cap;
+    hctx = pr_all + Hq * sel_cap;
 
     for (t = 0; t < tokens && st == KQO_OK; ++t) {
         const float *x = hidden + t * H;
@@ -557,6 +613,13 @@ int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
         if (sel_counts != NULL) sel_counts[t] = (uint32_t)nsel;
         if (scores_out != NULL && nblocks > 0)
             memcpy(scores_out + t * max_blocks, sc, sizeof(float) * nblocks);
+        kqo_emit(cb, user, 0, t, 2, Hi, di, 0, iq, iqw);                  /* INDEX_QUERY */
+        kqo_emit(cb, user, 1, t, 1, di, 0, 0, rk, di);                    /* RAW_INDEX_KEY */
+        kqo_emit(cb, user, 2, t, 2, nblocks, di, 0, bk, nblocks * di);    /* BLOCK_KEYS */
+        kqo_emit(cb, user, 3, t, 1, nblocks, 0, 0, sc, nblocks);          /* CANDIDATE_SCORES */
+        kqo_emit(cb, user, 4, t, 2, Hq, d, 0, q, qw);                     /* QUERY */
+        kqo_emit(cb, user, 5, t, 2, Hkv, d, 0, kk, kvw);                  /* KEY */
+        kqo_emit(cb, user, 6, t, 2, Hkv, d, 0, vv, kvw);                  /* VALUE */
         /* sparse softmax attention (:716-773) */
         for (h = 0; h < Hq; ++h) {
             uint64_t kvh = h / rep, s;
@@ -567,6 +630,7 @@ int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
                 for (f = 0; f < d; ++f) dot = dot + q[h * d + f] * krow[f];
                 dot = dot / sqrtf((float)d);
                 logit[s] = dot;
+                lg_all[h * ntok + s] = dot;
                 if (dot > mx) mx = dot;
             }
             for (s = 0; s < ntok; ++s) {
@@ -575,7 +639,10 @@ int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
                 sum = sum + p;
             }
             if (!(sum > 0.0f) || !isfinite(sum)) { st = KQO_NUMERIC_DOMAIN; break; }
-            for (s = 0; s < ntok; ++s) logit[s] /= sum;
+            for (s = 0; s < ntok; ++s) {
+                logit[s] /= sum;
+                pr_all[h * ntok + s] = logit[s];
+            }
             for (f = 0; f < d; ++f) {
                 float acc = 0.0f;
                 for (s = 0; s < ntok; ++s)
@@ -584,6 +651,7 @@ int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
             }
         }
         if (st != KQO_OK) break;
+        memcpy(hctx, ctx, sizeof(float) * qw);
         /* sigmoid output gate (:774-782), simple form */
         for (h = 0; h < Hq; ++h)
             for (f = 0; f < d; ++f) {
@@ -597,6 +665,11 @@ int kqo_qsa_run(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
         }
         if (st != KQO_OK) break;
         memcpy(staged + t * H, y, sizeof(float) * H);
+        kqo_emit(cb, user, 7, t, 2, Hq, ntok, 0, lg_all, Hq * ntok);      /* ATTENTION_LOGITS */
+        kqo_emit(cb, user, 8, t, 2, Hq, ntok, 0, pr_all, Hq * ntok);      /* ATTENTION_PROBABILITIES */
+        kqo_emit(cb, user, 9, t, 2, Hq, d, 0, hctx, qw);                  /* HEAD_CONTEXT */
+        kqo_emit(cb, user, 10, t, 2, Hq, d, 0, ctx, qw);                  /* GATED_CONTEXT */
+        kqo_emit(cb, user, 11, t, 1, H, 0, 0, y, H);                      /* OPERATOR_OUTPUT */
     }
     if (st == KQO_OK) {
         memcpy(output, staged, sizeof(float) * tokens * H);

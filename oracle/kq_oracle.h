@@ -72,11 +72,23 @@ typedef struct kqo_gdn_weights {
     const float *output;   /* [H][Hv*dv] */
 } kqo_gdn_weights;
 
+/* Checkpoint callback of the observed runs: `kind` is the operator's
+ * checkpoint enumerator (kq_gdn_checkpoint_kind / kq_qsa_checkpoint_kind of
+ * the reference headers), emitted in the reference's order with its rank and
+ * dimensions (src/kq_gdn_qwen38.c:248-271, src/kq_qsa_qwen38.c:309-330). */
+typedef void (*kqo_checkpoint_fn)(uint32_t kind, uint64_t token, uint32_t rank, const uint64_t *dims,
+                                  const float *values, uint64_t count, void *user);
+
 /* Runs T tokens; conv_state [C*K] and recurrent_state [Hv*dk*dv] are updated
  * in place only on success (the reference's transactional contract). */
 int kqo_gdn_run(const kqo_gdn_dims *dims, const kqo_gdn_weights *weights,
                 const float *hidden, uint64_t tokens, const uint8_t *mask,
                 float *output, float *conv_state, float *recurrent_state);
+/* kqo_gdn_run with the reference's 21 checkpoints per token sent to `cb`. */
+int kqo_gdn_run_observed(const kqo_gdn_dims *dims, const kqo_gdn_weights *weights,
+                         const float *hidden, uint64_t tokens, const uint8_t *mask,
+                         float *output, float *conv_state, float *recurrent_state,
+                         kqo_checkpoint_fn cb, void *user);
 
 typedef struct kqo_qsa_dims {
     uint32_t hidden_size;
@@ -115,6 +127,13 @@ int kqo_qsa_run(const kqo_qsa_dims *dims, const kqo_qsa_weights *weights,
                 uint64_t capacity, uint64_t *length,
                 uint32_t *selected_ids, uint32_t *selected_counts,
                 float *scores);
+/* kqo_qsa_run with the reference's 12 checkpoints per token sent to `cb`. */
+int kqo_qsa_run_observed(const kqo_qsa_dims *dims, const kqo_qsa_weights *weights,
+                         const float *hidden, uint64_t tokens, float *output,
+                         float *key_cache, float *value_cache, float *raw_cache,
+                         uint64_t capacity, uint64_t *length,
+                         uint32_t *selected_ids, uint32_t *selected_counts,
+                         float *scores, kqo_checkpoint_fn cb, void *user);
 
 /* Stable top-k by (score desc, id asc): src/kq_qsa_qwen38.c:328-359. */
 uint64_t kqo_select_blocks(const float *scores, uint64_t count, uint64_t limit,

@@ -340,3 +340,141 @@ def qsa_weights_f32(layer) -> dict:
             "query_norm": layer.query_norm, "key_norm": layer.key_norm, "index_query": dq(layer.index_query),
             "index_key": dq(layer.index_key), "index_query_norm": layer.index_query_norm,
             "index_key_norm": layer.index_key_norm}
+
+
+# ------------------------------------------------------------------ checkpoints
+
+_PORT_CB = C.CFUNCTYPE(None, u32, u64, u32, C.POINTER(u64), C.POINTER(f32), u64, vp)
+
+
+class _RefGdnCheckpoint(C.Structure):   # include/kq_gdn.h:46-53
+    _fields_ = [("kind", C.c_int), ("token_index", u64), ("rank", u32), ("dimensions", u64 * 4),
+                ("values", C.POINTER(f32)), ("value_count", u64)]
+
+
+class _RefQsaCheckpoint(C.Structure):   # include/kq_qsa.h:38-45
+    _fields_ = [("kind", C.c_int), ("token_index", u64), ("rank", u32), ("dimensions", u64 * 3),
+                ("values", C.POINTER(f32)), ("value_count", u64)]
+
+
+_REF_GDN_CB = C.CFUNCTYPE(None, C.POINTER(_RefGdnCheckpoint), vp)
+_REF_QSA_CB = C.CFUNCTYPE(None, C.POINTER(_RefQsaCheckpoint), vp)
+
+
+def _record(out, kind, token, rank, dims, values, count):
+    vals = np.ctypeslib.as_array(values, (count,)).copy() if count else np.zeros(0, np.float32)
+    out.append({"kind": int(kind), "token": int(token), "rank": int(rank),
+                "dims": tuple(int(dims[i]) for i in range(rank)), "values": vals})
+
+
+def gdn_checkpoints(dims, w: dict, x: np.ndarray, conv: np.ndarray, rec: np.ndarray, mask=None,
+                    impl: str = "port"):
+    """Every checkpoint of a GDN run, in emission order: a list of dicts
+    (kind, token, rank, dims, values).  impl "port": the restatement's
+    kqo_gdn_run_observed; "reference": the reference's kq_gdn_prefill_f32 with
+    a checkpoint observer.  Returns (status, checkpoints)."""
+    xv = _a(x).reshape(-1, dims.hidden)
+    T = xv.shape[0]
+    y = np.zeros((T, dims.hidden), np.float32)
+    conv2, rec2 = _a(conv).copy(), _a(rec).copy()
+    ws = {k: _a(w[k]) for k in GDN_FIELDS}
+    m = None if mask is None else np.ascontiguousarray(mask, np.uint8)
+    out = []
+    if impl == "port":
+        cb = _PORT_CB(lambda kind, tok, rank, dp, vals, n, _u: _record(out, kind, tok, rank, dp, vals, n))
+        gd = _GdnDims(dims.hidden, dims.key_heads, dims.value_heads, dims.key_dim, dims.value_dim,
+                      dims.conv_kernel, dims.eps)
+        gw = _GdnWeights(*[ws[k].ctypes.data for k in GDN_FIELDS])
+        st = port().kqo_gdn_run_observed(C.byref(gd), C.byref(gw), xv.ctypes.data_as(vp), u64(T),
+                                         None if m is None else m.ctypes.data_as(vp), y.ctypes.data_as(vp),
+                                         conv2.ctypes.data_as(vp), rec2.ctypes.data_as(vp), cb, None)
+        return st, out
+    L = ref()
+    cb = _REF_GDN_CB(lambda p, _u: _record(out, p.contents.kind, p.contents.token_index, p.contents.rank,
+                                           p.contents.dimensions, p.contents.values, p.contents.value_count))
+    gd = _RefGdnDims(dims.hidden, dims.key_heads, dims.value_heads, dims.key_dim, dims.value_dim,
+                     dims.conv_kernel, dims.eps, 0)
+    cfg, state = vp(), vp()
+    d = _Diag()
+    if L.kq_gdn_test_config_create(C.byref(gd), C.byref(cfg), C.byref(d)) != 0:
+        raise RuntimeError(d.message)
+    try:
+        if L.kq_gdn_state_create(cfg, C.byref(state), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        init = 0 if (not conv2.any() and not rec2.any()) else 1
+        if L.kq_gdn_state_import_f32(state, conv2.ctypes.data_as(vp), u64(conv2.size), rec2.ctypes.data_as(vp),
+                                     u64(rec2.size), C.c_int(init), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        L.kq_gdn_config_scratch_bytes.restype = u64
+        sb = L.kq_gdn_config_scratch_bytes(cfg)
+        scratch = np.empty(sb // 4 + 1, np.float32)
+        gw = _RefGdnWeights()
+        for k in GDN_FIELDS:
+            setattr(gw, k, ws[k].ctypes.data)
+            setattr(gw, k + "_count", ws[k].size)
+        st = L.kq_gdn_prefill_f32(cfg, C.byref(gw), xv.ctypes.data_as(vp), u64(T),
+                                  None if m is None else m.ctypes.data_as(vp), y.ctypes.data_as(vp), u64(y.size),
+                                  state, scratch.ctypes.data_as(vp), u64(sb), cb, None, C.byref(d))
+        return st, out
+    finally:
+        if state:
+            L.kq_gdn_state_close(state)
+        L.kq_gdn_config_close(cfg)
+
+
+def qsa_checkpoints(dims, w: dict, x: np.ndarray, key: np.ndarray, value: np.ndarray, raw: np.ndarray,
+                    length: int, capacity: int, impl: str = "port"):
+    """Every checkpoint of a QSA run over caches holding `length` prior rows,
+    in emission order (see gdn_checkpoints).  Returns (status, checkpoints)."""
+    xv = _a(x).reshape(-1, dims.hidden)
+    T = xv.shape[0]
+    y = np.zeros((T, dims.hidden), np.float32)
+    kc = np.zeros((capacity, dims.kv_width), np.float32)
+    vc = np.zeros((capacity, dims.kv_width), np.float32)
+    rc = np.zeros((capacity, dims.index_dim), np.float32)
+    kc[:length], vc[:length], rc[:length] = key[:length], value[:length], raw[:length]
+    ws = {k: _a(w[k]) for k in QSA_FIELDS}
+    out = []
+    if impl == "port":
+        cb = _PORT_CB(lambda kind, tok, rank, dp, vals, n, _u: _record(out, kind, tok, rank, dp, vals, n))
+        qd = _QsaDims(dims.hidden, dims.query_heads, dims.kv_heads, dims.head_dim, dims.index_heads, dims.index_dim,
+                      dims.block, dims.budget, dims.rotary, dims.eps, dims.theta)
+        qw = _QsaWeights(*[ws[k].ctypes.data for k in QSA_FIELDS])
+        ln = u64(length)
+        st = port().kqo_qsa_run_observed(C.byref(qd), C.byref(qw), xv.ctypes.data_as(vp), u64(T),
+                                         y.ctypes.data_as(vp), kc.ctypes.data_as(vp), vc.ctypes.data_as(vp),
+                                         rc.ctypes.data_as(vp), u64(capacity), C.byref(ln), None, None, None, cb,
+                                         None)
+        return st, out
+    L = ref()
+    cb = _REF_QSA_CB(lambda p, _u: _record(out, p.contents.kind, p.contents.token_index, p.contents.rank,
+                                           p.contents.dimensions, p.contents.values, p.contents.value_count))
+    qd = _RefQsaDims(dims.hidden, dims.query_heads, dims.kv_heads, dims.head_dim, dims.index_heads, dims.index_dim,
+                     dims.block, dims.budget, max(capacity, dims.max_context if dims.max_context else capacity),
+                     dims.rotary, dims.eps, dims.theta, 0)
+    cfg, state = vp(), vp()
+    d = _Diag()
+    if L.kq_qsa_test_config_create(C.byref(qd), C.byref(cfg), C.byref(d)) != 0:
+        raise RuntimeError(d.message)
+    try:
+        if L.kq_qsa_state_create(cfg, u64(capacity), C.byref(state), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        if L.kq_qsa_state_import_f32(state, kc.ctypes.data_as(vp), u64(length * dims.kv_width),
+                                     vc.ctypes.data_as(vp), u64(length * dims.kv_width), rc.ctypes.data_as(vp),
+                                     u64(length * dims.index_dim), u64(length), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        need = u64()
+        L.kq_qsa_required_scratch_bytes(cfg, state, u64(T), C.byref(need), C.byref(d))
+        scratch = np.empty(need.value // 4 + 1, np.float32)
+        qw = _RefQsaWeights()
+        for k in QSA_FIELDS:
+            setattr(qw, k, ws[k].ctypes.data)
+            setattr(qw, k + "_count", ws[k].size)
+        st = L.kq_qsa_prefill_f32(cfg, C.byref(qw), xv.ctypes.data_as(vp), u64(T), y.ctypes.data_as(vp),
+                                  u64(y.size), state, scratch.ctypes.data_as(vp), need, _SEL_CB(), cb, None,
+                                  C.byref(d))
+        return st, out
+    finally:
+        if state:
+            L.kq_qsa_state_close(state)
+        L.kq_qsa_config_close(cfg)

@@ -182,6 +182,38 @@ def test_gdn_golden_cases_f32_api(kq, oracle):
         layer.close()
 
 
+def test_f32_api_reuses_uploaded_weights_until_they_change(kq, oracle):
+    """The F32 entry point keeps host weight arrays it has uploaded on the
+    device for later calls; an array changed in place (same address, new
+    contents) must be uploaded again, so every call matches the oracle on
+    the weights as they are at that call."""
+    from kqb200 import synth
+    dims = synth.GdnDims(hidden=256, key_heads=2, value_heads=4)
+    weights = synth.gdn_layer(31, dims, synth.TYPE_Q8_0, synth.TYPE_Q8_0, synth.TYPE_F32)
+    w = {k: np.ascontiguousarray(v, np.float32) for k, v in oracle.gdn_weights_f32(weights).items()}
+    addresses = {k: v.ctypes.data for k, v in w.items()}
+    layer = kq.GdnLayer(dims)
+    try:
+        for call in range(3):
+            if call == 2:
+                w["qkv"] *= 1.5
+                w["output"][0, :] += 0.01
+                w["a_log"][1] -= 0.25
+            assert all(v.ctypes.data == addresses[k] for k, v in w.items())
+            s = kq.GdnState(layer)
+            c0, r0 = synth.gdn_state(32, dims)
+            s.load(c0, r0)
+            x = synth.hidden(33 + call, 3, dims.hidden)
+            st, y, d = _gdn_f32_call(kq, layer.handle, dims, w, x, s)
+            assert st == 0, d.text()
+            _, yo, _, reco = oracle.gdn_run(dims, w, x, c0, r0)
+            assert_close(y, yo, f"call {call} output")
+            assert_close(s.save()[1], reco, f"call {call} state")
+            s.close()
+    finally:
+        layer.close()
+
+
 def _gdn_setup(kq, oracle, dims, seed, in_type, out_type, gate_type):
     from kqb200 import synth
     weights = synth.gdn_layer(seed, dims, in_type, out_type, gate_type)

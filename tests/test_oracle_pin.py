@@ -272,6 +272,52 @@ def test_port_qsa_matches_reference_bits(oracle, seed, L0, T):
         assert np.array_equal(bits(s1["scores"]), bits(s2["scores"]))
 
 
+def _same_checkpoints(a, b, expected_kinds):
+    assert len(a) == len(b) and len(a) > 0
+    for x, y in zip(a, b):
+        assert (x["kind"], x["token"], x["rank"], x["dims"]) == (y["kind"], y["token"], y["rank"], y["dims"])
+        assert np.array_equal(bits(x["values"]), bits(y["values"])), (x["kind"], x["token"])
+    assert {c["kind"] for c in a} == set(range(expected_kinds))
+
+
+@ref_only
+@pytest.mark.parametrize("seed,T,masked,init", [(4, 3, True, True), (5, 2, False, False)])
+def test_port_gdn_checkpoints_match_reference_bits(oracle, seed, T, masked, init):
+    """The restatement emits the reference's 21 GDN checkpoint kinds per token
+    (include/kq_gdn.h:23-44) in the same order, with the same ranks,
+    dimensions and bits (src/kq_gdn_qwen38.c:554-838)."""
+    from kqb200 import synth
+    dims = synth.GdnDims(hidden=64, key_heads=2, value_heads=4, key_dim=16, value_dim=8)
+    layer = synth.gdn_layer(seed, dims, synth.TYPE_Q8_0, synth.TYPE_Q8_0, synth.TYPE_F32)
+    w = oracle.gdn_weights_f32(layer)
+    conv, rec = synth.gdn_state(seed + 10, dims, zero=not init)
+    x = synth.hidden(seed + 20, T, dims.hidden)
+    mask = (np.arange(T) % 2 == 0).astype(np.uint8) if masked else None
+    sa, a = oracle.gdn_checkpoints(dims, w, x, conv, rec, mask, "port")
+    sb, b = oracle.gdn_checkpoints(dims, w, x, conv, rec, mask, "reference")
+    assert sa == sb == 0 and len(a) == 21 * T
+    _same_checkpoints(a, b, 21)
+
+
+@ref_only
+@pytest.mark.parametrize("seed,L0,T", [(6, 0, 6), (7, 41, 3)])
+def test_port_qsa_checkpoints_match_reference_bits(oracle, seed, L0, T):
+    """The restatement emits the reference's 12 QSA checkpoint kinds per token
+    (include/kq_qsa.h:23-36) in the same order, with the same ranks,
+    dimensions and bits (src/kq_qsa_qwen38.c:687-815)."""
+    from kqb200 import synth
+    dims = synth.QsaDims(hidden=128, query_heads=4, kv_heads=2, head_dim=32, index_heads=2, index_dim=32,
+                         block=4, budget=32, max_context=256, rotary=16)
+    layer = synth.qsa_layer(seed, dims, synth.TYPE_Q8_0, index_type=synth.TYPE_BF16)
+    w = oracle.qsa_weights_f32(layer)
+    k, v, r = synth.qsa_cache(seed + 5, dims, L0)
+    x = synth.hidden(seed + 7, T, dims.hidden)
+    sa, a = oracle.qsa_checkpoints(dims, w, x, k, v, r, L0, 128, "port")
+    sb, b = oracle.qsa_checkpoints(dims, w, x, k, v, r, L0, 128, "reference")
+    assert sa == sb == 0 and len(a) == 12 * T
+    _same_checkpoints(a, b, 12)
+
+
 def test_q6k_restatement_properties(oracle):
     """Q6_K has no reference decoder (parity unpinned by the reference): the
     restatement is checked against an independent numpy decode of the public
