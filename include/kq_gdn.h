@@ -10,8 +10,12 @@
  *     short) but device work space is owned by the state;
  *   - failure leaves the state unchanged (double-buffered state, flipped only
  *     after the whole call succeeded);
- *   - a non-NULL observer selects the debug path, which copies each
- *     checkpoint to the host (slow; for parity work only).
+ *   - a non-NULL observer selects the checkpoint path: the operator runs
+ *     token by token and every checkpoint of the reference's list (all 21
+ *     kinds, same order, ranks and dimensions) is copied to the host and
+ *     handed to the observer once its token has run without a device error;
+ *     a failing token stops the stream and the whole call is rolled back
+ *     (slow; for validation work only).
  * Entry points that need a GGUF model (config_create with a kq_model)
  * return KQ_STATUS_UNSUPPORTED_MODEL: configs come from
  * kq_gdn_test_config_create / kq_b200.h.

@@ -13,7 +13,13 @@
  *     scores and the selected blocks are bit-identical to the reference
  *     given bit-identical inputs;
  *   - failure leaves the state (length and committed rows) and the output
- *     unchanged.
+ *     unchanged;
+ *   - a non-NULL checkpoint observer selects the checkpoint path: one token
+ *     at a time, the selection observer (if any) and then all 12 checkpoint
+ *     kinds of the reference's list (same order, ranks and dimensions; the
+ *     attention logits and probabilities over the selected tokens in the
+ *     reference's rank order) are copied to the host and handed over once
+ *     the token has run without a device error (slow; for validation work).
  */
 #ifndef KQ_QSA_H
 #define KQ_QSA_H

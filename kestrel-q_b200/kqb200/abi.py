@@ -105,9 +105,37 @@ class QsaSelection(C.Structure):
                 ("selected_token_count", u64), ("tail_count", u64)]
 
 
+class GdnCheckpoint(C.Structure):   # include/kq_gdn.h kq_gdn_checkpoint
+    _fields_ = [("kind", C.c_int), ("token_index", u64), ("rank", u32), ("dimensions", u64 * 4),
+                ("values", C.POINTER(f32)), ("value_count", u64)]
+
+
+class QsaCheckpoint(C.Structure):   # include/kq_qsa.h kq_qsa_checkpoint
+    _fields_ = [("kind", C.c_int), ("token_index", u64), ("rank", u32), ("dimensions", u64 * 3),
+                ("values", C.POINTER(f32)), ("value_count", u64)]
+
+
 # int (*)(void *words, uint64_t count, void *cuda_stream, void *user)
 EXCHANGE_FN = C.CFUNCTYPE(C.c_int, vp, u64, vp, vp)
 SELECTION_OBSERVER = C.CFUNCTYPE(None, C.POINTER(QsaSelection), vp)
+GDN_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(GdnCheckpoint), vp)
+QSA_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(QsaCheckpoint), vp)
+
+
+def checkpoint_collector():
+    """(list, callback body): the body appends each checkpoint it sees as a
+    dict (kind, token, rank, dims, values copied out of the library's buffer,
+    which is valid only during the call)."""
+    import numpy as np
+    out = []
+
+    def on_checkpoint(p, _user):
+        c = p.contents
+        vals = np.ctypeslib.as_array(c.values, (c.value_count,)).copy() if c.value_count else np.zeros(0, np.float32)
+        out.append({"kind": int(c.kind), "token": int(c.token_index), "rank": int(c.rank),
+                    "dims": tuple(int(c.dimensions[i]) for i in range(c.rank)), "values": vals})
+
+    return out, on_checkpoint
 
 _SIGNATURES = {
     "kq_status_string": (C.c_char_p, [C.c_int]),
