@@ -139,6 +139,71 @@ kq_status kq_b200_provider_add_vector_f32(kq_weight_provider *provider,
                                           const kq_semantic_tensor **out_tensor,
                                           kq_diagnostic *diagnostic);
 
+/* The model GGUF's storage of GDN tensors: value heads in tiled order (the
+ * converter stores canonical value head g * R + r, key head g, as head
+ * r * Hk + g).  The target model has 16 key heads, 3 value heads per key
+ * head, 128 features per head. */
+typedef struct kq_b200_gguf_layout {
+    uint32_t gdn_key_heads;
+    uint32_t gdn_value_repeat;
+    uint32_t gdn_head_width;
+} kq_b200_gguf_layout;
+
+/* Uploads a matrix as the model's GGUF stores it and presents the canonical
+ * tensor the operators read: the transforms of the reference provider
+ * (src/kq_weight_provider.c:205-248,438-451) for `role`:
+ *   KQ_ROLE_GDN_QKV    value rows (after the 2 Hk W q/k rows) reordered
+ *   KQ_ROLE_GDN_GATE   rows reordered (head width W)
+ *   KQ_ROLE_GDN_ALPHA, KQ_ROLE_GDN_BETA  rows reordered (one per head)
+ *   KQ_ROLE_GDN_OUT    columns kept in tiled order: the GDN operator writes
+ *                      its gated output in that order and the linear entry
+ *                      points permute their canonical input
+ *   other roles        stored as given (kq_b200_provider_add_matrix).
+ * The allocation-free linear takes canonical-column tensors only. */
+kq_status kq_b200_provider_add_gguf_matrix(kq_weight_provider *provider,
+                                           const char *semantic_id,
+                                           kq_semantic_role role,
+                                           uint32_t type_id,
+                                           uint64_t rows,
+                                           uint64_t columns,
+                                           const void *packed,
+                                           uint64_t packed_bytes,
+                                           const kq_b200_gguf_layout *layout,
+                                           const kq_semantic_tensor **out_tensor,
+                                           kq_diagnostic *diagnostic);
+
+/* Uploads an F32 vector as the model's GGUF stores it, presented canonical
+ * (src/kq_weight_provider.c:680-717): KQ_ROLE_GDN_A_LOG stored as -exp(A_log)
+ * (canonical = logf(-stored), heads reordered), KQ_ROLE_GDN_DT_BIAS heads
+ * reordered, KQ_ROLE_GDN_CONV channels reordered like the qkv rows, the QSA
+ * q/k and index q/k norms stored as 1 + delta (canonical = stored - 1). */
+kq_status kq_b200_provider_add_gguf_vector_f32(kq_weight_provider *provider,
+                                               const char *semantic_id,
+                                               kq_semantic_role role,
+                                               const float *values,
+                                               uint64_t count,
+                                               const kq_b200_gguf_layout *layout,
+                                               const kq_semantic_tensor **out_tensor,
+                                               kq_diagnostic *diagnostic);
+
+/* Uploads the QSA index projection the way the model's GGUF splits it: one
+ * KQ_ROLE_QSA_INDEX_QK semantic with an INDEX_QUERY part (query_rows rows)
+ * and an INDEX_KEY part (key_rows rows), in that order (src/kq_qsa.c:184-201).
+ * kq_weight_provider_linear_f32 reads a part by its part role; pass the
+ * semantic as both index_query and index_key of kq_b200_qsa_tensors. */
+kq_status kq_b200_provider_add_index_qk(kq_weight_provider *provider,
+                                        const char *semantic_id,
+                                        uint32_t type_id,
+                                        uint64_t query_rows,
+                                        uint64_t key_rows,
+                                        uint64_t columns,
+                                        const void *query_packed,
+                                        uint64_t query_bytes,
+                                        const void *key_packed,
+                                        uint64_t key_bytes,
+                                        const kq_semantic_tensor **out_tensor,
+                                        kq_diagnostic *diagnostic);
+
 /* Batched form of kq_weight_provider_linear_f32:
  * y[b][r] = sum_c W[r][c] * x[b][c] for b < batch, with x [batch][columns]
  * and y [batch][rows] device arrays.  Batches above 8 run on the tensor

@@ -35,6 +35,7 @@ struct kq_gdn_config {
     kq_weight_provider *provider;
     QMatrix qkv, gate, beta, alpha, out;
     const float *a_log, *conv, *dt_bias, *norm;
+    const int32_t *gated_head;   // output projection column heads (null: canonical)
     bool bound;
 };
 
@@ -251,7 +252,7 @@ static kq_status gdn_debug_run(DeviceContext *c, const kq_gdn_config *cfg, const
     const uint32_t ldp = C + Vd + 2 * Hv;
     const size_t rk = (size_t)Hv * dk, rec_n = cfg->recurrent_elements;
     const size_t need = Carve::round((size_t)H * 4) + Carve::round((size_t)ldp * 4) + Carve::round((size_t)C * 4) +
-                        Carve::round((size_t)C * K * 4) + 4 * Carve::round(rk * 4) + 5 * Carve::round((size_t)Vd * 4) +
+                        Carve::round((size_t)C * K * 4) + 4 * Carve::round(rk * 4) + 6 * Carve::round((size_t)Vd * 4) +
                         2 * Carve::round((size_t)Hv * 4) + 4096;
     void *ws;
     kq_status st = c->workspace(need, &ws, diag);
@@ -271,6 +272,7 @@ static kq_status gdn_debug_run(DeviceContext *c, const kq_gdn_config *cfg, const
     b.delta = cv.take<float>(Vd);
     b.core = cv.take<float>(Vd);
     b.gated = cv.take<float>(Vd);
+    b.gated_proj = w.vec.gated_head != nullptr ? cv.take<float>(Vd) : b.gated;
     b.log_decay = cv.take<float>(Hv);
     b.beta = cv.take<float>(Hv);
     ProjSegments in{};
@@ -297,7 +299,7 @@ static kq_status gdn_debug_run(DeviceContext *c, const kq_gdn_config *cfg, const
         launch_gdn_debug_token(gd, w.vec, s->conv[cur], s->conv[1 - cur], s->rec[cur], s->rec[1 - cur], proj, b,
                                err, c->stream);
         float *yt = y + (size_t)t * H;
-        if (!launch_projection(out, b.gated, Vd, yt, H, 1, err, c->stream))
+        if (!launch_projection(out, b.gated_proj, Vd, yt, H, 1, err, c->stream))
             launch_check_finite(yt, H, err, c->stream);
         s->cur = 1 - cur;
         s->initialized = 1;
@@ -538,6 +540,7 @@ static bool resolve_bound(const kq_gdn_config *cfg, GdnResolved *w) {
     w->vec.conv = cfg->conv;
     w->vec.dt_bias = cfg->dt_bias;
     w->vec.norm = cfg->norm;
+    w->vec.gated_head = cfg->gated_head;
     return true;
 }
 
@@ -613,10 +616,17 @@ kq_status kq_b200_gdn_config_bind(kq_gdn_config *config, kq_weight_provider *pro
         {t->dt_bias, Hv, &config->dt_bias}, {t->norm, config->dims.value_head_dimension, &config->norm}};
     for (auto &m : mats) {
         ProviderTensor *p = provider_lookup(provider, m.s);
-        if (p == nullptr || p->is_vector)
+        if (p == nullptr || p->is_vector || p->parts[0] != nullptr)
             return fail(diagnostic, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "GDN provider matrix semantic is missing");
         if (p->m.rows != m.rows || p->m.cols != m.cols)
             return fail(diagnostic, KQ_STATUS_INCOMPATIBLE_GDN, "GDN canonical tensor shape mismatch");
+        // only the output projection may keep the model's tiled column
+        // order, with one head position per value head of this config
+        if (!p->col_heads.empty() &&
+            (m.dst != &config->out || p->col_heads.size() != Hv ||
+             p->head_width != config->dims.value_head_dimension))
+            return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH,
+                        "GDN tiled columns must belong to the output projection of this value-head geometry");
     }
     for (auto &v : vecs) {
         ProviderTensor *p = provider_lookup(provider, v.s);
@@ -627,6 +637,7 @@ kq_status kq_b200_gdn_config_bind(kq_gdn_config *config, kq_weight_provider *pro
     }
     for (auto &m : mats) *m.dst = provider_lookup(provider, m.s)->m;
     for (auto &v : vecs) *v.dst = provider_lookup(provider, v.s)->vec_dev;
+    config->gated_head = provider_lookup(provider, t->output)->col_heads_dev;
     config->provider = provider;
     config->bound = true;
     return KQ_STATUS_OK;

@@ -3,6 +3,8 @@
 // Kestrel-Q) over GGUF blocks uploaded once to HBM.
 #include <algorithm>
 #include <cfenv>
+#include <functional>
+#include <string>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -74,6 +76,42 @@ ProviderTensor *provider_lookup(const kq_weight_provider *provider,
     return nullptr;
 }
 
+ProviderTensor *provider_part(const kq_weight_provider *provider, const kq_semantic_tensor *semantic,
+                              kq_binding_part_role part_role) {
+    ProviderTensor *t = provider_lookup(provider, semantic);
+    if (t == nullptr) return nullptr;
+    if (t->parts[0] == nullptr) return part_role == KQ_BINDING_PART_WHOLE ? t : nullptr;
+    if (part_role == KQ_BINDING_PART_INDEX_QUERY) return t->parts[0];
+    if (part_role == KQ_BINDING_PART_INDEX_KEY) return t->parts[1];
+    return nullptr;
+}
+
+namespace {
+
+// Canonical (grouped) index of a GDN value-head-major element -> its
+// position in the model GGUF's tiled order: canonical head g * R + r is
+// stored as head r * Hk + g (src/kq_weight_provider.c:205-211; the
+// converter's reordering, docs/MODEL-GGUF-MAPPING.md of Kestrel-Q).
+uint64_t grouped_to_tiled(uint64_t canonical, uint64_t width, const kq_b200_gguf_layout &g) {
+    const uint64_t group = canonical / (g.gdn_value_repeat * width);
+    const uint64_t within = canonical % (g.gdn_value_repeat * width);
+    const uint64_t repeat = within / width, feature = within % width;
+    return (repeat * g.gdn_key_heads + group) * width + feature;
+}
+
+bool layout_valid(const kq_b200_gguf_layout *g) {
+    return g != nullptr && g->gdn_key_heads > 0 && g->gdn_value_repeat > 0 && g->gdn_head_width > 0 &&
+           (uint64_t)g->gdn_key_heads * g->gdn_value_repeat * g->gdn_head_width <= UINT32_MAX;
+}
+
+// QSA norms the converter stores as 1 + delta (src/kq_weight_provider.c:218-230)
+bool folded_gamma(kq_semantic_role role) {
+    return role == KQ_ROLE_QSA_Q_NORM || role == KQ_ROLE_QSA_K_NORM || role == KQ_ROLE_QSA_INDEX_Q_NORM ||
+           role == KQ_ROLE_QSA_INDEX_K_NORM;
+}
+
+}  // namespace
+
 static ProviderTensor *new_tensor(kq_weight_provider *p, const char *id, kq_semantic_role role) {
     auto t = std::make_unique<ProviderTensor>();
     std::memset(&t->desc, 0, sizeof(t->desc));
@@ -124,8 +162,10 @@ void kq_weight_provider_close(kq_weight_provider *provider) {
     if (provider == nullptr || provider->magic != kProviderMagic) return;
     cudaSetDevice(provider->device);
     cudaDeviceSynchronize();
-    for (auto &t : provider->tensors)
+    for (auto &t : provider->tensors) {
         if (t->owned) cudaFree(t->owned);
+        if (t->col_heads_dev) cudaFree(t->col_heads_dev);
+    }
     provider->magic = 0;
     delete provider;
 }
@@ -257,8 +297,10 @@ kq_status kq_weight_provider_linear_f32(kq_weight_provider *provider,
     ProviderTensor *t = provider_lookup(provider, semantic);
     if (t == nullptr || input == nullptr || output == nullptr)
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, semantic and buffers are required");
-    if (t->is_vector || part_role != KQ_BINDING_PART_WHOLE || expert_id != KQ_WEIGHT_PROVIDER_NO_EXPERT)
-        return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "semantic is not a whole dense matrix");
+    // a split semantic is read by part (src/kq_weight_provider.c:250-262)
+    t = provider_part(provider, semantic, part_role);
+    if (t == nullptr || t->is_vector || expert_id != KQ_WEIGHT_PROVIDER_NO_EXPERT)
+        return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "requested semantic binding part is absent");
     if (rows != t->m.rows || columns != t->m.cols)
         return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "linear shape does not match the semantic");
     if (output_capacity < rows) return fail(diagnostic, KQ_STATUS_BUFFER_TOO_SMALL, "linear output is too small");
@@ -280,7 +322,22 @@ kq_status kq_weight_provider_linear_f32(kq_weight_provider *provider,
     if (st != KQ_STATUS_OK) return st;
     Carve cv(ws);
     const float *x = input;
-    if (!dev_in) {
+    std::vector<float> permuted;
+    if (!t->col_heads.empty()) {
+        // tiled columns: the canonical input goes to the physical column
+        // positions first (src/kq_weight_provider.c:438-451)
+        std::vector<float> canonical(columns);
+        KQB_CUDA(cudaMemcpy(canonical.data(), input, columns * 4, cudaMemcpyDefault), diagnostic, "input read");
+        permuted.resize(columns);
+        const uint64_t w = t->head_width;
+        for (uint64_t h = 0; h < t->col_heads.size(); ++h)
+            std::memcpy(permuted.data() + (uint64_t)t->col_heads[h] * w, canonical.data() + h * w, w * 4);
+        float *p = cv.take<float>(columns);
+        KQB_CUDA(cudaMemcpyAsync(p, permuted.data(), columns * 4, cudaMemcpyHostToDevice, c->stream), diagnostic,
+                 "H2D");
+        KQB_CUDA(cudaStreamSynchronize(c->stream), diagnostic, "H2D");
+        x = p;
+    } else if (!dev_in) {
         float *p = cv.take<float>(columns);
         KQB_CUDA(cudaMemcpyAsync(p, input, columns * 4, cudaMemcpyHostToDevice, c->stream), diagnostic, "H2D");
         x = p;
@@ -313,7 +370,8 @@ kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
     ProviderTensor *t = provider_lookup(provider, semantic);
     if (t == nullptr || x == nullptr || y == nullptr || batch == 0)
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, semantic and buffers are required");
-    if (t->is_vector) return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "semantic is not a matrix");
+    if (t->is_vector || t->parts[0] != nullptr)
+        return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "semantic is not a whole matrix");
     if (rows != t->m.rows || columns != t->m.cols)
         return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "linear shape does not match the semantic");
     if (!is_device_pointer(x) || !is_device_pointer(y))
@@ -327,16 +385,26 @@ kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
     if (st != KQ_STATUS_OK) return st;
     std::lock_guard<std::recursive_mutex> lk(c->mu);
     const size_t partial_floats = projection_workspace_floats(batch, (uint32_t)rows, (uint32_t)columns);
+    const size_t perm_bytes = t->col_heads.empty() ? 0 : Carve::round((size_t)batch * columns * 4);
     void *ws;
-    st = c->workspace(Carve::round(partial_floats * 4) + 256, &ws, diagnostic);
+    st = c->workspace(Carve::round(partial_floats * 4) + perm_bytes + 256, &ws, diagnostic);
     if (st != KQ_STATUS_OK) return st;
+    Carve cv(ws);
+    float *partial = partial_floats ? cv.take<float>(partial_floats) : nullptr;
     ErrorWord err = c->begin_call();
     launch_check_finite(x, (uint64_t)batch * columns, err, c->stream);
+    if (!t->col_heads.empty()) {
+        // tiled columns: the canonical input rows go to the physical column positions
+        float *xp = cv.take<float>((size_t)batch * columns);
+        launch_permute_column_heads(x, batch, (uint32_t)columns, t->head_width, t->col_heads_dev,
+                                    (uint32_t)t->col_heads.size(), xp, c->stream);
+        x = xp;
+    }
     ProjSegments segs{};
     segs.count = 1;
     segs.m[0] = t->m;
-    launch_projection(segs, x, (uint32_t)columns, y, (uint32_t)rows, batch, err, c->stream,
-                      partial_floats ? static_cast<float *>(ws) : nullptr, partial_floats);
+    launch_projection(segs, x, (uint32_t)columns, y, (uint32_t)rows, batch, err, c->stream, partial,
+                      partial_floats);
     KQB_CUDA(cudaGetLastError(), diagnostic, "linear launch");
     provider->metrics.linear_requests += 1;
     return KQ_STATUS_OK;
@@ -357,6 +425,143 @@ kq_status kq_weight_provider_vector_f32(kq_weight_provider *provider,
     if (output_capacity < element_count) return fail(diagnostic, KQ_STATUS_BUFFER_TOO_SMALL, "vector output is too small");
     std::memcpy(output, t->vec_host.data(), element_count * sizeof(float));
     provider->metrics.vector_requests += 1;
+    return KQ_STATUS_OK;
+}
+
+kq_status kq_b200_provider_add_gguf_matrix(kq_weight_provider *provider, const char *semantic_id,
+                                           kq_semantic_role role, uint32_t type_id, uint64_t rows,
+                                           uint64_t columns, const void *packed, uint64_t packed_bytes,
+                                           const kq_b200_gguf_layout *layout,
+                                           const kq_semantic_tensor **out_tensor, kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_tensor) *out_tensor = nullptr;
+    if (!layout_valid(layout) || packed == nullptr || rows == 0 || columns == 0)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid GGUF layout and tensor are required");
+    const kq_b200_gguf_layout &g = *layout;
+    const uint64_t W = g.gdn_head_width, Hv = (uint64_t)g.gdn_key_heads * g.gdn_value_repeat;
+    const uint64_t qk = 2ull * g.gdn_key_heads * W;
+    uint32_t be, bb;
+    if (!block_geometry(type_id, be, bb) || columns % be != 0)
+        return fail(diagnostic, KQ_STATUS_INVALID_QUANTIZED_GEOMETRY, "columns are not whole blocks of the type");
+    const uint64_t row_bytes = columns / be * bb;
+    if (rows > UINT32_MAX || row_bytes > UINT32_MAX || packed_bytes != rows * row_bytes)
+        return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "packed byte count does not match the shape");
+    // canonical row r is stored at physical row phys(r)
+    // (src/kq_weight_provider.c:232-248)
+    std::function<uint64_t(uint64_t)> phys;
+    if (role == KQ_ROLE_GDN_QKV) {
+        if (rows != qk + Hv * W)
+            return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "GDN qkv rows do not match the layout");
+        phys = [&](uint64_t r) { return r < qk ? r : qk + grouped_to_tiled(r - qk, W, g); };
+    } else if (role == KQ_ROLE_GDN_GATE) {
+        if (rows != Hv * W)
+            return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "GDN gate rows do not match the layout");
+        phys = [&](uint64_t r) { return grouped_to_tiled(r, W, g); };
+    } else if (role == KQ_ROLE_GDN_ALPHA || role == KQ_ROLE_GDN_BETA) {
+        if (rows != Hv)
+            return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "GDN alpha/beta rows do not match the layout");
+        phys = [&](uint64_t r) { return grouped_to_tiled(r, 1, g); };
+    }
+    const uint8_t *src = static_cast<const uint8_t *>(packed);
+    std::vector<uint8_t> canonical;
+    if (phys) {
+        canonical.resize(packed_bytes);
+        for (uint64_t r = 0; r < rows; ++r)
+            std::memcpy(canonical.data() + r * row_bytes, src + phys(r) * row_bytes, row_bytes);
+        src = canonical.data();
+    }
+    if (role == KQ_ROLE_GDN_OUT && columns != Hv * W)
+        return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "GDN output columns do not match the layout");
+    const kq_semantic_tensor *desc = nullptr;
+    kq_status st = kq_b200_provider_add_matrix(provider, semantic_id, role, type_id, rows, columns, src,
+                                               packed_bytes, &desc, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    if (role == KQ_ROLE_GDN_OUT) {
+        // tiled columns stay as stored: the operator writes its gated output
+        // in this order and the linear seam permutes its input
+        // (src/kq_weight_provider.c:438-451)
+        ProviderTensor *t = provider_lookup(provider, desc);
+        t->head_width = (uint32_t)W;
+        t->col_heads.resize(Hv);
+        for (uint64_t h = 0; h < Hv; ++h) t->col_heads[h] = (int32_t)(grouped_to_tiled(h * W, W, g) / W);
+        KQB_CUDA(cudaMalloc(&t->col_heads_dev, Hv * sizeof(int32_t)), diagnostic, "column head map");
+        KQB_CUDA(cudaMemcpy(t->col_heads_dev, t->col_heads.data(), Hv * sizeof(int32_t), cudaMemcpyHostToDevice),
+                 diagnostic, "column head map");
+    }
+    *out_tensor = desc;
+    return KQ_STATUS_OK;
+}
+
+kq_status kq_b200_provider_add_gguf_vector_f32(kq_weight_provider *provider, const char *semantic_id,
+                                               kq_semantic_role role, const float *values, uint64_t count,
+                                               const kq_b200_gguf_layout *layout,
+                                               const kq_semantic_tensor **out_tensor, kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_tensor) *out_tensor = nullptr;
+    if (!layout_valid(layout) || values == nullptr || count == 0 || count > (1ull << 28))
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid GGUF layout and values are required");
+    const kq_b200_gguf_layout &g = *layout;
+    const uint64_t W = g.gdn_head_width, Hv = (uint64_t)g.gdn_key_heads * g.gdn_value_repeat;
+    const uint64_t qk = 2ull * g.gdn_key_heads * W;
+    std::vector<float> out(values, values + count);
+    // src/kq_weight_provider.c:680-717
+    if (role == KQ_ROLE_GDN_A_LOG || role == KQ_ROLE_GDN_DT_BIAS) {
+        if (count != Hv)
+            return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "GDN per-head vector does not match the layout");
+        for (uint64_t i = 0; i < count; ++i) {
+            const float v = values[grouped_to_tiled(i, 1, g)];
+            // A_log is stored as -exp(A_log)
+            out[i] = role == KQ_ROLE_GDN_A_LOG ? logf(-v) : v;
+            if (!std::isfinite(out[i]))
+                return fail(diagnostic, KQ_STATUS_NUMERIC_DOMAIN, "stored GDN A_log must be negative and finite");
+        }
+    } else if (role == KQ_ROLE_GDN_CONV) {
+        if (count % 4 != 0 || count / 4 != qk + Hv * W)
+            return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "GDN conv channels do not match the layout");
+        for (uint64_t c = 0; c < count / 4; ++c) {
+            const uint64_t p = c < qk ? c : qk + grouped_to_tiled(c - qk, W, g);
+            std::memcpy(out.data() + c * 4, values + p * 4, 4 * sizeof(float));
+        }
+    } else if (folded_gamma(role)) {
+        for (uint64_t i = 0; i < count; ++i) out[i] = values[i] - 1.0f;   // stored as 1 + delta
+    }
+    return kq_b200_provider_add_vector_f32(provider, semantic_id, role, out.data(), count, out_tensor, diagnostic);
+}
+
+kq_status kq_b200_provider_add_index_qk(kq_weight_provider *provider, const char *semantic_id, uint32_t type_id,
+                                        uint64_t query_rows, uint64_t key_rows, uint64_t columns,
+                                        const void *query_packed, uint64_t query_bytes, const void *key_packed,
+                                        uint64_t key_bytes, const kq_semantic_tensor **out_tensor,
+                                        kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_tensor) *out_tensor = nullptr;
+    if (provider == nullptr || provider->magic != kProviderMagic || out_tensor == nullptr)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider and output are required");
+    const kq_semantic_tensor *q = nullptr, *k = nullptr;
+    const std::string base = semantic_id ? semantic_id : "index_qk";
+    kq_status st = kq_b200_provider_add_matrix(provider, (base + ".index_query").c_str(), KQ_ROLE_QSA_INDEX_QK,
+                                               type_id, query_rows, columns, query_packed, query_bytes, &q,
+                                               diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    st = kq_b200_provider_add_matrix(provider, (base + ".index_key").c_str(), KQ_ROLE_QSA_INDEX_QK, type_id, key_rows,
+                                     columns, key_packed, key_bytes, &k, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    // one semantic, two bindings: INDEX_QUERY (part 0 of 2), INDEX_KEY
+    // (part 1 of 2), the order src/kq_qsa.c:184-201 requires
+    ProviderTensor *t = new_tensor(provider, semantic_id, KQ_ROLE_QSA_INDEX_QK);
+    t->parts[0] = provider_lookup(provider, q);
+    t->parts[1] = provider_lookup(provider, k);
+    t->desc.canonical_rank = 2;
+    t->desc.canonical_dimensions[0] = query_rows + key_rows;
+    t->desc.canonical_dimensions[1] = columns;
+    t->desc.binding_count = 2;
+    t->desc.bindings[0].part_role = KQ_BINDING_PART_INDEX_QUERY;
+    t->desc.bindings[0].part_index = 0;
+    t->desc.bindings[0].part_count = 2;
+    t->desc.bindings[1].part_role = KQ_BINDING_PART_INDEX_KEY;
+    t->desc.bindings[1].part_index = 1;
+    t->desc.bindings[1].part_count = 2;
+    *out_tensor = &t->desc;
     return KQ_STATUS_OK;
 }
 

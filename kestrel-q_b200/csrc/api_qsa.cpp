@@ -851,18 +851,31 @@ kq_status kq_b200_qsa_config_bind(kq_qsa_config *config, kq_weight_provider *pro
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid config, provider and tensors are required");
     const kq_qsa_dimensions &d = config->dims;
     const uint32_t H = d.hidden_size, qw = d.query_head_count * d.head_dimension, kvw = (uint32_t)config->kv_per_token;
-    struct M { const kq_semantic_tensor *s; uint32_t rows, cols; QMatrix *dst; } mats[6] = {
-        {t->query, 2 * qw, H, &config->q}, {t->key, kvw, H, &config->k}, {t->value, kvw, H, &config->v},
-        {t->output, H, qw, &config->o}, {t->index_query, d.index_query_head_count * d.index_head_dimension, H, &config->iq},
-        {t->index_key, d.index_head_dimension, H, &config->ik}};
+    // the index projections may be one split semantic (INDEX_QUERY and
+    // INDEX_KEY parts, src/kq_qsa.c:184-201) or two whole ones
+    struct M { const kq_semantic_tensor *s; uint32_t rows, cols; QMatrix *dst; kq_binding_part_role part; } mats[6] = {
+        {t->query, 2 * qw, H, &config->q, KQ_BINDING_PART_WHOLE},
+        {t->key, kvw, H, &config->k, KQ_BINDING_PART_WHOLE},
+        {t->value, kvw, H, &config->v, KQ_BINDING_PART_WHOLE},
+        {t->output, H, qw, &config->o, KQ_BINDING_PART_WHOLE},
+        {t->index_query, d.index_query_head_count * d.index_head_dimension, H, &config->iq,
+         KQ_BINDING_PART_INDEX_QUERY},
+        {t->index_key, d.index_head_dimension, H, &config->ik, KQ_BINDING_PART_INDEX_KEY}};
+    auto matrix = [&](const M &m) -> ProviderTensor * {
+        ProviderTensor *p = provider_lookup(provider, m.s);
+        if (p != nullptr && p->parts[0] != nullptr) return provider_part(provider, m.s, m.part);
+        return p;
+    };
     struct V { const kq_semantic_tensor *s; uint64_t count; const float **dst; } vecs[4] = {
         {t->query_norm, d.head_dimension, &config->q_norm}, {t->key_norm, d.head_dimension, &config->k_norm},
         {t->index_query_norm, d.index_head_dimension, &config->iq_norm},
         {t->index_key_norm, d.index_head_dimension, &config->ik_norm}};
     for (auto &m : mats) {
-        ProviderTensor *p = provider_lookup(provider, m.s);
+        ProviderTensor *p = matrix(m);
         if (p == nullptr || p->is_vector)
             return fail(diagnostic, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "required QSA semantic tensor is missing");
+        if (!p->col_heads.empty())
+            return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "QSA tensors keep canonical columns");
         if (p->m.rows != m.rows || p->m.cols != m.cols)
             return fail(diagnostic, KQ_STATUS_INCOMPATIBLE_QSA, "QSA canonical tensor shape mismatch");
     }
@@ -873,7 +886,7 @@ kq_status kq_b200_qsa_config_bind(kq_qsa_config *config, kq_weight_provider *pro
         if (p->vec_host.size() != v.count)
             return fail(diagnostic, KQ_STATUS_INCOMPATIBLE_QSA, "QSA canonical tensor shape mismatch");
     }
-    for (auto &m : mats) *m.dst = provider_lookup(provider, m.s)->m;
+    for (auto &m : mats) *m.dst = matrix(m)->m;
     for (auto &v : vecs) *v.dst = provider_lookup(provider, v.s)->vec_dev;
     config->provider = provider;
     config->bound = true;

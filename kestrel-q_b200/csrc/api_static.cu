@@ -104,6 +104,9 @@ kq_status kq_b200_provider_linear_batch_f32_static(kq_weight_provider *provider,
     if (t == nullptr || x == nullptr || y == nullptr || batch == 0)
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, semantic and buffers are required");
     if (t->is_vector) return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "semantic is not a matrix");
+    if (t->parts[0] != nullptr || !t->col_heads.empty())
+        return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH,
+                    "the allocation-free linear takes whole tensors with canonical columns");
     if (rows != t->m.rows || columns != t->m.cols)
         return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "linear shape does not match the semantic");
     if (!is_device_pointer(x) || !is_device_pointer(y))

@@ -159,6 +159,10 @@ void launch_row_dot(uint32_t type, const uint8_t *packed, uint64_t elements,
                     cudaStream_t stream);
 void launch_check_finite(const float *x, uint64_t count, ErrorWord err,
                          cudaStream_t stream);
+// y[b][heads[h] * width + f] = x[b][h * width + f] for the `nheads` heads of
+// each of `batch` rows of `cols` values (canonical -> tiled column order).
+void launch_permute_column_heads(const float *x, uint32_t batch, uint32_t cols, uint32_t width,
+                                 const int32_t *heads, uint32_t nheads, float *y, cudaStream_t stream);
 // y[t][i] = x[t][i] * (float)mask[t] (padding mask of src/kq_gdn_qwen38.c:548-553)
 void launch_mask_rows(const float *x, const uint8_t *mask, uint32_t rows,
                       uint32_t cols, float *y, cudaStream_t stream);
@@ -181,7 +185,19 @@ struct GdnBatchPtrs {
 
 struct GdnWeightsDev {
     const float *a_log, *conv, *dt_bias, *norm;
+    // The output projection's column order, by value head: the gated output
+    // of canonical head h is stored at head position gated_head[h] (a model
+    // GGUF keeps GDN value heads in tiled order, so its out-projection reads
+    // its input in that order); null: canonical order.
+    const int32_t *gated_head = nullptr;
 };
+
+#ifdef __CUDACC__
+// Head position of value head h in the gated output.
+__device__ __forceinline__ uint32_t gated_head_pos(const GdnWeightsDev &w, uint32_t h) {
+    return w.gated_head != nullptr ? (uint32_t)w.gated_head[h] : h;
+}
+#endif
 
 // proj: [B*T][ldp] (qkv | gate | beta | alpha), item = b*T + t.
 // `logdecay` (may be null) receives g as well as decay = exp(g).
@@ -214,7 +230,8 @@ struct GdnDebugBufs {
     float *q_norm, *k_norm;       // [Hv][dk] normalised (q also scaled by 1/sqrt(dk))
     float *log_decay, *beta;      // [Hv]
     float *read, *delta, *core;   // [Hv][dv] recurrence read, delta and output
-    float *gated;                 // [Hv][dv] gated RMSNorm output
+    float *gated;                 // [Hv][dv] gated RMSNorm output, canonical head order
+    float *gated_proj;            // the same in the out-projection's head order (may equal gated)
 };
 void launch_gdn_debug_token(const GdnDims &d, const GdnWeightsDev &w, const float *conv_in, float *conv_out,
                             const float *rec_in, float *rec_out, const float *proj, const GdnDebugBufs &b,

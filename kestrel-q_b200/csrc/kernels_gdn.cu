@@ -372,7 +372,7 @@ gdn_recurrence128_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t to
             float z = proj[item * ldp + d.conv_channels + h * kDim + threadIdx.x];
             float g = (w.norm[threadIdx.x] * (o * inv)) * stable_sigmoid(z);
             bad |= !isfinite(g);
-            gated[item * d.value_width + h * kDim + threadIdx.x] = g;
+            gated[item * d.value_width + gated_head_pos(w, h) * kDim + threadIdx.x] = g;
         }
         // part/ks/qs are rewritten next token only after the barrier inside
         // block_sum's successor __syncthreads at the loop head
@@ -514,7 +514,7 @@ gdn_decode_fused_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, const float 
             float z = prow[d.conv_channels + h * kDim + threadIdx.x];
             float g = (w.norm[threadIdx.x] * (o * inv)) * stable_sigmoid(z);
             bad |= !isfinite(g);
-            gated[(size_t)b * d.value_width + h * kDim + threadIdx.x] = g;
+            gated[(size_t)b * d.value_width + gated_head_pos(w, h) * kDim + threadIdx.x] = g;
         }
     }
 #pragma unroll
@@ -652,6 +652,7 @@ gdn_debug_token_kernel(GdnDims d, GdnWeightsDev w, const float *__restrict__ con
         const float z = proj[d.conv_channels + h * dv + f];
         const float g = __fmul_rn(__fmul_rn(w.norm[f], __fmul_rn(sc[f], inv[0])), stable_sigmoid(z));
         o.gated[(size_t)h * dv + f] = g;
+        o.gated_proj[(size_t)gated_head_pos(w, h) * dv + f] = g;
         bad |= !isfinite(g);
     }
     if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
@@ -733,7 +734,7 @@ gdn_recurrence_generic_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32
             float z = proj[item * ldp + d.conv_channels + h * dv + f];
             float g = (w.norm[f] * (outs[n] * inv)) * stable_sigmoid(z);
             bad |= !isfinite(g);
-            gated[item * d.value_width + h * dv + f] = g;
+            gated[item * d.value_width + gated_head_pos(w, h) * dv + f] = g;
         }
         __syncthreads();
     }

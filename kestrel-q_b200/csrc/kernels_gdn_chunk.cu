@@ -523,7 +523,7 @@ gdn_gate_norm_kernel(GdnDims d, GdnWeightsDev w, const float *__restrict__ obuf,
     const float4 g = make_float4((nw.x * (o.x * inv)) * chunk_sigmoid(z.x), (nw.y * (o.y * inv)) * chunk_sigmoid(z.y),
                                  (nw.z * (o.z * inv)) * chunk_sigmoid(z.z), (nw.w * (o.w * inv)) * chunk_sigmoid(z.w));
     if (!isfinite(g.x) || !isfinite(g.y) || !isfinite(g.z) || !isfinite(g.w)) chunk_raise(err, kErrNonFinite);
-    *reinterpret_cast<float4 *>(gated + (size_t)t * d.value_width + h * kD + 4 * lane) = g;
+    *reinterpret_cast<float4 *>(gated + (size_t)t * d.value_width + gated_head_pos(w, h) * kD + 4 * lane) = g;
 }
 
 void launch_gdn_chunked(const GdnDims &d, const GdnWeightsDev &w, const GdnBatchPtrs &p, uint32_t tokens,

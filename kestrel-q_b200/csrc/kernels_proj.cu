@@ -550,6 +550,25 @@ __global__ void check_finite_kernel(const float *x, uint64_t count, ErrorWord er
     if (__syncthreads_or(bad) && threadIdx.x == 0) raise_error(err, kErrNonFinite);
 }
 
+__global__ void permute_column_heads_kernel(const float *__restrict__ x, uint32_t batch, uint32_t cols,
+                                            uint32_t width, const int32_t *__restrict__ heads, uint32_t nheads,
+                                            float *__restrict__ y) {
+    pdl_wait();
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)batch * nheads * width) return;
+    const uint64_t b = i / ((uint64_t)nheads * width);
+    const uint32_t h = (uint32_t)(i / width % nheads), f = (uint32_t)(i % width);
+    y[b * cols + (uint64_t)heads[h] * width + f] = x[b * cols + (uint64_t)h * width + f];
+}
+
+void launch_permute_column_heads(const float *x, uint32_t batch, uint32_t cols, uint32_t width,
+                                 const int32_t *heads, uint32_t nheads, float *y, cudaStream_t stream) {
+    const uint64_t n = (uint64_t)batch * nheads * width;
+    launch_pdl(permute_column_heads_kernel, (unsigned)((n + 255) / 256), 256, 0, stream, x, batch, cols, width,
+               heads, nheads, y);
+    count_launch();
+}
+
 void launch_check_finite(const float *x, uint64_t count, ErrorWord err,
                          cudaStream_t stream) {
     uint64_t blocks = std::min<uint64_t>((count + 255) / 256, 1184);

@@ -19,7 +19,22 @@ struct ProviderTensor {
     std::vector<float> vec_host;
     uint64_t bytes = 0;
     void *owned = nullptr;
+    // A GDN output projection kept in the model GGUF's tiled column order:
+    // column head position of every canonical value head (host and device
+    // copies, width `head_width`), empty for canonical columns.
+    std::vector<int32_t> col_heads;
+    int32_t *col_heads_dev = nullptr;
+    uint32_t head_width = 0;
+    // A semantic stored as two separate tensors (the QSA index projection:
+    // INDEX_QUERY then INDEX_KEY part), each its own record.
+    ProviderTensor *parts[2] = {nullptr, nullptr};
 };
+
+// The record of `semantic`'s binding part `part_role`: the semantic itself
+// for a whole tensor (part_role WHOLE), one of its parts for a split one;
+// nullptr when the part does not exist.
+ProviderTensor *provider_part(const kq_weight_provider *provider, const kq_semantic_tensor *semantic,
+                              kq_binding_part_role part_role);
 
 struct kq_weight_provider {
     uint32_t magic = kProviderMagic;

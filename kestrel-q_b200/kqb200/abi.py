@@ -105,6 +105,10 @@ class QsaSelection(C.Structure):
                 ("selected_token_count", u64), ("tail_count", u64)]
 
 
+class GgufLayout(C.Structure):   # include/kq_b200.h kq_b200_gguf_layout
+    _fields_ = [("gdn_key_heads", u32), ("gdn_value_repeat", u32), ("gdn_head_width", u32)]
+
+
 class GdnCheckpoint(C.Structure):   # include/kq_gdn.h kq_gdn_checkpoint
     _fields_ = [("kind", C.c_int), ("token_index", u64), ("rank", u32), ("dimensions", u64 * 4),
                 ("values", C.POINTER(f32)), ("value_count", u64)]
@@ -157,6 +161,12 @@ _SIGNATURES = {
     "kq_b200_provider_add_matrix": (C.c_int, [vp, C.c_char_p, C.c_int, u32, u64, u64, vp, u64,
                                               C.POINTER(vp), vp]),
     "kq_b200_provider_add_vector_f32": (C.c_int, [vp, C.c_char_p, C.c_int, vp, u64, C.POINTER(vp), vp]),
+    "kq_b200_provider_add_gguf_matrix": (C.c_int, [vp, C.c_char_p, C.c_int, u32, u64, u64, vp, u64,
+                                                   C.POINTER(GgufLayout), C.POINTER(vp), vp]),
+    "kq_b200_provider_add_gguf_vector_f32": (C.c_int, [vp, C.c_char_p, C.c_int, vp, u64, C.POINTER(GgufLayout),
+                                                       C.POINTER(vp), vp]),
+    "kq_b200_provider_add_index_qk": (C.c_int, [vp, C.c_char_p, u32, u64, u64, u64, vp, u64, vp, u64,
+                                                C.POINTER(vp), vp]),
     "kq_weight_provider_linear_f32": (C.c_int, [vp, vp, C.c_int, u32, u64, u64, vp, vp, u64, vp, u64, vp]),
     "kq_weight_provider_vector_f32": (C.c_int, [vp, vp, u64, vp, u64, vp, u64, vp]),
     "kq_b200_provider_linear_batch_f32": (C.c_int, [vp, vp, u64, u64, vp, u32, vp, vp]),
