@@ -221,9 +221,23 @@ kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *
         src = planar.data();
         layout = 1;
     }
+    const int32_t scale_exp =
+        weight_scale_exponent(weight_abs_bound(type_id, static_cast<const uint8_t *>(packed), rows, row_bytes));
+    // Q4_K: the factored tensor-core kernel's per-super-block side data
+    // (kernels.hpp q4k_build_aux) follows the blocks in the same allocation
+    const uint64_t aux_offset = (total + 255) & ~uint64_t(255);
+    std::vector<uint8_t> aux;
+    if (type_id == KQ_GGUF_TYPE_Q4_K) {
+        aux.resize(q4k_aux_bytes((uint32_t)rows, (uint32_t)columns));
+        q4k_build_aux(static_cast<const uint8_t *>(packed), (uint32_t)rows, (uint32_t)columns, scale_exp,
+                      aux.data());
+    }
+    const uint64_t alloc = aux.empty() ? total : aux_offset + aux.size();
     void *dev = nullptr;
-    KQB_CUDA(cudaMalloc(&dev, total), diagnostic, "weight allocation");
+    KQB_CUDA(cudaMalloc(&dev, alloc), diagnostic, "weight allocation");
     cudaError_t e = cudaMemcpy(dev, src, total, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && !aux.empty())
+        e = cudaMemcpy(static_cast<uint8_t *>(dev) + aux_offset, aux.data(), aux.size(), cudaMemcpyHostToDevice);
     // a pageable upload may return before its DMA lands; the library's
     // streams do not wait for the legacy stream, so finish it here
     if (e == cudaSuccess) e = cudaStreamSynchronize(cudaStreamLegacy);
@@ -233,19 +247,19 @@ kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *
     }
     ProviderTensor *t = new_tensor(provider, semantic_id, role);
     t->owned = dev;
-    t->bytes = total;
+    t->bytes = total;   // logical payload (the side data is not part of it)
     t->m.data = static_cast<const uint8_t *>(dev);
     t->m.type = type_id;
     t->m.rows = (uint32_t)rows;
     t->m.cols = (uint32_t)columns;
     t->m.row_bytes = (uint32_t)row_bytes;
     t->m.layout = layout;
-    t->m.scale_exp = weight_scale_exponent(
-        weight_abs_bound(type_id, static_cast<const uint8_t *>(packed), rows, row_bytes));
+    t->m.scale_exp = scale_exp;
+    t->m.aux = aux.empty() ? nullptr : static_cast<const uint8_t *>(dev) + aux_offset;
     t->desc.canonical_rank = 2;
     t->desc.canonical_dimensions[0] = rows;
     t->desc.canonical_dimensions[1] = columns;
-    provider->metrics.provider_owned_bytes += total;
+    provider->metrics.provider_owned_bytes += alloc;
     *out_tensor = &t->desc;
     return KQ_STATUS_OK;
 }

@@ -93,7 +93,22 @@ struct QMatrix {
     uint32_t row_bytes;
     uint32_t layout;
     int32_t scale_exp;
+    // Q4_K only (may be null): per-super-block side data of the factored
+    // tensor-core kernel, built at upload by q4k_build_aux.
+    const uint8_t *aux = nullptr;
 };
+
+// Q4_K side data, per row and super-block sb (pitches padded to groups of 4
+// super-blocks):
+//   plane A  [rows][q4k_aux_pitch_a]  16 fp16 at byte 32*sb: dmin*m_s*2^e
+//            rounded to fp16 (s = 0..7), then the 8 residuals (exact F32
+//            minus the rounded value, rounded to fp16)
+//   plane D  [rows][q4k_aux_pitch_d]  F32 d at byte 4*sb
+// e = scale_exp.  Plane D follows plane A at offset rows * pitch_a.
+uint32_t q4k_aux_pitch_a(uint32_t cols);
+uint32_t q4k_aux_pitch_d(uint32_t cols);
+size_t q4k_aux_bytes(uint32_t rows, uint32_t cols);
+void q4k_build_aux(const uint8_t *packed, uint32_t rows, uint32_t cols, int32_t scale_exp, uint8_t *out);
 
 // Power-of-two exponent e for a matrix whose decoded values are bounded by
 // |w| <= bound: bound * 2^e < 2^14, clamped to [-64, 64] (0 for a zero or

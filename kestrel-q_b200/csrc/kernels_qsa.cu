@@ -1345,7 +1345,7 @@ __device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, vol
     uint32_t ok = 1;
     if ((threadIdx.x & 31) == 0) {
         const uint32_t a = tc_smem(bar);
-        const uint64_t t0 = tc_now();
+        uint64_t t0 = 0;   // the clock is read only once a wait is slow
         ok = 0;
         for (uint32_t i = 0; i < kTcWaitPolls; ++i) {
             if (tc_poll(a, parity)) {
@@ -1354,7 +1354,9 @@ __device__ __forceinline__ bool tc_wait_warp(uint64_t *bar, uint32_t parity, vol
             }
             if ((i & 63u) == 63u) {
                 if (*abort_flag) break;
-                if (tc_now() - t0 > kTcWaitNs) {
+                const uint64_t now = tc_now();
+                if (t0 == 0) t0 = now;
+                else if (now - t0 > kTcWaitNs) {
                     atomicCAS(const_cast<uint32_t *>(abort_flag), 0u, kTcWaitSite);
                     break;
                 }

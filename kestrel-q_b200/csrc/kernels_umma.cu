@@ -55,6 +55,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -89,6 +90,7 @@ constexpr uint32_t kTmemCols = 512;
 // beyond 65504.  The epilogue multiplies by 2^(2 - scale_exp).
 constexpr float kXScale = 0.25f;
 constexpr float kXRangeLimit = 262016.0f;
+constexpr uint32_t kXmSlotBytes = 16384;   // minimum-term activation tile (factored kernel)
 
 // Geometry of a tile of NT batch rows.
 //  NT = 64: TMEM columns [0, 128) hold the accumulator: wh * [xh | xl]
@@ -117,7 +119,8 @@ constexpr uint64_t kWaitNs = 2000000000ull;          // or 2 s of global time, w
 // Wait sites, recorded in the abort flag by the first wait that gives up
 // and reported in the error code (kErrTimeout | site << 8).
 enum WaitSite : uint32_t {
-    kSiteRawFree = 1, kSiteXFree, kSiteAReady, kSiteXFull, kSiteRawFull, kSiteADone, kSiteAccum
+    kSiteRawFree = 1, kSiteXFree, kSiteAReady, kSiteXFull, kSiteRawFull, kSiteADone, kSiteAccum,
+    kSiteDFree, kSiteDFull, kSiteXmFull, kSiteXmFree, kSiteScale
 };
 
 __device__ __forceinline__ uint64_t global_ns() {
@@ -140,7 +143,7 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile uint32_t *abort,
                                           uint32_t site) {
     const uint32_t addr = smem_u32(bar);
-    const uint64_t t0 = global_ns();
+    uint64_t t0 = 0;   // the clock is read only once a wait is slow
     for (uint32_t i = 0; i < kWaitLimit; ++i) {
         uint32_t done;
         asm volatile(
@@ -153,7 +156,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         if (done) return true;
         if ((i & 63u) == 63u) {
             if (*abort) return false;
-            if (global_ns() - t0 > kWaitNs) break;
+            const uint64_t now = global_ns();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > kWaitNs) break;
         }
     }
     atomicCAS(const_cast<uint32_t *>(abort), 0u, site);
@@ -287,11 +292,6 @@ __device__ __forceinline__ void unf2(uint64_t v, float &a, float &b) {
 __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
     uint64_t r;
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
     return r;
 }
 
@@ -456,6 +456,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
                  ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
@@ -476,10 +482,15 @@ struct TmapSet {
 // Activations x 2^-2 to fp16 hi/lo tiles in the MMA's shared-memory image:
 // out[btile][chunk] = { hi: NT rows x 128 B swizzled, lo: same }.
 // One CTA converts 16 rows of one chunk; one thread 8 values.
+// With `xm` (64-row tiles whose weights include Q4_K), also the minimum-term
+// tiles of the factored kernel: per batch tile and group of 4 super-blocks a
+// 128-row SW128 image whose K step u (16 values) holds, for super-block 4g+u
+// and batch row r, [Xh_0..7 | Xh_0..7] in row r and [Xl_0..7 | 0] in row
+// 64 + r, X_s = (sum of sub-block s's 32 values of x / 4) / 32.
 template <uint32_t NT>
 __global__ void __launch_bounds__(128)
 xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t cols, uint32_t nchunks,
-             uint8_t *__restrict__ out, ErrorWord err) {
+             uint8_t *__restrict__ out, uint8_t *__restrict__ xm, uint32_t nxm, ErrorWord err) {
     pdl_wait();
     constexpr uint32_t kGroups = NT / 16u;
     const uint32_t c = blockIdx.x / kGroups, bt = blockIdx.y;
@@ -508,6 +519,28 @@ xconv_kernel(const float *__restrict__ x, uint32_t ldx, uint32_t batch, uint32_t
         atomicCAS(err.word, 0ull, ((unsigned long long)kErrNonFinite << 32) | err.call_id);
     if (__any_sync(0xffffffffu, big) && (threadIdx.x & 31) == 0)
         atomicCAS(err.word, 0ull, ((unsigned long long)kErrRange << 32) | err.call_id);
+    if (NT == kUN && xm != nullptr) {
+        // sub-block of 32 = 4 neighbouring lanes (q8 0..3 or 4..7 of a row)
+        float t = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t = __fadd_rn(t, v[i]);
+        t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+        t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 2));
+        if ((q8 & 3u) == 0) {
+            uint32_t h, l;
+            split_f16(__fmul_rn(t, 0.03125f), 0.0f, h, l);
+            const uint32_t sb = c >> 2, s = 2u * (c & 3u) + (q8 >> 2), ks = (sb & 3u) * 16u + s;
+            uint8_t *mt = xm + ((size_t)bt * nxm + (sb >> 2)) * kXmSlotBytes;
+            auto at = [](uint32_t R, uint32_t k) {   // fp16 element k of row R, SW128
+                const uint32_t byte = 2u * k;
+                return R * 128u + ((((byte >> 4) ^ (R & 7u))) << 4) + (byte & 15u);
+            };
+            *reinterpret_cast<uint16_t *>(mt + at(r, ks)) = (uint16_t)h;
+            *reinterpret_cast<uint16_t *>(mt + at(r, ks + 8u)) = (uint16_t)h;
+            *reinterpret_cast<uint16_t *>(mt + at(64u + r, ks)) = (uint16_t)l;
+            *reinterpret_cast<uint16_t *>(mt + at(64u + r, ks + 8u)) = 0;
+        }
+    }
     uint4 hi, lo;
     pack8(v, hi, lo);
     uint8_t *tile = out + ((size_t)bt * nchunks + c) * Tile<NT>::xslot;
@@ -825,6 +858,622 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     }
 }
 
+// ---- factored-scale projection (Q4_K, Q6_K; batch tiles of 64)
+//
+// The kernel above turns every weight into F32 and splits it into two fp16
+// terms: about 15 instructions per weight on the CUDA cores.  A K-quant
+// weight is a small integer times per-block scales, so the scales can leave
+// the MMA operand:
+//   Q4_K  w = d*sc_s*q - dmin*m_s   (s: sub-block of 32; sc, m 6-bit; q 4-bit)
+//         sum_k w x = sum_sb d_sb * sum_{k in sb} (sc*q) x
+//                     - sum_{sb,s} (dmin*m_s) * X_s,  X_s = sum of the
+//         sub-block's 32 activations.  sc*q <= 945 is an exact fp16
+//         integer: one A term.
+//   Q6_K  w = d*sc_s*(q - 32)       (s: sub-block of 16; sc int8; q 6-bit)
+//         sc*(q - 32) lies in [-4096, 4096] and needs up to 12 bits:
+//         A = RN16(sc*(q - 32)) plus its residual e in {-1, 0, 1} (exact
+//         fp16 FMA): two A terms.
+// The activations keep the fp16 hi/lo split of x / 4.  The MMAs of one
+// super-block (256 K) accumulate A*[xh | xl] (Q6_K also e*xh) into one of
+// two TMEM accumulators; epilogue warps add the halves, scale by the
+// super-block's d and accumulate in F32 registers while the MMAs of the next
+// super-block run into the other accumulator.  Q4_K's minimum term is a
+// second, K/32-sized product accumulated over the CTA's whole K range:
+// A' = dmin*m*2^scale_exp (17 significant bits, exact as fp16 hi | lo over
+// the 8 sub-blocks = one K step of 16) times X/32 as [Xh | Xh] and [Xl | 0]
+// (two N = 64 MMAs; tiles written by the activation kernel).  A' and the
+// F32 d of every super-block are built once at upload (q4k_build_aux) and
+// arrive by TMA, 4 super-blocks per tile, with the minimum-term activations.
+//
+// Decode: Q4_K one PRMT per two weights (a nibble pair as fp16 1024 + q) and
+// one fp16 FMA ((1024 + q)*sc - 1024*sc = sc*q, exact); Q6_K one PRMT, one
+// subtraction (q - 32), one multiply (RN) and one FMA (residual) per pair.
+//
+// Pipelining.  mbarrier operations by many warps on one barrier serialise
+// (measured: hundreds of cycles per hand-off with 16 arriving warps), so
+// each role group meets on a hardware named barrier and one leader thread
+// does the group's single mbarrier wait and arrive.  The ring works in units
+// of U chunks of 64 K; each unit has ONE readiness barrier (the decode
+// leader + the TMA's activation bytes) and ONE consumed barrier (the MMA
+// commit that frees both its A buffer and its activation slot), so the
+// activation ring has as many slots as there are A buffers.
+//
+// Warp roles (864 threads, one CTA per SM):
+//   0       TMEM owner; weight producer (raw super-blocks and the Q4_K group
+//           tiles), which runs up to three super-blocks ahead
+//   1       MMA issue
+//   2       activation producer (one unit per slot, gated by the MMAs), kept
+//           apart from the weight loads so that their HBM latency stays hidden
+//   3..18   decode: lane = weight row in TMEM quarter (warp & 3), 16 K values
+//           of each chunk of 64 (the layout of the kernel above)
+//   19..26  epilogue: lane = weight row, 32 of the 64 batch columns
+// TMEM columns: accumulators 2 x 128 at 0.  Q4_K: minimum term 64 at 256,
+// three A buffers of 2 x 32 at 320.  Q6_K: A buffers of U x (32 RN + 32
+// residual) at 256.
+constexpr int kFTmaWarp = 0;      // weight producer; also owns TMEM
+constexpr int kFAllocWarp = 0;
+constexpr int kFMmaWarp = 1;
+constexpr int kFXWarp = 2;        // activation producer
+constexpr int kFDecode0 = 3;      // first decode warp
+constexpr int kFDecodeWarps = 16;
+constexpr int kFEpi0 = kFDecode0 + kFDecodeWarps;
+constexpr int kFEpiWarps = 8;
+constexpr int kFThreads = (kFEpi0 + kFEpiWarps) * 32;
+constexpr uint32_t kXmSlot = kXmSlotBytes;   // 4 super-blocks x 16 K, 128 rows
+constexpr uint32_t kMlSlot = 16384;          // Q4_K A': 128 rows x 4 super-blocks x 16 K
+constexpr uint32_t kDgSlot = 2048;           // Q4_K d: 128 rows x 4 super-blocks, F32
+
+template <uint32_t T> struct Fact {
+    static constexpr bool q4 = T == kTypeQ4_K;
+    static constexpr uint32_t U = 2u;                           // chunks per unit
+    static constexpr uint32_t kU = q4 ? 3u : 2u;                // units in flight
+    static constexpr uint32_t dm = 256u;                        // Q4_K minimum term (64 columns)
+    static constexpr uint32_t abase = q4 ? 320u : 256u;
+    static constexpr uint32_t ecols = q4 ? 0u : U * 32u;        // residual offset in a buffer
+    static constexpr uint32_t astride = q4 ? U * 32u : U * 64u;
+    static constexpr uint32_t raw = TypeCfg<T>::raw;
+    static constexpr uint32_t rr = 3u;
+    static constexpr uint32_t xm = q4 ? 2u : 0u;                // minimum-term activation tiles
+    static constexpr uint32_t ml = q4 ? 2u : 0u;                // A' tiles
+    static constexpr uint32_t dg = q4 ? 2u : 0u;                // d tiles
+    static constexpr uint32_t xslot = U * Tile<kUN>::xslot;     // one unit of activations
+    static constexpr uint32_t smem =
+        rr * raw + xm * kXmSlot + ml * kMlSlot + dg * kDgSlot + kU * xslot + 1024u;
+    static_assert(abase + kU * astride <= kTmemCols, "TMEM budget");
+    static_assert(smem <= 227u * 1024u - 4096u, "shared memory per CTA");
+    static_assert(kUM * kUN * 4u <= kU * xslot, "exchange tile");
+    static_assert(4u % U == 0u, "units tile a super-block");
+};
+
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+// Scale and minimum (6-bit each) of Q4_K sub-block j (0..7) from the
+// super-block header (d, dmin, 12 packed bytes).
+__device__ __forceinline__ void q4k_scale_min(const uint4 &hdr, uint32_t j, uint32_t &sc, uint32_t &mn) {
+    auto sbyte = [&](uint32_t k) { return (word_of(hdr, 1u + (k >> 2)) >> (8u * (k & 3u))) & 0xFFu; };
+    if (j < 4) {
+        sc = sbyte(j) & 63u;
+        mn = sbyte(j + 4) & 63u;
+    } else {
+        sc = (sbyte(j + 4) & 15u) | ((sbyte(j - 4) >> 6) << 4);
+        mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
+    }
+}
+
+// The integer A operand of the 16 values [16q, 16q + 16) of chunk c of one
+// staged row (same staging as decode16), as fp16 pairs: Q4_K sc*q in a;
+// Q6_K RN16(sc*(q - 32)) in a and the residual in e.
+template <uint32_t T>
+__device__ __forceinline__ void fact_decode(const uint8_t *raw, uint32_t row, uint32_t c, uint32_t q,
+                                            uint32_t (&a)[8], uint32_t (&e)[8]) {
+    if constexpr (T == kTypeQ4_K) {
+        const uint8_t *blk = raw + row * 144u;
+        const uint4 hdr = lds16(blk);
+        const uint4 qs = lds16(blk + 16u + (c & 3u) * 32u + 16u * (q & 1u));
+        const uint32_t high = q >> 1;
+        uint32_t sc, mn;
+        q4k_scale_min(hdr, 2u * (c & 3u) + high, sc, mn);
+        const __half2 s2 = __half2half2(__uint2half_rn(sc));                 // exact
+        const __half2 n2 = __hneg2(__half2half2(__uint2half_rn(sc << 10)));  // -1024 sc, exact
+        const uint32_t wq[4] = {qs.x, qs.y, qs.z, qs.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t nib = high ? (wq[k] >> 4) & 0x0F0F0F0Fu : wq[k] & 0x0F0F0F0Fu;
+            // bytes {q, 0x64, q', 0x64}: the fp16 pair (1024 + q, 1024 + q')
+            a[2 * k] = h2_bits(__hfma2(bits_h2(__byte_perm(nib, 0x64u, 0x4140u)), s2, n2));
+            a[2 * k + 1] = h2_bits(__hfma2(bits_h2(__byte_perm(nib, 0x64u, 0x4342u)), s2, n2));
+            e[2 * k] = e[2 * k + 1] = 0u;
+        }
+    } else {
+        const uint32_t half = (c & 3u) >> 1;
+        const uint32_t h = q >> 1, s = 2u * (c & 1u) + h, part = q & 1u;
+        const uint4 ql = lds16(raw + sw128_at(row, 4u * half + 2u * h + part));
+        const uint4 qh = lds16(raw + 16384u + sw64_at(row, 2u * half + part));
+        const uint32_t scb = raw[24576u + row * 16u + half * 8u + 2u * s + part];
+        const __half2 s2 = __half2half2(__int2half_rn((int)(int8_t)scb));      // exact
+        const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6420u));   // 1056
+        const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t nib = (c & 1u) ? (wl[k] >> 4) & 0x0F0F0F0Fu : wl[k] & 0x0F0F0F0Fu;
+            const uint32_t bw = nib | (((wh[k] >> (2u * s)) & 0x03030303u) << 4);
+            // (1024 + q) - 1056 = q - 32, exact
+            const __half2 t0 = __hsub2(bits_h2(__byte_perm(bw, 0x64u, 0x4140u)), off);
+            const __half2 t1 = __hsub2(bits_h2(__byte_perm(bw, 0x64u, 0x4342u)), off);
+            const __half2 r0 = __hmul2(t0, s2), r1 = __hmul2(t1, s2);
+            a[2 * k] = h2_bits(r0);
+            a[2 * k + 1] = h2_bits(r1);
+            e[2 * k] = h2_bits(__hfma2(t0, s2, __hneg2(r0)));       // sc*(q-32) - RN(...), exact
+            e[2 * k + 1] = h2_bits(__hfma2(t1, s2, __hneg2(r1)));
+        }
+    }
+}
+
+// Q6_K: the super-block scale d of chunk c's super-block.
+__device__ __forceinline__ float q6k_scale(const uint8_t *raw, uint32_t row, uint32_t cols, uint32_t c) {
+    const uint32_t nsb = cols >> 8, sb = c >> 2;
+    return h2f(*reinterpret_cast<const uint16_t *>(raw + 26624u + row * 16u + ((nsb * 208u + sb * 2u) & 15u)));
+}
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+    return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Hardware named barriers among a subset of the CTA's warps.
+__device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(uint32_t id, uint32_t threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+enum NamedBarrier : uint32_t { kBarDecIn = 1, kBarDecOut, kBarEpiIn, kBarEpiOut };
+
+// D (TMEM) += A (shared-memory descriptor) * B (shared-memory descriptor).
+template <uint32_t N>
+__device__ __forceinline__ void umma_ss(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(a), "l"(b), "n"(idesc_for(N)), "r"(accumulate));
+}
+
+// 16-byte load from the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t local_addr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(remote));
+    return v;
+}
+
+// Split-K exchange tile: 128 rows x 64 floats, 16-byte chunk c of row r at
+// chunk c ^ (r & 15) (conflict-free for a warp of consecutive rows).
+__device__ __forceinline__ uint32_t xchg_off(uint32_t r, uint32_t c) { return r * 256u + ((c ^ (r & 15u)) << 4); }
+
+template <uint32_t T>
+__global__ void __launch_bounds__(kFThreads, 1)
+proj_fact_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const uint8_t *__restrict__ xtiles,
+                 uint32_t nchunks_x, const uint8_t *__restrict__ xmtiles, uint32_t nxm, float *__restrict__ y,
+                 uint32_t ldy, uint32_t batch, uint32_t kchunks_per_split, ErrorWord err) {
+    using F = Fact<T>;
+    constexpr bool kQ4 = F::q4;
+    constexpr uint32_t U = F::U, kU = F::kU, kRR = F::rr, kRaw = F::raw, kXSlot = F::xslot;
+    constexpr uint32_t kPerSb = 4u / U;   // units per super-block
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ uint64_t rfull[kRR], rfree[kRR], ready[kU], ucons[kU];
+    __shared__ uint64_t dfull[2], dfree[2], xmfull[2], xmfree[2], dready[4], accum;
+    __shared__ float dscale[4][kUM];
+    __shared__ uint32_t tmem_base_slot, skip_slot;
+    __shared__ volatile uint32_t abort_flag, dec_stop, epi_stop;
+    // No early return anywhere: every CTA of a split-K cluster must reach
+    // the cluster barriers.
+
+    uint8_t *raw_ring = align1024(smem_raw);
+    uint8_t *xm_ring = raw_ring + kRR * kRaw;
+    uint8_t *ml_ring = xm_ring + F::xm * kXmSlot;
+    uint8_t *dg_ring = ml_ring + F::ml * kMlSlot;
+    uint8_t *x_ring = dg_ring + F::dg * kDgSlot;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    int seg = 0;
+    while (seg + 1 < segs.count && blockIdx.x >= segs.tile_start[seg + 1]) ++seg;
+    const QMatrix m = segs.m[seg];
+    const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * kUM;
+    const uint32_t b0 = blockIdx.y * kUN;
+    const uint32_t nchunks_total = m.cols / kUK;
+    // kchunks_per_split is a multiple of 4: every CTA starts a super-block
+    const uint32_t c_begin = blockIdx.z * kchunks_per_split;
+    const uint32_t c_end = min(nchunks_total, c_begin + kchunks_per_split);
+    const uint32_t nchunks_planned = c_end > c_begin ? c_end - c_begin : 0;
+    const uint32_t sb0 = c_begin >> 2;
+
+    if (tid == 0) {
+        for (uint32_t s = 0; s < kRR; ++s) {
+            mbar_init(&rfull[s], 1);
+            mbar_init(&rfree[s], 1);
+        }
+        for (uint32_t u = 0; u < kU; ++u) {
+            mbar_init(&ready[u], 2);   // decode leader + the TMA's activation bytes
+            mbar_init(&ucons[u], 1);
+        }
+        for (uint32_t i = 0; i < 2; ++i) {
+            mbar_init(&dfull[i], 1);
+            mbar_init(&dfree[i], 1);    // epilogue leader
+            mbar_init(&xmfull[i], 1);
+            mbar_init(&xmfree[i], 2);   // MMA commit + epilogue leader (d tile)
+        }
+        for (uint32_t i = 0; i < 4; ++i) mbar_init(&dready[i], 1);
+        mbar_init(&accum, 1);
+        abort_flag = 0u;
+        dec_stop = 0u;
+        epi_stop = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kFAllocWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&tmem_base_slot)), "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base_slot;
+
+    // weights of the first raw slots before the wait (never written by a kernel)
+    uint32_t prefetched = 0;
+    const CUtensorMap *maps = tmaps.map[seg];
+    const uint32_t rtx = raw_tx<T>(tmaps.box_rows[seg]);
+    if (warp == kFTmaWarp && lane == 0 && nchunks_planned > 0) {
+        prefetched = min(nchunks_planned / 4u, kRR);
+        for (uint32_t j = 0; j < prefetched; ++j) {
+            mbar_expect_tx(&rfull[j], rtx);
+            load_raw<T>(smem_u32(raw_ring + j * kRaw), maps, m.cols, sb0 + j, (int)row0, &rfull[j]);
+        }
+    }
+    pdl_wait();
+    if (tid == 0) skip_slot = *reinterpret_cast<volatile unsigned long long *>(err.word) != 0ull ? 1u : 0u;
+    __syncthreads();
+    const bool skip = skip_slot != 0u;
+    const uint32_t nchunks = skip ? 0u : nchunks_planned;
+    const uint32_t nsb = nchunks >> 2, nunits = nchunks / U;
+
+    float acc[32];   // epilogue warps only (initialised there)
+    bool epi_ok = true;
+    const bool epi = warp >= kFEpi0;
+
+    if (warp == kFTmaWarp) {
+        // ---- weight producer: raw super-blocks (three ahead) and group tiles
+        if (lane == 0 && skip) {
+            for (uint32_t j = 0; j < prefetched; ++j)
+                if (!mbar_wait(&rfull[j], 0u, &abort_flag, kSiteRawFull)) break;
+        }
+        if (lane == 0 && nsb > 0) {
+            for (uint32_t j = 0; j < nsb; ++j) {
+                if constexpr (kQ4) {
+                    const uint32_t sb = sb0 + j, lt = (sb >> 2) - (sb0 >> 2);
+                    if (j == 0 || (sb & 3u) == 0) {
+                        const uint32_t slot = lt & 1u;
+                        if (lt >= 2 && !mbar_wait(&xmfree[slot], ((lt - 2) >> 1) & 1u, &abort_flag, kSiteXmFree))
+                            break;
+                        const uint32_t brows = tmaps.box_rows[seg];
+                        mbar_expect_tx(&xmfull[slot], kXmSlot + 128u * brows + 16u * brows);
+                        bulk_load(smem_u32(xm_ring + slot * kXmSlot),
+                                  xmtiles + ((size_t)blockIdx.y * nxm + (sb >> 2)) * kXmSlot, kXmSlot, &xmfull[slot]);
+                        tma_load_2d(smem_u32(ml_ring + slot * kMlSlot), &maps[1], (int)((sb >> 2) * 128u), (int)row0,
+                                    &xmfull[slot]);
+                        tma_load_2d(smem_u32(dg_ring + slot * kDgSlot), &maps[2], (int)((sb >> 2) * 16u), (int)row0,
+                                    &xmfull[slot]);
+                    }
+                }
+                if (j >= prefetched) {
+                    const uint32_t rs = j % kRR;
+                    if (j >= kRR && !mbar_wait(&rfree[rs], ((j - kRR) / kRR) & 1u, &abort_flag, kSiteRawFree)) break;
+                    mbar_expect_tx(&rfull[rs], rtx);
+                    load_raw<T>(smem_u32(raw_ring + rs * kRaw), maps, m.cols, sb0 + j, (int)row0, &rfull[rs]);
+                }
+            }
+        }
+    } else if (warp == kFXWarp) {
+        // ---- activation producer: the unit's slot was last read by the MMAs of unit u - kU
+        if (lane == 0) {
+            for (uint32_t u = 0; u < nunits; ++u) {
+                const uint32_t us = u % kU;
+                if (u >= kU && !mbar_wait(&ucons[us], ((u - kU) / kU) & 1u, &abort_flag, kSiteXFree)) break;
+                mbar_expect_tx(&ready[us], kXSlot);
+                bulk_load(smem_u32(x_ring + us * kXSlot),
+                          xtiles + ((size_t)blockIdx.y * nchunks_x + c_begin + u * U) * Tile<kUN>::xslot, kXSlot,
+                          &ready[us]);
+            }
+        }
+    } else if (warp == kFMmaWarp) {
+        // ---- MMA issue: one thread
+        if (lane == 0) {
+            const uint64_t desc0 = sw128_desc(smem_u32(x_ring));
+            const uint64_t descm = sw128_desc(smem_u32(xm_ring));
+            const uint64_t descl = sw128_desc(smem_u32(ml_ring));
+            for (uint32_t u = 0; u < nunits; ++u) {
+                const uint32_t j = u / kPerSb, us = u % kU, dbuf = j & 1u;
+                const bool first = u % kPerSb == 0, last = u % kPerSb == kPerSb - 1;
+                const uint32_t sb = sb0 + j, lt = (sb >> 2) - (sb0 >> 2);
+                // accumulator dbuf was last read by the epilogue of super-block j - 2
+                if (first && j >= 2 && !mbar_wait(&dfree[dbuf], ((j - 2) >> 1) & 1u, &abort_flag, kSiteDFree))
+                    break;
+                if constexpr (kQ4) {
+                    if (first && (j == 0 || (sb & 3u) == 0) &&
+                        !mbar_wait(&xmfull[lt & 1u], (lt >> 1) & 1u, &abort_flag, kSiteXmFull))
+                        break;
+                }
+                if (!mbar_wait(&ready[us], (u / kU) & 1u, &abort_flag, kSiteAReady)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t dacc = tmem + dbuf * 128u;
+#pragma unroll
+                for (uint32_t c2 = 0; c2 < U; ++c2) {
+                    const uint64_t db = desc0 + (uint64_t)((us * kXSlot + c2 * Tile<kUN>::xslot) >> 4);
+                    const uint32_t a = tmem + F::abase + us * F::astride + c2 * 32u;
+#pragma unroll
+                    for (uint32_t kk = 0; kk < kUK / 16; ++kk) {
+                        umma_ts<2 * kUN>(dacc, a + kk * 8u, db + 2u * kk, (first && c2 == 0 && kk == 0) ? 0u : 1u);
+                        if constexpr (!kQ4) umma_ts<kUN>(dacc, a + F::ecols + kk * 8u, db + 2u * kk, 1u);
+                    }
+                }
+                if constexpr (kQ4) {
+                    if (first) {
+                        // minimum term: A' rows x [Xh | Xh], then x [Xl | 0]
+                        const uint64_t da = descl + (uint64_t)((lt & 1u) * (kMlSlot >> 4)) + 2u * (sb & 3u);
+                        const uint64_t dx = descm + (uint64_t)((lt & 1u) * (kXmSlot >> 4)) + 2u * (sb & 3u);
+                        umma_ss<kUN>(tmem + F::dm, da, dx, j == 0 ? 0u : 1u);
+                        umma_ss<kUN>(tmem + F::dm, da, dx + (uint64_t)((64u * 128u) >> 4), 1u);
+                    }
+                }
+                umma_commit(&ucons[us]);
+                if (last) {
+                    umma_commit(&rfree[j % kRR]);
+                    umma_commit(&dfull[dbuf]);
+                    if constexpr (kQ4) {
+                        if ((sb & 3u) == 3u || j + 1 == nsb) umma_commit(&xmfree[lt & 1u]);
+                    }
+                }
+            }
+            umma_commit(&accum);   // completes once every MMA this thread issued has
+        }
+    } else if (warp < kFEpi0) {
+        // ---- decode warps: lane = weight row within the warp's TMEM quarter
+        const uint32_t quarter = warp & 3, q = (uint32_t)(warp - kFDecode0) >> 2;
+        const uint32_t row = quarter * 32u + lane;
+        const uint32_t lane_addr = (quarter * 32u) << 16;
+        constexpr uint32_t kDecThreads = kFDecodeWarps * 32;
+        const bool leader = warp == kFDecode0;
+        for (uint32_t u = 0; u < nunits; ++u) {
+            const uint32_t j = u / kPerSb, rs = j % kRR, us = u % kU;
+            const bool first = u % kPerSb == 0;
+            if (leader) {
+                // the unit's raw slot landed; its A buffer was last read by
+                // the MMAs of unit u - kU
+                bool ok = !first || mbar_wait_warp(&rfull[rs], (j / kRR) & 1u, &abort_flag, kSiteRawFull);
+                ok = ok && (u < kU || mbar_wait_warp(&ucons[us], ((u - kU) / kU) & 1u, &abort_flag, kSiteADone));
+                if (!ok && lane == 0) dec_stop = 1u;
+            }
+            named_sync(kBarDecIn, kDecThreads);
+            if (dec_stop) break;
+            const uint8_t *rawp = raw_ring + rs * kRaw;
+#pragma unroll
+            for (uint32_t c2 = 0; c2 < U; ++c2) {
+                uint32_t a[8], e[8];
+                fact_decode<T>(rawp, row, c_begin + u * U + c2, q, a, e);
+                const uint32_t ta = tmem + lane_addr + F::abase + us * F::astride + c2 * 32u + q * 8u;
+                tmem_st8(ta, a);
+                if constexpr (!kQ4) tmem_st8(ta + F::ecols, e);
+            }
+            // Q6_K: the super-block's d for the epilogue (Q4_K's comes by TMA)
+            const bool head = !kQ4 && first;
+            if (head && q == 0) dscale[j & 3u][row] = q6k_scale(rawp, row, m.cols, c_begin + u * U);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            if (leader) {
+                named_sync(kBarDecOut, kDecThreads);   // every decode warp's stores of unit u
+                if (lane == 0) {
+                    mbar_arrive(&ready[us]);
+                    if (head) mbar_arrive(&dready[j & 3u]);
+                }
+            } else {
+                named_arrive(kBarDecOut, kDecThreads);
+            }
+        }
+    } else if (epi) {
+        // ---- epilogue warps: per super-block acc += d * (A*xh + A*xl)
+        const uint32_t eq = warp & 3, eh = (uint32_t)(warp - kFEpi0) >> 2;
+        const uint32_t row = eq * 32u + lane;
+        const uint32_t lane_addr = (eq * 32u) << 16;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+        constexpr uint32_t kEpiThreads = kFEpiWarps * 32;
+        const bool eleader = warp == kFEpi0;
+        for (uint32_t j = 0; j < nsb; ++j) {
+            const uint32_t sb = sb0 + j, lt = (sb >> 2) - (sb0 >> 2);
+            if (eleader) {
+                bool ok = mbar_wait_warp(&dfull[j & 1u], (j >> 1) & 1u, &abort_flag, kSiteDFull);
+                if constexpr (kQ4) {
+                    // the group's d tile (loaded with its minimum-term tiles)
+                    if (ok && (j == 0 || (sb & 3u) == 0))
+                        ok = mbar_wait_warp(&xmfull[lt & 1u], (lt >> 1) & 1u, &abort_flag, kSiteXmFull);
+                } else {
+                    ok = ok && mbar_wait_warp(&dready[j & 3u], (j >> 2) & 1u, &abort_flag, kSiteScale);
+                }
+                if (!ok && lane == 0) epi_stop = 1u;
+            }
+            named_sync(kBarEpiIn, kEpiThreads);
+            if (epi_stop) {
+                epi_ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            float d;
+            if constexpr (kQ4)
+                d = reinterpret_cast<const float *>(dg_ring + (lt & 1u) * kDgSlot)[row * 4u + (sb & 3u)];
+            else
+                d = dscale[j & 3u][row];
+            const uint32_t base = tmem + lane_addr + (j & 1u) * 128u + eh * 32u;
+#pragma unroll
+            for (uint32_t g = 0; g < 4; ++g) {
+                uint32_t h[8], l[8];
+                tmem_ld8(base + g * 8u, h);
+                tmem_ld8(base + kUN + g * 8u, l);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    acc[g * 8 + i] =
+                        __fmaf_rn(d, __fadd_rn(__uint_as_float(h[i]), __uint_as_float(l[i])), acc[g * 8 + i]);
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            if (eleader) {
+                named_sync(kBarEpiOut, kEpiThreads);   // every epilogue warp has read the accumulator
+                if (lane == 0) {
+                    mbar_arrive(&dfree[j & 1u]);
+                    if (kQ4 && ((sb & 3u) == 3u || j + 1 == nsb)) mbar_arrive(&xmfree[lt & 1u]);
+                }
+            } else {
+                named_arrive(kBarEpiOut, kEpiThreads);
+            }
+        }
+        // every MMA of the CTA complete before TMEM is read again or freed
+        epi_ok = mbar_wait_warp(&accum, 0, &abort_flag, kSiteAccum) && epi_ok;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // minus 2^(5 - scale_exp) * the minimum term
+        if constexpr (kQ4) {
+            if (epi_ok && nsb > 0) {
+                const float mscale = __uint_as_float((uint32_t)(127 + 5 - m.scale_exp) << 23);
+                const uint32_t base = tmem + lane_addr + F::dm + eh * 32u;
+#pragma unroll
+                for (uint32_t g = 0; g < 4; ++g) {
+                    uint32_t v[8];
+                    tmem_ld8(base + g * 8u, v);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[g * 8 + i] = __fmaf_rn(-mscale, __uint_as_float(v[i]), acc[g * 8 + i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = __fmul_rn(acc[i], 4.0f);   // x was scaled by 1/4
+    }
+
+    const bool all_ok = __syncthreads_and(!epi || epi_ok) && abort_flag == 0u;
+    if (!all_ok && tid == 0)
+        atomicCAS(err.word, 0ull, ((unsigned long long)(kErrTimeout | (abort_flag << 8)) << 32) | err.call_id);
+    const bool write = all_ok && !skip;
+    bool out_bad = false;
+
+    const uint32_t eh = (uint32_t)(warp - kFEpi0) >> 2;
+    const uint32_t erow = (warp & 3) * 32u + lane;
+    const uint32_t nsplit = gridDim.z;
+    if (nsplit == 1) {
+        const uint32_t row = row0 + erow;
+        if (epi && write && row < m.rows) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const uint32_t b = b0 + eh * 32u + i;
+                if (b < batch) {
+                    out_bad |= !isfinite(acc[i]);
+                    y[(size_t)b * ldy + segs.out_offset[seg] + row] = acc[i];
+                }
+            }
+        }
+    } else {
+        // exchange tile in the drained activation ring (xchg_off layout);
+        // each CTA then sums a slice of the rows over the cluster, in rank
+        // order, with 16-byte loads
+        uint8_t *xt = x_ring;
+        if (epi) {
+#pragma unroll
+            for (uint32_t c = 0; c < 8; ++c)
+                *reinterpret_cast<float4 *>(xt + xchg_off(erow, eh * 8u + c)) =
+                    make_float4(acc[4 * c], acc[4 * c + 1], acc[4 * c + 2], acc[4 * c + 3]);
+        }
+        cluster_sync();
+        const uint32_t rank = cluster_rank();
+        const uint32_t rows_per = kUM / nsplit;
+        const uint32_t base = smem_u32(xt);
+        for (uint32_t i = tid; i < rows_per * (kUN / 4u); i += kFThreads) {
+            const uint32_t rr = i % rows_per, g = i / rows_per;
+            const uint32_t lr = rank * rows_per + rr;
+            const uint32_t off = base + xchg_off(lr, g);
+            float4 v[8];
+#pragma unroll
+            for (uint32_t z = 0; z < 8; ++z)
+                if (z < nsplit) v[z] = ld_dsmem4(off, z);
+            float4 sum = v[0];
+#pragma unroll
+            for (uint32_t z = 1; z < 8; ++z)
+                if (z < nsplit) {
+                    sum.x = __fadd_rn(sum.x, v[z].x);
+                    sum.y = __fadd_rn(sum.y, v[z].y);
+                    sum.z = __fadd_rn(sum.z, v[z].z);
+                    sum.w = __fadd_rn(sum.w, v[z].w);
+                }
+            const uint32_t row = row0 + lr, b = b0 + 4u * g;
+            if (write && row < m.rows) {
+                const float s4[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+                for (uint32_t k = 0; k < 4; ++k)
+                    if (b + k < batch) {
+                        out_bad |= !isfinite(s4[k]);
+                        y[(size_t)(b + k) * ldy + segs.out_offset[seg] + row] = s4[k];
+                    }
+            }
+        }
+        cluster_sync();   // peers finish reading this CTA's tile before it exits
+    }
+    if (out_bad) atomicCAS(err.word, 0ull, ((unsigned long long)kErrNonFinite << 32) | err.call_id);
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == kFAllocWarp) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    }
+}
+
+// ---- Q4_K side data (host, at upload)
+
+uint32_t q4k_aux_pitch_a(uint32_t cols) { return (cols / 256u + 3u) / 4u * 128u; }
+uint32_t q4k_aux_pitch_d(uint32_t cols) { return (cols / 256u + 3u) / 4u * 16u; }
+size_t q4k_aux_bytes(uint32_t rows, uint32_t cols) {
+    return (size_t)rows * (q4k_aux_pitch_a(cols) + q4k_aux_pitch_d(cols));
+}
+
+static float host_half(const uint8_t *p) {
+    __half_raw r;
+    r.x = (unsigned short)(p[0] | (p[1] << 8));
+    return __half2float(__half(r));
+}
+
+void q4k_build_aux(const uint8_t *packed, uint32_t rows, uint32_t cols, int32_t scale_exp, uint8_t *out) {
+    const uint32_t nsb = cols / 256u, pa = q4k_aux_pitch_a(cols), pd = q4k_aux_pitch_d(cols);
+    std::memset(out, 0, q4k_aux_bytes(rows, cols));
+    uint8_t *plane_d = out + (size_t)rows * pa;
+    const float wscale = std::ldexp(1.0f, scale_exp);
+    for (uint32_t r = 0; r < rows; ++r) {
+        for (uint32_t sb = 0; sb < nsb; ++sb) {
+            const uint8_t *blk = packed + ((size_t)r * nsb + sb) * 144u;
+            const float d = host_half(blk), dmin = host_half(blk + 2) * wscale;   // exact power of two
+            const uint8_t *sc = blk + 4;
+            uint16_t hl[16];
+            for (uint32_t j = 0; j < 8; ++j) {
+                const uint32_t mn = j < 4 ? (sc[j + 4] & 63u) : ((sc[j + 4] >> 4) | ((sc[j] >> 6) << 4));
+                const float v = dmin * (float)mn;   // exact: 11 x 6 significant bits
+                const __half h = __float2half_rn(v);
+                const __half l = __float2half_rn(v - __half2float(h));
+                hl[j] = __half_raw(h).x;
+                hl[8 + j] = __half_raw(l).x;
+            }
+            std::memcpy(out + (size_t)r * pa + sb * 32u, hl, sizeof(hl));
+            std::memcpy(plane_d + (size_t)r * pd + sb * 4u, &d, 4);
+        }
+    }
+}
+
 bool umma_supported(const QMatrix &m) {
     const bool aligned = (m.row_bytes & 15u) == 0u && (reinterpret_cast<uintptr_t>(m.data) & 15u) == 0u;
     if (!aligned) return false;
@@ -837,9 +1486,18 @@ bool umma_supported(const QMatrix &m) {
     }
 }
 
+// Narrow activation tiles, followed by the factored kernel's minimum-term
+// tiles (one per batch tile and group of 16 chunks).
+static size_t narrow_xtile_bytes(uint32_t batch, uint32_t cols) {
+    const size_t nch = (cols + kUK - 1) / kUK;
+    return (size_t)((batch + kUN - 1) / kUN) * nch * Tile<kUN>::xslot;
+}
+static uint32_t xm_tiles(uint32_t nchunks) { return (nchunks + 15u) / 16u; }
+
 size_t umma_xtile_bytes(uint32_t batch, uint32_t cols, bool allow_wide) {
     const size_t nch = (cols + kUK - 1) / kUK;
-    const size_t narrow = (size_t)((batch + kUN - 1) / kUN) * nch * Tile<kUN>::xslot;
+    const size_t narrow = narrow_xtile_bytes(batch, cols) +
+                          (size_t)((batch + kUN - 1) / kUN) * xm_tiles((uint32_t)nch) * kXmSlotBytes;
     if (batch <= (uint32_t)kUN || !allow_wide) return narrow;
     const size_t wide = (size_t)((batch + kUNWide - 1) / kUNWide) * nch * Tile<kUNWide>::xslot;
     return std::max(narrow, wide);
@@ -923,7 +1581,17 @@ static bool tensor_map(const QMatrix &m, uint32_t width, CUtensorMapSwizzle swiz
 template <uint32_t T>
 static bool segment_maps(const QMatrix &m, CUtensorMap (&maps)[3], bool cache = true) {
     if constexpr (T == kTypeQ4_K) {
-        return tensor_map(m, 144, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[0], cache);
+        if (!tensor_map(m, 144, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[0], cache)) return false;
+        if (m.aux == nullptr) return true;
+        // side planes: A' rows (128-byte boxes = 4 super-blocks, swizzled as
+        // the MMA reads them) and d
+        QMatrix pa = m, pd = m;
+        pa.data = m.aux;
+        pa.row_bytes = q4k_aux_pitch_a(m.cols);
+        pd.data = m.aux + (size_t)m.rows * pa.row_bytes;
+        pd.row_bytes = q4k_aux_pitch_d(m.cols);
+        return tensor_map(pa, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[1], cache) &&
+               tensor_map(pd, 16, CU_TENSOR_MAP_SWIZZLE_NONE, &maps[2], cache);
     } else if constexpr (T == kTypeQ6_K) {
         return tensor_map(m, 128, CU_TENSOR_MAP_SWIZZLE_128B, &maps[0], cache) &&
                tensor_map(m, 64, CU_TENSOR_MAP_SWIZZLE_64B, &maps[1], cache) &&
@@ -950,6 +1618,12 @@ static bool maps_for(const QMatrix &m, CUtensorMap (&maps)[3], bool cache = true
 // pipeline fill and epilogue) + 2 per cluster member for the
 // distributed-shared-memory reduction, with one CTA per SM.  The constants
 // are fitted to measured B200 times of the in-/out-projection shapes.
+// Split-count cost constants of the factored kernel: chunks cost about a
+// quarter of the two-term kernel's, so fill and the cluster reduction weigh
+// more (fitted to measured in-/out-projection times).
+constexpr double kFactFill = 16.0;
+constexpr double kFactMember = 3.0;
+
 static int sm_count() {
     static int sms = 0;
     if (sms == 0) {
@@ -961,14 +1635,15 @@ static int sm_count() {
     return sms;
 }
 
-static uint32_t choose_splits(uint32_t tiles, uint32_t nchunks, uint32_t max_splits, double *cost_out = nullptr) {
+static uint32_t choose_splits(uint32_t tiles, uint32_t nchunks, uint32_t max_splits, double *cost_out = nullptr,
+                              double fill = 8.0, double per_member = 2.0) {
     const int sms = sm_count();
     uint32_t best = 1;
     double best_cost = 1e30;
     for (uint32_t s = 1; s <= max_splits; s *= 2) {
         if (s > 1 && nchunks < 4 * s) break;
         const double waves = std::ceil((double)tiles * s / sms);
-        const double cost = waves * ((nchunks + s - 1) / s + 8.0) + (s > 1 ? 2.0 * s : 0.0);
+        const double cost = waves * ((nchunks + s - 1) / s + fill) + (s > 1 ? per_member * s : 0.0);
         if (cost < best_cost - 1e-9) { best_cost = cost; best = s; }
     }
     if (cost_out) *cost_out = best_cost;
@@ -993,6 +1668,53 @@ static bool choose_wide(uint32_t tiles, uint32_t nchunks, uint32_t batch) {
 // Largest split cluster (8, 4, 2 or 1) the device can co-schedule for this
 // kernel; queried once per type and device (the attribute it sets belongs to
 // the current device).
+template <typename Kernel>
+static uint32_t probe_splits(Kernel kernel, uint32_t threads, uint32_t smem) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    uint32_t best = 1;
+    for (uint32_t s = 8; s >= 2; s /= 2) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(1, 1, s);
+        cfg.blockDim = dim3(threads);
+        cfg.dynamicSmemBytes = smem;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 1;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = s;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && n > 0) {
+            best = s;
+            break;
+        }
+    }
+    (void)cudaGetLastError();
+    return best;
+}
+
+// The same for the factored kernel (its own shared memory and block size).
+template <uint32_t T>
+static uint32_t max_splits_fact() {
+    static std::atomic<uint32_t> per_device[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 63;
+    uint32_t cached = per_device[dev].load(std::memory_order_acquire);
+    if (cached == 0) {
+        cached = probe_splits(proj_fact_kernel<T>, kFThreads, Fact<T>::smem);
+        per_device[dev].store(cached, std::memory_order_release);
+    }
+    return cached;
+}
+
+// Factored kernel for Q4_K / Q6_K batch tiles of 64 (KQ_B200_PROJ_FACT=0
+// selects the two-term kernel instead; tuning and tests).
+static bool fact_enabled() {
+    const char *e = getenv("KQ_B200_PROJ_FACT");
+    return !(e && e[0] == '0');
+}
+
 template <uint32_t T>
 static uint32_t max_splits_for() {
     static std::atomic<uint32_t> per_device[64];
@@ -1030,8 +1752,8 @@ static uint32_t max_splits_for() {
 
 template <uint32_t T>
 static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &segs, const uint8_t *xt,
-                         uint32_t nchunks_x, float *y, uint32_t ldy, uint32_t batch, bool wide, ErrorWord err,
-                         cudaStream_t stream, bool cache_maps) {
+                         uint32_t nchunks_x, const uint8_t *xm, float *y, uint32_t ldy, uint32_t batch, bool wide,
+                         ErrorWord err, cudaStream_t stream, bool cache_maps) {
     TmapSet maps;
     for (int i = 0; i < segs.count; ++i) {
         if (!segment_maps<T>(segs.m[i], maps.map[i], cache_maps)) return false;
@@ -1058,10 +1780,34 @@ static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &s
         return true;
     }
     const uint32_t btiles = (batch + kUN - 1) / kUN;
-    static const int forced = [] {
-        const char *e = getenv("KQ_B200_PROJ_SPLITS");   // tuning: fixed split count
-        return e ? atoi(e) : 0;
-    }();
+    const char *forced_env = getenv("KQ_B200_PROJ_SPLITS");   // tuning: fixed split count
+    const int forced = forced_env ? atoi(forced_env) : 0;
+    if constexpr (T == kTypeQ4_K || T == kTypeQ6_K) {
+        bool aux = true;   // Q4_K: every segment carries its side data
+        for (int i = 0; i < segs.count; ++i) aux &= T != kTypeQ4_K || segs.m[i].aux != nullptr;
+        if (fact_enabled() && aux && (T != kTypeQ4_K || xm != nullptr)) {
+            static DeviceOnce attr;
+            attr.run([] {
+                cudaFuncSetAttribute(proj_fact_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     Fact<T>::smem);
+            });
+            const uint32_t cap = max_splits_fact<T>();
+            uint32_t splits = choose_splits(tiles * btiles, nchunks, cap, nullptr, kFactFill, kFactMember);
+            if (forced == 1 || forced == 2 || forced == 4 || forced == 8) splits = std::min<uint32_t>((uint32_t)forced, cap);
+            const uint32_t per = ((nchunks + splits - 1) / splits + 3u) / 4u * 4u;
+            cfg.gridDim = dim3(tiles, btiles, splits);
+            cfg.blockDim = dim3(kFThreads);
+            cfg.dynamicSmemBytes = Fact<T>::smem;
+            at[1].id = cudaLaunchAttributeClusterDimension;
+            at[1].val.clusterDim.x = 1;
+            at[1].val.clusterDim.y = 1;
+            at[1].val.clusterDim.z = splits;
+            cfg.numAttrs = 2;
+            cudaLaunchKernelEx(&cfg, proj_fact_kernel<T>, maps, segs, xt, nchunks_x, xm, xm_tiles(nchunks_x), y,
+                               ldy, batch, per, err);
+            return true;
+        }
+    }
     uint32_t splits = choose_splits(tiles * btiles, nchunks, max_splits_for<T>());
     if (forced == 1 || forced == 2 || forced == 4 || forced == 8)
         splits = std::min<uint32_t>((uint32_t)forced, max_splits_for<T>());
@@ -1080,9 +1826,9 @@ static bool launch_typed(uint32_t tiles, uint32_t nchunks, const ProjSegments &s
 }
 
 // Launches one group of segments that share a weight type.
-static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, uint32_t nchunks_x, float *y,
-                         uint32_t ldy, uint32_t batch, bool wide, ErrorWord err, cudaStream_t stream,
-                         bool cache_maps) {
+static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, uint32_t nchunks_x,
+                         const uint8_t *xm, float *y, uint32_t ldy, uint32_t batch, bool wide, ErrorWord err,
+                         cudaStream_t stream, bool cache_maps) {
     uint32_t acc = 0, cols = 0;
     for (int i = 0; i < segs.count; ++i) {
         segs.tile_start[i] = acc;
@@ -1093,10 +1839,10 @@ static bool launch_group(uint32_t type, ProjSegments segs, const uint8_t *xt, ui
     const uint32_t nchunks = (cols + kUK - 1) / kUK;
     bool ok;
     switch (type) {
-    case kTypeQ4_K: ok = launch_typed<kTypeQ4_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, wide, err, stream, cache_maps); break;
-    case kTypeQ6_K: ok = launch_typed<kTypeQ6_K>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, wide, err, stream, cache_maps); break;
-    case kTypeQ8_0: ok = launch_typed<kTypeQ8_0>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, wide, err, stream, cache_maps); break;
-    default: ok = launch_typed<kTypeBF16>(acc, nchunks, segs, xt, nchunks_x, y, ldy, batch, wide, err, stream, cache_maps); break;
+    case kTypeQ4_K: ok = launch_typed<kTypeQ4_K>(acc, nchunks, segs, xt, nchunks_x, xm, y, ldy, batch, wide, err, stream, cache_maps); break;
+    case kTypeQ6_K: ok = launch_typed<kTypeQ6_K>(acc, nchunks, segs, xt, nchunks_x, xm, y, ldy, batch, wide, err, stream, cache_maps); break;
+    case kTypeQ8_0: ok = launch_typed<kTypeQ8_0>(acc, nchunks, segs, xt, nchunks_x, xm, y, ldy, batch, wide, err, stream, cache_maps); break;
+    default: ok = launch_typed<kTypeBF16>(acc, nchunks, segs, xt, nchunks_x, xm, y, ldy, batch, wide, err, stream, cache_maps); break;
     }
     if (ok) count_launch();
     return ok;
@@ -1122,12 +1868,18 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
     uint32_t tiles = 0;
     for (int i = 0; i < in.count; ++i) tiles += (in.m[i].rows + kUM - 1) / kUM;
     const bool wide = allow_wide && choose_wide(tiles, nchunks, batch);
+    // the factored Q4_K kernel also reads the sub-block sums of the activations
+    bool q4 = false;
+    for (int i = 0; i < in.count; ++i) q4 |= in.m[i].type == kTypeQ4_K;
+    uint8_t *xm = (!wide && q4 && fact_enabled()) ? xtiles + narrow_xtile_bytes(batch, cols) : nullptr;
     if (wide) {
         const dim3 xg(nchunks * (kUNWide / 16), (batch + kUNWide - 1) / kUNWide);
-        launch_pdl(xconv_kernel<kUNWide>, xg, 128, 0, stream, x, ldx, batch, cols, nchunks, xtiles, err);
+        launch_pdl(xconv_kernel<kUNWide>, xg, 128, 0, stream, x, ldx, batch, cols, nchunks, xtiles,
+                   (uint8_t *)nullptr, 0u, err);
     } else {
         const dim3 xg(nchunks * (kUN / 16), (batch + kUN - 1) / kUN);
-        launch_pdl(xconv_kernel<kUN>, xg, 128, 0, stream, x, ldx, batch, cols, nchunks, xtiles, err);
+        launch_pdl(xconv_kernel<kUN>, xg, 128, 0, stream, x, ldx, batch, cols, nchunks, xtiles, xm,
+                   xm_tiles(nchunks), err);
     }
     count_launch();
     // one launch per weight type present
@@ -1142,7 +1894,7 @@ bool launch_projection_umma(const ProjSegments &in, const float *x, uint32_t ldx
             ++g.count;
             done[j] = true;
         }
-        launch_group(in.m[i].type, g, xtiles, nchunks, y, ldy, batch, wide, err, stream, cache_maps);
+        launch_group(in.m[i].type, g, xtiles, nchunks, xm, y, ldy, batch, wide, err, stream, cache_maps);
     }
     return true;
 }

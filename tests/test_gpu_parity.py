@@ -133,6 +133,39 @@ def test_tensor_core_projection(kq, oracle, type_id, rows, cols, batch, wide, mo
         p.close()
 
 
+@pytest.mark.parametrize("type_id,rows,cols,batch,mean", [
+    (12, 520, 2048, 64, 0.0), (12, 12352, 2048, 64, 1.5), (12, 640, 4096, 130, -2.0), (12, 96, 256, 17, 0.0),
+    (14, 2048, 4096, 64, 0.0), (14, 2048, 4096, 64, 1.5), (14, 300, 1024, 100, 0.5), (14, 130, 256, 9, 0.0)])
+def test_factored_projection(kq, oracle, type_id, rows, cols, batch, mean, monkeypatch):
+    """The factored-scale Q4_K / Q6_K kernel (integer A operand, per
+    super-block d in the epilogue, Q4_K minimum term as a second product) and
+    the two-term kernel both against the reference's sequential row dots,
+    including activations with a large common mode, where the Q4_K minimum
+    term and the scaled main term nearly cancel."""
+    import torch
+    from kqb200 import synth
+    rng = np.random.default_rng(rows * 3 + cols + batch)
+    q = synth.pack(type_id, rng, rows, cols)
+    x = (rng.normal(size=(batch, cols)) + mean).astype(np.float32)
+    want = oracle.matvec(type_id, q.data, rows, cols, x)
+    p = kq.Provider(0)
+    try:
+        h = p.add_matrix("m", 11, q)
+        xd = torch.from_numpy(x).cuda()
+        for fact in ("1", "0"):
+            monkeypatch.setenv("KQ_B200_PROJ_FACT", fact)
+            yd = torch.full((batch, rows), float("nan"), device="cuda")
+            torch.cuda.synchronize()
+            d = kq.abi.Diagnostic()
+            st = kq.lib().kq_b200_provider_linear_batch_f32(p.handle, h, rows, cols, xd.data_ptr(), batch,
+                                                            yd.data_ptr(), C.byref(d))
+            assert st == 0, d.text()
+            kq.synchronize()
+            assert_close(yd.cpu().numpy(), want, f"type {type_id} factored={fact}")
+    finally:
+        p.close()
+
+
 # ------------------------------------------------------------------ GDN
 
 def _gdn_f32_call(kq, layer_handle, dims, w, x, state, mask=None):
