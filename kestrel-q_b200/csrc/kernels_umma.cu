@@ -462,6 +462,15 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
                  : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
                  ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
@@ -904,8 +913,9 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
 //   1       MMA issue
 //   2       activation producer (one unit per slot, gated by the MMAs), kept
 //           apart from the weight loads so that their HBM latency stays hidden
-//   3..18   decode: lane = weight row in TMEM quarter (warp & 3), 16 K values
-//           of each chunk of 64 (the layout of the kernel above)
+//   3..18   decode, two groups of 8 warps taking alternate units, so that one
+//           group's hand-off latency overlaps the other's decoding; lane =
+//           weight row in TMEM quarter (warp & 3), 32 K values of each chunk
 //   19..26  epilogue: lane = weight row, 32 of the 64 batch columns
 // TMEM columns: accumulators 2 x 128 at 0.  Q4_K: minimum term 64 at 256,
 // three A buffers of 2 x 32 at 320.  Q6_K: A buffers of U x (32 RN + 32
@@ -961,52 +971,54 @@ __device__ __forceinline__ void q4k_scale_min(const uint4 &hdr, uint32_t j, uint
     }
 }
 
-// The integer A operand of the 16 values [16q, 16q + 16) of chunk c of one
-// staged row (same staging as decode16), as fp16 pairs: Q4_K sc*q in a;
-// Q6_K RN16(sc*(q - 32)) in a and the residual in e.
-template <uint32_t T>
-__device__ __forceinline__ void fact_decode(const uint8_t *raw, uint32_t row, uint32_t c, uint32_t q,
-                                            uint32_t (&a)[8], uint32_t (&e)[8]) {
-    if constexpr (T == kTypeQ4_K) {
-        const uint8_t *blk = raw + row * 144u;
-        const uint4 hdr = lds16(blk);
-        const uint4 qs = lds16(blk + 16u + (c & 3u) * 32u + 16u * (q & 1u));
-        const uint32_t high = q >> 1;
-        uint32_t sc, mn;
-        q4k_scale_min(hdr, 2u * (c & 3u) + high, sc, mn);
-        const __half2 s2 = __half2half2(__uint2half_rn(sc));                 // exact
-        const __half2 n2 = __hneg2(__half2half2(__uint2half_rn(sc << 10)));  // -1024 sc, exact
-        const uint32_t wq[4] = {qs.x, qs.y, qs.z, qs.w};
+// Q6_K: the integer A operand of the 16 values [16q, 16q + 16) of chunk c of
+// one staged row (same staging as decode16) as fp16 pairs: RN16(sc*(q - 32))
+// in a and the exact residual in e.
+__device__ __forceinline__ void fact_decode_q6k16(const uint8_t *raw, uint32_t row, uint32_t c, uint32_t q,
+                                                  uint32_t (&a)[8], uint32_t (&e)[8]) {
+    const uint32_t half = (c & 3u) >> 1;
+    const uint32_t h = q >> 1, s = 2u * (c & 1u) + h, part = q & 1u;
+    const uint4 ql = lds16(raw + sw128_at(row, 4u * half + 2u * h + part));
+    const uint4 qh = lds16(raw + 16384u + sw64_at(row, 2u * half + part));
+    const uint32_t scb = raw[24576u + row * 16u + half * 8u + 2u * s + part];
+    const __half2 s2 = __half2half2(__int2half_rn((int)(int8_t)scb));      // exact
+    const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6420u));   // 1056
+    const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t nib = high ? (wq[k] >> 4) & 0x0F0F0F0Fu : wq[k] & 0x0F0F0F0Fu;
-            // bytes {q, 0x64, q', 0x64}: the fp16 pair (1024 + q, 1024 + q')
-            a[2 * k] = h2_bits(__hfma2(bits_h2(__byte_perm(nib, 0x64u, 0x4140u)), s2, n2));
-            a[2 * k + 1] = h2_bits(__hfma2(bits_h2(__byte_perm(nib, 0x64u, 0x4342u)), s2, n2));
-            e[2 * k] = e[2 * k + 1] = 0u;
-        }
-    } else {
-        const uint32_t half = (c & 3u) >> 1;
-        const uint32_t h = q >> 1, s = 2u * (c & 1u) + h, part = q & 1u;
-        const uint4 ql = lds16(raw + sw128_at(row, 4u * half + 2u * h + part));
-        const uint4 qh = lds16(raw + 16384u + sw64_at(row, 2u * half + part));
-        const uint32_t scb = raw[24576u + row * 16u + half * 8u + 2u * s + part];
-        const __half2 s2 = __half2half2(__int2half_rn((int)(int8_t)scb));      // exact
-        const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6420u));   // 1056
-        const uint32_t wl[4] = {ql.x, ql.y, ql.z, ql.w}, wh[4] = {qh.x, qh.y, qh.z, qh.w};
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t nib = (c & 1u) ? (wl[k] >> 4) & 0x0F0F0F0Fu : wl[k] & 0x0F0F0F0Fu;
+        const uint32_t bw = nib | (((wh[k] >> (2u * s)) & 0x03030303u) << 4);
+        // bytes {q, 0x64, q', 0x64}: the fp16 pair (1024 + q, 1024 + q'); minus 1056 = q - 32, exact
+        const __half2 t0 = __hsub2(bits_h2(__byte_perm(bw, 0x64u, 0x4140u)), off);
+        const __half2 t1 = __hsub2(bits_h2(__byte_perm(bw, 0x64u, 0x4342u)), off);
+        const __half2 r0 = __hmul2(t0, s2), r1 = __hmul2(t1, s2);
+        a[2 * k] = h2_bits(r0);
+        a[2 * k + 1] = h2_bits(r1);
+        e[2 * k] = h2_bits(__hfma2(t0, s2, __hneg2(r0)));       // sc*(q-32) - RN(...), exact
+        e[2 * k + 1] = h2_bits(__hfma2(t1, s2, __hneg2(r1)));
+    }
+}
+
+// Q4_K: the 32 values [32p, 32p + 32) of chunk c of one staged row (one
+// sub-block: the low (p = 0) or high (p = 1) nibbles of the chunk's 32 quant
+// bytes) as 16 fp16 pairs sc*q, with one header read and scale unpack.
+__device__ __forceinline__ void fact_decode_q4k32(const uint8_t *raw, uint32_t row, uint32_t c, uint32_t p,
+                                                  uint32_t (&a)[16]) {
+    const uint8_t *blk = raw + row * 144u;
+    const uint4 hdr = lds16(blk);
+    const uint4 q0 = lds16(blk + 16u + (c & 3u) * 32u), q1 = lds16(blk + 32u + (c & 3u) * 32u);
+    uint32_t sc, mn;
+    q4k_scale_min(hdr, 2u * (c & 3u) + p, sc, mn);
+    const __half2 s2 = __half2half2(__uint2half_rn(sc));                 // exact
+    const __half2 n2 = __hneg2(__half2half2(__uint2half_rn(sc << 10)));  // -1024 sc, exact
+    const uint32_t wq[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t nib = (c & 1u) ? (wl[k] >> 4) & 0x0F0F0F0Fu : wl[k] & 0x0F0F0F0Fu;
-            const uint32_t bw = nib | (((wh[k] >> (2u * s)) & 0x03030303u) << 4);
-            // (1024 + q) - 1056 = q - 32, exact
-            const __half2 t0 = __hsub2(bits_h2(__byte_perm(bw, 0x64u, 0x4140u)), off);
-            const __half2 t1 = __hsub2(bits_h2(__byte_perm(bw, 0x64u, 0x4342u)), off);
-            const __half2 r0 = __hmul2(t0, s2), r1 = __hmul2(t1, s2);
-            a[2 * k] = h2_bits(r0);
-            a[2 * k + 1] = h2_bits(r1);
-            e[2 * k] = h2_bits(__hfma2(t0, s2, __hneg2(r0)));       // sc*(q-32) - RN(...), exact
-            e[2 * k + 1] = h2_bits(__hfma2(t1, s2, __hneg2(r1)));
-        }
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t nib = p ? (wq[k] >> 4) & 0x0F0F0F0Fu : wq[k] & 0x0F0F0F0Fu;
+        // bytes {q, 0x64, q', 0x64}: the fp16 pair (1024 + q, 1024 + q'), then
+        // (1024 + q)*sc - 1024*sc = sc*q exactly
+        a[2 * k] = h2_bits(__hfma2(bits_h2(__byte_perm(nib, 0x64u, 0x4140u)), s2, n2));
+        a[2 * k + 1] = h2_bits(__hfma2(bits_h2(__byte_perm(nib, 0x64u, 0x4342u)), s2, n2));
     }
 }
 
@@ -1027,7 +1039,7 @@ __device__ __forceinline__ void named_sync(uint32_t id, uint32_t threads) {
 __device__ __forceinline__ void named_arrive(uint32_t id, uint32_t threads) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
-enum NamedBarrier : uint32_t { kBarDecIn = 1, kBarDecOut, kBarEpiIn, kBarEpiOut };
+enum NamedBarrier : uint32_t { kBarEpiIn = 1, kBarEpiOut, kBarDecIn, kBarDecOut };   // decode: 2 per group
 
 // D (TMEM) += A (shared-memory descriptor) * B (shared-memory descriptor).
 template <uint32_t N>
@@ -1067,7 +1079,7 @@ proj_fact_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     __shared__ uint64_t dfull[2], dfree[2], xmfull[2], xmfree[2], dready[4], accum;
     __shared__ float dscale[4][kUM];
     __shared__ uint32_t tmem_base_slot, skip_slot;
-    __shared__ volatile uint32_t abort_flag, dec_stop, epi_stop;
+    __shared__ volatile uint32_t abort_flag, dec_stop[2], epi_stop;
     // No early return anywhere: every CTA of a split-K cluster must reach
     // the cluster barriers.
 
@@ -1108,7 +1120,7 @@ proj_fact_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
         for (uint32_t i = 0; i < 4; ++i) mbar_init(&dready[i], 1);
         mbar_init(&accum, 1);
         abort_flag = 0u;
-        dec_stop = 0u;
+        dec_stop[0] = dec_stop[1] = 0u;
         epi_stop = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -1240,46 +1252,58 @@ proj_fact_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
             umma_commit(&accum);   // completes once every MMA this thread issued has
         }
     } else if (warp < kFEpi0) {
-        // ---- decode warps: lane = weight row within the warp's TMEM quarter
-        const uint32_t quarter = warp & 3, q = (uint32_t)(warp - kFDecode0) >> 2;
+        // ---- decode warps: group g takes units g, g + 2, ...; lane = weight
+        // row within the warp's TMEM quarter, 32 K values of each chunk
+        constexpr uint32_t kGroupWarps = kFDecodeWarps / 2, kGroupThreads = kGroupWarps * 32;
+        const uint32_t g = (uint32_t)(warp - kFDecode0) / kGroupWarps;
+        const uint32_t quarter = warp & 3, part = ((uint32_t)(warp - kFDecode0) % kGroupWarps) >> 2;
         const uint32_t row = quarter * 32u + lane;
         const uint32_t lane_addr = (quarter * 32u) << 16;
-        constexpr uint32_t kDecThreads = kFDecodeWarps * 32;
-        const bool leader = warp == kFDecode0;
-        for (uint32_t u = 0; u < nunits; ++u) {
+        const bool leader = (uint32_t)(warp - kFDecode0) % kGroupWarps == 0;
+        const uint32_t bar_in = kBarDecIn + 2u * g, bar_out = kBarDecOut + 2u * g;
+        for (uint32_t u = g; u < nunits; u += 2) {
             const uint32_t j = u / kPerSb, rs = j % kRR, us = u % kU;
             const bool first = u % kPerSb == 0;
             if (leader) {
-                // the unit's raw slot landed; its A buffer was last read by
-                // the MMAs of unit u - kU
-                bool ok = !first || mbar_wait_warp(&rfull[rs], (j / kRR) & 1u, &abort_flag, kSiteRawFull);
+                // the super-block's raw slot landed; the A buffer was last
+                // read by the MMAs of unit u - kU
+                bool ok = mbar_wait_warp(&rfull[rs], (j / kRR) & 1u, &abort_flag, kSiteRawFull);
                 ok = ok && (u < kU || mbar_wait_warp(&ucons[us], ((u - kU) / kU) & 1u, &abort_flag, kSiteADone));
-                if (!ok && lane == 0) dec_stop = 1u;
+                if (!ok && lane == 0) dec_stop[g] = 1u;
             }
-            named_sync(kBarDecIn, kDecThreads);
-            if (dec_stop) break;
+            named_sync(bar_in, kGroupThreads);
+            if (dec_stop[g]) break;
             const uint8_t *rawp = raw_ring + rs * kRaw;
 #pragma unroll
             for (uint32_t c2 = 0; c2 < U; ++c2) {
-                uint32_t a[8], e[8];
-                fact_decode<T>(rawp, row, c_begin + u * U + c2, q, a, e);
-                const uint32_t ta = tmem + lane_addr + F::abase + us * F::astride + c2 * 32u + q * 8u;
-                tmem_st8(ta, a);
-                if constexpr (!kQ4) tmem_st8(ta + F::ecols, e);
+                const uint32_t ta = tmem + lane_addr + F::abase + us * F::astride + c2 * 32u + part * 16u;
+                if constexpr (kQ4) {
+                    uint32_t a[16];
+                    fact_decode_q4k32(rawp, row, c_begin + u * U + c2, part, a);
+                    tmem_st16(ta, a);
+                } else {
+#pragma unroll
+                    for (uint32_t h = 0; h < 2; ++h) {
+                        uint32_t a[8], e[8];
+                        fact_decode_q6k16(rawp, row, c_begin + u * U + c2, 2u * part + h, a, e);
+                        tmem_st8(ta + h * 8u, a);
+                        tmem_st8(ta + h * 8u + F::ecols, e);
+                    }
+                }
             }
             // Q6_K: the super-block's d for the epilogue (Q4_K's comes by TMA)
             const bool head = !kQ4 && first;
-            if (head && q == 0) dscale[j & 3u][row] = q6k_scale(rawp, row, m.cols, c_begin + u * U);
+            if (head && part == 0) dscale[j & 3u][row] = q6k_scale(rawp, row, m.cols, c_begin + u * U);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             if (leader) {
-                named_sync(kBarDecOut, kDecThreads);   // every decode warp's stores of unit u
+                named_sync(bar_out, kGroupThreads);   // every warp of the group stored unit u
                 if (lane == 0) {
                     mbar_arrive(&ready[us]);
                     if (head) mbar_arrive(&dready[j & 3u]);
                 }
             } else {
-                named_arrive(kBarDecOut, kDecThreads);
+                named_arrive(bar_out, kGroupThreads);
             }
         }
     } else if (epi) {
