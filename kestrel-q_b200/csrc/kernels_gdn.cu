@@ -14,7 +14,9 @@
 // ([B*T][ldp]: qkv | gate | beta | alpha).
 #include "kernels.hpp"
 
+#include <algorithm>
 #include <cmath>
+#include <cstdlib>
 
 namespace kqb {
 
@@ -525,6 +527,263 @@ gdn_decode_fused_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, const float 
     if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
 }
 
+// ------------------------------------------------------------ persistent decode
+//
+// The fused decode kernel above as a persistent loop: each CTA (two per SM)
+// walks items (sequence b, value head h), item = n * gridDim.x + blockIdx.x,
+// and while it computes item n the bulk-copy engine fetches item n+1's
+// 64 KiB state and its conv / projection runs into shared memory, so the
+// state stream never stops between items (the one-shot kernel leaves HBM
+// idle while a CTA runs its prologue, recurrence and epilogue).  The state
+// of item n goes back to HBM from registers.  Arithmetic identical to
+// gdn_decode_fused_kernel.
+//
+// Shared memory: S (next state, 64 KiB) | IN[2] (per item: conv history of
+// the q, k and v channels, 3 x 2 KiB, their conv taps, 3 x 2 KiB, and the
+// projected q, k, v and gate rows, 4 x 512 B).  The norm weights stay in
+// registers for the CTA's life.  Requires 16-byte aligned state, conv,
+// conv-tap and projection rows (checked by the launcher).
+constexpr uint32_t kPStateBytes = kDim * kDim * 4;
+constexpr uint32_t kPConvRun = kDim * 4 * 4;           // 128 channels x 4 slots
+constexpr uint32_t kPProjRun = kDim * 4;
+constexpr uint32_t kPInBytes = 6 * kPConvRun + 4 * kPProjRun;
+constexpr uint32_t kPSmem = kPStateBytes + 2 * kPInBytes + 128;
+constexpr uint32_t kPWaitPolls = 1u << 26;
+
+__device__ __forceinline__ uint32_t gdn_smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void gdn_bulk(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(gdn_smem_u32(dst)), "l"(src), "r"(bytes), "r"(gdn_smem_u32(bar))
+                 : "memory");
+}
+
+// Bounded wait for phase `parity` of `bar` (one thread).
+__device__ __forceinline__ bool gdn_bar_wait(uint64_t *bar, uint32_t parity) {
+    const uint32_t a = gdn_smem_u32(bar);
+    for (uint32_t i = 0; i < kPWaitPolls; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.b32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(kRecThreads, 2)
+gdn_decode_persist_kernel(GdnDims d, GdnWeightsDev w, GdnBatchPtrs p, uint32_t batch, const float *__restrict__ proj,
+                          uint32_t ldp, float *__restrict__ gated, ErrorWord err) {
+    pdl_wait();
+    extern __shared__ __align__(128) uint8_t psm[];
+    __shared__ __align__(16) float ks[kDim];
+    __shared__ __align__(16) float qs[kDim];
+    __shared__ __align__(16) float vs[kDim];
+    __shared__ __align__(16) float part[kRecThreads / 32][kDim];
+    __shared__ __align__(16) float delta[kDim];
+    __shared__ float red[kRecThreads / 32];
+    __shared__ float gates[2];   // beta, decay
+    __shared__ uint64_t bar;
+    __shared__ uint32_t stop;
+    if (gdn_error_raised(err)) return;
+    float *S = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(psm) + 127) & ~uintptr_t(127));
+    uint8_t *inbuf = reinterpret_cast<uint8_t *>(S) + kPStateBytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t items = batch * d.value_heads;
+    bool bad = false;
+
+    // item it: state, conv history and projected rows into IN[slot]
+    auto fetch = [&](uint32_t it, uint32_t slot) {
+        const uint32_t b = it / d.value_heads, h = it % d.value_heads, kh = h / d.repeat;
+        uint8_t *in = inbuf + slot * kPInBytes;
+        const float *prow = proj + (size_t)b * ldp;
+        const float *conv_in = p.conv_in[b];
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
+                     ::"r"(gdn_smem_u32(&bar)), "r"(kPStateBytes + kPInBytes) : "memory");
+        gdn_bulk(S, p.rec_in[b] + (size_t)h * kDim * kDim, kPStateBytes, &bar);
+        gdn_bulk(in, conv_in + (size_t)(kh * kDim) * 4, kPConvRun, &bar);
+        gdn_bulk(in + kPConvRun, conv_in + (size_t)(d.key_width + kh * kDim) * 4, kPConvRun, &bar);
+        gdn_bulk(in + 2 * kPConvRun, conv_in + (size_t)(2 * d.key_width + h * kDim) * 4, kPConvRun, &bar);
+        gdn_bulk(in + 3 * kPConvRun, w.conv + (size_t)(kh * kDim) * 4, kPConvRun, &bar);
+        gdn_bulk(in + 4 * kPConvRun, w.conv + (size_t)(d.key_width + kh * kDim) * 4, kPConvRun, &bar);
+        gdn_bulk(in + 5 * kPConvRun, w.conv + (size_t)(2 * d.key_width + h * kDim) * 4, kPConvRun, &bar);
+        uint8_t *pr = in + 6 * kPConvRun;
+        gdn_bulk(pr, prow + kh * kDim, kPProjRun, &bar);
+        gdn_bulk(pr + kPProjRun, prow + d.key_width + kh * kDim, kPProjRun, &bar);
+        gdn_bulk(pr + 2 * kPProjRun, prow + 2 * d.key_width + h * kDim, kPProjRun, &bar);
+        gdn_bulk(pr + 3 * kPProjRun, prow + d.conv_channels + h * kDim, kPProjRun, &bar);
+    };
+
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(gdn_smem_u32(&bar)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        stop = 0u;
+        if (blockIdx.x < items) fetch(blockIdx.x, 0);
+    }
+    __syncthreads();
+
+    const float normw = threadIdx.x < kDim ? w.norm[threadIdx.x] : 0.0f;
+    uint32_t n = 0;
+    for (uint32_t it = blockIdx.x; it < items; it += gridDim.x, ++n) {
+        const uint32_t b = it / d.value_heads, h = it % d.value_heads, kh = h / d.repeat;
+        const uint32_t slot = n & 1u;
+        // this item's inputs; the gate scalars by plain loads meanwhile
+        const float *prow = proj + (size_t)b * ldp;
+        float pb = 0.0f, pa = 0.0f, alog = 0.0f, dtb = 0.0f;
+        if (threadIdx.x == 0) {
+            pb = prow[d.conv_channels + d.value_width + h];
+            pa = prow[d.conv_channels + d.value_width + d.value_heads + h];
+            alog = w.a_log[h];
+            dtb = w.dt_bias[h];
+            if (!gdn_bar_wait(&bar, n & 1u)) {
+                gdn_raise(err, kErrTimeout);
+                stop = 1u;
+            }
+        }
+        __syncthreads();
+        if (stop) break;
+        float4 s[kRows];
+#pragma unroll
+        for (int j = 0; j < kRows; ++j)
+            s[j] = *reinterpret_cast<const float4 *>(S + (size_t)(warp + 8 * j) * kDim + 4 * lane);
+        __syncthreads();   // S drained: the next item's state may land in it
+        if (threadIdx.x == 0 && it + gridDim.x < items) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            fetch(it + gridDim.x, slot ^ 1u);
+        }
+        const uint8_t *in = inbuf + slot * kPInBytes;
+        const float *cq = reinterpret_cast<const float *>(in);
+        const float *ck = reinterpret_cast<const float *>(in + kPConvRun);
+        const float *cv = reinterpret_cast<const float *>(in + 2 * kPConvRun);
+        const float *tq = reinterpret_cast<const float *>(in + 3 * kPConvRun);   // conv taps
+        const float *tk = reinterpret_cast<const float *>(in + 4 * kPConvRun);
+        const float *tv = reinterpret_cast<const float *>(in + 5 * kPConvRun);
+        const float *pq = reinterpret_cast<const float *>(in + 6 * kPConvRun);
+        const float *pk = pq + kDim, *pv = pk + kDim, *pz = pv + kDim;
+        float *conv_out = p.conv_out[b];
+        float *sout = p.rec_out[b] + (size_t)h * kDim * kDim;
+
+        // ---- conv + SiLU, L2 norms, gates (gdn_decode_fused_kernel's prologue)
+        {
+            const uint32_t which = threadIdx.x >> 7, i = threadIdx.x & (kDim - 1);
+            const uint32_t c = which * d.key_width + kh * kDim + i;
+            const float *hist = (which == 0 ? cq : ck) + 4 * i;
+            const float hv[4] = {hist[1], hist[2], hist[3], (which == 0 ? pq : pk)[i]};
+            const float *taps = (which == 0 ? tq : tk) + 4 * i;
+            float sconv = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sconv = __fadd_rn(sconv, __fmul_rn(taps[j], hv[j]));
+            if ((h % d.repeat) == 0) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) conv_out[(size_t)c * 4 + j] = hv[j];
+            }
+            const float val = sconv * stable_sigmoid(sconv);
+            bad |= !isfinite(val);
+            float v2 = val * val;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v2 += __shfl_xor_sync(0xffffffffu, v2, o);
+            if (lane == 0) red[warp] = v2;
+            __syncthreads();
+            const float sumsq = red[4 * which] + red[4 * which + 1] + red[4 * which + 2] + red[4 * which + 3];
+            const float inv = 1.0f / sqrtf(sumsq + 1.0e-6f);
+            float out = val * inv;
+            if (which == 0) out = out * (1.0f / sqrtf((float)d.key_dim));
+            (which == 0 ? qs : ks)[i] = out;
+            if (threadIdx.x < kDim) {
+                const uint32_t vc = 2 * d.key_width + h * kDim + threadIdx.x;
+                const float *vh = cv + 4 * threadIdx.x;
+                const float vhv[4] = {vh[1], vh[2], vh[3], pv[threadIdx.x]};
+                const float *vt = tv + 4 * threadIdx.x;
+                float sv = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sv = __fadd_rn(sv, __fmul_rn(vt[j], vhv[j]));
+#pragma unroll
+                for (int j = 0; j < 4; ++j) conv_out[(size_t)vc * 4 + j] = vhv[j];
+                const float vv = sv * stable_sigmoid(sv);
+                bad |= !isfinite(vv);
+                vs[threadIdx.x] = vv;
+            }
+            if (threadIdx.x == 0) {
+                const float bt = stable_sigmoid(pb);
+                const float a = pa + dtb;
+                const float sp = a > 20.0f ? a : log1pf(expf(a));
+                const float g = -expf(alog) * sp;
+                if (!isfinite(g) || g > 0.0f || !isfinite(bt)) gdn_raise(err, kErrDecay);
+                gates[0] = bt;
+                gates[1] = expf(g);
+            }
+            __syncthreads();
+        }
+        // ---- recurrence (one token)
+        {
+            const float dec = gates[1];
+            const float bt = gates[0];
+            float r0 = 0.f, r1 = 0.f, r2 = 0.f, r3 = 0.f;
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) {
+                s[j].x *= dec; s[j].y *= dec; s[j].z *= dec; s[j].w *= dec;
+                const float kv = ks[warp + 8 * j];
+                r0 = fmaf(s[j].x, kv, r0);
+                r1 = fmaf(s[j].y, kv, r1);
+                r2 = fmaf(s[j].z, kv, r2);
+                r3 = fmaf(s[j].w, kv, r3);
+            }
+            *reinterpret_cast<float4 *>(&part[warp][4 * lane]) = make_float4(r0, r1, r2, r3);
+            __syncthreads();
+            if (threadIdx.x < kDim) {
+                float rd = 0.f;
+#pragma unroll
+                for (int wv = 0; wv < kRecThreads / 32; ++wv) rd += part[wv][threadIdx.x];
+                delta[threadIdx.x] = (vs[threadIdx.x] - rd) * bt;
+            }
+            __syncthreads();
+            const float4 dl = *reinterpret_cast<const float4 *>(&delta[4 * lane]);
+            float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+#pragma unroll
+            for (int j = 0; j < kRows; ++j) {
+                const float kv = ks[warp + 8 * j];
+                const float qv = qs[warp + 8 * j];
+                s[j].x = fmaf(kv, dl.x, s[j].x);
+                s[j].y = fmaf(kv, dl.y, s[j].y);
+                s[j].z = fmaf(kv, dl.z, s[j].z);
+                s[j].w = fmaf(kv, dl.w, s[j].w);
+                o0 = fmaf(s[j].x, qv, o0);
+                o1 = fmaf(s[j].y, qv, o1);
+                o2 = fmaf(s[j].z, qv, o2);
+                o3 = fmaf(s[j].w, qv, o3);
+            }
+            *reinterpret_cast<float4 *>(&part[warp][4 * lane]) = make_float4(o0, o1, o2, o3);
+            __syncthreads();
+            float o = 0.f;
+            if (threadIdx.x < kDim) {
+#pragma unroll
+                for (int wv = 0; wv < kRecThreads / 32; ++wv) o += part[wv][threadIdx.x];
+                bad |= !isfinite(o);
+            }
+            const float sumsq = block_sum<kRecThreads>(threadIdx.x < kDim ? o * o : 0.f, red);
+            if (threadIdx.x < kDim) {
+                const float mean = sumsq / (float)kDim;
+                const float inv = 1.0f / sqrtf(mean + d.eps);
+                const float z = pz[threadIdx.x];
+                const float g = (normw * (o * inv)) * stable_sigmoid(z);
+                bad |= !isfinite(g);
+                gated[(size_t)b * d.value_width + gated_head_pos(w, h) * kDim + threadIdx.x] = g;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) {
+            bad |= !isfinite(s[j].x) || !isfinite(s[j].y) || !isfinite(s[j].z) || !isfinite(s[j].w);
+            *reinterpret_cast<float4 *>(sout + (size_t)(warp + 8 * j) * kDim + 4 * lane) = s[j];
+        }
+        __syncthreads();   // ks / qs / vs / part / IN[slot] reads done before the next item overwrites them
+    }
+    if (__syncthreads_or(bad) && threadIdx.x == 0) gdn_raise(err, kErrNonFinite);
+}
+
 // ------------------------------------------------------------ checkpoint path
 //
 // One token, grid (Hv), 128 threads, dynamic shared memory of 2 dk + 2 dv
@@ -674,8 +933,36 @@ bool gdn_decode_fused_supported(const GdnDims &d) {
 void launch_gdn_decode_fused(const GdnDims &d, const GdnWeightsDev &w, const GdnBatchPtrs &p, uint32_t batch,
                              const float *proj, uint32_t ldp, float *gated, ErrorWord err, cudaStream_t stream) {
     KernelTimer timer("gdn_recurrence", stream);
-    launch_pdl(gdn_decode_fused_kernel, dim3(d.value_heads, batch), kRecThreads, 0, stream, d, w, p, proj, ldp,
-               gated, err);
+    // persistent form when every bulk-copy source is 16-byte aligned
+    // (KQ_B200_GDN_PERSIST=0 selects the one-shot kernel: tuning and tests)
+    const char *env = getenv("KQ_B200_GDN_PERSIST");
+    bool persist = !(env && env[0] == '0') && (ldp % 4u) == 0u && (reinterpret_cast<uintptr_t>(proj) & 15u) == 0u &&
+                   (reinterpret_cast<uintptr_t>(w.conv) & 15u) == 0u;
+    for (uint32_t b = 0; b < batch && persist; ++b)
+        persist = (reinterpret_cast<uintptr_t>(p.rec_in[b]) & 15u) == 0u &&
+                  (reinterpret_cast<uintptr_t>(p.conv_in[b]) & 15u) == 0u;
+    if (persist) {
+        static DeviceOnce attr;
+        static int per_sm[64];
+        attr.run([] {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaFuncSetAttribute(gdn_decode_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
+            int n = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gdn_decode_persist_kernel, kRecThreads, kPSmem);
+            per_sm[dev & 63] = n > 0 ? n : 1;
+        });
+        int dev = 0, sms = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const uint32_t items = batch * d.value_heads;
+        const uint32_t grid = std::min<uint32_t>(items, (uint32_t)(std::max(sms, 1) * per_sm[dev & 63]));
+        launch_pdl(gdn_decode_persist_kernel, dim3(grid), kRecThreads, kPSmem, stream, d, w, p, batch, proj, ldp,
+                   gated, err);
+    } else {
+        launch_pdl(gdn_decode_fused_kernel, dim3(d.value_heads, batch), kRecThreads, 0, stream, d, w, p, proj, ldp,
+                   gated, err);
+    }
     count_launch();
 }
 
