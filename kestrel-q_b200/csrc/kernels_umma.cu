@@ -913,9 +913,10 @@ proj_umma_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
 //   1       MMA issue
 //   2       activation producer (one unit per slot, gated by the MMAs), kept
 //           apart from the weight loads so that their HBM latency stays hidden
-//   3..18   decode, two groups of 8 warps taking alternate units, so that one
-//           group's hand-off latency overlaps the other's decoding; lane =
-//           weight row in TMEM quarter (warp & 3), 32 K values of each chunk
+//   3..18   decode, Fact::groups groups taking units in turn, so that a
+//           group's hand-off latency overlaps the others' decoding; lane =
+//           weight row in TMEM quarter (warp & 3), 16 * groups K values of
+//           each chunk
 //   19..26  epilogue: lane = weight row, 32 of the 64 batch columns
 // TMEM columns: accumulators 2 x 128 at 0.  Q4_K: minimum term 64 at 256,
 // three A buffers of 2 x 32 at 320.  Q6_K: A buffers of U x (32 RN + 32
@@ -937,6 +938,13 @@ template <uint32_t T> struct Fact {
     static constexpr bool q4 = T == kTypeQ4_K;
     static constexpr uint32_t U = 2u;                           // chunks per unit
     static constexpr uint32_t kU = q4 ? 3u : 2u;                // units in flight
+    // Decode groups.  A group's consecutive units are `groups` apart and the
+    // group waits on the consumed barrier of unit u + groups - kU; that
+    // barrier's previous phase (unit u + groups - 2 kU) must already be
+    // complete, or the parity test would accept a phase from two completions
+    // ago.  The group waited for unit u - kU before unit u, so groups <= kU.
+    // (Four groups measured no faster than two.)
+    static constexpr uint32_t groups = 2u;
     static constexpr uint32_t dm = 256u;                        // Q4_K minimum term (64 columns)
     static constexpr uint32_t abase = q4 ? 320u : 256u;
     static constexpr uint32_t ecols = q4 ? 0u : U * 32u;        // residual offset in a buffer
@@ -953,6 +961,7 @@ template <uint32_t T> struct Fact {
     static_assert(smem <= 227u * 1024u - 4096u, "shared memory per CTA");
     static_assert(kUM * kUN * 4u <= kU * xslot, "exchange tile");
     static_assert(4u % U == 0u, "units tile a super-block");
+    static_assert(groups <= kU && kFDecodeWarps % (4 * groups) == 0, "decode groups");
 };
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
@@ -1040,6 +1049,7 @@ __device__ __forceinline__ void named_arrive(uint32_t id, uint32_t threads) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 enum NamedBarrier : uint32_t { kBarEpiIn = 1, kBarEpiOut, kBarDecIn, kBarDecOut };   // decode: 2 per group
+constexpr uint32_t kFMaxGroups = 4;   // decode groups (kBarDecIn + 2 * groups - 1 <= 15)
 
 // D (TMEM) += A (shared-memory descriptor) * B (shared-memory descriptor).
 template <uint32_t N>
@@ -1079,7 +1089,7 @@ proj_fact_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
     __shared__ uint64_t dfull[2], dfree[2], xmfull[2], xmfree[2], dready[4], accum;
     __shared__ float dscale[4][kUM];
     __shared__ uint32_t tmem_base_slot, skip_slot;
-    __shared__ volatile uint32_t abort_flag, dec_stop[2], epi_stop;
+    __shared__ volatile uint32_t abort_flag, dec_stop[kFMaxGroups], epi_stop;
     // No early return anywhere: every CTA of a split-K cluster must reach
     // the cluster barriers.
 
@@ -1120,7 +1130,7 @@ proj_fact_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
         for (uint32_t i = 0; i < 4; ++i) mbar_init(&dready[i], 1);
         mbar_init(&accum, 1);
         abort_flag = 0u;
-        dec_stop[0] = dec_stop[1] = 0u;
+        for (uint32_t i = 0; i < kFMaxGroups; ++i) dec_stop[i] = 0u;
         epi_stop = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -1252,16 +1262,18 @@ proj_fact_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
             umma_commit(&accum);   // completes once every MMA this thread issued has
         }
     } else if (warp < kFEpi0) {
-        // ---- decode warps: group g takes units g, g + 2, ...; lane = weight
-        // row within the warp's TMEM quarter, 32 K values of each chunk
-        constexpr uint32_t kGroupWarps = kFDecodeWarps / 2, kGroupThreads = kGroupWarps * 32;
+        // ---- decode warps: group g takes units g, g + groups, ...; lane =
+        // weight row within the warp's TMEM quarter
+        constexpr uint32_t kFGroups = F::groups;
+        constexpr uint32_t kGroupWarps = kFDecodeWarps / kFGroups, kGroupThreads = kGroupWarps * 32;
+        constexpr uint32_t kParts = 16u / kGroupWarps;   // 16-value parts of a chunk per thread
         const uint32_t g = (uint32_t)(warp - kFDecode0) / kGroupWarps;
-        const uint32_t quarter = warp & 3, part = ((uint32_t)(warp - kFDecode0) % kGroupWarps) >> 2;
+        const uint32_t quarter = warp & 3, part0 = ((uint32_t)(warp - kFDecode0) % kGroupWarps >> 2) * kParts;
         const uint32_t row = quarter * 32u + lane;
         const uint32_t lane_addr = (quarter * 32u) << 16;
         const bool leader = (uint32_t)(warp - kFDecode0) % kGroupWarps == 0;
         const uint32_t bar_in = kBarDecIn + 2u * g, bar_out = kBarDecOut + 2u * g;
-        for (uint32_t u = g; u < nunits; u += 2) {
+        for (uint32_t u = g; u < nunits; u += kFGroups) {
             const uint32_t j = u / kPerSb, rs = j % kRR, us = u % kU;
             const bool first = u % kPerSb == 0;
             if (leader) {
@@ -1276,24 +1288,27 @@ proj_fact_kernel(const __grid_constant__ TmapSet tmaps, ProjSegments segs, const
             const uint8_t *rawp = raw_ring + rs * kRaw;
 #pragma unroll
             for (uint32_t c2 = 0; c2 < U; ++c2) {
-                const uint32_t ta = tmem + lane_addr + F::abase + us * F::astride + c2 * 32u + part * 16u;
+                const uint32_t ta0 = tmem + lane_addr + F::abase + us * F::astride + c2 * 32u;
                 if constexpr (kQ4) {
-                    uint32_t a[16];
-                    fact_decode_q4k32(rawp, row, c_begin + u * U + c2, part, a);
-                    tmem_st16(ta, a);
+#pragma unroll
+                    for (uint32_t h = 0; h < kParts; h += 2) {
+                        uint32_t a[16];
+                        fact_decode_q4k32(rawp, row, c_begin + u * U + c2, (part0 + h) >> 1, a);
+                        tmem_st16(ta0 + (part0 + h) * 8u, a);
+                    }
                 } else {
 #pragma unroll
-                    for (uint32_t h = 0; h < 2; ++h) {
+                    for (uint32_t h = 0; h < kParts; ++h) {
                         uint32_t a[8], e[8];
-                        fact_decode_q6k16(rawp, row, c_begin + u * U + c2, 2u * part + h, a, e);
-                        tmem_st8(ta + h * 8u, a);
-                        tmem_st8(ta + h * 8u + F::ecols, e);
+                        fact_decode_q6k16(rawp, row, c_begin + u * U + c2, part0 + h, a, e);
+                        tmem_st8(ta0 + (part0 + h) * 8u, a);
+                        tmem_st8(ta0 + (part0 + h) * 8u + F::ecols, e);
                     }
                 }
             }
             // Q6_K: the super-block's d for the epilogue (Q4_K's comes by TMA)
             const bool head = !kQ4 && first;
-            if (head && part == 0) dscale[j & 3u][row] = q6k_scale(rawp, row, m.cols, c_begin + u * U);
+            if (head && part0 == 0) dscale[j & 3u][row] = q6k_scale(rawp, row, m.cols, c_begin + u * U);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             if (leader) {
