@@ -694,7 +694,7 @@ def decode_record(args, cx: Ctx):
             "step_hbm_frac": step_bytes / (ms * 1e-3) / 1e9 / hbm,
         },
         "roofline": {
-            "kernel": "gdn_decode_fused (conv/gates + recurrence + gated norm; B=64, one GDN layer)",
+            "kernel": "gdn_decode_persist (conv/gates + recurrence + gated norm, persistent with next-item prefetch; B=64, one GDN layer)",
             "bound": "hbm",
             "achieved": achieved,
             "peak": hbm,
