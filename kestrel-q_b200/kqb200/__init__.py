@@ -96,9 +96,9 @@ class GdnLayer:
     provider weights (kq_b200_gdn_config_bind)."""
 
     def __init__(self, dims: synth.GdnDims, weights: synth.GdnLayerWeights | None = None,
-                 provider: Provider | None = None, layer: int = 0):
+                 provider: Provider | None = None, layer: int = 0, activation_dtype: int = 0):
         gd = abi.GdnDimensions(dims.hidden, dims.key_heads, dims.value_heads, dims.key_dim,
-                               dims.value_dim, dims.conv_kernel, dims.eps, 0)
+                               dims.value_dim, dims.conv_kernel, dims.eps, activation_dtype)
         self.handle = C.c_void_p()
         d = abi.Diagnostic()
         abi.check(lib().kq_gdn_test_config_create(C.byref(gd), C.byref(self.handle), C.byref(d)), d)
@@ -188,10 +188,10 @@ def gdn_decode_batch(layer: GdnLayer, states: Sequence[GdnState], x_ptr: int, y_
 
 class QsaLayer:
     def __init__(self, dims: synth.QsaDims, weights: synth.QsaLayerWeights | None = None,
-                 provider: Provider | None = None, layer: int = 3):
+                 provider: Provider | None = None, layer: int = 3, activation_dtype: int = 0):
         qd = abi.QsaDimensions(dims.hidden, dims.query_heads, dims.kv_heads, dims.head_dim, dims.index_heads,
                                dims.index_dim, dims.block, dims.budget, dims.max_context, dims.rotary,
-                               dims.eps, dims.theta, 0)
+                               dims.eps, dims.theta, activation_dtype)
         self.handle = C.c_void_p()
         d = abi.Diagnostic()
         abi.check(lib().kq_qsa_test_config_create(C.byref(qd), C.byref(self.handle), C.byref(d)), d)

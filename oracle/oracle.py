@@ -478,3 +478,99 @@ def qsa_checkpoints(dims, w: dict, x: np.ndarray, key: np.ndarray, value: np.nda
         if state:
             L.kq_qsa_state_close(state)
         L.kq_qsa_config_close(cfg)
+
+
+# ------------------------------------------------------------------ state descriptors
+
+def gdn_state_roundtrip_ref(dims, dtype: int, conv: np.ndarray, rec: np.ndarray, x: np.ndarray, w: dict):
+    """The reference (compiled kq_gdn.c) with activation dtype `dtype` (0 F32,
+    1 BF16; src/kq_gdn.c:109-122,599-701): imports the state, exports it
+    again, and tries one F32 execution (src/kq_gdn_qwen38.c:393-397).
+    Returns (create status, exported conv, exported rec, execute status)."""
+    L = ref()
+    gd = _RefGdnDims(dims.hidden, dims.key_heads, dims.value_heads, dims.key_dim, dims.value_dim,
+                     dims.conv_kernel, dims.eps, dtype)
+    cfg, state = vp(), vp()
+    d = _Diag()
+    st = L.kq_gdn_test_config_create(C.byref(gd), C.byref(cfg), C.byref(d))
+    if st != 0:
+        return st, None, None, None
+    try:
+        if L.kq_gdn_state_create(cfg, C.byref(state), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        c, r = _a(conv).copy(), _a(rec).copy()
+        if L.kq_gdn_state_import_f32(state, c.ctypes.data_as(vp), u64(c.size), r.ctypes.data_as(vp), u64(r.size),
+                                     C.c_int(1), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        c2, r2 = np.zeros_like(c), np.zeros_like(r)
+        init = C.c_int()
+        L.kq_gdn_state_export_f32(state, c2.ctypes.data_as(vp), u64(c2.size), r2.ctypes.data_as(vp), u64(r2.size),
+                                  C.byref(init), C.byref(d))
+        L.kq_gdn_config_scratch_bytes.restype = u64
+        sb = L.kq_gdn_config_scratch_bytes(cfg)
+        scratch = np.empty(sb // 4 + 1, np.float32)
+        gw = _RefGdnWeights()
+        ws = {k: _a(w[k]) for k in GDN_FIELDS}
+        for k in GDN_FIELDS:
+            setattr(gw, k, ws[k].ctypes.data)
+            setattr(gw, k + "_count", ws[k].size)
+        xv = _a(x).reshape(-1, dims.hidden)
+        y = np.zeros_like(xv)
+        est = L.kq_gdn_prefill_f32(cfg, C.byref(gw), xv.ctypes.data_as(vp), u64(xv.shape[0]), None,
+                                   y.ctypes.data_as(vp), u64(y.size), state, scratch.ctypes.data_as(vp), u64(sb),
+                                   None, None, C.byref(d))
+        return 0, c2, r2, est
+    finally:
+        if state:
+            L.kq_gdn_state_close(state)
+        L.kq_gdn_config_close(cfg)
+
+
+def qsa_state_roundtrip_ref(dims, dtype: int, key: np.ndarray, value: np.ndarray, raw: np.ndarray, length: int,
+                            capacity: int, x: np.ndarray | None = None, w: dict | None = None):
+    """The reference (compiled kq_qsa.c) with activation dtype `dtype`
+    (src/kq_qsa.c:80-93,513-620): imports `length` cache rows, exports them
+    again and, given `x` and `w`, tries one F32 prefill of `x`.  Returns
+    (create status, key, value, raw, exported length, execute status or
+    None)."""
+    L = ref()
+    qd = _RefQsaDims(dims.hidden, dims.query_heads, dims.kv_heads, dims.head_dim, dims.index_heads, dims.index_dim,
+                     dims.block, dims.budget, max(capacity, dims.max_context if dims.max_context else capacity),
+                     dims.rotary, dims.eps, dims.theta, dtype)
+    cfg, state = vp(), vp()
+    d = _Diag()
+    st = L.kq_qsa_test_config_create(C.byref(qd), C.byref(cfg), C.byref(d))
+    if st != 0:
+        return st, None, None, None, 0, None
+    try:
+        if L.kq_qsa_state_create(cfg, u64(capacity), C.byref(state), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        k, v, r = _a(key)[:length].copy(), _a(value)[:length].copy(), _a(raw)[:length].copy()
+        if L.kq_qsa_state_import_f32(state, k.ctypes.data_as(vp), u64(k.size), v.ctypes.data_as(vp), u64(v.size),
+                                     r.ctypes.data_as(vp), u64(r.size), u64(length), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        k2, v2, r2 = np.zeros_like(k), np.zeros_like(v), np.zeros_like(r)
+        ln = u64()
+        L.kq_qsa_state_export_f32(state, k2.ctypes.data_as(vp), u64(k2.size), v2.ctypes.data_as(vp), u64(v2.size),
+                                  r2.ctypes.data_as(vp), u64(r2.size), C.byref(ln), C.byref(d))
+        est = None
+        if x is not None:
+            xv = _a(x).reshape(-1, dims.hidden)
+            T = xv.shape[0]
+            need = u64()
+            L.kq_qsa_required_scratch_bytes(cfg, state, u64(T), C.byref(need), C.byref(d))
+            scratch = np.empty(need.value // 4 + 1, np.float32)
+            ws = {k: _a(w[k]) for k in QSA_FIELDS}
+            qw = _RefQsaWeights()
+            for k in QSA_FIELDS:
+                setattr(qw, k, ws[k].ctypes.data)
+                setattr(qw, k + "_count", ws[k].size)
+            y = np.zeros_like(xv)
+            est = L.kq_qsa_prefill_f32(cfg, C.byref(qw), xv.ctypes.data_as(vp), u64(T), y.ctypes.data_as(vp),
+                                       u64(y.size), state, scratch.ctypes.data_as(vp), need, None, None, None,
+                                       C.byref(d))
+        return 0, k2, v2, r2, ln.value, est
+    finally:
+        if state:
+            L.kq_qsa_state_close(state)
+        L.kq_qsa_config_close(cfg)

@@ -340,3 +340,47 @@ def test_q6k_restatement_properties(oracle):
             val = (d[..., None] * scale).astype(np.float32) * code.astype(np.float32)
             want[..., half * 128 + s * 32: half * 128 + s * 32 + 32] = val.astype(np.float32)
     assert np.array_equal(bits(got), bits(want))
+
+
+def _bf16_rne(a):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
+    return r.view(np.float32)
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_reference_state_descriptors(oracle, dtype):
+    """What the B200 descriptor test holds the library to, stated on the
+    reference alone: BF16 configs keep the GDN convolution history and the
+    QSA key/value/raw caches as round-to-nearest-even BF16, the GDN recurrent
+    state stays F32, and F32 execution on a BF16 config is refused with the
+    subsystem's INCOMPATIBLE status (src/kq_gdn.c:599-701,
+    src/kq_qsa.c:513-620, src/kq_gdn_qwen38.c:393-397,
+    src/kq_qsa_qwen38.c:415-418)."""
+    rng = np.random.default_rng(3)
+    v = (rng.standard_normal(4096) * 3).astype(np.float32)
+    u = v.view(np.uint32).copy()
+    u[::5] = (u[::5] & 0xFFFF0000) | 0x8000           # exact ties, odd and even upper halves
+    v = u.view(np.float32)
+    meta, arr = gdn_golden()
+    dims = gdn_dims(meta)
+    nc, nr = arr["c0_conv0"].size, arr["c0_rec0"].size
+    conv, rec = np.resize(v, nc), np.resize(v[::-1], nr)
+    x = rng.standard_normal((2, dims.hidden)).astype(np.float32)
+    st, c2, r2, est = oracle.gdn_state_roundtrip_ref(dims, dtype, conv, rec, x, gdn_weights(arr))
+    assert st == 0
+    assert np.array_equal(bits(c2), bits(_bf16_rne(conv) if dtype else conv))
+    assert np.array_equal(bits(r2), bits(rec))
+    assert (est == 0) if dtype == 0 else (est == 42)     # KQ_STATUS_INCOMPATIBLE_GDN
+    qm, qarr = qsa_golden()
+    qd = qsa_dims(qm)
+    n = 6
+    key = np.resize(v, n * qd.kv_width).reshape(n, -1)
+    val = np.resize(v[1:], n * qd.kv_width).reshape(n, -1)
+    raw = np.resize(v[2:], n * qd.index_dim).reshape(n, -1)
+    w = {k: np.ascontiguousarray(qarr[f"w_{k}"]) for k in QSA_W}
+    st, k2, v2, r2, ln, est = oracle.qsa_state_roundtrip_ref(qd, dtype, key, val, raw, n, 16, x[:, :qd.hidden], w)
+    assert st == 0 and ln == n
+    for got, src in ((k2, key), (v2, val), (r2, raw)):
+        assert np.array_equal(bits(got), bits(_bf16_rne(src) if dtype else src))
+    assert (est == 0) if dtype == 0 else (est != 0)
