@@ -243,5 +243,50 @@ def qsa_cache(seed: int, dims: QsaDims, length: int):
     return k, v, r
 
 
+# ----------------------------------------------------------------- MoE
+
+@dataclass
+class MoeDims:
+    """Routed experts + gated shared expert (target: 512 experts, top-10,
+    hidden 2560, routed / shared intermediate 640)."""
+    hidden: int = 2560
+    experts: int = 512
+    top_k: int = 10
+    routed: int = 640
+    shared: int = 640
+
+
+@dataclass
+class MoeLayerWeights:
+    dims: MoeDims
+    router: QTensor              # [E][H] F32
+    gate: QTensor                # [E*I][H] expert stack (expert-major rows)
+    up: QTensor                  # [E*I][H]
+    down: QTensor                # [E*H][I]
+    shared_gate: QTensor         # [S][H]
+    shared_up: QTensor           # [S][H]
+    shared_down: QTensor         # [H][S]
+    shared_gate_weight: np.ndarray  # [H] F32
+
+
+def moe_layer(seed: int, dims: MoeDims, gate_up_type: int = TYPE_Q4_K, down_type: int = TYPE_Q8_0,
+              shared_type: int = TYPE_Q8_0) -> MoeLayerWeights:
+    """One MoE layer in the target's GGUF types (gate/up Q4_K, down Q8_0,
+    shared Q8_0, router and shared gate F32 ~ N(0, 0.02))."""
+    rng = np.random.default_rng(seed)
+    E, H, I, S = dims.experts, dims.hidden, dims.routed, dims.shared
+    return MoeLayerWeights(
+        dims=dims,
+        router=pack_f32(rng, E, H),
+        gate=pack(gate_up_type, rng, E * I, H),
+        up=pack(gate_up_type, rng, E * I, H),
+        down=pack(down_type, rng, E * H, I),
+        shared_gate=pack(shared_type, rng, S, H),
+        shared_up=pack(shared_type, rng, S, H),
+        shared_down=pack(shared_type, rng, H, S),
+        shared_gate_weight=rng.normal(0.0, 0.02, H).astype(np.float32),
+    )
+
+
 def hidden(seed: int, rows: int, width: int) -> np.ndarray:
     return np.random.default_rng(seed).normal(0.0, 1.0, (rows, width)).astype(np.float32)

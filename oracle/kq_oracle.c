@@ -679,3 +679,183 @@ int kqo_qsa_run_observed(const kqo_qsa_dims *dm, const kqo_qsa_weights *w,
     free(sel);
     return st;
 }
+
+/* ------------------------------------------------------------------- MoE */
+
+/* Top-k of src/kq_moe_qwen38.c:211-245: the first k ids seed the set; a
+ * later id replaces the set's worst entry (lowest value, the lowest id among
+ * equal lowest values) only when strictly greater; the set is then ordered
+ * by value descending, id ascending. */
+static void kqo_moe_top_k(const float *p, uint32_t n, uint32_t k, uint32_t *ids) {
+    uint32_t i;
+    for (i = 0; i < k; ++i) ids[i] = i;
+    for (i = k; i < n; ++i) {
+        uint32_t pos, worst = 0;
+        for (pos = 1; pos < k; ++pos) {
+            uint32_t c = ids[pos], wv = ids[worst];
+            if (p[c] < p[wv] || (p[c] == p[wv] && c < wv)) worst = pos;
+        }
+        if (p[i] > p[ids[worst]]) ids[worst] = i;
+    }
+    for (i = 1; i < k; ++i) {
+        uint32_t v = ids[i], pos = i;
+        while (pos > 0) {
+            uint32_t prev = ids[pos - 1];
+            if (p[prev] > p[v] || (p[prev] == p[v] && prev < v)) break;
+            ids[pos] = prev;
+            pos -= 1;
+        }
+        ids[pos] = v;
+    }
+}
+
+/* SwiGLU of src/kq_numeric.c:700-728: silu(gate) * up, branch-stable sigmoid. */
+static int kqo_swiglu(const float *g, const float *u, uint64_t n, float *out) {
+    uint64_t i;
+    for (i = 0; i < n; ++i) {
+        float s = kqo_sigmoid(g[i]);
+        float silu = g[i] * s;
+        out[i] = silu * u[i];
+        if (!isfinite(out[i])) return KQO_NUMERIC_DOMAIN;
+    }
+    return KQO_OK;
+}
+
+static int kqo_matvec_f32(const float *w, uint64_t rows, uint64_t cols, const float *x, float *y) {
+    uint64_t r;
+    for (r = 0; r < rows; ++r) {
+        y[r] = kqo_dot(w + r * cols, x, cols);
+        if (!isfinite(y[r])) return KQO_NUMERIC_DOMAIN;
+    }
+    return KQO_OK;
+}
+
+static void kqo_moe_emit(kqo_moe_checkpoint_fn cb, void *user, uint32_t kind, uint64_t token, uint32_t expert,
+                         uint32_t position, uint64_t count, const float *values) {
+    uint64_t dims[2];
+    if (cb == NULL) return;
+    dims[0] = count;
+    dims[1] = 0;
+    cb(kind, token, expert, position, 1, dims, values, count, user);
+}
+
+int kqo_moe_run(const kqo_moe_dims *dm, const kqo_moe_weights *w, const float *hidden, uint64_t tokens,
+                float *output, float *logits_out, float *probs_out, uint32_t *ids_out, float *weights_out) {
+    return kqo_moe_run_observed(dm, w, hidden, tokens, output, logits_out, probs_out, ids_out, weights_out,
+                                NULL, NULL);
+}
+
+/* Per-token loop of src/kq_moe_qwen38.c:604-867 over F32 weights: router
+ * logits (kq_f32_dot per expert), softmax (src/kq_numeric.c:776-813), top-k,
+ * renormalised selected weights (:247-274), the selected experts in
+ * ascending id order accumulated as routed_sum + weight * output, then the
+ * shared expert scaled by sigmoid(shared_gate_weight . x).  Checkpoint
+ * kinds follow include/kq_moe.h:24-41 in the reference's emission order.
+ * The output is written only when every token succeeded. */
+int kqo_moe_run_observed(const kqo_moe_dims *dm, const kqo_moe_weights *w, const float *hidden,
+                         uint64_t tokens, float *output, float *logits_out, float *probs_out,
+                         uint32_t *ids_out, float *weights_out, kqo_moe_checkpoint_fn cb, void *user) {
+    const uint64_t H = dm->hidden_size, E = dm->expert_count, K = dm->top_k,
+                   I = dm->routed_intermediate_size, S = dm->shared_intermediate_size;
+    float *buf, *lg, *pr, *sw, *gate, *up, *act, *eo, *wo, *rsum, *sg, *su, *sa, *so, *gs, *staged;
+    uint32_t *ids;
+    uint64_t t, i;
+    int st = KQO_OK;
+    if (H == 0 || E == 0 || K == 0 || K > E || I == 0 || S == 0) return KQO_INVALID_ARGUMENT;
+    for (i = 0; i < tokens * H; ++i)
+        if (!isfinite(hidden[i])) return KQO_NUMERIC_DOMAIN;
+    buf = (float *)malloc(sizeof(float) * (2 * E + K + 3 * I + 3 * H + 3 * S + 2 * H + tokens * H));
+    ids = (uint32_t *)malloc(sizeof(uint32_t) * K);
+    if (buf == NULL || ids == NULL) { free(buf); free(ids); return KQO_INVALID_ARGUMENT; }
+    lg = buf; pr = lg + E; sw = pr + E; gate = sw + K; up = gate + I; act = up + I;
+    eo = act + I; wo = eo + H; rsum = wo + H; sg = rsum + H; su = sg + S; sa = su + S;
+    so = sa + S; gs = so + H; staged = gs + H;
+    for (t = 0; t < tokens && st == KQO_OK; ++t) {
+        const float *x = hidden + t * H;
+        float *y = staged + t * H;
+        float mx, sum = 0.0f, ssum = 0.0f, logit, scale;
+        uint64_t e;
+        st = kqo_matvec_f32(w->router, E, H, x, lg);
+        if (st != KQO_OK) break;
+        mx = lg[0];
+        for (e = 1; e < E; ++e) if (lg[e] > mx) mx = lg[e];
+        for (e = 0; e < E; ++e) {
+            pr[e] = expf(lg[e] - mx);
+            sum = sum + pr[e];
+        }
+        if (!isfinite(sum) || sum <= 0.0f) { st = KQO_NUMERIC_DOMAIN; break; }
+        for (e = 0; e < E; ++e) pr[e] = pr[e] / sum;
+        kqo_moe_top_k(pr, (uint32_t)E, (uint32_t)K, ids);
+        for (i = 0; i < K; ++i) {
+            sw[i] = pr[ids[i]];
+            ssum = ssum + sw[i];
+        }
+        if (!(ssum > 0.0f) || !isfinite(ssum)) { st = KQO_NUMERIC_DOMAIN; break; }
+        for (i = 0; i < K; ++i) {
+            sw[i] = sw[i] / ssum;
+            if (!isfinite(sw[i])) { st = KQO_NUMERIC_DOMAIN; break; }
+        }
+        if (st != KQO_OK) break;
+        if (logits_out) memcpy(logits_out + t * E, lg, sizeof(float) * E);
+        if (probs_out) memcpy(probs_out + t * E, pr, sizeof(float) * E);
+        if (ids_out) memcpy(ids_out + t * K, ids, sizeof(uint32_t) * K);
+        if (weights_out) memcpy(weights_out + t * K, sw, sizeof(float) * K);
+        kqo_moe_emit(cb, user, 0, t, UINT32_MAX, UINT32_MAX, E, lg);   /* ROUTER_LOGITS */
+        kqo_moe_emit(cb, user, 1, t, UINT32_MAX, UINT32_MAX, E, pr);   /* ROUTER_PROBABILITIES */
+        kqo_moe_emit(cb, user, 2, t, UINT32_MAX, UINT32_MAX, K, sw);   /* SELECTED_WEIGHTS */
+        for (i = 0; i < H; ++i) rsum[i] = 0.0f;
+        for (e = 0; e < E && st == KQO_OK; ++e) {
+            uint64_t pos;
+            for (pos = 0; pos < K; ++pos) if (ids[pos] == e) break;
+            if (pos == K) continue;
+            st = kqo_matvec_f32(w->routed_gate + e * I * H, I, H, x, gate);
+            if (st == KQO_OK) st = kqo_matvec_f32(w->routed_up + e * I * H, I, H, x, up);
+            if (st == KQO_OK) st = kqo_swiglu(gate, up, I, act);
+            if (st == KQO_OK) st = kqo_matvec_f32(w->routed_down + e * H * I, H, I, act, eo);
+            if (st != KQO_OK) break;
+            kqo_moe_emit(cb, user, 3, t, (uint32_t)e, (uint32_t)pos, I, gate);   /* ROUTED_GATE */
+            kqo_moe_emit(cb, user, 4, t, (uint32_t)e, (uint32_t)pos, I, up);     /* ROUTED_UP */
+            kqo_moe_emit(cb, user, 5, t, (uint32_t)e, (uint32_t)pos, I, act);    /* ROUTED_ACTIVATED */
+            kqo_moe_emit(cb, user, 6, t, (uint32_t)e, (uint32_t)pos, H, eo);     /* ROUTED_EXPERT_OUTPUT */
+            for (i = 0; i < H; ++i) {
+                wo[i] = eo[i] * sw[pos];
+                if (!isfinite(wo[i])) { st = KQO_NUMERIC_DOMAIN; break; }
+            }
+            if (st != KQO_OK) break;
+            kqo_moe_emit(cb, user, 7, t, (uint32_t)e, (uint32_t)pos, H, wo);     /* ROUTED_WEIGHTED_OUTPUT */
+            for (i = 0; i < H; ++i) {
+                rsum[i] = rsum[i] + wo[i];
+                if (!isfinite(rsum[i])) { st = KQO_NUMERIC_DOMAIN; break; }
+            }
+        }
+        if (st != KQO_OK) break;
+        kqo_moe_emit(cb, user, 8, t, UINT32_MAX, UINT32_MAX, H, rsum);   /* ROUTED_WEIGHTED_SUM */
+        st = kqo_matvec_f32(w->shared_gate, S, H, x, sg);
+        if (st == KQO_OK) st = kqo_matvec_f32(w->shared_up, S, H, x, su);
+        if (st == KQO_OK) st = kqo_swiglu(sg, su, S, sa);
+        if (st == KQO_OK) st = kqo_matvec_f32(w->shared_down, H, S, sa, so);
+        if (st != KQO_OK) break;
+        logit = kqo_dot(w->shared_gate_weight, x, H);
+        if (!isfinite(logit)) { st = KQO_NUMERIC_DOMAIN; break; }
+        scale = kqo_sigmoid(logit);
+        if (!isfinite(scale)) { st = KQO_NUMERIC_DOMAIN; break; }
+        for (i = 0; i < H; ++i) {
+            gs[i] = so[i] * scale;
+            y[i] = rsum[i] + gs[i];
+            if (!isfinite(gs[i]) || !isfinite(y[i])) { st = KQO_NUMERIC_DOMAIN; break; }
+        }
+        if (st != KQO_OK) break;
+        kqo_moe_emit(cb, user, 9, t, UINT32_MAX, UINT32_MAX, S, sg);     /* SHARED_GATE_PROJECTION */
+        kqo_moe_emit(cb, user, 10, t, UINT32_MAX, UINT32_MAX, S, su);    /* SHARED_UP_PROJECTION */
+        kqo_moe_emit(cb, user, 11, t, UINT32_MAX, UINT32_MAX, S, sa);    /* SHARED_ACTIVATED */
+        kqo_moe_emit(cb, user, 12, t, UINT32_MAX, UINT32_MAX, H, so);    /* SHARED_OUTPUT */
+        kqo_moe_emit(cb, user, 13, t, UINT32_MAX, UINT32_MAX, 1, &logit); /* SHARED_SCALE_LOGIT */
+        kqo_moe_emit(cb, user, 14, t, UINT32_MAX, UINT32_MAX, 1, &scale); /* SHARED_SCALE */
+        kqo_moe_emit(cb, user, 15, t, UINT32_MAX, UINT32_MAX, H, gs);    /* GATED_SHARED_OUTPUT */
+        kqo_moe_emit(cb, user, 16, t, UINT32_MAX, UINT32_MAX, H, y);     /* OPERATOR_OUTPUT */
+    }
+    if (st == KQO_OK) memcpy(output, staged, sizeof(float) * tokens * H);
+    free(buf);
+    free(ids);
+    return st;
+}

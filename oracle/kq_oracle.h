@@ -1,5 +1,5 @@
 /*
- * kq_oracle — CPU restatement of Kestrel-Q's GDN / QSA / GGUF-dequant hot path.
+ * kq_oracle — CPU restatement of Kestrel-Q's GDN / QSA / MoE / GGUF-dequant hot path.
  *
  * TEST INFRASTRUCTURE ONLY.  This code is the checker for the B200 kernels: it
  * is loaded by tests/, by __graft_entry__.smoke() and by bench.py's
@@ -134,6 +134,43 @@ int kqo_qsa_run_observed(const kqo_qsa_dims *dims, const kqo_qsa_weights *weight
                          uint64_t capacity, uint64_t *length,
                          uint32_t *selected_ids, uint32_t *selected_counts,
                          float *scores, kqo_checkpoint_fn cb, void *user);
+
+typedef struct kqo_moe_dims {
+    uint32_t hidden_size;
+    uint32_t expert_count;
+    uint32_t top_k;
+    uint32_t routed_intermediate_size;
+    uint32_t shared_intermediate_size;
+} kqo_moe_dims;
+
+typedef struct kqo_moe_weights {
+    const float *router;             /* [E][H] */
+    const float *routed_gate;        /* [E][I][H] */
+    const float *routed_up;          /* [E][I][H] */
+    const float *routed_down;        /* [E][H][I] */
+    const float *shared_gate;        /* [S][H] */
+    const float *shared_up;          /* [S][H] */
+    const float *shared_down;        /* [H][S] */
+    const float *shared_gate_weight; /* [H] */
+} kqo_moe_weights;
+
+/* MoE checkpoint callback: kind is kq_moe_checkpoint_kind (include/kq_moe.h
+ * of the reference); expert and position are UINT32_MAX for token-level
+ * checkpoints. */
+typedef void (*kqo_moe_checkpoint_fn)(uint32_t kind, uint64_t token, uint32_t expert, uint32_t position,
+                                      uint32_t rank, const uint64_t *dims, const float *values, uint64_t count,
+                                      void *user);
+
+/* T tokens through router, top-k experts and the gated shared expert
+ * (src/kq_moe_qwen38.c:604-867).  Optional per-token route outputs:
+ * logits [T][E], probabilities [T][E], selected ids [T][K] (top-k order) and
+ * renormalised weights [T][K]. */
+int kqo_moe_run(const kqo_moe_dims *dims, const kqo_moe_weights *weights, const float *hidden,
+                uint64_t tokens, float *output, float *logits, float *probabilities, uint32_t *selected_ids,
+                float *selected_weights);
+int kqo_moe_run_observed(const kqo_moe_dims *dims, const kqo_moe_weights *weights, const float *hidden,
+                         uint64_t tokens, float *output, float *logits, float *probabilities,
+                         uint32_t *selected_ids, float *selected_weights, kqo_moe_checkpoint_fn cb, void *user);
 
 /* Stable top-k by (score desc, id asc): src/kq_qsa_qwen38.c:328-359. */
 uint64_t kqo_select_blocks(const float *scores, uint64_t count, uint64_t limit,

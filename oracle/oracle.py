@@ -574,3 +574,116 @@ def qsa_state_roundtrip_ref(dims, dtype: int, key: np.ndarray, value: np.ndarray
         if state:
             L.kq_qsa_state_close(state)
         L.kq_qsa_config_close(cfg)
+
+
+# ------------------------------------------------------------------ MoE
+
+MOE_FIELDS = ["router", "routed_gate", "routed_up", "routed_down", "shared_gate", "shared_up", "shared_down",
+              "shared_gate_weight"]
+
+
+class _MoeDims(C.Structure):   # kqo_moe_dims
+    _fields_ = [("hidden_size", u32), ("expert_count", u32), ("top_k", u32), ("routed_intermediate_size", u32),
+                ("shared_intermediate_size", u32)]
+
+
+class _MoeWeights(C.Structure):   # kqo_moe_weights
+    _fields_ = [(n, vp) for n in MOE_FIELDS]
+
+
+class _RefMoeDims(C.Structure):   # src/kq_moe_internal.h:10-17
+    _fields_ = [("hidden_size", u32), ("expert_count", u32), ("top_k", u32), ("routed_intermediate_size", u32),
+                ("shared_intermediate_size", u32), ("activation_dtype", C.c_int)]
+
+
+class _RefMoeWeights(C.Structure):   # include/kq_moe.h:72-89
+    _fields_ = _pairs(MOE_FIELDS)
+
+
+class _RefMoeRoute(C.Structure):   # include/kq_moe.h:58-66
+    _fields_ = [("token_index", u64), ("router_logits", C.POINTER(f32)), ("router_probabilities", C.POINTER(f32)),
+                ("expert_count", u64), ("selected_expert_ids", C.POINTER(u32)),
+                ("selected_weights", C.POINTER(f32)), ("selected_count", u32)]
+
+
+class _RefMoeCheckpoint(C.Structure):   # include/kq_moe.h:43-52
+    _fields_ = [("kind", C.c_int), ("token_index", u64), ("expert_id", u32), ("top_k_position", u32),
+                ("rank", u32), ("dimensions", u64 * 2), ("values", C.POINTER(f32)), ("value_count", u64)]
+
+
+_REF_ROUTE_CB = C.CFUNCTYPE(None, C.POINTER(_RefMoeRoute), vp)
+_REF_MOE_CB = C.CFUNCTYPE(None, C.POINTER(_RefMoeCheckpoint), vp)
+_PORT_MOE_CB = C.CFUNCTYPE(None, u32, u64, u32, u32, u32, C.POINTER(u64), C.POINTER(f32), u64, vp)
+
+
+def moe_weights_f32(layer) -> dict:
+    """Canonical F32 arrays of a synth.MoeLayerWeights (quantized stacks
+    dequantized with the oracle's bit-exact decoders)."""
+    def deq(t):
+        return dequantize(t.type_id, t.data).reshape(-1)
+    return {"router": deq(layer.router), "routed_gate": deq(layer.gate), "routed_up": deq(layer.up),
+            "routed_down": deq(layer.down), "shared_gate": deq(layer.shared_gate), "shared_up": deq(layer.shared_up),
+            "shared_down": deq(layer.shared_down), "shared_gate_weight": _a(layer.shared_gate_weight).reshape(-1)}
+
+
+def moe_run(dims, w: dict, x: np.ndarray, impl: str = "port", checkpoints: bool = False):
+    """T tokens through the MoE operator.  Returns (status, y[T,H], route,
+    checkpoints) with route = dict(logits [T,E], probabilities [T,E], ids
+    [T,K] in top-k order, weights [T,K]) and checkpoints a list of (kind,
+    token, expert, position, values) in emission order (empty unless asked)."""
+    xv = _a(x).reshape(-1, dims.hidden)
+    T, E, K = xv.shape[0], dims.experts, dims.top_k
+    y = np.zeros((T, dims.hidden), np.float32)
+    ws = {k: _a(w[k]).reshape(-1) for k in MOE_FIELDS}
+    route = {"logits": np.zeros((T, E), np.float32), "probabilities": np.zeros((T, E), np.float32),
+             "ids": np.zeros((T, K), np.uint32), "weights": np.zeros((T, K), np.float32)}
+    cps = []
+    if impl == "port":
+        md = _MoeDims(dims.hidden, E, K, dims.routed, dims.shared)
+        mw = _MoeWeights(*[ws[k].ctypes.data for k in MOE_FIELDS])
+
+        def on_cp(kind, token, expert, position, rank, dp, values, count, _u):
+            cps.append((int(kind), int(token), int(expert), int(position),
+                        np.ctypeslib.as_array(values, (count,)).copy()))
+
+        cb = _PORT_MOE_CB(on_cp) if checkpoints else _PORT_MOE_CB()
+        st = port().kqo_moe_run_observed(C.byref(md), C.byref(mw), xv.ctypes.data_as(vp), u64(T),
+                                         y.ctypes.data_as(vp), route["logits"].ctypes.data_as(vp),
+                                         route["probabilities"].ctypes.data_as(vp), route["ids"].ctypes.data_as(vp),
+                                         route["weights"].ctypes.data_as(vp), cb, None)
+        return st, y, route, cps
+    L = ref()
+    qd = _RefMoeDims(dims.hidden, E, K, dims.routed, dims.shared, 0)
+    cfg = vp()
+    d = _Diag()
+    if L.kq_moe_test_config_create(C.byref(qd), C.byref(cfg), C.byref(d)) != 0:
+        raise RuntimeError(d.message)
+    try:
+        L.kq_moe_config_scratch_bytes.restype = u64
+        sb = L.kq_moe_config_scratch_bytes(cfg)
+        scratch = np.empty(sb // 4 + 1, np.float32)
+        mw = _RefMoeWeights()
+        for k in MOE_FIELDS:
+            setattr(mw, k, ws[k].ctypes.data)
+            setattr(mw, k + "_count", ws[k].size)
+
+        def on_route(p, _u):
+            r = p.contents
+            t = r.token_index
+            route["logits"][t] = np.ctypeslib.as_array(r.router_logits, (r.expert_count,))
+            route["probabilities"][t] = np.ctypeslib.as_array(r.router_probabilities, (r.expert_count,))
+            route["ids"][t] = np.ctypeslib.as_array(r.selected_expert_ids, (r.selected_count,))
+            route["weights"][t] = np.ctypeslib.as_array(r.selected_weights, (r.selected_count,))
+
+        def on_cp(p, _u):
+            c = p.contents
+            cps.append((int(c.kind), int(c.token_index), int(c.expert_id), int(c.top_k_position),
+                        np.ctypeslib.as_array(c.values, (c.value_count,)).copy()))
+
+        rcb = _REF_ROUTE_CB(on_route)
+        ccb = _REF_MOE_CB(on_cp) if checkpoints else _REF_MOE_CB()
+        st = L.kq_moe_execute_f32(cfg, C.byref(mw), xv.ctypes.data_as(vp), u64(T), y.ctypes.data_as(vp),
+                                  u64(y.size), scratch.ctypes.data_as(vp), u64(sb), rcb, ccb, None, C.byref(d))
+        return st, y, route, cps
+    finally:
+        L.kq_moe_config_close(cfg)

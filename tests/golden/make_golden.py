@@ -10,6 +10,9 @@ the reference at run time:
   qsa_golden.npz / qsa_golden.json   research/operators/.../qsa-{contract,
                                      calibration,holdout,state-vectors,
                                      selection-vectors,native-validation}.json
+  moe_golden.npz / moe_golden.json   research/operators/.../moe-{contract,
+                                     calibration,holdout,routing-vectors,
+                                     native-validation}.json
   dequant_golden.json                research/numerics/.../dequant-vectors.json
 
 Expected values in those files come from pinned Transformers / llama.cpp
@@ -151,6 +154,61 @@ def qsa(ops: Path) -> None:
     (OUT / "qsa_golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True) + "\n")
 
 
+def moe(ops: Path) -> None:
+    contract = json.loads((ops / "moe-contract.json").read_text())
+    cal = json.loads((ops / "moe-calibration.json").read_text())
+    hold = json.loads((ops / "moe-holdout.json").read_text())
+    routing = json.loads((ops / "moe-routing-vectors.json").read_text())
+    native = json.loads((ops / "moe-native-validation.json").read_text())
+    tier = contract["tier_a_config"]
+    E, H, I = tier["expert_count"], tier["hidden_size"], tier["routed_intermediate_size"]
+    w = contract["weights"]
+    arrays: dict[str, np.ndarray] = {}
+    gate_up = f32(w["experts.gate_up_proj"]).reshape(E, 2 * I, H)   # gate rows, then up rows
+    arrays["w_router"] = f32(w["gate.weight"]).reshape(-1)
+    arrays["w_routed_gate"] = np.ascontiguousarray(gate_up[:, :I, :]).reshape(-1)
+    arrays["w_routed_up"] = np.ascontiguousarray(gate_up[:, I:, :]).reshape(-1)
+    arrays["w_routed_down"] = f32(w["experts.down_proj"]).reshape(-1)
+    arrays["w_shared_gate"] = f32(w["shared_expert.gate_proj.weight"]).reshape(-1)
+    arrays["w_shared_up"] = f32(w["shared_expert.up_proj.weight"]).reshape(-1)
+    arrays["w_shared_down"] = f32(w["shared_expert.down_proj.weight"]).reshape(-1)
+    arrays["w_shared_gate_weight"] = f32(w["shared_expert_gate.weight"]).reshape(-1)
+    fields = ["final_output", "gated_shared_output", "routed_weighted_sum", "router_logits", "router_probabilities",
+              "selected_weights", "shared_activated", "shared_gate", "shared_gate_logit", "shared_gate_projection",
+              "shared_output", "shared_up_projection"]
+    cases = []
+    for split, src in (("calibration", cal["cases"]), ("holdout", hold["cases"])):
+        for c in src:
+            i = len(cases)
+            x = f32(c["input"]).reshape(-1, H)
+            arrays[f"c{i}_input"] = x
+            for k in fields:
+                arrays[f"c{i}_{k}"] = f32(c["expected"][k]).reshape(x.shape[0], -1)
+            experts = []
+            for j, e in enumerate(c["expected"]["selected_experts"]):
+                for k in ("gate", "up", "activated", "output", "weighted_output"):
+                    arrays[f"c{i}_e{j}_{k}"] = f32(e[k]).reshape(-1)
+                experts.append({"token": e["token"], "expert_id": e["expert_id"],
+                                "top_k_position": e["top_k_position"]})
+            cases.append({"id": c["id"], "split": split, "selected_expert_ids": c["expected"]["selected_expert_ids"],
+                          "selected_experts": experts})
+    routing_cases = []
+    for j, c in enumerate(routing["cases"]):
+        arrays[f"r{j}_input"] = f32(c["input"]).reshape(-1, routing["config"]["hidden_size"])
+        arrays[f"r{j}_router"] = f32(c["router_weight"]).reshape(-1)
+        for k in ("router_logits", "router_probabilities", "selected_weights"):
+            arrays[f"r{j}_{k}"] = f32(c["expected"][k]).reshape(arrays[f"r{j}_input"].shape[0], -1)
+        routing_cases.append({"id": c["id"], "selected_expert_ids": c["expected"]["selected_expert_ids"]})
+    contracts = {k: {kk: v[kk] for kk in ("class", "abs_limit", "rel_limit", "ulp_limit")}
+                 for k, v in native["contracts"].items()}
+    meta = {"source": f"Kestrel-Q research/operators/Qwen3.8-Flash-Next/{REV}/moe-*.json",
+            "tier_a_config": tier, "tier_b_config": routing["config"], "routing_contract": contract["routing_contract"],
+            "cases": cases, "routing_cases": routing_cases, "contracts": contracts,
+            "comparison_classes": cal["comparison_classes"]}
+    np.savez_compressed(OUT / "moe_golden.npz", **arrays)
+    (OUT / "moe_golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True) + "\n")
+
+
 def dequant(num: Path) -> None:
     d = json.loads((num / "dequant-vectors.json").read_text())
     keep = {"F32", "BF16", "Q8_0", "Q4_K"}
@@ -173,6 +231,7 @@ def main() -> None:
     root = Path(a.reference) / "research"
     gdn(root / "operators" / "Qwen3.8-Flash-Next" / REV)
     qsa(root / "operators" / "Qwen3.8-Flash-Next" / REV)
+    moe(root / "operators" / "Qwen3.8-Flash-Next" / REV)
     dequant(root / "numerics" / "Qwen3.8-Flash-Next" / REV)
 
 
