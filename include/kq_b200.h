@@ -10,8 +10,11 @@
  *       kq_gdn_execute_quantized    src/kq_gdn_internal.h:81-96
  *       kq_qsa_test_config_create   src/kq_qsa_internal.h:65-68
  *       kq_qsa_execute_quantized    src/kq_qsa_internal.h:94-102
+ *       kq_moe_test_config_create   src/kq_moe_internal.h:45-48
+ *       kq_moe_execute_quantized    src/kq_moe_internal.h:52-60
  *     The dimension records keep the reference's field order and types
- *     (src/kq_gdn_internal.h:11-20, src/kq_qsa_internal.h:11-25).
+ *     (src/kq_gdn_internal.h:11-20, src/kq_qsa_internal.h:11-25,
+ *     src/kq_moe_internal.h:10-17).
  *
  *  2. The device weight provider that stands in for the GGUF-backed one
  *     (src/kq_weight_provider.c:378-509): quantized GGUF blocks are uploaded
@@ -30,6 +33,7 @@
 
 #include "kq_gdn.h"
 #include "kq_model.h"
+#include "kq_moe.h"
 #include "kq_qsa.h"
 #include "kq_status.h"
 #include "kq_weight_provider.h"
@@ -67,6 +71,15 @@ typedef struct kq_qsa_dimensions {
     kq_qsa_activation_dtype activation_dtype;
 } kq_qsa_dimensions;
 
+typedef struct kq_moe_dimensions {
+    uint32_t hidden_size;
+    uint32_t expert_count;
+    uint32_t top_k;
+    uint32_t routed_intermediate_size;
+    uint32_t shared_intermediate_size;
+    kq_moe_activation_dtype activation_dtype;
+} kq_moe_dimensions;
+
 kq_status kq_gdn_test_config_create(const kq_gdn_dimensions *dimensions,
                                     kq_gdn_config **out_config,
                                     kq_diagnostic *diagnostic);
@@ -74,9 +87,16 @@ kq_status kq_qsa_test_config_create(const kq_qsa_dimensions *dimensions,
                                     kq_qsa_config **out_config,
                                     kq_diagnostic *diagnostic);
 
+/* B200 limits on top of the reference's validation: top_k <= 32 and
+ * expert_count <= 8192 (else KQ_STATUS_INCOMPATIBLE_MOE). */
+kq_status kq_moe_test_config_create(const kq_moe_dimensions *dimensions,
+                                    kq_moe_config **out_config,
+                                    kq_diagnostic *diagnostic);
+
 /* Provider mode: weights are the tensors bound to the config with
- * kq_b200_gdn_config_bind / kq_b200_qsa_config_bind.  weight_scratch keeps
- * the reference's minimum-size contract and is otherwise unused. */
+ * kq_b200_gdn_config_bind / kq_b200_qsa_config_bind /
+ * kq_b200_moe_config_bind.  weight_scratch keeps the reference's
+ * minimum-size contract and is otherwise unused. */
 kq_status kq_gdn_execute_quantized(const kq_gdn_config *config,
                                    kq_weight_provider *provider,
                                    const float *hidden_states,
@@ -105,6 +125,21 @@ kq_status kq_qsa_execute_quantized(const kq_qsa_config *config,
                                    uint64_t weight_scratch_bytes,
                                    kq_qsa_selection_observer selection_observer,
                                    kq_qsa_checkpoint_observer checkpoint_observer,
+                                   void *observer_user_data,
+                                   kq_diagnostic *diagnostic);
+
+kq_status kq_moe_execute_quantized(const kq_moe_config *config,
+                                   kq_weight_provider *provider,
+                                   const float *hidden_states,
+                                   uint64_t token_count,
+                                   float *output,
+                                   uint64_t output_capacity,
+                                   void *scratch,
+                                   uint64_t scratch_bytes,
+                                   void *weight_scratch,
+                                   uint64_t weight_scratch_bytes,
+                                   kq_moe_route_observer route_observer,
+                                   kq_moe_checkpoint_observer checkpoint_observer,
                                    void *observer_user_data,
                                    kq_diagnostic *diagnostic);
 
@@ -204,6 +239,40 @@ kq_status kq_b200_provider_add_index_qk(kq_weight_provider *provider,
                                         const kq_semantic_tensor **out_tensor,
                                         kq_diagnostic *diagnostic);
 
+/* Uploads a routed-expert stack: `experts` matrices of rows x columns GGUF
+ * rows, expert-major (the model GGUF's [experts][rows][columns] tensor,
+ * e.g. blk.N.ffn_down_exps).  kq_weight_provider_linear_f32 reads one
+ * expert's matrix by its expert id. */
+kq_status kq_b200_provider_add_expert_stack(kq_weight_provider *provider,
+                                            const char *semantic_id,
+                                            kq_semantic_role role,
+                                            uint32_t type_id,
+                                            uint32_t experts,
+                                            uint64_t rows,
+                                            uint64_t columns,
+                                            const void *packed,
+                                            uint64_t packed_bytes,
+                                            const kq_semantic_tensor **out_tensor,
+                                            kq_diagnostic *diagnostic);
+
+/* Uploads the routed gate/up projection the way the model's GGUF splits it:
+ * one KQ_ROLE_ROUTED_GATE_UP semantic with a GATE part (ffn_gate_exps) and
+ * an UP part (ffn_up_exps), each an expert stack of rows x columns
+ * matrices (src/kq_model.c:1055-1096).  kq_weight_provider_linear_f32 reads
+ * a part by its part role and expert id. */
+kq_status kq_b200_provider_add_expert_gate_up(kq_weight_provider *provider,
+                                             const char *semantic_id,
+                                             uint32_t type_id,
+                                             uint32_t experts,
+                                             uint64_t rows,
+                                             uint64_t columns,
+                                             const void *gate_packed,
+                                             uint64_t gate_bytes,
+                                             const void *up_packed,
+                                             uint64_t up_bytes,
+                                             const kq_semantic_tensor **out_tensor,
+                                             kq_diagnostic *diagnostic);
+
 /* Batched form of kq_weight_provider_linear_f32:
  * y[b][r] = sum_c W[r][c] * x[b][c] for b < batch, with x [batch][columns]
  * and y [batch][rows] device arrays.  Batches above 8 run on the tensor
@@ -264,6 +333,17 @@ typedef struct kq_b200_gdn_tensors {
     const kq_semantic_tensor *output;   /* matrix [H x Hv*dv] */
 } kq_b200_gdn_tensors;
 
+/* MoE weights in the reference's role order (src/kq_moe.c:27-54). */
+typedef struct kq_b200_moe_tensors {
+    const kq_semantic_tensor *router;             /* matrix [E x H] */
+    const kq_semantic_tensor *routed_down;        /* expert stack [E][H x I] */
+    const kq_semantic_tensor *routed_gate_up;     /* gate/up expert stacks [E][I x H] */
+    const kq_semantic_tensor *shared_down;        /* matrix [H x S] */
+    const kq_semantic_tensor *shared_gate;        /* matrix [S x H] */
+    const kq_semantic_tensor *shared_up;          /* matrix [S x H] */
+    const kq_semantic_tensor *shared_gate_weight; /* matrix [1 x H] */
+} kq_b200_moe_tensors;
+
 typedef struct kq_b200_qsa_tensors {
     const kq_semantic_tensor *query;            /* [2*Hq*d x H], q/gate interleaved per head */
     const kq_semantic_tensor *key;              /* [Hkv*d x H] */
@@ -286,6 +366,10 @@ kq_status kq_b200_gdn_config_bind(kq_gdn_config *config,
 kq_status kq_b200_qsa_config_bind(kq_qsa_config *config,
                                   kq_weight_provider *provider,
                                   const kq_b200_qsa_tensors *tensors,
+                                  kq_diagnostic *diagnostic);
+kq_status kq_b200_moe_config_bind(kq_moe_config *config,
+                                  kq_weight_provider *provider,
+                                  const kq_b200_moe_tensors *tensors,
                                   kq_diagnostic *diagnostic);
 
 /* ---------------------------------------------------------------- group 3 */
@@ -314,6 +398,17 @@ kq_status kq_b200_qsa_decode_batch(const kq_qsa_config *config,
                                    const float *hidden,
                                    float *output,
                                    kq_diagnostic *diagnostic);
+
+/* kq_moe_execute_quantized over device arrays hidden / output
+ * [tokens][hidden_size] of a provider-bound config, without observers,
+ * asynchronous on the library stream: non-finite values surface at
+ * kq_b200_synchronize (output then undefined).  Every token is independent,
+ * so a batch of decode tokens of many sequences is one call. */
+kq_status kq_b200_moe_execute_async(const kq_moe_config *config,
+                                    const float *hidden,
+                                    uint64_t tokens,
+                                    float *output,
+                                    kq_diagnostic *diagnostic);
 
 /* T tokens of one sequence, like kq_gdn_execute_quantized /
  * kq_qsa_execute_quantized (src/kq_gdn_internal.h:81-96,

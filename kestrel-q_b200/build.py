@@ -31,11 +31,13 @@ SOURCES = [
     "kernels_gdn_chunk.cu",
     "kernels_qsa.cu",
     "kernels_umma.cu",
+    "kernels_moe.cu",
     "runtime.cpp",
     "api_basic.cpp",
     "api_provider.cpp",
     "api_gdn.cpp",
     "api_qsa.cpp",
+    "api_moe.cpp",
     "api_static.cu",
 ]
 

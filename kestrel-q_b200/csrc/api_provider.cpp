@@ -81,8 +81,9 @@ ProviderTensor *provider_part(const kq_weight_provider *provider, const kq_seman
     ProviderTensor *t = provider_lookup(provider, semantic);
     if (t == nullptr) return nullptr;
     if (t->parts[0] == nullptr) return part_role == KQ_BINDING_PART_WHOLE ? t : nullptr;
-    if (part_role == KQ_BINDING_PART_INDEX_QUERY) return t->parts[0];
-    if (part_role == KQ_BINDING_PART_INDEX_KEY) return t->parts[1];
+    const kq_binding_part_role first = t->desc.bindings[0].part_role, second = t->desc.bindings[1].part_role;
+    if (part_role == first) return t->parts[0];
+    if (part_role == second) return t->parts[1];
     return nullptr;
 }
 
@@ -170,15 +171,17 @@ void kq_weight_provider_close(kq_weight_provider *provider) {
     delete provider;
 }
 
-kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *semantic_id,
-                                      kq_semantic_role role, uint32_t type_id, uint64_t rows,
-                                      uint64_t columns, const void *packed, uint64_t packed_bytes,
-                                      const kq_semantic_tensor **out_tensor,
-                                      kq_diagnostic *diagnostic) {
-    kq_diagnostic_clear(diagnostic);
-    if (out_tensor) *out_tensor = nullptr;
-    if (provider == nullptr || provider->magic != kProviderMagic || packed == nullptr ||
-        out_tensor == nullptr || rows == 0 || columns == 0)
+}  // extern "C"
+
+// Uploads rows x columns GGUF rows (see kq_b200_provider_add_matrix).
+// `side_data` builds the Q4_K side data of the factored tensor-core kernel
+// (not for expert stacks, whose experts the grouped MoE kernels read).
+static kq_status upload_matrix(kq_weight_provider *provider, const char *semantic_id, kq_semantic_role role,
+                               uint32_t type_id, uint64_t rows, uint64_t columns, const void *packed,
+                               uint64_t packed_bytes, bool side_data, ProviderTensor **out,
+                               kq_diagnostic *diagnostic) {
+    *out = nullptr;
+    if (provider == nullptr || provider->magic != kProviderMagic || packed == nullptr || rows == 0 || columns == 0)
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, data and output are required");
     uint32_t be, bb;
     if (!block_geometry(type_id, be, bb))
@@ -227,7 +230,7 @@ kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *
     // (kernels.hpp q4k_build_aux) follows the blocks in the same allocation
     const uint64_t aux_offset = (total + 255) & ~uint64_t(255);
     std::vector<uint8_t> aux;
-    if (type_id == KQ_GGUF_TYPE_Q4_K) {
+    if (type_id == KQ_GGUF_TYPE_Q4_K && side_data) {
         aux.resize(q4k_aux_bytes((uint32_t)rows, (uint32_t)columns));
         q4k_build_aux(static_cast<const uint8_t *>(packed), (uint32_t)rows, (uint32_t)columns, scale_exp,
                       aux.data());
@@ -260,6 +263,93 @@ kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *
     t->desc.canonical_dimensions[0] = rows;
     t->desc.canonical_dimensions[1] = columns;
     provider->metrics.provider_owned_bytes += alloc;
+    *out = t;
+    return KQ_STATUS_OK;
+}
+
+extern "C" {
+
+kq_status kq_b200_provider_add_matrix(kq_weight_provider *provider, const char *semantic_id,
+                                      kq_semantic_role role, uint32_t type_id, uint64_t rows,
+                                      uint64_t columns, const void *packed, uint64_t packed_bytes,
+                                      const kq_semantic_tensor **out_tensor,
+                                      kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_tensor) *out_tensor = nullptr;
+    if (out_tensor == nullptr) return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "output is required");
+    ProviderTensor *t;
+    kq_status st = upload_matrix(provider, semantic_id, role, type_id, rows, columns, packed, packed_bytes, true, &t,
+                                 diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    *out_tensor = &t->desc;
+    return KQ_STATUS_OK;
+}
+
+kq_status kq_b200_provider_add_expert_stack(kq_weight_provider *provider, const char *semantic_id,
+                                            kq_semantic_role role, uint32_t type_id, uint32_t experts,
+                                            uint64_t rows, uint64_t columns, const void *packed,
+                                            uint64_t packed_bytes, const kq_semantic_tensor **out_tensor,
+                                            kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_tensor) *out_tensor = nullptr;
+    uint64_t total_rows;
+    if (out_tensor == nullptr || experts == 0 || rows == 0)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "experts, rows and output are required");
+    if (!mul_ok(rows, experts, &total_rows) || rows > UINT32_MAX)
+        return fail(diagnostic, KQ_STATUS_ARITHMETIC_OVERFLOW, "expert stack size overflows");
+    ProviderTensor *t;
+    kq_status st = upload_matrix(provider, semantic_id, role, type_id, total_rows, columns, packed, packed_bytes,
+                                 false, &t, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    t->experts = experts;
+    t->expert_rows = (uint32_t)rows;
+    t->desc.canonical_rank = 3;
+    t->desc.canonical_dimensions[0] = experts;
+    t->desc.canonical_dimensions[1] = rows;
+    t->desc.canonical_dimensions[2] = columns;
+    t->desc.canonical_expert_axis = 0;
+    t->desc.expert_count = experts;
+    *out_tensor = &t->desc;
+    return KQ_STATUS_OK;
+}
+
+kq_status kq_b200_provider_add_expert_gate_up(kq_weight_provider *provider, const char *semantic_id,
+                                             uint32_t type_id, uint32_t experts, uint64_t rows, uint64_t columns,
+                                             const void *gate_packed, uint64_t gate_bytes, const void *up_packed,
+                                             uint64_t up_bytes, const kq_semantic_tensor **out_tensor,
+                                             kq_diagnostic *diagnostic) {
+    kq_diagnostic_clear(diagnostic);
+    if (out_tensor) *out_tensor = nullptr;
+    if (provider == nullptr || provider->magic != kProviderMagic || out_tensor == nullptr)
+        return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider and output are required");
+    const kq_semantic_tensor *g = nullptr, *u = nullptr;
+    const std::string base = semantic_id ? semantic_id : "gate_up";
+    kq_status st = kq_b200_provider_add_expert_stack(provider, (base + ".gate").c_str(), KQ_ROLE_ROUTED_GATE_UP,
+                                                     type_id, experts, rows, columns, gate_packed, gate_bytes, &g,
+                                                     diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    st = kq_b200_provider_add_expert_stack(provider, (base + ".up").c_str(), KQ_ROLE_ROUTED_GATE_UP, type_id,
+                                           experts, rows, columns, up_packed, up_bytes, &u, diagnostic);
+    if (st != KQ_STATUS_OK) return st;
+    // one semantic, two bindings: GATE (part 0 of 2), UP (part 1 of 2), the
+    // order of src/kq_model.c:1083-1094 and src/kq_tensor_view.c:333-334
+    ProviderTensor *t = new_tensor(provider, semantic_id, KQ_ROLE_ROUTED_GATE_UP);
+    t->parts[0] = provider_lookup(provider, g);
+    t->parts[1] = provider_lookup(provider, u);
+    t->desc.relation = KQ_BINDING_ONE_CANONICAL_TO_MULTIPLE_PHYSICAL;
+    t->desc.canonical_rank = 3;
+    t->desc.canonical_dimensions[0] = experts;
+    t->desc.canonical_dimensions[1] = 2 * rows;
+    t->desc.canonical_dimensions[2] = columns;
+    t->desc.canonical_expert_axis = 0;
+    t->desc.expert_count = experts;
+    t->desc.binding_count = 2;
+    t->desc.bindings[0].part_role = KQ_BINDING_PART_GATE;
+    t->desc.bindings[0].part_index = 0;
+    t->desc.bindings[0].part_count = 2;
+    t->desc.bindings[1].part_role = KQ_BINDING_PART_UP;
+    t->desc.bindings[1].part_index = 1;
+    t->desc.bindings[1].part_count = 2;
     *out_tensor = &t->desc;
     return KQ_STATUS_OK;
 }
@@ -313,9 +403,20 @@ kq_status kq_weight_provider_linear_f32(kq_weight_provider *provider,
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, semantic and buffers are required");
     // a split semantic is read by part (src/kq_weight_provider.c:250-262)
     t = provider_part(provider, semantic, part_role);
-    if (t == nullptr || t->is_vector || expert_id != KQ_WEIGHT_PROVIDER_NO_EXPERT)
+    if (t == nullptr || t->is_vector)
         return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "requested semantic binding part is absent");
-    if (rows != t->m.rows || columns != t->m.cols)
+    // an expert stack is read one expert at a time (src/kq_weight_provider.c:250-272)
+    QMatrix m = t->m;
+    if (expert_id != KQ_WEIGHT_PROVIDER_NO_EXPERT) {
+        if (t->experts == 0 || expert_id >= t->experts)
+            return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "selected expert ID is outside the semantic stack");
+        m.data += (size_t)expert_id * t->expert_rows * m.row_bytes;
+        m.rows = t->expert_rows;
+        m.aux = nullptr;
+    } else if (t->experts != 0) {
+        return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "routed expert stack requires an explicit expert ID");
+    }
+    if (rows != m.rows || columns != m.cols)
         return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "linear shape does not match the semantic");
     if (output_capacity < rows) return fail(diagnostic, KQ_STATUS_BUFFER_TOO_SMALL, "linear output is too small");
     if (ranges_overlap(input, columns * 4, output, rows * 4))
@@ -361,7 +462,7 @@ kq_status kq_weight_provider_linear_f32(kq_weight_provider *provider,
     launch_check_finite(x, columns, err, c->stream);
     ProjSegments segs{};
     segs.count = 1;
-    segs.m[0] = t->m;
+    segs.m[0] = m;
     segs.out_offset[0] = 0;
     launch_projection(segs, x, (uint32_t)columns, y, (uint32_t)rows, 1, err, c->stream);
     launch_check_finite(y, rows, err, c->stream);
@@ -372,7 +473,8 @@ kq_status kq_weight_provider_linear_f32(kq_weight_provider *provider,
              diagnostic, "linear output");
     provider->metrics.linear_requests += 1;
     provider->metrics.row_requests += rows;
-    provider->metrics.logical_payload_bytes_touched += t->bytes;
+    provider->metrics.logical_payload_bytes_touched += (uint64_t)m.rows * m.row_bytes;
+    if (expert_id != KQ_WEIGHT_PROVIDER_NO_EXPERT) provider->metrics.selected_expert_requests += 1;
     return KQ_STATUS_OK;
 }
 
@@ -384,7 +486,7 @@ kq_status kq_b200_provider_linear_batch_f32(kq_weight_provider *provider,
     ProviderTensor *t = provider_lookup(provider, semantic);
     if (t == nullptr || x == nullptr || y == nullptr || batch == 0)
         return fail(diagnostic, KQ_STATUS_INVALID_ARGUMENT, "valid provider, semantic and buffers are required");
-    if (t->is_vector || t->parts[0] != nullptr)
+    if (t->is_vector || t->parts[0] != nullptr || t->experts != 0)
         return fail(diagnostic, KQ_STATUS_TENSOR_LAYOUT_MISMATCH, "semantic is not a whole matrix");
     if (rows != t->m.rows || columns != t->m.cols)
         return fail(diagnostic, KQ_STATUS_DIMENSION_MISMATCH, "linear shape does not match the semantic");

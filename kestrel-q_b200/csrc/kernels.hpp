@@ -381,6 +381,65 @@ void launch_qsa_block_keys(const QsaDims &d, const QsaWeightsDev &w,
                            uint32_t end_block, ErrorWord err,
                            cudaStream_t stream);
 
+// ---- MoE (kernels_moe.cu)
+constexpr uint32_t kMoeMaxTopK = 32;
+constexpr uint32_t kMoeMaxExperts = 8192;
+
+struct MoeDims {
+    uint32_t hidden, experts, top_k, routed, shared;
+};
+
+// Device weights: router [E x H] and shared gate weight [1 x H] (exact
+// products), expert stacks gate / up [E*I x H] and down [E*H x I]
+// (expert-major rows), shared gate / up [S x H], shared down [H x S].
+struct MoeWeightsDev {
+    QMatrix router, gate, up, down, shared_gate, shared_up, shared_down, shared_gate_weight;
+};
+
+// Intermediate values kept for the checkpoint observer (all null when not
+// observed): routed gate / up [picks][I] and weighted outputs [picks][H] by
+// slot, routed sum and gated shared output [T][H], (shared logit, scale)
+// [T][2].
+struct MoeDebug {
+    float *gate, *up, *weighted, *routed_sum, *gated_shared, *scale;
+};
+
+// Work space of one call over T tokens (moe_carve).  Picks p = t*K + k;
+// slots are expert-major.
+struct MoeBuffers {
+    float *logits;          // [T][E+1]: router logits, then the shared gate logit
+    float *probs;           // [T][E]
+    uint32_t *sel_ids;      // [T][K], top-k order
+    float *sel_w;           // [T][K]
+    uint32_t *counts;       // [E]
+    uint32_t *offsets;      // [E+1]
+    uint32_t *active;       // [1+E]: active expert count, then their ids
+    uint32_t *rank;         // [picks] position among the expert's picks
+    uint32_t *slot;         // [picks] pick -> slot
+    uint32_t *pick_of_slot; // [picks] slot -> pick
+    float *act;             // [picks][I] by slot
+    float *eout;            // [picks][H] by slot
+    float *shared_gu;       // [T][2S]
+    float *shared_act;      // [T][S]
+    float *shared_out;      // [T][H]
+    float *proj_gu, *proj_down;   // tensor-core projection work space
+    size_t proj_floats_gu, proj_floats_down;
+    MoeDebug dbg;
+};
+
+size_t moe_workspace_bytes(const MoeDims &d, uint32_t T, bool debug);
+void moe_carve(const MoeDims &d, uint32_t T, bool debug, void *ws, MoeBuffers &b);
+// The whole operator on device arrays x [T][H] -> y [T][H].
+void launch_moe(const MoeDims &d, const MoeWeightsDev &w, const float *x, uint32_t T, float *y, MoeBuffers &b,
+                ErrorWord err, cudaStream_t stream);
+// Its stages (launch_moe runs router, route, dispatch, experts, shared
+// expert, combine).
+void launch_moe_route(const MoeDims &d, const float *logits, uint32_t ldl, uint32_t T, MoeBuffers &b,
+                      ErrorWord err, cudaStream_t stream);
+void launch_moe_dispatch(const MoeDims &d, uint32_t T, MoeBuffers &b, ErrorWord err, cudaStream_t stream);
+void launch_moe_experts(const MoeDims &d, const MoeWeightsDev &w, const float *x, uint32_t ldx, uint32_t T,
+                        MoeBuffers &b, ErrorWord err, cudaStream_t stream);
+
 uint64_t launches_total();
 bool force_simt_projection();
 void count_launch();

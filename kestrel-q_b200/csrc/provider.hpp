@@ -26,8 +26,13 @@ struct ProviderTensor {
     int32_t *col_heads_dev = nullptr;
     uint32_t head_width = 0;
     // A semantic stored as two separate tensors (the QSA index projection:
-    // INDEX_QUERY then INDEX_KEY part), each its own record.
+    // INDEX_QUERY then INDEX_KEY part; the routed gate/up projection: GATE
+    // then UP part), each its own record.
     ProviderTensor *parts[2] = {nullptr, nullptr};
+    // A routed-expert stack: `experts` matrices of `expert_rows` rows each,
+    // expert-major in `m` (0 for plain matrices).
+    uint32_t experts = 0;
+    uint32_t expert_rows = 0;
 };
 
 // The record of `semantic`'s binding part `part_role`: the semantic itself

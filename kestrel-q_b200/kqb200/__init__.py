@@ -88,7 +88,8 @@ class Provider:
 # roles (include/kq_model.h)
 ROLE = {"a_log": 6, "conv": 7, "dt_bias": 8, "alpha": 9, "beta": 10, "qkv": 11, "gate": 12, "norm": 13,
         "out": 14, "k_norm": 15, "k": 16, "o": 17, "q_norm": 18, "q": 19, "v": 20, "index_qk": 21,
-        "index_k_norm": 22, "index_q_norm": 23}
+        "index_k_norm": 22, "index_q_norm": 23, "moe_router": 24, "routed_down": 25, "routed_gate_up": 26,
+        "shared_down": 27, "shared_gate": 28, "shared_up": 29, "shared_gate_weight": 30}
 
 
 class GdnLayer:
@@ -295,6 +296,113 @@ def qsa_decode_batch(layer: QsaLayer, states: Sequence[QsaState], x_ptr: int, y_
     arr = (C.c_void_p * len(states))(*[s.handle.value for s in states])
     d = abi.Diagnostic()
     abi.check(lib().kq_b200_qsa_decode_batch(layer.handle, arr, len(states), x_ptr, y_ptr, C.byref(d)), d)
+
+
+class MoeLayer:
+    """An MoE test config (kq_moe_test_config_create), optionally bound to
+    provider weights (kq_b200_moe_config_bind): router F32 matrix, gate/up as
+    one split semantic of two expert stacks, down as an expert stack, the
+    shared expert's three matrices and its [1 x H] gate weight."""
+
+    def __init__(self, dims: synth.MoeDims, weights: synth.MoeLayerWeights | None = None,
+                 provider: Provider | None = None, layer: int = 0, activation_dtype: int = 0):
+        md = abi.MoeDimensions(dims.hidden, dims.experts, dims.top_k, dims.routed, dims.shared, activation_dtype)
+        self.handle = C.c_void_p()
+        d = abi.Diagnostic()
+        abi.check(lib().kq_moe_test_config_create(C.byref(md), C.byref(self.handle), C.byref(d)), d)
+        self.dims = dims
+        self.provider = provider
+        self.tensors = None
+        if weights is not None:
+            assert provider is not None
+            p, L = provider, lib()
+            E, H, I = dims.experts, dims.hidden, dims.routed
+
+            def stack(name, role, t, rows, cols):
+                out = C.c_void_p()
+                data = np.ascontiguousarray(t.data)
+                abi.check(L.kq_b200_provider_add_expert_stack(p.handle, name.encode(), role, t.type_id, E, rows, cols,
+                                                              data.ctypes.data, data.size, C.byref(out),
+                                                              C.byref(d)), d)
+                return out.value
+
+            gu = C.c_void_p()
+            g, u = np.ascontiguousarray(weights.gate.data), np.ascontiguousarray(weights.up.data)
+            abi.check(L.kq_b200_provider_add_expert_gate_up(p.handle, f"l{layer}.moe.gate_up".encode(),
+                                                            weights.gate.type_id, E, I, H, g.ctypes.data, g.size,
+                                                            u.ctypes.data, u.size, C.byref(gu), C.byref(d)), d)
+            gw = synth.f32_tensor(weights.shared_gate_weight.reshape(1, -1))
+            t = abi.MoeTensors(
+                router=p.add_matrix(f"l{layer}.moe.router", ROLE["moe_router"], weights.router),
+                routed_down=stack(f"l{layer}.moe.down", ROLE["routed_down"], weights.down, H, I),
+                routed_gate_up=gu.value,
+                shared_down=p.add_matrix(f"l{layer}.moe.shared_down", ROLE["shared_down"], weights.shared_down),
+                shared_gate=p.add_matrix(f"l{layer}.moe.shared_gate", ROLE["shared_gate"], weights.shared_gate),
+                shared_up=p.add_matrix(f"l{layer}.moe.shared_up", ROLE["shared_up"], weights.shared_up),
+                shared_gate_weight=p.add_matrix(f"l{layer}.moe.shared_gate_weight", ROLE["shared_gate_weight"], gw))
+            self.tensors = t
+            abi.check(L.kq_b200_moe_config_bind(self.handle, p.handle, C.byref(t), C.byref(d)), d)
+
+    @property
+    def scratch_bytes(self) -> int:
+        return lib().kq_moe_config_scratch_bytes(self.handle)
+
+    def _run(self, fn, first, x, route: bool, checkpoints: bool):
+        xv = _f32(x)
+        T = xv.shape[0]
+        y = np.zeros((T, self.dims.hidden), np.float32)
+        scratch = np.zeros(self.scratch_bytes // 4 + 1, np.float32)
+        routes, cps = [], []
+
+        def on_route(p, _u):
+            r = p.contents
+            routes.append({"token": int(r.token_index),
+                           "logits": np.ctypeslib.as_array(r.router_logits, (r.expert_count,)).copy(),
+                           "probabilities": np.ctypeslib.as_array(r.router_probabilities, (r.expert_count,)).copy(),
+                           "ids": np.ctypeslib.as_array(r.selected_expert_ids, (r.selected_count,)).copy(),
+                           "weights": np.ctypeslib.as_array(r.selected_weights, (r.selected_count,)).copy()})
+
+        def on_cp(p, _u):
+            c = p.contents
+            cps.append((int(c.kind), int(c.token_index), int(c.expert_id), int(c.top_k_position),
+                        np.ctypeslib.as_array(c.values, (c.value_count,)).copy()))
+
+        rcb = abi.MOE_ROUTE_OBSERVER(on_route) if route else abi.MOE_ROUTE_OBSERVER()
+        ccb = abi.MOE_CHECKPOINT_OBSERVER(on_cp) if checkpoints else abi.MOE_CHECKPOINT_OBSERVER()
+        d = abi.Diagnostic()
+        st = fn(*first, xv.ctypes.data, T, y.ctypes.data, y.size, scratch.ctypes.data, scratch.nbytes, rcb, ccb,
+                None, C.byref(d))
+        return st, y, routes, cps, d
+
+    def execute_quantized(self, x: np.ndarray, route: bool = False, checkpoints: bool = False):
+        """(status, y, routes, checkpoints, diagnostic) of kq_moe_execute_quantized."""
+        ws = np.zeros(16384 + 1, np.float32)
+        L = lib()
+
+        def call(cfg, prov, xp, T, yp, cap, sp, sb, rcb, ccb, user, dp):
+            return L.kq_moe_execute_quantized(cfg, prov, xp, T, yp, cap, sp, sb, ws.ctypes.data, ws.nbytes, rcb, ccb,
+                                              user, dp)
+        return self._run(call, (self.handle, self.provider.handle), x, route, checkpoints)
+
+    def execute_f32(self, w: dict, x: np.ndarray, route: bool = False, checkpoints: bool = False):
+        """(status, y, routes, checkpoints, diagnostic) of kq_moe_execute_f32
+        with canonical F32 weights `w` (abi.MOE_WEIGHT_FIELDS)."""
+        arrs = {k: _f32(np.asarray(w[k]).reshape(-1)) for k in abi.MOE_WEIGHT_FIELDS}
+        mw = abi.MoeWeightsF32()
+        for k in abi.MOE_WEIGHT_FIELDS:
+            setattr(mw, k, arrs[k].ctypes.data)
+            setattr(mw, k + "_count", arrs[k].size)
+        return self._run(lib().kq_moe_execute_f32, (self.handle, C.byref(mw)), x, route, checkpoints)
+
+    def close(self):
+        if self.handle:
+            lib().kq_moe_config_close(self.handle)
+            self.handle = C.c_void_p()
+
+
+def moe_execute_async(layer: MoeLayer, x_ptr: int, tokens: int, y_ptr: int) -> None:
+    d = abi.Diagnostic()
+    abi.check(lib().kq_b200_moe_execute_async(layer.handle, x_ptr, tokens, y_ptr, C.byref(d)), d)
 
 
 def gdn_prefill_async(state: GdnState, x_ptr: int, tokens: int, y_ptr: int) -> None:

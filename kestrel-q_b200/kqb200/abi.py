@@ -34,6 +34,7 @@ INCOMPATIBLE_GDN = 42
 INVALID_GDN_STATE = 43
 INCOMPATIBLE_QSA = 44
 INVALID_QSA_STATE = 45
+INCOMPATIBLE_MOE = 46
 
 TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_BF16 = 0, 8, 12, 14, 30
 
@@ -71,12 +72,35 @@ def _pair_fields(names):
     return out
 
 
+MOE_WEIGHT_FIELDS = ["router", "routed_gate", "routed_up", "routed_down", "shared_gate", "shared_up",
+                     "shared_down", "shared_gate_weight"]
+MOE_TENSOR_FIELDS = ["router", "routed_down", "routed_gate_up", "shared_down", "shared_gate", "shared_up",
+                     "shared_gate_weight"]
+
+
+class MoeDimensions(C.Structure):   # include/kq_b200.h kq_moe_dimensions
+    _fields_ = [("hidden_size", u32), ("expert_count", u32), ("top_k", u32), ("routed_intermediate_size", u32),
+                ("shared_intermediate_size", u32), ("activation_dtype", C.c_int)]
+
+
 class GdnWeightsF32(C.Structure):
     _fields_ = _pair_fields(GDN_WEIGHT_FIELDS)
 
 
 class QsaWeightsF32(C.Structure):
     _fields_ = _pair_fields(QSA_WEIGHT_FIELDS)
+
+
+class MoeWeightsF32(C.Structure):
+    _fields_ = _pair_fields(MOE_WEIGHT_FIELDS)
+
+
+class MoeExpertWeightsF32(C.Structure):
+    _fields_ = _pair_fields(["gate", "up", "down"])
+
+
+class MoeTensors(C.Structure):
+    _fields_ = [(n, vp) for n in MOE_TENSOR_FIELDS]
 
 
 class GdnTensors(C.Structure):
@@ -119,11 +143,24 @@ class QsaCheckpoint(C.Structure):   # include/kq_qsa.h kq_qsa_checkpoint
                 ("values", C.POINTER(f32)), ("value_count", u64)]
 
 
+class MoeRoute(C.Structure):   # include/kq_moe.h kq_moe_route
+    _fields_ = [("token_index", u64), ("router_logits", C.POINTER(f32)), ("router_probabilities", C.POINTER(f32)),
+                ("expert_count", u64), ("selected_expert_ids", C.POINTER(u32)), ("selected_weights", C.POINTER(f32)),
+                ("selected_count", u32)]
+
+
+class MoeCheckpoint(C.Structure):   # include/kq_moe.h kq_moe_checkpoint
+    _fields_ = [("kind", C.c_int), ("token_index", u64), ("expert_id", u32), ("top_k_position", u32),
+                ("rank", u32), ("dimensions", u64 * 2), ("values", C.POINTER(f32)), ("value_count", u64)]
+
+
 # int (*)(void *words, uint64_t count, void *cuda_stream, void *user)
 EXCHANGE_FN = C.CFUNCTYPE(C.c_int, vp, u64, vp, vp)
 SELECTION_OBSERVER = C.CFUNCTYPE(None, C.POINTER(QsaSelection), vp)
 GDN_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(GdnCheckpoint), vp)
 QSA_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(QsaCheckpoint), vp)
+MOE_ROUTE_OBSERVER = C.CFUNCTYPE(None, C.POINTER(MoeRoute), vp)
+MOE_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(MoeCheckpoint), vp)
 
 
 def checkpoint_collector():
@@ -219,6 +256,34 @@ _SIGNATURES = {
     "kq_b200_qsa_prefill_async": (C.c_int, [vp, vp, vp, u64, vp, vp]),
     "kq_b200_qsa_prefill_sharded_async": (C.c_int, [vp, vp, vp, u64, vp, u32, u32, vp, vp, vp]),
     "kq_b200_qsa_prefill_split_async": (C.c_int, [vp, vp, vp, u64, vp, u32, u32, u32, u32, vp, vp, vp]),
+    "kq_b200_provider_add_expert_stack": (C.c_int, [vp, C.c_char_p, C.c_int, u32, u32, u64, u64, vp, u64,
+                                                    C.POINTER(vp), vp]),
+    "kq_b200_provider_add_expert_gate_up": (C.c_int, [vp, C.c_char_p, u32, u32, u64, u64, vp, u64, vp, u64,
+                                                      C.POINTER(vp), vp]),
+    "kq_moe_test_config_create": (C.c_int, [C.POINTER(MoeDimensions), C.POINTER(vp), vp]),
+    "kq_moe_config_create": (C.c_int, [vp, u32, C.POINTER(vp), vp]),
+    "kq_moe_config_close": (None, [vp]),
+    "kq_b200_moe_config_bind": (C.c_int, [vp, vp, C.POINTER(MoeTensors), vp]),
+    "kq_moe_config_scratch_bytes": (u64, [vp]),
+    "kq_moe_config_one_expert_workspace_bytes": (u64, [vp]),
+    "kq_moe_config_router_workspace_bytes": (u64, [vp]),
+    "kq_moe_config_top_k_workspace_bytes": (u64, [vp]),
+    "kq_moe_config_routed_accumulation_workspace_bytes": (u64, [vp]),
+    "kq_moe_config_shared_workspace_bytes": (u64, [vp]),
+    "kq_moe_config_owned_bytes": (u64, [vp]),
+    "kq_moe_config_layer_id": (u32, [vp]),
+    "kq_moe_config_top_k": (u32, [vp]),
+    "kq_moe_config_expert_count": (u32, [vp]),
+    "kq_moe_config_activation_dtype": (C.c_int, [vp]),
+    "kq_moe_route_f32": (C.c_int, [vp, vp, u64, vp, vp, u64, vp, u64, vp, u64, vp, u64, vp]),
+    "kq_moe_execute_routed_expert_f32": (C.c_int, [vp, C.POINTER(MoeExpertWeightsF32), u32, vp, vp, u64, vp, u64,
+                                                   vp]),
+    "kq_moe_execute_f32": (C.c_int, [vp, C.POINTER(MoeWeightsF32), vp, u64, vp, u64, vp, u64, MOE_ROUTE_OBSERVER,
+                                     MOE_CHECKPOINT_OBSERVER, vp, vp]),
+    "kq_moe_execute_quantized": (C.c_int, [vp, vp, vp, u64, vp, u64, vp, u64, vp, u64, MOE_ROUTE_OBSERVER,
+                                           MOE_CHECKPOINT_OBSERVER, vp, vp]),
+    "kq_b200_moe_execute_async": (C.c_int, [vp, vp, u64, vp, vp]),
+    "kq_moe_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
     "kq_gdn_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
     "kq_qsa_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
 }

@@ -174,3 +174,81 @@ def test_prefill_entry_points_validate_before_any_device_work(kq):
     assert lib.kq_b200_qsa_prefill_split_async(None, None, None, 16, None, 0, 1, 0, 2, exch, None,
                                                C.byref(d)) == abi.INVALID_ARGUMENT
     assert b"token_part" in d.message or b"rank" in d.message or b"valid" in d.message
+
+
+def test_moe_config_matches_reference_accounting(kq, oracle):
+    """MoE config sizes and validation against the compiled reference
+    (kq_moe_workspace_sizes, src/kq_moe.c:83-140): the target geometry, the
+    golden tier configs, and rejected dimensions with the same status."""
+    lib, abi = kq.lib(), kq.abi
+    d = abi.Diagnostic()
+    getters = ["scratch_bytes", "one_expert_workspace_bytes", "router_workspace_bytes", "top_k_workspace_bytes",
+               "routed_accumulation_workspace_bytes", "shared_workspace_bytes"]
+    cases = [(2560, 512, 10, 640, 640, 0), (6, 4, 2, 4, 4, 0), (4, 512, 10, 2, 2, 0), (2560, 512, 10, 640, 640, 1)]
+    have_ref = oracle.ref_available()
+    for dims in cases:
+        cfg = C.c_void_p()
+        assert lib.kq_moe_test_config_create(C.byref(abi.MoeDimensions(*dims)), C.byref(cfg), C.byref(d)) == 0
+        try:
+            assert lib.kq_moe_config_top_k(cfg) == dims[2]
+            assert lib.kq_moe_config_activation_dtype(cfg) == dims[5]
+            assert lib.kq_moe_config_layer_id(cfg) == 0xFFFFFFFF
+            mine = [getattr(lib, "kq_moe_config_" + g)(cfg) for g in getters]
+        finally:
+            lib.kq_moe_config_close(cfg)
+        if have_ref:
+            L = oracle.ref()
+            rc = C.c_void_p()
+            assert L.kq_moe_test_config_create(C.byref(oracle._RefMoeDims(*dims)), C.byref(rc), C.byref(d)) == 0
+            try:
+                for g in getters:
+                    getattr(L, "kq_moe_config_" + g).restype = C.c_uint64
+                ref = [getattr(L, "kq_moe_config_" + g)(rc) for g in getters]
+            finally:
+                L.kq_moe_config_close(rc)
+            assert mine == ref, dims
+    cfg = C.c_void_p()
+    for bad in [(0, 4, 2, 4, 4, 0), (6, 4, 5, 4, 4, 0), (6, 4, 0, 4, 4, 0), (6, 4, 2, 0, 4, 0), (6, 4, 2, 4, 0, 0),
+                (6, 4, 2, 4, 4, 7)]:
+        assert lib.kq_moe_test_config_create(C.byref(abi.MoeDimensions(*bad)), C.byref(cfg),
+                                             C.byref(d)) == abi.INCOMPATIBLE_MOE, bad
+    # B200 limits
+    assert lib.kq_moe_test_config_create(C.byref(abi.MoeDimensions(8, 64, 33, 4, 4, 0)), C.byref(cfg),
+                                         C.byref(d)) == abi.INCOMPATIBLE_MOE
+    assert lib.kq_moe_config_create(None, 0, C.byref(cfg), C.byref(d)) == abi.UNSUPPORTED_MODEL
+
+
+def test_moe_entry_points_validate_before_any_device_work(kq):
+    """kq_moe_execute_* status codes of src/kq_moe_qwen38.c:619-660,882-899
+    for arguments the host rejects."""
+    import numpy as np
+    lib, abi = kq.lib(), kq.abi
+    d = abi.Diagnostic()
+    cfg = C.c_void_p()
+    assert lib.kq_moe_test_config_create(C.byref(abi.MoeDimensions(6, 4, 2, 4, 4, 0)), C.byref(cfg), C.byref(d)) == 0
+    bf = C.c_void_p()
+    assert lib.kq_moe_test_config_create(C.byref(abi.MoeDimensions(6, 4, 2, 4, 4, 1)), C.byref(bf), C.byref(d)) == 0
+    try:
+        x = np.zeros((2, 6), np.float32)
+        y = np.zeros((2, 6), np.float32)
+        sb = lib.kq_moe_config_scratch_bytes(cfg)
+        scratch = np.zeros(sb // 4 + 1, np.float32)
+        w = abi.MoeWeightsF32()
+        none_r, none_c = abi.MOE_ROUTE_OBSERVER(), abi.MOE_CHECKPOINT_OBSERVER()
+        args = lambda c, wt, T, cap, sbytes: (c, wt, x.ctypes.data, T, y.ctypes.data, cap, scratch.ctypes.data, sbytes,
+                                              none_r, none_c, None, C.byref(d))
+        assert lib.kq_moe_execute_f32(*args(cfg, None, 2, 12, sb)) == abi.INVALID_ARGUMENT
+        assert lib.kq_moe_execute_f32(*args(bf, C.byref(w), 2, 12, sb)) == abi.INCOMPATIBLE_MOE
+        assert lib.kq_moe_execute_f32(*args(cfg, C.byref(w), 0, 12, sb)) == abi.LIMIT_EXCEEDED
+        assert lib.kq_moe_execute_f32(*args(cfg, C.byref(w), 2, 11, sb)) == abi.BUFFER_TOO_SMALL
+        assert lib.kq_moe_execute_f32(*args(cfg, C.byref(w), 2, 12, sb - 1)) == abi.BUFFER_TOO_SMALL
+        assert lib.kq_moe_execute_f32(*args(cfg, C.byref(w), 2, 12, sb)) == abi.DIMENSION_MISMATCH
+        x[1, 3] = np.inf
+        assert lib.kq_moe_execute_f32(*args(cfg, C.byref(w), 2, 12, sb)) == abi.NUMERIC_DOMAIN
+        ws = np.zeros(100, np.float32)
+        assert lib.kq_moe_execute_quantized(cfg, None, x.ctypes.data, 2, y.ctypes.data, 12, scratch.ctypes.data, sb,
+                                            ws.ctypes.data, ws.nbytes, none_r, none_c, None,
+                                            C.byref(d)) == abi.BUFFER_TOO_SMALL
+    finally:
+        lib.kq_moe_config_close(cfg)
+        lib.kq_moe_config_close(bf)
