@@ -272,18 +272,23 @@ class MoeLayerWeights:
 def moe_layer(seed: int, dims: MoeDims, gate_up_type: int = TYPE_Q4_K, down_type: int = TYPE_Q8_0,
               shared_type: int = TYPE_Q8_0) -> MoeLayerWeights:
     """One MoE layer in the target's GGUF types (gate/up Q4_K, down Q8_0,
-    shared Q8_0, router and shared gate F32 ~ N(0, 0.02))."""
+    shared Q8_0, router and shared gate F32 ~ N(0, 0.02)).  Q8_0 scales are
+    drawn so that decoded values stay within +-0.05 (std ~0.015), the scale of
+    trained FFN weights; with N(0,1) inputs the SwiGLU activations stay O(10)."""
     rng = np.random.default_rng(seed)
     E, H, I, S = dims.experts, dims.hidden, dims.routed, dims.shared
+
+    def small(t, rows, cols):
+        return pack_q8_0(rng, rows, cols, d_range=(1e-4, 4e-4)) if t == TYPE_Q8_0 else pack(t, rng, rows, cols)
     return MoeLayerWeights(
         dims=dims,
         router=pack_f32(rng, E, H),
         gate=pack(gate_up_type, rng, E * I, H),
         up=pack(gate_up_type, rng, E * I, H),
-        down=pack(down_type, rng, E * H, I),
-        shared_gate=pack(shared_type, rng, S, H),
-        shared_up=pack(shared_type, rng, S, H),
-        shared_down=pack(shared_type, rng, H, S),
+        down=small(down_type, E * H, I),
+        shared_gate=small(shared_type, S, H),
+        shared_up=small(shared_type, S, H),
+        shared_down=small(shared_type, H, S),
         shared_gate_weight=rng.normal(0.0, 0.02, H).astype(np.float32),
     )
 

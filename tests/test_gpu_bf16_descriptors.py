@@ -106,7 +106,8 @@ def test_qsa_cache_descriptor_matches_reference(kq, oracle, dtype):
             scratch = np.zeros(need.value // 4 + 1, np.float32)
             y = np.zeros((x.shape[0], dims.hidden), np.float32)
             st = lib.kq_qsa_prefill_f32(layer.handle, C.byref(qw), x.ctypes.data, x.shape[0], y.ctypes.data, y.size,
-                                        s.handle, scratch.ctypes.data, need.value, None, None, None, C.byref(d))
+                                        s.handle, scratch.ctypes.data, need.value, abi.SELECTION_OBSERVER(), None,
+                                        None, C.byref(d))
             assert st == exec_ref, d.text()
             if dtype == 1:
                 assert st != 0 and s.length == length
