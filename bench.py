@@ -21,6 +21,8 @@ prefill ones):
   prefill_8k.block      the 4-layer block of config 4 on 8192 tokens
   prefill_131k          config 4: the 4-layer block (all projections Q4_K,
                         index BF16) on 131072 tokens
+  moe_decode            the routed-expert MoE layer (512 experts, top-10,
+                        shared expert) on a batch of 64 decode tokens
 Every prefill runs tensor-parallel over the run's ranks (GDN by value-head
 group, QSA by query-head group or by token within a KV-head group, the
 indexer's selections exchanged once per layer call) with one NCCL
@@ -371,6 +373,192 @@ def cpu_prefill_record(kind: str, tokens: int = CPU_PREFILL_TOKENS):
                       f"({secs:.1f} s wall)"}
 
 
+# ---------------------------------------------------------------- MoE
+
+MOE_BATCH = 64
+MOE_POOL = 16   # distinct input batches cycled through the timed steps
+MOE_CPU_TOKENS = 8
+
+
+def moe_weights():
+    """The target MoE layer (512 experts, top-10, hidden 2560, routed and
+    shared intermediate 640): gate/up Q4_K, down and shared Q8_0, router and
+    shared gate F32 (src/kq_moe.c:27-54 type masks)."""
+    from kqb200 import synth
+    return synth.moe_layer(11, synth.MoeDims())
+
+
+def moe_routes(w, x: np.ndarray) -> np.ndarray:
+    """Selected experts [T][K] of tokens x from the F32 router (host float64
+    product: byte accounting only, near ties do not matter there)."""
+    d = w.dims
+    R = w.router.data.view(np.float32).reshape(d.experts, d.hidden).astype(np.float64)
+    logits = x.astype(np.float64) @ R.T
+    return np.argpartition(-logits, d.top_k - 1, axis=1)[:, :d.top_k]
+
+
+def moe_step_bytes(w, x: np.ndarray):
+    """Algorithmic HBM bytes of one MoE call over the tokens x: each selected
+    expert's gate/up/down rows once, the shared expert, the router, the
+    activations in and out.  Returns (total, experts part, distinct experts)."""
+    d = w.dims
+    per_expert = (w.gate.nbytes + w.up.nbytes + w.down.nbytes) // d.experts
+    distinct = len(np.unique(moe_routes(w, x)))
+    shared = w.shared_gate.nbytes + w.shared_up.nbytes + w.shared_down.nbytes + d.hidden * 4
+    io = 2 * x.shape[0] * d.hidden * 4
+    return distinct * per_expert + shared + w.router.nbytes + io, distinct * per_expert, distinct
+
+
+def cpu_moe_sample(w, tokens: int, threads: int):
+    """The reference's own MoE operators on the host cores: per token
+    kq_moe_route_f32, then kq_moe_execute_routed_expert_f32 for each selected
+    expert and for the shared expert (F32 weights; the selected experts are
+    dequantised outside the timed spans).  Returns (tokens/s, kind, threads)."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None, "unavailable", 0
+    d = w.dims
+    H, I, S = d.hidden, d.routed, d.shared
+    router = np.ascontiguousarray(w.router.data.view(np.float32).reshape(d.experts, H))
+    xs = np.random.default_rng(77).normal(size=(tokens, H)).astype(np.float32)
+
+    def rows(t, e, n):
+        rb = t.row_bytes
+        return O.dequantize(t.type_id, t.data[e * n * rb:(e + 1) * n * rb]).reshape(n, -1)
+
+    shared = (O.dequantize(w.shared_gate.type_id, w.shared_gate.data).reshape(S, H),
+              O.dequantize(w.shared_up.type_id, w.shared_up.data).reshape(S, H),
+              O.dequantize(w.shared_down.type_id, w.shared_down.data).reshape(H, S))
+
+    def one(i):
+        ref = O.RefMoe(d)
+        try:
+            x = xs[i]
+            spent = 0.0
+            t0 = time.perf_counter()
+            ids, wt = ref.route(router, x)
+            spent += time.perf_counter() - t0
+            y = np.zeros(H, np.float32)
+            for p in sorted(range(d.top_k), key=lambda q: ids[q]):
+                e = int(ids[p])
+                g, u, dn = rows(w.gate, e, I), rows(w.up, e, I), rows(w.down, e, H)
+                t0 = time.perf_counter()
+                out = ref.expert(g, u, dn, x)
+                spent += time.perf_counter() - t0
+                y = y + out * wt[p]
+            t0 = time.perf_counter()
+            ref.expert(*shared, x)
+            spent += time.perf_counter() - t0
+            return spent
+        finally:
+            ref.close()
+
+    spans = [0.0] * threads
+    with cf.ThreadPoolExecutor(max_workers=threads) as pool:
+        for i, t in enumerate(pool.map(one, range(tokens))):
+            spans[i % threads] += t
+    return tokens / max(spans), "reference", threads
+
+
+def cpu_moe_record(w=None, tokens: int = MOE_CPU_TOKENS):
+    w = w if w is not None else moe_weights()
+    threads = min(cpu_threads(), tokens)
+    v, kind, threads = cpu_moe_sample(w, tokens, threads)
+    if v is None:
+        return {"unavailable": "reference library not built"}
+    return {"value": v, "unit": "tok/s", "cores": threads, "kind": kind,
+            "sample": f"{tokens} tokens, one per thread: kq_moe_route_f32 + kq_moe_execute_routed_expert_f32 for "
+                      f"the 10 selected experts and the shared expert (F32 weights, dequantised outside the timing)"}
+
+
+def moe_record(args, cx: Ctx, cpu: bool):
+    """The routed-expert MoE layer decoding a batch of 64 tokens (one per
+    sequence), target geometry.  A step = one kq_b200_moe_execute_async call
+    over 64 tokens; the inputs cycle through 16 seeded batches so the set of
+    selected experts changes every step.  Bound: HBM (each selected expert's
+    weights once per step)."""
+    torch, kqb200 = cx.torch, cx.kq
+    w = moe_weights()
+    d = w.dims
+    B, H = MOE_BATCH, d.hidden
+    prov = kqb200.Provider(cx.local_rank)
+    layer = kqb200.MoeLayer(d, w, prov, layer=0)
+    try:
+        rng = np.random.default_rng(500 + cx.rank)
+        xs = [rng.normal(size=(B, H)).astype(np.float32) for _ in range(MOE_POOL)]
+        xd = [torch.from_numpy(x).cuda() for x in xs]
+        y = torch.empty(B, H, device="cuda")
+        torch.cuda.synchronize()
+        it = [0]
+
+        def step():
+            kqb200.moe_execute_async(layer, xd[it[0] % MOE_POOL].data_ptr(), B, y.data_ptr())
+            it[0] += 1
+
+        with torch.cuda.stream(cx.stream):
+            for _ in range(args.warmup):
+                step()
+        cx.sync()
+        steps = args.moe_steps
+        it[0] = 0
+        launches0 = cx.lib.kq_b200_kernel_launch_count()
+        with ClockSampler(cx.local_rank) as clocks:
+            ms = cx.timed(steps, step)
+        launches = cx.lib.kq_b200_kernel_launch_count() - launches0
+        assert torch.isfinite(y).all(), "non-finite MoE output"
+        it[0] = 0
+        gu_ms, gu_n = cx.family_ms("moe_gate_up", steps, step)
+        it[0] = 0
+        dn_ms, dn_n = cx.family_ms("moe_down", steps, step)
+        # end to end: the reference-shaped synchronous entry point with host
+        # activations (kq_moe_execute_quantized, 64 tokens per call)
+        it[0] = 0
+
+        def e2e_step():
+            st, out, *_ = layer.execute_quantized(xs[it[0] % MOE_POOL])
+            it[0] += 1
+            assert st == 0
+
+        e2e_step()
+        it[0] = 0
+        e2e_ms = cx.timed(max(3, steps // 4), e2e_step)
+        ms, e2e_ms, gu_ms, dn_ms = max_over_ranks([ms, e2e_ms, gu_ms, dn_ms], cx.world, cx.device)
+        acc = [moe_step_bytes(w, xs[i % MOE_POOL]) for i in range(MOE_POOL)]
+        step_bytes = float(np.mean([a[0] for a in acc]))
+        distinct = float(np.mean([a[2] for a in acc]))
+        per_expert_gu = (w.gate.nbytes + w.up.nbytes) // d.experts
+        gu_bytes = distinct * per_expert_gu
+        hbm, peak_kind = peaks()
+        gu_avg = gu_ms / max(1.0, gu_n)
+        achieved = gu_bytes / (gu_avg * 1e-3) / 1e9
+        rec = {
+            "workload": "MoE layer decode, 64 tokens/GPU (one per sequence), 512 experts top-10 + shared expert, "
+                        "hidden 2560, intermediate 640, gate/up Q4_K, down/shared Q8_0, router F32",
+            "value": job_tokens_per_s(cx.world, B, ms), "unit": "tok/s", "ms_per_step": ms, "steps": steps,
+            "step_algorithmic_bytes": step_bytes, "distinct_experts_per_step": distinct,
+            "step_hbm_frac": step_bytes / (ms * 1e-3) / 1e9 / hbm,
+            "roofline": {
+                "kernel": "moe_gate_up (grouped Q4_K gate+up GEMV of the selected experts, SwiGLU epilogue)",
+                "bound": "hbm", "achieved": achieved, "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": achieved / hbm, "traffic": None,
+                "algorithmic_bytes_per_launch": gu_bytes, "avg_launch_ms": gu_avg,
+                "down_ms_per_step": dn_ms, "down_frac": distinct * (w.down.nbytes // d.experts) /
+                (dn_ms / max(1.0, dn_n) * 1e-3) / 1e9 / hbm,
+                "timing": "CUDA events around each launch of the kernel, in a pass of its own"},
+            "e2e": {"value": job_tokens_per_s(cx.world, B, e2e_ms), "unit": "tok/s", "ms_per_step": e2e_ms,
+                    "api": "kq_moe_execute_quantized, 64 tokens per call, host activations",
+                    "h2d_bytes_per_step": B * H * 4, "d2h_bytes_per_step": B * H * 4},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        if cpu and cx.rank == 0:
+            rec["cpu_baseline"] = cpu_moe_record(w)
+        return rec
+    finally:
+        layer.close()
+        prov.close()
+
+
 def run_reference(args, rank, world):
     """The reference arm: rank 0 alone times the reference's CPU operators on
     every host core it may use; other ranks exit at once."""
@@ -408,6 +596,8 @@ def run_reference(args, rank, world):
         line["prefill_8k"] = {k: {"impl": "reference", "cpu_baseline": cpu_prefill_record(k)}
                               for k in ("gdn_layer", "block")}
         line["prefill_131k"] = {"impl": "reference", "cpu_baseline": cpu_prefill_record("block")}
+    if not args.no_moe:
+        line["moe_decode"] = {"impl": "reference", "cpu_baseline": cpu_moe_record()}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -958,6 +1148,8 @@ def run_b200(args, rank, world, local_rank):
                                               f"per thread ({secs:.1f} s wall)"}
         if world == 1 and args.b1_steps > 0:
             line["decode_b1"] = decode_b1_record(args, cx, cpu)
+        if not args.no_moe:
+            line["moe_decode"] = moe_record(args, cx, cpu)
         if not args.no_prefill:
             ps, pw = args.prefill_steps, args.prefill_warmup
             line["prefill_8k"] = {k: prefill_record(args, cx, k, 8192, ps, pw, cpu) for k in ("gdn_layer", "block")}
@@ -976,6 +1168,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="headline decode record only")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE decode sub-record")
+    ap.add_argument("--moe-steps", type=int, default=50, help="timed steps of the MoE decode sub-record")
     ap.add_argument("--breakdown", action="store_true", help="time every kernel family (extra passes)")
     ap.add_argument("--ctx-max", type=int, default=CTX_RANGE[1],
                     help="upper end of the context distribution (profiling runs use a small one)")

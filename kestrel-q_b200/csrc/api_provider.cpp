@@ -198,16 +198,22 @@ static kq_status upload_matrix(kq_weight_provider *provider, const char *semanti
     kq_status st = kq_b200_set_device(provider->device, diagnostic);
     if (st != KQ_STATUS_OK) return st;
     // Q6_K and Q8_0 rows are stored as aligned planes (same bytes, see
-    // kernels.hpp QMatrix) so the kernels can use 16-byte loads
+    // kernels.hpp QMatrix) so the kernels can use 16-byte loads; a row whose
+    // byte count is not a multiple of 16 (Q8_0 rows of 640 values: 680 B)
+    // is padded to the next multiple, so every row starts 16-byte aligned
     const uint8_t *src = static_cast<const uint8_t *>(packed);
     std::vector<uint8_t> planar;
     uint32_t layout = 0;
+    uint64_t pitch = row_bytes, stored = total;
     if (type_id == KQ_GGUF_TYPE_Q6_K || type_id == KQ_GGUF_TYPE_Q8_0) {
-        planar.resize(total);
+        pitch = (row_bytes + 15) & ~uint64_t(15);
+        if (!mul_ok(rows, pitch, &stored))
+            return fail(diagnostic, KQ_STATUS_ARITHMETIC_OVERFLOW, "matrix size overflows");
+        planar.assign(stored, 0);
         const uint64_t nblk = columns / be;
         for (uint64_t r = 0; r < rows; ++r) {
             const uint8_t *in = src + r * row_bytes;
-            uint8_t *out = planar.data() + r * row_bytes;
+            uint8_t *out = planar.data() + r * pitch;
             for (uint64_t b = 0; b < nblk; ++b) {
                 const uint8_t *blk = in + b * bb;
                 if (type_id == KQ_GGUF_TYPE_Q6_K) {
@@ -228,17 +234,17 @@ static kq_status upload_matrix(kq_weight_provider *provider, const char *semanti
         weight_scale_exponent(weight_abs_bound(type_id, static_cast<const uint8_t *>(packed), rows, row_bytes));
     // Q4_K: the factored tensor-core kernel's per-super-block side data
     // (kernels.hpp q4k_build_aux) follows the blocks in the same allocation
-    const uint64_t aux_offset = (total + 255) & ~uint64_t(255);
+    const uint64_t aux_offset = (stored + 255) & ~uint64_t(255);
     std::vector<uint8_t> aux;
     if (type_id == KQ_GGUF_TYPE_Q4_K && side_data) {
         aux.resize(q4k_aux_bytes((uint32_t)rows, (uint32_t)columns));
         q4k_build_aux(static_cast<const uint8_t *>(packed), (uint32_t)rows, (uint32_t)columns, scale_exp,
                       aux.data());
     }
-    const uint64_t alloc = aux.empty() ? total : aux_offset + aux.size();
+    const uint64_t alloc = aux.empty() ? stored : aux_offset + aux.size();
     void *dev = nullptr;
     KQB_CUDA(cudaMalloc(&dev, alloc), diagnostic, "weight allocation");
-    cudaError_t e = cudaMemcpy(dev, src, total, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpy(dev, src, stored, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && !aux.empty())
         e = cudaMemcpy(static_cast<uint8_t *>(dev) + aux_offset, aux.data(), aux.size(), cudaMemcpyHostToDevice);
     // a pageable upload may return before its DMA lands; the library's
@@ -255,7 +261,7 @@ static kq_status upload_matrix(kq_weight_provider *provider, const char *semanti
     t->m.type = type_id;
     t->m.rows = (uint32_t)rows;
     t->m.cols = (uint32_t)columns;
-    t->m.row_bytes = (uint32_t)row_bytes;
+    t->m.row_bytes = (uint32_t)pitch;
     t->m.layout = layout;
     t->m.scale_exp = scale_exp;
     t->m.aux = aux.empty() ? nullptr : static_cast<const uint8_t *>(dev) + aux_offset;

@@ -80,6 +80,7 @@ enum DeviceError : uint32_t {
 // 32-element run loads with 16-byte vector loads:
 //   Q6_K: [ql nsb*128][qh nsb*64][scales nsb*16][d nsb*2]
 //   Q8_0: [codes nb*32][d nb*2]
+// and the row pitch `row_bytes` is rounded up to a multiple of 16 bytes.
 // (Q4_K's 144-byte super-blocks are already 16-byte aligned and stay GGUF.)
 // `scale_exp`: the tensor-core projection multiplies the decoded weights by
 // 2^scale_exp (exact) before splitting them into fp16 hi/lo parts, so that

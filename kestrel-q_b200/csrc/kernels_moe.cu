@@ -408,6 +408,264 @@ moe_down_kernel(MoeDims d, QMatrix down, const float *__restrict__ act, const ui
     }
 }
 
+// ------------------------------------------------- staged (bulk-copy) paths
+//
+// Q4_K gate/up and planar Q8_0 down: a CTA copies its whole row block into
+// shared memory with one bulk copy per row (HBM -> SMEM, mbarrier
+// completion), then, per group of the expert's tokens, copies their
+// activation rows into shared memory and decodes the block against them, so
+// the block crosses HBM once whatever the token count.  Two (gate/up) or
+// three (down) CTAs per SM keep the next blocks' copies in flight while one
+// decodes.  Lane = sub * 8 + unit: the eight lanes of a shared-memory phase
+// read the same activation words (a broadcast) and eight different rows,
+// whose pitch is chosen so that they fall in distinct banks.  Codes become
+// floats without a conversion instruction: a code byte placed in the
+// mantissa of 2^23 (PRMT) minus 2^23 (one FADD) is the exact integer.
+
+constexpr uint32_t kGuRows = 32;     // gate rows (and as many up rows) per CTA
+constexpr uint32_t kGuGroup = 2;     // tokens per pass (activation rows staged)
+constexpr uint32_t kDnRows = 64;     // down rows per CTA
+constexpr uint32_t kDnGroup = 8;
+constexpr uint32_t kMaxStageBytes = 112u * 1024u;
+constexpr uint32_t kStageWaitPolls = 1u << 26;
+
+__device__ __forceinline__ uint32_t moe_smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void moe_bulk(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(moe_smem_u32(dst)), "l"(src), "r"(bytes), "r"(moe_smem_u32(bar))
+                 : "memory");
+}
+
+// Bounded wait for phase 0 of `bar`; false when it gave up.
+__device__ __forceinline__ bool moe_bar_wait(uint64_t *bar) {
+    const uint32_t a = moe_smem_u32(bar);
+    for (uint32_t i = 0; i < kStageWaitPolls; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+            "selp.b32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(a)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+// Byte k of `v` as the float value of that byte (0..255).
+__device__ __forceinline__ float byte_float(uint32_t v, int k) {
+    return __int_as_float(__byte_perm(v, 0x4B000000u, (uint32_t)k | 0x7540u)) - 8388608.0f;
+}
+
+// Copies `rows` rows of `row_bytes` from `src` (pitch row_bytes) to `dst`
+// (pitch `dst_pitch`), and as many from `src2` to `dst2` when given, then
+// waits for them; every thread returns the same verdict.
+__device__ __forceinline__ bool stage_rows(uint8_t *dst, const uint8_t *src, uint32_t rows, uint32_t row_bytes,
+                                           uint32_t dst_pitch, const uint8_t *src2, uint8_t *dst2, uint64_t *bar,
+                                           int *ok, const ErrorWord &err) {
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(moe_smem_u32(bar)));
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        const uint32_t total = rows * row_bytes * (src2 ? 2u : 1u);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(moe_smem_u32(bar)), "r"(total)
+                     : "memory");
+        for (uint32_t r = 0; r < rows; ++r) {
+            moe_bulk(dst + (size_t)r * dst_pitch, src + (size_t)r * row_bytes, row_bytes, bar);
+            if (src2) moe_bulk(dst2 + (size_t)r * dst_pitch, src2 + (size_t)r * row_bytes, row_bytes, bar);
+        }
+        *ok = 1;
+        if (!moe_bar_wait(bar)) {
+            moe_raise(err, kErrTimeout | (1u << 8));
+            *ok = 0;
+            moe_bar_wait(bar);   // let the copies in flight land before the CTA exits
+        }
+    }
+    __syncthreads();
+    return *ok != 0;
+}
+
+// `nb` activation rows (row ids rows_of(j), `cols` floats each) into
+// shared memory xs[j][cols], all threads, 16-byte moves.
+template <typename RowOf>
+__device__ __forceinline__ void stage_acts(float *xs, const float *src, uint32_t ld, uint32_t cols, uint32_t nb,
+                                           RowOf rows_of) {
+    const uint32_t q = cols / 4u;
+    for (uint32_t i = threadIdx.x; i < nb * q; i += blockDim.x) {
+        const uint32_t j = i / q, c = i % q;
+        reinterpret_cast<float4 *>(xs + (size_t)j * cols)[c] =
+            reinterpret_cast<const float4 *>(src + (size_t)rows_of(j) * ld)[c];
+    }
+}
+
+// 32 decoded Q4_K values of run c (multiple of 32) of a row in shared memory
+// (144-byte super-blocks: fp16 d, fp16 dmin, 12 scale/min bytes, 128 code
+// bytes), value = d*sc*q - dmin*m with one rounding per value.
+__device__ __forceinline__ void q4k_run_smem(const uint8_t *row, uint32_t c, float (&w)[32]) {
+    const uint8_t *sb = row + (c >> 8) * 144u;
+    const uint32_t group = (c & 255u) >> 6, high = (c >> 5) & 1u;
+    const uint4 hdr = *reinterpret_cast<const uint4 *>(sb);
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(sb + 16u + group * 32u);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(sb + 32u + group * 32u);
+    uint8_t h[16];
+    bytes16(hdr, h);
+    const float d = half_bits_to_float((uint32_t)h[0] | ((uint32_t)h[1] << 8));
+    const float dmin = half_bits_to_float((uint32_t)h[2] | ((uint32_t)h[3] << 8));
+    uint32_t sc, mn;
+    q4k_scale_min(h + 4, (int)(2u * group + high), sc, mn);
+    const float dl = __fmul_rn(d, (float)sc), ml = __fmul_rn(dmin, (float)mn);
+    const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const uint32_t nib = (words[k] >> (4u * high)) & 0x0F0F0F0Fu;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) w[4 * k + b] = fmaf(dl, byte_float(nib, b), -ml);
+    }
+}
+
+// s += w . xs[0..32)
+__device__ __forceinline__ float dot32_smem(const float (&w)[32], const float *xs, float s) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = reinterpret_cast<const float4 *>(xs)[i];
+        s = fmaf(w[4 * i], v.x, s);
+        s = fmaf(w[4 * i + 1], v.y, s);
+        s = fmaf(w[4 * i + 2], v.z, s);
+        s = fmaf(w[4 * i + 3], v.w, s);
+    }
+    return s;
+}
+
+// grid (max active experts, ceil(I / 32)), 256 threads.  Warp w owns local
+// rows 4w..4w+3; lane = sub * 8 + unit with unit = row * 2 + {0 gate, 1 up}
+// and the four subs splitting a row's 32-value runs.  Shared memory: gate
+// rows, up rows (pitch rb + 16 keeps the eight units' rows in distinct
+// banks), then kGuGroup activation rows.
+__global__ void __launch_bounds__(kMoeThreads, 2)
+moe_gate_up_staged_kernel(MoeDims d, QMatrix gate, QMatrix up, const float *__restrict__ x, uint32_t ldx,
+                          const uint32_t *__restrict__ active, const uint32_t *__restrict__ offsets,
+                          const uint32_t *__restrict__ pick_of_slot, float *__restrict__ act, float *gate_dbg,
+                          float *up_dbg, ErrorWord err) {
+    extern __shared__ __align__(128) uint8_t gsm[];
+    __shared__ uint64_t bar;
+    __shared__ int ok;
+    pdl_wait();
+    if (moe_err_raised(err) || blockIdx.x >= active[0]) return;
+    const uint32_t e = active[1 + blockIdx.x];
+    const uint32_t s0 = offsets[e], n = offsets[e + 1] - s0;
+    const uint32_t I = d.routed, H = d.hidden, rb = gate.row_bytes, pitch = rb + 16u;
+    const uint32_t r0 = blockIdx.y * kGuRows, rows = min(kGuRows, I - r0);
+    uint8_t *gs = gsm, *us = gsm + (size_t)kGuRows * pitch;
+    float *xs = reinterpret_cast<float *>(gsm + (size_t)2 * kGuRows * pitch);
+    if (!stage_rows(gs, gate.data + ((size_t)e * I + r0) * rb, rows, rb, pitch, up.data + ((size_t)e * I + r0) * rb,
+                    us, &bar, &ok, err))
+        return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t unit = (uint32_t)lane & 7u, sub = (uint32_t)lane >> 3;
+    const uint32_t lr = (uint32_t)warp * 4u + (unit >> 1);
+    const bool is_up = (unit & 1u) != 0u, live = lr < rows;
+    const uint8_t *row = (is_up ? us : gs) + (size_t)(live ? lr : 0u) * pitch;
+    for (uint32_t g0 = 0; g0 < n; g0 += kGuGroup) {
+        const uint32_t nb = min(kGuGroup, n - g0);
+        __syncthreads();   // the previous group's activation rows are no longer read
+        stage_acts(xs, x, ldx, H, nb, [&](uint32_t j) { return pick_of_slot[s0 + g0 + j] / d.top_k; });
+        __syncthreads();
+        float a0 = 0.0f, a1 = 0.0f;
+        if (live) {
+            for (uint32_t c = sub * 32u; c < H; c += 128u) {
+                float w[32];
+                q4k_run_smem(row, c, w);
+                a0 = dot32_smem(w, xs + c, a0);
+                if (nb > 1) a1 = dot32_smem(w, xs + H + c, a1);
+            }
+        }
+        a0 += __shfl_xor_sync(0xffffffffu, a0, 8);
+        a0 += __shfl_xor_sync(0xffffffffu, a0, 16);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, 8);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, 16);
+        const float u0 = __shfl_down_sync(0xffffffffu, a0, 1), u1 = __shfl_down_sync(0xffffffffu, a1, 1);
+        if (sub == 0 && !is_up && live) {
+            const size_t o = (size_t)(s0 + g0) * I + r0 + lr;
+            act[o] = moe_swiglu(a0, u0);
+            if (gate_dbg) {
+                gate_dbg[o] = a0;
+                up_dbg[o] = u0;
+            }
+            if (nb > 1) {
+                act[o + I] = moe_swiglu(a1, u1);
+                if (gate_dbg) {
+                    gate_dbg[o + I] = a1;
+                    up_dbg[o + I] = u1;
+                }
+            }
+        }
+    }
+}
+
+// grid (max active experts, ceil(H / 64)), 256 threads.  Warp w owns local
+// rows 8w..8w+7; lane = sub * 8 + row.  Planar Q8_0 rows: I code bytes,
+// then the I/32 fp16 scales; shared memory: the rows (pitch rb), then
+// kDnGroup activation rows.
+__global__ void __launch_bounds__(kMoeThreads, 3)
+moe_down_staged_kernel(MoeDims d, QMatrix down, const float *__restrict__ act, const uint32_t *__restrict__ active,
+                       const uint32_t *__restrict__ offsets, float *__restrict__ eout, ErrorWord err) {
+    extern __shared__ __align__(128) uint8_t dsm[];
+    __shared__ uint64_t bar;
+    __shared__ int ok;
+    pdl_wait();
+    if (moe_err_raised(err) || blockIdx.x >= active[0]) return;
+    const uint32_t e = active[1 + blockIdx.x];
+    const uint32_t s0 = offsets[e], n = offsets[e + 1] - s0;
+    const uint32_t H = d.hidden, I = d.routed, rb = down.row_bytes;
+    const uint32_t r0 = blockIdx.y * kDnRows, rows = min(kDnRows, H - r0);
+    float *as = reinterpret_cast<float *>(dsm + (size_t)kDnRows * rb);
+    if (!stage_rows(dsm, down.data + ((size_t)e * H + r0) * rb, rows, rb, rb, nullptr, nullptr, &bar, &ok, err))
+        return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t lr = (uint32_t)warp * 8u + ((uint32_t)lane & 7u), sub = (uint32_t)lane >> 3;
+    const bool live = lr < rows;
+    const uint8_t *row = dsm + (size_t)(live ? lr : 0u) * rb;
+    const uint16_t *scales = reinterpret_cast<const uint16_t *>(row + I);
+    for (uint32_t g0 = 0; g0 < n; g0 += kDnGroup) {
+        const uint32_t nb = min(kDnGroup, n - g0);
+        __syncthreads();
+        stage_acts(as, act + (size_t)(s0 + g0) * I, I, I, nb, [](uint32_t j) { return j; });
+        __syncthreads();
+        float acc[kDnGroup];
+#pragma unroll
+        for (int j = 0; j < (int)kDnGroup; ++j) acc[j] = 0.0f;
+        if (live) {
+            for (uint32_t c = sub * 32u; c < I; c += 128u) {
+                const uint4 q0 = *reinterpret_cast<const uint4 *>(row + c);
+                const uint4 q1 = *reinterpret_cast<const uint4 *>(row + c + 16u);
+                const float dsc = half_bits_to_float(scales[c >> 5]);
+                const uint32_t words[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u,
+                                           q0.w ^ 0x80808080u, q1.x ^ 0x80808080u, q1.y ^ 0x80808080u,
+                                           q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
+                float w[32];
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) w[4 * k + b] = byte_float(words[k], b) - 128.0f;   // the int8 code
+#pragma unroll
+                for (int j = 0; j < (int)kDnGroup; ++j) {
+                    if ((uint32_t)j >= nb) break;
+                    acc[j] = fmaf(dsc, dot32_smem(w, as + (size_t)j * I + c, 0.0f), acc[j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < (int)kDnGroup; ++j) {
+            if ((uint32_t)j >= nb) break;
+            float v = acc[j];
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            if (sub == 0 && live) eout[(size_t)(s0 + g0 + j) * H + r0 + lr] = v;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- shared
 
 // act[t][i] = swiglu(gu[t][i], gu[t][S + i])
@@ -582,21 +840,64 @@ void launch_moe_dispatch(const MoeDims &d, uint32_t T, MoeBuffers &b, ErrorWord 
     count_launch();
 }
 
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u; }
+
+// The staged kernels' conditions: the types they decode, 16-byte aligned
+// rows and float4-aligned activations, a row block within kMaxStageBytes.
+static size_t gate_up_stage_bytes(const MoeDims &d, const QMatrix &g) {
+    return (size_t)2 * kGuRows * (g.row_bytes + 16u) + (size_t)kGuGroup * d.hidden * 4u;
+}
+
+static size_t down_stage_bytes(const MoeDims &d, const QMatrix &m) {
+    return (size_t)kDnRows * m.row_bytes + (size_t)kDnGroup * d.routed * 4u;
+}
+
+static bool gate_up_staged_ok(const MoeDims &d, const QMatrix &g, const QMatrix &u, const float *x, uint32_t ldx) {
+    return g.type == kTypeQ4_K && u.type == kTypeQ4_K && g.row_bytes == u.row_bytes && g.row_bytes % 16u == 0u &&
+           aligned16(g.data) && aligned16(u.data) && d.hidden % 256u == 0u && aligned16(x) && ldx % 4u == 0u &&
+           gate_up_stage_bytes(d, g) <= kMaxStageBytes;
+}
+
+static bool down_staged_ok(const MoeDims &d, const QMatrix &m, const float *act) {
+    return m.type == kTypeQ8_0 && m.layout == 1 && m.row_bytes % 16u == 0u && aligned16(m.data) &&
+           d.routed % 32u == 0u && aligned16(act) && down_stage_bytes(d, m) <= kMaxStageBytes;
+}
+
 void launch_moe_experts(const MoeDims &d, const MoeWeightsDev &w, const float *x, uint32_t ldx, uint32_t T,
                         MoeBuffers &b, ErrorWord err, cudaStream_t stream) {
     const uint32_t max_active = (uint32_t)std::min<uint64_t>(d.experts, (uint64_t)T * d.top_k);
+    static DeviceOnce attr;
+    attr.run([] {
+        cudaFuncSetAttribute(moe_gate_up_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kMaxStageBytes);
+        cudaFuncSetAttribute(moe_down_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kMaxStageBytes);
+    });
     {
         KernelTimer timer("moe_gate_up", stream);
-        dim3 grid(max_active, (d.routed + kMoeRowsPerCta - 1) / kMoeRowsPerCta);
-        launch_pdl(moe_gate_up_kernel, grid, kMoeThreads, 0, stream, d, w.gate, w.up, x, ldx, b.active, b.offsets,
-                   b.pick_of_slot, b.act, b.dbg.gate, b.dbg.up, err);
+        if (gate_up_staged_ok(d, w.gate, w.up, x, ldx)) {
+            dim3 grid(max_active, (d.routed + kGuRows - 1) / kGuRows);
+            launch_pdl(moe_gate_up_staged_kernel, grid, kMoeThreads, gate_up_stage_bytes(d, w.gate), stream,
+                       d, w.gate, w.up, x, ldx, b.active, b.offsets, b.pick_of_slot, b.act, b.dbg.gate, b.dbg.up,
+                       err);
+        } else {
+            dim3 grid(max_active, (d.routed + kMoeRowsPerCta - 1) / kMoeRowsPerCta);
+            launch_pdl(moe_gate_up_kernel, grid, kMoeThreads, 0, stream, d, w.gate, w.up, x, ldx, b.active,
+                       b.offsets, b.pick_of_slot, b.act, b.dbg.gate, b.dbg.up, err);
+        }
         count_launch();
     }
     {
         KernelTimer timer("moe_down", stream);
-        dim3 grid(max_active, (d.hidden + kMoeRowsPerCta - 1) / kMoeRowsPerCta);
-        launch_pdl(moe_down_kernel, grid, kMoeThreads, 0, stream, d, w.down, b.act, b.active, b.offsets, b.eout,
-                   err);
+        if (down_staged_ok(d, w.down, b.act)) {
+            dim3 grid(max_active, (d.hidden + kDnRows - 1) / kDnRows);
+            launch_pdl(moe_down_staged_kernel, grid, kMoeThreads, down_stage_bytes(d, w.down), stream, d,
+                       w.down, b.act, b.active, b.offsets, b.eout, err);
+        } else {
+            dim3 grid(max_active, (d.hidden + kMoeRowsPerCta - 1) / kMoeRowsPerCta);
+            launch_pdl(moe_down_kernel, grid, kMoeThreads, 0, stream, d, w.down, b.act, b.active, b.offsets, b.eout,
+                       err);
+        }
         count_launch();
     }
 }

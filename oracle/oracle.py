@@ -687,3 +687,53 @@ def moe_run(dims, w: dict, x: np.ndarray, impl: str = "port", checkpoints: bool 
         return st, y, route, cps
     finally:
         L.kq_moe_config_close(cfg)
+
+
+class RefMoe:
+    """The reference's own MoE operators (oracle/_ref) on one test config:
+    kq_moe_route_f32 and kq_moe_execute_routed_expert_f32 with F32 weights
+    (src/kq_moe_qwen38.c:276-376,461-568).  Used as the CPU baseline of the
+    MoE decode record: every selected expert and the shared expert run
+    through the reference's expert operator."""
+
+    def __init__(self, dims):
+        L = ref()
+        self.L, self.dims = L, dims
+        self.cfg = vp()
+        d = _Diag()
+        qd = _RefMoeDims(dims.hidden, dims.experts, dims.top_k, dims.routed, dims.shared, 0)
+        if L.kq_moe_test_config_create(C.byref(qd), C.byref(self.cfg), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        L.kq_moe_config_one_expert_workspace_bytes.restype = u64
+        self.scratch = np.empty(L.kq_moe_config_one_expert_workspace_bytes(self.cfg) // 4 + 1, np.float32)
+        self.out = np.empty(dims.hidden, np.float32)
+
+    def route(self, router: np.ndarray, x: np.ndarray):
+        E, K = self.dims.experts, self.dims.top_k
+        lg, pr = np.empty(E, np.float32), np.empty(E, np.float32)
+        ids, w = np.empty(K, np.uint32), np.empty(K, np.float32)
+        d = _Diag()
+        st = self.L.kq_moe_route_f32(self.cfg, router.ctypes.data_as(vp), u64(router.size), x.ctypes.data_as(vp),
+                                     lg.ctypes.data_as(vp), u64(E), pr.ctypes.data_as(vp), u64(E),
+                                     ids.ctypes.data_as(vp), u64(K), w.ctypes.data_as(vp), u64(K), C.byref(d))
+        if st != 0:
+            raise RuntimeError(d.message)
+        return ids, w
+
+    def expert(self, gate: np.ndarray, up: np.ndarray, down: np.ndarray, x: np.ndarray) -> np.ndarray:
+        ew = (_RefExpertWeights)(gate.ctypes.data, gate.size, up.ctypes.data, up.size, down.ctypes.data, down.size)
+        d = _Diag()
+        st = self.L.kq_moe_execute_routed_expert_f32(self.cfg, C.byref(ew), u32(0), x.ctypes.data_as(vp),
+                                                     self.out.ctypes.data_as(vp), u64(self.out.size),
+                                                     self.scratch.ctypes.data_as(vp), u64(self.scratch.nbytes),
+                                                     C.byref(d))
+        if st != 0:
+            raise RuntimeError(d.message)
+        return self.out.copy()
+
+    def close(self):
+        self.L.kq_moe_config_close(self.cfg)
+
+
+class _RefExpertWeights(C.Structure):   # include/kq_moe.h:91-98
+    _fields_ = _pairs(["gate", "up", "down"])
