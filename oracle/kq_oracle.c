@@ -859,3 +859,150 @@ int kqo_moe_run_observed(const kqo_moe_dims *dm, const kqo_moe_weights *w, const
     free(ids);
     return st;
 }
+
+/* ----------------------------------------------------------------- layer */
+
+/* Gated-residual read of src/kq_layer_qwen38.c:37-165 over F32 weights:
+ * per-branch (1 + w) RMSNorm, rank = silu(down . n / B), read gate =
+ * sigmoid(up . rank), mixed = sum_b gate * n / B, write gate =
+ * 2 sigmoid(inject . n / B). */
+static int kqo_gr_read(const kqo_layer_dims *dm, const kqo_gr_weights *w, const float *br, float *nm, float *rg,
+                       float *mixed, float *rank, float *wg) {
+    const uint64_t H = dm->hidden_size, B = dm->branch_count, R = dm->gr_rank, W = H * B;
+    uint64_t b, i, j;
+    for (b = 0; b < B; ++b) {
+        /* kq_f32_rms_norm: src/kq_numeric.c:730-774 */
+        float sum = 0.0f, mean, inv;
+        const float *x = br + b * H;
+        for (i = 0; i < H; ++i) {
+            float sq = x[i] * x[i];
+            sum = sum + sq;
+        }
+        mean = sum / (float)H;
+        inv = 1.0f / sqrtf(mean + dm->rms_epsilon);
+        if (!isfinite(inv)) return KQO_NUMERIC_DOMAIN;
+        for (i = 0; i < H; ++i) {
+            float n = x[i] * inv;
+            float wt = 1.0f + w->norm[b * H + i];
+            nm[b * H + i] = n * wt;
+            if (!isfinite(nm[b * H + i])) return KQO_NUMERIC_DOMAIN;
+        }
+    }
+    for (i = 0; i < R; ++i) {
+        float sum = 0.0f;
+        for (j = 0; j < W; ++j) sum += w->down[i * W + j] * nm[j];
+        rank[i] = sum;
+    }
+    for (i = 0; i < R; ++i) rank[i] /= (float)B;
+    for (i = 0; i < R; ++i) rank[i] *= kqo_sigmoid(rank[i]);
+    for (i = 0; i < W; ++i) {
+        float sum = 0.0f;
+        for (j = 0; j < R; ++j) sum += w->up[i * R + j] * rank[j];
+        rg[i] = sum;
+    }
+    for (i = 0; i < W; ++i) rg[i] = kqo_sigmoid(rg[i]);
+    for (i = 0; i < H; ++i) {
+        float sum = 0.0f;
+        for (b = 0; b < B; ++b) sum += rg[b * H + i] * nm[b * H + i];
+        mixed[i] = sum / (float)B;
+    }
+    for (b = 0; b < B; ++b) {
+        float sum = 0.0f;
+        for (j = 0; j < W; ++j) sum += w->inject[b * W + j] * nm[j];
+        wg[b] = sum;
+    }
+    for (b = 0; b < B; ++b) wg[b] /= (float)B;
+    for (b = 0; b < B; ++b) wg[b] = 2.0f * kqo_sigmoid(wg[b]);
+    return KQO_OK;
+}
+
+/* kq_layer_gr_write_f32: src/kq_layer_qwen38.c:196-209. */
+static void kqo_gr_write(const kqo_layer_dims *dm, const float *br, const float *block, const float *wg, float *out) {
+    uint64_t b, i;
+    for (b = 0; b < dm->branch_count; ++b)
+        for (i = 0; i < dm->hidden_size; ++i) {
+            uint64_t o = b * dm->hidden_size + i;
+            out[o] = br[o] + block[i] * wg[b];
+        }
+}
+
+/* One decoder layer over T tokens (src/kq_layer.c:639-827 without PLE):
+ * attention gated-residual read per token, the mixer over all T tokens
+ * (GDN with the padding mask, or QSA), write, MoE gated-residual read, the
+ * MoE over all T tokens, write.  The mixer's state arrays are updated only
+ * on success (the layer's transactional contract); checkpoints follow
+ * include/kq_layer.h's kinds in the reference's order (rank 2 ones with
+ * dims (branches, hidden)). */
+int kqo_layer_run_observed(const kqo_layer_dims *dm, const kqo_gr_weights *attn_gr, const kqo_gr_weights *moe_gr,
+                           const kqo_gdn_dims *gd, const kqo_gdn_weights *gw, float *conv, float *rec,
+                           const kqo_qsa_dims *qd, const kqo_qsa_weights *qw, float *kc, float *vc, float *rc,
+                           uint64_t capacity, uint64_t *length, const kqo_moe_dims *md, const kqo_moe_weights *mw,
+                           const float *input, uint64_t tokens, const uint8_t *mask, float *output,
+                           kqo_checkpoint_fn cb, void *user) {
+    const uint64_t H = dm->hidden_size, B = dm->branch_count, W = H * B, R = dm->gr_rank;
+    float *buf, *nm, *rg, *rank, *mixed, *awg, *block, *after, *moe_in, *mwg, *moe_out, *staged;
+    float *conv2 = NULL, *rec2 = NULL;
+    uint64_t t, len = length ? *length : 0;
+    int st = KQO_OK;
+    if (H == 0 || B == 0 || R == 0 || (dm->family == 1) == (gd == NULL)) return KQO_INVALID_ARGUMENT;
+    buf = (float *)malloc(sizeof(float) * (2 * W + R + tokens * (2 * H + B + W + H + B + H + W)));
+    if (buf == NULL) return KQO_INVALID_ARGUMENT;
+    nm = buf; rg = nm + W; rank = rg + W; mixed = rank + R; awg = mixed + tokens * H; block = awg + tokens * B;
+    after = block + tokens * H; moe_in = after + tokens * W; mwg = moe_in + tokens * H; moe_out = mwg + tokens * B;
+    staged = moe_out + tokens * H;
+    for (t = 0; t < tokens; ++t) kqo_emit(cb, user, 0, t, 2, B, H, 0, input + t * W, W);   /* INPUT */
+    for (t = 0; t < tokens && st == KQO_OK; ++t) {
+        st = kqo_gr_read(dm, attn_gr, input + t * W, nm, rg, mixed + t * H, rank, awg + t * B);
+        if (st != KQO_OK) break;
+        kqo_emit(cb, user, 3, t, 2, B, H, 0, nm, W);             /* ATTN_GR_NORMALIZED */
+        kqo_emit(cb, user, 4, t, 2, B, H, 0, rg, W);             /* ATTN_GR_READ_GATE */
+        kqo_emit(cb, user, 5, t, 1, H, 0, 0, mixed + t * H, H);  /* MIXER_INPUT */
+    }
+    if (st == KQO_OK) {
+        if (gd != NULL) {
+            const uint64_t nc = ((uint64_t)2 * gd->key_heads * gd->key_dim +
+                                 (uint64_t)gd->value_heads * gd->value_dim) * gd->conv_kernel;
+            const uint64_t nr = (uint64_t)gd->value_heads * gd->key_dim * gd->value_dim;
+            conv2 = (float *)malloc(sizeof(float) * nc);
+            rec2 = (float *)malloc(sizeof(float) * nr);
+            if (conv2 == NULL || rec2 == NULL) st = KQO_INVALID_ARGUMENT;
+            else {
+                memcpy(conv2, conv, sizeof(float) * nc);
+                memcpy(rec2, rec, sizeof(float) * nr);
+                st = kqo_gdn_run(gd, gw, mixed, tokens, mask, block, conv2, rec2);
+                if (st == KQO_OK) {
+                    memcpy(conv, conv2, sizeof(float) * nc);
+                    memcpy(rec, rec2, sizeof(float) * nr);
+                }
+            }
+        } else {
+            st = kqo_qsa_run(qd, qw, mixed, tokens, block, kc, vc, rc, capacity, &len, NULL, NULL, NULL);
+        }
+    }
+    for (t = 0; t < tokens && st == KQO_OK; ++t) {
+        kqo_emit(cb, user, 6, t, 1, H, 0, 0, block + t * H, H);   /* MIXER_OUTPUT */
+        kqo_emit(cb, user, 7, t, 1, B, 0, 0, awg + t * B, B);     /* ATTN_GR_WRITE_GATE */
+        kqo_gr_write(dm, input + t * W, block + t * H, awg + t * B, after + t * W);
+        kqo_emit(cb, user, 8, t, 2, B, H, 0, after + t * W, W);   /* AFTER_MIXER_RESIDUAL */
+        st = kqo_gr_read(dm, moe_gr, after + t * W, nm, rg, moe_in + t * H, rank, mwg + t * B);
+        if (st != KQO_OK) break;
+        kqo_emit(cb, user, 9, t, 2, B, H, 0, nm, W);              /* MOE_GR_NORMALIZED */
+        kqo_emit(cb, user, 10, t, 2, B, H, 0, rg, W);             /* MOE_GR_READ_GATE */
+        kqo_emit(cb, user, 11, t, 1, H, 0, 0, moe_in + t * H, H); /* MOE_INPUT */
+    }
+    if (st == KQO_OK) st = kqo_moe_run(md, mw, moe_in, tokens, moe_out, NULL, NULL, NULL, NULL);
+    for (t = 0; t < tokens && st == KQO_OK; ++t) {
+        kqo_emit(cb, user, 12, t, 1, H, 0, 0, moe_out + t * H, H);  /* MOE_OUTPUT */
+        kqo_emit(cb, user, 13, t, 1, B, 0, 0, mwg + t * B, B);      /* MOE_GR_WRITE_GATE */
+        kqo_gr_write(dm, after + t * W, moe_out + t * H, mwg + t * B, staged + t * W);
+        kqo_emit(cb, user, 14, t, 2, B, H, 0, staged + t * W, W);   /* OUTPUT */
+    }
+    if (st == KQO_OK) {
+        memcpy(output, staged, sizeof(float) * tokens * W);
+        if (length) *length = len;
+    }
+    free(conv2);
+    free(rec2);
+    free(buf);
+    return st;
+}

@@ -172,6 +172,33 @@ int kqo_moe_run_observed(const kqo_moe_dims *dims, const kqo_moe_weights *weight
                          uint64_t tokens, float *output, float *logits, float *probabilities,
                          uint32_t *selected_ids, float *selected_weights, kqo_moe_checkpoint_fn cb, void *user);
 
+typedef struct kqo_layer_dims {
+    uint32_t hidden_size;
+    uint32_t branch_count;
+    uint32_t gr_rank;
+    float rms_epsilon;
+    uint32_t family;   /* 1 GDN, 2 QSA (kq_layer_family) */
+} kqo_layer_dims;
+
+typedef struct kqo_gr_weights {
+    const float *norm;    /* [B*H] (1 + w form) */
+    const float *down;    /* [R][B*H] */
+    const float *up;      /* [B*H][R] */
+    const float *inject;  /* [B][B*H] */
+} kqo_gr_weights;
+
+/* One decoder layer (gated residual, GDN or QSA mixer, gated residual, MoE)
+ * over T tokens of [B][H] branches: src/kq_layer.c:639-827 without PLE.
+ * Pass the GDN arguments (and NULL QSA ones) for family 1, the QSA ones for
+ * family 2; state arrays and *length change only on success. */
+int kqo_layer_run_observed(const kqo_layer_dims *dims, const kqo_gr_weights *attn_gr, const kqo_gr_weights *moe_gr,
+                           const kqo_gdn_dims *gdn_dims, const kqo_gdn_weights *gdn_weights, float *conv_state,
+                           float *recurrent_state, const kqo_qsa_dims *qsa_dims, const kqo_qsa_weights *qsa_weights,
+                           float *key_cache, float *value_cache, float *raw_cache, uint64_t capacity,
+                           uint64_t *length, const kqo_moe_dims *moe_dims, const kqo_moe_weights *moe_weights,
+                           const float *input, uint64_t tokens, const uint8_t *mask, float *output,
+                           kqo_checkpoint_fn cb, void *user);
+
 /* Stable top-k by (score desc, id asc): src/kq_qsa_qwen38.c:328-359. */
 uint64_t kqo_select_blocks(const float *scores, uint64_t count, uint64_t limit,
                            uint32_t *selected);

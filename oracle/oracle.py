@@ -737,3 +737,175 @@ class RefMoe:
 
 class _RefExpertWeights(C.Structure):   # include/kq_moe.h:91-98
     _fields_ = _pairs(["gate", "up", "down"])
+
+
+# ------------------------------------------------------------------ layer
+
+GR_FIELDS = ["norm", "down", "up", "inject"]
+
+
+class _LayerDims(C.Structure):   # kqo_layer_dims
+    _fields_ = [("hidden_size", u32), ("branch_count", u32), ("gr_rank", u32), ("rms_epsilon", f32),
+                ("family", u32)]
+
+
+class _GrWeights(C.Structure):   # kqo_gr_weights
+    _fields_ = [(n, vp) for n in GR_FIELDS]
+
+
+class _RefLayerDims(C.Structure):   # src/kq_layer_internal.h:10-17
+    _fields_ = [("layer_id", u32), ("hidden_size", u32), ("branch_count", u32), ("gr_rank", u32),
+                ("rms_epsilon", f32), ("family", C.c_int)]
+
+
+class _RefGrWeights(C.Structure):   # include/kq_layer.h kq_layer_gr_weights_f32
+    _fields_ = _pairs(GR_FIELDS)
+
+
+class _RefLayerWeights(C.Structure):   # include/kq_layer.h kq_layer_weights_f32
+    _fields_ = [("attention_gr", _RefGrWeights), ("moe_gr", _RefGrWeights), ("gdn", vp), ("qsa", vp), ("moe", vp),
+                ("ple_value", vp), ("ple_provider", vp)]
+
+
+class _RefLayerCheckpoint(C.Structure):   # include/kq_layer.h kq_layer_checkpoint
+    _fields_ = [("kind", C.c_int), ("token_index", u64), ("rank", u32), ("dimensions", u64 * 3),
+                ("values", C.POINTER(f32)), ("value_count", u64)]
+
+
+_REF_LAYER_CB = C.CFUNCTYPE(None, C.POINTER(_RefLayerCheckpoint), vp)
+
+
+def layer_sequence(impl: str, ld, gr: dict, mixer_dims, mixer_w: dict, moe_dims, moe_w: dict, blocks, masks=None,
+                   capacity: int = 64, checkpoints: bool = False):
+    """Runs the token blocks `blocks` ([T_i][B*H] each) one after another
+    through one decoder layer from a zero state.  ld: (hidden, branches,
+    rank, eps, family 1 GDN / 2 QSA); gr: {"attn": {norm, down, up, inject},
+    "moe": {...}}.  Returns a list of (status, output, checkpoints)."""
+    hidden, branches, rank, eps, family = ld
+    gw = {side: {k: _a(gr[side][k]).reshape(-1) for k in GR_FIELDS} for side in ("attn", "moe")}
+    mw = {k: _a(moe_w[k]).reshape(-1) for k in MOE_FIELDS}
+    fields = GDN_FIELDS if family == 1 else QSA_FIELDS
+    xw = {k: _a(mixer_w[k]).reshape(-1) for k in fields}
+    out = []
+    if impl == "port":
+        ldm = _LayerDims(hidden, branches, rank, eps, family)
+        grs = [_GrWeights(*[gw[s][k].ctypes.data for k in GR_FIELDS]) for s in ("attn", "moe")]
+        md = _MoeDims(moe_dims.hidden, moe_dims.experts, moe_dims.top_k, moe_dims.routed, moe_dims.shared)
+        mws = _MoeWeights(*[mw[k].ctypes.data for k in MOE_FIELDS])
+        if family == 1:
+            d = mixer_dims
+            gd = _GdnDims(d.hidden, d.key_heads, d.value_heads, d.key_dim, d.value_dim, d.conv_kernel, d.eps)
+            gws = _GdnWeights(*[xw[k].ctypes.data for k in GDN_FIELDS])
+            conv = np.zeros(d.conv_channels * d.conv_kernel, np.float32)
+            rec = np.zeros(d.value_heads * d.key_dim * d.value_dim, np.float32)
+        else:
+            d = mixer_dims
+            qd = _QsaDims(d.hidden, d.query_heads, d.kv_heads, d.head_dim, d.index_heads, d.index_dim, d.block,
+                          d.budget, d.rotary, d.eps, d.theta)
+            qws = _QsaWeights(*[xw[k].ctypes.data for k in QSA_FIELDS])
+            kc = np.zeros((capacity, d.kv_width), np.float32)
+            vc = np.zeros((capacity, d.kv_width), np.float32)
+            rc = np.zeros((capacity, d.index_dim), np.float32)
+            length = u64(0)
+        for bi, x in enumerate(blocks):
+            xv = _a(x).reshape(-1, hidden * branches)
+            y = np.zeros_like(xv)
+            cps = []
+
+            def on_cp(kind, token, rank_, dp, values, count, _u):
+                cps.append((int(kind), int(token), int(rank_), tuple(int(dp[i]) for i in range(rank_)),
+                            np.ctypeslib.as_array(values, (count,)).copy()))
+
+            cb = _PORT_CB(on_cp) if checkpoints else _PORT_CB()
+            m = None if masks is None or masks[bi] is None else np.ascontiguousarray(masks[bi], np.uint8)
+            if family == 1:
+                st = port().kqo_layer_run_observed(
+                    C.byref(ldm), C.byref(grs[0]), C.byref(grs[1]), C.byref(gd), C.byref(gws),
+                    conv.ctypes.data_as(vp), rec.ctypes.data_as(vp), None, None, None, None, None, u64(0), None,
+                    C.byref(md), C.byref(mws), xv.ctypes.data_as(vp), u64(xv.shape[0]),
+                    None if m is None else m.ctypes.data_as(vp), y.ctypes.data_as(vp), cb, None)
+            else:
+                st = port().kqo_layer_run_observed(
+                    C.byref(ldm), C.byref(grs[0]), C.byref(grs[1]), None, None, None, None, C.byref(qd),
+                    C.byref(qws), kc.ctypes.data_as(vp), vc.ctypes.data_as(vp), rc.ctypes.data_as(vp), u64(capacity),
+                    C.byref(length), C.byref(md), C.byref(mws), xv.ctypes.data_as(vp), u64(xv.shape[0]), None,
+                    y.ctypes.data_as(vp), cb, None)
+            out.append((st, y, cps))
+        return out
+    L = ref()
+    d0 = _Diag()
+    sub = vp()
+    if family == 1:
+        d = mixer_dims
+        g = _RefGdnDims(d.hidden, d.key_heads, d.value_heads, d.key_dim, d.value_dim, d.conv_kernel, d.eps, 0)
+        if L.kq_gdn_test_config_create(C.byref(g), C.byref(sub), C.byref(d0)) != 0:
+            raise RuntimeError(d0.message)
+        sw = _RefGdnWeights()
+    else:
+        d = mixer_dims
+        q = _RefQsaDims(d.hidden, d.query_heads, d.kv_heads, d.head_dim, d.index_heads, d.index_dim, d.block,
+                        d.budget, capacity, d.rotary, d.eps, d.theta, 0)
+        if L.kq_qsa_test_config_create(C.byref(q), C.byref(sub), C.byref(d0)) != 0:
+            raise RuntimeError(d0.message)
+        sw = _RefQsaWeights()
+    for k in fields:
+        setattr(sw, k, xw[k].ctypes.data)
+        setattr(sw, k + "_count", xw[k].size)
+    moe_cfg = vp()
+    if L.kq_moe_test_config_create(C.byref(_RefMoeDims(moe_dims.hidden, moe_dims.experts, moe_dims.top_k,
+                                                       moe_dims.routed, moe_dims.shared, 0)),
+                                   C.byref(moe_cfg), C.byref(d0)) != 0:
+        raise RuntimeError(d0.message)
+    rmw = _RefMoeWeights()
+    for k in MOE_FIELDS:
+        setattr(rmw, k, mw[k].ctypes.data)
+        setattr(rmw, k + "_count", mw[k].size)
+    lcfg, state = vp(), vp()
+    rd = _RefLayerDims(0 if family == 1 else 3, hidden, branches, rank, eps, family)
+    st = L.kq_layer_test_config_create(C.byref(rd), sub if family == 1 else None, sub if family == 2 else None,
+                                       moe_cfg, None, None, C.byref(lcfg), C.byref(d0))
+    if st != 0:
+        raise RuntimeError(f"layer config: {st} {d0.message}")
+    lw = _RefLayerWeights()
+    for side, dst in (("attn", lw.attention_gr), ("moe", lw.moe_gr)):
+        for k in GR_FIELDS:
+            setattr(dst, k, gw[side][k].ctypes.data)
+            setattr(dst, k + "_count", gw[side][k].size)
+    lw.gdn = C.cast(C.pointer(sw), vp) if family == 1 else None
+    lw.qsa = C.cast(C.pointer(sw), vp) if family == 2 else None
+    lw.moe = C.cast(C.pointer(rmw), vp)
+    try:
+        if L.kq_layer_state_create(lcfg, u64(capacity if family == 2 else 0), C.byref(state), C.byref(d0)) != 0:
+            raise RuntimeError(d0.message)
+        for bi, x in enumerate(blocks):
+            xv = _a(x).reshape(-1, hidden * branches)
+            T = xv.shape[0]
+            y = np.zeros_like(xv)
+            need = u64()
+            L.kq_layer_required_scratch_bytes(lcfg, state, u64(T), C.byref(need), C.byref(d0))
+            scratch = np.zeros(need.value // 4 + 1, np.float32)
+            cps = []
+
+            def on_cp(p, _u):
+                c = p.contents
+                cps.append((int(c.kind), int(c.token_index), int(c.rank),
+                            tuple(int(c.dimensions[i]) for i in range(c.rank)),
+                            np.ctypeslib.as_array(c.values, (c.value_count,)).copy()))
+
+            cb = _REF_LAYER_CB(on_cp) if checkpoints else _REF_LAYER_CB()
+            m = None if masks is None or masks[bi] is None else np.ascontiguousarray(masks[bi], np.uint8)
+            st = L.kq_layer_prefill_f32(lcfg, C.byref(lw), xv.ctypes.data_as(vp), None, u64(T),
+                                        None if m is None else m.ctypes.data_as(vp), y.ctypes.data_as(vp),
+                                        u64(y.size), state, scratch.ctypes.data_as(vp), need, cb, None, None,
+                                        C.byref(d0))
+            out.append((st, y, cps))
+        return out
+    finally:
+        if state:
+            L.kq_layer_state_close(state)
+        L.kq_layer_config_close(lcfg)
+        L.kq_moe_config_close(moe_cfg)
+        if family == 1:
+            L.kq_gdn_config_close(sub)
+        else:
+            L.kq_qsa_config_close(sub)

@@ -13,6 +13,9 @@ the reference at run time:
   moe_golden.npz / moe_golden.json   research/operators/.../moe-{contract,
                                      calibration,holdout,routing-vectors,
                                      native-validation}.json
+  layer_golden.npz / layer_golden.json
+                                     research/operators/.../layer-{contract,
+                                     calibration,holdout,native-validation}.json
   dequant_golden.json                research/numerics/.../dequant-vectors.json
 
 Expected values in those files come from pinned Transformers / llama.cpp
@@ -209,6 +212,68 @@ def moe(ops: Path) -> None:
     (OUT / "moe_golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True) + "\n")
 
 
+def layer(ops: Path) -> None:
+    """GDN and QSA decoder-layer cases (the PLE_GDN family needs the PLE
+    operator, which the B200 library does not provide)."""
+    cal = json.loads((ops / "layer-calibration.json").read_text())
+    hold = json.loads((ops / "layer-holdout.json").read_text())
+    contract = json.loads((ops / "layer-contract.json").read_text())
+    native = json.loads((ops / "layer-native-validation.json").read_text())
+    rc = contract["reduced"]
+    H, B = rc["hidden"], rc["branches"]
+    arrays: dict[str, np.ndarray] = {}
+    gr = {"norm": "hc_norm.weight", "down": "input_mix_weight_down.weight", "up": "input_mix_weight_up.weight",
+          "inject": "block_inject_weight.weight"}
+    gdn_names = {"a_log": "A_log", "conv": "conv1d.weight", "dt_bias": "dt_bias", "alpha": "in_proj_a.weight",
+                 "beta": "in_proj_b.weight", "qkv": "in_proj_qkv.weight", "gate": "in_proj_z.weight",
+                 "norm": "norm.weight", "output": "out_proj.weight"}
+    qsa_names = {"query": "q_proj.weight", "key": "k_proj.weight", "value": "v_proj.weight", "output": "o_proj.weight",
+                 "query_norm": "q_norm.weight", "key_norm": "k_norm.weight",
+                 "index_query_norm": "indexer.q_layernorm.weight", "index_key_norm": "indexer.k_layernorm.weight"}
+    cases = []
+    for split, src in (("calibration", cal["cases"]), ("holdout", hold["cases"])):
+        for c in src:
+            if c["family"] not in ("GDN", "QSA"):
+                continue
+            i = len(cases)
+            w = c["weights"]
+            T = c["input"]["shape"][1]
+            arrays[f"c{i}_input"] = f32(c["input"]).reshape(T, B * H)
+            arrays[f"c{i}_output"] = f32(c["output"]).reshape(T, B * H)
+            for k, v in c["checkpoints"].items():
+                arrays[f"c{i}_ck_{k}"] = f32(v).reshape(T, H)
+            for side in ("attn", "mlp"):
+                for k, v in gr.items():
+                    arrays[f"c{i}_{side}_gr_{k}"] = f32(w[f"{side}_hyper_connection.{v}"]).reshape(-1)
+            if c["family"] == "GDN":
+                for k, v in gdn_names.items():
+                    arrays[f"c{i}_gdn_{k}"] = f32(w[f"linear_attn.{v}"]).reshape(-1)
+            else:
+                for k, v in qsa_names.items():
+                    arrays[f"c{i}_qsa_{k}"] = f32(w[f"self_attn.{v}"]).reshape(-1)
+                qk = f32(w["self_attn.indexer.index_qk_proj.weight"])
+                di = qk.shape[0] // 3   # index_qk rows: 2 query heads then the key head
+                arrays[f"c{i}_qsa_index_query"] = qk[:2 * di].reshape(-1)
+                arrays[f"c{i}_qsa_index_key"] = qk[2 * di:].reshape(-1)
+            E = rc["experts"]
+            I = rc["intermediate"]
+            gate_up = f32(w["mlp.experts.gate_up_proj"]).reshape(E, 2 * I, H)
+            arrays[f"c{i}_moe_router"] = f32(w["mlp.gate.weight"]).reshape(-1)
+            arrays[f"c{i}_moe_routed_gate"] = np.ascontiguousarray(gate_up[:, :I, :]).reshape(-1)
+            arrays[f"c{i}_moe_routed_up"] = np.ascontiguousarray(gate_up[:, I:, :]).reshape(-1)
+            arrays[f"c{i}_moe_routed_down"] = f32(w["mlp.experts.down_proj"]).reshape(-1)
+            arrays[f"c{i}_moe_shared_gate"] = f32(w["mlp.shared_expert.gate_proj.weight"]).reshape(-1)
+            arrays[f"c{i}_moe_shared_up"] = f32(w["mlp.shared_expert.up_proj.weight"]).reshape(-1)
+            arrays[f"c{i}_moe_shared_down"] = f32(w["mlp.shared_expert.down_proj.weight"]).reshape(-1)
+            arrays[f"c{i}_moe_shared_gate_weight"] = f32(w["mlp.shared_expert_gate.weight"]).reshape(-1)
+            cases.append({"id": c["id"], "split": split, "family": c["family"], "tokens": T,
+                          "token_ids": c["token_ids"], "state_position": c["state_position"]})
+    meta = {"source": f"Kestrel-Q research/operators/Qwen3.8-Flash-Next/{REV}/layer-*.json",
+            "reduced": rc, "cases": cases, "validation": native["records"]}
+    np.savez_compressed(OUT / "layer_golden.npz", **arrays)
+    (OUT / "layer_golden.json").write_text(json.dumps(meta, indent=1, sort_keys=True) + "\n")
+
+
 def dequant(num: Path) -> None:
     d = json.loads((num / "dequant-vectors.json").read_text())
     keep = {"F32", "BF16", "Q8_0", "Q4_K"}
@@ -232,6 +297,7 @@ def main() -> None:
     gdn(root / "operators" / "Qwen3.8-Flash-Next" / REV)
     qsa(root / "operators" / "Qwen3.8-Flash-Next" / REV)
     moe(root / "operators" / "Qwen3.8-Flash-Next" / REV)
+    layer(root / "operators" / "Qwen3.8-Flash-Next" / REV)
     dequant(root / "numerics" / "Qwen3.8-Flash-Next" / REV)
 
 

@@ -488,3 +488,75 @@ def test_port_moe_matches_reference_bits(oracle, seed, T):
     assert len(ca) == len(cb) == T * (12 + 5 * dims.top_k)
     for p, q in zip(ca, cb):
         assert p[:4] == q[:4] and np.array_equal(bits(p[4]), bits(q[4]))
+
+
+# ------------------------------------------------------------------ layer
+
+def layer_golden():
+    meta = json.loads((GOLD / "layer_golden.json").read_text())
+    return meta, np.load(GOLD / "layer_golden.npz")
+
+
+def layer_case(oracle, meta, arr, i):
+    """(layer dims tuple, gated-residual weights, mixer dims, mixer weights,
+    MoE dims, MoE weights) of golden case i, with the reduced geometry of the
+    reference's own layer fixture (tests/layer_test.c:43-45)."""
+    from kqb200 import synth
+    fam = 1 if meta["cases"][i]["family"] == "GDN" else 2
+    gr = {"attn": {k: arr[f"c{i}_attn_gr_{k}"] for k in oracle.GR_FIELDS},
+          "moe": {k: arr[f"c{i}_mlp_gr_{k}"] for k in oracle.GR_FIELDS}}
+    if fam == 1:
+        md = synth.GdnDims(hidden=8, key_heads=2, value_heads=4, key_dim=4, value_dim=4, conv_kernel=4, eps=1e-6)
+        mw = {k: arr[f"c{i}_gdn_{k}"] for k in oracle.GDN_FIELDS}
+    else:
+        md = synth.QsaDims(hidden=8, query_heads=2, kv_heads=1, head_dim=4, index_heads=2, index_dim=4, block=4,
+                           budget=8, max_context=32, rotary=4, eps=1e-6, theta=1e7)
+        mw = {k: arr[f"c{i}_qsa_{k}"] for k in oracle.QSA_FIELDS}
+    moe_d = synth.MoeDims(hidden=8, experts=4, top_k=2, routed=4, shared=4)
+    moe_w = {k: arr[f"c{i}_moe_{k}"] for k in oracle.MOE_FIELDS}
+    return (8, 4, 4, 1e-6, fam), gr, md, mw, moe_d, moe_w
+
+
+def test_layer_oracle_matches_golden_cases(oracle):
+    """GDN and QSA decoder layers (gated residual, mixer, gated residual,
+    MoE) on the reference's golden cases: output and the four per-token
+    checkpoints within the reference's own validation limit (2e-6 absolute,
+    tools/validate-native-layer.py)."""
+    meta, arr = layer_golden()
+    names = {5: "attn_gr", 6: "mixer_output", 11: "moe_gr", 12: "moe_output"}
+    for i, c in enumerate(meta["cases"]):
+        ld, gr, md, mw, moe_d, moe_w = layer_case(oracle, meta, arr, i)
+        [(st, y, cps)] = oracle.layer_sequence("port", ld, gr, md, mw, moe_d, moe_w, [arr[f"c{i}_input"]],
+                                               capacity=16, checkpoints=True)
+        assert st == 0, c["id"]
+        assert np.abs(y - arr[f"c{i}_output"]).max() <= 2e-6, c["id"]
+        seen = 0
+        for kind, t, rank, dims, vals in cps:
+            if kind in names:
+                assert np.abs(vals - arr[f"c{i}_ck_{names[kind]}"][t]).max() <= 2e-6, (c["id"], kind, t)
+                seen += 1
+        assert seen == 4 * c["tokens"]
+        assert len(cps) == 13 * c["tokens"]
+
+
+@pytest.mark.parametrize("case", [0, 1, 2, 3])
+def test_port_layer_matches_reference_bits(oracle, case):
+    """Restatement vs the compiled reference (kq_layer_prefill_f32) on the
+    golden cases and on a prefill followed by two one-token steps (the state
+    carried across calls): every output and checkpoint bit for bit."""
+    if not oracle.ref_available():
+        pytest.skip("reference not built")
+    meta, arr = layer_golden()
+    ld, gr, md, mw, moe_d, moe_w = layer_case(oracle, meta, arr, case)
+    x = arr[f"c{case}_input"]
+    rng = np.random.default_rng(case)
+    blocks = [x, (x[:1] * 0.5 + rng.normal(0, 0.1, x[:1].shape)).astype(np.float32),
+              rng.normal(0, 0.3, x[:1].shape).astype(np.float32)]
+    a = oracle.layer_sequence("port", ld, gr, md, mw, moe_d, moe_w, blocks, capacity=16, checkpoints=True)
+    b = oracle.layer_sequence("reference", ld, gr, md, mw, moe_d, moe_w, blocks, capacity=16, checkpoints=True)
+    for (sa, ya, ca), (sb, yb, cb) in zip(a, b):
+        assert sa == sb == 0
+        assert np.array_equal(bits(ya), bits(yb))
+        assert len(ca) == len(cb)
+        for p, q in zip(ca, cb):
+            assert p[:4] == q[:4] and np.array_equal(bits(p[4]), bits(q[4]))
