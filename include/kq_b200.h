@@ -12,9 +12,11 @@
  *       kq_qsa_execute_quantized    src/kq_qsa_internal.h:94-102
  *       kq_moe_test_config_create   src/kq_moe_internal.h:45-48
  *       kq_moe_execute_quantized    src/kq_moe_internal.h:52-60
+ *       kq_layer_test_config_create src/kq_layer_internal.h:73-77
+ *       kq_layer_state_rollback_last src/kq_layer_internal.h:64-66
  *     The dimension records keep the reference's field order and types
  *     (src/kq_gdn_internal.h:11-20, src/kq_qsa_internal.h:11-25,
- *     src/kq_moe_internal.h:10-17).
+ *     src/kq_moe_internal.h:10-17, src/kq_layer_internal.h:9-16).
  *
  *  2. The device weight provider that stands in for the GGUF-backed one
  *     (src/kq_weight_provider.c:378-509): quantized GGUF blocks are uploaded
@@ -32,6 +34,7 @@
 #include <stdint.h>
 
 #include "kq_gdn.h"
+#include "kq_layer.h"
 #include "kq_model.h"
 #include "kq_moe.h"
 #include "kq_qsa.h"
@@ -80,6 +83,15 @@ typedef struct kq_moe_dimensions {
     kq_moe_activation_dtype activation_dtype;
 } kq_moe_dimensions;
 
+typedef struct kq_layer_dimensions {
+    uint32_t layer_id;
+    uint32_t hidden_size;
+    uint32_t branch_count;
+    uint32_t gr_rank;
+    float rms_epsilon;
+    kq_layer_family family;
+} kq_layer_dimensions;
+
 kq_status kq_gdn_test_config_create(const kq_gdn_dimensions *dimensions,
                                     kq_gdn_config **out_config,
                                     kq_diagnostic *diagnostic);
@@ -92,6 +104,26 @@ kq_status kq_qsa_test_config_create(const kq_qsa_dimensions *dimensions,
 kq_status kq_moe_test_config_create(const kq_moe_dimensions *dimensions,
                                     kq_moe_config **out_config,
                                     kq_diagnostic *diagnostic);
+
+/* A layer over caller-owned sub-configs (closed by the caller after the
+ * layer config): exactly one of gdn (families GDN) and qsa (QSA), and moe.
+ * ple and ple_value must be NULL (the PLE_GDN family is refused with
+ * KQ_STATUS_INCOMPATIBLE_LAYER). */
+kq_status kq_layer_test_config_create(const kq_layer_dimensions *dimensions,
+                                      kq_gdn_config *gdn,
+                                      kq_qsa_config *qsa,
+                                      kq_moe_config *moe,
+                                      kq_ple_config *ple,
+                                      kq_ple_value_config *ple_value,
+                                      kq_layer_config **out_config,
+                                      kq_diagnostic *diagnostic);
+
+/* Undoes the state's last successful call of `token_count` tokens (once; a
+ * second call, another count or a state without a commit is
+ * KQ_STATUS_INVALID_LAYER_STATE). */
+kq_status kq_layer_state_rollback_last(kq_layer_state *state,
+                                       uint64_t token_count,
+                                       kq_diagnostic *diagnostic);
 
 /* Provider mode: weights are the tensors bound to the config with
  * kq_b200_gdn_config_bind / kq_b200_qsa_config_bind /
@@ -357,6 +389,20 @@ typedef struct kq_b200_qsa_tensors {
     const kq_semantic_tensor *index_key_norm;   /* F32 [di] */
 } kq_b200_qsa_tensors;
 
+/* Gated-residual tensors of a layer in the reference's binding order
+ * (src/kq_layer.c:100-120): per side inject [B x W], norm F32 vector [W]
+ * (1 + w form), down [rank x W], up [W x rank]. */
+typedef struct kq_b200_layer_tensors {
+    const kq_semantic_tensor *attention_inject;
+    const kq_semantic_tensor *attention_norm;
+    const kq_semantic_tensor *attention_down;
+    const kq_semantic_tensor *attention_up;
+    const kq_semantic_tensor *moe_inject;
+    const kq_semantic_tensor *moe_norm;
+    const kq_semantic_tensor *moe_down;
+    const kq_semantic_tensor *moe_up;
+} kq_b200_layer_tensors;
+
 /* Binds provider tensors to a config (what kq_*_config_create does from a
  * GGUF model in the reference).  Shapes are validated against the config. */
 kq_status kq_b200_gdn_config_bind(kq_gdn_config *config,
@@ -371,6 +417,12 @@ kq_status kq_b200_moe_config_bind(kq_moe_config *config,
                                   kq_weight_provider *provider,
                                   const kq_b200_moe_tensors *tensors,
                                   kq_diagnostic *diagnostic);
+/* The layer's gated-residual tensors; its mixer and MoE configs are bound
+ * to the same provider with their own bind calls. */
+kq_status kq_b200_layer_config_bind(kq_layer_config *config,
+                                    kq_weight_provider *provider,
+                                    const kq_b200_layer_tensors *tensors,
+                                    kq_diagnostic *diagnostic);
 
 /* ---------------------------------------------------------------- group 3 */
 
@@ -409,6 +461,23 @@ kq_status kq_b200_moe_execute_async(const kq_moe_config *config,
                                     uint64_t tokens,
                                     float *output,
                                     kq_diagnostic *diagnostic);
+
+/* The decoder layer on device arrays of branches [tokens][B][H] of a
+ * provider-bound config, asynchronous on the library stream: one token for
+ * each of `batch` sequences (distinct states), or T tokens of one sequence.
+ * Errors surface at kq_b200_synchronize, which rolls every state back. */
+kq_status kq_b200_layer_decode_batch(const kq_layer_config *config,
+                                     kq_layer_state *const *states,
+                                     uint32_t batch,
+                                     const float *branches,
+                                     float *output,
+                                     kq_diagnostic *diagnostic);
+kq_status kq_b200_layer_prefill_async(const kq_layer_config *config,
+                                      kq_layer_state *state,
+                                      const float *branches,
+                                      uint64_t T,
+                                      float *output,
+                                      kq_diagnostic *diagnostic);
 
 /* T tokens of one sequence, like kq_gdn_execute_quantized /
  * kq_qsa_execute_quantized (src/kq_gdn_internal.h:81-96,

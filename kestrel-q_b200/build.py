@@ -32,12 +32,14 @@ SOURCES = [
     "kernels_qsa.cu",
     "kernels_umma.cu",
     "kernels_moe.cu",
+    "kernels_layer.cu",
     "runtime.cpp",
     "api_basic.cpp",
     "api_provider.cpp",
     "api_gdn.cpp",
     "api_qsa.cpp",
     "api_moe.cpp",
+    "api_layer.cpp",
     "api_static.cu",
 ]
 

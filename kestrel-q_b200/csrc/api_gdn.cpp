@@ -14,6 +14,7 @@
 
 #include "kq_b200.h"
 #include "kq_gdn.h"
+#include "operators.hpp"
 #include "provider.hpp"
 #include "runtime.hpp"
 
@@ -360,6 +361,57 @@ static kq_status gdn_debug_run(DeviceContext *c, const kq_gdn_config *cfg, const
 
 // Host/device staging + synchronous execution shared by the F32 and the
 // provider entry points (`observer` non-null: the checkpoint path).
+// F32 weight arrays (host: uploaded once and reused while their contents
+// stay the same; device: used in place, checked on the device) as the
+// operator's dense matrices.
+static kq_status resolve_f32(DeviceContext *c, const kq_gdn_config *cfg, const kq_gdn_weights_f32 *wf, ErrorWord err,
+                             GdnResolved *out, kq_diagnostic *diag) {
+    const uint32_t H = cfg->dims.hidden_size;
+    kq_status st = KQ_STATUS_OK;
+    GdnResolved &w = *out;
+
+    {
+        const uint32_t Hh = H, C = cfg->conv_channels, Vd = cfg->value_width, Hv = cfg->dims.value_head_count;
+        const float *ptrs[9] = {wf->a_log, wf->conv, wf->dt_bias, wf->alpha, wf->beta,
+                                wf->qkv, wf->gate, wf->norm, wf->output};
+        const uint64_t counts[9] = {wf->a_log_count, wf->conv_count, wf->dt_bias_count,
+                                    wf->alpha_count, wf->beta_count, wf->qkv_count,
+                                    wf->gate_count, wf->norm_count, wf->output_count};
+        // host weights: uploaded once and reused while their contents stay
+        // the same; device weights: used in place, checked on the device
+        const float *dev[9];
+        for (int i = 0; i < 9; ++i) {
+            if (is_device_pointer(ptrs[i])) {
+                dev[i] = ptrs[i];
+                launch_check_finite(dev[i], counts[i], err, c->stream);
+            } else {
+                st = c->upload_cached(ptrs[i], counts[i], &dev[i], diag);
+                if (st != KQ_STATUS_OK) return st;
+            }
+        }
+        auto dense = [](const float *p, uint32_t rows, uint32_t cols) {
+            QMatrix m{};
+            m.data = reinterpret_cast<const uint8_t *>(p);
+            m.type = 0;
+            m.rows = rows;
+            m.cols = cols;
+            m.row_bytes = cols * 4;
+            m.layout = 0;
+            return m;
+        };
+        w.vec.a_log = dev[0];
+        w.vec.conv = dev[1];
+        w.vec.dt_bias = dev[2];
+        w.alpha = dense(dev[3], Hv, Hh);
+        w.beta = dense(dev[4], Hv, Hh);
+        w.qkv = dense(dev[5], C, Hh);
+        w.gate = dense(dev[6], Vd, Hh);
+        w.vec.norm = dev[7];
+        w.out = dense(dev[8], Hh, Vd);
+    }
+    return st;
+}
+
 static kq_status gdn_execute_sync(const kq_gdn_config *cfg, const GdnResolved *w_in,
                                   const kq_gdn_weights_f32 *wf, const float *hidden, uint64_t T,
                                   const uint8_t *mask, float *output, kq_gdn_state *state,
@@ -403,43 +455,8 @@ static kq_status gdn_execute_sync(const kq_gdn_config *cfg, const GdnResolved *w
     if (w_in) {
         w = *w_in;
     } else {
-        const uint32_t Hh = H, C = cfg->conv_channels, Vd = cfg->value_width, Hv = cfg->dims.value_head_count;
-        const float *ptrs[9] = {wf->a_log, wf->conv, wf->dt_bias, wf->alpha, wf->beta,
-                                wf->qkv, wf->gate, wf->norm, wf->output};
-        const uint64_t counts[9] = {wf->a_log_count, wf->conv_count, wf->dt_bias_count,
-                                    wf->alpha_count, wf->beta_count, wf->qkv_count,
-                                    wf->gate_count, wf->norm_count, wf->output_count};
-        // host weights: uploaded once and reused while their contents stay
-        // the same; device weights: used in place, checked on the device
-        const float *dev[9];
-        for (int i = 0; i < 9; ++i) {
-            if (is_device_pointer(ptrs[i])) {
-                dev[i] = ptrs[i];
-                launch_check_finite(dev[i], counts[i], err, c->stream);
-            } else {
-                st = c->upload_cached(ptrs[i], counts[i], &dev[i], diag);
-                if (st != KQ_STATUS_OK) return st;
-            }
-        }
-        auto dense = [](const float *p, uint32_t rows, uint32_t cols) {
-            QMatrix m{};
-            m.data = reinterpret_cast<const uint8_t *>(p);
-            m.type = 0;
-            m.rows = rows;
-            m.cols = cols;
-            m.row_bytes = cols * 4;
-            m.layout = 0;
-            return m;
-        };
-        w.vec.a_log = dev[0];
-        w.vec.conv = dev[1];
-        w.vec.dt_bias = dev[2];
-        w.alpha = dense(dev[3], Hv, Hh);
-        w.beta = dense(dev[4], Hv, Hh);
-        w.qkv = dense(dev[5], C, Hh);
-        w.gate = dense(dev[6], Vd, Hh);
-        w.vec.norm = dev[7];
-        w.out = dense(dev[8], Hh, Vd);
+        st = resolve_f32(c, cfg, wf, err, &w, diag);
+        if (st != KQ_STATUS_OK) return st;
     }
     kq_gdn_state *states[1] = {state};
     st = observer != nullptr
@@ -915,3 +932,49 @@ const char *kq_gdn_checkpoint_kind_name(kq_gdn_checkpoint_kind kind) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- layer bridge
+
+namespace kqb {
+
+kq_status gdn_layer_enqueue(DeviceContext *c, const kq_gdn_config *cfg, const kq_gdn_weights_f32 *wf,
+                            kq_gdn_state *const *states, uint32_t batch, uint32_t tokens, const float *x,
+                            const uint8_t *mask, float *y, ErrorWord err, kq_diagnostic *diag) {
+    if (!config_valid(cfg) || states == nullptr || batch == 0 || tokens == 0 || (batch > 1 && tokens > 1))
+        return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "valid compatible GDN call arguments are required");
+    if (cfg->dims.activation_dtype != KQ_GDN_ACTIVATION_F32)
+        return fail(diag, KQ_STATUS_INCOMPATIBLE_GDN, "F32 scalar execution requires an F32 reference configuration");
+    for (uint32_t b = 0; b < batch; ++b)
+        if (!state_valid(states[b]) || states[b]->config != cfg)
+            return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "every state must belong to the config");
+    GdnResolved w;
+    if (wf != nullptr) {
+        const uint64_t Hv = cfg->dims.value_head_count, H = cfg->dims.hidden_size;
+        const uint64_t want[9] = {Hv, (uint64_t)cfg->conv_channels * cfg->dims.conv_kernel_size, Hv, Hv * H, Hv * H,
+                                  (uint64_t)cfg->conv_channels * H, (uint64_t)cfg->value_width * H,
+                                  cfg->dims.value_head_dimension, H * cfg->value_width};
+        const float *ptrs[9] = {wf->a_log, wf->conv, wf->dt_bias, wf->alpha, wf->beta, wf->qkv, wf->gate, wf->norm,
+                                wf->output};
+        const uint64_t have[9] = {wf->a_log_count, wf->conv_count, wf->dt_bias_count, wf->alpha_count,
+                                  wf->beta_count, wf->qkv_count, wf->gate_count, wf->norm_count, wf->output_count};
+        for (int i = 0; i < 9; ++i) {
+            if (have[i] != want[i]) return fail(diag, KQ_STATUS_DIMENSION_MISMATCH, "GDN F32 weight count mismatch");
+            if (ptrs[i] == nullptr) return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "GDN F32 weights must be finite");
+        }
+        kq_status st = resolve_f32(c, cfg, wf, err, &w, diag);
+        if (st != KQ_STATUS_OK) return st;
+    } else if (!resolve_bound(cfg, &w)) {
+        return fail(diag, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "GDN provider matrix semantic is missing");
+    }
+    return gdn_enqueue(c, cfg, w, states, batch, tokens, x, mask, y, err, diag);
+}
+
+GdnSnapshot gdn_state_snapshot(const kq_gdn_state *s) { return GdnSnapshot{s->cur, s->initialized}; }
+
+void gdn_state_restore(kq_gdn_state *s, const GdnSnapshot &snap) {
+    s->cur = snap.cur;
+    s->initialized = snap.initialized;
+    s->on_success();
+}
+
+}  // namespace kqb

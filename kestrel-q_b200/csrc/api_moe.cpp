@@ -16,6 +16,7 @@
 
 #include "kq_b200.h"
 #include "kq_moe.h"
+#include "operators.hpp"
 #include "provider.hpp"
 #include "runtime.hpp"
 
@@ -675,3 +676,49 @@ const char *kq_moe_checkpoint_kind_name(kq_moe_checkpoint_kind kind) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- layer bridge
+
+namespace kqb {
+
+kq_status moe_layer_enqueue(DeviceContext *c, const kq_moe_config *cfg, const kq_moe_weights_f32 *wf, const float *x,
+                            uint64_t tokens, float *y, ErrorWord err, kq_diagnostic *diag) {
+    if (!config_valid(cfg) || tokens == 0)
+        return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "complete MoE execution arguments are required");
+    const kq_moe_dimensions &d = cfg->dims;
+    if (d.activation_dtype != KQ_MOE_ACTIVATION_F32)
+        return fail(diag, KQ_STATUS_INCOMPATIBLE_MOE, "scalar execution requires an F32 MoE config");
+    MoeWeightsDev w;
+    if (wf != nullptr) {
+        const uint64_t E = d.expert_count, H = d.hidden_size, I = d.routed_intermediate_size,
+                       S = d.shared_intermediate_size;
+        const float *src[8] = {wf->router, wf->routed_gate, wf->routed_up, wf->routed_down,
+                               wf->shared_gate, wf->shared_up, wf->shared_down, wf->shared_gate_weight};
+        const uint64_t cnt[8] = {wf->router_count, wf->routed_gate_count, wf->routed_up_count,
+                                 wf->routed_down_count, wf->shared_gate_count, wf->shared_up_count,
+                                 wf->shared_down_count, wf->shared_gate_weight_count};
+        const uint64_t want[8] = {E * H, E * I * H, E * I * H, E * I * H, S * H, S * H, S * H, H};
+        const float *p[8];
+        for (int i = 0; i < 8; ++i) {
+            if (cnt[i] != want[i]) return fail(diag, KQ_STATUS_DIMENSION_MISMATCH, "MoE weight shape/data mismatch");
+            if (src[i] == nullptr) return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "MoE weight shape/data mismatch");
+            kq_status st = device_weights(c, src[i], cnt[i], err, &p[i], diag);
+            if (st != KQ_STATUS_OK) return st;
+        }
+        w.router = dense(p[0], (uint32_t)E, (uint32_t)H);
+        w.gate = dense(p[1], (uint32_t)(E * I), (uint32_t)H);
+        w.up = dense(p[2], (uint32_t)(E * I), (uint32_t)H);
+        w.down = dense(p[3], (uint32_t)(E * H), (uint32_t)I);
+        w.shared_gate = dense(p[4], (uint32_t)S, (uint32_t)H);
+        w.shared_up = dense(p[5], (uint32_t)S, (uint32_t)H);
+        w.shared_down = dense(p[6], (uint32_t)H, (uint32_t)S);
+        w.shared_gate_weight = dense(p[7], 1, (uint32_t)H);
+    } else {
+        if (!cfg->bound)
+            return fail(diag, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "MoE provider weights are not bound to the config");
+        w = cfg->w;
+    }
+    return moe_run(c, cfg, w, x, tokens, y, err, nullptr, nullptr, nullptr, diag);
+}
+
+}  // namespace kqb

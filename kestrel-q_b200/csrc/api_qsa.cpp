@@ -15,6 +15,7 @@
 
 #include "kq_b200.h"
 #include "kq_qsa.h"
+#include "operators.hpp"
 #include "provider.hpp"
 #include "runtime.hpp"
 
@@ -684,39 +685,15 @@ static kq_status qsa_debug_run(DeviceContext *c, const kq_qsa_config *cfg, const
     return KQ_STATUS_OK;
 }
 
-static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w_in, const kq_qsa_weights_f32 *wf,
-                                  const float *hidden, uint64_t T, float *output, kq_qsa_state *state,
-                                  kq_qsa_selection_observer sel_obs, kq_qsa_checkpoint_observer ck_obs, void *user,
-                                  kq_diagnostic *diag) {
-    DeviceContext *c;
-    kq_status st = context(&c, diag);
-    if (st != KQ_STATUS_OK) return st;
-    std::lock_guard<std::recursive_mutex> lk(c->mu);
-    st = c->synchronize(diag);
-    if (st != KQ_STATUS_OK) return st;
+// F32 weight arrays (host: uploaded once and reused while their contents
+// stay the same; device: used in place, checked on the device) as the
+// operator's dense matrices.
+static kq_status resolve_f32(DeviceContext *c, const kq_qsa_config *cfg, const kq_qsa_weights_f32 *wf, ErrorWord err,
+                             QsaResolved *out, kq_diagnostic *diag) {
     const uint32_t H = cfg->dims.hidden_size;
-    const uint64_t n = T * H;
-    ErrorWord err = c->begin_call();
-    // host input and the output go through the context's staging arena (no
-    // allocation once it has grown to this call's size)
-    const bool x_host = !is_device_pointer(hidden);
-    void *stage;
-    st = c->staging(Carve::round(n * 4) + (x_host ? Carve::round(n * 4) : 0), &stage, diag);
-    if (st != KQ_STATUS_OK) return st;
-    Carve sc(stage);
-    float *dy = sc.take<float>(n);
-    const float *dx = hidden;
-    if (x_host) {
-        float *t = sc.take<float>(n);
-        KQB_CUDA(cudaMemcpyAsync(t, hidden, n * 4, cudaMemcpyHostToDevice, c->stream), diag, "input copy");
-        dx = t;
-    }
-    launch_check_finite(dx, n, err, c->stream);
-
-    QsaResolved w;
-    if (w_in) {
-        w = *w_in;
-    } else {
+    kq_status st = KQ_STATUS_OK;
+    QsaResolved &w = *out;
+    {
         const kq_qsa_dimensions &d = cfg->dims;
         const uint32_t qw = d.query_head_count * d.head_dimension, kvw = (uint32_t)cfg->kv_per_token;
         const float *ptrs[10] = {wf->query, wf->key, wf->value, wf->output, wf->query_norm, wf->key_norm,
@@ -756,15 +733,61 @@ static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w
         w.ik = dense(dev[7], d.index_head_dimension, H);
         w.iq_norm = dev[8];
         w.ik_norm = dev[9];
-    }
-    {
-        std::vector<float> norm(cfg->dims.index_head_dimension);
-        KQB_CUDA(cudaMemcpy(norm.data(), w.ik_norm, norm.size() * 4, cudaMemcpyDefault), diag, "norm read");
-        if (norm != state->bk_norm) {
-            state->bk_norm = norm;
-            state->bk_valid = 0;
         }
+    return st;
+}
+
+// The state's cached block keys were built with one index-key norm; another
+// norm invalidates them.
+static kq_status sync_block_key_norm(const kq_qsa_config *cfg, const QsaResolved &w, kq_qsa_state *state,
+                                     kq_diagnostic *diag) {
+    std::vector<float> norm(cfg->dims.index_head_dimension);
+    KQB_CUDA(cudaMemcpy(norm.data(), w.ik_norm, norm.size() * 4, cudaMemcpyDefault), diag, "norm read");
+    if (norm != state->bk_norm) {
+        state->bk_norm = norm;
+        state->bk_valid = 0;
     }
+    return KQ_STATUS_OK;
+}
+
+static kq_status qsa_execute_sync(const kq_qsa_config *cfg, const QsaResolved *w_in, const kq_qsa_weights_f32 *wf,
+                                  const float *hidden, uint64_t T, float *output, kq_qsa_state *state,
+                                  kq_qsa_selection_observer sel_obs, kq_qsa_checkpoint_observer ck_obs, void *user,
+                                  kq_diagnostic *diag) {
+    DeviceContext *c;
+    kq_status st = context(&c, diag);
+    if (st != KQ_STATUS_OK) return st;
+    std::lock_guard<std::recursive_mutex> lk(c->mu);
+    st = c->synchronize(diag);
+    if (st != KQ_STATUS_OK) return st;
+    const uint32_t H = cfg->dims.hidden_size;
+    const uint64_t n = T * H;
+    ErrorWord err = c->begin_call();
+    // host input and the output go through the context's staging arena (no
+    // allocation once it has grown to this call's size)
+    const bool x_host = !is_device_pointer(hidden);
+    void *stage;
+    st = c->staging(Carve::round(n * 4) + (x_host ? Carve::round(n * 4) : 0), &stage, diag);
+    if (st != KQ_STATUS_OK) return st;
+    Carve sc(stage);
+    float *dy = sc.take<float>(n);
+    const float *dx = hidden;
+    if (x_host) {
+        float *t = sc.take<float>(n);
+        KQB_CUDA(cudaMemcpyAsync(t, hidden, n * 4, cudaMemcpyHostToDevice, c->stream), diag, "input copy");
+        dx = t;
+    }
+    launch_check_finite(dx, n, err, c->stream);
+
+    QsaResolved w;
+    if (w_in) {
+        w = *w_in;
+    } else {
+        st = resolve_f32(c, cfg, wf, err, &w, diag);
+        if (st != KQ_STATUS_OK) return st;
+    }
+    st = sync_block_key_norm(cfg, w, state, diag);
+    if (st != KQ_STATUS_OK) return st;
     const uint64_t L0 = state->length;
     std::vector<SelectionCopy> sels;
     kq_qsa_state *states[1] = {state};
@@ -1271,3 +1294,64 @@ const char *kq_qsa_checkpoint_kind_name(kq_qsa_checkpoint_kind kind) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- layer bridge
+
+namespace kqb {
+
+kq_status qsa_layer_enqueue(DeviceContext *c, const kq_qsa_config *cfg, const kq_qsa_weights_f32 *wf,
+                            kq_qsa_state *const *states, uint32_t batch, uint32_t tokens, const float *x, float *y,
+                            ErrorWord err, kq_diagnostic *diag) {
+    if (!config_valid(cfg) || states == nullptr || batch == 0 || tokens == 0 || (batch > 1 && tokens > 1))
+        return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "valid compatible QSA call arguments are required");
+    if (cfg->dims.activation_dtype != KQ_QSA_ACTIVATION_F32)
+        return fail(diag, KQ_STATUS_INCOMPATIBLE_QSA, "scalar execution requires an F32 QSA reference config");
+    for (uint32_t b = 0; b < batch; ++b) {
+        if (!state_valid(states[b]) || states[b]->config != cfg)
+            return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "every state must belong to the config");
+        if (states[b]->length + tokens > states[b]->capacity)
+            return fail(diag, KQ_STATUS_LIMIT_EXCEEDED, "QSA sequence exceeds bounded state capacity or overflows");
+    }
+    QsaResolved w;
+    if (wf != nullptr) {
+        const kq_qsa_dimensions &d = cfg->dims;
+        const uint64_t qw = (uint64_t)d.query_head_count * d.head_dimension, H = d.hidden_size;
+        const float *ptrs[10] = {wf->query, wf->key, wf->value, wf->output, wf->query_norm, wf->key_norm,
+                                 wf->index_query, wf->index_key, wf->index_query_norm, wf->index_key_norm};
+        const uint64_t have[10] = {wf->query_count, wf->key_count, wf->value_count, wf->output_count,
+                                   wf->query_norm_count, wf->key_norm_count, wf->index_query_count,
+                                   wf->index_key_count, wf->index_query_norm_count, wf->index_key_norm_count};
+        const uint64_t want[10] = {2 * qw * H, cfg->kv_per_token * H, cfg->kv_per_token * H, H * qw,
+                                   d.head_dimension, d.head_dimension,
+                                   (uint64_t)d.index_query_head_count * d.index_head_dimension * H,
+                                   (uint64_t)d.index_head_dimension * H, d.index_head_dimension, d.index_head_dimension};
+        for (int i = 0; i < 10; ++i) {
+            if (have[i] != want[i]) return fail(diag, KQ_STATUS_DIMENSION_MISMATCH, "QSA F32 weight shape mismatch");
+            if (ptrs[i] == nullptr) return fail(diag, KQ_STATUS_INVALID_ARGUMENT, "QSA F32 weights are required");
+        }
+        kq_status st = resolve_f32(c, cfg, wf, err, &w, diag);
+        if (st != KQ_STATUS_OK) return st;
+        for (uint32_t b = 0; b < batch; ++b) {
+            st = sync_block_key_norm(cfg, w, states[b], diag);
+            if (st != KQ_STATUS_OK) return st;
+        }
+    } else {
+        if (!cfg->bound)
+            return fail(diag, KQ_STATUS_SEMANTIC_MAPPING_FAILED, "QSA provider matrix semantic is missing");
+        w = QsaResolved{cfg->q, cfg->k, cfg->v, cfg->o, cfg->iq, cfg->ik, cfg->q_norm, cfg->k_norm, cfg->iq_norm,
+                        cfg->ik_norm};
+    }
+    return qsa_enqueue(c, cfg, w, states, batch, tokens, x, y, err, nullptr, diag);
+}
+
+uint64_t qsa_state_committed_length(const kq_qsa_state *s) { return s->length; }
+
+void qsa_state_truncate(kq_qsa_state *s, uint64_t length) {
+    if (length < s->length) {
+        s->length = length;
+        s->bk_valid = std::min<uint64_t>(s->bk_valid, length / s->config->dims.block_size);
+    }
+    s->on_success();
+}
+
+}  // namespace kqb

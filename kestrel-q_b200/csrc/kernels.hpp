@@ -441,6 +441,37 @@ void launch_moe_dispatch(const MoeDims &d, uint32_t T, MoeBuffers &b, ErrorWord 
 void launch_moe_experts(const MoeDims &d, const MoeWeightsDev &w, const float *x, uint32_t ldx, uint32_t T,
                         MoeBuffers &b, ErrorWord err, cudaStream_t stream);
 
+// ---- layer gated residual (kernels_layer.cu)
+struct GrDims {
+    uint32_t hidden, branches, rank;
+    float eps;
+};
+
+// norm: device F32 [B*H] (1 + w form); down [rank x W], up [W x rank],
+// inject [B x W] (W = B*H), any projection type.
+struct GrWeightsDev {
+    const float *norm;
+    QMatrix down, up, inject;
+};
+
+// Work space of one read over T tokens (gr_carve); after launch_gr_read,
+// `normalized` and `read` hold every token's normalised branches and read
+// gates [T][W].
+struct GrBuffers {
+    float *normalized, *proj, *rank, *read;
+    float *ws_down, *ws_up;
+    size_t ws_down_floats, ws_up_floats;
+};
+
+size_t gr_workspace_bytes(const GrDims &d, uint32_t T);
+void gr_carve(const GrDims &d, uint32_t T, void *ws, GrBuffers &b);
+// Branches [T][B][H] -> mixed [T][H] and write gates [T][B].
+void launch_gr_read(const GrDims &d, const GrWeightsDev &w, const float *branches, uint32_t T, float *mixed,
+                    float *write_gate, GrBuffers &b, ErrorWord err, cudaStream_t stream);
+// out[t][b][h] = branches[t][b][h] + block[t][h] * write_gate[t][b]
+void launch_gr_write(const GrDims &d, const float *branches, const float *block, const float *write_gate, uint32_t T,
+                     float *out, ErrorWord err, cudaStream_t stream);
+
 uint64_t launches_total();
 bool force_simt_projection();
 void count_launch();
