@@ -89,7 +89,7 @@ class Provider:
 ROLE = {"a_log": 6, "conv": 7, "dt_bias": 8, "alpha": 9, "beta": 10, "qkv": 11, "gate": 12, "norm": 13,
         "out": 14, "k_norm": 15, "k": 16, "o": 17, "q_norm": 18, "q": 19, "v": 20, "index_qk": 21,
         "index_k_norm": 22, "index_q_norm": 23, "moe_router": 24, "routed_down": 25, "routed_gate_up": 26,
-        "shared_down": 27, "shared_gate": 28, "shared_up": 29, "shared_gate_weight": 30}
+        "shared_down": 27, "shared_gate": 28, "shared_up": 29, "shared_gate_weight": 30, "hc_norm": 2, "hc_down": 3, "hc_up": 4, "hc_inject": 5}
 
 
 class GdnLayer:
@@ -398,6 +398,154 @@ class MoeLayer:
         if self.handle:
             lib().kq_moe_config_close(self.handle)
             self.handle = C.c_void_p()
+
+
+class DecoderLayer:
+    """A decoder layer (kq_layer_test_config_create) over a GdnLayer or
+    QsaLayer mixer and a MoeLayer, optionally with provider gated-residual
+    tensors (kq_b200_layer_config_bind).  family: 1 GDN, 2 QSA."""
+
+    def __init__(self, family: int, hidden: int, branches: int, rank: int, eps: float, mixer, moe: MoeLayer,
+                 gr: dict | None = None, provider: Provider | None = None, layer: int = 0):
+        self.family, self.hidden, self.branches, self.rank = family, hidden, branches, rank
+        self.mixer, self.moe, self.provider = mixer, moe, provider
+        ld = abi.LayerDimensions(layer, hidden, branches, rank, eps, family)
+        self.handle = C.c_void_p()
+        d = abi.Diagnostic()
+        abi.check(lib().kq_layer_test_config_create(C.byref(ld), mixer.handle if family == 1 else None,
+                                                    mixer.handle if family == 2 else None, moe.handle, None, None,
+                                                    C.byref(self.handle), C.byref(d)), d)
+        if gr is not None:
+            p = provider
+            t = abi.LayerTensors()
+            for side, prefix in (("attn", "attention"), ("moe", "moe")):
+                g = gr[side]
+                setattr(t, f"{prefix}_norm", p.add_vector(f"l{layer}.{side}_gr.norm", ROLE["hc_norm"], g.norm))
+                setattr(t, f"{prefix}_down", p.add_matrix(f"l{layer}.{side}_gr.down", ROLE["hc_down"], g.down))
+                setattr(t, f"{prefix}_up", p.add_matrix(f"l{layer}.{side}_gr.up", ROLE["hc_up"], g.up))
+                setattr(t, f"{prefix}_inject", p.add_matrix(f"l{layer}.{side}_gr.inject", ROLE["hc_inject"], g.inject))
+            abi.check(lib().kq_b200_layer_config_bind(self.handle, p.handle, C.byref(t), C.byref(d)), d)
+
+    @property
+    def width(self) -> int:
+        return self.hidden * self.branches
+
+    def state(self, capacity: int = 0) -> "DecoderLayerState":
+        return DecoderLayerState(self, capacity)
+
+    def close(self):
+        if self.handle:
+            lib().kq_layer_config_close(self.handle)
+            self.handle = C.c_void_p()
+
+
+class DecoderLayerState:
+    def __init__(self, layer: DecoderLayer, capacity: int = 0):
+        self.layer = layer
+        self.handle = C.c_void_p()
+        d = abi.Diagnostic()
+        abi.check(lib().kq_layer_state_create(layer.handle, capacity, C.byref(self.handle), C.byref(d)), d)
+
+    @property
+    def position(self) -> int:
+        return lib().kq_layer_state_position(self.handle)
+
+    def rollback_last(self, tokens: int) -> int:
+        d = abi.Diagnostic()
+        return lib().kq_layer_state_rollback_last(self.handle, tokens, C.byref(d))
+
+    def _scratch(self, T: int, quantized: bool):
+        need = C.c_uint64()
+        d = abi.Diagnostic()
+        fn = lib().kq_layer_required_quantized_scratch_bytes if quantized else lib().kq_layer_required_scratch_bytes
+        abi.check(fn(self.layer.handle, self.handle, T, C.byref(need), C.byref(d)), d)
+        return np.zeros(need.value // 4 + 1, np.float32)
+
+    def _observer(self, checkpoints: bool):
+        cps = []
+
+        def on_cp(p, _u):
+            c = p.contents
+            cps.append((int(c.kind), int(c.token_index), int(c.rank),
+                        tuple(int(c.dimensions[i]) for i in range(c.rank)),
+                        np.ctypeslib.as_array(c.values, (c.value_count,)).copy()))
+
+        return cps, (abi.LAYER_CHECKPOINT_OBSERVER(on_cp) if checkpoints else abi.LAYER_CHECKPOINT_OBSERVER())
+
+    def run_f32(self, weights: dict, x: np.ndarray, mask: np.ndarray | None = None, checkpoints: bool = False):
+        """kq_layer_prefill_f32 with F32 arrays: weights = {"attn": {norm, down,
+        up, inject}, "moe_gr": {...}, "mixer": {fields}, "moe": {fields}}.
+        Returns (status, y, checkpoints, metrics, diagnostic)."""
+        L = self.layer
+        keep = []
+
+        def arr(a):
+            v = _f32(np.asarray(a).reshape(-1))
+            keep.append(v)
+            return v
+
+        lw = abi.LayerWeightsF32()
+        for side, dst in (("attn", lw.attention_gr), ("moe_gr", lw.moe_gr)):
+            for k in abi.GR_FIELDS:
+                v = arr(weights[side][k])
+                setattr(dst, k, v.ctypes.data)
+                setattr(dst, k + "_count", v.size)
+        fields = abi.GDN_WEIGHT_FIELDS if L.family == 1 else abi.QSA_WEIGHT_FIELDS
+        mw = abi.GdnWeightsF32() if L.family == 1 else abi.QsaWeightsF32()
+        for k in fields:
+            v = arr(weights["mixer"][k])
+            setattr(mw, k, v.ctypes.data)
+            setattr(mw, k + "_count", v.size)
+        ew = abi.MoeWeightsF32()
+        for k in abi.MOE_WEIGHT_FIELDS:
+            v = arr(weights["moe"][k])
+            setattr(ew, k, v.ctypes.data)
+            setattr(ew, k + "_count", v.size)
+        if L.family == 1:
+            lw.gdn = C.cast(C.pointer(mw), C.c_void_p)
+        else:
+            lw.qsa = C.cast(C.pointer(mw), C.c_void_p)
+        lw.moe = C.cast(C.pointer(ew), C.c_void_p)
+        xv = _f32(x).reshape(-1, L.width)
+        T = xv.shape[0]
+        y = np.zeros_like(xv)
+        scratch = self._scratch(T, False)
+        cps, cb = self._observer(checkpoints)
+        m = None if mask is None else np.ascontiguousarray(mask, np.uint8)
+        met = abi.LayerMetrics()
+        d = abi.Diagnostic()
+        st = lib().kq_layer_prefill_f32(L.handle, C.byref(lw), xv.ctypes.data, None, T,
+                                        None if m is None else m.ctypes.data, y.ctypes.data, y.size, self.handle,
+                                        scratch.ctypes.data, scratch.nbytes, cb, None, C.byref(met), C.byref(d))
+        return st, y, cps, met, d
+
+    def run_quantized(self, x: np.ndarray, mask: np.ndarray | None = None, checkpoints: bool = False):
+        """kq_layer_prefill_quantized_f32 (provider-bound config)."""
+        L = self.layer
+        xv = _f32(x).reshape(-1, L.width)
+        T = xv.shape[0]
+        y = np.zeros_like(xv)
+        scratch = self._scratch(T, True)
+        cps, cb = self._observer(checkpoints)
+        m = None if mask is None else np.ascontiguousarray(mask, np.uint8)
+        met = abi.LayerMetrics()
+        d = abi.Diagnostic()
+        st = lib().kq_layer_prefill_quantized_f32(L.handle, L.provider.handle, xv.ctypes.data, None, T,
+                                                  None if m is None else m.ctypes.data, y.ctypes.data, y.size,
+                                                  self.handle, scratch.ctypes.data, scratch.nbytes, cb, None,
+                                                  C.byref(met), C.byref(d))
+        return st, y, cps, met, d
+
+    def close(self):
+        if self.handle:
+            lib().kq_layer_state_close(self.handle)
+            self.handle = C.c_void_p()
+
+
+def layer_decode_batch(layer: DecoderLayer, states: Sequence[DecoderLayerState], x_ptr: int, y_ptr: int) -> None:
+    arr = (C.c_void_p * len(states))(*[s.handle.value for s in states])
+    d = abi.Diagnostic()
+    abi.check(lib().kq_b200_layer_decode_batch(layer.handle, arr, len(states), x_ptr, y_ptr, C.byref(d)), d)
 
 
 def moe_execute_async(layer: MoeLayer, x_ptr: int, tokens: int, y_ptr: int) -> None:

@@ -35,6 +35,8 @@ INVALID_GDN_STATE = 43
 INCOMPATIBLE_QSA = 44
 INVALID_QSA_STATE = 45
 INCOMPATIBLE_MOE = 46
+INCOMPATIBLE_LAYER = 50
+INVALID_LAYER_STATE = 51
 
 TYPE_F32, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_BF16 = 0, 8, 12, 14, 30
 
@@ -103,6 +105,35 @@ class MoeTensors(C.Structure):
     _fields_ = [(n, vp) for n in MOE_TENSOR_FIELDS]
 
 
+GR_FIELDS = ["norm", "down", "up", "inject"]
+LAYER_TENSOR_FIELDS = ["attention_inject", "attention_norm", "attention_down", "attention_up", "moe_inject",
+                       "moe_norm", "moe_down", "moe_up"]
+
+
+class LayerDimensions(C.Structure):   # include/kq_b200.h kq_layer_dimensions
+    _fields_ = [("layer_id", u32), ("hidden_size", u32), ("branch_count", u32), ("gr_rank", u32),
+                ("rms_epsilon", f32), ("family", C.c_int)]
+
+
+class LayerGrWeightsF32(C.Structure):   # include/kq_layer.h kq_layer_gr_weights_f32
+    _fields_ = _pair_fields(GR_FIELDS)
+
+
+class LayerWeightsF32(C.Structure):   # include/kq_layer.h kq_layer_weights_f32
+    _fields_ = [("attention_gr", LayerGrWeightsF32), ("moe_gr", LayerGrWeightsF32), ("gdn", vp), ("qsa", vp),
+                ("moe", vp), ("ple_value", vp), ("ple_provider", vp)]
+
+
+class LayerMetrics(C.Structure):   # include/kq_layer.h kq_layer_metrics
+    _fields_ = [(n, u64) for n in ["elapsed_nanoseconds", "tokens_processed", "scratch_bytes", "gr_workspace_bytes",
+                                   "transaction_staging_bytes", "qsa_selection_events", "qsa_candidate_blocks",
+                                   "qsa_selected_blocks", "qsa_selected_tokens"]]
+
+
+class LayerTensors(C.Structure):
+    _fields_ = [(n, vp) for n in LAYER_TENSOR_FIELDS]
+
+
 class GdnTensors(C.Structure):
     _fields_ = [(n, vp) for n in GDN_WEIGHT_FIELDS]
 
@@ -159,6 +190,12 @@ EXCHANGE_FN = C.CFUNCTYPE(C.c_int, vp, u64, vp, vp)
 SELECTION_OBSERVER = C.CFUNCTYPE(None, C.POINTER(QsaSelection), vp)
 GDN_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(GdnCheckpoint), vp)
 QSA_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(QsaCheckpoint), vp)
+class LayerCheckpoint(C.Structure):   # include/kq_layer.h kq_layer_checkpoint
+    _fields_ = [("kind", C.c_int), ("token_index", u64), ("rank", u32), ("dimensions", u64 * 3),
+                ("values", C.POINTER(f32)), ("value_count", u64)]
+
+
+LAYER_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(LayerCheckpoint), vp)
 MOE_ROUTE_OBSERVER = C.CFUNCTYPE(None, C.POINTER(MoeRoute), vp)
 MOE_CHECKPOINT_OBSERVER = C.CFUNCTYPE(None, C.POINTER(MoeCheckpoint), vp)
 
@@ -284,6 +321,34 @@ _SIGNATURES = {
                                            MOE_CHECKPOINT_OBSERVER, vp, vp]),
     "kq_b200_moe_execute_async": (C.c_int, [vp, vp, u64, vp, vp]),
     "kq_moe_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
+    "kq_layer_test_config_create": (C.c_int, [C.POINTER(LayerDimensions), vp, vp, vp, vp, vp, C.POINTER(vp), vp]),
+    "kq_layer_config_create": (C.c_int, [vp, u32, C.POINTER(vp), vp]),
+    "kq_layer_config_close": (None, [vp]),
+    "kq_layer_config_family": (C.c_int, [vp]),
+    "kq_layer_config_gr_workspace_bytes": (u64, [vp]),
+    "kq_layer_config_persistent_semantic_bytes": (u64, [vp, u64]),
+    "kq_layer_config_owned_bytes": (u64, [vp]),
+    "kq_b200_layer_config_bind": (C.c_int, [vp, vp, C.POINTER(LayerTensors), vp]),
+    "kq_layer_state_create": (C.c_int, [vp, u64, C.POINTER(vp), vp]),
+    "kq_layer_state_close": (None, [vp]),
+    "kq_layer_state_reset": (C.c_int, [vp, vp]),
+    "kq_layer_state_position": (u64, [vp]),
+    "kq_layer_state_owned_bytes": (u64, [vp]),
+    "kq_layer_state_rollback_last": (C.c_int, [vp, u64, vp]),
+    "kq_layer_required_scratch_bytes": (C.c_int, [vp, vp, u64, C.POINTER(u64), vp]),
+    "kq_layer_required_quantized_scratch_bytes": (C.c_int, [vp, vp, u64, C.POINTER(u64), vp]),
+    "kq_layer_prefill_f32": (C.c_int, [vp, C.POINTER(LayerWeightsF32), vp, vp, u64, vp, vp, u64, vp, vp, u64,
+                                       LAYER_CHECKPOINT_OBSERVER, vp, vp, vp]),
+    "kq_layer_decode_f32": (C.c_int, [vp, C.POINTER(LayerWeightsF32), vp, u32, vp, u64, vp, vp, u64,
+                                      LAYER_CHECKPOINT_OBSERVER, vp, vp, vp]),
+    "kq_layer_prefill_quantized_f32": (C.c_int, [vp, vp, vp, vp, u64, vp, vp, u64, vp, vp, u64,
+                                                 LAYER_CHECKPOINT_OBSERVER, vp, vp, vp]),
+    "kq_layer_decode_quantized_f32": (C.c_int, [vp, vp, vp, u32, vp, u64, vp, vp, u64, LAYER_CHECKPOINT_OBSERVER,
+                                                vp, vp, vp]),
+    "kq_b200_layer_decode_batch": (C.c_int, [vp, C.POINTER(vp), u32, vp, vp, vp]),
+    "kq_b200_layer_prefill_async": (C.c_int, [vp, vp, vp, u64, vp, vp]),
+    "kq_layer_family_name": (C.c_char_p, [C.c_int]),
+    "kq_layer_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
     "kq_gdn_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
     "kq_qsa_checkpoint_kind_name": (C.c_char_p, [C.c_int]),
 }

@@ -293,5 +293,25 @@ def moe_layer(seed: int, dims: MoeDims, gate_up_type: int = TYPE_Q4_K, down_type
     )
 
 
+# ----------------------------------------------------------------- layer
+
+@dataclass
+class GrWeights:
+    """One gated residual over B branches of width H (W = B*H)."""
+    norm: np.ndarray    # [W] F32, (1 + w) form
+    down: QTensor       # [rank][W]
+    up: QTensor         # [W][rank]
+    inject: QTensor     # [B][W]
+
+
+def gr_weights(seed: int, hidden: int, branches: int, rank: int, type_id: int = TYPE_BF16) -> GrWeights:
+    """Gated-residual tensors: norm deltas ~ N(0, 0.05), projections
+    ~ N(0, 0.02) in `type_id`."""
+    rng = np.random.default_rng(seed)
+    W = hidden * branches
+    return GrWeights(norm=rng.normal(0.0, 0.05, W).astype(np.float32), down=pack(type_id, rng, rank, W),
+                     up=pack(type_id, rng, W, rank), inject=pack(type_id, rng, branches, W))
+
+
 def hidden(seed: int, rows: int, width: int) -> np.ndarray:
     return np.random.default_rng(seed).normal(0.0, 1.0, (rows, width)).astype(np.float32)

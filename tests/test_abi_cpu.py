@@ -252,3 +252,56 @@ def test_moe_entry_points_validate_before_any_device_work(kq):
     finally:
         lib.kq_moe_config_close(cfg)
         lib.kq_moe_config_close(bf)
+
+
+def test_layer_config_matches_reference_accounting(kq, oracle):
+    """kq_layer_test_config_create checks and sizes against the compiled
+    reference (src/kq_layer.c:220-262,294-318): the gated-residual workspace
+    and persistent-state bytes of the reference's reduced fixture, argument
+    and geometry failures, and the PLE_GDN family refused."""
+    import ctypes as Cx
+    lib, abi = kq.lib(), kq.abi
+    d = abi.Diagnostic()
+    gdn, moe, lay = Cx.c_void_p(), Cx.c_void_p(), Cx.c_void_p()
+    assert lib.kq_gdn_test_config_create(Cx.byref(abi.GdnDimensions(8, 2, 4, 4, 4, 4, 1e-6, 0)), Cx.byref(gdn),
+                                         Cx.byref(d)) == 0
+    assert lib.kq_moe_test_config_create(Cx.byref(abi.MoeDimensions(8, 4, 2, 4, 4, 0)), Cx.byref(moe),
+                                         Cx.byref(d)) == 0
+    try:
+        ld = abi.LayerDimensions(0, 8, 4, 4, 1e-6, 1)
+        assert lib.kq_layer_test_config_create(Cx.byref(ld), gdn, None, moe, None, None, Cx.byref(lay),
+                                               Cx.byref(d)) == 0
+        mine = (lib.kq_layer_config_gr_workspace_bytes(lay), lib.kq_layer_config_persistent_semantic_bytes(lay, 16))
+        assert lib.kq_layer_config_family(lay) == 1
+        lib.kq_layer_config_close(lay)
+        if oracle.ref_available():
+            L = oracle.ref()
+            rg, rm, rl = Cx.c_void_p(), Cx.c_void_p(), Cx.c_void_p()
+            assert L.kq_gdn_test_config_create(Cx.byref(oracle._RefGdnDims(8, 2, 4, 4, 4, 4, 1e-6, 0)),
+                                               Cx.byref(rg), Cx.byref(d)) == 0
+            assert L.kq_moe_test_config_create(Cx.byref(oracle._RefMoeDims(8, 4, 2, 4, 4, 0)), Cx.byref(rm),
+                                               Cx.byref(d)) == 0
+            assert L.kq_layer_test_config_create(Cx.byref(oracle._RefLayerDims(0, 8, 4, 4, 1e-6, 1)), rg, None, rm,
+                                                 None, None, Cx.byref(rl), Cx.byref(d)) == 0
+            L.kq_layer_config_gr_workspace_bytes.restype = Cx.c_uint64
+            L.kq_layer_config_persistent_semantic_bytes.restype = Cx.c_uint64
+            ref = (L.kq_layer_config_gr_workspace_bytes(rl),
+                   L.kq_layer_config_persistent_semantic_bytes(rl, Cx.c_uint64(16)))
+            L.kq_layer_config_close(rl)
+            L.kq_moe_config_close(rm)
+            L.kq_gdn_config_close(rg)
+            assert mine == ref
+        bad = abi.LayerDimensions(0, 0, 4, 4, 1e-6, 1)
+        assert lib.kq_layer_test_config_create(Cx.byref(bad), gdn, None, moe, None, None, Cx.byref(lay),
+                                               Cx.byref(d)) == abi.INVALID_ARGUMENT
+        wrong = abi.LayerDimensions(0, 16, 4, 4, 1e-6, 1)   # sub-configs of hidden 8
+        assert lib.kq_layer_test_config_create(Cx.byref(wrong), gdn, None, moe, None, None, Cx.byref(lay),
+                                               Cx.byref(d)) == abi.INCOMPATIBLE_LAYER
+        ple = abi.LayerDimensions(1, 8, 4, 4, 1e-6, 3)
+        assert lib.kq_layer_test_config_create(Cx.byref(ple), gdn, None, moe, None, None, Cx.byref(lay),
+                                               Cx.byref(d)) == abi.INCOMPATIBLE_LAYER
+        assert lib.kq_layer_config_create(None, 0, Cx.byref(lay), Cx.byref(d)) == abi.UNSUPPORTED_MODEL
+        assert lib.kq_layer_family_name(3) == b"PLE_GDN"
+    finally:
+        lib.kq_moe_config_close(moe)
+        lib.kq_gdn_config_close(gdn)
