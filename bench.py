@@ -23,6 +23,8 @@ prefill ones):
                         index BF16) on 131072 tokens
   moe_decode            the routed-expert MoE layer (512 experts, top-10,
                         shared expert) on a batch of 64 decode tokens
+  layer_decode          one target GDN decoder layer (gated residuals, GDN,
+                        MoE) decoding one token of each of 64 sequences
 Every prefill runs tensor-parallel over the run's ranks (GDN by value-head
 group, QSA by query-head group or by token within a KV-head group, the
 indexer's selections exchanged once per layer call) with one NCCL
@@ -53,6 +55,7 @@ from __future__ import annotations
 
 import argparse
 import concurrent.futures as cf
+import functools
 import json
 import os
 import statistics
@@ -380,6 +383,7 @@ MOE_POOL = 16   # distinct input batches cycled through the timed steps
 MOE_CPU_TOKENS = 8
 
 
+@functools.lru_cache(maxsize=1)
 def moe_weights():
     """The target MoE layer (512 experts, top-10, hidden 2560, routed and
     shared intermediate 640): gate/up Q4_K, down and shared Q8_0, router and
@@ -559,6 +563,173 @@ def moe_record(args, cx: Ctx, cpu: bool):
         prov.close()
 
 
+# ---------------------------------------------------------------- layer
+
+LAYER_BRANCHES, LAYER_RANK = 4, 320
+LAYER_CPU_TOKENS = 4
+
+
+def decoder_layer_weights():
+    """One target GDN decoder layer: GDN at the target model's geometry
+    (hidden 2560, 16 x 128 key / 48 x 128 value heads; projections typed as
+    in config 3: in Q4_K, out Q6_K, alpha/beta Q4_K), the target MoE
+    (moe_weights) and gated residuals over 4 branches of rank 320 (BF16)."""
+    from kqb200 import synth
+    gd = synth.GdnDims(hidden=2560, key_heads=16, value_heads=48, key_dim=128, value_dim=128)
+    gw = synth.gdn_layer(31, gd, synth.TYPE_Q4_K, synth.TYPE_Q6_K, synth.TYPE_Q4_K)
+    gr = {"attn": synth.gr_weights(32, gd.hidden, LAYER_BRANCHES, LAYER_RANK),
+          "moe": synth.gr_weights(33, gd.hidden, LAYER_BRANCHES, LAYER_RANK)}
+    return gd, gw, gr
+
+
+def cpu_layer_record(tokens: int = LAYER_CPU_TOKENS):
+    """The reference's own operators for one decode token of the layer, per
+    token: kq_layer_gr_read_f32, the GDN decode (kq_gdn_prefill_f32 on one
+    token), kq_layer_gr_write_f32, the MoE gated residual, kq_moe_route_f32
+    with kq_moe_execute_routed_expert_f32 for the selected and the shared
+    expert, and the final write (F32 weights, dequantised outside the timed
+    spans).  One token per thread."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return {"unavailable": "reference library not built"}
+    gd, gw, gr = decoder_layer_weights()
+    mw = moe_weights()
+    md = mw.dims
+    H, I, S = md.hidden, md.routed, md.shared
+    gwf = O.gdn_weights_f32(gw)
+
+    def deq(t):
+        return O.dequantize(t.type_id, t.data).reshape(-1)
+
+    grf = {k: {"norm": g.norm, "down": deq(g.down), "up": deq(g.up), "inject": deq(g.inject)} for k, g in gr.items()}
+    router = np.ascontiguousarray(mw.router.data.view(np.float32).reshape(md.experts, H))
+    shared = (deq(mw.shared_gate).reshape(S, H), deq(mw.shared_up).reshape(S, H), deq(mw.shared_down).reshape(H, S))
+
+    def rows(t, e, n):
+        rb = t.row_bytes
+        return O.dequantize(t.type_id, t.data[e * n * rb:(e + 1) * n * rb]).reshape(n, -1)
+
+    def one(i):
+        rng = np.random.default_rng(900 + i)
+        x = rng.normal(0, 1, LAYER_BRANCHES * H).astype(np.float32)
+        conv = rng.normal(0, 1, gd.conv_channels * 4).astype(np.float32)
+        rec = (rng.normal(0, 0.02, gd.value_heads * gd.key_dim * gd.value_dim)).astype(np.float32)
+        gr_ref, moe_ref = O.RefLayerGr(H, LAYER_BRANCHES, LAYER_RANK), O.RefMoe(md)
+        try:
+            spent = 0.0
+            t0 = time.perf_counter()
+            mixed, awg = gr_ref.read(grf["attn"], x)
+            st, block, _, _ = O.gdn_run(gd, gwf, mixed, conv, rec, impl="reference")
+            assert st == 0
+            after = gr_ref.write(x, block, awg)
+            moe_in, mwg = gr_ref.read(grf["moe"], after)
+            ids, wt = moe_ref.route(router, moe_in)
+            spent += time.perf_counter() - t0
+            y = np.zeros(H, np.float32)
+            for p in sorted(range(md.top_k), key=lambda q: ids[q]):
+                e = int(ids[p])
+                g, u, dn = rows(mw.gate, e, I), rows(mw.up, e, I), rows(mw.down, e, H)
+                t0 = time.perf_counter()
+                y = y + moe_ref.expert(g, u, dn, moe_in) * wt[p]
+                spent += time.perf_counter() - t0
+            t0 = time.perf_counter()
+            moe_ref.expert(*shared, moe_in)
+            gr_ref.write(after, y, mwg)
+            spent += time.perf_counter() - t0
+            return spent
+        finally:
+            gr_ref.close()
+            moe_ref.close()
+
+    threads = min(cpu_threads(), tokens)
+    spans = [0.0] * threads
+    with cf.ThreadPoolExecutor(max_workers=threads) as pool:
+        for i, t in enumerate(pool.map(one, range(tokens))):
+            spans[i % threads] += t
+    return {"value": tokens / max(spans), "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{tokens} decode tokens of the target GDN layer, one per thread: the reference's gated "
+                      f"residual, GDN and MoE operators (F32 weights, dequantised outside the timed spans)"}
+
+
+def layer_record(args, cx: Ctx, cpu: bool):
+    """One target GDN decoder layer (gated residual, GDN, gated residual,
+    MoE) decoding one token for each of 64 sequences per step through
+    kq_b200_layer_decode_batch; the inputs cycle through 16 seeded batches.
+    Bound: HBM (the step's weights, the selected experts' weights, the GDN
+    states)."""
+    torch, kqb200 = cx.torch, cx.kq
+    gd, gw, gr = decoder_layer_weights()
+    mw = moe_weights()
+    B, W = MOE_BATCH, LAYER_BRANCHES * gd.hidden
+    prov = kqb200.Provider(cx.local_rank)
+    mixer = kqb200.GdnLayer(gd, gw, prov, layer=0)
+    moe = kqb200.MoeLayer(mw.dims, mw, prov, layer=0)
+    layer = kqb200.DecoderLayer(1, gd.hidden, LAYER_BRANCHES, LAYER_RANK, 1e-6, mixer, moe, gr, prov)
+    states = [layer.state() for _ in range(B)]
+    try:
+        # the states start from zero: a decode step's work does not depend on them
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(4321 + cx.rank)
+        xs = [torch.randn(B, W, device="cuda", generator=gen) for _ in range(MOE_POOL)]
+        y = torch.empty(B, W, device="cuda")
+        torch.cuda.synchronize()
+        it = [0]
+
+        def step():
+            kqb200.layer_decode_batch(layer, states, xs[it[0] % MOE_POOL].data_ptr(), y.data_ptr())
+            it[0] += 1
+
+        with torch.cuda.stream(cx.stream):
+            for _ in range(args.warmup):
+                step()
+        cx.sync()
+        steps = args.moe_steps
+        launches0 = cx.lib.kq_b200_kernel_launch_count()
+        with ClockSampler(cx.local_rank) as clocks:
+            ms = cx.timed(steps, step)
+        launches = cx.lib.kq_b200_kernel_launch_count() - launches0
+        assert torch.isfinite(y).all(), "non-finite layer output"
+        xh = torch.randn(B, W, generator=torch.Generator().manual_seed(6)).pin_memory()
+        yh = torch.empty(B, W).pin_memory()
+
+        def e2e_step():
+            xs[0].copy_(xh, non_blocking=True)
+            kqb200.layer_decode_batch(layer, states, xs[0].data_ptr(), y.data_ptr())
+            yh.copy_(y, non_blocking=True)
+
+        e2e_ms = cx.timed(max(3, steps // 4), e2e_step)
+        ms, e2e_ms = max_over_ranks([ms, e2e_ms], cx.world, cx.device)
+        hbm, peak_kind = peaks()
+        xhost = [x.cpu().numpy() for x in xs[:4]]
+        moe_bytes = float(np.mean([moe_step_bytes(mw, x[:, :gd.hidden])[0] for x in xhost]))
+        gdn_w = sum(t.nbytes for t in (gw.qkv, gw.gate, gw.beta, gw.alpha, gw.output))
+        gdn_state = B * 2 * 4 * (gd.value_heads * gd.key_dim * gd.value_dim + gd.conv_channels * 4)
+        gr_bytes = 2 * sum(t.nbytes for t in (gr["attn"].down, gr["attn"].up, gr["attn"].inject))
+        step_bytes = moe_bytes + gdn_w + gdn_state + gr_bytes + 2 * B * W * 4
+        rec = {
+            "workload": "target GDN decoder layer decode, 64 sequences/GPU: gated residual (4 branches, rank 320, "
+                        "BF16), GDN (hidden 2560, 16x128 key / 48x128 value heads, Q4_K in / Q6_K out), gated "
+                        "residual, MoE (512 experts top-10 + shared, Q4_K / Q8_0)",
+            "value": job_tokens_per_s(cx.world, B, ms), "unit": "tok/s", "ms_per_step": ms, "steps": steps,
+            "step_algorithmic_bytes": step_bytes,
+            "step_hbm_frac": step_bytes / (ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind,
+            "e2e": {"value": job_tokens_per_s(cx.world, B, e2e_ms), "unit": "tok/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": B * W * 4, "d2h_bytes_per_step": B * W * 4},
+            "gpu_launches": int(launches),
+            "clocks": clocks.summary(),
+        }
+        if cpu and cx.rank == 0:
+            rec["cpu_baseline"] = cpu_layer_record()
+        return rec
+    finally:
+        for s in states:
+            s.close()
+        layer.close()
+        moe.close()
+        mixer.close()
+        prov.close()
+
+
 def run_reference(args, rank, world):
     """The reference arm: rank 0 alone times the reference's CPU operators on
     every host core it may use; other ranks exit at once."""
@@ -598,6 +769,7 @@ def run_reference(args, rank, world):
         line["prefill_131k"] = {"impl": "reference", "cpu_baseline": cpu_prefill_record("block")}
     if not args.no_moe:
         line["moe_decode"] = {"impl": "reference", "cpu_baseline": cpu_moe_record()}
+        line["layer_decode"] = {"impl": "reference", "cpu_baseline": cpu_layer_record()}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -1150,6 +1322,7 @@ def run_b200(args, rank, world, local_rank):
             line["decode_b1"] = decode_b1_record(args, cx, cpu)
         if not args.no_moe:
             line["moe_decode"] = moe_record(args, cx, cpu)
+            line["layer_decode"] = layer_record(args, cx, cpu)
         if not args.no_prefill:
             ps, pw = args.prefill_steps, args.prefill_warmup
             line["prefill_8k"] = {k: prefill_record(args, cx, k, 8192, ps, pw, cpu) for k in ("gdn_layer", "block")}

@@ -909,3 +909,58 @@ def layer_sequence(impl: str, ld, gr: dict, mixer_dims, mixer_w: dict, moe_dims,
             L.kq_gdn_config_close(sub)
         else:
             L.kq_qsa_config_close(sub)
+
+
+class RefLayerGr:
+    """The reference's gated-residual read and write
+    (kq_layer_gr_read_f32 / kq_layer_gr_write_f32, src/kq_layer_qwen38.c:
+    166-209) on a reference test layer config of the given geometry (GDN
+    family; the sub-configs only carry the hidden size).  Used as part of the
+    CPU baseline of the layer decode record."""
+
+    def __init__(self, hidden: int, branches: int, rank: int, eps: float = 1e-6):
+        L = ref()
+        self.L, self.H, self.B, self.R = L, hidden, branches, rank
+        d = _Diag()
+        self.g, self.m, self.cfg = vp(), vp(), vp()
+        if L.kq_gdn_test_config_create(C.byref(_RefGdnDims(hidden, 1, 1, 4, 4, 4, 1e-6, 0)), C.byref(self.g),
+                                       C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        if L.kq_moe_test_config_create(C.byref(_RefMoeDims(hidden, 1, 1, 1, 1, 0)), C.byref(self.m), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        if L.kq_layer_test_config_create(C.byref(_RefLayerDims(0, hidden, branches, rank, eps, 1)), self.g, None,
+                                         self.m, None, None, C.byref(self.cfg), C.byref(d)) != 0:
+            raise RuntimeError(d.message)
+        W = hidden * branches
+        self.nm, self.rg = np.empty(W, np.float32), np.empty(W, np.float32)
+        self.rank = np.empty(rank, np.float32)
+        L.kq_layer_gr_write_f32.restype = None
+
+    def read(self, w: dict, branches: np.ndarray):
+        """(mixed [H], write gate [B]) of one token's branches [B*H]."""
+        gw = _RefGrWeights()
+        ws = {k: _a(w[k]).reshape(-1) for k in GR_FIELDS}
+        for k in GR_FIELDS:
+            setattr(gw, k, ws[k].ctypes.data)
+            setattr(gw, k + "_count", ws[k].size)
+        x = _a(branches).reshape(-1)
+        mixed, wg = np.empty(self.H, np.float32), np.empty(self.B, np.float32)
+        d = _Diag()
+        st = self.L.kq_layer_gr_read_f32(self.cfg, C.byref(gw), x.ctypes.data_as(vp), self.nm.ctypes.data_as(vp),
+                                         self.rg.ctypes.data_as(vp), mixed.ctypes.data_as(vp),
+                                         self.rank.ctypes.data_as(vp), wg.ctypes.data_as(vp), C.byref(d))
+        if st != 0:
+            raise RuntimeError(d.message)
+        return mixed, wg
+
+    def write(self, branches: np.ndarray, block: np.ndarray, wg: np.ndarray) -> np.ndarray:
+        x, b, g = _a(branches).reshape(-1), _a(block).reshape(-1), _a(wg).reshape(-1)
+        out = np.empty_like(x)
+        self.L.kq_layer_gr_write_f32(self.cfg, x.ctypes.data_as(vp), b.ctypes.data_as(vp), g.ctypes.data_as(vp),
+                                     out.ctypes.data_as(vp))
+        return out
+
+    def close(self):
+        self.L.kq_layer_config_close(self.cfg)
+        self.L.kq_moe_config_close(self.m)
+        self.L.kq_gdn_config_close(self.g)
