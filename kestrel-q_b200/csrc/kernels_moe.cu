@@ -14,11 +14,12 @@
 //             renormalised weights; ranks each pick within its expert
 //   dispatch  one CTA: per-expert offsets, the list of active experts, the
 //             slot of every pick (slots are expert-major)
-//   gate_up   one CTA per (active expert, 64 intermediate rows): gate and up
-//             rows decoded once per group of up to 8 of the expert's tokens,
-//             SwiGLU in the epilogue -> act[slot][I]
-//   down      one CTA per (active expert, 64 hidden rows), four lanes per
-//             row -> eout[slot][H]
+//   gate_up   grouped gate and up GEMV of the active experts, SwiGLU in the
+//             epilogue -> act[slot][I]; Q4_K: persistent streamed kernel on
+//             the tensor cores (every selected expert's rows cross HBM once
+//             per call)
+//   down      grouped down GEMV -> eout[slot][H]; planar Q8_0: streamed, on
+//             the tensor cores
 //   combine   one CTA per token: the selected experts' weighted outputs
 //             summed in ascending expert id (the reference's accumulation
 //             order), plus the shared expert scaled by sigmoid(logit)
@@ -28,6 +29,8 @@
 // kernel decide) does not change any value.
 #include "kernels.hpp"
 #include "quant.cuh"
+
+#include <cuda_fp16.h>
 
 #include <cmath>
 
@@ -408,26 +411,54 @@ moe_down_kernel(MoeDims d, QMatrix down, const float *__restrict__ act, const ui
     }
 }
 
-// ------------------------------------------------- staged (bulk-copy) paths
+// ------------------------------------------------ streamed (persistent) paths
 //
-// Q4_K gate/up and planar Q8_0 down: a CTA copies its whole row block into
-// shared memory with one bulk copy per row (HBM -> SMEM, mbarrier
-// completion), then, per group of the expert's tokens, copies their
-// activation rows into shared memory and decodes the block against them, so
-// the block crosses HBM once whatever the token count.  Two (gate/up) or
-// three (down) CTAs per SM keep the next blocks' copies in flight while one
-// decodes.  Lane = sub * 8 + unit: the eight lanes of a shared-memory phase
-// read the same activation words (a broadcast) and eight different rows,
-// whose pitch is chosen so that they fall in distinct banks.  Codes become
-// floats without a conversion instruction: a code byte placed in the
-// mantissa of 2^23 (PRMT) minus 2^23 (one FADD) is the exact integer.
+// Q4_K gate/up and planar Q8_0 down.  One CTA per SM walks a contiguous
+// range of tiles (tile = one active expert's block of rows; an expert's
+// tiles are consecutive, so a CTA changes experts a few times per launch).
+// Tiles stream HBM -> shared memory through a ring of stages (bulk copies,
+// mbarrier completion); thread 0 refills a stage as soon as the CTA has read
+// it, so ring - 1 tiles are in flight while one is decoded.  The activations
+// of the expert's tokens stay in registers (as tensor-core B fragments) for
+// every tile of the expert: shared memory carries the weights only.
+//
+// The products run on the tensor cores (mma.sync m16n8k16, f16 operands,
+// F32 accumulation) with both operands built in registers:
+//   A (16 rows x 16 columns of codes): each code becomes an exact fp16 by
+//     OR-ing it into the mantissa of 1024 (Q4_K nibbles moved to mantissa
+//     bits 6..9: 1024 + 64 q, one SHF + LOP3 per pair; sign-flipped Q8_0
+//     bytes in the low mantissa byte: 1152 + c, one PRMT per pair).  The
+//     offset is removed per sub-block with the sum of the activations, which
+//     the same MMA computes against an all-ones A.
+//   B (16 columns x 8 MMA columns): column 2t holds the high fp16 part of
+//     token t's activations, column 2t + 1 the low part (x' - hi rounded to
+//     fp16): hi + lo carries about 22 bits of x' = x * 2^k, k chosen per
+//     (warp, token) so that max |x'| lies in [2^14, 2^15).  Four tokens per
+//     pass.
+// Every fp16 product is exact in F32; the error is the split (2^-22 of |x'|)
+// and the F32 accumulation.  The K order inside a 16-column step is a
+// permutation applied to A and B alike; it does not change the sum.
+//
+// A warp owns a fixed column range (Q4_K: one super-block of the tile's gate
+// or up rows; Q8_0: one or two 32-code blocks of every row) and walks its
+// rows in blocks of 16; lane (g = lane / 4, q = lane % 4) holds rows g and
+// g + 8 of a block and token q's two accumulator columns.  Per-warp partial
+// sums meet in shared memory, where one thread per output finishes the sum.
 
-constexpr uint32_t kGuRows = 32;     // gate rows (and as many up rows) per CTA
-constexpr uint32_t kGuGroup = 2;     // tokens per pass (activation rows staged)
-constexpr uint32_t kDnRows = 64;     // down rows per CTA
-constexpr uint32_t kDnGroup = 8;
-constexpr uint32_t kMaxStageBytes = 112u * 1024u;
+constexpr uint32_t kStreamThreads = 640;
+constexpr uint32_t kStreamRing = 4;
+constexpr uint32_t kGuTile = 16;      // gate rows (and as many up rows) per tile
+constexpr uint32_t kDnTile = 64;      // down rows per tile
+// The dynamic shared memory the streamed kernels may ask for: the 227 KB
+// per-block opt-in less the static part and the 1 KB reserved per CTA.
+constexpr uint32_t kStreamSmemLimit = 224u * 1024u;
 constexpr uint32_t kStageWaitPolls = 1u << 26;
+constexpr uint32_t kMmaWarps = kStreamThreads / 32u;
+constexpr uint32_t kGuSbMax = kMmaWarps / 2u;   // super-blocks per row the gate/up warps cover
+constexpr uint32_t kMmaTokens = 4;              // tokens per pass
+constexpr uint32_t kDnMaxBpw = 2;               // Q8_0 blocks per down warp
+constexpr uint32_t kH1024 = 0x64006400u;        // fp16 pair (1024, 1024)
+constexpr uint32_t kHOnes = 0x3C003C00u;        // fp16 pair (1, 1)
 
 __device__ __forceinline__ uint32_t moe_smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -437,231 +468,517 @@ __device__ __forceinline__ void moe_bulk(void *dst, const void *src, uint32_t by
                  : "memory");
 }
 
-// Bounded wait for phase 0 of `bar`; false when it gave up.
-__device__ __forceinline__ bool moe_bar_wait(uint64_t *bar) {
+__device__ __forceinline__ void moe_expect(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(moe_smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+// Bounded wait for the phase of `bar` with the given parity; false when it
+// gave up.
+__device__ __forceinline__ bool moe_bar_wait(uint64_t *bar, uint32_t parity) {
     const uint32_t a = moe_smem_u32(bar);
     for (uint32_t i = 0; i < kStageWaitPolls; ++i) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
             "selp.b32 %0, 1, 0, p;\n\t}"
             : "=r"(done)
-            : "r"(a)
+            : "r"(a), "r"(parity)
             : "memory");
         if (done) return true;
     }
     return false;
 }
 
-// Byte k of `v` as the float value of that byte (0..255).
-__device__ __forceinline__ float byte_float(uint32_t v, int k) {
-    return __int_as_float(__byte_perm(v, 0x4B000000u, (uint32_t)k | 0x7540u)) - 8388608.0f;
+// The CTA's share [begin, end) of `total` tiles.
+__device__ __forceinline__ void tile_range(uint64_t total, uint32_t &begin, uint32_t &end) {
+    begin = (uint32_t)(total * blockIdx.x / gridDim.x);
+    end = (uint32_t)(total * (blockIdx.x + 1) / gridDim.x);
 }
 
-// Copies `rows` rows of `row_bytes` from `src` (pitch row_bytes) to `dst`
-// (pitch `dst_pitch`), and as many from `src2` to `dst2` when given, then
-// waits for them; every thread returns the same verdict.
-__device__ __forceinline__ bool stage_rows(uint8_t *dst, const uint8_t *src, uint32_t rows, uint32_t row_bytes,
-                                           uint32_t dst_pitch, const uint8_t *src2, uint8_t *dst2, uint64_t *bar,
-                                           int *ok, const ErrorWord &err) {
+// A cursor over the CTA's tiles: tile (a, j) (active expert a, row block j)
+// sits in ring slot `slot`, and its copies complete the phase of that slot's
+// barrier with parity `phase`.  It advances without division.
+struct TileCursor {
+    uint32_t a, j, slot, phase;
+
+    __device__ __forceinline__ void start(uint32_t tau, uint32_t J) { a = tau / J, j = tau % J, slot = 0, phase = 0; }
+    __device__ __forceinline__ void next(uint32_t J, uint32_t ring) {
+        if (++j == J) j = 0, ++a;
+        if (++slot == ring) slot = 0, phase ^= 1u;
+    }
+};
+
+struct StreamRing {
+    uint64_t *full;
+    uint8_t *base;
+    uint32_t stage_bytes, ring;
+
+    __device__ __forceinline__ uint8_t *stage(uint32_t slot) const { return base + (size_t)slot * stage_bytes; }
+    __device__ __forceinline__ uint64_t *bar(uint32_t slot) const { return full + slot; }
+
+    // Thread 0 only: waits (bounded) for the `count` issued tiles from cursor
+    // c on, so that no copy lands in shared memory after the CTA has exited.
+    __device__ void drain(TileCursor c, uint32_t count, uint32_t J) const {
+        for (uint32_t i = 0; i < count; ++i, c.next(J, ring)) moe_bar_wait(bar(c.slot), c.phase);
+    }
+};
+
+__device__ __forceinline__ void ring_init(uint64_t *full, uint32_t ring) {
     if (threadIdx.x == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(moe_smem_u32(bar)));
+        for (uint32_t s = 0; s < ring; ++s)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(moe_smem_u32(full + s)));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        const uint32_t total = rows * row_bytes * (src2 ? 2u : 1u);
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(moe_smem_u32(bar)), "r"(total)
-                     : "memory");
-        for (uint32_t r = 0; r < rows; ++r) {
-            moe_bulk(dst + (size_t)r * dst_pitch, src + (size_t)r * row_bytes, row_bytes, bar);
-            if (src2) moe_bulk(dst2 + (size_t)r * dst_pitch, src2 + (size_t)r * row_bytes, row_bytes, bar);
-        }
-        *ok = 1;
-        if (!moe_bar_wait(bar)) {
-            moe_raise(err, kErrTimeout | (1u << 8));
-            *ok = 0;
-            moe_bar_wait(bar);   // let the copies in flight land before the CTA exits
-        }
     }
     __syncthreads();
-    return *ok != 0;
 }
 
-// `nb` activation rows (row ids rows_of(j), `cols` floats each) into
-// shared memory xs[j][cols], all threads, 16-byte moves.
-template <typename RowOf>
-__device__ __forceinline__ void stage_acts(float *xs, const float *src, uint32_t ld, uint32_t cols, uint32_t nb,
-                                           RowOf rows_of) {
-    const uint32_t q = cols / 4u;
-    for (uint32_t i = threadIdx.x; i < nb * q; i += blockDim.x) {
-        const uint32_t j = i / q, c = i % q;
-        reinterpret_cast<float4 *>(xs + (size_t)j * cols)[c] =
-            reinterpret_cast<const float4 *>(src + (size_t)rows_of(j) * ld)[c];
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 2^k for |k| <= 126.
+__device__ __forceinline__ float pow2i(int k) { return __uint_as_float((uint32_t)(k + 127) << 23); }
+
+// The prescale exponent k of a token whose largest |x| over the warp's
+// columns is m: max |x * 2^k| in [2^14, 2^15); 0 for zero or non-finite m.
+__device__ __forceinline__ int prescale_exp(float m) {
+    if (!(m > 0.0f) || !isfinite(m)) return 0;
+    const int e = (int)((__float_as_uint(m) >> 23) & 0xFFu) - 126;   // m < 2^e (subnormal m: e = -126)
+    return max(-126, min(126, 15 - e));
+}
+
+// The B register of two scaled activation values: their high fp16 parts for
+// an even MMA column, their low parts (value - high part) for an odd one.
+__device__ __forceinline__ uint32_t b_part(float x0, float x1, bool low) {
+    const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+    const __half2 v = low ? __floats2half2_rn(x0 - __half2float(h0), x1 - __half2float(h1)) : __halves2half2(h0, h1);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+// Byte i of v as a float (0..255): the byte in the mantissa of 2^23, minus
+// 2^23.
+__device__ __forceinline__ float byte_f(uint32_t v, uint32_t i) {
+    return __uint_as_float(__byte_perm(v, 0x4B000000u, 0x7540u | i)) - 8388608.0f;
+}
+
+// ---- Q4_K gate/up: a warp owns one super-block of the tile's gate or up
+// rows (H / 256 <= kGuSbMax).  Lane (g, q) reads bytes 8q .. 8q + 7 of each
+// 32-byte code group: their low nibbles are values 8q .. 8q + 7 of the
+// group's first sub-block, their high nibbles the same values of the second.
+
+// Scale-table entries of one super-block header h (fp16 d, fp16 dmin, 12
+// packed 6-bit scale / min bytes) for sub-blocks 4*half .. 4*half + 3: per
+// code group (two sub-blocks) (d*sc/64, 16*d*sc + dmin*m) of each, d*sc and
+// dmin*m rounded as the reference rounds them (src/kq_numeric.c:161-174
+// layout).  The four scales and mins come out one per byte lane: sub-block
+// j < 4: scale s[j] & 63, min s[j+4] & 63; j >= 4: scale
+// (s[j+4] & 15) | (s[j-4] >> 6) << 4, min (s[j+4] >> 4) | (s[j] >> 6) << 4.
+__device__ __forceinline__ void q4k_header_entries(uint4 h, uint32_t half, float4 &e0, float4 &e1) {
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFFu)));
+    const float dm = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const uint32_t sc = half ? (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u) : h.y & 0x3F3F3F3Fu;
+    const uint32_t mn = half ? ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u) : h.z & 0x3F3F3F3Fu;
+    float a[4], b[4];
+#pragma unroll
+    for (uint32_t i = 0; i < 4; ++i) {
+        const float dl = __fmul_rn(d, byte_f(sc, i));
+        a[i] = dl * 0.015625f;
+        b[i] = fmaf(16.0f, dl, __fmul_rn(dm, byte_f(mn, i)));
+    }
+    e0 = make_float4(a[0], b[0], a[1], b[1]);
+    e1 = make_float4(a[2], b[2], a[3], b[3]);
+}
+
+// The fp16 pairs of code word w (bytes b0..b3): low nibbles of (b0, b2) and
+// of (b1, b3), high nibbles of (b0, b2) and of (b1, b3), each nibble moved
+// to mantissa bits 6..9: value 1024 + 64 q.
+__device__ __forceinline__ uint32_t q4_lo02(uint32_t w) { return ((w << 6) & 0x03C003C0u) | kH1024; }
+__device__ __forceinline__ uint32_t q4_lo13(uint32_t w) { return ((w >> 2) & 0x03C003C0u) | kH1024; }
+__device__ __forceinline__ uint32_t q4_hi02(uint32_t w) { return ((w << 2) & 0x03C003C0u) | kH1024; }
+__device__ __forceinline__ uint32_t q4_hi13(uint32_t w) { return ((w >> 6) & 0x03C003C0u) | kH1024; }
+
+// One warp's B operand for one pass of up to four tokens: per code group gg
+// of the super-block, the first sub-block's value pairs (8q, 8q+2),
+// (8q+1, 8q+3), (8q+4, 8q+6), (8q+5, 8q+7), then the second's; the sums of
+// x' over each sub-block for token q; 2^-k of token q.
+struct GuFrags {
+    uint32_t b[4][8];
+    float xs[4][2];
+    float unscale;
+};
+
+// xrow: the activation row of this lane's token (MMA column g = lane / 4:
+// token g / 2, high part for even g, low part for odd g), null past the
+// pass's tokens.
+__device__ __forceinline__ void gu_frags(const float *__restrict__ xrow, uint32_t s, uint32_t lane, GuFrags &f) {
+    const uint32_t g = lane >> 2, q = lane & 3u;
+    const bool low = (g & 1u) != 0u;
+    const float *xr = xrow ? xrow + s * 256u + 8u * q : nullptr;
+    float m = 0.0f;   // pass 1: the token's largest |x| over the warp's 256 columns
+    if (xr) {
+#pragma unroll
+        for (int o = 0; o < 16; ++o) {   // 4 code groups x 2 sub-blocks x 2 float4
+            const float4 v =
+                __ldg(reinterpret_cast<const float4 *>(xr + 64 * (o >> 2) + 32 * ((o >> 1) & 1) + 4 * (o & 1)));
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const int k = prescale_exp(m);
+    const float sc = pow2i(k);
+#pragma unroll
+    for (int gg = 0; gg < 4; ++gg) {   // pass 2: scaled values -> fp16 parts
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+            if (xr) {
+                a = __ldg(reinterpret_cast<const float4 *>(xr + 64 * gg + 32 * h));
+                b = __ldg(reinterpret_cast<const float4 *>(xr + 64 * gg + 32 * h + 4));
+            }
+            f.b[gg][4 * h] = b_part(a.x * sc, a.z * sc, low);
+            f.b[gg][4 * h + 1] = b_part(a.y * sc, a.w * sc, low);
+            f.b[gg][4 * h + 2] = b_part(b.x * sc, b.z * sc, low);
+            f.b[gg][4 * h + 3] = b_part(b.y * sc, b.w * sc, low);
+        }
+        float dl[4] = {0.f, 0.f, 0.f, 0.f}, dh[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_f16(dl, kHOnes, kHOnes, kHOnes, kHOnes, f.b[gg][0], f.b[gg][1]);
+        mma_f16(dl, kHOnes, kHOnes, kHOnes, kHOnes, f.b[gg][2], f.b[gg][3]);
+        mma_f16(dh, kHOnes, kHOnes, kHOnes, kHOnes, f.b[gg][4], f.b[gg][5]);
+        mma_f16(dh, kHOnes, kHOnes, kHOnes, kHOnes, f.b[gg][6], f.b[gg][7]);
+        f.xs[gg][0] = dl[0] + dl[1];
+        f.xs[gg][1] = dh[0] + dh[1];
+    }
+    f.unscale = pow2i(-__shfl_sync(0xffffffffu, k, (int)(8u * q)));
+}
+
+// Partial sums over super-block s of rows g, g + 8 of the 16-row block at
+// `rows` (pitch rb), token q.  tab: the block's first row of the scale table
+// (pitch tp float4).
+__device__ __forceinline__ void gu_block(const uint8_t *rows, uint32_t rb, const float4 *tab, uint32_t tp,
+                                         uint32_t s, uint32_t lane, const GuFrags &f, float &t0, float &t1) {
+    const uint32_t g = lane >> 2, q = lane & 3u;
+    const uint8_t *r0 = rows + (size_t)g * rb + s * 144u + 16u + 8u * q, *r1 = r0 + (size_t)8 * rb;
+    const float4 *s0 = tab + (size_t)g * tp + s * 4u, *s1 = s0 + (size_t)8 * tp;
+#pragma unroll
+    for (int gg = 0; gg < 4; ++gg) {
+        const uint2 c0 = *reinterpret_cast<const uint2 *>(r0 + 32 * gg);
+        const uint2 c1 = *reinterpret_cast<const uint2 *>(r1 + 32 * gg);
+        float dl[4] = {0.f, 0.f, 0.f, 0.f}, dh[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_f16(dl, q4_lo02(c0.x), q4_lo02(c1.x), q4_lo13(c0.x), q4_lo13(c1.x), f.b[gg][0], f.b[gg][1]);
+        mma_f16(dl, q4_lo02(c0.y), q4_lo02(c1.y), q4_lo13(c0.y), q4_lo13(c1.y), f.b[gg][2], f.b[gg][3]);
+        mma_f16(dh, q4_hi02(c0.x), q4_hi02(c1.x), q4_hi13(c0.x), q4_hi13(c1.x), f.b[gg][4], f.b[gg][5]);
+        mma_f16(dh, q4_hi02(c0.y), q4_hi02(c1.y), q4_hi13(c0.y), q4_hi13(c1.y), f.b[gg][6], f.b[gg][7]);
+        const float4 a = s0[gg], b = s1[gg];
+        t0 += fmaf(a.x, dl[0] + dl[1], fmaf(a.z, dh[0] + dh[1], -fmaf(a.y, f.xs[gg][0], a.w * f.xs[gg][1])));
+        t1 += fmaf(b.x, dl[2] + dl[3], fmaf(b.z, dh[2] + dh[3], -fmaf(b.y, f.xs[gg][0], b.w * f.xs[gg][1])));
     }
 }
 
-// 32 decoded Q4_K values of run c (multiple of 32) of a row in shared memory
-// (144-byte super-blocks: fp16 d, fp16 dmin, 12 scale/min bytes, 128 code
-// bytes), value = d*sc*q - dmin*m with one rounding per value.
-__device__ __forceinline__ void q4k_run_smem(const uint8_t *row, uint32_t c, float (&w)[32]) {
-    const uint8_t *sb = row + (c >> 8) * 144u;
-    const uint32_t group = (c & 255u) >> 6, high = (c >> 5) & 1u;
-    const uint4 hdr = *reinterpret_cast<const uint4 *>(sb);
-    const uint4 q0 = *reinterpret_cast<const uint4 *>(sb + 16u + group * 32u);
-    const uint4 q1 = *reinterpret_cast<const uint4 *>(sb + 32u + group * 32u);
-    uint8_t h[16];
-    bytes16(hdr, h);
-    const float d = half_bits_to_float((uint32_t)h[0] | ((uint32_t)h[1] << 8));
-    const float dmin = half_bits_to_float((uint32_t)h[2] | ((uint32_t)h[3] << 8));
-    uint32_t sc, mn;
-    q4k_scale_min(h + 4, (int)(2u * group + high), sc, mn);
-    const float dl = __fmul_rn(d, (float)sc), ml = __fmul_rn(dmin, (float)mn);
-    const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-        const uint32_t nib = (words[k] >> (4u * high)) & 0x0F0F0F0Fu;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) w[4 * k + b] = fmaf(dl, byte_float(nib, b), -ml);
-    }
-}
-
-// s += w . xs[0..32)
-__device__ __forceinline__ float dot32_smem(const float (&w)[32], const float *xs, float s) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 v = reinterpret_cast<const float4 *>(xs)[i];
-        s = fmaf(w[4 * i], v.x, s);
-        s = fmaf(w[4 * i + 1], v.y, s);
-        s = fmaf(w[4 * i + 2], v.z, s);
-        s = fmaf(w[4 * i + 3], v.w, s);
-    }
-    return s;
-}
-
-// grid (max active experts, ceil(I / 32)), 256 threads.  Warp w owns local
-// rows 4w..4w+3; lane = sub * 8 + unit with unit = row * 2 + {0 gate, 1 up}
-// and the four subs splitting a row's 32-value runs.  Shared memory: gate
-// rows, up rows (pitch rb + 16 keeps the eight units' rows in distinct
-// banks), then kGuGroup activation rows.
-__global__ void __launch_bounds__(kMoeThreads, 2)
-moe_gate_up_staged_kernel(MoeDims d, QMatrix gate, QMatrix up, const float *__restrict__ x, uint32_t ldx,
+// Grid: one CTA per SM; block kStreamThreads.  Warp w decodes super-block
+// w % kGuSbMax of the tile's gate rows (w < kGuSbMax) or up rows.  Dynamic
+// shared memory: the ring (ring stages of kGuTile gate rows then kGuTile up
+// rows, pitch row_bytes), the tile's scale table [2*kGuTile][H/64] float4
+// (each warp writes and reads its own rows and super-block), the per-warp
+// partial sums [kMmaWarps][kGuTile][kMmaTokens].  Tiles in active-expert-
+// major order.
+__global__ void __launch_bounds__(kStreamThreads, 1)
+moe_gate_up_stream_kernel(MoeDims d, QMatrix gate, QMatrix up, const float *__restrict__ x, uint32_t ldx,
                           const uint32_t *__restrict__ active, const uint32_t *__restrict__ offsets,
-                          const uint32_t *__restrict__ pick_of_slot, float *__restrict__ act, float *gate_dbg,
-                          float *up_dbg, ErrorWord err) {
+                          const uint32_t *__restrict__ pick_of_slot, uint32_t ring, float *__restrict__ act,
+                          float *gate_dbg, float *up_dbg, ErrorWord err) {
     extern __shared__ __align__(128) uint8_t gsm[];
-    __shared__ uint64_t bar;
-    __shared__ int ok;
+    __shared__ __align__(8) uint64_t full[kStreamRing];
+    const uint32_t H = d.hidden, I = d.routed, rb = gate.row_bytes;
+    const uint32_t SB = H / 256u, TR = 2u * kGuTile, tp = H / 64u;
+    const uint32_t J = (I + kGuTile - 1u) / kGuTile;
+    const StreamRing rg{full, gsm, TR * rb, ring};
+    float4 *table = reinterpret_cast<float4 *>(gsm + (size_t)ring * rg.stage_bytes);
+    float *red = reinterpret_cast<float *>(table + (size_t)TR * tp);
+    ring_init(full, ring);
     pdl_wait();
-    if (moe_err_raised(err) || blockIdx.x >= active[0]) return;
-    const uint32_t e = active[1 + blockIdx.x];
-    const uint32_t s0 = offsets[e], n = offsets[e + 1] - s0;
-    const uint32_t I = d.routed, H = d.hidden, rb = gate.row_bytes, pitch = rb + 16u;
-    const uint32_t r0 = blockIdx.y * kGuRows, rows = min(kGuRows, I - r0);
-    uint8_t *gs = gsm, *us = gsm + (size_t)kGuRows * pitch;
-    float *xs = reinterpret_cast<float *>(gsm + (size_t)2 * kGuRows * pitch);
-    if (!stage_rows(gs, gate.data + ((size_t)e * I + r0) * rb, rows, rb, pitch, up.data + ((size_t)e * I + r0) * rb,
-                    us, &bar, &ok, err))
-        return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t unit = (uint32_t)lane & 7u, sub = (uint32_t)lane >> 3;
-    const uint32_t lr = (uint32_t)warp * 4u + (unit >> 1);
-    const bool is_up = (unit & 1u) != 0u, live = lr < rows;
-    const uint8_t *row = (is_up ? us : gs) + (size_t)(live ? lr : 0u) * pitch;
-    for (uint32_t g0 = 0; g0 < n; g0 += kGuGroup) {
-        const uint32_t nb = min(kGuGroup, n - g0);
-        __syncthreads();   // the previous group's activation rows are no longer read
-        stage_acts(xs, x, ldx, H, nb, [&](uint32_t j) { return pick_of_slot[s0 + g0 + j] / d.top_k; });
-        __syncthreads();
-        float a0 = 0.0f, a1 = 0.0f;
-        if (live) {
-            for (uint32_t c = sub * 32u; c < H; c += 128u) {
-                float w[32];
-                q4k_run_smem(row, c, w);
-                a0 = dot32_smem(w, xs + c, a0);
-                if (nb > 1) a1 = dot32_smem(w, xs + H + c, a1);
-            }
+    if (moe_err_raised(err)) return;
+    uint32_t tb, te;
+    tile_range((uint64_t)active[0] * J, tb, te);
+    if (tb >= te) return;
+    const uint32_t n_tiles = te - tb;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const uint32_t sb = warp % kGuSbMax, half = warp / kGuSbMax;   // super-block; 0 gate rows, 1 up rows
+    const bool worker = sb < SB;
+    const uint32_t g = lane >> 2, q = lane & 3u;
+
+    TileCursor pc;   // thread 0: the next tile to issue
+    pc.start(tb, J);
+    uint32_t issued = 0;
+    auto issue = [&]() {
+        const uint32_t e = active[1u + pc.a], r0 = pc.j * kGuTile, rows = min(kGuTile, I - r0);
+        uint8_t *st = rg.stage(pc.slot);
+        uint64_t *bar = rg.bar(pc.slot);
+        const size_t off = ((size_t)e * I + r0) * rb;
+        moe_expect(bar, 2u * rows * rb);
+        moe_bulk(st, gate.data + off, rows * rb, bar);
+        moe_bulk(st + (size_t)kGuTile * rb, up.data + off, rows * rb, bar);
+        pc.next(J, ring);
+        ++issued;
+    };
+    if (tid == 0)
+        while (issued < n_tiles && issued < ring) issue();
+
+    GuFrags f;
+    float *pr = red + (size_t)warp * kGuTile * kMmaTokens;
+    const float4 *tab = table + (size_t)half * kGuTile * tp;
+    TileCursor c;
+    c.start(tb, J);
+    uint32_t cur = 0xFFFFFFFFu, s0 = 0, n = 0, loaded = 0xFFFFFFFFu;
+    for (uint32_t k = 0; k < n_tiles; ++k, c.next(J, ring)) {
+        const uint32_t r0 = c.j * kGuTile, rows = min(kGuTile, I - r0);
+        if (c.a != cur) {
+            const uint32_t e = active[1u + c.a];
+            cur = c.a, s0 = offsets[e], n = offsets[e + 1u] - s0, loaded = 0xFFFFFFFFu;
         }
-        a0 += __shfl_xor_sync(0xffffffffu, a0, 8);
-        a0 += __shfl_xor_sync(0xffffffffu, a0, 16);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, 8);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, 16);
-        const float u0 = __shfl_down_sync(0xffffffffu, a0, 1), u1 = __shfl_down_sync(0xffffffffu, a1, 1);
-        if (sub == 0 && !is_up && live) {
-            const size_t o = (size_t)(s0 + g0) * I + r0 + lr;
-            act[o] = moe_swiglu(a0, u0);
-            if (gate_dbg) {
-                gate_dbg[o] = a0;
-                up_dbg[o] = u0;
+        const uint8_t *st = rg.stage(c.slot);
+        const bool ok = moe_bar_wait(rg.bar(c.slot), c.phase);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                moe_raise(err, kErrTimeout | (1u << 8));
+                rg.drain(c, issued - k, J);
             }
-            if (nb > 1) {
-                act[o + I] = moe_swiglu(a1, u1);
-                if (gate_dbg) {
-                    gate_dbg[o + I] = a1;
-                    up_dbg[o + I] = u1;
+            return;
+        }
+        const uint8_t *blk = st + (size_t)half * kGuTile * rb;
+        if (worker) {   // lanes 2r, 2r + 1: the scale entries of row r's super-block sb
+            const uint32_t r = lane >> 1, hh = lane & 1u;
+            if (r < rows) {
+                const uint4 hd = *reinterpret_cast<const uint4 *>(blk + (size_t)r * rb + sb * 144u);
+                float4 e0, e1;
+                q4k_header_entries(hd, hh, e0, e1);
+                float4 *tr = table + ((size_t)half * kGuTile + r) * tp + sb * 4u + 2u * hh;
+                tr[0] = e0;
+                tr[1] = e1;
+            }
+            __syncwarp();
+        }
+        for (uint32_t g0 = 0; g0 < n; g0 += kMmaTokens) {
+            const uint32_t nb = min(kMmaTokens, n - g0);
+            if (worker) {
+                if (loaded != g0) {
+                    const uint32_t t = lane >> 3;   // this lane's token in the pass
+                    gu_frags(t < nb ? x + (size_t)(pick_of_slot[s0 + g0 + t] / d.top_k) * ldx : nullptr, sb, lane,
+                             f);
+                    loaded = g0;
+                }
+                float t0 = 0.0f, t1 = 0.0f;
+                gu_block(blk, rb, tab, tp, sb, lane, f, t0, t1);
+                if (q < nb) {
+                    pr[g * kMmaTokens + q] = t0 * f.unscale;
+                    pr[(g + 8u) * kMmaTokens + q] = t1 * f.unscale;
                 }
             }
+            __syncthreads();   // partial sums complete; the stage has been read
+            const bool last = g0 + kMmaTokens >= n;
+            if (last && tid == 0 && issued < n_tiles) issue();
+            if (tid < kGuTile * nb) {   // one thread per (row, token): gate and up sums, SwiGLU
+                const uint32_t i = tid % kGuTile, t = tid / kGuTile;
+                if (i < rows) {
+                    float sg = 0.0f, su = 0.0f;
+                    for (uint32_t w = 0; w < SB; ++w) {
+                        sg += red[((size_t)w * kGuTile + i) * kMmaTokens + t];
+                        su += red[((size_t)(kGuSbMax + w) * kGuTile + i) * kMmaTokens + t];
+                    }
+                    const size_t oo = (size_t)(s0 + g0 + t) * I + r0 + i;
+                    act[oo] = moe_swiglu(sg, su);
+                    if (gate_dbg) {
+                        gate_dbg[oo] = sg;
+                        up_dbg[oo] = su;
+                    }
+                }
+            }
+            if (!last) __syncthreads();   // the partial sums are rewritten by the next pass
+        }
+        if (n == 0) {   // no rows to write (not produced by the dispatch): keep the ring going
+            __syncthreads();
+            if (tid == 0 && issued < n_tiles) issue();
         }
     }
 }
 
-// grid (max active experts, ceil(H / 64)), 256 threads.  Warp w owns local
-// rows 8w..8w+7; lane = sub * 8 + row.  Planar Q8_0 rows: I code bytes,
-// then the I/32 fp16 scales; shared memory: the rows (pitch rb), then
-// kDnGroup activation rows.
-__global__ void __launch_bounds__(kMoeThreads, 3)
-moe_down_staged_kernel(MoeDims d, QMatrix down, const float *__restrict__ act, const uint32_t *__restrict__ active,
-                       const uint32_t *__restrict__ offsets, float *__restrict__ eout, ErrorWord err) {
+// ---- planar Q8_0 down: row = I code bytes, then the I/32 fp16 block
+// scales (pitch row_bytes).  A warp owns code blocks c0 .. c0 + nblk - 1 of
+// every row; lane (g, q) reads bytes 8q .. 8q + 7 of each block.
+
+// The fp16 pairs of sign-flipped code bytes (b0, b1) and (b2, b3) of word v:
+// each byte c + 128 in the low mantissa byte of 1024: value 1152 + c.
+__device__ __forceinline__ uint32_t q8_01(uint32_t v) { return __byte_perm(v, 0x64646464u, 0x4140u); }
+__device__ __forceinline__ uint32_t q8_23(uint32_t v) { return __byte_perm(v, 0x64646464u, 0x4342u); }
+
+struct DnFrags {
+    uint32_t b[kDnMaxBpw][4];
+    float xs[kDnMaxBpw];
+    float unscale;
+};
+
+// arow: this lane's token's activation row (null past the pass's tokens).
+__device__ __forceinline__ void dn_frags(const float *__restrict__ arow, uint32_t c0, uint32_t nblk, uint32_t lane,
+                                         DnFrags &f) {
+    const uint32_t g = lane >> 2, q = lane & 3u;
+    const bool low = (g & 1u) != 0u;
+    float v[kDnMaxBpw][8];
+    float m = 0.0f;
+#pragma unroll
+    for (uint32_t j = 0; j < kDnMaxBpw; ++j) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+        if (arow && j < nblk) {
+            const float *xr = arow + (c0 + j) * 32u + 8u * q;
+            a = *reinterpret_cast<const float4 *>(xr);
+            b = *reinterpret_cast<const float4 *>(xr + 4);
+        }
+        const float w8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            v[j][i] = w8[i];
+            m = fmaxf(m, fabsf(w8[i]));
+        }
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    const int k = prescale_exp(m);
+    const float sc = pow2i(k);
+#pragma unroll
+    for (uint32_t j = 0; j < kDnMaxBpw; ++j) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f.b[j][i] = b_part(v[j][2 * i] * sc, v[j][2 * i + 1] * sc, low);
+        float dx[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_f16(dx, kHOnes, kHOnes, kHOnes, kHOnes, f.b[j][0], f.b[j][1]);
+        mma_f16(dx, kHOnes, kHOnes, kHOnes, kHOnes, f.b[j][2], f.b[j][3]);
+        f.xs[j] = dx[0] + dx[1];
+    }
+    f.unscale = pow2i(-__shfl_sync(0xffffffffu, k, (int)(8u * q)));
+}
+
+// Partial sums over the warp's blocks of rows g, g + 8 of the 16-row block
+// at `rows` (pitch rb), token q.  code: byte offset of the lane's first code
+// (c0*32 + 8q); scale: byte offset of the first block's scale (I + 2*c0).
+__device__ __forceinline__ void dn_block(const uint8_t *rows, uint32_t rb, uint32_t code, uint32_t scale,
+                                         uint32_t nblk, uint32_t lane, const DnFrags &f, float &t0, float &t1) {
+    const uint8_t *r0 = rows + (size_t)(lane >> 2) * rb, *r1 = r0 + (size_t)8 * rb;
+#pragma unroll
+    for (uint32_t j = 0; j < kDnMaxBpw; ++j) {
+        if (j >= nblk) break;
+        const uint2 a = *reinterpret_cast<const uint2 *>(r0 + code + 32u * j);
+        const uint2 b = *reinterpret_cast<const uint2 *>(r1 + code + 32u * j);
+        const uint32_t ax = a.x ^ 0x80808080u, ay = a.y ^ 0x80808080u, bx = b.x ^ 0x80808080u,
+                       by = b.y ^ 0x80808080u;
+        float dd[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_f16(dd, q8_01(ax), q8_01(bx), q8_23(ax), q8_23(bx), f.b[j][0], f.b[j][1]);
+        mma_f16(dd, q8_01(ay), q8_01(by), q8_23(ay), q8_23(by), f.b[j][2], f.b[j][3]);
+        const float d0 = __half2float(*reinterpret_cast<const __half *>(r0 + scale + 2u * j));
+        const float d1 = __half2float(*reinterpret_cast<const __half *>(r1 + scale + 2u * j));
+        t0 = fmaf(d0, (dd[0] + dd[1]) - 1152.0f * f.xs[j], t0);
+        t1 = fmaf(d1, (dd[2] + dd[3]) - 1152.0f * f.xs[j], t1);
+    }
+}
+
+// Grid: one CTA per SM; block kStreamThreads.  Dynamic shared memory: the
+// ring (ring stages of kDnTile rows, pitch row_bytes), the per-warp partial
+// sums [kMmaWarps][kDnTile][kMmaTokens].  Tiles in active-expert-major
+// order; act [slots][I] by slot -> eout [slots][H].
+__global__ void __launch_bounds__(kStreamThreads, 1)
+moe_down_stream_kernel(MoeDims d, QMatrix down, const float *__restrict__ act, const uint32_t *__restrict__ active,
+                       const uint32_t *__restrict__ offsets, uint32_t ring, float *__restrict__ eout, ErrorWord err) {
     extern __shared__ __align__(128) uint8_t dsm[];
-    __shared__ uint64_t bar;
-    __shared__ int ok;
-    pdl_wait();
-    if (moe_err_raised(err) || blockIdx.x >= active[0]) return;
-    const uint32_t e = active[1 + blockIdx.x];
-    const uint32_t s0 = offsets[e], n = offsets[e + 1] - s0;
+    __shared__ __align__(8) uint64_t full[kStreamRing];
     const uint32_t H = d.hidden, I = d.routed, rb = down.row_bytes;
-    const uint32_t r0 = blockIdx.y * kDnRows, rows = min(kDnRows, H - r0);
-    float *as = reinterpret_cast<float *>(dsm + (size_t)kDnRows * rb);
-    if (!stage_rows(dsm, down.data + ((size_t)e * H + r0) * rb, rows, rb, rb, nullptr, nullptr, &bar, &ok, err))
-        return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t lr = (uint32_t)warp * 8u + ((uint32_t)lane & 7u), sub = (uint32_t)lane >> 3;
-    const bool live = lr < rows;
-    const uint8_t *row = dsm + (size_t)(live ? lr : 0u) * rb;
-    const uint16_t *scales = reinterpret_cast<const uint16_t *>(row + I);
-    for (uint32_t g0 = 0; g0 < n; g0 += kDnGroup) {
-        const uint32_t nb = min(kDnGroup, n - g0);
-        __syncthreads();
-        stage_acts(as, act + (size_t)(s0 + g0) * I, I, I, nb, [](uint32_t j) { return j; });
-        __syncthreads();
-        float acc[kDnGroup];
+    const uint32_t NB = I / 32u, bpw = (NB + kMmaWarps - 1u) / kMmaWarps;
+    const uint32_t J = (H + kDnTile - 1u) / kDnTile;
+    const StreamRing rg{full, dsm, kDnTile * rb, ring};
+    float *red = reinterpret_cast<float *>(dsm + (size_t)ring * rg.stage_bytes);
+    ring_init(full, ring);
+    pdl_wait();
+    if (moe_err_raised(err)) return;
+    uint32_t tb, te;
+    tile_range((uint64_t)active[0] * J, tb, te);
+    if (tb >= te) return;
+    const uint32_t n_tiles = te - tb;
+    const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
+    const uint32_t c0 = warp * bpw, nblk = c0 < NB ? min(bpw, NB - c0) : 0u;
+    const uint32_t wk = (NB + bpw - 1u) / bpw;   // warps with blocks
+    const bool worker = nblk > 0u;
+    const uint32_t g = lane >> 2, q = lane & 3u;
+
+    TileCursor pc;   // thread 0: the next tile to issue
+    pc.start(tb, J);
+    uint32_t issued = 0;
+    auto issue = [&]() {
+        const uint32_t e = active[1u + pc.a], r0 = pc.j * kDnTile, rows = min(kDnTile, H - r0);
+        uint64_t *bar = rg.bar(pc.slot);
+        moe_expect(bar, rows * rb);
+        moe_bulk(rg.stage(pc.slot), down.data + ((size_t)e * H + r0) * rb, rows * rb, bar);
+        pc.next(J, ring);
+        ++issued;
+    };
+    if (tid == 0)
+        while (issued < n_tiles && issued < ring) issue();
+
+    DnFrags f;
+    float *pr = red + (size_t)warp * kDnTile * kMmaTokens;
+    TileCursor c;
+    c.start(tb, J);
+    uint32_t cur = 0xFFFFFFFFu, s0 = 0, n = 0, loaded = 0xFFFFFFFFu;
+    for (uint32_t k = 0; k < n_tiles; ++k, c.next(J, ring)) {
+        const uint32_t r0 = c.j * kDnTile, rows = min(kDnTile, H - r0);
+        if (c.a != cur) {
+            const uint32_t e = active[1u + c.a];
+            cur = c.a, s0 = offsets[e], n = offsets[e + 1u] - s0, loaded = 0xFFFFFFFFu;
+        }
+        const uint8_t *st = rg.stage(c.slot);
+        const bool ok = moe_bar_wait(rg.bar(c.slot), c.phase);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                moe_raise(err, kErrTimeout | (2u << 8));
+                rg.drain(c, issued - k, J);
+            }
+            return;
+        }
+        for (uint32_t g0 = 0; g0 < n; g0 += kMmaTokens) {
+            const uint32_t nb = min(kMmaTokens, n - g0);
+            if (worker) {
+                if (loaded != g0) {
+                    const uint32_t t = lane >> 3;   // this lane's token in the pass
+                    dn_frags(t < nb ? act + (size_t)(s0 + g0 + t) * I : nullptr, c0, nblk, lane, f);
+                    loaded = g0;
+                }
 #pragma unroll
-        for (int j = 0; j < (int)kDnGroup; ++j) acc[j] = 0.0f;
-        if (live) {
-            for (uint32_t c = sub * 32u; c < I; c += 128u) {
-                const uint4 q0 = *reinterpret_cast<const uint4 *>(row + c);
-                const uint4 q1 = *reinterpret_cast<const uint4 *>(row + c + 16u);
-                const float dsc = half_bits_to_float(scales[c >> 5]);
-                const uint32_t words[8] = {q0.x ^ 0x80808080u, q0.y ^ 0x80808080u, q0.z ^ 0x80808080u,
-                                           q0.w ^ 0x80808080u, q1.x ^ 0x80808080u, q1.y ^ 0x80808080u,
-                                           q1.z ^ 0x80808080u, q1.w ^ 0x80808080u};
-                float w[32];
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) w[4 * k + b] = byte_float(words[k], b) - 128.0f;   // the int8 code
-#pragma unroll
-                for (int j = 0; j < (int)kDnGroup; ++j) {
-                    if ((uint32_t)j >= nb) break;
-                    acc[j] = fmaf(dsc, dot32_smem(w, as + (size_t)j * I + c, 0.0f), acc[j]);
+                for (uint32_t b = 0; b < kDnTile / 16u; ++b) {
+                    float t0 = 0.0f, t1 = 0.0f;
+                    dn_block(st + (size_t)b * 16u * rb, rb, c0 * 32u + 8u * q, I + 2u * c0, nblk, lane, f, t0, t1);
+                    if (q < nb) {
+                        pr[(b * 16u + g) * kMmaTokens + q] = t0 * f.unscale;
+                        pr[(b * 16u + g + 8u) * kMmaTokens + q] = t1 * f.unscale;
+                    }
                 }
             }
+            __syncthreads();   // partial sums complete; the stage has been read
+            const bool last = g0 + kMmaTokens >= n;
+            if (last && tid == 0 && issued < n_tiles) issue();
+            for (uint32_t o = tid; o < kDnTile * nb; o += kStreamThreads) {   // one thread per (row, token)
+                const uint32_t i = o % kDnTile, t = o / kDnTile;
+                if (i < rows) {
+                    float sum = 0.0f;
+                    for (uint32_t w = 0; w < wk; ++w) sum += red[((size_t)w * kDnTile + i) * kMmaTokens + t];
+                    eout[(size_t)(s0 + g0 + t) * H + r0 + i] = sum;
+                }
+            }
+            if (!last) __syncthreads();   // the partial sums are rewritten by the next pass
         }
-#pragma unroll
-        for (int j = 0; j < (int)kDnGroup; ++j) {
-            if ((uint32_t)j >= nb) break;
-            float v = acc[j];
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            v += __shfl_xor_sync(0xffffffffu, v, 16);
-            if (sub == 0 && live) eout[(size_t)(s0 + g0 + j) * H + r0 + lr] = v;
+        if (n == 0) {
+            __syncthreads();
+            if (tid == 0 && issued < n_tiles) issue();
         }
     }
 }
@@ -842,44 +1159,75 @@ void launch_moe_dispatch(const MoeDims &d, uint32_t T, MoeBuffers &b, ErrorWord 
 
 static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0u; }
 
-// The staged kernels' conditions: the types they decode, 16-byte aligned
-// rows and float4-aligned activations, a row block within kMaxStageBytes.
-static size_t gate_up_stage_bytes(const MoeDims &d, const QMatrix &g) {
-    return (size_t)2 * kGuRows * (g.row_bytes + 16u) + (size_t)kGuGroup * d.hidden * 4u;
+static int moe_sm_count() {
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    return sms;
 }
 
-static size_t down_stage_bytes(const MoeDims &d, const QMatrix &m) {
-    return (size_t)kDnRows * m.row_bytes + (size_t)kDnGroup * d.routed * 4u;
+// Stages of a streamed kernel's ring that fit next to its fixed shared
+// memory (0 when fewer than two fit).
+static uint32_t stream_ring(size_t stage, size_t fixed) {
+    if (fixed + 2 * stage > kStreamSmemLimit) return 0;
+    return (uint32_t)std::min<size_t>(kStreamRing, (kStreamSmemLimit - fixed) / stage);
 }
 
-static bool gate_up_staged_ok(const MoeDims &d, const QMatrix &g, const QMatrix &u, const float *x, uint32_t ldx) {
-    return g.type == kTypeQ4_K && u.type == kTypeQ4_K && g.row_bytes == u.row_bytes && g.row_bytes % 16u == 0u &&
-           aligned16(g.data) && aligned16(u.data) && d.hidden % 256u == 0u && aligned16(x) && ldx % 4u == 0u &&
-           gate_up_stage_bytes(d, g) <= kMaxStageBytes;
+static size_t gate_up_fixed_bytes(const MoeDims &d) {
+    return (size_t)2 * kGuTile * (d.hidden / 64u) * 16u + (size_t)kMmaWarps * kGuTile * kMmaTokens * 4u;
 }
 
-static bool down_staged_ok(const MoeDims &d, const QMatrix &m, const float *act) {
-    return m.type == kTypeQ8_0 && m.layout == 1 && m.row_bytes % 16u == 0u && aligned16(m.data) &&
-           d.routed % 32u == 0u && aligned16(act) && down_stage_bytes(d, m) <= kMaxStageBytes;
+static size_t down_fixed_bytes() { return (size_t)kMmaWarps * kDnTile * kMmaTokens * 4u; }
+
+// The streamed kernels' conditions: the types they decode (GGUF Q4_K rows,
+// planar Q8_0 rows), 16-byte aligned rows and activations, the columns one
+// CTA's warps cover, a ring of at least two stages.
+static bool gate_up_stream_ok(const MoeDims &d, const QMatrix &g, const QMatrix &u, const float *x, uint32_t ldx) {
+    return g.type == kTypeQ4_K && u.type == kTypeQ4_K && d.hidden % 256u == 0u && d.hidden / 256u <= kGuSbMax &&
+           g.row_bytes == d.hidden / 256u * 144u && u.row_bytes == g.row_bytes && aligned16(g.data) &&
+           aligned16(u.data) && aligned16(x) && ldx % 4u == 0u &&
+           stream_ring((size_t)2 * kGuTile * g.row_bytes, gate_up_fixed_bytes(d)) >= 2u;
+}
+
+static bool down_stream_ok(const MoeDims &d, const QMatrix &m, const float *act) {
+    return m.type == kTypeQ8_0 && m.layout == 1 && d.routed % 32u == 0u &&
+           d.routed / 32u <= kMmaWarps * kDnMaxBpw && m.row_bytes % 16u == 0u &&
+           m.row_bytes >= d.routed + d.routed / 16u && aligned16(m.data) && aligned16(act) &&
+           stream_ring((size_t)kDnTile * m.row_bytes, down_fixed_bytes()) >= 2u;
 }
 
 void launch_moe_experts(const MoeDims &d, const MoeWeightsDev &w, const float *x, uint32_t ldx, uint32_t T,
                         MoeBuffers &b, ErrorWord err, cudaStream_t stream) {
     const uint32_t max_active = (uint32_t)std::min<uint64_t>(d.experts, (uint64_t)T * d.top_k);
     static DeviceOnce attr;
-    attr.run([] {
-        cudaFuncSetAttribute(moe_gate_up_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kMaxStageBytes);
-        cudaFuncSetAttribute(moe_down_staged_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kMaxStageBytes);
+    static bool stream_attr_ok[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    attr.run([dev] {
+        const cudaError_t e1 = cudaFuncSetAttribute(moe_gate_up_stream_kernel,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStreamSmemLimit);
+        const cudaError_t e2 = cudaFuncSetAttribute(moe_down_stream_kernel,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStreamSmemLimit);
+        if (e1 != cudaSuccess || e2 != cudaSuccess)
+            cudaGetLastError();   // the streamed kernels stay off on this device; nothing is left pending
+        else if (dev >= 0 && dev < 64)
+            stream_attr_ok[dev] = true;
     });
+    const bool streamed = dev >= 0 && dev < 64 && stream_attr_ok[dev];
+    const uint32_t sms = (uint32_t)moe_sm_count();
     {
         KernelTimer timer("moe_gate_up", stream);
-        if (gate_up_staged_ok(d, w.gate, w.up, x, ldx)) {
-            dim3 grid(max_active, (d.routed + kGuRows - 1) / kGuRows);
-            launch_pdl(moe_gate_up_staged_kernel, grid, kMoeThreads, gate_up_stage_bytes(d, w.gate), stream,
-                       d, w.gate, w.up, x, ldx, b.active, b.offsets, b.pick_of_slot, b.act, b.dbg.gate, b.dbg.up,
-                       err);
+        if (streamed && gate_up_stream_ok(d, w.gate, w.up, x, ldx)) {
+            const size_t stage = (size_t)2 * kGuTile * w.gate.row_bytes, fixed = gate_up_fixed_bytes(d);
+            const uint32_t ring = stream_ring(stage, fixed);
+            const uint64_t tiles = (uint64_t)max_active * ((d.routed + kGuTile - 1) / kGuTile);
+            const uint32_t grid = (uint32_t)std::min<uint64_t>(sms, tiles);
+            launch_pdl(moe_gate_up_stream_kernel, grid, kStreamThreads, fixed + ring * stage, stream, d, w.gate,
+                       w.up, x, ldx, b.active, b.offsets, b.pick_of_slot, ring, b.act, b.dbg.gate, b.dbg.up, err);
         } else {
             dim3 grid(max_active, (d.routed + kMoeRowsPerCta - 1) / kMoeRowsPerCta);
             launch_pdl(moe_gate_up_kernel, grid, kMoeThreads, 0, stream, d, w.gate, w.up, x, ldx, b.active,
@@ -889,10 +1237,13 @@ void launch_moe_experts(const MoeDims &d, const MoeWeightsDev &w, const float *x
     }
     {
         KernelTimer timer("moe_down", stream);
-        if (down_staged_ok(d, w.down, b.act)) {
-            dim3 grid(max_active, (d.hidden + kDnRows - 1) / kDnRows);
-            launch_pdl(moe_down_staged_kernel, grid, kMoeThreads, down_stage_bytes(d, w.down), stream, d,
-                       w.down, b.act, b.active, b.offsets, b.eout, err);
+        if (streamed && down_stream_ok(d, w.down, b.act)) {
+            const size_t stage = (size_t)kDnTile * w.down.row_bytes, fixed = down_fixed_bytes();
+            const uint32_t ring = stream_ring(stage, fixed);
+            const uint64_t tiles = (uint64_t)max_active * ((d.hidden + kDnTile - 1) / kDnTile);
+            const uint32_t grid = (uint32_t)std::min<uint64_t>(sms, tiles);
+            launch_pdl(moe_down_stream_kernel, grid, kStreamThreads, fixed + ring * stage, stream, d, w.down,
+                       b.act, b.active, b.offsets, ring, b.eout, err);
         } else {
             dim3 grid(max_active, (d.hidden + kMoeRowsPerCta - 1) / kMoeRowsPerCta);
             launch_pdl(moe_down_kernel, grid, kMoeThreads, 0, stream, d, w.down, b.act, b.active, b.offsets, b.eout,
