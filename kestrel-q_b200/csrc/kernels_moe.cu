@@ -70,18 +70,6 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// The reference's "worst" member of the selected set
-// (src/kq_moe_qwen38.c:217-228): lowest probability, the lowest id among
-// equal lowest probabilities.
-__device__ __forceinline__ uint32_t worst_position(const float *p, const uint32_t *ids, uint32_t k) {
-    uint32_t worst = 0;
-    for (uint32_t pos = 1; pos < k; ++pos) {
-        const uint32_t c = ids[pos], w = ids[worst];
-        if (p[c] < p[w] || (p[c] == p[w] && c < w)) worst = pos;
-    }
-    return worst;
-}
-
 }  // namespace
 
 // ------------------------------------------------------------------ route
@@ -129,9 +117,15 @@ moe_route_kernel(MoeDims d, const float *__restrict__ logits, uint32_t ldl, floa
     // except within 2^-29 of a rounding boundary
     for (uint32_t e = tid; e < E; e += kMoeThreads) sp[e] = (float)exp((double)__fsub_rn(lg[e], mx));
     __syncthreads();
-    if (tid == 0) {
+    if (tid == 0) {   // one sequential sum in index order (four values per shared-memory load)
         float s = 0.0f;
-        for (uint32_t e = 0; e < E; ++e) s = __fadd_rn(s, sp[e]);
+        uint32_t e = 0;
+#pragma unroll 4
+        for (; e + 4u <= E; e += 4u) {
+            const float4 v = *reinterpret_cast<const float4 *>(sp + e);
+            s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
+        }
+        for (; e < E; ++e) s = __fadd_rn(s, sp[e]);
         if (!isfinite(s) || s <= 0.0f) bad = 1;
         total = s;
     }
@@ -147,20 +141,48 @@ moe_route_kernel(MoeDims d, const float *__restrict__ logits, uint32_t ldl, floa
         probs[(size_t)t * E + e] = p;
     }
     __syncthreads();
-    if (tid == 0) {
-        // top-k of src/kq_moe_qwen38.c:211-245; the worst member only
-        // changes when the set does, so it is recomputed after a replacement
-        for (uint32_t i = 0; i < K; ++i) ids[i] = i;
-        uint32_t worst = worst_position(sp, ids, K);
-        float wv = sp[ids[worst]];
-        for (uint32_t i = K; i < E; ++i) {
-            const float v = sp[i];
-            if (v > wv) {
-                ids[worst] = i;
-                worst = worst_position(sp, ids, K);
-                wv = sp[ids[worst]];
+    if (warp == 0) {
+        // top-k of src/kq_moe_qwen38.c:211-245, in index order: the set
+        // starts as experts 0..K-1; expert i replaces the worst member (lowest
+        // value, lowest id among equal values) when its value is strictly
+        // greater.  Lane p < K holds member p; a ballot tests 32 experts
+        // against the current worst at once, and the hits are inserted one at
+        // a time in index order, the rest of the chunk tested again against
+        // the new worst.
+        uint32_t my_id = (uint32_t)lane < K ? (uint32_t)lane : 0xFFFFFFFFu;
+        float my_v = (uint32_t)lane < K ? sp[lane] : INFINITY;
+        uint32_t wpos;
+        float wv;
+        auto find_worst = [&]() {
+            float v = my_v;
+            uint32_t id = my_id, pos = (uint32_t)lane;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                const uint32_t oid = __shfl_xor_sync(0xffffffffu, id, o);
+                const uint32_t opos = __shfl_xor_sync(0xffffffffu, pos, o);
+                if (ov < v || (ov == v && oid < id)) v = ov, id = oid, pos = opos;
+            }
+            wpos = pos, wv = v;
+        };
+        find_worst();
+        for (uint32_t base = K; base < E; base += 32u) {
+            const uint32_t i = base + (uint32_t)lane;
+            const float v = i < E ? sp[i] : -INFINITY;
+            uint32_t m = __ballot_sync(0xffffffffu, v > wv);
+            while (m != 0u) {
+                const int l = __ffs((int)m) - 1;
+                const float nv = __shfl_sync(0xffffffffu, v, l);
+                if ((uint32_t)lane == wpos) my_id = base + (uint32_t)l, my_v = nv;
+                find_worst();
+                m &= ~((2u << l) - 1u);                       // the experts after l in this chunk
+                m &= __ballot_sync(0xffffffffu, v > wv);      // still above the new worst
             }
         }
+        if ((uint32_t)lane < K) ids[lane] = my_id;
+    }
+    __syncthreads();
+    if (tid == 0) {
         for (uint32_t i = 1; i < K; ++i) {   // value descending, id ascending
             const uint32_t v = ids[i];
             uint32_t pos = i;
@@ -999,9 +1021,10 @@ __global__ void moe_swiglu_kernel(const float *__restrict__ gu, uint32_t S, uint
 
 // ---------------------------------------------------------------- combine
 
-// One CTA per token: y = sum over the selected experts in ascending id of
-// eout * weight (each product and sum rounded, src/kq_moe_qwen38.c:745-759),
-// plus shared_out * sigmoid(shared gate logit) (:820-836).
+// One CTA per (token, 256 features): y = sum over the selected experts in
+// ascending id of eout * weight (each product and sum rounded,
+// src/kq_moe_qwen38.c:745-759), plus shared_out * sigmoid(shared gate logit)
+// (:820-836).
 __global__ void __launch_bounds__(kMoeThreads)
 moe_combine_kernel(MoeDims d, const float *__restrict__ logits, uint32_t ldl, const uint32_t *__restrict__ sel_ids,
                    const float *__restrict__ sel_w, const uint32_t *__restrict__ slot,
@@ -1030,7 +1053,7 @@ moe_combine_kernel(MoeDims d, const float *__restrict__ logits, uint32_t ldl, co
         const float sc = moe_sigmoid(logit);
         if (!isfinite(logit) || !isfinite(sc)) bad = 1;
         scale_s = sc;
-        if (dbg.scale) {
+        if (dbg.scale && blockIdx.y == 0) {
             dbg.scale[2 * t] = logit;
             dbg.scale[2 * t + 1] = sc;
         }
@@ -1038,7 +1061,7 @@ moe_combine_kernel(MoeDims d, const float *__restrict__ logits, uint32_t ldl, co
     __syncthreads();
     const float sc = scale_s;
     bool ok = bad == 0;
-    for (uint32_t f = tid; f < H; f += kMoeThreads) {
+    for (uint32_t f = blockIdx.y * kMoeThreads + tid; f < H; f += kMoeThreads * gridDim.y) {
         float s = 0.0f;
         for (uint32_t q = 0; q < K; ++q) {
             const uint32_t p = order[q];
@@ -1262,7 +1285,8 @@ void launch_moe_swiglu(const float *gu, uint32_t S, uint32_t T, float *act, Erro
 
 void launch_moe_combine(const MoeDims &d, uint32_t T, const MoeBuffers &b, float *y, ErrorWord err,
                         cudaStream_t stream) {
-    launch_pdl(moe_combine_kernel, T, kMoeThreads, 0, stream, d, b.logits, d.experts + 1, b.sel_ids, b.sel_w, b.slot,
+    const dim3 grid(T, (d.hidden + kMoeThreads - 1) / kMoeThreads);
+    launch_pdl(moe_combine_kernel, grid, kMoeThreads, 0, stream, d, b.logits, d.experts + 1, b.sel_ids, b.sel_w, b.slot,
                b.eout, b.shared_out, y, b.dbg, err);
     count_launch();
 }
