@@ -210,27 +210,28 @@ proj_warp_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
 // in shared memory by cp.async four chunks deep (raw F32 or BF16 weight bytes,
 // F32 activations) and read as 16-byte vectors, four chain steps per load.
 // Other weight types are decoded into the stage synchronously (slow path).
-constexpr int kExBatch = 64;          // batch rows per CTA
 constexpr int kExK = 128;             // K per staged chunk
 constexpr int kExXStride = kExK + 4;  // padded activation row (conflict-free float4 reads)
-constexpr int kExThreads = 256;
-constexpr size_t kExXBytes = (size_t)kExBatch * kExXStride * 4;   // per stage
 
-// Tile of TR weight rows x 64 batch rows.  TR = 4 (one batch tile: twice
-// the CTAs of TR = 8, all resident at two per SM): a thread owns 1 row x 1
-// batch row; TR = 8: 2 rows x 1 batch row; TR = 32 (large batches): 4 rows
-// x 2 batch rows, eight independent sequential chains per thread, each
-// weight value read from shared memory feeding two of them.
-template <int TR> struct ExTile {
+// Tile of TR weight rows x BB batch rows.  TR = 4 (decode batches): a
+// thread owns 1 row x 1 batch row; BB = 16 makes four times the CTAs of a
+// 64-row batch span, small enough that all of a decode launch's CTAs are
+// resident at once, about evenly over the SMs.  TR = 8: 2 rows x 1 batch
+// row; TR = 32 (large batches): 4 rows x 2 batch rows, eight independent
+// sequential chains per thread, each weight value read from shared memory
+// feeding two of them.
+template <int TR, int BB = 64> struct ExTile {
     static constexpr int stages = TR == 8 ? 4 : 3;
     static constexpr int rpt = TR == 4 ? 1 : TR == 8 ? 2 : 4;    // rows per thread
     static constexpr int bpt = TR == 32 ? 2 : 1;                  // batch rows per thread
-    static constexpr size_t wbytes = (size_t)TR * kExK * 4;   // per stage (F32 room)
-    static constexpr size_t smem = stages * (kExXBytes + wbytes);
-    static_assert(TR / rpt * (kExBatch / bpt) == kExThreads, "one output group per thread");
+    static constexpr int batch = BB;
+    static constexpr int threads = TR / rpt * (BB / bpt);
+    static constexpr size_t xbytes = (size_t)BB * kExXStride * 4;   // per stage
+    static constexpr size_t wbytes = (size_t)TR * kExK * 4;         // per stage (F32 room)
+    static constexpr size_t smem = stages * (xbytes + wbytes);
+    static_assert(TR != 32 || (BB == 64 && threads == 256), "the 32-row tile spans 64 batch rows");
 };
 
-template <int TR> __host__ __device__ constexpr int rpt_of() { return ExTile<TR>::rpt; }
 
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem);
@@ -241,13 +242,14 @@ __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
 // 2: any type, decoded into F32 by the staging threads.  Every output is one
 // sequential F32 chain over K in the reference's order (products and sums
 // rounded separately).
-template <int MODE, int TR>
-__global__ void __launch_bounds__(kExThreads)
+template <int MODE, int TR, int BB>
+__global__ void __launch_bounds__(ExTile<TR, BB>::threads)
 proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                   float *__restrict__ y, uint32_t ldy, uint32_t batch,
                   ErrorWord err) {
-    using TT = ExTile<TR>;
-    constexpr int kStages = TT::stages, RPT = TT::rpt, BPT = TT::bpt;
+    using TT = ExTile<TR, BB>;
+    constexpr int kStages = TT::stages, RPT = TT::rpt, BPT = TT::bpt, kThreads = TT::threads;
+    constexpr size_t kExXBytes = TT::xbytes;
     pdl_wait();
     extern __shared__ __align__(16) uint8_t ex_smem[];
     if (error_raised(err)) return;
@@ -257,12 +259,12 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
     while (seg + 1 < segs.count && blockIdx.x >= segs.tile_start[seg + 1]) ++seg;
     const QMatrix m = segs.m[seg];
     const uint32_t row0 = (blockIdx.x - segs.tile_start[seg]) * TR;
-    const uint32_t b0 = blockIdx.y * kExBatch;
+    const uint32_t b0 = blockIdx.y * BB;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // the thread's rows rb .. rb + RPT - 1 (warp-uniform: broadcast weight
-    // reads) and batch rows bb + 32 j
-    const int rb = TR == 32 ? 4 * warp : rpt_of<TR>() * (warp >> 1);
-    const int bb = TR == 32 ? lane : (warp & 1) * 32 + lane;
+    // the thread's rows rb .. rb + RPT - 1 (weight reads broadcast to the
+    // threads of a row) and batch rows bb + 32 j
+    const int rb = TR == 32 ? 4 * warp : RPT * (tid / BB);
+    const int bb = TR == 32 ? lane : tid % BB;
     const uint32_t nchunks = (m.cols + kExK - 1) / kExK;
     const bool xvec = (ldx % 4u) == 0u && (reinterpret_cast<uintptr_t>(x) & 15u) == 0u;
     constexpr uint32_t kElem = MODE == 1 ? 2u : 4u;   // staged weight bytes per value
@@ -270,11 +272,11 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
     auto stage = [&](uint32_t c) {
         const int buf = c % kStages;
         const uint32_t k0 = c * kExK;
-        float *xs = xs_base + (size_t)buf * kExBatch * kExXStride;
+        float *xs = xs_base + (size_t)buf * BB * kExXStride;
         uint8_t *ws = ws_base + (size_t)buf * TT::wbytes;
         // weights: TR rows x 128 values
         if constexpr (MODE == 2) {
-            for (int i = tid; i < TR * (kExK / 4); i += kExThreads) {
+            for (int i = tid; i < TR * (kExK / 4); i += kThreads) {
                 const int r = i / (kExK / 4), kk = (i % (kExK / 4)) * 4;
                 const uint32_t grow = row0 + r;
                 float w[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -285,7 +287,7 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
             }
         } else {
             constexpr int kPieces = kExK * kElem / 16;   // 16-byte pieces per row
-            for (int i = tid; i < TR * kPieces; i += kExThreads) {
+            for (int i = tid; i < TR * kPieces; i += kThreads) {
                 const int r = i / kPieces, pc = i % kPieces;
                 const uint32_t grow = row0 + r, k = k0 + pc * (16 / kElem);
                 uint8_t *dst = ws + (size_t)r * kExK * kElem + pc * 16;
@@ -306,7 +308,7 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
             }
         }
         // activations: 64 rows x 128 values
-        for (int i = tid; i < kExBatch * (kExK / 4); i += kExThreads) {
+        for (int i = tid; i < BB * (kExK / 4); i += kThreads) {
             const int br = i / (kExK / 4), q4 = (i % (kExK / 4)) * 4;
             const uint32_t gb = b0 + br, k = k0 + q4;
             float *dst = xs + (size_t)br * kExXStride + q4;
@@ -336,7 +338,7 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
         __syncthreads();
         const int buf = c % kStages;
         const uint32_t kc = min((uint32_t)kExK, m.cols - c * kExK);
-        const float *xv = xs_base + (size_t)buf * kExBatch * kExXStride + (size_t)bb * kExXStride;
+        const float *xv = xs_base + (size_t)buf * BB * kExXStride + (size_t)bb * kExXStride;
         const uint8_t *ws = ws_base + (size_t)buf * TT::wbytes + (size_t)rb * kExK * kElem;
         auto wq = [&](int r, int k) {   // 4 F32 weights of row rb + r at k
             const uint8_t *row = ws + (size_t)r * kExK * kElem;
@@ -348,8 +350,8 @@ proj_exact_kernel(ProjSegments segs, const float *__restrict__ x, uint32_t ldx,
                 return *reinterpret_cast<const float4 *>(row + (size_t)k * 4);
             }
         };
-        if (kc == (uint32_t)kExK) {
-#pragma unroll 2
+        if (kc == (uint32_t)kExK) {   // fully unrolled: every operand address is an immediate offset
+#pragma unroll
             for (int k = 0; k < kExK; k += 4) {
                 float xv4[BPT][4];
 #pragma unroll
@@ -439,12 +441,13 @@ bool launch_projection(const ProjSegments &in, const float *x, uint32_t ldx,
     return false;
 }
 
-template <int TR>
+template <int TR, int BB>
 static void launch_exact_tiles(const ProjSegments &in, const float *x, uint32_t ldx, float *y, uint32_t ldy,
                                uint32_t batch, ErrorWord err, cudaStream_t stream) {
+    using TT = ExTile<TR, BB>;
     ProjSegments segs = in;
     fill_tile_starts(segs, TR);
-    dim3 grid(segs.tile_start[segs.count], (batch + kExBatch - 1) / kExBatch);
+    dim3 grid(segs.tile_start[segs.count], (batch + BB - 1) / BB);
     // one launch per mode; segments of mixed types go through the generic mode
     int mode = 0;
     for (int i = 0; i < segs.count; ++i) {
@@ -453,19 +456,19 @@ static void launch_exact_tiles(const ProjSegments &in, const float *x, uint32_t 
         const int mi = !aligned ? 2 : q.type == kTypeF32 ? 0 : q.type == kTypeBF16 ? 1 : 2;
         mode = i == 0 ? mi : (mode == mi ? mode : 2);
     }
-    constexpr size_t smem = ExTile<TR>::smem;
+    constexpr size_t smem = TT::smem;
     static DeviceOnce attr;
     attr.run([] {
-        cudaFuncSetAttribute(proj_exact_kernel<0, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(proj_exact_kernel<1, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(proj_exact_kernel<2, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(proj_exact_kernel<0, TR, BB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(proj_exact_kernel<1, TR, BB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(proj_exact_kernel<2, TR, BB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     });
     if (mode == 0)
-        launch_pdl(proj_exact_kernel<0, TR>, grid, kExThreads, smem, stream, segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<0, TR, BB>, grid, TT::threads, smem, stream, segs, x, ldx, y, ldy, batch, err);
     else if (mode == 1)
-        launch_pdl(proj_exact_kernel<1, TR>, grid, kExThreads, smem, stream, segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<1, TR, BB>, grid, TT::threads, smem, stream, segs, x, ldx, y, ldy, batch, err);
     else
-        launch_pdl(proj_exact_kernel<2, TR>, grid, kExThreads, smem, stream, segs, x, ldx, y, ldy, batch, err);
+        launch_pdl(proj_exact_kernel<2, TR, BB>, grid, TT::threads, smem, stream, segs, x, ldx, y, ldy, batch, err);
 }
 
 void launch_projection_exact(const ProjSegments &in, const float *x,
@@ -473,14 +476,15 @@ void launch_projection_exact(const ProjSegments &in, const float *x,
                              uint32_t batch, ErrorWord err,
                              cudaStream_t stream) {
     KernelTimer timer("proj_exact", stream);
-    // 32-row tiles once the batch alone gives several CTAs per SM; 4-row
-    // tiles for one batch tile (decode), so that the rows alone fill the SMs
+    // 32-row tiles once the batch alone gives several CTAs per SM; 4-row x
+    // 16-batch-row tiles for decode batches (up to 64), so that the rows
+    // and batch spans together fill the SMs evenly
     if (batch >= 1024)
-        launch_exact_tiles<32>(in, x, ldx, y, ldy, batch, err, stream);
-    else if (batch <= (uint32_t)kExBatch)
-        launch_exact_tiles<4>(in, x, ldx, y, ldy, batch, err, stream);
+        launch_exact_tiles<32, 64>(in, x, ldx, y, ldy, batch, err, stream);
+    else if (batch <= 64u)
+        launch_exact_tiles<4, 16>(in, x, ldx, y, ldy, batch, err, stream);
     else
-        launch_exact_tiles<8>(in, x, ldx, y, ldy, batch, err, stream);
+        launch_exact_tiles<8, 64>(in, x, ldx, y, ldy, batch, err, stream);
     count_launch();
 }
 
