@@ -326,32 +326,37 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
 
 // A fragment (rows m0 .. m0+15, K k0 .. k0+15) of a row-major bf16 tile with
 // row stride ld; B fragment (columns n0 .. n0+7) of a [n][k] bf16 tile.
-__device__ __forceinline__ void frag_a(const uint16_t *t, int ld, int m0, int k0, int g, int q, uint32_t (&a)[4]) {
-    a[0] = *reinterpret_cast<const uint32_t *>(t + (m0 + g) * ld + k0 + 2 * q);
-    a[1] = *reinterpret_cast<const uint32_t *>(t + (m0 + g + 8) * ld + k0 + 2 * q);
-    a[2] = *reinterpret_cast<const uint32_t *>(t + (m0 + g) * ld + k0 + 2 * q + 8);
-    a[3] = *reinterpret_cast<const uint32_t *>(t + (m0 + g + 8) * ld + k0 + 2 * q + 8);
+// Four 8x8 bf16 matrices from shared memory (ldmatrix): thread t gives the
+// address of row t % 8 of matrix t / 8 and receives, from each matrix, the
+// pair (row lane / 4, columns 2 * (lane % 4) ..): the mma.sync m16n8k16
+// fragment layout of A (four matrices) and of two B operands (two each).
+__device__ __forceinline__ void ldsm_x4(const uint16_t *p, uint32_t (&r)[4]) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
 }
-__device__ __forceinline__ void frag_b(const uint16_t *t, int ld, int n0, int k0, int g, int q, uint32_t &b0,
-                                       uint32_t &b1) {
-    b0 = *reinterpret_cast<const uint32_t *>(t + (n0 + g) * ld + k0 + 2 * q);
-    b1 = *reinterpret_cast<const uint32_t *>(t + (n0 + g) * ld + k0 + 2 * q + 8);
-}
-// acc += A B over K = 16 * KS steps, three-term split
+
+// acc += A B over K = 16 * KS steps, three-term split (hi.hi, hi.lo, lo.hi
+// in that order).  Per step one ldmatrix.x4 for each A part (rows m0.. and
+// m0 + 8.., columns k and k + 8) and one for both B parts (hi then lo,
+// columns k and k + 8); row strides of 136 or 72 bf16 put the eight rows of
+// a matrix in distinct banks.
 template <int KS>
 __device__ __forceinline__ void mma3(float (&acc)[4], const uint16_t *ah, const uint16_t *al, int lda, int m0,
                                      const uint16_t *bh, const uint16_t *bl, int ldb, int n0, int g, int q) {
+    const int lane = 4 * g + q, mi = lane >> 3, r = lane & 7;
+    const size_t oa = (size_t)(m0 + r + 8 * (mi & 1)) * lda + 8 * (mi >> 1);
+    const uint16_t *pah = ah + oa, *pal = al + oa;
+    const uint16_t *pb = (mi < 2 ? bh : bl) + (size_t)(n0 + r) * ldb + 8 * (mi & 1);
 #pragma unroll
     for (int kk = 0; kk < KS; ++kk) {
-        uint32_t a[4], b0, b1;
-        frag_a(ah, lda, m0, 16 * kk, g, q, a);
-        frag_b(bh, ldb, n0, 16 * kk, g, q, b0, b1);
-        mma_bf16(acc, a, b0, b1);
-        uint32_t c0, c1;
-        frag_b(bl, ldb, n0, 16 * kk, g, q, c0, c1);
-        mma_bf16(acc, a, c0, c1);
-        frag_a(al, lda, m0, 16 * kk, g, q, a);
-        mma_bf16(acc, a, b0, b1);
+        uint32_t a[4], b[4];
+        ldsm_x4(pah + 16 * kk, a);
+        ldsm_x4(pb + 16 * kk, b);
+        mma_bf16(acc, a, b[0], b[1]);
+        mma_bf16(acc, a, b[2], b[3]);
+        ldsm_x4(pal + 16 * kk, a);
+        mma_bf16(acc, a, b[0], b[1]);
     }
 }
 
