@@ -470,7 +470,7 @@ moe_down_kernel(MoeDims d, QMatrix down, const float *__restrict__ act, const ui
 constexpr uint32_t kStreamThreads = 640;
 constexpr uint32_t kStreamRing = 4;
 constexpr uint32_t kGuTile = 16;      // gate rows (and as many up rows) per tile
-constexpr uint32_t kDnTile = 64;      // down rows per tile
+constexpr uint32_t kDnTile = 128;     // down rows per tile
 // The dynamic shared memory the streamed kernels may ask for: the 227 KB
 // per-block opt-in less the static part and the 1 KB reserved per CTA.
 constexpr uint32_t kStreamSmemLimit = 224u * 1024u;
