@@ -469,7 +469,7 @@ moe_down_kernel(MoeDims d, QMatrix down, const float *__restrict__ act, const ui
 
 constexpr uint32_t kStreamThreads = 640;
 constexpr uint32_t kStreamRing = 4;
-constexpr uint32_t kGuTile = 16;      // gate rows (and as many up rows) per tile
+constexpr uint32_t kGuTile = 32;      // gate rows (and as many up rows) per tile: two 16-row MMA blocks
 constexpr uint32_t kDnTile = 128;     // down rows per tile
 // The dynamic shared memory the streamed kernels may ask for: the 227 KB
 // per-block opt-in less the static part and the 1 KB reserved per CTA.
@@ -704,10 +704,11 @@ __device__ __forceinline__ void gu_block(const uint8_t *rows, uint32_t rb, const
 }
 
 // Grid: one CTA per SM; block kStreamThreads.  Warp w decodes super-block
-// w % kGuSbMax of the tile's gate rows (w < kGuSbMax) or up rows.  Dynamic
-// shared memory: the ring (ring stages of kGuTile gate rows then kGuTile up
-// rows, pitch row_bytes), the tile's scale table [2*kGuTile][H/64] float4
-// (each warp writes and reads its own rows and super-block), the per-warp
+// w % kGuSbMax of the tile's gate rows (w < kGuSbMax) or up rows, as two
+// 16-row MMA blocks.  Dynamic shared memory: the ring (ring stages of
+// kGuTile gate rows then kGuTile up rows, pitch row_bytes), the scale table
+// of one 16-row block of each half [2][16][H/64] float4 (each warp writes
+// and reads its own rows and super-block, block by block), the per-warp
 // partial sums [kMmaWarps][kGuTile][kMmaTokens].  Tiles in active-expert-
 // major order.
 __global__ void __launch_bounds__(kStreamThreads, 1)
@@ -722,7 +723,7 @@ moe_gate_up_stream_kernel(MoeDims d, QMatrix gate, QMatrix up, const float *__re
     const uint32_t J = (I + kGuTile - 1u) / kGuTile;
     const StreamRing rg{full, gsm, TR * rb, ring};
     float4 *table = reinterpret_cast<float4 *>(gsm + (size_t)ring * rg.stage_bytes);
-    float *red = reinterpret_cast<float *>(table + (size_t)TR * tp);
+    float *red = reinterpret_cast<float *>(table + (size_t)2 * 16u * tp);
     ring_init(full, ring);
     pdl_wait();
     if (moe_err_raised(err)) return;
@@ -754,7 +755,7 @@ moe_gate_up_stream_kernel(MoeDims d, QMatrix gate, QMatrix up, const float *__re
 
     GuFrags f;
     float *pr = red + (size_t)warp * kGuTile * kMmaTokens;
-    const float4 *tab = table + (size_t)half * kGuTile * tp;
+    const float4 *tab = table + (size_t)half * 16u * tp;   // the warp's half of the 16-row table
     TileCursor c;
     c.start(tb, J);
     uint32_t cur = 0xFFFFFFFFu, s0 = 0, n = 0, loaded = 0xFFFFFFFFu;
@@ -774,18 +775,6 @@ moe_gate_up_stream_kernel(MoeDims d, QMatrix gate, QMatrix up, const float *__re
             return;
         }
         const uint8_t *blk = st + (size_t)half * kGuTile * rb;
-        if (worker) {   // lanes 2r, 2r + 1: the scale entries of row r's super-block sb
-            const uint32_t r = lane >> 1, hh = lane & 1u;
-            if (r < rows) {
-                const uint4 hd = *reinterpret_cast<const uint4 *>(blk + (size_t)r * rb + sb * 144u);
-                float4 e0, e1;
-                q4k_header_entries(hd, hh, e0, e1);
-                float4 *tr = table + ((size_t)half * kGuTile + r) * tp + sb * 4u + 2u * hh;
-                tr[0] = e0;
-                tr[1] = e1;
-            }
-            __syncwarp();
-        }
         for (uint32_t g0 = 0; g0 < n; g0 += kMmaTokens) {
             const uint32_t nb = min(kMmaTokens, n - g0);
             if (worker) {
@@ -795,11 +784,27 @@ moe_gate_up_stream_kernel(MoeDims d, QMatrix gate, QMatrix up, const float *__re
                              f);
                     loaded = g0;
                 }
-                float t0 = 0.0f, t1 = 0.0f;
-                gu_block(blk, rb, tab, tp, sb, lane, f, t0, t1);
-                if (q < nb) {
-                    pr[g * kMmaTokens + q] = t0 * f.unscale;
-                    pr[(g + 8u) * kMmaTokens + q] = t1 * f.unscale;
+                for (uint32_t b = 0; b < kGuTile / 16u; ++b) {   // the half's 16-row MMA blocks
+                    {   // lanes 2r, 2r + 1: the scale entries of block row r's super-block sb
+                        const uint32_t r = lane >> 1, hh = lane & 1u;
+                        if (16u * b + r < rows) {
+                            const uint4 hd =
+                                *reinterpret_cast<const uint4 *>(blk + (size_t)(16u * b + r) * rb + sb * 144u);
+                            float4 e0, e1;
+                            q4k_header_entries(hd, hh, e0, e1);
+                            float4 *tr = table + ((size_t)half * 16u + r) * tp + sb * 4u + 2u * hh;
+                            tr[0] = e0;
+                            tr[1] = e1;
+                        }
+                        __syncwarp();
+                    }
+                    float t0 = 0.0f, t1 = 0.0f;
+                    gu_block(blk + (size_t)16u * b * rb, rb, tab, tp, sb, lane, f, t0, t1);
+                    if (q < nb) {
+                        pr[(16u * b + g) * kMmaTokens + q] = t0 * f.unscale;
+                        pr[(16u * b + g + 8u) * kMmaTokens + q] = t1 * f.unscale;
+                    }
+                    __syncwarp();   // the table is rewritten by the next block
                 }
             }
             __syncthreads();   // partial sums complete; the stage has been read
@@ -1201,7 +1206,7 @@ static uint32_t stream_ring(size_t stage, size_t fixed) {
 }
 
 static size_t gate_up_fixed_bytes(const MoeDims &d) {
-    return (size_t)2 * kGuTile * (d.hidden / 64u) * 16u + (size_t)kMmaWarps * kGuTile * kMmaTokens * 4u;
+    return (size_t)2 * 16u * (d.hidden / 64u) * 16u + (size_t)kMmaWarps * kGuTile * kMmaTokens * 4u;
 }
 
 static size_t down_fixed_bytes() { return (size_t)kMmaWarps * kDnTile * kMmaTokens * 4u; }
