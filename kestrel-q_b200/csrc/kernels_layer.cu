@@ -84,61 +84,69 @@ gr_norm_kernel(GrDims d, const float *__restrict__ norm, const float *__restrict
 
 // rank[t][i] = silu(proj[t][i] / B) for i < R; write_gate[t][b] =
 // 2 sigmoid(proj[t][R + b] / B) (src/kq_layer_qwen38.c:109-116,155-163).
+// Grid (column blocks, tokens).
 __global__ void gr_gate_kernel(GrDims d, uint32_t T, const float *__restrict__ proj, float *__restrict__ rank,
                                float *__restrict__ wg, ErrorWord err) {
     pdl_wait();
     if (gr_err_raised(err)) return;
     const uint32_t R = d.rank, B = d.branches, per = R + B;
     const float fb = (float)B;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (uint64_t)T * per;
-         i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t t = i / per, c = i % per;
-        const float v = __fdiv_rn(proj[i], fb);
-        if (c < R)
-            rank[t * R + c] = __fmul_rn(v, gr_sigmoid(v));
-        else
-            wg[t * B + (c - R)] = __fmul_rn(2.0f, gr_sigmoid(v));
-    }
+    for (uint32_t t = blockIdx.y; t < T; t += gridDim.y)
+        for (uint32_t c = blockIdx.x * blockDim.x + threadIdx.x; c < per; c += gridDim.x * blockDim.x) {
+            const float v = __fdiv_rn(proj[(size_t)t * per + c], fb);
+            if (c < R)
+                rank[(size_t)t * R + c] = __fmul_rn(v, gr_sigmoid(v));
+            else
+                wg[(size_t)t * B + (c - R)] = __fmul_rn(2.0f, gr_sigmoid(v));
+        }
 }
 
 // read[t][*] = sigmoid(read logits) in place; mixed[t][h] =
 // (sum_b read[t][b][h] * nm[t][b][h]) / B (src/kq_layer_qwen38.c:129-143).
+// Grid (feature blocks, tokens).
 __global__ void gr_mix_kernel(GrDims d, uint32_t T, float *__restrict__ read, const float *__restrict__ nm,
                               float *__restrict__ mixed, ErrorWord err) {
     pdl_wait();
     if (gr_err_raised(err)) return;
     const uint32_t H = d.hidden, B = d.branches;
     const size_t W = (size_t)H * B;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (uint64_t)T * H;
-         i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t t = i / H, h = i % H;
-        float s = 0.0f;
-        for (uint32_t b = 0; b < B; ++b) {
-            const size_t o = t * W + (size_t)b * H + h;
-            const float g = gr_sigmoid(read[o]);
-            read[o] = g;
-            s = __fadd_rn(s, __fmul_rn(g, nm[o]));
+    for (uint32_t t = blockIdx.y; t < T; t += gridDim.y)
+        for (uint32_t h = blockIdx.x * blockDim.x + threadIdx.x; h < H; h += gridDim.x * blockDim.x) {
+            float s = 0.0f;
+            for (uint32_t b = 0; b < B; ++b) {
+                const size_t o = (size_t)t * W + (size_t)b * H + h;
+                const float g = gr_sigmoid(read[o]);
+                read[o] = g;
+                s = __fadd_rn(s, __fmul_rn(g, nm[o]));
+            }
+            mixed[(size_t)t * H + h] = __fdiv_rn(s, (float)B);
         }
-        mixed[i] = __fdiv_rn(s, (float)B);
-    }
 }
 
 // out[t][b][h] = br[t][b][h] + block[t][h] * wg[t][b]
-// (src/kq_layer_qwen38.c:196-209).
+// (src/kq_layer_qwen38.c:196-209).  Grid (feature blocks, tokens); a thread
+// reads block[t][h] once for every branch.
 __global__ void gr_write_kernel(GrDims d, uint32_t T, const float *__restrict__ br, const float *__restrict__ block,
                                 const float *__restrict__ wg, float *__restrict__ out, ErrorWord err) {
     pdl_wait();
     if (gr_err_raised(err)) return;
     const uint32_t H = d.hidden, B = d.branches;
-    const uint64_t W = (uint64_t)H * B;
-    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (uint64_t)T * W;
-         i += (uint64_t)gridDim.x * blockDim.x) {
-        const uint64_t t = i / W, r = i % W, b = r / H, h = r % H;
-        out[i] = __fadd_rn(br[i], __fmul_rn(block[t * H + h], wg[t * B + b]));
-    }
+    const size_t W = (size_t)H * B;
+    for (uint32_t t = blockIdx.y; t < T; t += gridDim.y)
+        for (uint32_t h = blockIdx.x * blockDim.x + threadIdx.x; h < H; h += gridDim.x * blockDim.x) {
+            const float v = block[(size_t)t * H + h];
+            for (uint32_t b = 0; b < B; ++b) {
+                const size_t o = (size_t)t * W + (size_t)b * H + h;
+                out[o] = __fadd_rn(br[o], __fmul_rn(v, wg[(size_t)t * B + b]));
+            }
+        }
 }
 
-static uint32_t grid_for(uint64_t n) { return (uint32_t)std::min<uint64_t>((n + 255) / 256, 148u * 16u); }
+// Grid of the per-token kernels: blocks of 256 over `n` columns, one row of
+// blocks per token (at most 65535 rows; the kernels stride over the rest).
+static dim3 grid_tokens(uint32_t n, uint32_t T) {
+    return dim3((n + 255) / 256, std::min<uint32_t>(std::max<uint32_t>(T, 1u), 65535u));
+}
 
 size_t gr_workspace_bytes(const GrDims &d, uint32_t T) {
     const uint64_t W = (uint64_t)d.hidden * d.branches;
@@ -179,23 +187,20 @@ void launch_gr_read(const GrDims &d, const GrWeightsDev &w, const float *br, uin
     s.m[1] = w.inject;
     s.out_offset[1] = d.rank;
     launch_projection(s, b.normalized, W, b.proj, d.rank + d.branches, T, err, stream, b.ws_down, b.ws_down_floats);
-    launch_pdl(gr_gate_kernel, grid_for((uint64_t)T * (d.rank + d.branches)), 256, 0, stream, d, T, b.proj, b.rank,
-               wg, err);
+    launch_pdl(gr_gate_kernel, grid_tokens(d.rank + d.branches, T), 256, 0, stream, d, T, b.proj, b.rank, wg, err);
     count_launch();
     ProjSegments u{};
     u.count = 1;
     u.m[0] = w.up;
     u.out_offset[0] = 0;
     launch_projection(u, b.rank, d.rank, b.read, W, T, err, stream, b.ws_up, b.ws_up_floats);
-    launch_pdl(gr_mix_kernel, grid_for((uint64_t)T * d.hidden), 256, 0, stream, d, T, b.read, b.normalized, mixed,
-               err);
+    launch_pdl(gr_mix_kernel, grid_tokens(d.hidden, T), 256, 0, stream, d, T, b.read, b.normalized, mixed, err);
     count_launch();
 }
 
 void launch_gr_write(const GrDims &d, const float *br, const float *block, const float *wg, uint32_t T, float *out,
                      ErrorWord err, cudaStream_t stream) {
-    launch_pdl(gr_write_kernel, grid_for((uint64_t)T * d.hidden * d.branches), 256, 0, stream, d, T, br, block, wg,
-               out, err);
+    launch_pdl(gr_write_kernel, grid_tokens(d.hidden, T), 256, 0, stream, d, T, br, block, wg, out, err);
     count_launch();
 }
 
